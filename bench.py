@@ -1,0 +1,551 @@
+#!/usr/bin/env python
+"""Benchmark of the vllm_nt B200 hot path.
+
+Headline (one JSON line on rank 0): paged-attention decode throughput in tokens/s for the
+decode workload -- 256 sequences x one query token, 32 query / 8 KV heads, head 128,
+block 16, context lengths U[512, 8192], distinct block ids from a 150000-block pool, bf16
+with fp32 softmax -- sharded across the N ranks by KV head (rank r owns KV heads
+[r*8/N, (r+1)*8/N) of the pool and their query heads; no collective on the data path).
+A step is one decode call over the whole batch; value = 256 * steps / (max over ranks of
+the device time of the timed steps).
+
+Also reported: the roofline of the decode kernel against measured HBM bandwidth, the
+end-to-end rate through the plugin's public decode entry point with host buffers, the
+oracle's CPU rate on a bounded sample, clocks sampled during the timed region, and (at
+N = 1) a per-op table: achieved HBM GB/s for every memory-bound op at its benchmark
+config and tensor TFLOP/s for the projection GEMM.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-ops]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "vllm-nt_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+METRIC = "per-op HBM GB/s (% of B200 peak); paged-attn decode tok/s at 1/2/4/8 GPUs"
+BATCH, HQ, HKV, HEAD, BLOCK, POOL, CTX_LO, CTX_HI, MAX_BLOCKS = 256, 32, 8, 128, 16, 150000, 512, 8192, 512
+L2_BYTES = 126 * 1024 * 1024
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def workload(seed: int = 0):
+    """Context lengths and block tables of the decode workload (CPU, deterministic)."""
+    g = torch.Generator().manual_seed(seed)
+    ctx = torch.randint(CTX_LO, CTX_HI + 1, (BATCH,), generator=g)
+    nblk = (ctx + BLOCK - 1) // BLOCK
+    ids = torch.randperm(POOL, generator=g)[: int(nblk.sum())].to(torch.int32)
+    table = torch.zeros(BATCH, MAX_BLOCKS, dtype=torch.int32)
+    off = 0
+    for i, n in enumerate(nblk.tolist()):
+        table[i, :n] = ids[off : off + n]
+        off += n
+    q = torch.randn(BATCH, HQ, HEAD, generator=g).to(torch.bfloat16)
+    return ctx.to(torch.int32), table, q
+
+
+def decode_bytes(ctx: torch.Tensor, hkv_local: int) -> int:
+    """Algorithmic HBM bytes of one decode call: every cached K and V row of the local
+    heads once, q and out once, the block-table entries used and the sequence lengths."""
+    tokens = int(ctx.sum())
+    blocks = int(((ctx + BLOCK - 1) // BLOCK).sum())
+    hq_local = hkv_local * (HQ // HKV)
+    return tokens * hkv_local * HEAD * 2 * 2 + 2 * BATCH * hq_local * HEAD * 2 + blocks * 4 + BATCH * 4
+
+
+class ClockSampler:
+    """nvidia-smi sampling (200 ms) of SM clock and throttle reasons during the run."""
+
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"ntb200_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"),
+                stderr=subprocess.DEVNULL,
+            )
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        power = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        loaded = [s for s, p in zip(sm, power) if p > 300.0] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {
+            "sm_mhz": statistics.median(loaded) if loaded else None,
+            "sm_max_mhz": smax,
+            "reasons": reasons,
+            "samples": len(rows),
+            "samples_under_load": len([p for p in power if p > 300.0]),
+        }
+
+
+def traffic_from_profile() -> float | None:
+    """Per-launch DRAM bytes of the decode split kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "paged_decode_split_b256.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# --------------------------------------------------------------------------------------
+# reference arm / CPU baseline: the oracle on a bounded sample of sequences
+# --------------------------------------------------------------------------------------
+
+
+def oracle_decode_rate(ctx, q, seqs_per_call: int, calls: int, seed: int = 1) -> tuple[float, int, str]:
+    """Times oracle.paged_decode over `calls` calls of `seqs_per_call` sequences each
+    (K/V of each sampled sequence generated ~N(0,1) in a local paged cache).  Returns
+    (tokens/s, threads, sample description)."""
+    import oracle
+
+    g = torch.Generator().manual_seed(seed)
+    order = torch.randperm(BATCH, generator=g).tolist()
+    total_t = 0.0
+    done = 0
+    k = 0
+    for _ in range(calls):
+        pick = [order[(k + i) % BATCH] for i in range(seqs_per_call)]
+        k += seqs_per_call
+        lens = ctx[pick]
+        nblk = int(((lens + BLOCK - 1) // BLOCK).sum())
+        kc = torch.randn(nblk, BLOCK, HKV, HEAD, generator=g).to(torch.bfloat16)
+        vc = torch.randn(nblk, BLOCK, HKV, HEAD, generator=g).to(torch.bfloat16)
+        table = torch.zeros(len(pick), MAX_BLOCKS, dtype=torch.int32)
+        off = 0
+        for i, n in enumerate(((lens + BLOCK - 1) // BLOCK).tolist()):
+            table[i, :n] = torch.arange(off, off + n, dtype=torch.int32)
+            off += n
+        t0 = time.perf_counter()
+        oracle.paged_decode(q[pick], kc, vc, lens, table, 1.0 / math.sqrt(HEAD))
+        total_t += time.perf_counter() - t0
+        done += len(pick)
+    sample = f"{done} sequences of the decode workload ({calls} calls x {seqs_per_call}), torch CPU oracle"
+    return done / total_t, torch.get_num_threads(), sample
+
+
+def run_reference(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    ctx, table, q = workload()
+    # size each step so warmup + steps take about two minutes
+    t_one, _, _ = oracle_decode_rate(ctx, q, 1, 1)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    per_step = max(1, min(BATCH, int(budget * t_one)))
+    oracle_decode_rate(ctx, q, per_step, args.warmup)
+    value, threads, sample = oracle_decode_rate(ctx, q, per_step, args.steps, seed=2)
+    line = {
+        "metric": METRIC,
+        "impl": "reference",
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1000.0 * per_step / value,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(n: int) -> dict:
+    return {
+        "workload": "paged-attn decode: 256 seqs x 1 token, 32 q / 8 kv heads, head 128, block 16, "
+        "ctx U[512,8192], distinct ids from a 150000-block pool, bf16 (fp32 softmax)",
+        "global_batch": BATCH,
+        "seq_len": "U[512,8192]",
+        "parallelism": f"kv-head shard x{n}" if n > 1 else "single GPU",
+        "kv_heads_per_gpu": HKV // n,
+        "l2": "inputs larger than L2 (K/V working set per step >= 570 MB per GPU)",
+    }
+
+
+# --------------------------------------------------------------------------------------
+# per-op table (N = 1)
+# --------------------------------------------------------------------------------------
+
+
+def time_graph(fn_list, iters: int) -> float:
+    """Average device ms per call of a round-robin over fn_list, captured in a CUDA graph
+    (launch gaps minimal); the set of buffers the calls touch exceeds L2."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for f in fn_list:
+            f()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(iters):
+            fn_list[i % len(fn_list)]()
+    graph.replay()
+    torch.cuda.synchronize()
+    reps = 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / (reps * iters)
+
+
+def per_op_table(dev, peaks) -> dict:
+    from vllm_nt._ntops.torch._ext import ops
+
+    o = ops()
+    hbm = peaks["hbm_gbs"]
+    tens = peaks["bf16_tflops"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    res = {}
+
+    def copies(nbytes):
+        return max(2, math.ceil(3 * L2_BYTES / nbytes))
+
+    def report(name, nbytes, ms, extra=None):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        d = {"bytes": nbytes, "us": ms * 1e3, "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 3)}
+        if extra:
+            d.update(extra)
+        res[name] = d
+
+    # (a) fused_add_rms_norm fp32 [128, 4096]
+    M, H = 128, 4096
+    nb = 4 * M * H * 4 + H * 4
+    r = copies(nb)
+    xs = [torch.randn(M, H, device=dev, generator=g) for _ in range(r)]
+    rs = [torch.randn(M, H, device=dev, generator=g) for _ in range(r)]
+    w = 1 + 0.1 * torch.randn(H, device=dev, generator=g)
+    outs = [torch.empty(M, H, device=dev) for _ in range(r)]
+    fns = [lambda i=i: o.fused_add_rms_norm(outs[i], rs[i], xs[i], w, 1e-6) for i in range(r)]
+    report("fused_add_rms_norm f32 [128,4096]", nb, time_graph(fns, 20 * r))
+    # bf16 M-sweep point at a size where launch latency no longer dominates
+    M2 = 8192
+    nb2 = 4 * M2 * H * 2 + H * 2
+    r2 = copies(nb2)
+    xs2 = [torch.randn(M2, H, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(r2)]
+    rs2 = [torch.randn(M2, H, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(r2)]
+    w2 = w.to(torch.bfloat16)
+    outs2 = [torch.empty_like(xs2[0]) for _ in range(r2)]
+    fns = [lambda i=i: o.fused_add_rms_norm(outs2[i], rs2[i], xs2[i], w2, 1e-6) for i in range(r2)]
+    report("fused_add_rms_norm bf16 [8192,4096]", nb2, time_graph(fns, 10 * r2))
+    del xs, rs, outs, xs2, rs2, outs2
+
+    # (b) silu_and_mul fp32 [128,22016] -> [128,11008]
+    nb = 128 * 22016 * 4 + 128 * 11008 * 4
+    r = copies(nb)
+    xs = [torch.randn(128, 22016, device=dev, generator=g) for _ in range(r)]
+    outs = [torch.empty(128, 11008, device=dev) for _ in range(r)]
+    fns = [lambda i=i: o.silu_and_mul(outs[i], xs[i]) for i in range(r)]
+    report("silu_and_mul f32 [128,22016]", nb, time_graph(fns, 20 * r))
+    del xs, outs
+
+    # (c) RoPE fp32 q [128,32,128], k [128,8,128], positions U[0,4096)
+    T = 128
+    nb = 2 * T * (32 + 8) * 128 * 4 + T * 128 * 4 + T * 8
+    r = copies(nb)
+    qs = [torch.randn(T, 32, 128, device=dev, generator=g) for _ in range(r)]
+    ks = [torch.randn(T, 8, 128, device=dev, generator=g) for _ in range(r)]
+    pos = [torch.randint(0, 4096, (T,), device=dev, generator=g) for _ in range(r)]
+    import oracle
+
+    cache = oracle.build_cos_sin_cache(128, 4096, 10000.0).to(dev)
+    fns = [lambda i=i: o.rotary_embedding_neox(pos[i], qs[i], ks[i], cache, 128, 128) for i in range(r)]
+    report("rope_neox f32 q[128,32,128] k[128,8,128]", nb, time_graph(fns, 20 * r))
+    del qs, ks
+
+    # KV store bf16: 4096 tokens x 8 x 128 into [8192,16,8,128] caches, distinct slots
+    N = 4096
+    nb = 2 * N * 8 * 128 * 2 * 2 + N * 8
+    kc = torch.zeros(8192, 16, 8, 128, device=dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    r = copies(nb)
+    keys = [torch.randn(N, 8, 128, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(r)]
+    vals = [torch.randn(N, 8, 128, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(r)]
+    slots = [torch.randperm(8192 * 16, device=dev, generator=g)[:N] for _ in range(r)]
+    fns = [lambda i=i: o.reshape_and_cache(keys[i], vals[i], kc, vc, slots[i]) for i in range(r)]
+    report("reshape_and_cache bf16 4096x8x128", nb, time_graph(fns, 20 * r))
+    del keys, vals, kc, vc
+
+    # embedding bf16: 4096 ids into a [128256, 4096] table
+    Tn = 4096
+    wt = torch.randn(128256, 4096, device=dev, generator=g, dtype=torch.bfloat16)
+    ids = [torch.randint(0, 128256, (Tn,), device=dev, generator=g) for _ in range(8)]
+    outs = [torch.empty(Tn, 4096, device=dev, dtype=torch.bfloat16) for _ in range(8)]
+    nb = 2 * Tn * 4096 * 2 + Tn * 8
+    fns = [lambda i=i: o.embedding(outs[i], ids[i], wt) for i in range(8)]
+    report("embedding bf16 4096 ids x 4096", nb, time_graph(fns, 80))
+    del wt, outs
+
+    # projection GEMM bf16 (fp32 accumulate)
+    for (K, Nn, tag) in ((4096, 6144, "qkv"), (4096, 4096, "o_proj"), (4096, 28672, "gate_up"), (14336, 4096, "down")):
+        for M in (1, 16, 128, 1024, 8192):
+            x = torch.randn(M, K, device=dev, generator=g, dtype=torch.bfloat16)
+            wts = [0.02 * torch.randn(Nn, K, device=dev, generator=g, dtype=torch.bfloat16)
+                   for _ in range(max(1, math.ceil(3 * L2_BYTES / (Nn * K * 2))) if M <= 128 else 1)]
+            out = torch.empty(M, Nn, device=dev, dtype=torch.bfloat16)
+            fns = [lambda w_=w_: o.linear(out, x, w_, None, None) for w_ in wts]
+            ms = time_graph(fns, max(4, 2 * len(wts)))
+            flops = 2.0 * M * Nn * K
+            nbytes = Nn * K * 2 + M * K * 2 + M * Nn * 2
+            tf = flops / (ms * 1e-3) / 1e12
+            if M <= 128:
+                report(f"linear {tag} M={M}", nbytes, ms, {"TFLOP/s": round(tf, 2)})
+            else:
+                res[f"linear {tag} M={M}"] = {"us": ms * 1e3, "TFLOP/s": round(tf, 1), "frac_of_bf16": round(tf / tens, 3)}
+            del x, wts, out
+    return res
+
+
+# --------------------------------------------------------------------------------------
+# main arm
+# --------------------------------------------------------------------------------------
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-ops", action="store_true", help="skip the per-op table")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n = world
+    if HKV % n != 0:
+        raise SystemExit(f"--gpus {n}: the 8 KV heads must divide evenly across ranks")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from vllm_nt import oot  # noqa: F401  (the plugin's public surface)
+    from vllm_nt._ntops.torch.attention import decode_workspace_bytes, paged_decode
+
+    peaks, peak_kind = load_peaks()
+    ctx, table, q_all = workload()
+    hkv = HKV // n
+    hq = hkv * (HQ // HKV)
+    h0 = rank * hkv
+    q = q_all[:, h0 * (HQ // HKV) : h0 * (HQ // HKV) + hq].contiguous()
+    gk = torch.Generator(device=dev).manual_seed(1000 + rank)
+    kc = torch.randn(POOL, BLOCK, hkv, HEAD, device=dev, generator=gk, dtype=torch.bfloat16)
+    vc = torch.randn(POOL, BLOCK, hkv, HEAD, device=dev, generator=gk, dtype=torch.bfloat16)
+    qd, sd, td = q.to(dev), ctx.to(dev), table.to(dev)
+    out = torch.empty_like(qd)
+    scale = 1.0 / math.sqrt(HEAD)
+    ws = torch.empty(decode_workspace_bytes(BATCH, hq, hkv, CTX_HI), dtype=torch.uint8, device=dev)
+
+    def step():
+        paged_decode(out, qd, kc, vc, sd, td, scale, CTX_HI, ws)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    ms_max = ms
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+    value = BATCH * args.steps / (ms_max * 1e-3)
+
+    # roofline of this rank's decode call (split + combine launches)
+    algo = decode_bytes(ctx, hkv)
+    achieved = algo / (ms / args.steps * 1e-3) / 1e9
+    traffic = traffic_from_profile()
+    roofline = {
+        "bound": "hbm",
+        "achieved": round(achieved, 1),
+        "peak": peaks["hbm_gbs"],
+        "unit": "GB/s",
+        "frac": round(achieved / peaks["hbm_gbs"], 3),
+        "traffic": traffic * (hkv / HKV) if traffic is not None else None,
+        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+        "algorithmic_bytes_per_launch": algo,
+        "note": "decode call = split kernel + combine kernel, timed together with CUDA events",
+    }
+
+    # e2e: the plugin's public decode entry point with host buffers
+    from vllm_nt.oot import paged_attention_decode
+
+    q_host = q.view(BATCH, 1, hq, HEAD).pin_memory()
+    s_host = ctx.pin_memory()
+    t_host = table.pin_memory()
+    o_host = torch.empty(BATCH, 1, hq, HEAD, dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(10, min(args.steps, 200))
+
+    def e2e_step():
+        qq = q_host.to(dev, non_blocking=True)
+        ss = s_host.to(dev, non_blocking=True)
+        tt = t_host.to(dev, non_blocking=True)
+        res = paged_attention_decode(qq, kc, vc, ss, tt, softmax_scale=scale, max_seq_len=CTX_HI)
+        o_host.copy_(res, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max(e0.elapsed_time(e1), 1e3 * (time.perf_counter() - t0))
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {
+        "value": BATCH * e2e_steps / (e2e_ms * 1e-3),
+        "unit": "tok/s",
+        "h2d_bytes_per_step": q_host.numel() * 2 + s_host.numel() * 4 + t_host.numel() * 4,
+        "d2h_bytes_per_step": o_host.numel() * 2,
+        "steps": e2e_steps,
+        "path": "vllm_nt.oot.paged_attention_decode (pinned host in/out)",
+    }
+
+    per_op = None
+    if rank == 0 and n == 1 and not args.no_ops:
+        del kc, vc, ws
+        torch.cuda.empty_cache()
+        per_op = per_op_table(dev, peaks)
+
+    cpu = None
+    if rank == 0 and n == 1 and not args.no_cpu:
+        torch.set_num_threads(os.cpu_count() or 1)
+        t_one, _, _ = oracle_decode_rate(ctx, q_all, 1, 1)
+        per_call = max(1, min(BATCH, int(4.0 * t_one)))
+        calls = max(1, min(64, int(15.0 / max(per_call / t_one, 1e-3))))
+        v, threads, sample = oracle_decode_rate(ctx, q_all, per_call, calls)
+        cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
+
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": n,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": workload_config(n),
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": 2 * args.steps,  # split + combine per timed step
+        "clocks": clocks,
+        "per_op": per_op,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,175 @@
+/*
+ * ntb200.h -- C ABI of the B200 (sm_100a) operator backend behind the vllm_nt plugin.
+ *
+ * Every entry point takes plain device pointers, element counts and element strides
+ * (strides are in ELEMENTS, never bytes), launches its kernels on `stream` (a
+ * cudaStream_t passed as void*), never synchronises the host, never allocates, and
+ * returns NTB200_OK (0) or a negative NTB200_ERR_* status.  The caller owns all memory;
+ * the only scratch an op needs (split-K partials of the paged decode) is passed in as
+ * `workspace` and sized by the matching *_workspace_size() query.  Nothing here holds a
+ * lock: the per-thread error message is thread-local.
+ *
+ * Each function names the reference (vllm_nt) interface it replaces.  Citations are
+ * paths inside the vllm_nt project.
+ */
+#ifndef NTB200_H_
+#define NTB200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+enum {
+  NTB200_DTYPE_F32 = 0,
+  NTB200_DTYPE_BF16 = 1,
+  NTB200_DTYPE_F16 = 2,
+  NTB200_DTYPE_I32 = 3,
+  NTB200_DTYPE_I64 = 4
+};
+
+/* host-side status codes */
+enum {
+  NTB200_OK = 0,
+  NTB200_ERR_INVALID_ARGUMENT = -1, /* null pointer, negative size, bad stride */
+  NTB200_ERR_UNSUPPORTED_DTYPE = -2,
+  NTB200_ERR_MISALIGNED = -3,       /* pointer/stride not aligned for the vector path */
+  NTB200_ERR_WORKSPACE = -4,        /* workspace missing or too small */
+  NTB200_ERR_CUDA = -5,             /* a CUDA runtime/driver call failed */
+  NTB200_ERR_UNSUPPORTED_SHAPE = -6,
+  NTB200_ERR_DEVICE = -7            /* reported by ntb200_read_device_error */
+};
+
+/* bits of the device-side error word (see ntb200_read_device_error) */
+enum {
+  NTB200_DEVERR_WAIT_TIMEOUT = 1,   /* a bounded mbarrier wait gave up; the kernel returned early */
+  NTB200_DEVERR_INDEX_RANGE = 2     /* an id / slot / block id was out of range and was skipped */
+};
+
+int ntb200_version(void);
+const char* ntb200_status_string(int status);
+/* Detail of the last non-OK status returned on the calling thread. */
+const char* ntb200_last_error(void);
+/* Copies the device error word of the current device into *word (0 = clean) and clears it.
+ * Synchronises `stream`. */
+int ntb200_read_device_error(int* word, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * RMS norm:  out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * weight   (fp32 statistics)
+ * Replaces vllm_nt/_ntops/torch/rms_norm.py:10-33 (_fused_rms_norm_last_dim) and
+ * vllm_nt/_ntops/kernels/fused_rms_norm.py:9-24.  weight may be NULL (all ones).
+ * dtype: F32, BF16 or F16 (x, weight and out share it).
+ */
+int ntb200_rms_norm(void* out, const void* x, const void* weight, int64_t num_rows,
+                    int64_t hidden, int64_t x_row_stride, int64_t out_row_stride, float eps,
+                    int dtype, void* stream);
+
+/* Fused residual add + RMS norm:  s = x + residual (fp32);  residual <- s (rounded to
+ * dtype);  out = s * rsqrt(mean(s^2) + eps) * weight.  out may alias x.
+ * Replaces vllm_nt/_ntops/oot_support.py:32-48 (norm with a residual) which vllm_nt's
+ * RMSNorm hook reaches from vllm_nt/_ntops/patching.py:229-256. */
+int ntb200_fused_add_rms_norm(void* out, void* residual, const void* x, const void* weight,
+                              int64_t num_rows, int64_t hidden, int64_t x_row_stride,
+                              int64_t residual_row_stride, int64_t out_row_stride, float eps,
+                              int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * out[r, i] = silu(x[r, i]) * x[r, d + i],  i < d.
+ * Replaces vllm_nt/_ntops/oot_support.py:51-56 (act_and_mul with nt_silu),
+ * vllm_nt/_ntops/torch/silu.py:7-17 and vllm_nt/_ntops/kernels/silu.py:9-18. */
+int ntb200_silu_and_mul(void* out, const void* x, int64_t num_rows, int64_t d,
+                        int64_t x_row_stride, int64_t out_row_stride, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * In-place NeoX rotary embedding of the first rotary_dim dims of every query/key head:
+ *   c, s = cos_sin_cache[pos][:rot/2], cos_sin_cache[pos][rot/2:rot]
+ *   x1' = x1*c - x2*s ;  x2' = x2*c + x1*s
+ * key may be NULL.  positions: I64 or I32.  cos_sin_cache [num_cache_rows, >= rotary_dim]
+ * has the dtype of query/key.  A token whose position is outside [0, num_cache_rows) is
+ * left untouched and sets NTB200_DEVERR_INDEX_RANGE.
+ * Replaces vllm_nt/_ntops/oot_support.py:134-204 (rope/_apply_rotary),
+ * vllm_nt/_ntops/torch/rotary_emb.py:7-9 and vllm_nt/_ntops/kernels/rotary_emb.py:6-37. */
+int ntb200_rotary_embedding_neox(const void* positions, int positions_dtype, void* query,
+                                 void* key, const void* cos_sin_cache, int64_t num_tokens,
+                                 int64_t num_q_heads, int64_t num_k_heads, int64_t head_size,
+                                 int64_t rotary_dim, int64_t q_token_stride,
+                                 int64_t q_head_stride, int64_t k_token_stride,
+                                 int64_t k_head_stride, int64_t cache_row_stride,
+                                 int64_t num_cache_rows, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Paged KV-cache store (slot-mapped scatter; bit-exact copy):
+ *   for t with slot = slot_mapping[t] >= 0:
+ *     key_cache  [slot / block_size, slot % block_size, h, :] = key  [t, h, :]
+ *     value_cache[slot / block_size, slot % block_size, h, :] = value[t, h, :]
+ * Negative slots (vLLM padding) are skipped; slots >= num_slots are skipped and set
+ * NTB200_DEVERR_INDEX_RANGE.  Both caches share the strides given.  elem_bytes: 1, 2 or 4.
+ * slot_dtype: I64 or I32.
+ * Replaces vllm_nt/_ntops/torch/kv_cache.py:7-21 (store_kvcache) and
+ * vllm_nt/_ntops/kernels/kv_cache.py:4-45. */
+int ntb200_reshape_and_cache(const void* key, const void* value, void* key_cache,
+                             void* value_cache, const void* slot_mapping, int slot_dtype,
+                             int64_t num_tokens, int64_t num_heads, int64_t head_size,
+                             int64_t block_size, int64_t num_slots, int64_t key_token_stride,
+                             int64_t key_head_stride, int64_t value_token_stride,
+                             int64_t value_head_stride, int64_t cache_block_stride,
+                             int64_t cache_page_stride, int64_t cache_head_stride,
+                             int elem_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Embedding gather (bit-exact copy): out[t, :] = weight[ids[t], :].
+ * Ids outside [0, num_embeddings) produce a zero row and set NTB200_DEVERR_INDEX_RANGE.
+ * ids_dtype: I64 or I32.  elem_bytes: 1, 2 or 4.
+ * Replaces vllm_nt/_ntops/torch/embedding.py:7-30 and vllm_nt/_ntops/kernels/wpe.py:11-67
+ * (reached from vllm_nt/_ntops/patching.py:2661-2679). */
+int ntb200_embedding(void* out, const void* ids, int ids_dtype, const void* weight,
+                     int64_t num_tokens, int64_t num_embeddings, int64_t embedding_dim,
+                     int64_t weight_row_stride, int64_t out_row_stride, int elem_bytes,
+                     void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Paged-attention decode (one query token per sequence), split-K over KV blocks:
+ *   out[b, h] = softmax(scale * q[b, h] . K_b^T) V_b  over the seq_lens[b] cached tokens of
+ *   sequence b, K/V head = h / (num_q_heads / num_kv_heads).  fp32 softmax/accumulate.
+ * Cache layout [num_blocks, block_size, num_kv_heads, head_size] (vLLM flash layout, one
+ * of K/V); block_tables [num_seqs, block_table_stride] int32; seq_lens [num_seqs] int32.
+ * max_seq_len bounds every seq_lens[b] (<= 0: derived from max_blocks_per_seq).
+ * dtype BF16 or F16; head_size 128; block_size 16 (the decode kernel's tile shape).
+ * workspace: ntb200_paged_attention_decode_workspace_size(...) bytes, 256-byte aligned.
+ * Sequences with seq_lens[b] == 0 produce zeros.
+ * Replaces vllm_nt/_ntops/torch/attention.py:51-77 (flash_attn_with_kvcache) and
+ * vllm_nt/_ntops/kernels/attention.py:97-197 (KvCache), reached from
+ * vllm_nt/_ntops/oot_support.py:112-123. */
+size_t ntb200_paged_attention_decode_workspace_size(int64_t num_seqs, int64_t num_q_heads,
+                                                    int64_t num_kv_heads, int64_t head_size,
+                                                    int64_t block_size, int64_t max_seq_len);
+int ntb200_paged_attention_decode(
+    void* out, const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* seq_lens, const int32_t* block_tables, int64_t num_seqs,
+    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size,
+    int64_t num_blocks, int64_t max_blocks_per_seq, int64_t block_table_stride,
+    int64_t max_seq_len, float scale, int64_t q_seq_stride, int64_t q_head_stride,
+    int64_t out_seq_stride, int64_t out_head_stride, int64_t cache_block_stride,
+    int64_t cache_page_stride, int64_t cache_head_stride, void* workspace,
+    size_t workspace_bytes, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Dense projection  out[M, N] = x[M, K] . weight[N, K]^T (+ bias[N]),  fp32 accumulate,
+ * tcgen05/TMEM tensor cores fed by TMA.  dtype BF16 or F16; K a multiple of 8, rows 16-byte
+ * aligned.  bias may be NULL.
+ * Replaces vllm_nt/_ntops/torch/linear.py:7-21 and vllm_nt/_ntops/kernels/linear.py:9-85
+ * (reached from vllm_nt/_ntops/oot_support.py:59-65). */
+size_t ntb200_linear_workspace_size(int64_t M, int64_t N, int64_t K);
+int ntb200_linear(void* out, const void* x, const void* weight, const void* bias, int64_t M,
+                  int64_t N, int64_t K, int64_t x_row_stride, int64_t weight_row_stride,
+                  int64_t out_row_stride, void* workspace, size_t workspace_bytes, int dtype,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NTB200_H_ */

@@ -1,0 +1,36 @@
+"""oracle -- TEST INFRASTRUCTURE ONLY.
+
+CPU restatements of the seven hooked decoder ops, used as the checker of the sm_100a
+kernels: by tests/, by ``__graft_entry__.smoke()`` and by ``bench.py``'s cpu_baseline /
+``--impl reference`` legs.  No product code imports this package; the plugin has no CPU
+fallback.
+
+What each function restates (citations: ``vllm:`` = vLLM 0.22 sources, the host framework
+the plugin patches; other paths are inside the vllm_nt reference project):
+
+* floating-point ops follow vLLM's torch-native implementations -- the oracle named for
+  parity -- with the same fp32 intermediates and the same rounding points to the storage
+  dtype;
+* the KV-cache store and the embedding gather are byte copies (numpy on raw 16-bit views),
+  exact;
+* paged decode follows the reference's own test oracle (gather the cached tokens through
+  the block table, fp32 softmax attention per sequence, GQA by head grouping).
+
+Pinning: tests/golden/make_golden.py runs vLLM's real forward_native code (and torch's
+scaled_dot_product_attention for decode) on seeded inputs and commits the outputs;
+tests/test_oracle.py checks these functions against those fixtures and against the
+known-answer cases of the reference's tests (tests/test_kv_cache.py:26-45,
+tests/test_rope.py:26-46, tests/test_attention.py:75-104, tests/test_oot.py:33-177).
+"""
+
+from oracle.ops import (  # noqa: F401
+    build_cos_sin_cache,
+    embedding,
+    fused_add_rms_norm,
+    linear,
+    paged_decode,
+    reshape_and_cache,
+    rms_norm,
+    rope_neox,
+    silu_and_mul,
+)

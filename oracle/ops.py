@@ -1,0 +1,198 @@
+"""CPU restatements of the hooked ops (test infrastructure; see oracle/__init__.py).
+
+All functions take and return CPU tensors / numpy arrays; nothing here touches a GPU."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+
+def _round(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """fp32 -> storage dtype -> fp32 (round-to-nearest-even), a torch op's rounding point."""
+    return t.to(dtype).to(torch.float32)
+
+
+# --------------------------------------------------------------------------------------
+# RMS norm  (vllm:ir/ops/layernorm.py:10-62; vllm_nt/_ntops/oot_support.py:32-48)
+# --------------------------------------------------------------------------------------
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor | None, eps: float) -> torch.Tensor:
+    """x * rsqrt(mean(x^2) + eps) in fp32; normalised value rounded to the weight dtype,
+    multiplied by the weight, rounded to x's dtype."""
+    dtype = x.dtype
+    xf = x.to(torch.float32)
+    var = xf.pow(2).mean(dim=-1, keepdim=True)
+    y = xf * torch.rsqrt(var + eps)
+    if weight is not None:
+        y = _round(y, weight.dtype) * weight.to(torch.float32)
+    return y.to(dtype)
+
+
+def fused_add_rms_norm(
+    x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor | None, eps: float
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """s = x + residual in fp32; returns (rms_norm of the fp32 s, s rounded to x's dtype).
+
+    (vLLM adds in fp32, vllm:ir/ops/layernorm.py:40-62; the reference's adapter adds in the
+    input dtype first, vllm_nt/_ntops/oot_support.py:39-41 -- parity is defined against
+    vLLM's native path.)"""
+    dtype = x.dtype
+    s = x.to(torch.float32) + residual.to(torch.float32)
+    new_residual = s.to(dtype)
+    var = s.pow(2).mean(dim=-1, keepdim=True)
+    y = s * torch.rsqrt(var + eps)
+    if weight is not None:
+        y = _round(y, weight.dtype) * weight.to(torch.float32)
+    return y.to(dtype), new_residual
+
+
+# --------------------------------------------------------------------------------------
+# SiluAndMul  (vllm:model_executor/layers/activation.py:137-141;
+#              vllm_nt/_ntops/oot_support.py:51-56, vllm_nt/_ntops/kernels/silu.py:9-18)
+# --------------------------------------------------------------------------------------
+
+
+def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
+    """silu(gate) rounded to x's dtype, times up, rounded again."""
+    d = x.shape[-1] // 2
+    g = x[..., :d].to(torch.float32)
+    u = x[..., d:].to(torch.float32)
+    a = _round(g / (1.0 + torch.exp(-g)), x.dtype)
+    return (a * u).to(x.dtype)
+
+
+# --------------------------------------------------------------------------------------
+# NeoX RoPE  (vllm:model_executor/layers/rotary_embedding/base.py:69-92 (cache),
+#             base.py:140-180 + common.py:144-183 (apply);
+#             vllm_nt/_ntops/oot_support.py:134-204, vllm_nt/_ntops/kernels/rotary_emb.py:6-37)
+# --------------------------------------------------------------------------------------
+
+
+def build_cos_sin_cache(rotary_dim: int, max_position: int, base: float) -> torch.Tensor:
+    """[max_position, rotary_dim] fp32 table cat(cos, sin) of position * inv_freq."""
+    inv_freq = 1.0 / (base ** (torch.arange(0, rotary_dim, 2, dtype=torch.float32) / rotary_dim))
+    t = torch.arange(max_position, dtype=torch.float32)
+    freqs = torch.einsum("i,j->ij", t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1)
+
+
+def rope_neox(
+    positions: torch.Tensor,
+    query: torch.Tensor,
+    key: torch.Tensor | None,
+    cos_sin_cache: torch.Tensor,
+    head_size: int,
+    rotary_dim: int,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Returns rotated copies of query/key ([tokens, heads*head_size] or 3-D).  Each torch
+    op of the native path is one rounding point: x1*c, x2*s, their difference, ..."""
+
+    def rot(x: torch.Tensor) -> torch.Tensor:
+        dtype = x.dtype
+        n = positions.numel()
+        cs = cos_sin_cache.index_select(0, positions.reshape(-1).long()).to(dtype)
+        c = cs[:, : rotary_dim // 2].to(torch.float32).unsqueeze(1)
+        s = cs[:, rotary_dim // 2 : rotary_dim].to(torch.float32).unsqueeze(1)
+        v = x.reshape(n, -1, head_size)
+        r = v[..., :rotary_dim].to(torch.float32)
+        x1, x2 = r[..., : rotary_dim // 2], r[..., rotary_dim // 2 :]
+        o1 = (_round(x1 * c, dtype) - _round(x2 * s, dtype)).to(dtype)
+        o2 = (_round(x2 * c, dtype) + _round(x1 * s, dtype)).to(dtype)
+        out = v.clone()
+        out[..., : rotary_dim // 2] = o1
+        out[..., rotary_dim // 2 : rotary_dim] = o2
+        return out.reshape(x.shape)
+
+    return rot(query), (rot(key) if key is not None else None)
+
+
+# --------------------------------------------------------------------------------------
+# KV-cache store  (vllm_nt/_ntops/kernels/kv_cache.py:4-45, vllm_nt/_ntops/torch/kv_cache.py:7-21;
+#                  negative padding slots skipped as vllm_nt/_ntops/patching.py:1752-1770 does)
+# --------------------------------------------------------------------------------------
+
+
+def reshape_and_cache(
+    key: np.ndarray,
+    value: np.ndarray,
+    key_cache: np.ndarray,
+    value_cache: np.ndarray,
+    slot_mapping: np.ndarray,
+) -> None:
+    """In place on numpy arrays: cache[slot // bs, slot % bs] = key[t] for slot >= 0.
+    key/value [T, H, D]; caches [blocks, bs, H, D]; any element type (a byte copy)."""
+    bs = key_cache.shape[1]
+    slots = np.asarray(slot_mapping).reshape(-1).astype(np.int64)
+    t = np.nonzero(slots >= 0)[0]
+    s = slots[t]
+    key_cache[s // bs, s % bs] = key[t]
+    value_cache[s // bs, s % bs] = value[t]
+
+
+# --------------------------------------------------------------------------------------
+# Embedding  (vllm_nt/_ntops/kernels/wpe.py:11-67, vllm_nt/_ntops/torch/embedding.py:7-30;
+#             vllm:model_executor/layers/vocab_parallel_embedding.py:77-78 = F.embedding)
+# --------------------------------------------------------------------------------------
+
+
+def embedding(ids: np.ndarray, weight: np.ndarray) -> np.ndarray:
+    """weight[ids] (a row gather, exact)."""
+    return weight[np.asarray(ids).astype(np.int64)]
+
+
+# --------------------------------------------------------------------------------------
+# Paged decode  (vllm_nt/tests/test_attention.py:41-102 -- the reference's oracle for
+#                vllm_nt/_ntops/kernels/attention.py:97-197)
+# --------------------------------------------------------------------------------------
+
+
+def paged_decode(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    seq_lens: torch.Tensor,
+    block_table: torch.Tensor,
+    scale: float | None = None,
+    seqs: list[int] | None = None,
+) -> torch.Tensor:
+    """query [B, Hq, D]; caches [blocks, bs, Hkv, D]; returns fp32 [B, Hq, D] (rows of
+    sequences outside ``seqs`` are left zero).  For each sequence: gather its first
+    seq_len cached tokens block by block, s = scale * q . k in fp32, softmax, o = p . v.
+    A sequence with no cached tokens yields zeros."""
+    b_total, hq, d = query.shape
+    hkv = key_cache.shape[2]
+    bs = key_cache.shape[1]
+    group = hq // hkv
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    out = torch.zeros((b_total, hq, d), dtype=torch.float32)
+    for b in range(b_total) if seqs is None else seqs:
+        n = int(seq_lens[b])
+        if n <= 0:
+            continue
+        nblk = (n + bs - 1) // bs
+        ids = block_table[b, :nblk].long()
+        k = key_cache[ids].reshape(nblk * bs, hkv, d)[:n].to(torch.float32)  # [n, Hkv, D]
+        v = value_cache[ids].reshape(nblk * bs, hkv, d)[:n].to(torch.float32)
+        q = query[b].to(torch.float32).reshape(hkv, group, d)
+        s = torch.einsum("hgd,nhd->hgn", q, k) * scale
+        p = torch.softmax(s, dim=-1)
+        out[b] = torch.einsum("hgn,nhd->hgd", p, v).reshape(hq, d)
+    return out
+
+
+# --------------------------------------------------------------------------------------
+# Dense projection  (vllm_nt/_ntops/kernels/linear.py:9-85; vllm:model_executor/layers/utils.py
+#                    -> F.linear)
+# --------------------------------------------------------------------------------------
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """x @ weight^T (+ bias) with fp32 inputs and accumulation; returns fp32."""
+    y = x.to(torch.float32) @ weight.to(torch.float32).t()
+    if bias is not None:
+        y = y + bias.to(torch.float32)
+    return y

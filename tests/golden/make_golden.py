@@ -1,0 +1,132 @@
+"""Generates tests/golden/*.npz: small seeded inputs and the outputs of the REAL reference
+implementations, used to pin the CPU oracle (oracle/ops.py).
+
+Run here (CPU, vLLM 0.22 importable):  python tests/golden/make_golden.py
+
+Sources of truth per op:
+  rms_norm / fused_add_rms_norm  vllm.ir.ops.rms_norm / fused_add_rms_norm (native)
+  silu_and_mul                   vllm SiluAndMul.forward_native
+  rope (NeoX)                    vllm RotaryEmbedding.forward_static with the cache of
+                                 RotaryEmbeddingBase._compute_cos_sin_cache
+  kv store                       torch index_put at [slot // bs, slot % bs], slot < 0 skipped
+                                 (the reference's torch store, vllm_nt/_ntops/patching.py:1752-1770)
+  embedding                      torch.nn.functional.embedding
+  paged decode                   gather + torch scaled_dot_product_attention per sequence
+                                 (the reference's oracle, vllm_nt/tests/test_attention.py:41-102)
+  linear                         torch.nn.functional.linear in fp32
+bf16 tensors are stored as their uint16 bit patterns (key suffix ``__bf16``).
+"""
+
+from __future__ import annotations
+
+import math
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+OUT = Path(__file__).resolve().parent
+
+
+def _np(t: torch.Tensor) -> tuple[str, np.ndarray]:
+    if t.dtype == torch.bfloat16:
+        return "__bf16", t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    return "", t.contiguous().numpy()
+
+
+def save(name: str, **tensors: torch.Tensor) -> None:
+    arrays = {}
+    for key, t in tensors.items():
+        suffix, arr = _np(t)
+        arrays[key + suffix] = arr
+    np.savez_compressed(OUT / f"{name}.npz", **arrays)
+
+
+def main() -> None:
+    from vllm import ir
+    from vllm.model_executor.layers.activation import SiluAndMul
+    from vllm.model_executor.layers.rotary_embedding.base import RotaryEmbedding, RotaryEmbeddingBase
+
+    g = torch.Generator().manual_seed(20261201)
+
+    for dtype, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        x = torch.randn(4, 512, generator=g).to(dtype)
+        r = torch.randn(4, 512, generator=g).to(dtype)
+        w = (1.0 + 0.1 * torch.randn(512, generator=g)).to(dtype)
+        y, res = ir.ops.fused_add_rms_norm(x.clone(), r.clone(), w, 1e-6)
+        y0 = ir.ops.rms_norm(x.clone(), w, 1e-6)
+        save(f"rms_norm_{tag}", x=x, residual=r, weight=w, out=y, residual_out=res, out_plain=y0)
+
+        xs = torch.randn(4, 2 * 256, generator=g).to(dtype)
+        save(f"silu_and_mul_{tag}", x=xs, out=SiluAndMul.forward_native(xs.clone()))
+
+        head, rot, max_pos, base = 64, 64, 128, 10000.0
+        cache = RotaryEmbeddingBase._compute_cos_sin_cache(
+            type("C", (), {"rotary_dim": rot, "base": base, "max_position_embeddings": max_pos,
+                           "_compute_inv_freq": lambda self, b: RotaryEmbeddingBase._compute_inv_freq(self, b)})()
+        )
+        pos = torch.randint(0, max_pos, (6,), generator=g)
+        q = torch.randn(6, 4 * head, generator=g).to(dtype)
+        k = torch.randn(6, 2 * head, generator=g).to(dtype)
+        qo, ko = RotaryEmbedding.forward_static(pos, q.clone(), k.clone(), head, rot, cache.to(dtype), True)
+        # partial rotary (rotary_dim 32 < head_size 64): a 32-wide cos|sin table
+        cache32 = torch.cat((cache[:, :16], cache[:, 32:48]), dim=-1)
+        qp, kp = RotaryEmbedding.forward_static(pos, q.clone(), k.clone(), head, 32, cache32.to(dtype), True)
+        save(f"rope_{tag}", positions=pos, query=q, key=k, cos_sin_cache=cache, query_out=qo, key_out=ko,
+             cos_sin_cache_rot32=cache32, query_out_rot32=qp, key_out_rot32=kp)
+
+        xl = torch.randn(5, 32, generator=g).to(dtype)
+        wl = (0.02 * torch.randn(12, 32, generator=g)).to(dtype)
+        bl = torch.randn(12, generator=g).to(dtype)
+        save(f"linear_{tag}", x=xl, weight=wl, bias=bl,
+             out=F.linear(xl.float(), wl.float(), bl.float()))
+
+    # KV store (bf16, byte copy)
+    key = torch.randn(5, 2, 16, generator=g).to(torch.bfloat16)
+    value = torch.randn(5, 2, 16, generator=g).to(torch.bfloat16)
+    kc = torch.zeros(8, 4, 2, 16, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    slots = torch.tensor([3, -1, 17, 30, 8], dtype=torch.int64)
+    valid = slots >= 0
+    s = slots[valid]
+    kc2, vc2 = kc.clone(), vc.clone()
+    kc2[s // 4, s % 4] = key[valid]
+    vc2[s // 4, s % 4] = value[valid]
+    save("kv_store_bf16", key=key, value=value, slot_mapping=slots, key_cache_out=kc2, value_cache_out=vc2)
+
+    # embedding
+    wt = torch.randn(32, 16, generator=g).to(torch.bfloat16)
+    ids = torch.tensor([[0, 3, 7], [4, 1, 31]], dtype=torch.int64)
+    save("embedding_bf16", weight=wt, ids=ids, out=F.embedding(ids, wt))
+
+    # paged decode: B=3, Hq=4, Hkv=2, D=16, bs=4, ctx [1, 5, 9]
+    hq, hkv, d, bs, nb = 4, 2, 16, 4, 12
+    qd = torch.randn(3, hq, d, generator=g).to(torch.bfloat16)
+    kcd = torch.randn(nb, bs, hkv, d, generator=g).to(torch.bfloat16)
+    vcd = torch.randn(nb, bs, hkv, d, generator=g).to(torch.bfloat16)
+    seq = torch.tensor([1, 5, 9], dtype=torch.int32)
+    table = torch.randperm(nb, generator=g)[:9].reshape(3, 3).to(torch.int32)
+    outs = []
+    for b in range(3):
+        n = int(seq[b])
+        ks, vs, rem = [], [], n
+        for blk in table[b].tolist():
+            if rem <= 0:
+                break
+            take = min(bs, rem)
+            ks.append(kcd[blk, :take])
+            vs.append(vcd[blk, :take])
+            rem -= take
+        kk = torch.cat(ks).float().transpose(0, 1).repeat_interleave(hq // hkv, dim=0).unsqueeze(0)
+        vv = torch.cat(vs).float().transpose(0, 1).repeat_interleave(hq // hkv, dim=0).unsqueeze(0)
+        qq = qd[b].float().unsqueeze(0).unsqueeze(2)  # [1, Hq, 1, D]
+        o = F.scaled_dot_product_attention(qq, kk, vv, scale=1.0 / math.sqrt(d))
+        outs.append(o[0, :, 0, :])
+    save("paged_decode_bf16", query=qd, key_cache=kcd, value_cache=vcd, seq_lens=seq, block_table=table,
+         out=torch.stack(outs))
+    print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,87 @@
+"""The C-ABI library loads and exports every entry point include/ntb200.h declares, and
+its host-side argument checks reject bad calls before touching a device.  CPU only (no
+kernel is launched)."""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from vllm_nt._ntops import capi
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "ntb200.h"
+
+
+def declared_functions() -> set[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return set(re.findall(r"\b(ntb200_\w+)\s*\(", text))
+
+
+def test_header_declarations_are_all_exported():
+    names = declared_functions()
+    assert {"ntb200_rms_norm", "ntb200_paged_attention_decode", "ntb200_linear"} <= names
+    out = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIBRARY)], capture_output=True, text=True, check=True)
+    exported = set(re.findall(r"\bT (ntb200_\w+)", out.stdout))
+    assert names <= exported, names - exported
+
+
+def test_ctypes_view_covers_the_header():
+    assert declared_functions() == set(capi.SIGNATURES)
+    lib = capi.lib()
+    for name in capi.SIGNATURES:
+        assert hasattr(lib, name)
+
+
+def test_status_strings_and_version():
+    lib = capi.lib()
+    assert lib.ntb200_version() >= 1
+    assert lib.ntb200_status_string(0) == b"ok"
+    assert lib.ntb200_status_string(-4).startswith(b"workspace")
+
+
+@pytest.mark.parametrize(
+    "name,args,status",
+    [
+        ("ntb200_rms_norm", (1, 1, None, -1, 8, 8, 8, 1e-6, 0, None), -1),
+        ("ntb200_rms_norm", (1, 1, None, 4, 8, 8, 8, 1e-6, 9, None), -2),
+        ("ntb200_fused_add_rms_norm", (1, None, 1, None, 4, 8, 8, 8, 8, 1e-6, 1, None), -1),
+        ("ntb200_silu_and_mul", (1, 1, 4, 8, 16, 8, 7, None), -2),
+        ("ntb200_silu_and_mul", (1, 1, 4, 8, 8, 8, 1, None), -1),
+        ("ntb200_rotary_embedding_neox", (1, 4, 1, None, 1, 4, 2, 0, 64, 63, 128, 64, 0, 0, 64, 10, 1, None), -1),
+        ("ntb200_reshape_and_cache", (1, 1, 1, 1, 1, 4, 4, 2, 128, 16, 64, 256, 128, 256, 128, 4096, 256, 128, 3, None), -2),
+        ("ntb200_embedding", (1, 1, 4, 1, 4, 10, 16, 8, 16, 2, None), -1),
+        ("ntb200_linear", (1, 1, 1, None, 4, 8, 16, 16, 16, 8, None, 0, 0, None), -2),
+        ("ntb200_paged_attention_decode",
+         (1, 1, 1, 1, 1, 1, 2, 4, 1, 64, 16, 8, 4, 4, 64, 0.1, 512, 128, 512, 128, 2048, 128, 128, None, 0, 1, None), -6),
+        ("ntb200_paged_attention_decode",
+         (1, 1, 1, 1, 1, 1, 2, 36, 4, 128, 16, 8, 4, 4, 64, 0.1, 512, 128, 512, 128, 2048, 128, 128, None, 0, 1, None), -6),
+    ],
+)
+def test_host_validation_rejects_before_launch(name, args, status):
+    with pytest.raises(capi.NtB200Error) as e:
+        capi.call(name, *args)
+    assert e.value.status == status
+    assert capi.lib().ntb200_last_error()  # a detail message was recorded
+
+
+def test_zero_sized_calls_are_no_ops():
+    assert capi.call("ntb200_rms_norm", 1, 1, None, 0, 8, 8, 8, 1e-6, 0, None) == 0
+    assert capi.call("ntb200_silu_and_mul", 1, 1, 0, 8, 16, 8, 1, None) == 0
+    assert capi.call("ntb200_linear", 1, 1, 1, None, 0, 8, 16, 16, 16, 8, None, 0, 1, None) == 0
+
+
+def test_workspace_queries():
+    lib = capi.lib()
+    ws = lib.ntb200_paged_attention_decode_workspace_size(256, 32, 8, 128, 16, 8192)
+    # 256 seqs x 32 heads x 8 chunks of 1024 tokens x (128 fp32 partials + 1 lse), 256-aligned
+    assert ws == 256 * 32 * 8 * 128 * 4 + 256 * 32 * 8 * 4
+    assert lib.ntb200_paged_attention_decode_workspace_size(256, 32, 8, 64, 16, 8192) == 0
+    assert lib.ntb200_linear_workspace_size(1, 4096, 4096) == 0
+
+
+def test_read_device_error_rejects_null():
+    with pytest.raises(capi.NtB200Error):
+        capi.call("ntb200_read_device_error", ctypes.POINTER(ctypes.c_int)(), None)

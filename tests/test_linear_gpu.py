@@ -1,0 +1,112 @@
+"""GPU parity of the tcgen05 GEMM: out = x W^T (+ bias), bf16/f16 in, fp32 accumulate.
+
+Small M is checked against the CPU oracle; for M >= 1024 the reference is a torch fp32
+matmul on the GPU with TF32 disabled (a floating-point kernel's fp32 reference).
+Tolerance 2e-2 (rtol = atol) on the 16-bit output."""
+
+import pytest
+import torch
+
+import oracle
+from _util import cuda_device, dtype_code, ptr, seeded, stream
+from vllm_nt._ntops import capi
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+SHAPES = [(4096, 6144), (4096, 4096), (4096, 28672), (14336, 4096)]
+
+
+@pytest.fixture(autouse=True)
+def _setup():
+    cuda_device()
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    capi.read_device_error(stream())
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    torch.cuda.synchronize()
+    assert capi.read_device_error(stream()) == 0
+
+
+def _inputs(m, k, n, seed, dtype=torch.bfloat16, bias=False):
+    g = seeded(seed)
+    x = torch.randn(m, k, generator=g).to(dtype)
+    w = (0.02 * torch.randn(n, k, generator=g)).to(dtype)
+    b = torch.randn(n, generator=g).to(dtype) if bias else None
+    return x, w, b
+
+
+def _ntb200_linear(x, w, b=None):
+    from vllm_nt._ntops.torch.linear import linear
+
+    return linear(x, w, b)
+
+
+@pytest.mark.parametrize("k,n", SHAPES)
+@pytest.mark.parametrize("m", [1, 16, 128])
+def test_linear_small_m_vs_oracle(m, k, n):
+    x, w, _ = _inputs(m, k, n, seed=m + k + n)
+    out = _ntb200_linear(x.cuda(), w.cuda())
+    torch.testing.assert_close(out.float().cpu(), oracle.linear(x, w), rtol=TOL, atol=TOL)
+
+
+@pytest.mark.parametrize("k,n", SHAPES)
+def test_linear_m1024_vs_fp32(k, n):
+    x, w, _ = _inputs(1024, k, n, seed=k + n)
+    xd, wd = x.cuda(), w.cuda()
+    ref = xd.float() @ wd.float().t()
+    torch.testing.assert_close(_ntb200_linear(xd, wd).float(), ref, rtol=TOL, atol=TOL)
+
+
+def test_linear_m8192_gate_up_row_subset():
+    dev = cuda_device()
+    gd = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(8192, 4096, generator=gd, device=dev, dtype=torch.bfloat16)
+    w = 0.02 * torch.randn(28672, 4096, generator=gd, device=dev, dtype=torch.bfloat16)
+    out = _ntb200_linear(x, w)
+    rows = torch.randperm(8192, generator=seeded(4))[:96].to(dev)
+    ref = x[rows].float() @ w.float().t()
+    torch.testing.assert_close(out[rows].float(), ref, rtol=TOL, atol=TOL)
+
+
+@pytest.mark.parametrize("m,k,n", [(200, 72, 300), (5, 32, 12), (129, 4096, 257), (1, 8, 8)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_linear_tails_and_bias_capi(m, k, n, dtype):
+    x, w, b = _inputs(m, k, n, seed=m * 7 + n, dtype=dtype, bias=True)
+    xd, wd, bd = x.cuda(), w.cuda(), b.cuda()
+    out = torch.full((m, n), 3.0, dtype=dtype, device="cuda")
+    capi.call("ntb200_linear", ptr(out), ptr(xd), ptr(wd), ptr(bd), m, n, k, k, k, n, None, 0,
+              dtype_code(dtype), stream())
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.float().cpu(), oracle.linear(x, w, b), rtol=TOL, atol=TOL)
+
+
+def test_linear_strided_output_and_reference_cases():
+    """vllm_nt/tests/test_oot.py:121-162: matmul (64x128)(128x32) and linear with bias on
+    (2,3,16) x (8,16)."""
+    from vllm_nt._ntops.oot_support import linear
+    from vllm_nt._ntops.torch.linear import matmul
+
+    for dtype in (torch.float16, torch.bfloat16):
+        g = seeded(5)
+        lhs = torch.randn(64, 128, generator=g).to(dtype)
+        rhs = torch.randn(128, 32, generator=g).to(dtype)
+        torch.testing.assert_close(matmul(lhs.cuda(), rhs.cuda()).float().cpu(), lhs.float() @ rhs.float(),
+                                   rtol=5e-2, atol=5e-2)
+        x = torch.randn(2, 3, 16, generator=g).to(dtype)
+        w = torch.randn(8, 16, generator=g).to(dtype)
+        b = torch.randn(8, generator=g).to(dtype)
+        ref = torch.nn.functional.linear(x.float(), w.float(), b.float())
+        torch.testing.assert_close(linear(x.cuda(), w.cuda(), b.cuda()).float().cpu(), ref, rtol=5e-2, atol=5e-2)
+
+
+def test_linear_rejects_unaligned_and_fp32():
+    x = torch.randn(4, 12, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(8, 12, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(4, 8, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(capi.NtB200Error) as e:  # row stride 12 elements = 24 bytes: not 16-aligned
+        capi.call("ntb200_linear", ptr(out), ptr(x), ptr(w), None, 4, 8, 12, 12, 12, 8, None, 0, 1, stream())
+    assert e.value.status == -3
+    with pytest.raises(capi.NtB200Error) as e:
+        capi.call("ntb200_linear", ptr(out), ptr(x), ptr(w), None, 4, 8, 12, 12, 12, 8, None, 0, 0, stream())
+    assert e.value.status == -2

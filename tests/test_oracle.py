@@ -1,0 +1,150 @@
+"""Pins the CPU oracle against (a) golden outputs of the real reference implementations
+(tests/golden/make_golden.py) and (b) the known-answer cases of the reference's own tests.
+CPU only."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+from _util import bits_equal, golden, seeded
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_rms_norm_matches_vllm_native(tag):
+    g = golden(f"rms_norm_{tag}")
+    y, res = oracle.fused_add_rms_norm(g["x"], g["residual"], g["weight"], 1e-6)
+    assert bits_equal(res, g["residual_out"])
+    torch.testing.assert_close(y, g["out"], rtol=0, atol=0)
+    torch.testing.assert_close(oracle.rms_norm(g["x"], g["weight"], 1e-6), g["out_plain"], rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_silu_and_mul_matches_vllm_native(tag):
+    g = golden(f"silu_and_mul_{tag}")
+    out = oracle.silu_and_mul(g["x"])
+    tol = 1e-6 if tag == "f32" else 0.0  # exp rounding may differ by an ulp in fp32
+    torch.testing.assert_close(out, g["out"], rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_rope_matches_vllm_forward_static(tag):
+    g = golden(f"rope_{tag}")
+    cache = oracle.build_cos_sin_cache(64, 128, 10000.0)
+    assert bits_equal(cache, g["cos_sin_cache"])
+    qo, ko = oracle.rope_neox(g["positions"], g["query"], g["key"], g["cos_sin_cache"], 64, 64)
+    assert bits_equal(qo, g["query_out"]) and bits_equal(ko, g["key_out"])
+    qp, kp = oracle.rope_neox(g["positions"], g["query"], g["key"], g["cos_sin_cache_rot32"], 64, 32)
+    assert bits_equal(qp, g["query_out_rot32"]) and bits_equal(kp, g["key_out_rot32"])
+
+
+def test_kv_store_matches_reference_torch_store():
+    g = golden("kv_store_bf16")
+    kc = np.zeros((8, 4, 2, 16), dtype=np.uint16)
+    vc = np.zeros_like(kc)
+    k16 = g["key"].view(torch.int16).numpy().view(np.uint16)
+    v16 = g["value"].view(torch.int16).numpy().view(np.uint16)
+    oracle.reshape_and_cache(k16, v16, kc, vc, g["slot_mapping"].numpy())
+    assert np.array_equal(kc, g["key_cache_out"].view(torch.int16).numpy().view(np.uint16))
+    assert np.array_equal(vc, g["value_cache_out"].view(torch.int16).numpy().view(np.uint16))
+
+
+def test_kv_store_reference_known_answer():
+    """vllm_nt/tests/test_kv_cache.py:26-45: 3 tokens x 2 heads x 4 dims into an 8x8 flat
+    cache at slots [1, 4, 6] (a flat cache is block_size 1)."""
+    rng = np.random.default_rng(0)
+    key = rng.standard_normal((3, 2, 4)).astype(np.float32)
+    value = rng.standard_normal((3, 2, 4)).astype(np.float32)
+    kc = np.zeros((8, 1, 2, 4), np.float32)
+    vc = np.zeros_like(kc)
+    oracle.reshape_and_cache(key, value, kc, vc, np.array([1, 4, 6], np.int32))
+    for t, s in enumerate([1, 4, 6]):
+        assert np.array_equal(kc[s, 0], key[t]) and np.array_equal(vc[s, 0], value[t])
+    assert not kc[[0, 2, 3, 5, 7]].any()
+
+
+def test_embedding_matches_f_embedding():
+    g = golden("embedding_bf16")
+    w16 = g["weight"].view(torch.int16).numpy()
+    out = oracle.embedding(g["ids"].numpy(), w16)
+    assert np.array_equal(out, g["out"].view(torch.int16).numpy())
+
+
+def test_paged_decode_matches_sdpa_golden():
+    g = golden("paged_decode_bf16")
+    out = oracle.paged_decode(g["query"], g["key_cache"], g["value_cache"], g["seq_lens"], g["block_table"])
+    torch.testing.assert_close(out, g["out"], rtol=1e-5, atol=1e-5)
+
+
+def test_paged_decode_reference_known_answer():
+    """vllm_nt/tests/test_attention.py:75-104: q (2,1,2,8), cache (4 blocks, bs 2, 2 heads,
+    8), seqlens [3, 4], tables [[0,1],[2,3]], checked against SDPA over gathered tokens."""
+    g = seeded(1)
+    q = torch.randn((2, 2, 8), generator=g)
+    kc = torch.randn((4, 2, 2, 8), generator=g)
+    vc = torch.randn((4, 2, 2, 8), generator=g)
+    seq = torch.tensor([3, 4], dtype=torch.int32)
+    table = torch.tensor([[0, 1], [2, 3]], dtype=torch.int32)
+    out = oracle.paged_decode(q, kc, vc, seq, table)
+    for b in range(2):
+        n = int(seq[b])
+        k = kc[table[b].long()].reshape(-1, 2, 8)[:n].transpose(0, 1).unsqueeze(0)
+        v = vc[table[b].long()].reshape(-1, 2, 8)[:n].transpose(0, 1).unsqueeze(0)
+        ref = F.scaled_dot_product_attention(q[b].unsqueeze(0).unsqueeze(2), k, v)[0, :, 0]
+        torch.testing.assert_close(out[b], ref, rtol=1e-5, atol=1e-5)
+
+
+def test_paged_decode_empty_sequence_is_zero():
+    q = torch.randn(2, 4, 16)
+    kc = torch.randn(3, 4, 2, 16)
+    out = oracle.paged_decode(q, kc, kc, torch.tensor([0, 2], dtype=torch.int32), torch.tensor([[0], [1]], dtype=torch.int32))
+    assert not out[0].any() and out[1].abs().sum() > 0
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+def test_linear_matches_f_linear(tag):
+    g = golden(f"linear_{tag}")
+    torch.testing.assert_close(oracle.linear(g["x"], g["weight"], g["bias"]), g["out"], rtol=1e-6, atol=1e-6)
+
+
+def test_rope_reference_known_answer():
+    """vllm_nt/tests/test_rope.py:26-46: x (5,4,8), per-token cos/sin (5,1,4); reference
+    cat(x1*cos - x2*sin, x2*cos + x1*sin)."""
+    g = seeded(2)
+    x = torch.randn(5, 4, 8, generator=g)
+    cos = torch.randn(5, 4, generator=g)
+    sin = torch.randn(5, 4, generator=g)
+    table = torch.cat((cos, sin), dim=-1)
+    out, _ = oracle.rope_neox(torch.arange(5), x, None, table, 8, 8)
+    x1, x2 = x[..., :4], x[..., 4:]
+    ref = torch.cat((x1 * cos[:, None] - x2 * sin[:, None], x2 * cos[:, None] + x1 * sin[:, None]), dim=-1)
+    assert bits_equal(out, ref)
+
+
+def test_rms_norm_reference_known_answer():
+    """vllm_nt/tests/test_oot.py:33-77 reference: fp32 statistics, cast back."""
+    g = seeded(3)
+    for shape in [(1, 4096), (32, 4096), (1, 32, 4096)]:
+        x = torch.randn(shape, generator=g)
+        w = torch.randn(shape[-1], generator=g)
+        ref = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * w
+        torch.testing.assert_close(oracle.rms_norm(x, w, 1e-6), ref, rtol=0, atol=0)
+
+
+def test_silu_reference_known_answer():
+    g = seeded(4)
+    for shape in [(1, 8192), (32, 8192), (1, 32, 8192)]:
+        x = torch.randn(shape, generator=g)
+        d = shape[-1] // 2
+        torch.testing.assert_close(oracle.silu_and_mul(x), F.silu(x[..., :d]) * x[..., d:], rtol=1e-6, atol=1e-6)
+
+
+def test_cos_sin_cache_matches_vllm_definition():
+    c = oracle.build_cos_sin_cache(128, 4096, 500000.0)
+    inv = 1.0 / (500000.0 ** (torch.arange(0, 128, 2, dtype=torch.float32) / 128))
+    assert c.shape == (4096, 128)
+    torch.testing.assert_close(c[:, :64], torch.cos(torch.arange(4096).float()[:, None] * inv), rtol=0, atol=0)
+    assert math.isclose(float(c[0, 0]), 1.0)

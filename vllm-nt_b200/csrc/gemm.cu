@@ -1,0 +1,389 @@
+// Dense projection GEMM on the 5th-generation tensor cores:
+//   out[M, N] = x[M, K] . W[N, K]^T (+ bias),  bf16/f16 in, fp32 accumulate in TMEM.
+//
+// Persistent, warp-specialised, one CTA per SM (192 threads):
+//   warp 0      TMA producer: 128x64 x-tile + 256x64 W-tile per k-step (128-byte swizzle,
+//               K-major) into a 4-stage shared-memory ring (48 KB per stage);
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and its lane 0
+//               issues tcgen05.mma (M=128, N=256, K=16; four per k-step), committing each
+//               stage back to the producer and each finished tile to the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
+//               32*(w%4)..+31, i.e. output rows), add bias, round, store.
+// The epilogue of tile i overlaps the MMAs of tile i+1 (double-buffered accumulator).
+// Tiles are walked with the M index fastest so a wave of CTAs shares W tiles through L2
+// while x (M*K*2 bytes) stays L2-resident.  No TMA multicast is used anywhere.
+//
+// Every mbarrier wait is bounded (2 s); a timeout sets NTB200_DEVERR_WAIT_TIMEOUT, the
+// roles leave their loops, in-flight copies and MMAs are drained (bounded), and TMEM is
+// freed before the CTA exits.
+//
+// Replaces vllm_nt/_ntops/kernels/linear.py:9-85 (a Triton tl.dot tile loop).
+#include "common.cuh"
+
+namespace ntb200 {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kATileBytes = BM * BK * 2;
+constexpr int kBTileBytes = BN * BK * 2;
+constexpr int kStageBytes = kATileBytes + kBTileBytes;
+constexpr int kTmemCols = 2 * BN;
+
+struct GemmSmem {
+  static constexpr int kRing = 0;
+  static constexpr int kFull = kStages * kStageBytes;
+  static constexpr int kEmpty = kFull + 8 * kStages;
+  static constexpr int kTmemFull = kEmpty + 8 * kStages;
+  static constexpr int kTmemEmpty = kTmemFull + 16;
+  static constexpr int kMmaDone = kTmemEmpty + 16;
+  static constexpr int kTmemBase = kMmaDone + 8;
+  static constexpr int kEnd = kTmemBase + 8;
+  static constexpr int kDynamicBytes = kEnd + 1024;
+};
+
+// K-major operand tile with 128-byte swizzle: 8-row atoms of 1024 bytes.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);  // start address
+  d |= static_cast<uint64_t>(1) << 16;                  // leading byte offset (unused here)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;          // stride byte offset: 8 rows
+  d |= static_cast<uint64_t>(1) << 46;                  // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;                  // SWIZZLE_128B
+  return d;
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, A/B both bf16 (or both f16),
+// both K-major, shape M x N.
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, int m, int n) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct GemmParams {
+  void* out;
+  const void* bias;
+  int64_t M, N, K;
+  int64_t out_stride;
+  int num_m_blocks, num_n_blocks;
+  unsigned int* err;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
+    const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
+    const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GemmSmem::kFull);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + GemmSmem::kEmpty);
+  uint64_t* tmem_full = reinterpret_cast<uint64_t*>(smem + GemmSmem::kTmemFull);
+  uint64_t* tmem_empty = reinterpret_cast<uint64_t*>(smem + GemmSmem::kTmemEmpty);
+  uint64_t* mma_done = reinterpret_cast<uint64_t*>(smem + GemmSmem::kMmaDone);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + GemmSmem::kTmemBase);
+  const uint32_t ring = smem_u32(smem + GemmSmem::kRing);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+  const int k_steps = static_cast<int>((p.K + BK - 1) / BK);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_base_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a_map)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&b_map)) : "memory");
+      uint32_t it = 0;  // global k-step counter of this CTA
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int mb = tile % p.num_m_blocks;
+        const int nb = tile / p.num_m_blocks;
+        for (int kb = 0; kb < k_steps; ++kb, ++it) {
+          const uint32_t s = it % kStages;
+          if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          const uint32_t a_dst = ring + s * kStageBytes;
+          const uint32_t b_dst = a_dst + kATileBytes;
+          tma_load_2d(a_dst, &a_map, kb * BK, mb * BM, smem_u32(&full[s]));
+          tma_load_2d(b_dst, &b_map, kb * BK, nb * BN, smem_u32(&full[s]));
+        }
+      }
+      // drain the copies still in flight
+      const uint32_t first = it > kStages ? it - kStages : 0;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % kStages], (j / kStages) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value, BM, BN);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const int use = local >> 1;
+        if (use >= 1 && !mbar_wait(&tmem_empty[acc], (use - 1) & 1, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < k_steps; ++kb, ++it) {
+          const uint32_t s = it % kStages;
+          if (!mbar_wait(&full[s], (it / kStages) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = ring + s * kStageBytes;
+          const uint32_t b_addr = a_addr + kATileBytes;
+          const uint64_t adesc = sw128_kmajor_desc(a_addr);
+          const uint64_t bdesc = sw128_kmajor_desc(b_addr);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // advance 16 elements (32 bytes) along K inside the swizzled 128-byte rows
+            umma_f16(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+        }
+        if (!ok) break;
+        umma_commit(&tmem_full[acc]);  // accumulator complete
+      }
+      // all issued MMAs complete before TMEM may be released
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.err);
+    }
+  } else {
+    // ------------------------------ epilogue ------------------------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    T* out = static_cast<T*>(p.out);
+    const T* bias = static_cast<const T*>(p.bias);
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const int use = local >> 1;
+      if (!mbar_wait(&tmem_full[acc], use & 1, p.err)) break;
+      tc_fence_after();
+      const int mb = tile % p.num_m_blocks;
+      const int nb = tile / p.num_m_blocks;
+      const int64_t row = int64_t(mb) * BM + row_in_tile;
+      const int64_t col0 = int64_t(nb) * BN;
+      T* orow = out + row * p.out_stride;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
+        tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + acc * BN + chunk * 32, r);
+        const int64_t c0 = col0 + chunk * 32;
+        if (row < p.M && c0 < p.N) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if (bias != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c0 + i < p.N) v[i] += Elem<T>::to_f(bias[c0 + i]);
+        }
+        if (c0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(orow + c0) & 15u) == 0)) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float w[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[i] = v[q * 8 + i];
+            store_f<T, 8>(orow + c0 + q * 8, w);
+          }
+        } else {
+          for (int i = 0; i < 32 && c0 + i < p.N; ++i) orow[c0 + i] = Elem<T>::from_f(v[i]);
+        }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// rows x K (K contiguous) operand, box = box_rows x 64, 128-byte swizzle
+int make_kmajor_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows, int64_t k,
+                    int64_t row_stride, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return fail(NTB200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(row_stride * 2)};
+  const cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NTB200_ERR_CUDA, "cuTensorMapEncodeTiled (gemm) failed (%d)", int(r));
+  return NTB200_OK;
+}
+
+}  // namespace
+}  // namespace ntb200
+
+extern "C" size_t ntb200_linear_workspace_size(int64_t M, int64_t N, int64_t K) {
+  (void)M;
+  (void)N;
+  (void)K;
+  return 0;
+}
+
+extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const void* bias,
+                             int64_t M, int64_t N, int64_t K, int64_t x_row_stride,
+                             int64_t weight_row_stride, int64_t out_row_stride, void* workspace,
+                             size_t workspace_bytes, int dtype, void* stream) {
+  using namespace ntb200;
+  (void)workspace;
+  (void)workspace_bytes;
+  if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
+    return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "linear: dtype %d (bf16/f16 only)", dtype);
+  if (M < 0 || N < 0 || K <= 0) return fail(NTB200_ERR_INVALID_ARGUMENT, "linear: bad shape");
+  if (M == 0 || N == 0) return NTB200_OK;
+  if (!out || !x || !weight) return fail(NTB200_ERR_INVALID_ARGUMENT, "linear: null pointer");
+  if (x_row_stride < K || weight_row_stride < K || out_row_stride < N)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "linear: row stride too small");
+  if (!aligned16(x) || !aligned16(weight) || x_row_stride % 8 != 0 || weight_row_stride % 8 != 0)
+    return fail(NTB200_ERR_MISALIGNED, "linear: x/weight must be 16-byte aligned with row strides %% 8 == 0");
+  const int64_t mblocks = ceil_div(M, BM), nblocks = ceil_div(N, BN);
+  if (mblocks * nblocks > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
+  const bool bf16 = dtype == NTB200_DTYPE_BF16;
+  CUtensorMap amap, bmap;
+  int st = make_kmajor_map(&amap, x, bf16, M, K, x_row_stride, BM);
+  if (st != NTB200_OK) return st;
+  st = make_kmajor_map(&bmap, weight, bf16, N, K, weight_row_stride, BN);
+  if (st != NTB200_OK) return st;
+
+  GemmParams prm;
+  prm.out = out;
+  prm.bias = bias;
+  prm.M = M;
+  prm.N = N;
+  prm.K = K;
+  prm.out_stride = out_row_stride;
+  prm.num_m_blocks = static_cast<int>(mblocks);
+  prm.num_n_blocks = static_cast<int>(nblocks);
+  prm.err = device_error_word();
+  const int64_t tiles = mblocks * nblocks;
+  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
+  const int smem = GemmSmem::kDynamicBytes;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bf16) {
+    st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__nv_bfloat16>), smem, 2);
+    if (st != NTB200_OK) return st;
+    gemm_tcgen05_kernel<__nv_bfloat16><<<grid, kThreads, smem, s>>>(amap, bmap, prm);
+  } else {
+    st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__half>), smem, 3);
+    if (st != NTB200_OK) return st;
+    gemm_tcgen05_kernel<__half><<<grid, kThreads, smem, s>>>(amap, bmap, prm);
+  }
+  return check_launch("linear");
+}

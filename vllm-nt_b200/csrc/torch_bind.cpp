@@ -1,0 +1,292 @@
+// torch.ops.ntb200.* -- a thin binding from torch tensors to the libntb200 C ABI.
+//
+// Every op writes into caller-allocated outputs (schemas mark them mutable), runs on the
+// current CUDA stream of the tensors' device, and turns a non-zero C-ABI status into a
+// c10::Error carrying the status string and detail.  There is no CPU implementation: a
+// CPU tensor reaching these ops is an error, never a silent fallback.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include "ntb200.h"
+
+namespace {
+
+int dtype_code(const at::Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kFloat: return NTB200_DTYPE_F32;
+    case at::kBFloat16: return NTB200_DTYPE_BF16;
+    case at::kHalf: return NTB200_DTYPE_F16;
+    case at::kInt: return NTB200_DTYPE_I32;
+    case at::kLong: return NTB200_DTYPE_I64;
+    default: TORCH_CHECK(false, "ntb200: unsupported dtype ", t.scalar_type());
+  }
+}
+
+void check(int status, const char* op) {
+  TORCH_CHECK(status == NTB200_OK, "ntb200.", op, " failed: ", ntb200_status_string(status),
+              ": ", ntb200_last_error());
+}
+
+void* stream_of(const at::Tensor& t) {
+  return static_cast<void*>(c10::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+void require_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "ntb200: ", name, " must be a CUDA tensor (no CPU path exists)");
+}
+
+void require_rows(const at::Tensor& t, const char* name) {
+  require_cuda(t, name);
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, "ntb200: ", name,
+              " must be 2-D with unit stride in the last dim");
+}
+
+void rms_norm(at::Tensor out, const at::Tensor& x, const std::optional<at::Tensor>& weight,
+              double eps) {
+  require_rows(x, "x");
+  require_rows(out, "out");
+  TORCH_CHECK(out.sizes() == x.sizes() && out.scalar_type() == x.scalar_type(), "ntb200.rms_norm: out mismatch");
+  const void* w = nullptr;
+  if (weight.has_value()) {
+    TORCH_CHECK(weight->is_contiguous() && weight->numel() == x.size(1) &&
+                    weight->scalar_type() == x.scalar_type(),
+                "ntb200.rms_norm: weight must be contiguous [hidden] of x's dtype");
+    w = weight->data_ptr();
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  check(ntb200_rms_norm(out.data_ptr(), x.data_ptr(), w, x.size(0), x.size(1), x.stride(0),
+                        out.stride(0), static_cast<float>(eps), dtype_code(x), stream_of(x)),
+        "rms_norm");
+}
+
+void fused_add_rms_norm(at::Tensor out, at::Tensor residual, const at::Tensor& x,
+                        const std::optional<at::Tensor>& weight, double eps) {
+  require_rows(x, "x");
+  require_rows(out, "out");
+  require_rows(residual, "residual");
+  TORCH_CHECK(out.sizes() == x.sizes() && residual.sizes() == x.sizes() &&
+                  out.scalar_type() == x.scalar_type() &&
+                  residual.scalar_type() == x.scalar_type(),
+              "ntb200.fused_add_rms_norm: shape/dtype mismatch");
+  const void* w = nullptr;
+  if (weight.has_value()) {
+    TORCH_CHECK(weight->is_contiguous() && weight->numel() == x.size(1) &&
+                    weight->scalar_type() == x.scalar_type(),
+                "ntb200.fused_add_rms_norm: weight must be contiguous [hidden] of x's dtype");
+    w = weight->data_ptr();
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  check(ntb200_fused_add_rms_norm(out.data_ptr(), residual.data_ptr(), x.data_ptr(), w,
+                                  x.size(0), x.size(1), x.stride(0), residual.stride(0),
+                                  out.stride(0), static_cast<float>(eps), dtype_code(x),
+                                  stream_of(x)),
+        "fused_add_rms_norm");
+}
+
+void silu_and_mul(at::Tensor out, const at::Tensor& x) {
+  require_rows(x, "x");
+  require_rows(out, "out");
+  TORCH_CHECK(x.size(1) % 2 == 0 && out.size(1) == x.size(1) / 2 && out.size(0) == x.size(0) &&
+                  out.scalar_type() == x.scalar_type(),
+              "ntb200.silu_and_mul: out must be [rows, d] for x [rows, 2d]");
+  c10::cuda::CUDAGuard guard(x.device());
+  check(ntb200_silu_and_mul(out.data_ptr(), x.data_ptr(), x.size(0), out.size(1), x.stride(0),
+                            out.stride(0), dtype_code(x), stream_of(x)),
+        "silu_and_mul");
+}
+
+void rotary_embedding_neox(const at::Tensor& positions, at::Tensor query,
+                           const std::optional<at::Tensor>& key, const at::Tensor& cache,
+                           int64_t head_size, int64_t rotary_dim) {
+  require_cuda(query, "query");
+  require_cuda(positions, "positions");
+  require_rows(cache, "cos_sin_cache");
+  TORCH_CHECK(positions.dim() == 1 && positions.is_contiguous(), "ntb200.rope: positions must be 1-D contiguous");
+  TORCH_CHECK(query.dim() == 3 && query.size(2) == head_size && query.stride(2) == 1 &&
+                  query.size(0) == positions.size(0),
+              "ntb200.rope: query must be [tokens, heads, head_size] with unit inner stride");
+  TORCH_CHECK(cache.scalar_type() == query.scalar_type(), "ntb200.rope: cos_sin_cache dtype must match query");
+  void* kptr = nullptr;
+  int64_t hk = 0, kts = 0, khs = 0;
+  if (key.has_value()) {
+    TORCH_CHECK(key->dim() == 3 && key->size(2) == head_size && key->stride(2) == 1 &&
+                    key->size(0) == positions.size(0) && key->scalar_type() == query.scalar_type(),
+                "ntb200.rope: key must be [tokens, heads, head_size] like query");
+    kptr = key->data_ptr();
+    hk = key->size(1);
+    kts = key->stride(0);
+    khs = key->stride(1);
+  }
+  c10::cuda::CUDAGuard guard(query.device());
+  check(ntb200_rotary_embedding_neox(positions.data_ptr(), dtype_code(positions), query.data_ptr(),
+                                     kptr, cache.data_ptr(), positions.size(0), query.size(1), hk,
+                                     head_size, rotary_dim, query.stride(0), query.stride(1), kts,
+                                     khs, cache.stride(0), cache.size(0), dtype_code(query),
+                                     stream_of(query)),
+        "rotary_embedding_neox");
+}
+
+void reshape_and_cache(const at::Tensor& key, const at::Tensor& value, at::Tensor key_cache,
+                       at::Tensor value_cache, const at::Tensor& slot_mapping) {
+  require_cuda(key, "key");
+  require_cuda(value, "value");
+  require_cuda(key_cache, "key_cache");
+  require_cuda(value_cache, "value_cache");
+  require_cuda(slot_mapping, "slot_mapping");
+  TORCH_CHECK(key.dim() == 3 && value.sizes() == key.sizes() && key.stride(2) == 1 &&
+                  value.stride(2) == 1,
+              "ntb200.reshape_and_cache: key/value must be [tokens, heads, head_size]");
+  TORCH_CHECK(key_cache.dim() == 4 && value_cache.sizes() == key_cache.sizes() &&
+                  key_cache.strides() == value_cache.strides() && key_cache.stride(3) == 1,
+              "ntb200.reshape_and_cache: caches must be [blocks, block_size, heads, head_size] with equal strides");
+  TORCH_CHECK(key_cache.size(2) == key.size(1) && key_cache.size(3) == key.size(2),
+              "ntb200.reshape_and_cache: head geometry mismatch");
+  TORCH_CHECK(key_cache.scalar_type() == key.scalar_type() && value.scalar_type() == key.scalar_type() &&
+                  value_cache.scalar_type() == key.scalar_type(),
+              "ntb200.reshape_and_cache: dtype mismatch");
+  TORCH_CHECK(slot_mapping.dim() == 1 && slot_mapping.is_contiguous() &&
+                  slot_mapping.size(0) <= key.size(0),
+              "ntb200.reshape_and_cache: slot_mapping must be 1-D contiguous, <= tokens");
+  c10::cuda::CUDAGuard guard(key.device());
+  check(ntb200_reshape_and_cache(
+            key.data_ptr(), value.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+            slot_mapping.data_ptr(), dtype_code(slot_mapping), slot_mapping.size(0), key.size(1),
+            key.size(2), key_cache.size(1), key_cache.size(0) * key_cache.size(1), key.stride(0),
+            key.stride(1), value.stride(0), value.stride(1), key_cache.stride(0),
+            key_cache.stride(1), key_cache.stride(2), static_cast<int>(key.element_size()),
+            stream_of(key)),
+        "reshape_and_cache");
+}
+
+void embedding(at::Tensor out, const at::Tensor& ids, const at::Tensor& weight) {
+  require_rows(weight, "weight");
+  require_rows(out, "out");
+  require_cuda(ids, "ids");
+  TORCH_CHECK(ids.dim() == 1 && ids.is_contiguous() && out.size(0) == ids.size(0) &&
+                  out.size(1) == weight.size(1) && out.scalar_type() == weight.scalar_type(),
+              "ntb200.embedding: ids [T], weight [V, H], out [T, H]");
+  c10::cuda::CUDAGuard guard(weight.device());
+  check(ntb200_embedding(out.data_ptr(), ids.data_ptr(), dtype_code(ids), weight.data_ptr(),
+                         ids.size(0), weight.size(0), weight.size(1), weight.stride(0),
+                         out.stride(0), static_cast<int>(weight.element_size()),
+                         stream_of(weight)),
+        "embedding");
+}
+
+void paged_attention_decode(at::Tensor out, const at::Tensor& query, const at::Tensor& key_cache,
+                            const at::Tensor& value_cache, const at::Tensor& seq_lens,
+                            const at::Tensor& block_table, double scale, int64_t max_seq_len,
+                            at::Tensor workspace) {
+  require_cuda(query, "query");
+  require_cuda(out, "out");
+  require_cuda(key_cache, "key_cache");
+  require_cuda(value_cache, "value_cache");
+  require_cuda(seq_lens, "seq_lens");
+  require_cuda(block_table, "block_table");
+  require_cuda(workspace, "workspace");
+  TORCH_CHECK(query.dim() == 3 && query.stride(2) == 1 && out.sizes() == query.sizes() &&
+                  out.stride(2) == 1 && out.scalar_type() == query.scalar_type(),
+              "ntb200.paged_attention_decode: query/out must be [seqs, q_heads, head_size]");
+  TORCH_CHECK(key_cache.dim() == 4 && value_cache.sizes() == key_cache.sizes() &&
+                  key_cache.strides() == value_cache.strides() && key_cache.stride(3) == 1 &&
+                  key_cache.scalar_type() == query.scalar_type() &&
+                  value_cache.scalar_type() == query.scalar_type(),
+              "ntb200.paged_attention_decode: caches must be [blocks, block_size, kv_heads, head_size] like query");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt && seq_lens.is_contiguous() &&
+                  seq_lens.numel() >= query.size(0),
+              "ntb200.paged_attention_decode: seq_lens must be int32 contiguous [seqs]");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2 &&
+                  block_table.stride(1) == 1 && block_table.size(0) >= query.size(0),
+              "ntb200.paged_attention_decode: block_table must be int32 [seqs, max_blocks]");
+  c10::cuda::CUDAGuard guard(query.device());
+  check(ntb200_paged_attention_decode(
+            out.data_ptr(), query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+            seq_lens.data_ptr<int32_t>(), block_table.data_ptr<int32_t>(), query.size(0),
+            query.size(1), key_cache.size(2), query.size(2), key_cache.size(1), key_cache.size(0),
+            block_table.size(1), block_table.stride(0), max_seq_len, static_cast<float>(scale),
+            query.stride(0), query.stride(1), out.stride(0), out.stride(1), key_cache.stride(0),
+            key_cache.stride(1), key_cache.stride(2), workspace.data_ptr(),
+            static_cast<size_t>(workspace.numel() * workspace.element_size()), dtype_code(query),
+            stream_of(query)),
+        "paged_attention_decode");
+}
+
+int64_t decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads,
+                              int64_t head_size, int64_t block_size, int64_t max_seq_len) {
+  return static_cast<int64_t>(ntb200_paged_attention_decode_workspace_size(
+      num_seqs, num_q_heads, num_kv_heads, head_size, block_size, max_seq_len));
+}
+
+void linear(at::Tensor out, const at::Tensor& x, const at::Tensor& weight,
+            const std::optional<at::Tensor>& bias, const std::optional<at::Tensor>& workspace) {
+  require_rows(x, "x");
+  require_rows(weight, "weight");
+  require_rows(out, "out");
+  TORCH_CHECK(weight.size(1) == x.size(1) && out.size(0) == x.size(0) &&
+                  out.size(1) == weight.size(0) && weight.scalar_type() == x.scalar_type() &&
+                  out.scalar_type() == x.scalar_type(),
+              "ntb200.linear: x [M, K], weight [N, K], out [M, N] of one dtype");
+  const void* b = nullptr;
+  if (bias.has_value()) {
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == weight.size(0) &&
+                    bias->scalar_type() == x.scalar_type(),
+                "ntb200.linear: bias must be contiguous [N]");
+    b = bias->data_ptr();
+  }
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  if (workspace.has_value()) {
+    require_cuda(*workspace, "workspace");
+    ws = workspace->data_ptr();
+    ws_bytes = static_cast<size_t>(workspace->numel() * workspace->element_size());
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  check(ntb200_linear(out.data_ptr(), x.data_ptr(), weight.data_ptr(), b, x.size(0),
+                      weight.size(0), x.size(1), x.stride(0), weight.stride(0), out.stride(0), ws,
+                      ws_bytes, dtype_code(x), stream_of(x)),
+        "linear");
+}
+
+int64_t linear_workspace_size(int64_t m, int64_t n, int64_t k) {
+  return static_cast<int64_t>(ntb200_linear_workspace_size(m, n, k));
+}
+
+}  // namespace
+
+TORCH_LIBRARY(ntb200, m) {
+  m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor? weight, float eps) -> ()");
+  m.def(
+      "fused_add_rms_norm(Tensor(a!) out, Tensor(b!) residual, Tensor x, Tensor? weight, "
+      "float eps) -> ()");
+  m.def("silu_and_mul(Tensor(a!) out, Tensor x) -> ()");
+  m.def(
+      "rotary_embedding_neox(Tensor positions, Tensor(a!) query, Tensor(b!)? key, "
+      "Tensor cos_sin_cache, int head_size, int rotary_dim) -> ()");
+  m.def(
+      "reshape_and_cache(Tensor key, Tensor value, Tensor(a!) key_cache, "
+      "Tensor(b!) value_cache, Tensor slot_mapping) -> ()");
+  m.def("embedding(Tensor(a!) out, Tensor ids, Tensor weight) -> ()");
+  m.def(
+      "paged_attention_decode(Tensor(a!) out, Tensor query, Tensor key_cache, "
+      "Tensor value_cache, Tensor seq_lens, Tensor block_table, float scale, int max_seq_len, "
+      "Tensor(b!) workspace) -> ()");
+  m.def(
+      "decode_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads, int head_size, "
+      "int block_size, int max_seq_len) -> int",
+      &decode_workspace_size);
+  m.def("linear(Tensor(a!) out, Tensor x, Tensor weight, Tensor? bias, Tensor(b!)? workspace) -> ()");
+  m.def("linear_workspace_size(int m, int n, int k) -> int", &linear_workspace_size);
+}
+
+TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
+  m.impl("rms_norm", &rms_norm);
+  m.impl("fused_add_rms_norm", &fused_add_rms_norm);
+  m.impl("silu_and_mul", &silu_and_mul);
+  m.impl("rotary_embedding_neox", &rotary_embedding_neox);
+  m.impl("reshape_and_cache", &reshape_and_cache);
+  m.impl("embedding", &embedding);
+  m.impl("paged_attention_decode", &paged_attention_decode);
+  m.impl("linear", &linear);
+}

@@ -1,0 +1,155 @@
+"""Backend router and per-(op, backend) counters.
+
+``route`` runs an op on its configured backend; if that raises, it records the failure,
+optionally disables the op's backend for the rest of the process, and runs the fallback
+backend instead (re-raising when the fallback is the backend that just failed).  This is
+the contract of vllm_nt/_ntops/backends.py:96-161, kept so that configs, env flags and
+usage summaries behave the same.  The ``b200`` backend (alias ``ninetoothed``) is the
+hand-written sm_100a kernel set; ``infinicore*`` adapters are not part of this build, so
+selecting them fails over to the configured fallback exactly as the reference does on a
+machine without InfiniCore.
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+from dataclasses import dataclass
+from typing import Any, Callable
+
+from vllm_nt._ntops.config import config_for, op_name_variants
+
+LOG = logging.getLogger("vllm_nt")
+DISABLE_OPS_ENV = "VLLM_NT_DISABLE_OPS"
+ENABLE_STATS_ENV = "VLLM_NT_ENABLE_STATS"
+_TRUE = frozenset({"1", "true", "yes", "on"})
+
+Thunk = Callable[[], Any]
+
+
+@dataclass
+class BackendStats:
+    attempts: int = 0
+    hits: int = 0
+    failures: int = 0
+    fallbacks: int = 0
+
+
+_DISABLED: set[str] = set()
+_STATS: dict[str, dict[str, BackendStats]] = {}
+
+
+def stats_enabled() -> bool:
+    return os.environ.get(ENABLE_STATS_ENV, "").strip().lower() in _TRUE
+
+
+def disabled_ops() -> set[str]:
+    listed = {n.strip() for n in os.environ.get(DISABLE_OPS_ENV, "").split(",") if n.strip()}
+    out: set[str] = set()
+    for name in listed | _DISABLED:
+        out |= op_name_variants(name)
+    return out
+
+
+def configured_backend(op_name: str) -> str:
+    return config_for(op_name).backend
+
+
+def fallback_backend(op_name: str) -> str:
+    return config_for(op_name).fallback_backend
+
+
+def active_backend(op_name: str) -> str:
+    cfg = config_for(op_name)
+    return cfg.fallback_backend if op_name in disabled_ops() else cfg.backend
+
+
+def backend_enabled(op_name: str) -> bool:
+    return active_backend(op_name) != "original"
+
+
+def _entry(op_name: str, backend: str) -> BackendStats:
+    return _STATS.setdefault(op_name, {}).setdefault(backend, BackendStats())
+
+
+def record_attempt(op_name: str, backend: str) -> None:
+    if stats_enabled():
+        _entry(op_name, backend).attempts += 1
+
+
+def record_hit(op_name: str, backend: str | None = None) -> None:
+    if stats_enabled():
+        _entry(op_name, backend or active_backend(op_name)).hits += 1
+
+
+def record_failure(op_name: str, backend: str | None = None) -> None:
+    if stats_enabled():
+        _entry(op_name, backend or active_backend(op_name)).failures += 1
+
+
+def record_fallback(op_name: str, backend: str | None = None) -> None:
+    if stats_enabled():
+        _entry(op_name, backend or fallback_backend(op_name)).fallbacks += 1
+
+
+def backend_stats(op_name: str) -> dict[str, BackendStats]:
+    return _STATS.get(op_name, {})
+
+
+def reset_backend_state() -> None:
+    _DISABLED.clear()
+    _STATS.clear()
+
+
+def _dispatch(op_name: str, backend: str, thunks: dict[str, Thunk | None], original: Thunk) -> Any:
+    if backend == "original":
+        record_fallback(op_name, backend)
+        return original()
+    fn = thunks.get(backend)
+    if fn is None:
+        raise RuntimeError(f"{op_name} has no adapter for backend {backend}")
+    record_attempt(op_name, backend)
+    result = fn()
+    if backend.startswith("infinicore"):
+        record_hit(op_name, backend)
+    return result
+
+
+def route(
+    op_name: str,
+    call_original: Thunk,
+    *,
+    call_infinicore: Thunk | None = None,
+    call_ninetoothed: Thunk | None = None,
+    call_infinicore_flash_attn: Thunk | None = None,
+    call_b200: Thunk | None = None,
+) -> Any:
+    """Runs ``op_name`` on its active backend with failure fallback (see module doc).
+
+    ``call_b200`` defaults to ``call_ninetoothed``: in this build both names select the
+    sm_100a kernels."""
+    kernels = call_b200 if call_b200 is not None else call_ninetoothed
+    thunks = {
+        "infinicore": call_infinicore,
+        "infinicore-flash-attn": call_infinicore_flash_attn,
+        "ninetoothed": call_ninetoothed if call_ninetoothed is not None else kernels,
+        "b200": kernels,
+    }
+    cfg = config_for(op_name)
+    backend = active_backend(op_name)
+    try:
+        return _dispatch(op_name, backend, thunks, call_original)
+    except Exception as exc:
+        record_failure(op_name, backend)
+        if cfg.disable_backend_on_first_failure and backend != "original":
+            _DISABLED.add(op_name)
+            LOG.warning(
+                "vllm-nt: %s backend %s disabled after failure; falling back to %s: %s",
+                op_name,
+                backend,
+                cfg.fallback_backend,
+                exc,
+            )
+        if cfg.fallback_backend == backend:
+            raise
+        return _dispatch(op_name, cfg.fallback_backend, thunks, call_original)

@@ -1,0 +1,109 @@
+"""Op adapters between the vLLM hooks and the B200 kernels.
+
+Same function names and argument meanings as vllm_nt/_ntops/oot_support.py:32-208; each
+adapter now lands on one sm_100a kernel (for example ``norm`` with a residual is the
+fused add+RMS-norm kernel instead of a torch add followed by a norm kernel, and ``rope``
+gathers cos/sin inside the kernel)."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+
+from vllm_nt._ntops.torch.attention import flash_attn_with_kvcache as nt_flash_attn_with_kvcache
+from vllm_nt._ntops.torch.attention import paged_decode as nt_paged_decode
+from vllm_nt._ntops.torch.embedding import embedding as nt_embedding
+from vllm_nt._ntops.torch.kv_cache import get_kv_from_cache as nt_get_kv_from_cache
+from vllm_nt._ntops.torch.kv_cache import store_kvcache as nt_store_kvcache
+from vllm_nt._ntops.torch.linear import linear as nt_linear
+from vllm_nt._ntops.torch.rms_norm import fused_add_rms_norm as nt_fused_add_rms_norm
+from vllm_nt._ntops.torch.rms_norm import rms_norm as nt_rms_norm
+from vllm_nt._ntops.torch.rotary_emb import apply_rotary_emb as nt_apply_rotary_emb
+from vllm_nt._ntops.torch.rotary_emb import rotary_embedding as nt_rotary_embedding
+from vllm_nt._ntops.torch.silu import silu_and_mul as nt_silu_and_mul
+
+
+@dataclass
+class OperatorStats:
+    hits: int = 0
+    logged: bool = False
+    registered_via: str | None = None
+
+
+def norm(self, x: torch.Tensor, weight: torch.Tensor | None, residual: torch.Tensor | None = None, gemma: bool = False):
+    """RMSNorm.forward contract: returns ``out`` or ``(out, new_residual)``.
+
+    With a residual the sum is formed in fp32 inside the kernel and written into the
+    residual buffer (vLLM's CUDA convention), the norm is taken of the fp32 sum."""
+    eps = self.variance_epsilon
+    if residual is not None:
+        return nt_fused_add_rms_norm(x, residual, weight, eps, inplace=True)
+    hidden = weight.shape[0] if weight is not None else self.hidden_size
+    return nt_rms_norm(x, hidden, weight=weight, eps=eps)
+
+
+def act_and_mul(x: torch.Tensor, act: Callable[[torch.Tensor], torch.Tensor] | None = None, reverse: bool = False) -> torch.Tensor:
+    """silu(x[..., :d]) * x[..., d:] as one kernel.  Other activations (or the reversed
+    MulAndSilu order) compose ``act`` with a multiply, as the reference does."""
+    if act is None and not reverse:
+        return nt_silu_and_mul(x)
+    d = x.shape[-1] // 2
+    left, right = (x[..., d:], x[..., :d]) if reverse else (x[..., :d], x[..., d:])
+    fn = act if act is not None else torch.nn.functional.silu
+    return fn(left) * right
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    out = nt_linear(x.reshape(-1, x.shape[-1]), weight, bias)
+    return out.view(*x.shape[:-1], weight.shape[0])
+
+
+def embedding(layer: torch.nn.Module, input_: torch.Tensor) -> torch.Tensor:
+    return nt_embedding(input_, layer.weight)
+
+
+def rope(
+    positions: torch.Tensor,
+    query: torch.Tensor,
+    key: torch.Tensor | None,
+    *,
+    cos_sin_cache: torch.Tensor,
+    head_size: int,
+    rotary_dim: int,
+    is_neox_style: bool,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """In-place NeoX rotary embedding of query/key (reference: oot_support.py:164-204)."""
+    if not is_neox_style:
+        raise NotImplementedError("Only NeoX-style RoPE is supported.")
+    if rotary_dim % 2:
+        raise ValueError("rotary_dim must be even.")
+    cache = cos_sin_cache
+    if cache.dtype != query.dtype:
+        cache = cache.to(query.dtype)
+    return nt_rotary_embedding(positions, query, key, head_size, cache, rotary_dim)
+
+
+def store_kv_cache(key, value, k_cache, v_cache, slot_mapping):
+    return nt_store_kvcache(key, value, k_cache, v_cache, slot_mapping)
+
+
+def paged_attention_decode(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale=None, causal=True, max_seq_len=None):
+    return nt_flash_attn_with_kvcache(
+        q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale=softmax_scale, causal=causal, max_seq_len=max_seq_len
+    )
+
+
+def paged_attention_prefill(*args, **kwargs):
+    """Prefill is not on this backend's hot path; callers route it to vLLM's original."""
+    raise NotImplementedError("paged prefill is served by vLLM's original attention backend")
+
+
+def get_kv_from_cache(k_cache, v_cache, seq_lens, block_table):
+    return nt_get_kv_from_cache(k_cache, v_cache, seq_lens, block_table)
+
+
+def sdpa(*args, **kwargs):
+    """Dense SDPA (vision/encoder models) is outside this backend; vLLM's path serves it."""
+    raise NotImplementedError("SDPA is served by vLLM's original path")

@@ -1,0 +1,29 @@
+"""Dense projection on the tcgen05 GEMM (replaces vllm_nt/_ntops/torch/linear.py and
+vllm_nt/_ntops/torch/matmul.py)."""
+
+from __future__ import annotations
+
+import torch
+
+from vllm_nt._ntops.torch._ext import ops
+
+
+def _k_contiguous(t: torch.Tensor) -> torch.Tensor:
+    ok = t.stride(-1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
+    return t if ok else t.contiguous()
+
+
+def linear(input: torch.Tensor, other: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """out = input @ other^T (+ bias) for input [M, K] and other [N, K] (vLLM layout)."""
+    x = _k_contiguous(input)
+    w = _k_contiguous(other)
+    out = torch.empty((x.shape[0], w.shape[0]), dtype=x.dtype, device=x.device)
+    if bias is not None and not bias.is_contiguous():
+        bias = bias.contiguous()
+    ops().linear(out, x, w, bias, None)
+    return out
+
+
+def matmul(lhs: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
+    """lhs [M, K] @ rhs [K, N]; rhs is transposed once into the [N, K] operand layout."""
+    return linear(lhs, rhs.t().contiguous())

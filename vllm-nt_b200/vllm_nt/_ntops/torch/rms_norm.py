@@ -1,0 +1,57 @@
+"""RMS norm on the sm_100a kernel (replaces vllm_nt/_ntops/torch/rms_norm.py)."""
+
+from __future__ import annotations
+
+import torch
+
+from vllm_nt._ntops.torch._ext import ops
+
+
+def _rows(t: torch.Tensor, hidden: int) -> torch.Tensor:
+    t2 = t.reshape(-1, hidden)
+    return t2 if t2.stride(-1) == 1 else t2.contiguous()
+
+
+def _weight(weight: torch.Tensor | None, hidden: int, dtype: torch.dtype) -> torch.Tensor | None:
+    if weight is None:
+        return None
+    w = weight.reshape(-1)[:hidden] if weight.numel() != hidden else weight.reshape(hidden)
+    if w.dtype != dtype:
+        w = w.to(dtype)
+    return w.contiguous()
+
+
+def rms_norm(input, normalized_shape, weight=None, eps=None):
+    """y = input * rsqrt(mean(input^2, -1) + eps) * weight over the last dimension.
+
+    Same signature as vllm_nt/_ntops/torch/rms_norm.py:36-61; only normalisation over
+    the last dimension is supported (the case every vLLM layer uses)."""
+    if isinstance(normalized_shape, int):
+        normalized_shape = (normalized_shape,)
+    normalized_shape = tuple(normalized_shape)
+    if len(normalized_shape) != 1 or normalized_shape[0] != input.shape[-1]:
+        raise NotImplementedError("ntb200.rms_norm normalises over the last dimension only")
+    if eps is None:
+        eps = torch.finfo(input.dtype).eps
+    hidden = input.shape[-1]
+    x = _rows(input, hidden)
+    out = torch.empty_like(x)
+    ops().rms_norm(out, x, _weight(weight, hidden, input.dtype), float(eps))
+    return out.view(input.shape)
+
+
+def fused_add_rms_norm(x, residual, weight, eps, inplace=False):
+    """Returns (rms_norm(x + residual), x + residual) with the sum and statistics in
+    fp32, as vLLM's fused_add_rms_norm (vllm/ir/ops/layernorm.py:40-62).
+
+    With ``inplace=True`` the sum is written into ``residual`` (vLLM's CUDA convention:
+    the caller no longer needs the old residual), which saves a copy; otherwise neither
+    input is modified."""
+    hidden = x.shape[-1]
+    x2 = _rows(x, hidden)
+    res = residual.reshape(-1, hidden)
+    if not inplace or res.stride(-1) != 1:
+        res = res.clone(memory_format=torch.contiguous_format)
+    out = torch.empty_like(x2)
+    ops().fused_add_rms_norm(out, res, x2, _weight(weight, hidden, x.dtype), float(eps))
+    return out.view(x.shape), res.view(residual.shape)

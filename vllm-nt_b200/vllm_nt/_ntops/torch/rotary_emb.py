@@ -1,0 +1,52 @@
+"""In-place NeoX rotary embedding on the sm_100a kernel (replaces
+vllm_nt/_ntops/torch/rotary_emb.py and the cos/sin gather of
+vllm_nt/_ntops/oot_support.py:164-204)."""
+
+from __future__ import annotations
+
+import torch
+
+from vllm_nt._ntops.torch._ext import ops
+
+
+def _heads(t: torch.Tensor, num_tokens: int, head_size: int) -> torch.Tensor:
+    v = t.view(num_tokens, -1, head_size)
+    if v.stride(-1) != 1:
+        raise ValueError("rotary_embedding needs unit stride in the head dimension")
+    return v
+
+
+def rotary_embedding(
+    positions: torch.Tensor,
+    query: torch.Tensor,
+    key: torch.Tensor | None,
+    head_size: int,
+    cos_sin_cache: torch.Tensor,
+    rotary_dim: int | None = None,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Rotates the first ``rotary_dim`` dims of every head of query (and key) in place,
+    NeoX style, with cos/sin = cos_sin_cache[positions] split in halves.  The cache must
+    already have query's dtype (vLLM's _match_cos_sin_cache_dtype)."""
+    positions = positions.reshape(-1)
+    if not positions.is_contiguous():
+        positions = positions.contiguous()
+    n = positions.shape[0]
+    rot = cos_sin_cache.shape[-1] if rotary_dim is None else int(rotary_dim)
+    cache = cos_sin_cache if cos_sin_cache.stride(-1) == 1 else cos_sin_cache.contiguous()
+    q = _heads(query, n, head_size)
+    k = _heads(key, n, head_size) if key is not None else None
+    ops().rotary_embedding_neox(positions, q, k, cache, int(head_size), rot)
+    return query, key
+
+
+def apply_rotary_emb(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Reference signature (vllm_nt/_ntops/torch/rotary_emb.py:7-9): x [T, H, R] rotated in
+    place with per-token cos/sin [T, 1, R/2] (or [T, R/2]).  Implemented by handing the
+    kernel a per-token cos|sin table and positions 0..T-1."""
+    t, _, r = x.shape
+    table = torch.cat((cos.reshape(t, r // 2), sin.reshape(t, r // 2)), dim=-1).to(x.dtype)
+    pos = torch.arange(t, device=x.device, dtype=torch.int64)
+    if x.stride(-1) != 1:
+        raise ValueError("apply_rotary_emb needs unit stride in the last dimension")
+    ops().rotary_embedding_neox(pos, x, None, table.contiguous(), r, r)
+    return x
