@@ -1,0 +1,251 @@
+"""Plugin registration and hook behaviour with vLLM imported, no GPU: which methods are
+replaced, what the hooks route where, and the usage-summary contract of the reference
+(vllm_nt/tests/test_plugin_integration.py).  Kernels are replaced by fakes here; the GPU
+versions of these paths are in test_hooks_gpu.py."""
+
+import re
+from pathlib import Path
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+pytest.importorskip("vllm")
+
+import vllm_nt  # noqa: E402
+from vllm_nt._ntops import backends, config, patching  # noqa: E402
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(autouse=True)
+def _fresh(monkeypatch):
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml"))
+    patching._reset_usage_state()
+    yield
+    patching._reset_usage_state()
+
+
+def test_entry_point_declared():
+    text = (ROOT / "pyproject.toml").read_text()
+    assert '[project.entry-points."vllm.general_plugins"]' in text
+    assert 'vllm_nt = "vllm_nt:register"' in text
+
+
+def test_vllm_plugin_loader_finds_the_entry_point(tmp_path, monkeypatch):
+    """A dist-info with the same entry point makes vLLM's loader call vllm_nt.register."""
+    dist = tmp_path / "vllm_nt-0.2.0.dist-info"
+    dist.mkdir()
+    (dist / "METADATA").write_text("Metadata-Version: 2.1\nName: vllm-nt\nVersion: 0.2.0\n")
+    (dist / "entry_points.txt").write_text("[vllm.general_plugins]\nvllm_nt = vllm_nt:register\n")
+    monkeypatch.syspath_prepend(str(tmp_path))
+    from vllm.plugins import load_plugins_by_group
+
+    plugins = load_plugins_by_group("vllm.general_plugins")
+    assert "vllm_nt" in plugins and plugins["vllm_nt"] is vllm_nt.register
+
+
+def test_register_is_idempotent_and_hooks_cuda_dispatch():
+    from vllm.model_executor.custom_op import op_registry_oot
+    from vllm.model_executor.layers.linear import UnquantizedLinearMethod
+    from vllm.model_executor.layers.rotary_embedding.base import RotaryEmbedding
+    from vllm.model_executor.layers.vocab_parallel_embedding import UnquantizedEmbeddingMethod
+
+    vllm_nt.register()
+    vllm_nt.register()
+    for name, fwd in (("RMSNorm", patching._nt_rms_norm_forward), ("SiluAndMul", patching._nt_silu_and_mul_forward)):
+        cls = op_registry_oot[name]
+        # CUDA platforms dispatch forward_cuda; disabled ops dispatch forward_native
+        assert cls.forward_cuda is fwd and cls.forward_native is fwd and cls.forward_oot is fwd
+    assert UnquantizedLinearMethod.apply is patching._nt_unquantized_linear_apply
+    assert UnquantizedEmbeddingMethod.embedding is patching._nt_unquantized_embedding
+    assert UnquantizedEmbeddingMethod.apply is patching._nt_unquantized_embedding_apply
+    assert patching._is_function_patch(RotaryEmbedding.forward_cuda, "RoPE")
+
+
+def test_usage_summary_shape_and_registered_ops():
+    vllm_nt.register()
+    s = patching.get_usage_summary()
+    assert set(s) == {"registered_ops", "hit_ops", "missed_ops", "operators", "disabled"}
+    for op in ("RMSNorm", "SiluAndMul", "RoPE", "MatMul", "LMHead", "Embedding", "StoreKVCache", "PagedAttentionDecode"):
+        assert op in s["registered_ops"]
+    assert s["hit_ops"] == [] and set(s["missed_ops"]) == set(s["registered_ops"])
+    d = s["operators"]["MatMul"]
+    assert set(d) == {"configured_backend", "active_backend", "hits", "failures", "fallbacks", "registered_via", "backends"}
+    assert d["configured_backend"] == "b200"
+
+
+def test_summary_empty_when_stats_disabled(monkeypatch, capsys):
+    monkeypatch.setenv("VLLM_NT_ENABLE_STATS", "0")
+    patching._record_hit("RMSNorm", torch.ones(1, 4))
+    assert patching.get_usage_summary() == {"registered_ops": [], "hit_ops": [], "missed_ops": [], "operators": {}, "disabled": []}
+    assert patching.maybe_print_usage_summary(include_empty=True) is False
+    assert capsys.readouterr().err == ""
+
+
+def test_feature_toggles(monkeypatch):
+    assert patching._nt_feature_enabled("FA") and patching._nt_feature_enabled("MM")
+    monkeypatch.setenv("VLLM_NT_ENABLE_FA", "0")
+    disabled = {s.patch_id for s in patching._FUNCTION_PATCH_SPECS if not patching._function_patch_enabled(s)}
+    assert {"StoreKVCache", "PagedAttentionDecode"} <= disabled and "RoPE" not in disabled
+    monkeypatch.setenv("VLLM_NT_ENABLE_ALL", "0")
+    monkeypatch.setenv("VLLM_NT_ENABLE_FA", "1")
+    assert not patching._operator_enabled("RMSNorm")
+
+
+def test_mm_toggle_skips_linear_and_lmhead(monkeypatch):
+    class FakeLinear:
+        apply = object()
+
+    class FakeEmbedding:
+        embedding = object()
+        apply = object()
+
+    monkeypatch.setattr(patching, "UnquantizedLinearMethod", FakeLinear)
+    monkeypatch.setattr(patching, "UnquantizedEmbeddingMethod", FakeEmbedding)
+    monkeypatch.setenv("VLLM_NT_ENABLE_MM", "0")
+    keep_lin, keep_apply = FakeLinear.apply, FakeEmbedding.apply
+    patching._patch_leaf_methods()
+    assert FakeLinear.apply is keep_lin and FakeEmbedding.apply is keep_apply
+    assert FakeEmbedding.embedding is patching._nt_unquantized_embedding
+
+
+def test_default_config_gates_attention_patches_off(monkeypatch):
+    monkeypatch.delenv("VLLM_NT_BACKEND_CONFIG")
+    config.reset_backend_config_cache()
+    enabled = {s.patch_id for s in patching._FUNCTION_PATCH_SPECS if patching._function_patch_enabled(s)}
+    assert "StoreKVCache" not in enabled and "PagedAttentionDecode" not in enabled
+    assert "RoPE" in enabled  # ApplyRotaryEmb -> ninetoothed (= these kernels) by default
+
+
+# ---------------------------------------------------------------------------- hook routing
+
+
+class _Norm:
+    variance_epsilon = 1e-6
+    has_weight = True
+    hidden_size = 8
+
+    def __init__(self):
+        self.weight = torch.nn.Parameter(torch.ones(8))
+
+
+def test_rms_norm_hook_hits_and_falls_back_on_failure(monkeypatch):
+    monkeypatch.setattr(patching, "_norm_eligible", lambda *a: True)
+    monkeypatch.setattr(patching, "norm", lambda self, x, w, r=None, gemma=False: "kernel")
+    monkeypatch.setitem(patching._ORIGINAL_OPERATOR_FORWARDS, "RMSNorm", {"native": lambda self, x, r=None: "native"})
+    assert patching._nt_rms_norm_forward(_Norm(), torch.ones(2, 8)) == "kernel"
+    assert patching.get_usage_summary()["operators"]["RMSNorm"]["hits"] == 1
+
+    def boom(*a, **k):
+        raise RuntimeError("kernel failed")
+
+    monkeypatch.setattr(patching, "norm", boom)
+    assert patching._nt_rms_norm_forward(_Norm(), torch.ones(2, 8)) == "native"
+    op = patching.get_usage_summary()["operators"]["RMSNorm"]
+    assert op["failures"] == 1 and op["active_backend"] == "original"
+
+
+def test_ineligible_calls_go_straight_to_vllm():
+    """CPU tensors are not eligible: vLLM's own forward runs and nothing is counted."""
+    from vllm.model_executor.layers.layernorm import RMSNorm
+    from vllm import ir
+
+    vllm_nt.register()
+    x, r = torch.randn(3, 16), torch.randn(3, 16)
+    layer = SimpleNamespace(weight=torch.nn.Parameter(torch.ones(16)), has_weight=True, variance_epsilon=1e-6,
+                            variance_size_override=None, hidden_size=16, pass_weight=True, pass_weight_add=True)
+    out, res = patching._nt_rms_norm_forward(layer, x.clone(), r.clone())
+    ref, ref_r = ir.ops.fused_add_rms_norm(x.clone(), r.clone(), layer.weight.data, 1e-6)
+    torch.testing.assert_close(out, ref)
+    assert patching.get_usage_summary()["operators"]["RMSNorm"]["hits"] == 0
+    assert RMSNorm is not None
+
+
+def test_linear_hook_routes_and_handles_residual(monkeypatch):
+    from vllm.model_executor.layers.linear import UnquantizedLinearMethod
+
+    monkeypatch.setattr(patching, "_gemm_eligible", lambda *a: True)
+    monkeypatch.setattr(patching, "linear", lambda x, w, b=None: x @ w.t())
+    setattr(patching._nt_unquantized_linear_apply, "_original", lambda *a, **k: "vllm")
+    layer = SimpleNamespace(weight=torch.ones(3, 4))
+    x = torch.ones(2, 4)
+    out = patching._nt_unquantized_linear_apply(UnquantizedLinearMethod(), layer, x, None, residual=torch.ones(2, 3))
+    assert torch.equal(out, torch.full((2, 3), 5.0))
+    assert patching.get_usage_summary()["operators"]["MatMul"]["hits"] == 1
+
+
+def test_rope_hook_uses_matched_cache_and_counts(monkeypatch):
+    captured = {}
+
+    def fake_rope(positions, query, key, **kw):
+        captured.update(kw)
+        return query, key
+
+    monkeypatch.setattr(patching, "rope", fake_rope)
+
+    class Rot:
+        is_neox_style = True
+        rotary_dim = 4
+        head_size = 4
+
+        def __init__(self):
+            self.cos_sin_cache = torch.ones(8, 4)
+
+        def _match_cos_sin_cache_dtype(self, q):
+            self.cos_sin_cache = self.cos_sin_cache.to(q.dtype)
+            return self.cos_sin_cache
+
+    fwd = patching._build_rotary_forward(lambda *a, **k: (_ for _ in ()).throw(AssertionError("fallback")))
+    q = torch.zeros(2, 4, dtype=torch.float16)
+    # CPU tensors are ineligible -> the original (here: raising) is called
+    with pytest.raises(AssertionError):
+        fwd(Rot(), torch.tensor([0, 1]), q, q.clone())
+    monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
+    res = fwd(Rot(), torch.tensor([0, 1]), q, q.clone())
+    assert res[0] is q and captured["cos_sin_cache"].dtype == torch.float16 and captured["rotary_dim"] == 4
+    assert patching.get_usage_summary()["operators"]["RoPE"]["hits"] == 1
+
+
+def test_attention_hooks_decode_only_and_kv_store(monkeypatch):
+    calls = {}
+    monkeypatch.setattr(patching, "_attn_impl_supported", lambda *a: True)
+    monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
+
+    def fake_decode(out, q, kc, vc, seq, table, scale, msl):
+        calls["decode"] = (tuple(out.shape), tuple(q.shape), tuple(kc.shape), tuple(seq.shape), scale, msl)
+        out.fill_(1.0)
+
+    def fake_store(key, value, kc, vc, slots):
+        calls["store"] = (tuple(key.shape), tuple(kc.shape), tuple(slots.shape))
+
+    monkeypatch.setattr(patching, "nt_paged_decode", fake_decode)
+    monkeypatch.setattr(patching, "store_kv_cache", fake_store)
+    orig = lambda *a, **k: "flash-attn"  # noqa: E731
+    fwd = patching._build_flash_attn_forward(orig)
+    upd = patching._build_flash_attn_kv_update(orig)
+    impl = SimpleNamespace(num_heads=4, head_size=128, scale=0.1)
+    kv = torch.zeros(2, 6, 16, 2, 128)
+    q = torch.zeros(5, 4, 128)  # 3 real decode tokens + 2 padding rows
+    out = torch.zeros(5, 4 * 128)
+    meta = SimpleNamespace(num_actual_tokens=3, max_query_len=1, use_cascade=False, max_seq_len=40,
+                           query_start_loc=torch.tensor([0, 1, 2, 3]), seq_lens=torch.tensor([4, 9, 40]),
+                           block_table=torch.zeros(3, 3, dtype=torch.int32))
+    assert fwd(impl, None, q, q, q, kv, meta, out) is out
+    assert calls["decode"] == ((3, 4, 128), (3, 4, 128), (6, 16, 2, 128), (3,), 0.1, 40)
+    assert out[:3].eq(1).all() and out[3:].eq(0).all()
+    prefill = SimpleNamespace(**{**vars(meta), "max_query_len": 7})
+    assert fwd(impl, None, q, q, q, kv, prefill, out) == "flash-attn"
+    upd(impl, None, torch.zeros(5, 2, 128), torch.zeros(5, 2, 128), kv, torch.tensor([1, 2, 3]))
+    assert calls["store"] == ((5, 2, 128), (6, 16, 2, 128), (3,))
+    ops = patching.get_usage_summary()["operators"]
+    assert ops["PagedAttentionDecode"]["hits"] == 1 and ops["StoreKVCache"]["hits"] == 1
+
+
+def test_no_vendor_imports_in_package():
+    """Like the reference's structural test: nothing in the package imports a vendor
+    accelerator stack or the reference's DSL."""
+    pkg = ROOT / "vllm-nt_b200" / "vllm_nt"
+    bad = re.compile(r"^\s*(import|from)\s+(torch_mlu|torch_musa|vllm_mlu|vllm_musa|vllm_metax|ninetoothed|triton|infinicore)\b", re.M)
+    offenders = [str(p) for p in pkg.rglob("*.py") if bad.search(p.read_text())]
+    assert offenders == []
