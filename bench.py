@@ -50,28 +50,32 @@ def load_peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def workload(seed: int = 0):
+def workload(seed: int = 0, batch: int = BATCH, pool: int = POOL):
     """Context lengths and block tables of the decode workload (CPU, deterministic)."""
     g = torch.Generator().manual_seed(seed)
     ctx = torch.randint(CTX_LO, CTX_HI + 1, (BATCH,), generator=g)
+    q = torch.randn(BATCH, HQ, HEAD, generator=g).to(torch.bfloat16)
+    ctx, q = ctx[:batch], q[:batch]
     nblk = (ctx + BLOCK - 1) // BLOCK
-    ids = torch.randperm(POOL, generator=g)[: int(nblk.sum())].to(torch.int32)
-    table = torch.zeros(BATCH, MAX_BLOCKS, dtype=torch.int32)
+    if int(nblk.sum()) > pool:
+        raise SystemExit(f"--pool {pool} is smaller than the {int(nblk.sum())} blocks the batch needs")
+    ids = torch.randperm(pool, generator=g)[: int(nblk.sum())].to(torch.int32)
+    table = torch.zeros(batch, MAX_BLOCKS, dtype=torch.int32)
     off = 0
     for i, n in enumerate(nblk.tolist()):
         table[i, :n] = ids[off : off + n]
         off += n
-    q = torch.randn(BATCH, HQ, HEAD, generator=g).to(torch.bfloat16)
     return ctx.to(torch.int32), table, q
 
 
 def decode_bytes(ctx: torch.Tensor, hkv_local: int) -> int:
     """Algorithmic HBM bytes of one decode call: every cached K and V row of the local
     heads once, q and out once, the block-table entries used and the sequence lengths."""
+    batch = ctx.shape[0]
     tokens = int(ctx.sum())
     blocks = int(((ctx + BLOCK - 1) // BLOCK).sum())
     hq_local = hkv_local * (HQ // HKV)
-    return tokens * hkv_local * HEAD * 2 * 2 + 2 * BATCH * hq_local * HEAD * 2 + blocks * 4 + BATCH * 4
+    return tokens * hkv_local * HEAD * 2 * 2 + 2 * batch * hq_local * HEAD * 2 + blocks * 4 + batch * 4
 
 
 class ClockSampler:
@@ -366,6 +370,32 @@ def per_op_table(dev, peaks) -> dict:
     return res
 
 
+def run_linear_case(args) -> int:
+    """One GEMM shape, warmup + steps launches, for profiling (prints its own timing)."""
+    from vllm_nt._ntops.torch._ext import ops
+
+    m, n, k = args.linear_case
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(m, k, device=dev, generator=g, dtype=torch.bfloat16)
+    w = 0.02 * torch.randn(n, k, device=dev, generator=g, dtype=torch.bfloat16)
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    o = ops()
+    for _ in range(args.warmup):
+        o.linear(out, x, w, None, None)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        o.linear(out, x, w, None, None)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"linear_case": [m, n, k], "us": ms * 1e3, "TFLOP/s": 2.0 * m * n * k / (ms * 1e-3) / 1e12}))
+    return 0
+
+
 # --------------------------------------------------------------------------------------
 # main arm
 # --------------------------------------------------------------------------------------
@@ -374,16 +404,23 @@ def per_op_table(dev, peaks) -> dict:
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op table")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--decode-batch", type=int, default=BATCH, help="profiling: fewer sequences than the workload")
+    ap.add_argument("--pool", type=int, default=POOL, help="profiling: smaller block pool")
+    ap.add_argument("--linear-case", type=int, nargs=3, metavar=("M", "N", "K"),
+                    help="profiling: run only the GEMM out[M,N] = x[M,K] W[N,K]^T, warmup+steps times")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.linear_case:
+        return run_linear_case(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -403,18 +440,21 @@ def main() -> int:
     from vllm_nt._ntops.torch.attention import decode_workspace_bytes, paged_decode
 
     peaks, peak_kind = load_peaks()
-    ctx, table, q_all = workload()
-    hkv = HKV // n
-    hq = hkv * (HQ // HKV)
-    h0 = rank * hkv
-    q = q_all[:, h0 * (HQ // HKV) : h0 * (HQ // HKV) + hq].contiguous()
+    batch, pool = args.decode_batch, args.pool
+    ctx, table, q_all = workload(0, batch, pool)
+    from vllm_nt._ntops import sharding
+
+    h0, h1 = sharding.kv_head_range(rank, n, HKV)
+    q0, q1 = sharding.q_head_range(rank, n, HQ, HKV)
+    hkv, hq = h1 - h0, q1 - q0
+    q = q_all[:, q0:q1].contiguous()
     gk = torch.Generator(device=dev).manual_seed(1000 + rank)
-    kc = torch.randn(POOL, BLOCK, hkv, HEAD, device=dev, generator=gk, dtype=torch.bfloat16)
-    vc = torch.randn(POOL, BLOCK, hkv, HEAD, device=dev, generator=gk, dtype=torch.bfloat16)
+    kc = torch.randn(pool, BLOCK, hkv, HEAD, device=dev, generator=gk, dtype=torch.bfloat16)
+    vc = torch.randn(pool, BLOCK, hkv, HEAD, device=dev, generator=gk, dtype=torch.bfloat16)
     qd, sd, td = q.to(dev), ctx.to(dev), table.to(dev)
     out = torch.empty_like(qd)
     scale = 1.0 / math.sqrt(HEAD)
-    ws = torch.empty(decode_workspace_bytes(BATCH, hq, hkv, CTX_HI), dtype=torch.uint8, device=dev)
+    ws = torch.empty(decode_workspace_bytes(batch, hq, hkv, CTX_HI), dtype=torch.uint8, device=dev)
 
     def step():
         paged_decode(out, qd, kc, vc, sd, td, scale, CTX_HI, ws)
@@ -443,7 +483,7 @@ def main() -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
     ms_per_step = ms_max / args.steps
-    value = BATCH * args.steps / (ms_max * 1e-3)
+    value = batch * args.steps / (ms_max * 1e-3)
 
     # roofline of this rank's decode call (split + combine launches)
     algo = decode_bytes(ctx, hkv)
@@ -464,11 +504,11 @@ def main() -> int:
     # e2e: the plugin's public decode entry point with host buffers
     from vllm_nt.oot import paged_attention_decode
 
-    q_host = q.view(BATCH, 1, hq, HEAD).pin_memory()
+    q_host = q.view(batch, 1, hq, HEAD).pin_memory()
     s_host = ctx.pin_memory()
     t_host = table.pin_memory()
-    o_host = torch.empty(BATCH, 1, hq, HEAD, dtype=torch.bfloat16).pin_memory()
-    e2e_steps = max(10, min(args.steps, 200))
+    o_host = torch.empty(batch, 1, hq, HEAD, dtype=torch.bfloat16).pin_memory()
+    e2e_steps = 0 if args.no_e2e else max(10, min(args.steps, 200))
 
     def e2e_step():
         qq = q_host.to(dev, non_blocking=True)
@@ -477,7 +517,7 @@ def main() -> int:
         res = paged_attention_decode(qq, kc, vc, ss, tt, softmax_scale=scale, max_seq_len=CTX_HI)
         o_host.copy_(res, non_blocking=True)
 
-    for _ in range(3):
+    for _ in range(3 if e2e_steps else 0):
         e2e_step()
     torch.cuda.synchronize()
     if dist:
@@ -488,13 +528,13 @@ def main() -> int:
         e2e_step()
     e1.record()
     torch.cuda.synchronize()
-    e2e_ms = max(e0.elapsed_time(e1), 1e3 * (time.perf_counter() - t0))
+    e2e_ms = max(e0.elapsed_time(e1), 1e3 * (time.perf_counter() - t0), 1e-6)
     if dist:
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e = {
-        "value": BATCH * e2e_steps / (e2e_ms * 1e-3),
+    e2e = None if not e2e_steps else {
+        "value": batch * e2e_steps / (e2e_ms * 1e-3),
         "unit": "tok/s",
         "h2d_bytes_per_step": q_host.numel() * 2 + s_host.numel() * 4 + t_host.numel() * 4,
         "d2h_bytes_per_step": o_host.numel() * 2,
@@ -509,7 +549,7 @@ def main() -> int:
         per_op = per_op_table(dev, peaks)
 
     cpu = None
-    if rank == 0 and n == 1 and not args.no_cpu:
+    if rank == 0 and n == 1 and not args.no_cpu and batch == BATCH:
         torch.set_num_threads(os.cpu_count() or 1)
         t_one, _, _ = oracle_decode_rate(ctx, q_all, 1, 1)
         per_call = max(1, min(BATCH, int(4.0 * t_one)))
@@ -535,7 +575,8 @@ def main() -> int:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": workload_config(n),
+        "config": workload_config(n) if batch == BATCH and pool == POOL else
+        {**workload_config(n), "profiling_case": f"batch {batch}, pool {pool}"},
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,

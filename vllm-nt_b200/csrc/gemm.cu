@@ -327,6 +327,236 @@ int make_kmajor_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows,
   return NTB200_OK;
 }
 
+// ------------------------------------------------------------------------------------
+// Small-M path (M <= 128: decode batches).  out^T = W . x^T ("swap AB"): the weight tile
+// fills the UMMA M=128 side, the few token rows are the UMMA N side (padded to MP = 16 ..
+// 128; rows past M are TMA zero-fill and cost no HBM traffic).  With only N/128 weight
+// tiles, K is split across the CTAs of a thread-block cluster (<= 8); each CTA parks its
+// fp32 partial tile in its own shared memory and, after a cluster barrier, every CTA sums
+// a share of the output rows across the cluster through distributed shared memory and
+// writes them (bias added, rounded).  One launch, no global workspace.
+// ------------------------------------------------------------------------------------
+
+constexpr int kSmallStages = 6;
+
+template <int MP>
+struct SmallSmem {
+  static constexpr int kXTile = MP * BK * 2;
+  static constexpr int kStage = kATileBytes + kXTile;  // 128 weight rows + MP x rows
+  static constexpr int kRing = 0;
+  static constexpr int kFull = kSmallStages * kStage;
+  static constexpr int kEmpty = kFull + 8 * kSmallStages;
+  static constexpr int kTmemFull = kEmpty + 8 * kSmallStages;
+  static constexpr int kTmemBase = kTmemFull + 8;
+  static constexpr int kEnd = kTmemBase + 8;
+  static constexpr int kDynamicBytes = kEnd + 1024;
+  static constexpr int kTmemCols = MP < 32 ? 32 : MP;
+  static_assert(MP * BM * 4 <= kSmallStages * kStage, "partial tile must fit in the ring");
+};
+
+struct SmallParams {
+  void* out;
+  const void* bias;
+  int64_t M, N;
+  int64_t out_stride;
+  int splits;
+  int k_steps_per_split;
+  int k_steps_total;
+  unsigned int* err;
+};
+
+__device__ __forceinline__ void tmem_ld_16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Remote shared-memory load.  Volatile keeps it after the (volatile) cluster barrier; no
+// memory clobber, so that several of these can be in flight before their values are used.
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
+  return v;
+}
+
+template <typename T, int MP>
+__global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
+    const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
+    const SmallParams p) {
+  using L = SmallSmem<MP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kFull);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L::kEmpty);
+  uint64_t* tmem_full = reinterpret_cast<uint64_t*>(smem + L::kTmemFull);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemBase);
+  const uint32_t ring = smem_u32(smem + L::kRing);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int split = blockIdx.x % p.splits;  // == rank in the cluster
+  const int ntile = blockIdx.x / p.splits;
+  const int kb0 = split * p.k_steps_per_split;
+  const int kb1 = min(kb0 + p.k_steps_per_split, p.k_steps_total);
+  const int nk = kb1 > kb0 ? kb1 - kb0 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSmallStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_base_slot)),
+                 "r"(L::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&w_map)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&x_map)) : "memory");
+      int issued = 0;
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % kSmallStages;
+        if (it >= kSmallStages && !mbar_wait(&empty[s], ((it / kSmallStages) - 1) & 1, p.err)) break;
+        mbar_arrive_expect_tx(&full[s], L::kStage);
+        const uint32_t w_dst = ring + s * L::kStage;
+        const uint32_t x_dst = w_dst + kATileBytes;
+        tma_load_2d(w_dst, &w_map, (kb0 + it) * BK, ntile * BM, smem_u32(&full[s]));
+        tma_load_2d(x_dst, &x_map, (kb0 + it) * BK, 0, smem_u32(&full[s]));
+        issued = it + 1;
+      }
+      const int first = issued > kSmallStages ? issued - kSmallStages : 0;
+      for (int j = first; j < issued; ++j) mbar_wait(&full[j % kSmallStages], (j / kSmallStages) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(std::is_same<T, __nv_bfloat16>::value, BM, MP);
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % kSmallStages;
+        if (!mbar_wait(&full[s], (it / kSmallStages) & 1, p.err)) break;
+        tc_fence_after();
+        const uint32_t w_addr = ring + s * L::kStage;
+        const uint64_t adesc = sw128_kmajor_desc(w_addr);
+        const uint64_t bdesc = sw128_kmajor_desc(w_addr + kATileBytes);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)
+          umma_f16(tmem_base, adesc + 2 * k, bdesc + 2 * k, idesc, (it > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(tmem_full);  // also the "all MMAs done" point before TMEM is released
+    }
+  } else {
+    // epilogue warps: TMEM (lane = weight row n, column = token m) -> smem partial [MP][128]
+    const int quad = warp & 3;
+    const int n_local = quad * 32 + lane;
+    float* part = reinterpret_cast<float*>(smem + L::kRing);
+    const bool ok = mbar_wait(tmem_full, 0, p.err);
+    tc_fence_after();
+#pragma unroll 1
+    for (int c = 0; c < MP / 16; ++c) {
+      uint32_t r[16];
+      __syncwarp();
+      tmem_ld_16(tmem_base + (uint32_t(quad * 32) << 16) + c * 16, r);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        part[(c * 16 + i) * BM + n_local] = (ok && nk > 0) ? __uint_as_float(r[i]) : 0.f;
+    }
+    tc_fence_before();
+  }
+
+  // every CTA of the cluster has its partial tile in shared memory
+  cluster_sync_all();
+  if (threadIdx.x < BM) {
+    const int n_local = threadIdx.x;
+    const int64_t n = int64_t(ntile) * BM + n_local;
+    const uint32_t part_addr = smem_u32(smem + L::kRing);
+    T* out = static_cast<T*>(p.out);
+    const T* bias = static_cast<const T*>(p.bias);
+    const float b = (bias != nullptr && n < p.N) ? Elem<T>::to_f(bias[n]) : 0.f;
+    for (int64_t m = split; m < p.M; m += p.splits) {
+      const uint32_t off = part_addr + uint32_t((m * BM + n_local) * 4);
+      float v[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) v[r] = r < p.splits ? ld_dsmem_f32(off, uint32_t(r)) : 0.f;
+      float acc = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) acc += v[r];
+      if (n < p.N) out[m * p.out_stride + n] = Elem<T>::from_f(acc + b);
+    }
+  }
+  // no CTA may leave (or free its shared memory) while its partner still reads it
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::kTmemCols)
+                 : "memory");
+  }
+}
+
+template <typename T, int MP>
+int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, int n_tiles,
+                 cudaStream_t s, int attr_slot) {
+  using L = SmallSmem<MP>;
+  const void* fn = reinterpret_cast<const void*>(gemm_small_m_kernel<T, MP>);
+  int st = ensure_smem_attribute(fn, L::kDynamicBytes, attr_slot);
+  if (st != NTB200_OK) return st;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * prm.splits));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kDynamicBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(prm.splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_m_kernel<T, MP>, wmap, xmap, prm);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(NTB200_ERR_CUDA, "linear (small M): launch failed: %s", cudaGetErrorString(e));
+  }
+  return NTB200_OK;
+}
+
+template <typename T>
+int dispatch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, int n_tiles,
+                   int mp, cudaStream_t s, int slot_base) {
+  switch (mp) {
+    case 16: return launch_small<T, 16>(wmap, xmap, prm, n_tiles, s, slot_base + 0);
+    case 32: return launch_small<T, 32>(wmap, xmap, prm, n_tiles, s, slot_base + 1);
+    case 64: return launch_small<T, 64>(wmap, xmap, prm, n_tiles, s, slot_base + 2);
+    default: return launch_small<T, 128>(wmap, xmap, prm, n_tiles, s, slot_base + 3);
+  }
+}
+
 }  // namespace
 }  // namespace ntb200
 
@@ -353,9 +583,39 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     return fail(NTB200_ERR_INVALID_ARGUMENT, "linear: row stride too small");
   if (!aligned16(x) || !aligned16(weight) || x_row_stride % 8 != 0 || weight_row_stride % 8 != 0)
     return fail(NTB200_ERR_MISALIGNED, "linear: x/weight must be 16-byte aligned with row strides %% 8 == 0");
+  const bool bf16 = dtype == NTB200_DTYPE_BF16;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M <= 128) {
+    // swap-AB + cluster split-K path for decode-sized batches
+    const int64_t n_tiles = ceil_div(N, BM);
+    if (n_tiles > 0x7fffffff / 8) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
+    const int ksteps = static_cast<int>(ceil_div(K, BK));
+    int splits = static_cast<int>(num_sms() / n_tiles);
+    splits = splits < 1 ? 1 : (splits > 8 ? 8 : splits);
+    if (splits > ksteps) splits = ksteps;
+    const int per = static_cast<int>(ceil_div(ksteps, splits));
+    splits = static_cast<int>(ceil_div(ksteps, per));  // no empty split
+    const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+    CUtensorMap wmap, xmap;
+    int st = make_kmajor_map(&wmap, weight, bf16, N, K, weight_row_stride, BM);
+    if (st != NTB200_OK) return st;
+    st = make_kmajor_map(&xmap, x, bf16, M, K, x_row_stride, mp);
+    if (st != NTB200_OK) return st;
+    SmallParams sp;
+    sp.out = out;
+    sp.bias = bias;
+    sp.M = M;
+    sp.N = N;
+    sp.out_stride = out_row_stride;
+    sp.splits = splits;
+    sp.k_steps_per_split = per;
+    sp.k_steps_total = ksteps;
+    sp.err = device_error_word();
+    return bf16 ? dispatch_small<__nv_bfloat16>(wmap, xmap, sp, static_cast<int>(n_tiles), mp, s, 4)
+                : dispatch_small<__half>(wmap, xmap, sp, static_cast<int>(n_tiles), mp, s, 8);
+  }
   const int64_t mblocks = ceil_div(M, BM), nblocks = ceil_div(N, BN);
   if (mblocks * nblocks > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
-  const bool bf16 = dtype == NTB200_DTYPE_BF16;
   CUtensorMap amap, bmap;
   int st = make_kmajor_map(&amap, x, bf16, M, K, x_row_stride, BM);
   if (st != NTB200_OK) return st;
@@ -375,7 +635,6 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
   const int64_t tiles = mblocks * nblocks;
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
   const int smem = GemmSmem::kDynamicBytes;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (bf16) {
     st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__nv_bfloat16>), smem, 2);
     if (st != NTB200_OK) return st;

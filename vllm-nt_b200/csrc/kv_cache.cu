@@ -43,12 +43,24 @@ __device__ __forceinline__ void st_stream<uint8_t>(uint8_t* p, uint8_t v) {
 
 // All strides in bytes.
 template <typename U, typename S>
-__global__ void __launch_bounds__(256) reshape_and_cache_kernel(
+__global__ void __launch_bounds__(1024) reshape_and_cache_kernel(
     const char* __restrict__ key, const char* __restrict__ value, char* __restrict__ kc,
     char* __restrict__ vc, const S* __restrict__ slots, int64_t num_slots, int64_t block_size,
     int num_heads, int units_per_head, int64_t kts, int64_t khs, int64_t vts, int64_t vhs,
     int64_t cbs, int64_t cps, int64_t chs, unsigned int* err) {
   const int64_t t = blockIdx.x;
+  const int per_tensor = num_heads * units_per_head;
+  // The first item's load does not depend on the slot: issue it together with the slot
+  // read so the two memory latencies overlap instead of adding up.
+  const int item0 = threadIdx.x;
+  U first{};
+  if (item0 < 2 * per_tensor) {
+    const bool is_v = item0 >= per_tensor;
+    const int rem = is_v ? item0 - per_tensor : item0;
+    const int h = rem / units_per_head;
+    const char* src = is_v ? value + t * vts + h * vhs : key + t * kts + h * khs;
+    first = ld_stream(reinterpret_cast<const U*>(src) + (rem - h * units_per_head));
+  }
   const int64_t slot = static_cast<int64_t>(slots[t]);
   if (slot < 0) return;  // padding token
   if (slot >= num_slots) {
@@ -57,15 +69,17 @@ __global__ void __launch_bounds__(256) reshape_and_cache_kernel(
   }
   const int64_t blk = slot / block_size;
   const int64_t dst_row = blk * cbs + (slot - blk * block_size) * cps;
-  const int per_tensor = num_heads * units_per_head;
-  for (int item = threadIdx.x; item < 2 * per_tensor; item += blockDim.x) {
+  for (int item = item0; item < 2 * per_tensor; item += blockDim.x) {
     const bool is_v = item >= per_tensor;
     const int rem = is_v ? item - per_tensor : item;
     const int h = rem / units_per_head;
     const int u = rem - h * units_per_head;
-    const char* src = is_v ? value + t * vts + h * vhs : key + t * kts + h * khs;
     char* dst = (is_v ? vc : kc) + dst_row + h * chs;
-    const U v = ld_stream(reinterpret_cast<const U*>(src) + u);
+    U v = first;
+    if (item != item0) {
+      const char* src = is_v ? value + t * vts + h * vhs : key + t * kts + h * khs;
+      v = ld_stream(reinterpret_cast<const U*>(src) + u);
+    }
     st_stream(reinterpret_cast<U*>(dst) + u, v);
   }
 }
@@ -77,7 +91,8 @@ int launch(const void* key, const void* value, void* kc, void* vc, const void* s
            int64_t cps, int64_t chs, cudaStream_t stream) {
   const int uph = static_cast<int>(head_bytes / sizeof(U));
   const int64_t items = 2 * heads * uph;
-  const int threads = items >= 256 ? 256 : static_cast<int>(ceil_div(items, 32) * 32);
+  // one unit per thread where the row allows it (all loads of a token in flight at once)
+  const int threads = items >= 1024 ? 1024 : static_cast<int>(ceil_div(items, 32) * 32);
   reshape_and_cache_kernel<U, S><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
       static_cast<const char*>(key), static_cast<const char*>(value), static_cast<char*>(kc),
       static_cast<char*>(vc), static_cast<const S*>(slots), num_slots, block_size,

@@ -86,26 +86,39 @@ __global__ void __launch_bounds__(THREADS) rms_norm_kernel(
     for (int j = 0; j < VEC; ++j) sumsq += t[j] * t[j];
   }
 
+  // weight of the register-resident vectors, fetched before the reduction so that its
+  // latency overlaps the block-wide sum
+  Vec<T, VEC> wraw[kMaxItems];
+#pragma unroll
+  for (int it = 0; it < kMaxItems; ++it) {
+    const int64_t vi = threadIdx.x + int64_t(it) * THREADS;
+    if (weight != nullptr && vi < nvec) wraw[it] = *reinterpret_cast<const Vec<T, VEC>*>(weight + vi * VEC);
+  }
+
   const float total = block_sum<THREADS>(sumsq, red);
   const float rstd = rsqrtf(total / static_cast<float>(hidden) + eps);
 
-  auto emit = [&](int64_t vi, const float (&v)[VEC]) {
-    float w[VEC];
-    if (weight != nullptr) {
-      load_f<T, VEC>(weight + vi * VEC, w);
-    } else {
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) w[j] = 1.f;
-    }
+  auto emit_w = [&](int64_t vi, const float (&v)[VEC], const Vec<T, VEC>* w) {
     float y[VEC];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) y[j] = Elem<T>::round(v[j] * rstd) * w[j];
+    for (int j = 0; j < VEC; ++j) {
+      const float wj = w != nullptr ? Elem<T>::to_f(w->v[j]) : 1.f;
+      y[j] = Elem<T>::round(v[j] * rstd) * wj;
+    }
     store_f<T, VEC>(orow + vi * VEC, y);
+  };
+  auto emit = [&](int64_t vi, const float (&v)[VEC]) {
+    if (weight != nullptr) {
+      const Vec<T, VEC> w = *reinterpret_cast<const Vec<T, VEC>*>(weight + vi * VEC);
+      emit_w(vi, v, &w);
+    } else {
+      emit_w(vi, v, nullptr);
+    }
   };
 #pragma unroll
   for (int it = 0; it < kMaxItems; ++it) {
     const int64_t vi = threadIdx.x + int64_t(it) * THREADS;
-    if (vi < nvec) emit(vi, s[it]);
+    if (vi < nvec) emit_w(vi, s[it], weight != nullptr ? &wraw[it] : nullptr);
   }
   for (int64_t vi = threadIdx.x + int64_t(kMaxItems) * THREADS; vi < nvec; vi += THREADS) {
     float t[VEC];
@@ -135,10 +148,10 @@ int launch_rows(T* out, T* residual, const T* x, const T* w, int64_t rows, int64
     NTB200_RMS_LAUNCH(128);
   } else if (want <= 256) {
     NTB200_RMS_LAUNCH(256);
-  } else if (want <= 512) {
-    NTB200_RMS_LAUNCH(512);
   } else {
-    NTB200_RMS_LAUNCH(1024);
+    // 512 threads keep 4 vectors each in registers without spilling; longer rows take
+    // the second (L2) pass
+    NTB200_RMS_LAUNCH(512);
   }
 #undef NTB200_RMS_LAUNCH
   return check_launch("rms_norm");

@@ -28,28 +28,43 @@ __device__ __forceinline__ void rotate(float x1, float x2, float c, float s, flo
 }
 
 template <typename T, int VEC, typename P>
-__global__ void __launch_bounds__(128) rope_neox_kernel(
+__global__ void __launch_bounds__(1024) rope_neox_kernel(
     const P* __restrict__ positions, T* __restrict__ q, T* __restrict__ k,
     const T* __restrict__ cache, int num_q_heads, int num_k_heads, int half,
     int64_t q_tok, int64_t q_head, int64_t k_tok, int64_t k_head, int64_t cache_row,
     int64_t cache_rows, unsigned int* err) {
   const int64_t t = blockIdx.x;
+  const int vph = half / VEC;  // vectors per head
+  const int total = (num_q_heads + (k != nullptr ? num_k_heads : 0)) * vph;
+  auto head_base = [&](int h) -> T* {
+    return h < num_q_heads ? q + t * q_tok + int64_t(h) * q_head
+                           : k + t * k_tok + int64_t(h - num_q_heads) * k_head;
+  };
+  // The x loads of this thread's first item do not depend on the position: issue them
+  // before the position read so the two latencies overlap.
+  float x1[VEC], x2[VEC];
+  const int item0 = threadIdx.x;
+  if (item0 < total) {
+    const int h = item0 / vph;
+    const int i = (item0 - h * vph) * VEC;
+    load_f<T, VEC>(head_base(h) + i, x1);
+    load_f<T, VEC>(head_base(h) + half + i, x2);
+  }
   const int64_t pos = static_cast<int64_t>(positions[t]);
   if (pos < 0 || pos >= cache_rows) {
     if (threadIdx.x == 0) raise_device_error(err, NTB200_DEVERR_INDEX_RANGE);
     return;
   }
   const T* cs = cache + pos * cache_row;
-  const int vph = half / VEC;  // vectors per head
-  const int total = (num_q_heads + (k != nullptr ? num_k_heads : 0)) * vph;
-  for (int item = threadIdx.x; item < total; item += blockDim.x) {
+  for (int item = item0; item < total; item += blockDim.x) {
     const int h = item / vph;
     const int i = (item - h * vph) * VEC;
-    T* base = h < num_q_heads ? q + t * q_tok + int64_t(h) * q_head
-                              : k + t * k_tok + int64_t(h - num_q_heads) * k_head;
-    float x1[VEC], x2[VEC], c[VEC], s[VEC], o1[VEC], o2[VEC];
-    load_f<T, VEC>(base + i, x1);
-    load_f<T, VEC>(base + half + i, x2);
+    T* base = head_base(h);
+    float c[VEC], s[VEC], o1[VEC], o2[VEC];
+    if (item != item0) {
+      load_f<T, VEC>(base + i, x1);
+      load_f<T, VEC>(base + half + i, x2);
+    }
     load_f<T, VEC>(cs + i, c);
     load_f<T, VEC>(cs + half + i, s);
 #pragma unroll
@@ -70,12 +85,17 @@ int launch(const void* positions, void* q, void* k, const void* cache, int64_t t
                 aligned16(q) && aligned16(cache);
   if (k != nullptr) vec_ok = vec_ok && kt % kVec == 0 && kh % kVec == 0 && aligned16(k);
   const unsigned grid = static_cast<unsigned>(tokens);
+  // one vector item per thread where possible: every load of the token is in flight at once
+  auto threads_for = [&](int64_t vec) {
+    const int64_t items = (hq + (k != nullptr ? hk : 0)) * (half / vec);
+    return static_cast<int>(items >= 1024 ? 1024 : (items < 32 ? 32 : ceil_div(items, 32) * 32));
+  };
   if (vec_ok) {
-    rope_neox_kernel<T, kVec, P><<<grid, 128, 0, stream>>>(
+    rope_neox_kernel<T, kVec, P><<<grid, threads_for(kVec), 0, stream>>>(
         static_cast<const P*>(positions), static_cast<T*>(q), static_cast<T*>(k),
         static_cast<const T*>(cache), int(hq), int(hk), int(half), qt, qh, kt, kh, cr, rows, err);
   } else {
-    rope_neox_kernel<T, 1, P><<<grid, 128, 0, stream>>>(
+    rope_neox_kernel<T, 1, P><<<grid, threads_for(1), 0, stream>>>(
         static_cast<const P*>(positions), static_cast<T*>(q), static_cast<T*>(k),
         static_cast<const T*>(cache), int(hq), int(hk), int(half), qt, qh, kt, kh, cr, rows, err);
   }
