@@ -156,6 +156,26 @@ int ntb200_paged_attention_decode(
     int64_t cache_page_stride, int64_t cache_head_stride, void* workspace,
     size_t workspace_bytes, int dtype, void* stream);
 
+/* The same decode without a caller workspace, for callers that cannot allocate device
+ * memory at the call: a serving loop that must not call cudaMalloc/cudaFree while decoding
+ * (they can synchronise the device and take a process-wide lock), code being recorded
+ * into a CUDA graph, or a host that binds only this C ABI and has no device allocator.
+ * The split-K partials go to a fixed 64 MiB array compiled into the library, held by every
+ * GPU on which this entry point is set up until the process exits.  A call that needs more
+ * scratch than that returns NTB200_ERR_WORKSPACE without launching.  The first call on a
+ * device resolves the array's address (cudaGetSymbolAddress), so make it before any stream
+ * capture.  All calls on a device share the array: calls that overlap on the GPU race;
+ * order them on one stream.  Arguments as ntb200_paged_attention_decode minus the
+ * workspace.  This entry point has no counterpart in the reference. */
+int ntb200_paged_attention_decode_noalloc(
+    void* out, const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* seq_lens, const int32_t* block_tables, int64_t num_seqs,
+    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size,
+    int64_t num_blocks, int64_t max_blocks_per_seq, int64_t block_table_stride,
+    int64_t max_seq_len, float scale, int64_t q_seq_stride, int64_t q_head_stride,
+    int64_t out_seq_stride, int64_t out_head_stride, int64_t cache_block_stride,
+    int64_t cache_page_stride, int64_t cache_head_stride, int dtype, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Dense projection  out[M, N] = x[M, K] . weight[N, K]^T (+ bias[N]),  fp32 accumulate,
  * tcgen05/TMEM tensor cores fed by TMA.  dtype BF16 or F16; K a multiple of 8, rows 16-byte

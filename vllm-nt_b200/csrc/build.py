@@ -37,6 +37,7 @@ KERNEL_SOURCES = (
     "kv_cache.cu",
     "embedding.cu",
     "paged_decode.cu",
+    "paged_decode_noalloc.cu",
     "gemm.cu",
 )
 SHARED_HEADERS = (CSRC / "common.cuh", INCLUDE / "ntb200.h", Path(__file__).resolve())

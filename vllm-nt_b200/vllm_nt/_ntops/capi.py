@@ -59,6 +59,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_int64, c_int64,
          c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_size_t, c_int, c_void_p],
     ),
+    "ntb200_paged_attention_decode_noalloc": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+         c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_float, c_int64, c_int64,
+         c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p],
+    ),
     "ntb200_linear_workspace_size": (c_size_t, [c_int64, c_int64, c_int64]),
     "ntb200_linear": (
         c_int,
