@@ -253,14 +253,16 @@ def time_graph(fn_list, iters: int) -> float:
             fn_list[i % len(fn_list)]()
     graph.replay()
     torch.cuda.synchronize()
-    reps = 3
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
+    # best of 5 replays (each replay = `iters` launches timed with CUDA events)
+    best = float("inf")
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / (reps * iters)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) / iters)
+    return best
 
 
 def per_op_table(dev, peaks) -> dict:

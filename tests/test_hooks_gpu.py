@@ -1,0 +1,145 @@
+"""The plugin's hooks on a GPU: vLLM layer objects dispatch into the B200 kernels (hits are
+counted under the b200 backend) and agree with the CPU oracle.  Uses vLLM's own classes
+(RMSNorm, SiluAndMul, RotaryEmbedding, Unquantized{Linear,Embedding}Method) and the
+FlashAttentionImpl hooks with a real paged KV cache."""
+
+import math
+from pathlib import Path
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+import oracle
+from _util import bits_equal, cuda_device, seeded
+
+pytestmark = pytest.mark.gpu
+pytest.importorskip("vllm")
+ROOT = Path(__file__).resolve().parents[1]
+TOL = dict(rtol=2e-2, atol=2e-2)
+
+
+@pytest.fixture(autouse=True)
+def _b200_config(monkeypatch):
+    cuda_device()
+    import vllm_nt
+    from vllm_nt._ntops import patching
+
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml"))
+    vllm_nt.register()
+    patching._reset_usage_state()
+    yield patching
+    patching._reset_usage_state()
+
+
+@pytest.fixture()
+def vllm_ctx():
+    from vllm.config import VllmConfig, set_current_vllm_config
+
+    with set_current_vllm_config(VllmConfig()):
+        yield
+
+
+def _hits(patching, op):
+    return patching.get_usage_summary()["operators"][op]["backends"].get("b200", {}).get("hits", 0)
+
+
+def test_rmsnorm_layer_runs_the_fused_kernel(_b200_config, vllm_ctx):
+    from vllm.model_executor.layers.layernorm import RMSNorm
+
+    layer = RMSNorm(4096, eps=1e-5).to(device="cuda", dtype=torch.bfloat16)
+    assert type(layer).__name__ == "NTRMSNorm"
+    g = seeded(0)
+    w = (1 + 0.1 * torch.randn(4096, generator=g)).to(torch.bfloat16)
+    layer.weight.data.copy_(w)
+    x = torch.randn(64, 4096, generator=g).to(torch.bfloat16)
+    r = torch.randn(64, 4096, generator=g).to(torch.bfloat16)
+    out, res = layer(x.cuda(), r.cuda())
+    ref, ref_r = oracle.fused_add_rms_norm(x, r, w, 1e-5)
+    torch.testing.assert_close(out.float().cpu(), ref.float(), **TOL)
+    assert bits_equal(res.cpu(), ref_r)
+    plain = layer(x.cuda())
+    torch.testing.assert_close(plain.float().cpu(), oracle.rms_norm(x, w, 1e-5).float(), **TOL)
+    assert _hits(_b200_config, "RMSNorm") == 2
+
+
+def test_silu_and_mul_layer(_b200_config, vllm_ctx):
+    from vllm.model_executor.layers.activation import SiluAndMul
+
+    layer = SiluAndMul()
+    x = torch.randn(16, 2 * 14336, generator=seeded(1)).to(torch.bfloat16)
+    out = layer(x.cuda())
+    torch.testing.assert_close(out.float().cpu(), oracle.silu_and_mul(x).float(), **TOL)
+    assert _hits(_b200_config, "SiluAndMul") == 1
+
+
+def test_rotary_embedding_layer_bit_exact(_b200_config, vllm_ctx):
+    from vllm.model_executor.layers.rotary_embedding.base import RotaryEmbedding
+
+    rope = RotaryEmbedding(128, 128, 4096, 500000.0, True, torch.bfloat16).cuda()
+    g = seeded(2)
+    pos = torch.randint(0, 4096, (24,), generator=g)
+    qkv = torch.randn(24, (32 + 16) * 128, generator=g).to(torch.bfloat16)
+    q, k = qkv[:, : 32 * 128], qkv[:, 32 * 128 : 40 * 128]
+    qd_all = qkv.cuda()
+    qd, kd = qd_all[:, : 32 * 128], qd_all[:, 32 * 128 : 40 * 128]
+    rope(pos.cuda(), qd, kd)
+    cache = rope.cos_sin_cache.float().cpu()
+    ref_q, ref_k = oracle.rope_neox(pos, q, k, cache, 128, 128)
+    assert bits_equal(qd.cpu().contiguous(), ref_q.contiguous()) and bits_equal(kd.cpu().contiguous(), ref_k.contiguous())
+    assert _hits(_b200_config, "RoPE") == 1
+
+
+def test_linear_and_embedding_methods(_b200_config, vllm_ctx):
+    from vllm.model_executor.layers.linear import UnquantizedLinearMethod
+    from vllm.model_executor.layers.vocab_parallel_embedding import UnquantizedEmbeddingMethod
+
+    g = seeded(3)
+    w = (0.02 * torch.randn(6144, 4096, generator=g)).to(torch.bfloat16)
+    x = torch.randn(7, 4096, generator=g).to(torch.bfloat16)
+    layer = SimpleNamespace(weight=torch.nn.Parameter(w.cuda(), requires_grad=False))
+    out = UnquantizedLinearMethod().apply(layer, x.cuda())
+    torch.testing.assert_close(out.float().cpu(), oracle.linear(x, w), **TOL)
+    assert _hits(_b200_config, "MatMul") == 1
+    table = torch.randn(1000, 4096, generator=g).to(torch.bfloat16)
+    emb_layer = SimpleNamespace(weight=torch.nn.Parameter(table.cuda(), requires_grad=False))
+    ids = torch.randint(0, 1000, (2, 5), generator=g)
+    e = UnquantizedEmbeddingMethod().embedding(emb_layer, ids.cuda())
+    assert torch.equal(e.cpu(), table[ids])
+    head = UnquantizedEmbeddingMethod().apply(emb_layer, x[:, :4096].cuda())
+    torch.testing.assert_close(head.float().cpu(), oracle.linear(x, table), **TOL)
+    assert _hits(_b200_config, "Embedding") == 1 and _hits(_b200_config, "LMHead") == 1
+
+
+def test_flash_attention_impl_hooks_store_and_decode(_b200_config):
+    patching = _b200_config
+    fwd = patching._build_flash_attn_forward(lambda *a, **k: pytest.fail("decode fell back to vLLM"))
+    upd = patching._build_flash_attn_kv_update(lambda *a, **k: pytest.fail("store fell back to vLLM"))
+    impl = SimpleNamespace(num_heads=32, num_kv_heads=8, head_size=128, scale=1 / math.sqrt(128), attn_type="decoder",
+                           kv_cache_dtype="auto", alibi_slopes=None, logits_soft_cap=None, sinks=None,
+                           sliding_window=None, dcp_world_size=1)
+    g = seeded(4)
+    nb = 64
+    kv = torch.randn(2, nb, 16, 8, 128, generator=g).to(torch.bfloat16)
+    ctx = [5, 40, 200]  # tokens already cached; this step appends one token each
+    table = torch.randperm(nb, generator=g)[:3 * 16].view(3, 16).to(torch.int32)
+    slots = torch.tensor([int(table[b, c // 16]) * 16 + c % 16 for b, c in enumerate(ctx)])
+    key = torch.randn(4, 8, 128, generator=g).to(torch.bfloat16)  # 3 real rows + 1 padding row
+    value = torch.randn(4, 8, 128, generator=g).to(torch.bfloat16)
+    kvd = kv.cuda()
+    upd(impl, None, key.cuda(), value.cuda(), kvd, slots.cuda())
+    ref_kv = kv.clone()
+    ref_kv[0][slots // 16, slots % 16] = key[:3]
+    ref_kv[1][slots // 16, slots % 16] = value[:3]
+    assert torch.equal(kvd.cpu(), ref_kv)
+    q = torch.randn(4, 32, 128, generator=g).to(torch.bfloat16)
+    out = torch.zeros(4, 32 * 128, dtype=torch.bfloat16, device="cuda")
+    seq = torch.tensor([c + 1 for c in ctx], dtype=torch.int32)
+    meta = SimpleNamespace(num_actual_tokens=3, max_query_len=1, use_cascade=False, max_seq_len=max(seq).item(),
+                           query_start_loc=torch.arange(4, dtype=torch.int32).cuda(), seq_lens=seq.cuda(),
+                           block_table=table.cuda())
+    fwd(impl, None, q.cuda(), None, None, kvd, meta, out)
+    ref = oracle.paged_decode(q[:3], ref_kv[0], ref_kv[1], seq, table, impl.scale)
+    torch.testing.assert_close(out[:3].view(3, 32, 128).float().cpu(), ref, **TOL)
+    assert not out[3].any()
+    assert _hits(patching, "StoreKVCache") == 1 and _hits(patching, "PagedAttentionDecode") == 1

@@ -337,10 +337,15 @@ int make_kmajor_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows,
 // writes them (bias added, rounded).  One launch, no global workspace.
 // ------------------------------------------------------------------------------------
 
-constexpr int kSmallStages = 6;
+// ring depth per token tile: about 96 KB of stages, so two CTAs fit on an SM
+template <int MP>
+constexpr int small_stages() {
+  return (96 * 1024) / (kATileBytes + MP * BK * 2) < 3 ? 3 : (96 * 1024) / (kATileBytes + MP * BK * 2);
+}
 
 template <int MP>
 struct SmallSmem {
+  static constexpr int kSmallStages = small_stages<MP>();
   static constexpr int kXTile = MP * BK * 2;
   static constexpr int kStage = kATileBytes + kXTile;  // 128 weight rows + MP x rows
   static constexpr int kRing = 0;
@@ -383,13 +388,16 @@ __device__ __forceinline__ void cluster_sync_all() {
       "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Remote shared-memory load.  Volatile keeps it after the (volatile) cluster barrier; no
-// memory clobber, so that several of these can be in flight before their values are used.
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
+// Remote shared-memory load of 4 floats.  Volatile keeps it after the (volatile) cluster
+// barrier; no memory clobber, so that several of these can be in flight before their
+// values are used.
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t local_addr, uint32_t rank) {
   uint32_t remote;
-  float v;
+  float4 v;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote));
   return v;
 }
 
@@ -398,6 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
     const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
     const SmallParams p) {
   using L = SmallSmem<MP>;
+  constexpr int kSmallStages = L::kSmallStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -491,22 +500,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
 
   // every CTA of the cluster has its partial tile in shared memory
   cluster_sync_all();
-  if (threadIdx.x < BM) {
-    const int n_local = threadIdx.x;
-    const int64_t n = int64_t(ntile) * BM + n_local;
+  {
+    // this CTA owns output rows [r0, r1); a row is 128 partial floats = 32 float4, so the
+    // 192 threads cover 6 rows per pass, and each pass has its splits x float4 remote loads
+    // in flight before any is summed
+    const int rows_per = static_cast<int>((p.M + p.splits - 1) / p.splits);
+    const int r0 = split * rows_per;
+    const int r1 = static_cast<int>(p.M < int64_t(r0) + rows_per ? p.M : int64_t(r0) + rows_per);
+    const int q4 = threadIdx.x & 31;  // float4 column group: n_local = 4 * q4 .. +3
     const uint32_t part_addr = smem_u32(smem + L::kRing);
     T* out = static_cast<T*>(p.out);
     const T* bias = static_cast<const T*>(p.bias);
-    const float b = (bias != nullptr && n < p.N) ? Elem<T>::to_f(bias[n]) : 0.f;
-    for (int64_t m = split; m < p.M; m += p.splits) {
-      const uint32_t off = part_addr + uint32_t((m * BM + n_local) * 4);
-      float v[8];
+    const int64_t n0 = int64_t(ntile) * BM + 4 * q4;
+    float bvec[4];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) v[r] = r < p.splits ? ld_dsmem_f32(off, uint32_t(r)) : 0.f;
-      float acc = 0.f;
+    for (int i = 0; i < 4; ++i) bvec[i] = (bias != nullptr && n0 + i < p.N) ? Elem<T>::to_f(bias[n0 + i]) : 0.f;
+    for (int m = r0 + (threadIdx.x >> 5); m < r1; m += kThreads / 32) {
+      const uint32_t off = part_addr + uint32_t((m * BM + 4 * q4) * 4);
+      float4 v[8];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) acc += v[r];
-      if (n < p.N) out[m * p.out_stride + n] = Elem<T>::from_f(acc + b);
+      for (int r = 0; r < 8; ++r) v[r] = r < p.splits ? ld_dsmem_f32x4(off, uint32_t(r)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float acc[4] = {bvec[0], bvec[1], bvec[2], bvec[3]};
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        acc[0] += v[r].x;
+        acc[1] += v[r].y;
+        acc[2] += v[r].z;
+        acc[3] += v[r].w;
+      }
+      T* orow = out + int64_t(m) * p.out_stride;
+      if (n0 + 4 <= p.N && ((reinterpret_cast<uintptr_t>(orow + n0) & 7u) == 0)) {
+        store_f<T, 4>(orow + n0, acc);
+      } else {
+        for (int i = 0; i < 4; ++i)
+          if (n0 + i < p.N) orow[n0 + i] = Elem<T>::from_f(acc[i]);
+      }
     }
   }
   // no CTA may leave (or free its shared memory) while its partner still reads it

@@ -392,19 +392,31 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   if (nch > 0) {
     const int64_t unit0 = (int64_t(b) * num_kv + kvh) * max_chunks;
+    // lane c holds the log-sum-exp of chunks c, c+32, ...: one round trip for all of them
     float M = -INFINITY;
-    for (int64_t ch = 0; ch < nch; ++ch) M = fmaxf(M, part_lse[(unit0 + ch) * group + hh]);
+    for (int64_t ch = lane; ch < nch; ch += 32) M = fmaxf(M, part_lse[(unit0 + ch) * group + hh]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
     float wsum = 0.f;
-    for (int64_t ch = 0; ch < nch; ++ch) {
-      const float lse = part_lse[(unit0 + ch) * group + hh];
-      const float w = lse == -INFINITY ? 0.f : exp2f(lse - M);
-      wsum += w;
-      const float4 v = *reinterpret_cast<const float4*>(
-          part_o + ((unit0 + ch) * group + hh) * kHeadDim + lane * 4);
-      acc[0] += w * v.x;
-      acc[1] += w * v.y;
-      acc[2] += w * v.z;
-      acc[3] += w * v.w;
+    for (int64_t base = 0; base < nch; base += 32) {
+      const int64_t mine = base + lane;
+      float w_lane = 0.f;
+      if (mine < nch) {
+        const float lse = part_lse[(unit0 + mine) * group + hh];
+        w_lane = lse == -INFINITY ? 0.f : exp2f(lse - M);
+      }
+      const int n = static_cast<int>(nch - base < 32 ? nch - base : 32);
+      // the partial rows of this group of chunks are independent loads: issue them all
+      for (int j = 0; j < n; ++j) {
+        const float w = __shfl_sync(0xffffffffu, w_lane, j);
+        const float4 v = *reinterpret_cast<const float4*>(
+            part_o + ((unit0 + base + j) * group + hh) * kHeadDim + lane * 4);
+        wsum += w;
+        acc[0] += w * v.x;
+        acc[1] += w * v.y;
+        acc[2] += w * v.z;
+        acc[3] += w * v.w;
+      }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
