@@ -24,16 +24,19 @@ namespace ntb200 {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kATileBytes = BM * BK * 2;
-constexpr int kBTileBytes = BN * BK * 2;
-constexpr int kStageBytes = kATileBytes + kBTileBytes;
-constexpr int kTmemCols = 2 * BN;
 
-struct GemmSmem {
+// Tile width BN (UMMA N) of the large-M kernel: 256, 192 or 128, chosen per shape so that
+// the tiles fill whole waves of SMs.  The ring holds ~192-200 KB of stages either way.
+template <int BN_>
+struct GemmCfg {
+  static constexpr int BN = BN_;
+  static constexpr int kBTileBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 192 ? 5 : 6);
+  static constexpr int kTmemCols = 2 * BN <= 256 ? 256 : 512;  // two accumulators, power of 2
   static constexpr int kRing = 0;
   static constexpr int kFull = kStages * kStageBytes;
   static constexpr int kEmpty = kFull + 8 * kStages;
@@ -43,6 +46,7 @@ struct GemmSmem {
   static constexpr int kTmemBase = kMmaDone + 8;
   static constexpr int kEnd = kTmemBase + 8;
   static constexpr int kDynamicBytes = kEnd + 1024;
+  static_assert(kDynamicBytes <= 227 * 1024, "ring exceeds shared memory");
 };
 
 // K-major operand tile with 128-byte swizzle: 8-row atoms of 1024 bytes.
@@ -120,20 +124,26 @@ struct GemmParams {
   unsigned int* err;
 };
 
-template <typename T>
+template <typename T, int BN_>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
     const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
     const GemmParams p) {
+  using C = GemmCfg<BN_>;
+  constexpr int BN = C::BN;
+  constexpr int kStages = C::kStages;
+  constexpr int kStageBytes = C::kStageBytes;
+  constexpr int kTmemCols = C::kTmemCols;
+  constexpr int kAccStride = BN == 192 ? 256 : BN;  // TMEM column offset of the 2nd accumulator
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GemmSmem::kFull);
-  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + GemmSmem::kEmpty);
-  uint64_t* tmem_full = reinterpret_cast<uint64_t*>(smem + GemmSmem::kTmemFull);
-  uint64_t* tmem_empty = reinterpret_cast<uint64_t*>(smem + GemmSmem::kTmemEmpty);
-  uint64_t* mma_done = reinterpret_cast<uint64_t*>(smem + GemmSmem::kMmaDone);
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + GemmSmem::kTmemBase);
-  const uint32_t ring = smem_u32(smem + GemmSmem::kRing);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kFull);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + C::kEmpty);
+  uint64_t* tmem_full = reinterpret_cast<uint64_t*>(smem + C::kTmemFull);
+  uint64_t* tmem_empty = reinterpret_cast<uint64_t*>(smem + C::kTmemEmpty);
+  uint64_t* mma_done = reinterpret_cast<uint64_t*>(smem + C::kMmaDone);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemBase);
+  const uint32_t ring = smem_u32(smem + C::kRing);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -203,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
         const int use = local >> 1;
         if (use >= 1 && !mbar_wait(&tmem_empty[acc], (use - 1) & 1, p.err)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * kAccStride;
         for (int kb = 0; kb < k_steps; ++kb, ++it) {
           const uint32_t s = it % kStages;
           if (!mbar_wait(&full[s], (it / kStages) & 1, p.err)) {
@@ -250,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         uint32_t r[32];
         __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
-        tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + acc * BN + chunk * 32, r);
+        tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + acc * kAccStride + chunk * 32, r);
         const int64_t c0 = col0 + chunk * 32;
         if (row < p.M && c0 < p.N) {
         float v[32];
@@ -585,6 +595,59 @@ int dispatch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const Small
   }
 }
 
+// Tile width for the large-M kernel: the widest of 256/192/128 whose tiles fill the SMs'
+// waves (and cover N with little padding) to within 95% of the best candidate.
+int pick_tile_width(int64_t M, int64_t N, int sms) {
+  const int cands[3] = {256, 192, 128};
+  double eff[3], best = 0.0;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t nb = ceil_div(N, cands[i]);
+    const int64_t tiles = ceil_div(M, BM) * nb;
+    const int64_t waves = ceil_div(tiles, sms);
+    eff[i] = (double(tiles) / double(waves * sms)) * (double(N) / double(nb * cands[i]));
+    best = eff[i] > best ? eff[i] : best;
+  }
+  for (int i = 0; i < 3; ++i)
+    if (eff[i] >= 0.95 * best) return cands[i];
+  return 256;
+}
+
+template <int BNV>
+int launch_large(void* out, const void* x, const void* weight, const void* bias, int64_t M, int64_t N,
+                 int64_t K, int64_t xs, int64_t ws, int64_t os, bool bf16, cudaStream_t s) {
+  using C = GemmCfg<BNV>;
+  const int64_t mblocks = ceil_div(M, BM), nblocks = ceil_div(N, BNV);
+  if (mblocks * nblocks > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
+  CUtensorMap amap, bmap;
+  int st = make_kmajor_map(&amap, x, bf16, M, K, xs, BM);
+  if (st != NTB200_OK) return st;
+  st = make_kmajor_map(&bmap, weight, bf16, N, K, ws, BNV);
+  if (st != NTB200_OK) return st;
+  GemmParams prm;
+  prm.out = out;
+  prm.bias = bias;
+  prm.M = M;
+  prm.N = N;
+  prm.K = K;
+  prm.out_stride = os;
+  prm.num_m_blocks = static_cast<int>(mblocks);
+  prm.num_n_blocks = static_cast<int>(nblocks);
+  prm.err = device_error_word();
+  const int64_t tiles = mblocks * nblocks;
+  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
+  const int slot = 16 + (BNV == 256 ? 0 : (BNV == 192 ? 2 : 4)) + (bf16 ? 0 : 1);
+  if (bf16) {
+    st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__nv_bfloat16, BNV>), C::kDynamicBytes, slot);
+    if (st != NTB200_OK) return st;
+    gemm_tcgen05_kernel<__nv_bfloat16, BNV><<<grid, kThreads, C::kDynamicBytes, s>>>(amap, bmap, prm);
+  } else {
+    st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__half, BNV>), C::kDynamicBytes, slot);
+    if (st != NTB200_OK) return st;
+    gemm_tcgen05_kernel<__half, BNV><<<grid, kThreads, C::kDynamicBytes, s>>>(amap, bmap, prm);
+  }
+  return check_launch("linear");
+}
+
 }  // namespace
 }  // namespace ntb200
 
@@ -642,35 +705,10 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     return bf16 ? dispatch_small<__nv_bfloat16>(wmap, xmap, sp, static_cast<int>(n_tiles), mp, s, 4)
                 : dispatch_small<__half>(wmap, xmap, sp, static_cast<int>(n_tiles), mp, s, 8);
   }
-  const int64_t mblocks = ceil_div(M, BM), nblocks = ceil_div(N, BN);
-  if (mblocks * nblocks > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
-  CUtensorMap amap, bmap;
-  int st = make_kmajor_map(&amap, x, bf16, M, K, x_row_stride, BM);
-  if (st != NTB200_OK) return st;
-  st = make_kmajor_map(&bmap, weight, bf16, N, K, weight_row_stride, BN);
-  if (st != NTB200_OK) return st;
-
-  GemmParams prm;
-  prm.out = out;
-  prm.bias = bias;
-  prm.M = M;
-  prm.N = N;
-  prm.K = K;
-  prm.out_stride = out_row_stride;
-  prm.num_m_blocks = static_cast<int>(mblocks);
-  prm.num_n_blocks = static_cast<int>(nblocks);
-  prm.err = device_error_word();
-  const int64_t tiles = mblocks * nblocks;
-  const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  const int smem = GemmSmem::kDynamicBytes;
-  if (bf16) {
-    st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__nv_bfloat16>), smem, 2);
-    if (st != NTB200_OK) return st;
-    gemm_tcgen05_kernel<__nv_bfloat16><<<grid, kThreads, smem, s>>>(amap, bmap, prm);
-  } else {
-    st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__half>), smem, 3);
-    if (st != NTB200_OK) return st;
-    gemm_tcgen05_kernel<__half><<<grid, kThreads, smem, s>>>(amap, bmap, prm);
+  const int bn = pick_tile_width(M, N, num_sms());
+  switch (bn) {
+    case 128: return launch_large<128>(out, x, weight, bias, M, N, K, x_row_stride, weight_row_stride, out_row_stride, bf16, s);
+    case 192: return launch_large<192>(out, x, weight, bias, M, N, K, x_row_stride, weight_row_stride, out_row_stride, bf16, s);
+    default: return launch_large<256>(out, x, weight, bias, M, N, K, x_row_stride, weight_row_stride, out_row_stride, bf16, s);
   }
-  return check_launch("linear");
 }
