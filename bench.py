@@ -354,21 +354,99 @@ def per_op_table(dev, peaks) -> dict:
 
     # projection GEMM bf16 (fp32 accumulate)
     for (K, Nn, tag) in ((4096, 6144, "qkv"), (4096, 4096, "o_proj"), (4096, 28672, "gate_up"), (14336, 4096, "down")):
-        for M in (1, 16, 128, 1024, 8192):
+        for M in (1, 16, 128, 256, 1024, 8192):
             x = torch.randn(M, K, device=dev, generator=g, dtype=torch.bfloat16)
             wts = [0.02 * torch.randn(Nn, K, device=dev, generator=g, dtype=torch.bfloat16)
-                   for _ in range(max(1, math.ceil(3 * L2_BYTES / (Nn * K * 2))) if M <= 128 else 1)]
+                   for _ in range(max(1, math.ceil(3 * L2_BYTES / (Nn * K * 2))) if M <= 256 else 1)]
             out = torch.empty(M, Nn, device=dev, dtype=torch.bfloat16)
             fns = [lambda w_=w_: o.linear(out, x, w_, None, None) for w_ in wts]
             ms = time_graph(fns, max(4, 2 * len(wts)))
             flops = 2.0 * M * Nn * K
             nbytes = Nn * K * 2 + M * K * 2 + M * Nn * 2
             tf = flops / (ms * 1e-3) / 1e12
-            if M <= 128:
+            if M <= 256:
                 report(f"linear {tag} M={M}", nbytes, ms, {"TFLOP/s": round(tf, 2)})
             else:
                 res[f"linear {tag} M={M}"] = {"us": ms * 1e3, "TFLOP/s": round(tf, 1), "frac_of_bf16": round(tf / tens, 3)}
             del x, wts, out
+    return res
+
+
+def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
+    """Row-parallel projections (o_proj K=4096, down K=14336; N=4096) on n ranks: each rank
+    multiplies its K-shard, the partial outputs are summed across ranks with an NCCL
+    all-reduce.  Times (max over ranks, CUDA events, median of 5): the local GEMM, the
+    all-reduce, the two back to back, and an M-chunked pipeline in which the all-reduce of
+    chunk i (on a second stream) overlaps the GEMM of chunk i+1."""
+    from vllm_nt._ntops import sharding
+    from vllm_nt._ntops.torch._ext import ops
+
+    o = ops()
+    g = torch.Generator(device=dev).manual_seed(50 + rank)
+    comm = torch.cuda.Stream(device=dev)
+    res = {}
+
+    def timed(fn, reps=5) -> float:
+        ts = []
+        for _ in range(reps):
+            dist.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        t = torch.tensor([statistics.median(ts)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for name, k_full in (("o_proj", 4096), ("down", 14336)):
+        k0, k1 = sharding.row_range(rank, n, k_full)
+        kl = k1 - k0
+        w = 0.02 * torch.randn(4096, kl, device=dev, generator=g, dtype=torch.bfloat16)
+        for m in (1, 128, 1024, 8192):
+            x = torch.randn(m, kl, device=dev, generator=g, dtype=torch.bfloat16)
+            out = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
+            chunks = 4 if m >= 1024 else 1
+            rows = m // chunks
+
+            def gemm():
+                o.linear(out, x, w, None, None)
+
+            def allreduce():
+                dist.all_reduce(out)
+
+            def serial():
+                gemm()
+                allreduce()
+
+            def pipelined():
+                main = torch.cuda.current_stream()
+                for c in range(chunks):
+                    sl = slice(c * rows, (c + 1) * rows)
+                    o.linear(out[sl], x[sl], w, None, None)
+                    ev = torch.cuda.Event()
+                    ev.record(main)
+                    comm.wait_event(ev)
+                    with torch.cuda.stream(comm):
+                        dist.all_reduce(out[sl])
+                main.wait_stream(comm)
+
+            for f in (gemm, allreduce, serial, pipelined):
+                f()
+            torch.cuda.synchronize()
+            t_gemm, t_ar, t_serial, t_pipe = timed(gemm), timed(allreduce), timed(serial), timed(pipelined)
+            res[f"{name} M={m}"] = {
+                "gemm_us": round(t_gemm * 1e3, 1),
+                "allreduce_us": round(t_ar * 1e3, 1),
+                "serial_us": round(t_serial * 1e3, 1),
+                "chunked_overlap_us": round(t_pipe * 1e3, 1),
+                "allreduce_bytes": m * 4096 * 2,
+                "chunks": chunks,
+            }
+            del x, out
+        del w
     return res
 
 
@@ -545,10 +623,15 @@ def main() -> int:
     }
 
     per_op = None
+    tp_table = None
     if rank == 0 and n == 1 and not args.no_ops:
         del kc, vc, ws
         torch.cuda.empty_cache()
         per_op = per_op_table(dev, peaks)
+    elif n > 1 and not args.no_ops:
+        del kc, vc, ws
+        torch.cuda.empty_cache()
+        tp_table = tp_projection_table(dev, n, rank, dist)
 
     cpu = None
     if rank == 0 and n == 1 and not args.no_cpu and batch == BATCH:
@@ -585,6 +668,7 @@ def main() -> int:
         "gpu_launches": 2 * args.steps,  # split + combine per timed step
         "clocks": clocks,
         "per_op": per_op,
+        "tp_projection": tp_table,
     }
     print(json.dumps(line), flush=True)
     return 0

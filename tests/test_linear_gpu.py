@@ -43,7 +43,7 @@ def _ntb200_linear(x, w, b=None):
 
 
 @pytest.mark.parametrize("k,n", SHAPES)
-@pytest.mark.parametrize("m", [1, 16, 128])
+@pytest.mark.parametrize("m", [1, 16, 128, 256])
 def test_linear_small_m_vs_oracle(m, k, n):
     x, w, _ = _inputs(m, k, n, seed=m + k + n)
     out = _ntb200_linear(x.cuda(), w.cuda())
@@ -69,7 +69,7 @@ def test_linear_m8192_gate_up_row_subset():
     torch.testing.assert_close(out[rows].float(), ref, rtol=TOL, atol=TOL)
 
 
-@pytest.mark.parametrize("m,k,n", [(200, 72, 300), (5, 32, 12), (129, 4096, 257), (1, 8, 8)])
+@pytest.mark.parametrize("m,k,n", [(200, 72, 300), (5, 32, 12), (129, 4096, 257), (1, 8, 8), (300, 136, 257), (1000, 4096, 640)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_linear_tails_and_bias_capi(m, k, n, dtype):
     x, w, b = _inputs(m, k, n, seed=m * 7 + n, dtype=dtype, bias=True)

@@ -1,12 +1,13 @@
 // Dense projection GEMM on the 5th-generation tensor cores:
 //   out[M, N] = x[M, K] . W[N, K]^T (+ bias),  bf16/f16 in, fp32 accumulate in TMEM.
 //
-// Persistent, warp-specialised, one CTA per SM (192 threads):
-//   warp 0      TMA producer: 128x64 x-tile + 256x64 W-tile per k-step (128-byte swizzle,
-//               K-major) into a 4-stage shared-memory ring (48 KB per stage);
-//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and its lane 0
-//               issues tcgen05.mma (M=128, N=256, K=16; four per k-step), committing each
-//               stage back to the producer and each finished tile to the epilogue;
+// M > 256: persistent, warp-specialised, one CTA per SM (192 threads), tile 128 x BN with
+// BN = 256, 192 or 128 picked per shape to fill whole waves of SMs:
+//   warp 0      TMA producer: 128x64 x-tile + BNx64 W-tile per k-step (128-byte swizzle,
+//               K-major) into a ~192-200 KB shared-memory ring;
+//   warp 1      allocates TMEM for two 128xBN fp32 accumulators and its lane 0 issues
+//               tcgen05.mma (M=128, N=BN, K=16; four per k-step), committing each stage
+//               back to the producer and each finished tile to the epilogue;
 //   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
 //               32*(w%4)..+31, i.e. output rows), add bias, round, store.
 // The epilogue of tile i overlaps the MMAs of tile i+1 (double-buffered accumulator).
@@ -338,9 +339,9 @@ int make_kmajor_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows,
 }
 
 // ------------------------------------------------------------------------------------
-// Small-M path (M <= 128: decode batches).  out^T = W . x^T ("swap AB"): the weight tile
+// Small-M path (M <= 256: decode batches).  out^T = W . x^T ("swap AB"): the weight tile
 // fills the UMMA M=128 side, the few token rows are the UMMA N side (padded to MP = 16 ..
-// 128; rows past M are TMA zero-fill and cost no HBM traffic).  With only N/128 weight
+// 256; rows past M are TMA zero-fill and cost no HBM traffic).  With only N/128 weight
 // tiles, K is split across the CTAs of a thread-block cluster (<= 8); each CTA parks its
 // fp32 partial tile in its own shared memory and, after a cluster barrier, every CTA sums
 // a share of the output rows across the cluster through distributed shared memory and
@@ -591,7 +592,8 @@ int dispatch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const Small
     case 16: return launch_small<T, 16>(wmap, xmap, prm, n_tiles, s, slot_base + 0);
     case 32: return launch_small<T, 32>(wmap, xmap, prm, n_tiles, s, slot_base + 1);
     case 64: return launch_small<T, 64>(wmap, xmap, prm, n_tiles, s, slot_base + 2);
-    default: return launch_small<T, 128>(wmap, xmap, prm, n_tiles, s, slot_base + 3);
+    case 128: return launch_small<T, 128>(wmap, xmap, prm, n_tiles, s, slot_base + 3);
+    default: return launch_small<T, 256>(wmap, xmap, prm, n_tiles, s, slot_base + 4);
   }
 }
 
@@ -676,7 +678,7 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     return fail(NTB200_ERR_MISALIGNED, "linear: x/weight must be 16-byte aligned with row strides %% 8 == 0");
   const bool bf16 = dtype == NTB200_DTYPE_BF16;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (M <= 128) {
+  if (M <= 256) {
     // swap-AB + cluster split-K path for decode-sized batches
     const int64_t n_tiles = ceil_div(N, BM);
     if (n_tiles > 0x7fffffff / 8) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
@@ -686,7 +688,7 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     if (splits > ksteps) splits = ksteps;
     const int per = static_cast<int>(ceil_div(ksteps, splits));
     splits = static_cast<int>(ceil_div(ksteps, per));  // no empty split
-    const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+    const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
     CUtensorMap wmap, xmap;
     int st = make_kmajor_map(&wmap, weight, bf16, N, K, weight_row_stride, BM);
     if (st != NTB200_OK) return st;
@@ -703,7 +705,7 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     sp.k_steps_total = ksteps;
     sp.err = device_error_word();
     return bf16 ? dispatch_small<__nv_bfloat16>(wmap, xmap, sp, static_cast<int>(n_tiles), mp, s, 4)
-                : dispatch_small<__half>(wmap, xmap, sp, static_cast<int>(n_tiles), mp, s, 8);
+                : dispatch_small<__half>(wmap, xmap, sp, static_cast<int>(n_tiles), mp, s, 9);
   }
   const int bn = pick_tile_width(M, N, num_sms());
   switch (bn) {

@@ -38,17 +38,53 @@ class BackendStats:
 _DISABLED: set[str] = set()
 _STATS: dict[str, dict[str, BackendStats]] = {}
 
+# The hooks sit on every decoder op, so the env flags are parsed once per distinct raw
+# value (and per change of the runtime-disabled set), not once per call.  The raw value
+# is read from os.environ's underlying bytes mapping (a dict lookup; os.environ.get
+# re-encodes the key and decodes the value on every call), which setenv/putenv keep current.
+_ENV_BYTES = getattr(os.environ, "_data", None)
+_disabled_version = 0
+_disabled_cache: tuple[object, int, frozenset[str]] = (object(), -1, frozenset())
+_stats_cache: tuple[object, bool] = (object(), False)
+
+
+def _raw_env(name: str, name_b: bytes) -> object:
+    if isinstance(_ENV_BYTES, dict):
+        return _ENV_BYTES.get(name_b)
+    return os.environ.get(name)
+
+
+def _decode(raw: object) -> str:
+    if raw is None:
+        return ""
+    return raw.decode(errors="replace") if isinstance(raw, bytes) else str(raw)
+
 
 def stats_enabled() -> bool:
-    return os.environ.get(ENABLE_STATS_ENV, "").strip().lower() in _TRUE
+    global _stats_cache
+    raw = _raw_env(ENABLE_STATS_ENV, b"VLLM_NT_ENABLE_STATS")
+    if raw != _stats_cache[0]:
+        _stats_cache = (raw, _decode(raw).strip().lower() in _TRUE)
+    return _stats_cache[1]
 
 
 def disabled_ops() -> set[str]:
-    listed = {n.strip() for n in os.environ.get(DISABLE_OPS_ENV, "").split(",") if n.strip()}
-    out: set[str] = set()
-    for name in listed | _DISABLED:
-        out |= op_name_variants(name)
-    return out
+    global _disabled_cache
+    raw_key = _raw_env(DISABLE_OPS_ENV, b"VLLM_NT_DISABLE_OPS")
+    if raw_key != _disabled_cache[0] or _disabled_version != _disabled_cache[1]:
+        raw = _decode(raw_key)
+        listed = {n.strip() for n in raw.split(",") if n.strip()}
+        out: set[str] = set()
+        for name in listed | _DISABLED:
+            out |= op_name_variants(name)
+        _disabled_cache = (raw_key, _disabled_version, frozenset(out))
+    return _disabled_cache[2]  # type: ignore[return-value]
+
+
+def _disable(op_name: str) -> None:
+    global _disabled_version
+    _DISABLED.add(op_name)
+    _disabled_version += 1
 
 
 def configured_backend(op_name: str) -> str:
@@ -97,8 +133,10 @@ def backend_stats(op_name: str) -> dict[str, BackendStats]:
 
 
 def reset_backend_state() -> None:
+    global _disabled_version
     _DISABLED.clear()
     _STATS.clear()
+    _disabled_version += 1
 
 
 def _dispatch(op_name: str, backend: str, thunks: dict[str, Thunk | None], original: Thunk) -> Any:
@@ -136,13 +174,13 @@ def route(
         "b200": kernels,
     }
     cfg = config_for(op_name)
-    backend = active_backend(op_name)
+    backend = cfg.fallback_backend if op_name in disabled_ops() else cfg.backend
     try:
         return _dispatch(op_name, backend, thunks, call_original)
     except Exception as exc:
         record_failure(op_name, backend)
         if cfg.disable_backend_on_first_failure and backend != "original":
-            _DISABLED.add(op_name)
+            _disable(op_name)
             LOG.warning(
                 "vllm-nt: %s backend %s disabled after failure; falling back to %s: %s",
                 op_name,
