@@ -74,7 +74,7 @@ int num_sms() {
 }
 
 namespace {
-constexpr int kAttrSlots = 32;
+constexpr int kAttrSlots = 64;
 std::atomic<int> g_attr_done[kMaxDevices][kAttrSlots];
 }  // namespace
 

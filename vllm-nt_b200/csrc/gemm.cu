@@ -19,6 +19,8 @@
 // freed before the CTA exits.
 //
 // Replaces vllm_nt/_ntops/kernels/linear.py:9-85 (a Triton tl.dot tile loop).
+#include <atomic>
+
 #include "common.cuh"
 
 namespace ntb200 {
@@ -339,35 +341,37 @@ int make_kmajor_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows,
 }
 
 // ------------------------------------------------------------------------------------
-// Small-M path (M <= 256: decode batches).  out^T = W . x^T ("swap AB"): the weight tile
-// fills the UMMA M=128 side, the few token rows are the UMMA N side (padded to MP = 16 ..
-// 256; rows past M are TMA zero-fill and cost no HBM traffic).  With only N/128 weight
-// tiles, K is split across the CTAs of a thread-block cluster (<= 8); each CTA parks its
-// fp32 partial tile in its own shared memory and, after a cluster barrier, every CTA sums
-// a share of the output rows across the cluster through distributed shared memory and
-// writes them (bias added, rounded).  One launch, no global workspace.
+// Small-M path (M <= 256: decode batches).  out^T = W . x^T ("swap AB"): weight rows fill
+// the UMMA M=128 side, the few token rows are the UMMA N side (padded to MP = 16 .. 256;
+// rows past M are TMA zero-fill and cost no HBM traffic).  A CTA owns NT adjacent 128-row
+// weight tiles that share each k-step's token tile (NT = 2 for token tiles of 128 rows and
+// more, halving the token operand's L2 re-reads; TMEM holds the NT accumulators).  With
+// few weight tiles, K is split across the CTAs of a thread-block cluster (<= 8): each CTA
+// parks one fp32 partial tile at a time in its shared memory and, after a cluster barrier,
+// every CTA sums a share of the output rows across the cluster through distributed shared
+// memory and writes them (bias added, rounded).  Without a split the epilogue stores
+// straight from TMEM.  One launch, no global workspace.
 // ------------------------------------------------------------------------------------
 
-// ring depth per token tile: about 96 KB of stages, so two CTAs fit on an SM
-template <int MP>
-constexpr int small_stages() {
-  return (96 * 1024) / (kATileBytes + MP * BK * 2) < 3 ? 3 : (96 * 1024) / (kATileBytes + MP * BK * 2);
-}
-
-template <int MP>
+// BIG: the grid fits in one wave (one CTA per SM), so the ring takes ~192 KB and keeps
+// twice the weight bytes in flight; otherwise ~96 KB so that two CTAs share an SM.
+template <int MP, int NT, bool BIG>
 struct SmallSmem {
-  static constexpr int kSmallStages = small_stages<MP>();
   static constexpr int kXTile = MP * BK * 2;
-  static constexpr int kStage = kATileBytes + kXTile;  // 128 weight rows + MP x rows
+  static constexpr int kStage = NT * kATileBytes + kXTile;  // NT weight tiles + token tile
+  static constexpr int kRingTarget = BIG ? 192 * 1024 : 96 * 1024;
+  static constexpr int kStages = kRingTarget / kStage < 3 ? 3 : kRingTarget / kStage;
   static constexpr int kRing = 0;
-  static constexpr int kFull = kSmallStages * kStage;
-  static constexpr int kEmpty = kFull + 8 * kSmallStages;
-  static constexpr int kTmemFull = kEmpty + 8 * kSmallStages;
+  static constexpr int kFull = kStages * kStage;
+  static constexpr int kEmpty = kFull + 8 * kStages;
+  static constexpr int kTmemFull = kEmpty + 8 * kStages;
   static constexpr int kTmemBase = kTmemFull + 8;
   static constexpr int kEnd = kTmemBase + 8;
   static constexpr int kDynamicBytes = kEnd + 1024;
-  static constexpr int kTmemCols = MP < 32 ? 32 : MP;
-  static_assert(MP * BM * 4 <= kSmallStages * kStage, "partial tile must fit in the ring");
+  static constexpr int kTmemCols = NT * MP < 32 ? 32 : NT * MP;
+  static_assert(NT * MP <= 512, "accumulators exceed TMEM");
+  static_assert(MP * BM * 4 <= kStages * kStage, "partial tile must fit in the ring");
+  static_assert(kDynamicBytes <= 227 * 1024, "ring exceeds shared memory");
 };
 
 struct SmallParams {
@@ -375,6 +379,7 @@ struct SmallParams {
   const void* bias;
   int64_t M, N;
   int64_t out_stride;
+  int n_tiles;  // 128-row weight tiles
   int splits;
   int k_steps_per_split;
   int k_steps_total;
@@ -412,12 +417,12 @@ __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t local_addr, uint32_t r
   return v;
 }
 
-template <typename T, int MP>
+template <typename T, int MP, int NT, bool BIG>
 __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
     const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
     const SmallParams p) {
-  using L = SmallSmem<MP>;
-  constexpr int kSmallStages = L::kSmallStages;
+  using L = SmallSmem<MP, NT, BIG>;
+  constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -430,13 +435,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int split = blockIdx.x % p.splits;  // == rank in the cluster
-  const int ntile = blockIdx.x / p.splits;
+  const int tile0 = (blockIdx.x / p.splits) * NT;
   const int kb0 = split * p.k_steps_per_split;
   const int kb1 = min(kb0 + p.k_steps_per_split, p.k_steps_total);
   const int nk = kb1 > kb0 ? kb1 - kb0 : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kSmallStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -461,95 +466,132 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&x_map)) : "memory");
       int issued = 0;
       for (int it = 0; it < nk; ++it) {
-        const int s = it % kSmallStages;
-        if (it >= kSmallStages && !mbar_wait(&empty[s], ((it / kSmallStages) - 1) & 1, p.err)) break;
+        const int s = it % kStages;
+        if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, p.err)) break;
         mbar_arrive_expect_tx(&full[s], L::kStage);
-        const uint32_t w_dst = ring + s * L::kStage;
-        const uint32_t x_dst = w_dst + kATileBytes;
-        tma_load_2d(w_dst, &w_map, (kb0 + it) * BK, ntile * BM, smem_u32(&full[s]));
-        tma_load_2d(x_dst, &x_map, (kb0 + it) * BK, 0, smem_u32(&full[s]));
+        const uint32_t stage = ring + s * L::kStage;
+        const int kx = (kb0 + it) * BK;
+        // weight tiles past N (the last group of an odd tile count) are TMA zero-fill
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+          tma_load_2d(stage + t * kATileBytes, &w_map, kx, (tile0 + t) * BM, smem_u32(&full[s]));
+        tma_load_2d(stage + NT * kATileBytes, &x_map, kx, 0, smem_u32(&full[s]));
         issued = it + 1;
       }
-      const int first = issued > kSmallStages ? issued - kSmallStages : 0;
-      for (int j = first; j < issued; ++j) mbar_wait(&full[j % kSmallStages], (j / kSmallStages) & 1, p.err);
+      const int first = issued > kStages ? issued - kStages : 0;
+      for (int j = first; j < issued; ++j) mbar_wait(&full[j % kStages], (j / kStages) & 1, p.err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = make_idesc(std::is_same<T, __nv_bfloat16>::value, BM, MP);
       for (int it = 0; it < nk; ++it) {
-        const int s = it % kSmallStages;
-        if (!mbar_wait(&full[s], (it / kSmallStages) & 1, p.err)) break;
+        const int s = it % kStages;
+        if (!mbar_wait(&full[s], (it / kStages) & 1, p.err)) break;
         tc_fence_after();
-        const uint32_t w_addr = ring + s * L::kStage;
-        const uint64_t adesc = sw128_kmajor_desc(w_addr);
-        const uint64_t bdesc = sw128_kmajor_desc(w_addr + kATileBytes);
+        const uint32_t stage = ring + s * L::kStage;
+        const uint64_t bdesc = sw128_kmajor_desc(stage + NT * kATileBytes);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          umma_f16(tmem_base, adesc + 2 * k, bdesc + 2 * k, idesc, (it > 0 || k > 0) ? 1u : 0u);
+        for (int t = 0; t < NT; ++t) {
+          const uint64_t adesc = sw128_kmajor_desc(stage + t * kATileBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16(tmem_base + t * MP, adesc + 2 * k, bdesc + 2 * k, idesc, (it > 0 || k > 0) ? 1u : 0u);
+        }
         umma_commit(&empty[s]);
       }
       umma_commit(tmem_full);  // also the "all MMAs done" point before TMEM is released
     }
-  } else {
-    // epilogue warps: TMEM (lane = weight row n, column = token m) -> smem partial [MP][128]
-    const int quad = warp & 3;
-    const int n_local = quad * 32 + lane;
-    float* part = reinterpret_cast<float*>(smem + L::kRing);
-    const bool ok = mbar_wait(tmem_full, 0, p.err);
-    tc_fence_after();
-#pragma unroll 1
-    for (int c = 0; c < MP / 16; ++c) {
-      uint32_t r[16];
-      __syncwarp();
-      tmem_ld_16(tmem_base + (uint32_t(quad * 32) << 16) + c * 16, r);
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        part[(c * 16 + i) * BM + n_local] = (ok && nk > 0) ? __uint_as_float(r[i]) : 0.f;
-    }
-    tc_fence_before();
   }
 
-  // every CTA of the cluster has its partial tile in shared memory
-  cluster_sync_all();
-  {
-    // this CTA owns output rows [r0, r1); a row is 128 partial floats = 32 float4, so the
-    // 192 threads cover 6 rows per pass, and each pass has its splits x float4 remote loads
-    // in flight before any is summed
+  T* out = static_cast<T*>(p.out);
+  const T* bias = static_cast<const T*>(p.bias);
+  const bool epilogue = warp >= 2;
+  const int quad = warp & 3;
+  const int n_local = quad * 32 + lane;  // TMEM lane = weight row within the tile
+  bool acc_ok = false;
+  if (epilogue) {
+    acc_ok = mbar_wait(tmem_full, 0, p.err) && nk > 0;
+    tc_fence_after();
+  }
+
+  if (p.splits == 1) {
+    // no split: TMEM -> registers -> global (lane = output column, column = token row)
+    if (epilogue) {
+#pragma unroll 1
+      for (int t = 0; t < NT; ++t) {
+        const int64_t n = int64_t(tile0 + t) * BM + n_local;
+        const float b = (bias != nullptr && n < p.N) ? Elem<T>::to_f(bias[n]) : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < MP / 16; ++c) {
+          uint32_t r[16];
+          __syncwarp();
+          tmem_ld_16(tmem_base + (uint32_t(quad * 32) << 16) + t * MP + c * 16, r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int64_t m = c * 16 + i;
+            if (m < p.M && n < p.N)
+              out[m * p.out_stride + n] = Elem<T>::from_f((acc_ok ? __uint_as_float(r[i]) : 0.f) + b);
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  } else {
+    // split-K: one weight tile at a time through shared memory and the cluster
+    float* part = reinterpret_cast<float*>(smem + L::kRing);
+    const uint32_t part_addr = smem_u32(smem + L::kRing);
     const int rows_per = static_cast<int>((p.M + p.splits - 1) / p.splits);
     const int r0 = split * rows_per;
     const int r1 = static_cast<int>(p.M < int64_t(r0) + rows_per ? p.M : int64_t(r0) + rows_per);
-    const int q4 = threadIdx.x & 31;  // float4 column group: n_local = 4 * q4 .. +3
-    const uint32_t part_addr = smem_u32(smem + L::kRing);
-    T* out = static_cast<T*>(p.out);
-    const T* bias = static_cast<const T*>(p.bias);
-    const int64_t n0 = int64_t(ntile) * BM + 4 * q4;
-    float bvec[4];
+    const int q4 = threadIdx.x & 31;  // float4 column group: rows of the partial are 32 float4
+#pragma unroll 1
+    for (int t = 0; t < NT; ++t) {
+      if (epilogue) {
+#pragma unroll 1
+        for (int c = 0; c < MP / 16; ++c) {
+          uint32_t r[16];
+          __syncwarp();
+          tmem_ld_16(tmem_base + (uint32_t(quad * 32) << 16) + t * MP + c * 16, r);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) bvec[i] = (bias != nullptr && n0 + i < p.N) ? Elem<T>::to_f(bias[n0 + i]) : 0.f;
-    for (int m = r0 + (threadIdx.x >> 5); m < r1; m += kThreads / 32) {
-      const uint32_t off = part_addr + uint32_t((m * BM + 4 * q4) * 4);
-      float4 v[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) v[r] = r < p.splits ? ld_dsmem_f32x4(off, uint32_t(r)) : make_float4(0.f, 0.f, 0.f, 0.f);
-      float acc[4] = {bvec[0], bvec[1], bvec[2], bvec[3]};
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        acc[0] += v[r].x;
-        acc[1] += v[r].y;
-        acc[2] += v[r].z;
-        acc[3] += v[r].w;
+          for (int i = 0; i < 16; ++i) part[(c * 16 + i) * BM + n_local] = acc_ok ? __uint_as_float(r[i]) : 0.f;
+        }
       }
-      T* orow = out + int64_t(m) * p.out_stride;
-      if (n0 + 4 <= p.N && ((reinterpret_cast<uintptr_t>(orow + n0) & 7u) == 0)) {
-        store_f<T, 4>(orow + n0, acc);
-      } else {
-        for (int i = 0; i < 4; ++i)
-          if (n0 + i < p.N) orow[n0 + i] = Elem<T>::from_f(acc[i]);
+      // every CTA of the cluster has partial tile t in shared memory
+      cluster_sync_all();
+      const int64_t n0 = int64_t(tile0 + t) * BM + 4 * q4;
+      float bvec[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) bvec[i] = (bias != nullptr && n0 + i < p.N) ? Elem<T>::to_f(bias[n0 + i]) : 0.f;
+      // 192 threads cover 6 rows per pass; a pass has its splits x float4 remote loads in
+      // flight before any is summed
+      for (int m = r0 + (threadIdx.x >> 5); m < r1; m += kThreads / 32) {
+        const uint32_t off = part_addr + uint32_t((m * BM + 4 * q4) * 4);
+        float4 v[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v[r] = r < p.splits ? ld_dsmem_f32x4(off, uint32_t(r)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float acc[4] = {bvec[0], bvec[1], bvec[2], bvec[3]};
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          acc[0] += v[r].x;
+          acc[1] += v[r].y;
+          acc[2] += v[r].z;
+          acc[3] += v[r].w;
+        }
+        T* orow = out + int64_t(m) * p.out_stride;
+        if (n0 + 4 <= p.N && ((reinterpret_cast<uintptr_t>(orow + n0) & 7u) == 0)) {
+          store_f<T, 4>(orow + n0, acc);
+        } else {
+          for (int i = 0; i < 4; ++i)
+            if (n0 + i < p.N) orow[n0 + i] = Elem<T>::from_f(acc[i]);
+        }
       }
+      // nobody overwrites (or frees) a partial tile while a partner still reads it
+      cluster_sync_all();
     }
+    if (epilogue) tc_fence_before();
   }
-  // no CTA may leave (or free its shared memory) while its partner still reads it
-  cluster_sync_all();
+
+  __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
@@ -558,15 +600,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
   }
 }
 
-template <typename T, int MP>
-int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, int n_tiles,
-                 cudaStream_t s, int attr_slot) {
-  using L = SmallSmem<MP>;
-  const void* fn = reinterpret_cast<const void*>(gemm_small_m_kernel<T, MP>);
+template <typename T, int MP, int NT, bool BIG>
+int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, cudaStream_t s,
+                 int attr_slot) {
+  using L = SmallSmem<MP, NT, BIG>;
+  const void* fn = reinterpret_cast<const void*>(gemm_small_m_kernel<T, MP, NT, BIG>);
   int st = ensure_smem_attribute(fn, L::kDynamicBytes, attr_slot);
   if (st != NTB200_OK) return st;
+  const int groups = (prm.n_tiles + NT - 1) / NT;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * prm.splits));
+  cfg.gridDim = dim3(static_cast<unsigned>(groups * prm.splits));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kDynamicBytes;
   cfg.stream = s;
@@ -577,7 +620,7 @@ int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallPa
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_m_kernel<T, MP>, wmap, xmap, prm);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_m_kernel<T, MP, NT, BIG>, wmap, xmap, prm);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(NTB200_ERR_CUDA, "linear (small M): launch failed: %s", cudaGetErrorString(e));
@@ -585,17 +628,81 @@ int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallPa
   return NTB200_OK;
 }
 
+// How many clusters of `cluster` CTAs of `fn` (with `smem` bytes each) can be resident at
+// once on the current device; cached per (device, variant slot, cluster size).
+int resident_clusters(const void* fn, int smem, int cluster, int slot) {
+  constexpr int kDevs = 16, kSlots = 64, kMaxCluster = 9;
+  static std::atomic<int> cache[kDevs][kSlots][kMaxCluster];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kDevs || slot < 0 || slot >= kSlots || cluster < 1 || cluster >= kMaxCluster) return 0;
+  const int hit = cache[dev][slot][cluster].load(std::memory_order_relaxed);
+  if (hit != 0) return hit;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(cluster));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = -1;  // unknown: callers treat it as "does not fit"
+  }
+  cache[dev][slot][cluster].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+// The ~192 KB ring when every cluster of the grid is resident at once with one CTA per
+// SM (clusters must fit inside a GPC, so this is asked of the runtime, not assumed);
+// otherwise the ~96 KB ring, two CTAs per SM.
+template <typename T, int MP, int NT>
+int launch_small_ring(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& big_plan,
+                      const SmallParams& small_plan, cudaStream_t s, int slot) {
+  const int groups = (big_plan.n_tiles + NT - 1) / NT;
+  {
+    using LB = SmallSmem<MP, NT, true>;
+    const void* fn = reinterpret_cast<const void*>(gemm_small_m_kernel<T, MP, NT, true>);
+    int st = ensure_smem_attribute(fn, LB::kDynamicBytes, slot + 1);
+    if (st != NTB200_OK) return st;
+    if (resident_clusters(fn, LB::kDynamicBytes, big_plan.splits, slot + 1) >= groups)
+      return launch_small<T, MP, NT, true>(wmap, xmap, big_plan, s, slot + 1);
+  }
+  using LS = SmallSmem<MP, NT, false>;
+  const void* fn = reinterpret_cast<const void*>(gemm_small_m_kernel<T, MP, NT, false>);
+  int st = ensure_smem_attribute(fn, LS::kDynamicBytes, slot);
+  if (st != NTB200_OK) return st;
+  if (resident_clusters(fn, LS::kDynamicBytes, small_plan.splits, slot) >= groups)
+    return launch_small<T, MP, NT, false>(wmap, xmap, small_plan, s, slot);
+  return launch_small<T, MP, NT, false>(wmap, xmap, big_plan, s, slot);
+}
+
+// token tile MP, weight tiles per CTA NT; two attribute slots (ring sizes) per (MP, NT)
 template <typename T>
-int dispatch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, int n_tiles,
-                   int mp, cudaStream_t s, int slot_base) {
+int dispatch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& big_plan,
+                   const SmallParams& small_plan, int mp, int nt, cudaStream_t s, int slot_base) {
   switch (mp) {
-    case 16: return launch_small<T, 16>(wmap, xmap, prm, n_tiles, s, slot_base + 0);
-    case 32: return launch_small<T, 32>(wmap, xmap, prm, n_tiles, s, slot_base + 1);
-    case 64: return launch_small<T, 64>(wmap, xmap, prm, n_tiles, s, slot_base + 2);
-    case 128: return launch_small<T, 128>(wmap, xmap, prm, n_tiles, s, slot_base + 3);
-    default: return launch_small<T, 256>(wmap, xmap, prm, n_tiles, s, slot_base + 4);
+    case 16: return launch_small_ring<T, 16, 1>(wmap, xmap, big_plan, small_plan, s, slot_base + 0);
+    case 32: return launch_small_ring<T, 32, 1>(wmap, xmap, big_plan, small_plan, s, slot_base + 2);
+    case 64: return launch_small_ring<T, 64, 1>(wmap, xmap, big_plan, small_plan, s, slot_base + 4);
+    case 128:
+      return nt == 2 ? launch_small_ring<T, 128, 2>(wmap, xmap, big_plan, small_plan, s, slot_base + 6)
+                     : launch_small_ring<T, 128, 1>(wmap, xmap, big_plan, small_plan, s, slot_base + 8);
+    default:
+      return nt == 2 ? launch_small_ring<T, 256, 2>(wmap, xmap, big_plan, small_plan, s, slot_base + 10)
+                     : launch_small_ring<T, 256, 1>(wmap, xmap, big_plan, small_plan, s, slot_base + 12);
   }
 }
+
+// Two weight tiles per CTA (one token tile shared by both) only when the weight tiles alone
+// fill the GPU, so that K is not split: halving the token re-reads does not pay for a
+// second cluster-reduction round.
+int small_tiles_per_cta(int mp, int64_t n_tiles, int sms) { return (mp >= 128 && n_tiles >= sms / 2) ? 2 : 1; }
 
 // Tile width for the large-M kernel: the widest of 256/192/128 whose tiles fill the SMs'
 // waves (and cover N with little padding) to within 95% of the best candidate.
@@ -637,7 +744,7 @@ int launch_large(void* out, const void* x, const void* weight, const void* bias,
   prm.err = device_error_word();
   const int64_t tiles = mblocks * nblocks;
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  const int slot = 16 + (BNV == 256 ? 0 : (BNV == 192 ? 2 : 4)) + (bf16 ? 0 : 1);
+  const int slot = 32 + (BNV == 256 ? 0 : (BNV == 192 ? 2 : 4)) + (bf16 ? 0 : 1);
   if (bf16) {
     st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__nv_bfloat16, BNV>), C::kDynamicBytes, slot);
     if (st != NTB200_OK) return st;
@@ -683,12 +790,21 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     const int64_t n_tiles = ceil_div(N, BM);
     if (n_tiles > 0x7fffffff / 8) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
     const int ksteps = static_cast<int>(ceil_div(K, BK));
-    int splits = static_cast<int>(num_sms() / n_tiles);
-    splits = splits < 1 ? 1 : (splits > 8 ? 8 : splits);
-    if (splits > ksteps) splits = ksteps;
-    const int per = static_cast<int>(ceil_div(ksteps, splits));
-    splits = static_cast<int>(ceil_div(ksteps, per));  // no empty split
     const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    const int nt = small_tiles_per_cta(mp, n_tiles, num_sms());
+    const int64_t groups = ceil_div(n_tiles, nt);
+    // split K so that the grid has about `target` CTAs; clusters of 1, 2, 4 or 8 CTAs pack
+    // into the GPCs without stranding SMs (a cluster must fit inside one GPC)
+    auto plan = [&](int64_t target, int& splits, int& per) {
+      const int64_t want = target / groups;
+      splits = want >= 8 ? 8 : want >= 4 ? 4 : want >= 2 ? 2 : 1;
+      if (splits > ksteps) splits = ksteps;
+      per = static_cast<int>(ceil_div(ksteps, splits));
+      splits = static_cast<int>(ceil_div(ksteps, per));
+    };
+    int splits_big, per_big, splits_small, per_small;
+    plan(num_sms(), splits_big, per_big);          // one CTA per SM, ~192 KB rings
+    plan(2 * num_sms(), splits_small, per_small);  // two CTAs per SM, ~96 KB rings
     CUtensorMap wmap, xmap;
     int st = make_kmajor_map(&wmap, weight, bf16, N, K, weight_row_stride, BM);
     if (st != NTB200_OK) return st;
@@ -700,12 +816,16 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     sp.M = M;
     sp.N = N;
     sp.out_stride = out_row_stride;
-    sp.splits = splits;
-    sp.k_steps_per_split = per;
+    sp.n_tiles = static_cast<int>(n_tiles);
     sp.k_steps_total = ksteps;
     sp.err = device_error_word();
-    return bf16 ? dispatch_small<__nv_bfloat16>(wmap, xmap, sp, static_cast<int>(n_tiles), mp, s, 4)
-                : dispatch_small<__half>(wmap, xmap, sp, static_cast<int>(n_tiles), mp, s, 9);
+    SmallParams sp_big = sp, sp_small = sp;
+    sp_big.splits = splits_big;
+    sp_big.k_steps_per_split = per_big;
+    sp_small.splits = splits_small;
+    sp_small.k_steps_per_split = per_small;
+    return bf16 ? dispatch_small<__nv_bfloat16>(wmap, xmap, sp_big, sp_small, mp, nt, s, 4)
+                : dispatch_small<__half>(wmap, xmap, sp_big, sp_small, mp, nt, s, 18);
   }
   const int bn = pick_tile_width(M, N, num_sms());
   switch (bn) {
