@@ -284,6 +284,25 @@ def per_op_table(dev, peaks) -> dict:
             d.update(extra)
         res[name] = d
 
+    # The same shapes through the kernels vLLM itself ships (its _C extension, cuBLAS via
+    # F.linear, F.embedding): reported beside ours for comparison only.
+    try:
+        import vllm._custom_ops as vops
+    except Exception:  # noqa: BLE001 - the comparison column is optional
+        vops = None
+
+    def lib(name, label, fns, iters):
+        if fns is None:
+            return
+        try:
+            us = time_graph(fns, iters) * 1e3
+        except Exception as exc:  # noqa: BLE001
+            res[name]["lib"] = f"{label}: unavailable ({type(exc).__name__})"
+            return
+        res[name]["lib"] = label
+        res[name]["lib_us"] = round(us, 2)
+        res[name]["ours_vs_lib"] = round(us / res[name]["us"], 3)
+
     # (a) fused_add_rms_norm fp32 [128, 4096]
     M, H = 128, 4096
     nb = 4 * M * H * 4 + H * 4
@@ -294,6 +313,8 @@ def per_op_table(dev, peaks) -> dict:
     outs = [torch.empty(M, H, device=dev) for _ in range(r)]
     fns = [lambda i=i: o.fused_add_rms_norm(outs[i], rs[i], xs[i], w, 1e-6) for i in range(r)]
     report("fused_add_rms_norm f32 [128,4096]", nb, time_graph(fns, 20 * r))
+    lib("fused_add_rms_norm f32 [128,4096]", "vllm _C.fused_add_rms_norm (in place)",
+        vops and [lambda i=i: vops.fused_add_rms_norm(xs[i], rs[i], w, 1e-6) for i in range(r)], 20 * r)
     # bf16 M-sweep point at a size where launch latency no longer dominates
     M2 = 8192
     nb2 = 4 * M2 * H * 2 + H * 2
@@ -304,6 +325,8 @@ def per_op_table(dev, peaks) -> dict:
     outs2 = [torch.empty_like(xs2[0]) for _ in range(r2)]
     fns = [lambda i=i: o.fused_add_rms_norm(outs2[i], rs2[i], xs2[i], w2, 1e-6) for i in range(r2)]
     report("fused_add_rms_norm bf16 [8192,4096]", nb2, time_graph(fns, 10 * r2))
+    lib("fused_add_rms_norm bf16 [8192,4096]", "vllm _C.fused_add_rms_norm (in place)",
+        vops and [lambda i=i: vops.fused_add_rms_norm(xs2[i], rs2[i], w2, 1e-6) for i in range(r2)], 10 * r2)
     del xs, rs, outs, xs2, rs2, outs2
 
     # (b) silu_and_mul fp32 [128,22016] -> [128,11008]
@@ -313,6 +336,8 @@ def per_op_table(dev, peaks) -> dict:
     outs = [torch.empty(128, 11008, device=dev) for _ in range(r)]
     fns = [lambda i=i: o.silu_and_mul(outs[i], xs[i]) for i in range(r)]
     report("silu_and_mul f32 [128,22016]", nb, time_graph(fns, 20 * r))
+    lib("silu_and_mul f32 [128,22016]", "vllm _C.silu_and_mul",
+        vops and [lambda i=i: torch.ops._C.silu_and_mul(outs[i], xs[i]) for i in range(r)], 20 * r)
     del xs, outs
 
     # (c) RoPE fp32 q [128,32,128], k [128,8,128], positions U[0,4096)
@@ -327,6 +352,9 @@ def per_op_table(dev, peaks) -> dict:
     cache = oracle.build_cos_sin_cache(128, 4096, 10000.0).to(dev)
     fns = [lambda i=i: o.rotary_embedding_neox(pos[i], qs[i], ks[i], cache, 128, 128) for i in range(r)]
     report("rope_neox f32 q[128,32,128] k[128,8,128]", nb, time_graph(fns, 20 * r))
+    lib("rope_neox f32 q[128,32,128] k[128,8,128]", "vllm _C.rotary_embedding (neox)",
+        vops and [lambda i=i: vops.rotary_embedding(pos[i], qs[i], ks[i], 128, cache, True) for i in range(r)],
+        20 * r)
     del qs, ks
 
     # KV store bf16: 4096 tokens x 8 x 128 into [8192,16,8,128] caches, distinct slots
@@ -340,6 +368,10 @@ def per_op_table(dev, peaks) -> dict:
     slots = [torch.randperm(8192 * 16, device=dev, generator=g)[:N] for _ in range(r)]
     fns = [lambda i=i: o.reshape_and_cache(keys[i], vals[i], kc, vc, slots[i]) for i in range(r)]
     report("reshape_and_cache bf16 4096x8x128", nb, time_graph(fns, 20 * r))
+    one = torch.ones((), device=dev)
+    lib("reshape_and_cache bf16 4096x8x128", "vllm _C_cache_ops.reshape_and_cache_flash",
+        vops and [lambda i=i: vops.reshape_and_cache_flash(keys[i], vals[i], kc, vc, slots[i], "auto", one, one)
+                  for i in range(r)], 20 * r)
     del keys, vals, kc, vc
 
     # embedding bf16: 4096 ids into a [128256, 4096] table
@@ -350,6 +382,8 @@ def per_op_table(dev, peaks) -> dict:
     nb = 2 * Tn * 4096 * 2 + Tn * 8
     fns = [lambda i=i: o.embedding(outs[i], ids[i], wt) for i in range(8)]
     report("embedding bf16 4096 ids x 4096", nb, time_graph(fns, 80))
+    lib("embedding bf16 4096 ids x 4096", "torch F.embedding",
+        [lambda i=i: torch.nn.functional.embedding(ids[i], wt) for i in range(8)], 80)
     del wt, outs
 
     # projection GEMM bf16 (fp32 accumulate)
@@ -360,14 +394,18 @@ def per_op_table(dev, peaks) -> dict:
                    for _ in range(max(1, math.ceil(3 * L2_BYTES / (Nn * K * 2))) if M <= 256 else 1)]
             out = torch.empty(M, Nn, device=dev, dtype=torch.bfloat16)
             fns = [lambda w_=w_: o.linear(out, x, w_, None, None) for w_ in wts]
-            ms = time_graph(fns, max(4, 2 * len(wts)))
+            iters = max(4, 2 * len(wts))
+            ms = time_graph(fns, iters)
             flops = 2.0 * M * Nn * K
             nbytes = Nn * K * 2 + M * K * 2 + M * Nn * 2
             tf = flops / (ms * 1e-3) / 1e12
+            name = f"linear {tag} M={M}"
             if M <= 256:
-                report(f"linear {tag} M={M}", nbytes, ms, {"TFLOP/s": round(tf, 2)})
+                report(name, nbytes, ms, {"TFLOP/s": round(tf, 2)})
             else:
-                res[f"linear {tag} M={M}"] = {"us": ms * 1e3, "TFLOP/s": round(tf, 1), "frac_of_bf16": round(tf / tens, 3)}
+                res[name] = {"us": ms * 1e3, "TFLOP/s": round(tf, 1), "frac_of_bf16": round(tf / tens, 3)}
+            lib(name, "cuBLAS (torch.mm, the F.linear GEMM)",
+                [lambda w_=w_: torch.mm(x, w_.t(), out=out) for w_ in wts], iters)
             del x, wts, out
     return res
 

@@ -51,6 +51,28 @@ def test_fused_add_rms_norm_config_a_capi(dtype):
     assert capi.read_device_error(stream()) == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(3, 40000), (7, 4095), (2, 16384), (4, 24), (1, 9000)])
+def test_fused_add_rms_norm_long_and_ragged_rows(dtype, shape):
+    """Rows past the register-resident window (second pass over L2), rows that need the
+    scalar path, and a row that fills exactly the largest CTA."""
+    dev = cuda_device()
+    g = seeded(11)
+    x = torch.randn(shape, generator=g).to(dtype)
+    r = torch.randn(shape, generator=g).to(dtype)
+    w = (1.0 + 0.1 * torch.randn(shape[-1], generator=g)).to(dtype)
+    ref_y, ref_r = oracle.fused_add_rms_norm(x, r, w, 1e-6)
+    xd, rd, wd = x.to(dev), r.to(dev), w.to(dev)
+    out = torch.empty_like(xd)
+    rows, hidden = shape
+    capi.call("ntb200_fused_add_rms_norm", ptr(out), ptr(rd), ptr(xd), ptr(wd), rows, hidden, hidden, hidden,
+              hidden, 1e-6, dtype_code(dtype), stream())
+    torch.cuda.synchronize()
+    _close(out, ref_y, dtype)
+    assert bits_equal(rd.cpu(), ref_r)
+    assert capi.read_device_error(stream()) == 0
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("shape", [(1, 4096), (32, 4096), (7, 4095), (3, 40000), (5, 96)])
 def test_rms_norm_shapes_torch_op(dtype, shape):

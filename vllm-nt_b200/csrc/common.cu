@@ -2,6 +2,7 @@
 // per-device error word that bounded device waits and range checks report into.
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -71,6 +72,14 @@ int num_sms() {
   const int dev = current_device();
   std::call_once(g_resolve_once[dev], resolve_device, dev);
   return g_sm_count[dev];
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("NTB200_PDL");
+    return !(v != nullptr && v[0] == '0' && v[1] == 0);
+  }();
+  return on;
 }
 
 namespace {

@@ -8,6 +8,7 @@
 
 #include <cstdarg>
 #include <cstdint>
+#include <utility>
 
 #include "ntb200.h"
 
@@ -43,6 +44,42 @@ inline int dtype_size(int dtype) {
   }
 }
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Programmatic dependent launch.  Every kernel of the library is launched with
+// programmatic stream serialization allowed, so that its launch and its prologue (index
+// math, shared-memory and mbarrier set-up) overlap the tail of the kernel before it on the
+// stream.  Each kernel calls pdl_wait() before its first global-memory access (read or
+// write) and before it allocates tensor memory; pdl_wait() returns once the preceding
+// kernel has completed and its writes are visible, so results are those of plain stream
+// order.  NTB200_PDL=0 in the environment (read once per process) launches without it.
+bool pdl_enabled();
+
+inline void set_pdl_attribute(cudaLaunchAttribute& a) {
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+}
+
+// Launches `kernel` on `stream` with the programmatic-serialization attribute; returns
+// NTB200_OK or NTB200_ERR_CUDA (with `what` in the detail).
+template <typename... KArgs, typename... Args>
+int launch_kernel(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                  size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  set_pdl_attribute(attr[0]);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(NTB200_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  }
+  return NTB200_OK;
+}
 
 // ------------------------------------------------------------------------------------
 // device side: element conversion
@@ -86,6 +123,15 @@ __device__ __forceinline__ void store_f(T* p, const float (&in)[N]) {
 #pragma unroll
   for (int i = 0; i < N; ++i) raw.v[i] = Elem<T>::from_f(in[i]);
   *reinterpret_cast<Vec<T, N>*>(p) = raw;
+}
+
+// Waits until the kernel before this one on the stream has completed (no-op when the
+// launch did not allow programmatic serialization).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allows the next kernel on the stream to launch once every CTA of this grid has called
+// it (or exited); that kernel still waits for this one's completion in its pdl_wait().
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 __device__ __forceinline__ void raise_device_error(unsigned int* word, unsigned int bit) {

@@ -1,7 +1,8 @@
 // Embedding gather: out[t, :] = weight[ids[t], :]  (bit-exact copy).
 //
 // One CTA per token row: the id is read once, then 16-byte units of the weight row are
-// copied (8/4/2/1-byte units when a pointer or stride is not 16-byte aligned).  Ids out
+// copied, each thread loading up to four units before storing them (8/4/2/1-byte units
+// when a pointer or stride is not 16-byte aligned).  Ids out
 // of range give a zero row and raise NTB200_DEVERR_INDEX_RANGE -- they never read outside
 // the table.  The reference kernel (vllm_nt/_ntops/kernels/wpe.py:11-67) tiles 64x64 with
 // num_tokens constexpr, i.e. one JIT compile per batch size; this kernel takes every size
@@ -11,6 +12,8 @@
 namespace ntb200 {
 namespace {
 
+constexpr int kItems = 4;  // units per thread, all loaded before any is stored
+
 template <typename U, typename I>
 __global__ void __launch_bounds__(256) embedding_kernel(char* __restrict__ out,
                                                          const I* __restrict__ ids,
@@ -19,6 +22,8 @@ __global__ void __launch_bounds__(256) embedding_kernel(char* __restrict__ out,
                                                          int64_t w_stride, int64_t o_stride,
                                                          unsigned int* err) {
   const int64_t t = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();
   const int64_t id = static_cast<int64_t>(ids[t]);
   U* dst = reinterpret_cast<U*>(out + t * o_stride);
   if (id < 0 || id >= num_embeddings) {
@@ -27,18 +32,28 @@ __global__ void __launch_bounds__(256) embedding_kernel(char* __restrict__ out,
     return;
   }
   const U* src = reinterpret_cast<const U*>(weight + id * w_stride);
-  for (int64_t u = threadIdx.x; u < units; u += blockDim.x) dst[u] = src[u];
+  const int64_t step = blockDim.x;
+  for (int64_t base = threadIdx.x; base < units; base += step * kItems) {
+    U v[kItems];
+#pragma unroll
+    for (int i = 0; i < kItems; ++i)
+      if (base + i * step < units) v[i] = src[base + i * step];
+#pragma unroll
+    for (int i = 0; i < kItems; ++i)
+      if (base + i * step < units) dst[base + i * step] = v[i];
+  }
 }
 
 template <typename U, typename I>
 int launch(void* out, const void* ids, const void* weight, int64_t tokens, int64_t num_emb,
            int64_t row_bytes, int64_t wsb, int64_t osb, cudaStream_t stream) {
   const int64_t units = row_bytes / static_cast<int64_t>(sizeof(U));
-  const int threads = units >= 256 ? 256 : static_cast<int>(ceil_div(units, 32) * 32);
-  embedding_kernel<U, I><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
-      static_cast<char*>(out), static_cast<const I*>(ids), static_cast<const char*>(weight),
-      num_emb, units, wsb, osb, device_error_word());
-  return check_launch("embedding");
+  const int64_t want = ceil_div(units, kItems);
+  const int threads = want >= 256 ? 256 : static_cast<int>(ceil_div(want, 32) * 32);
+  return launch_kernel("embedding", embedding_kernel<U, I>, dim3(static_cast<unsigned>(tokens)),
+                       dim3(threads), 0, stream, static_cast<char*>(out), static_cast<const I*>(ids),
+                       static_cast<const char*>(weight), num_emb, units, wsb, osb,
+                       device_error_word());
 }
 
 template <typename I>

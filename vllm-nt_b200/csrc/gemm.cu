@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
   const int lane = threadIdx.x & 31;
   const int num_tiles = p.num_m_blocks * p.num_n_blocks;
   const int k_steps = static_cast<int>((p.K + BK - 1) / BK);
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -165,6 +166,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
     mbar_init(mma_done, 1);
     fence_mbar_init();
   }
+  // tensor memory is allocated only after the preceding kernel has finished: a CTA of it
+  // that shares this SM may still be waiting to allocate its own
+  pdl_wait();
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_base_slot)),
@@ -439,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
   const int kb0 = split * p.k_steps_per_split;
   const int kb1 = min(kb0 + p.k_steps_per_split, p.k_steps_total);
   const int nk = kb1 > kb0 ? kb1 - kb0 : 0;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -448,6 +453,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
     mbar_init(tmem_full, 1);
     fence_mbar_init();
   }
+  // tensor memory is allocated only after the preceding kernel has finished (see the
+  // large-M kernel)
+  pdl_wait();
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_base_slot)),
@@ -613,13 +621,14 @@ int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallPa
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::kDynamicBytes;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(prm.splits);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  set_pdl_attribute(attr[1]);
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_m_kernel<T, MP, NT, BIG>, wmap, xmap, prm);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -748,13 +757,13 @@ int launch_large(void* out, const void* x, const void* weight, const void* bias,
   if (bf16) {
     st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__nv_bfloat16, BNV>), C::kDynamicBytes, slot);
     if (st != NTB200_OK) return st;
-    gemm_tcgen05_kernel<__nv_bfloat16, BNV><<<grid, kThreads, C::kDynamicBytes, s>>>(amap, bmap, prm);
-  } else {
-    st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__half, BNV>), C::kDynamicBytes, slot);
-    if (st != NTB200_OK) return st;
-    gemm_tcgen05_kernel<__half, BNV><<<grid, kThreads, C::kDynamicBytes, s>>>(amap, bmap, prm);
+    return launch_kernel("linear", gemm_tcgen05_kernel<__nv_bfloat16, BNV>, dim3(grid), dim3(kThreads),
+                         C::kDynamicBytes, s, amap, bmap, prm);
   }
-  return check_launch("linear");
+  st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__half, BNV>), C::kDynamicBytes, slot);
+  if (st != NTB200_OK) return st;
+  return launch_kernel("linear", gemm_tcgen05_kernel<__half, BNV>, dim3(grid), dim3(kThreads),
+                       C::kDynamicBytes, s, amap, bmap, prm);
 }
 
 }  // namespace

@@ -1,8 +1,8 @@
 // reshape_and_cache: slot-mapped scatter of one step's key/value rows into the paged cache.
 //
-// Pure data movement, bit-exact, no atomics.  One CTA per token: it reads the token's slot
-// once, then its threads move 16-byte units of every (K|V, head) row from the projection
-// output to cache[slot / block_size, slot % block_size, head, :].  The unit shrinks to 8,
+// Pure data movement, bit-exact, no atomics.  One CTA per token: its threads load up to
+// four 16-byte units each of the token's (K|V, head) rows while the slot is read, then
+// store them to cache[slot / block_size, slot % block_size, head, :].  The unit shrinks to 8,
 // 4, 2 or 1 bytes when a pointer or stride is not 16-byte aligned.  Loads are marked
 // streaming (read once) and stores evict-first: the cache rows written here are read
 // back only by a later decode step, from HBM.
@@ -42,6 +42,24 @@ __device__ __forceinline__ void st_stream<uint8_t>(uint8_t* p, uint8_t v) {
 }
 
 // All strides in bytes.
+constexpr int kItems = 4;  // units per thread, loaded together before any store
+
+template <typename U>
+struct RowSrc {
+  const char* key;
+  const char* value;
+  int64_t kts, khs, vts, vhs;
+  int per_tensor, units_per_head;
+  __device__ __forceinline__ const U* unit(int64_t t, int item, int& h, int& u, bool& is_v) const {
+    is_v = item >= per_tensor;
+    const int rem = is_v ? item - per_tensor : item;
+    h = rem / units_per_head;
+    u = rem - h * units_per_head;
+    const char* base = is_v ? value + t * vts + h * vhs : key + t * kts + h * khs;
+    return reinterpret_cast<const U*>(base) + u;
+  }
+};
+
 template <typename U, typename S>
 __global__ void __launch_bounds__(1024) reshape_and_cache_kernel(
     const char* __restrict__ key, const char* __restrict__ value, char* __restrict__ kc,
@@ -49,17 +67,19 @@ __global__ void __launch_bounds__(1024) reshape_and_cache_kernel(
     int num_heads, int units_per_head, int64_t kts, int64_t khs, int64_t vts, int64_t vhs,
     int64_t cbs, int64_t cps, int64_t chs, unsigned int* err) {
   const int64_t t = blockIdx.x;
-  const int per_tensor = num_heads * units_per_head;
-  // The first item's load does not depend on the slot: issue it together with the slot
-  // read so the two memory latencies overlap instead of adding up.
-  const int item0 = threadIdx.x;
-  U first{};
-  if (item0 < 2 * per_tensor) {
-    const bool is_v = item0 >= per_tensor;
-    const int rem = is_v ? item0 - per_tensor : item0;
-    const int h = rem / units_per_head;
-    const char* src = is_v ? value + t * vts + h * vhs : key + t * kts + h * khs;
-    first = ld_stream(reinterpret_cast<const U*>(src) + (rem - h * units_per_head));
+  const RowSrc<U> src{key, value, kts, khs, vts, vhs, num_heads * units_per_head, units_per_head};
+  const int total = 2 * src.per_tensor;
+  const int step = blockDim.x;
+  pdl_trigger();
+  pdl_wait();
+  // the first group of units is in flight before the slot is known
+  U v[kItems];
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) {
+    const int item = threadIdx.x + i * step;
+    int h, u;
+    bool is_v;
+    if (item < total) v[i] = ld_stream(src.unit(t, item, h, u, is_v));
   }
   const int64_t slot = static_cast<int64_t>(slots[t]);
   if (slot < 0) return;  // padding token
@@ -69,18 +89,27 @@ __global__ void __launch_bounds__(1024) reshape_and_cache_kernel(
   }
   const int64_t blk = slot / block_size;
   const int64_t dst_row = blk * cbs + (slot - blk * block_size) * cps;
-  for (int item = item0; item < 2 * per_tensor; item += blockDim.x) {
-    const bool is_v = item >= per_tensor;
-    const int rem = is_v ? item - per_tensor : item;
-    const int h = rem / units_per_head;
-    const int u = rem - h * units_per_head;
-    char* dst = (is_v ? vc : kc) + dst_row + h * chs;
-    U v = first;
-    if (item != item0) {
-      const char* src = is_v ? value + t * vts + h * vhs : key + t * kts + h * khs;
-      v = ld_stream(reinterpret_cast<const U*>(src) + u);
+  for (int base = threadIdx.x; base < total; base += step * kItems) {
+    if (base != threadIdx.x) {
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) {
+        const int item = base + i * step;
+        int h, u;
+        bool is_v;
+        if (item < total) v[i] = ld_stream(src.unit(t, item, h, u, is_v));
+      }
     }
-    st_stream(reinterpret_cast<U*>(dst) + u, v);
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int item = base + i * step;
+      if (item < total) {
+        int h, u;
+        bool is_v;
+        src.unit(t, item, h, u, is_v);
+        char* dst = (is_v ? vc : kc) + dst_row + h * chs;
+        st_stream(reinterpret_cast<U*>(dst) + u, v[i]);
+      }
+    }
   }
 }
 
@@ -91,13 +120,15 @@ int launch(const void* key, const void* value, void* kc, void* vc, const void* s
            int64_t cps, int64_t chs, cudaStream_t stream) {
   const int uph = static_cast<int>(head_bytes / sizeof(U));
   const int64_t items = 2 * heads * uph;
-  // one unit per thread where the row allows it (all loads of a token in flight at once)
-  const int threads = items >= 1024 ? 1024 : static_cast<int>(ceil_div(items, 32) * 32);
-  reshape_and_cache_kernel<U, S><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
-      static_cast<const char*>(key), static_cast<const char*>(value), static_cast<char*>(kc),
-      static_cast<char*>(vc), static_cast<const S*>(slots), num_slots, block_size,
-      static_cast<int>(heads), uph, kts, khs, vts, vhs, cbs, cps, chs, device_error_word());
-  return check_launch("reshape_and_cache");
+  // up to kItems units per thread (all loads of a token in flight at once)
+  const int64_t want = ceil_div(items, kItems);
+  const int threads = want >= 1024 ? 1024 : static_cast<int>(ceil_div(want, 32) * 32);
+  return launch_kernel("reshape_and_cache", reshape_and_cache_kernel<U, S>,
+                       dim3(static_cast<unsigned>(tokens)), dim3(threads), 0, stream,
+                       static_cast<const char*>(key), static_cast<const char*>(value),
+                       static_cast<char*>(kc), static_cast<char*>(vc), static_cast<const S*>(slots),
+                       num_slots, block_size, static_cast<int>(heads), uph, kts, khs, vts, vhs, cbs,
+                       cps, chs, device_error_word());
 }
 
 template <typename S>

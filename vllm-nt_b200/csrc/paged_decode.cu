@@ -148,6 +148,8 @@ __global__ void __launch_bounds__(kThreads) paged_decode_split_kernel(
   const int b = blockIdx.z;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
 
   int ctx = p.seq_lens[b];
   if (ctx < 0) ctx = 0;
@@ -376,6 +378,8 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(
     int64_t o_head_stride, unsigned int* err) {
   const int64_t wid = int64_t(blockIdx.x) * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
   if (wid >= int64_t(num_seqs) * num_q_heads) return;
   const int b = static_cast<int>(wid / num_q_heads);
   const int qh = static_cast<int>(wid - int64_t(b) * num_q_heads);
@@ -588,27 +592,27 @@ extern "C" int ntb200_paged_attention_decode(
   if (dtype == NTB200_DTYPE_BF16) {
     st = ensure_smem_attribute(reinterpret_cast<const void*>(paged_decode_split_kernel<__nv_bfloat16>), smem, 0);
     if (st != NTB200_OK) return st;
-    paged_decode_split_kernel<__nv_bfloat16><<<grid, kThreads, smem, s>>>(kmap, vmap, prm);
+    st = launch_kernel("paged_decode_split", paged_decode_split_kernel<__nv_bfloat16>, grid,
+                       dim3(kThreads), smem, s, kmap, vmap, prm);
   } else {
     st = ensure_smem_attribute(reinterpret_cast<const void*>(paged_decode_split_kernel<__half>), smem, 1);
     if (st != NTB200_OK) return st;
-    paged_decode_split_kernel<__half><<<grid, kThreads, smem, s>>>(kmap, vmap, prm);
+    st = launch_kernel("paged_decode_split", paged_decode_split_kernel<__half>, grid,
+                       dim3(kThreads), smem, s, kmap, vmap, prm);
   }
-  st = check_launch("paged_decode_split");
   if (st != NTB200_OK) return st;
 
   const int64_t warps = num_seqs * num_q_heads;
-  const unsigned cgrid = static_cast<unsigned>(ceil_div(warps, 4));
-  if (dtype == NTB200_DTYPE_BF16) {
-    paged_decode_combine_kernel<__nv_bfloat16><<<cgrid, 128, 0, s>>>(
-        static_cast<__nv_bfloat16*>(out), prm.part_o, prm.part_lse, seq_lens, int(num_seqs),
-        int(num_q_heads), int(group), chunk_tokens, int(max_chunks), max_blocks_per_seq,
-        out_seq_stride, out_head_stride, prm.err);
-  } else {
-    paged_decode_combine_kernel<__half><<<cgrid, 128, 0, s>>>(
-        static_cast<__half*>(out), prm.part_o, prm.part_lse, seq_lens, int(num_seqs),
-        int(num_q_heads), int(group), chunk_tokens, int(max_chunks), max_blocks_per_seq,
-        out_seq_stride, out_head_stride, prm.err);
-  }
-  return check_launch("paged_decode_combine");
+  const dim3 cgrid(static_cast<unsigned>(ceil_div(warps, 4)));
+  if (dtype == NTB200_DTYPE_BF16)
+    return launch_kernel("paged_decode_combine", paged_decode_combine_kernel<__nv_bfloat16>, cgrid,
+                         dim3(128), 0, s, static_cast<__nv_bfloat16*>(out), prm.part_o,
+                         prm.part_lse, seq_lens, int(num_seqs), int(num_q_heads), int(group),
+                         chunk_tokens, int(max_chunks), max_blocks_per_seq, out_seq_stride,
+                         out_head_stride, prm.err);
+  return launch_kernel("paged_decode_combine", paged_decode_combine_kernel<__half>, cgrid,
+                       dim3(128), 0, s, static_cast<__half*>(out), prm.part_o, prm.part_lse,
+                       seq_lens, int(num_seqs), int(num_q_heads), int(group), chunk_tokens,
+                       int(max_chunks), max_blocks_per_seq, out_seq_stride, out_head_stride,
+                       prm.err);
 }

@@ -1,9 +1,9 @@
 // RMS norm and fused residual-add RMS norm.
 //
-// One CTA per row.  Every thread issues all of its 128-bit loads of the row up front
-// (x, and the residual when fused), keeps the fp32 sum in registers, writes the new
-// residual, reduces sum(s^2) with warp shuffles + one shared-memory step, then streams
-// weight*normalised values out.  HBM traffic is the algorithmic minimum: x (+residual)
+// One CTA per row, two 16-byte vectors per thread.  Every thread issues all of its loads
+// of the row up front (x, the residual when fused, the weight), keeps the fp32 sum in
+// registers, writes the new residual, reduces sum(s^2) with warp shuffles + one
+// shared-memory step, then streams weight*normalised values out.  HBM traffic is the algorithmic minimum: x (+residual)
 // read once, out (+residual) written once, weight read from L2 after the first rows.
 //
 // out may alias x (vLLM's in-place convention): each thread reads its own vectors of x
@@ -19,7 +19,7 @@
 namespace ntb200 {
 namespace {
 
-constexpr int kMaxItems = 4;  // vectors per thread kept in registers
+constexpr int kMaxItems = 2;  // vectors per thread kept in registers
 
 template <int THREADS>
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -39,34 +39,50 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   }
 }
 
-// T: storage type; VEC: elements per vector access; THREADS: CTA size.
-// Rows with more than THREADS*kMaxItems vectors take a second pass (re-reading x and
-// residual from L2) -- the register-resident path covers hidden <= 32768 bf16.
-template <typename T, int VEC, int THREADS, bool FUSED>
+// T: storage type; VEC: elements per vector access; THREADS: CTA size; HAS_W: a weight
+// is given.  Rows with more than THREADS*kMaxItems vectors take a second pass (re-reading
+// x and residual from L2) -- the register-resident path covers hidden <= 16384 bf16.
+template <typename T, int VEC, int THREADS, bool FUSED, bool HAS_W>
 __global__ void __launch_bounds__(THREADS) rms_norm_kernel(
-    T* out, T* __restrict__ residual, const T* x, const T* __restrict__ weight, int64_t hidden, int64_t x_stride, int64_t r_stride,
-    int64_t o_stride, float eps) {
+    T* out, T* __restrict__ residual, const T* x, const T* __restrict__ weight, int64_t hidden,
+    int64_t x_stride, int64_t r_stride, int64_t o_stride, float eps) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * x_stride;
   T* rr = FUSED ? residual + row * r_stride : nullptr;
   T* orow = out + row * o_stride;
   const int64_t nvec = hidden / VEC;
+  pdl_trigger();
+  pdl_wait();
 
+  // Every load of the register-resident window (x, residual, weight) is issued before the
+  // first store: a residual store between them would keep the compiler from hoisting the
+  // later loads (x is not __restrict__), leaving one round trip to HBM per vector.
+  using V = Vec<T, VEC>;
+  V xraw[kMaxItems];
+  V rraw[FUSED ? kMaxItems : 1];
+  V wraw[HAS_W ? kMaxItems : 1];
+#pragma unroll
+  for (int it = 0; it < kMaxItems; ++it) {
+    const int64_t vi = threadIdx.x + int64_t(it) * THREADS;
+    if (vi < nvec) {
+      xraw[it] = *reinterpret_cast<const V*>(xr + vi * VEC);
+      if constexpr (FUSED) rraw[it] = *reinterpret_cast<const V*>(rr + vi * VEC);
+      if constexpr (HAS_W) wraw[it] = *reinterpret_cast<const V*>(weight + vi * VEC);
+    }
+  }
   float s[kMaxItems][VEC];
   float sumsq = 0.f;
 #pragma unroll
   for (int it = 0; it < kMaxItems; ++it) {
     const int64_t vi = threadIdx.x + int64_t(it) * THREADS;
     if (vi < nvec) {
-      load_f<T, VEC>(xr + vi * VEC, s[it]);
-      if constexpr (FUSED) {
-        float r[VEC];
-        load_f<T, VEC>(rr + vi * VEC, r);
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) s[it][j] += r[j];
-        store_f<T, VEC>(rr + vi * VEC, s[it]);
+      for (int j = 0; j < VEC; ++j) {
+        s[it][j] = Elem<T>::to_f(xraw[it].v[j]);
+        if constexpr (FUSED) s[it][j] += Elem<T>::to_f(rraw[it].v[j]);
       }
+      if constexpr (FUSED) store_f<T, VEC>(rr + vi * VEC, s[it]);
 #pragma unroll
       for (int j = 0; j < VEC; ++j) sumsq += s[it][j] * s[it][j];
     }
@@ -86,39 +102,22 @@ __global__ void __launch_bounds__(THREADS) rms_norm_kernel(
     for (int j = 0; j < VEC; ++j) sumsq += t[j] * t[j];
   }
 
-  // weight of the register-resident vectors, fetched before the reduction so that its
-  // latency overlaps the block-wide sum
-  Vec<T, VEC> wraw[kMaxItems];
-#pragma unroll
-  for (int it = 0; it < kMaxItems; ++it) {
-    const int64_t vi = threadIdx.x + int64_t(it) * THREADS;
-    if (weight != nullptr && vi < nvec) wraw[it] = *reinterpret_cast<const Vec<T, VEC>*>(weight + vi * VEC);
-  }
-
   const float total = block_sum<THREADS>(sumsq, red);
   const float rstd = rsqrtf(total / static_cast<float>(hidden) + eps);
 
-  auto emit_w = [&](int64_t vi, const float (&v)[VEC], const Vec<T, VEC>* w) {
+  auto emit = [&](int64_t vi, const float (&v)[VEC], const V& w) {
     float y[VEC];
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
-      const float wj = w != nullptr ? Elem<T>::to_f(w->v[j]) : 1.f;
+      const float wj = HAS_W ? Elem<T>::to_f(w.v[j]) : 1.f;
       y[j] = Elem<T>::round(v[j] * rstd) * wj;
     }
     store_f<T, VEC>(orow + vi * VEC, y);
   };
-  auto emit = [&](int64_t vi, const float (&v)[VEC]) {
-    if (weight != nullptr) {
-      const Vec<T, VEC> w = *reinterpret_cast<const Vec<T, VEC>*>(weight + vi * VEC);
-      emit_w(vi, v, &w);
-    } else {
-      emit_w(vi, v, nullptr);
-    }
-  };
 #pragma unroll
   for (int it = 0; it < kMaxItems; ++it) {
     const int64_t vi = threadIdx.x + int64_t(it) * THREADS;
-    if (vi < nvec) emit_w(vi, s[it], weight != nullptr ? &wraw[it] : nullptr);
+    if (vi < nvec) emit(vi, s[it], wraw[HAS_W ? it : 0]);
   }
   for (int64_t vi = threadIdx.x + int64_t(kMaxItems) * THREADS; vi < nvec; vi += THREADS) {
     float t[VEC];
@@ -128,33 +127,35 @@ __global__ void __launch_bounds__(THREADS) rms_norm_kernel(
     } else {
       load_f<T, VEC>(xr + vi * VEC, t);
     }
-    emit(vi, t);
+    V w{};
+    if constexpr (HAS_W) w = *reinterpret_cast<const V*>(weight + vi * VEC);
+    emit(vi, t, w);
   }
 }
 
-template <typename T, int VEC, bool FUSED>
+template <typename T, int VEC, bool FUSED, bool HAS_W>
 int launch_rows(T* out, T* residual, const T* x, const T* w, int64_t rows, int64_t hidden,
                 int64_t xs, int64_t rs, int64_t os, float eps, cudaStream_t stream) {
   const int64_t nvec = hidden / VEC;
   const int64_t want = ceil_div(nvec, kMaxItems);
-#define NTB200_RMS_LAUNCH(TH)                                                            \
-  rms_norm_kernel<T, VEC, TH, FUSED><<<static_cast<unsigned>(rows), TH, 0, stream>>>( \
-      out, residual, x, w, hidden, xs, rs, os, eps)
-  if (want <= 32) {
-    NTB200_RMS_LAUNCH(32);
-  } else if (want <= 64) {
-    NTB200_RMS_LAUNCH(64);
-  } else if (want <= 128) {
-    NTB200_RMS_LAUNCH(128);
-  } else if (want <= 256) {
-    NTB200_RMS_LAUNCH(256);
-  } else {
-    // 512 threads keep 4 vectors each in registers without spilling; longer rows take
-    // the second (L2) pass
-    NTB200_RMS_LAUNCH(512);
-  }
+#define NTB200_RMS_LAUNCH(TH)                                                                 \
+  return launch_kernel("rms_norm", rms_norm_kernel<T, VEC, TH, FUSED, HAS_W>,                \
+                       dim3(static_cast<unsigned>(rows)), dim3(TH), 0, stream, out, residual, x, w, \
+                       hidden, xs, rs, os, eps)
+  if (want <= 64) NTB200_RMS_LAUNCH(64);
+  if (want <= 128) NTB200_RMS_LAUNCH(128);
+  if (want <= 256) NTB200_RMS_LAUNCH(256);
+  if (want <= 512) NTB200_RMS_LAUNCH(512);
+  NTB200_RMS_LAUNCH(1024);
 #undef NTB200_RMS_LAUNCH
-  return check_launch("rms_norm");
+}
+
+template <typename T, int VEC, bool FUSED>
+int launch_weighted(T* out, T* residual, const T* x, const T* w, int64_t rows, int64_t hidden,
+                    int64_t xs, int64_t rs, int64_t os, float eps, cudaStream_t stream) {
+  if (w != nullptr)
+    return launch_rows<T, VEC, FUSED, true>(out, residual, x, w, rows, hidden, xs, rs, os, eps, stream);
+  return launch_rows<T, VEC, FUSED, false>(out, residual, x, w, rows, hidden, xs, rs, os, eps, stream);
 }
 
 template <typename T, bool FUSED>
@@ -169,8 +170,8 @@ int dispatch_vec(void* out, void* residual, const void* x, const void* w, int64_
   T* r = static_cast<T*>(residual);
   const T* xi = static_cast<const T*>(x);
   const T* wi = static_cast<const T*>(w);
-  if (vec_ok) return launch_rows<T, kVec, FUSED>(o, r, xi, wi, rows, hidden, xs, rs, os, eps, stream);
-  return launch_rows<T, 1, FUSED>(o, r, xi, wi, rows, hidden, xs, rs, os, eps, stream);
+  if (vec_ok) return launch_weighted<T, kVec, FUSED>(o, r, xi, wi, rows, hidden, xs, rs, os, eps, stream);
+  return launch_weighted<T, 1, FUSED>(o, r, xi, wi, rows, hidden, xs, rs, os, eps, stream);
 }
 
 template <bool FUSED>

@@ -44,6 +44,8 @@ __global__ void __launch_bounds__(1024) rope_neox_kernel(
   // before the position read so the two latencies overlap.
   float x1[VEC], x2[VEC];
   const int item0 = threadIdx.x;
+  pdl_trigger();
+  pdl_wait();
   if (item0 < total) {
     const int h = item0 / vph;
     const int i = (item0 - h * vph) * VEC;
@@ -90,16 +92,15 @@ int launch(const void* positions, void* q, void* k, const void* cache, int64_t t
     const int64_t items = (hq + (k != nullptr ? hk : 0)) * (half / vec);
     return static_cast<int>(items >= 1024 ? 1024 : (items < 32 ? 32 : ceil_div(items, 32) * 32));
   };
-  if (vec_ok) {
-    rope_neox_kernel<T, kVec, P><<<grid, threads_for(kVec), 0, stream>>>(
-        static_cast<const P*>(positions), static_cast<T*>(q), static_cast<T*>(k),
-        static_cast<const T*>(cache), int(hq), int(hk), int(half), qt, qh, kt, kh, cr, rows, err);
-  } else {
-    rope_neox_kernel<T, 1, P><<<grid, threads_for(1), 0, stream>>>(
-        static_cast<const P*>(positions), static_cast<T*>(q), static_cast<T*>(k),
-        static_cast<const T*>(cache), int(hq), int(hk), int(half), qt, qh, kt, kh, cr, rows, err);
-  }
-  return check_launch("rotary_embedding_neox");
+  if (vec_ok)
+    return launch_kernel("rotary_embedding_neox", rope_neox_kernel<T, kVec, P>, dim3(grid),
+                         dim3(threads_for(kVec)), 0, stream, static_cast<const P*>(positions),
+                         static_cast<T*>(q), static_cast<T*>(k), static_cast<const T*>(cache),
+                         int(hq), int(hk), int(half), qt, qh, kt, kh, cr, rows, err);
+  return launch_kernel("rotary_embedding_neox", rope_neox_kernel<T, 1, P>, dim3(grid),
+                       dim3(threads_for(1)), 0, stream, static_cast<const P*>(positions),
+                       static_cast<T*>(q), static_cast<T*>(k), static_cast<const T*>(cache),
+                       int(hq), int(hk), int(half), qt, qh, kt, kh, cr, rows, err);
 }
 
 template <typename T>

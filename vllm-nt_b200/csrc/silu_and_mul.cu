@@ -22,8 +22,10 @@ __global__ void __launch_bounds__(256) silu_and_mul_kernel(T* __restrict__ out,
                                                             int64_t o_stride) {
   const int64_t row = blockIdx.y;
   const int64_t vi = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  pdl_trigger();
   if (vi * VEC >= d) return;
   const T* xr = x + row * x_stride;
+  pdl_wait();
   float g[VEC], u[VEC], y[VEC];
   load_f<T, VEC>(xr + vi * VEC, g);
   load_f<T, VEC>(xr + d + vi * VEC, u);
@@ -41,14 +43,12 @@ int launch(void* out, const void* x, int64_t rows, int64_t d, int64_t xs, int64_
   const int threads = 256;
   if (vec_ok) {
     dim3 grid(static_cast<unsigned>(ceil_div(d / kVec, threads)), static_cast<unsigned>(rows));
-    silu_and_mul_kernel<T, kVec><<<grid, threads, 0, stream>>>(
-        static_cast<T*>(out), static_cast<const T*>(x), d, xs, os);
-  } else {
-    dim3 grid(static_cast<unsigned>(ceil_div(d, threads)), static_cast<unsigned>(rows));
-    silu_and_mul_kernel<T, 1><<<grid, threads, 0, stream>>>(static_cast<T*>(out),
-                                                             static_cast<const T*>(x), d, xs, os);
+    return launch_kernel("silu_and_mul", silu_and_mul_kernel<T, kVec>, grid, dim3(threads), 0,
+                         stream, static_cast<T*>(out), static_cast<const T*>(x), d, xs, os);
   }
-  return check_launch("silu_and_mul");
+  dim3 grid(static_cast<unsigned>(ceil_div(d, threads)), static_cast<unsigned>(rows));
+  return launch_kernel("silu_and_mul", silu_and_mul_kernel<T, 1>, grid, dim3(threads), 0, stream,
+                       static_cast<T*>(out), static_cast<const T*>(x), d, xs, os);
 }
 
 }  // namespace
