@@ -58,6 +58,17 @@ def test_linear_m1024_vs_fp32(k, n):
     torch.testing.assert_close(_ntb200_linear(xd, wd).float(), ref, rtol=TOL, atol=TOL)
 
 
+@pytest.mark.parametrize("k,n", SHAPES)
+def test_linear_m2048_cta_pairs_vs_fp32(k, n):
+    """M >= 2048 takes the CTA-pair kernel (256 x 256 tiles, tcgen05 cta_group::2)."""
+    dev = cuda_device()
+    gd = torch.Generator(device=dev).manual_seed(k + n + 1)
+    x = torch.randn(2048, k, generator=gd, device=dev, dtype=torch.bfloat16)
+    w = 0.02 * torch.randn(n, k, generator=gd, device=dev, dtype=torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    torch.testing.assert_close(_ntb200_linear(x, w).float(), ref, rtol=TOL, atol=TOL)
+
+
 def test_linear_m8192_gate_up_row_subset():
     dev = cuda_device()
     gd = torch.Generator(device=dev).manual_seed(3)
@@ -69,7 +80,8 @@ def test_linear_m8192_gate_up_row_subset():
     torch.testing.assert_close(out[rows].float(), ref, rtol=TOL, atol=TOL)
 
 
-@pytest.mark.parametrize("m,k,n", [(200, 72, 300), (5, 32, 12), (129, 4096, 257), (1, 8, 8), (300, 136, 257), (1000, 4096, 640)])
+@pytest.mark.parametrize("m,k,n", [(200, 72, 300), (5, 32, 12), (129, 4096, 257), (1, 8, 8), (300, 136, 257), (1000, 4096, 640),
+                                   (2100, 136, 520), (2048, 64, 256), (2304, 4096, 200), (4352, 6144, 520)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_linear_tails_and_bias_capi(m, k, n, dtype):
     x, w, b = _inputs(m, k, n, seed=m * 7 + n, dtype=dtype, bias=True)

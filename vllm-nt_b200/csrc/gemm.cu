@@ -1,8 +1,8 @@
 // Dense projection GEMM on the 5th-generation tensor cores:
 //   out[M, N] = x[M, K] . W[N, K]^T (+ bias),  bf16/f16 in, fp32 accumulate in TMEM.
 //
-// M > 256: persistent, warp-specialised, one CTA per SM (192 threads), tile 128 x BN with
-// BN = 256, 192 or 128 picked per shape to fill whole waves of SMs:
+// 256 < M < 2048: persistent, warp-specialised, one CTA per SM (192 threads), tile 128 x BN
+// with BN = 256, 192 or 128 picked per shape to fill whole waves of SMs:
 //   warp 0      TMA producer: 128x64 x-tile + BNx64 W-tile per k-step (128-byte swizzle,
 //               K-major) into a ~192-200 KB shared-memory ring;
 //   warp 1      allocates TMEM for two 128xBN fp32 accumulators and its lane 0 issues
@@ -11,6 +11,7 @@
 //   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
 //               32*(w%4)..+31, i.e. output rows), add bias, round, store.
 // The epilogue of tile i overlaps the MMAs of tile i+1 (double-buffered accumulator).
+// M >= 2048: the same roles in CTA pairs with 256 x 256 tiles (tcgen05 cta_group::2).
 // Tiles are walked with the M index fastest so a wave of CTAs shares W tiles through L2
 // while x (M*K*2 bytes) stays L2-resident.  No TMA multicast is used anywhere.
 //
@@ -124,8 +125,23 @@ struct GemmParams {
   int64_t M, N, K;
   int64_t out_stride;
   int num_m_blocks, num_n_blocks;
+  int group_m;  // M blocks per raster group (num_m_blocks: plain M-fastest order)
   unsigned int* err;
 };
+
+// Tile order: groups of `group_m` M blocks, M fastest inside a group, then N, then the next
+// group.  With group_m = num_m_blocks this is plain M-fastest order (x stays L2-resident
+// while each W tile is read once); a smaller group bounds the x rows a wave touches when x
+// is larger than L2, so that neither operand is streamed from HBM once per wave.
+__device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& mb, int& nb) {
+  const int per_group = p.group_m * p.num_n_blocks;
+  const int g = tile / per_group;
+  const int first_m = g * p.group_m;
+  const int rows = p.num_m_blocks - first_m < p.group_m ? p.num_m_blocks - first_m : p.group_m;
+  const int r = tile - g * per_group;
+  mb = first_m + r % rows;
+  nb = r / rows;
+}
 
 template <typename T, int BN_>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
@@ -189,8 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
       uint32_t it = 0;  // global k-step counter of this CTA
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile % p.num_m_blocks;
-        const int nb = tile / p.num_m_blocks;
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
         for (int kb = 0; kb < k_steps; ++kb, ++it) {
           const uint32_t s = it % kStages;
           if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, p.err)) {
@@ -258,8 +274,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
       const int use = local >> 1;
       if (!mbar_wait(&tmem_full[acc], use & 1, p.err)) break;
       tc_fence_after();
-      const int mb = tile % p.num_m_blocks;
-      const int nb = tile / p.num_m_blocks;
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
       const int64_t row = int64_t(mb) * BM + row_in_tile;
       const int64_t col0 = int64_t(nb) * BN;
       T* orow = out + row * p.out_stride;
@@ -303,6 +319,277 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ------------------------------------------------------------------------------------
+// Large M (M >= kPairMinM): CTA pairs.  A cluster of two CTAs computes a 256 x 256 output
+// tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16).  CTA r of the pair stages,
+// per 64-wide k-step, x rows [256*mb + 128*r, +128) and W rows [256*nb + 128*r, +128) in
+// its own shared memory; the MMA, issued by the even CTA, reads both CTAs' tiles and
+// leaves each CTA's 128 output rows (all 256 columns) in that CTA's TMEM.  For the same
+// tensor-core work per SM a k-step moves 32 KB into shared memory instead of the 48 KB of
+// a 128 x 256 single-CTA tile.  Synchronisation across the pair:
+//   full[s]       (even CTA) armed by its producer with both CTAs' bytes; both CTAs' TMA
+//                 loads complete_tx on it (.cta_group::2 lets a load signal the peer);
+//   empty[s]      (each CTA) the MMA issuer commits to both CTAs' barriers;
+//   tmem_full[a]  (each CTA) committed to both CTAs when an accumulator is final;
+//   tmem_empty[a] (even CTA) 8 arrivals: the 4 epilogue warps of each CTA.
+// A cluster barrier after set-up and another before TMEM is freed keep each CTA's shared
+// memory alive while its peer may still reach it.  No multicast is used.
+// ------------------------------------------------------------------------------------
+constexpr int64_t kPairMinM = 2048;
+
+struct PairCfg {
+  static constexpr int kHalf = 128;                  // x rows and W rows each CTA stages
+  static constexpr int kTile = 256;                  // output tile of the pair (M and N)
+  static constexpr int kHalfBytes = kHalf * BK * 2;  // 16 KB
+  static constexpr int kStageBytes = 2 * kHalfBytes;
+  static constexpr int kStages = 7;
+  static constexpr int kTmemCols = 512;  // two 128 x 256 fp32 accumulators per CTA
+  static constexpr int kRing = 0;
+  static constexpr int kFull = kStages * kStageBytes;
+  static constexpr int kEmpty = kFull + 8 * kStages;
+  static constexpr int kTmemFull = kEmpty + 8 * kStages;
+  static constexpr int kTmemEmpty = kTmemFull + 16;
+  static constexpr int kMmaDone = kTmemEmpty + 16;
+  static constexpr int kTmemBase = kMmaDone + 8;
+  static constexpr int kEnd = kTmemBase + 8;
+  static constexpr int kDynamicBytes = kEnd + 1024;
+  static_assert(kDynamicBytes <= 227 * 1024, "ring exceeds shared memory");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  return remote;
+}
+
+// TMA tile load into this CTA's shared memory whose completion is counted on an mbarrier
+// of either CTA of the pair (`bar` is a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` (a shared::cluster address in either CTA) once every tcgen05.mma this
+// thread has issued so far has completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void pair_cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
+    const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
+    const GemmParams p) {
+  using C = PairCfg;
+  constexpr int kStages = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kFull);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + C::kEmpty);
+  uint64_t* tmem_full = reinterpret_cast<uint64_t*>(smem + C::kTmemFull);
+  uint64_t* tmem_empty = reinterpret_cast<uint64_t*>(smem + C::kTmemEmpty);
+  uint64_t* mma_done = reinterpret_cast<uint64_t*>(smem + C::kMmaDone);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemBase);
+  const uint32_t ring = smem_u32(smem + C::kRing);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0: issues the MMAs; 1: its peer
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int num_pairs = static_cast<int>(gridDim.x >> 1);
+  const int num_tiles = p.num_m_blocks * p.num_n_blocks;
+  const int k_steps = static_cast<int>((p.K + BK - 1) / BK);
+  pdl_trigger();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 8);  // 4 epilogue warps in each CTA
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  // tensor memory is allocated only after the preceding kernel has finished
+  pdl_wait();
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_base_slot)),
+                 "r"(C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  pair_cluster_sync();  // both CTAs' barriers are initialised before either signals the other
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer (both CTAs) ------------------------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a_map)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&b_map)) : "memory");
+      const uint32_t full0 = peer_addr(smem_u32(&full[0]), 0);  // the even CTA's full[0]
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        int mb, nb;
+        tile_coords(tile, p, mb, nb);
+        const int arow = mb * C::kTile + static_cast<int>(rank) * C::kHalf;
+        const int brow = nb * C::kTile + static_cast<int>(rank) * C::kHalf;
+        for (int kb = 0; kb < k_steps; ++kb, ++it) {
+          const uint32_t s = it % kStages;
+          if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::kStageBytes);
+          const uint32_t a_dst = ring + s * C::kStageBytes;
+          tma_load_2d_pair(a_dst, &a_map, kb * BK, arow, full0 + 8 * s);
+          tma_load_2d_pair(a_dst + C::kHalfBytes, &b_map, kb * BK, brow, full0 + 8 * s);
+        }
+      }
+      // drain: every stage this CTA filled has been consumed (or the wait gives up)
+      const uint32_t first = it > kStages ? it - kStages : 0;
+      for (uint32_t j = first; j < it; ++j) mbar_wait(&empty[j % kStages], (j / kStages) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer (even CTA) ------------------------------
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = make_idesc(std::is_same<T, __nv_bfloat16>::value, C::kTile, C::kTile);
+      const uint32_t empty_peer = peer_addr(smem_u32(&empty[0]), 1);
+      const uint32_t tfull_peer = peer_addr(smem_u32(&tmem_full[0]), 1);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++local) {
+        const int acc = local & 1;
+        const int use = local >> 1;
+        if (use >= 1 && !mbar_wait(&tmem_empty[acc], (use - 1) & 1, p.err)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::kTile;
+        for (int kb = 0; kb < k_steps; ++kb, ++it) {
+          const uint32_t s = it % kStages;
+          if (!mbar_wait(&full[s], (it / kStages) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = ring + s * C::kStageBytes;
+          const uint64_t adesc = sw128_kmajor_desc(a_addr);
+          const uint64_t bdesc = sw128_kmajor_desc(a_addr + C::kHalfBytes);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_pair(d_tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair(smem_u32(&empty[s]));  // frees the stage in both CTAs
+          umma_commit_pair(empty_peer + 8 * s);
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&tmem_full[acc]));  // accumulator complete in both CTAs
+        umma_commit_pair(tfull_peer + 8 * acc);
+      }
+      umma_commit_pair(smem_u32(mma_done));
+      mbar_wait(mma_done, 0, p.err);
+    }
+  } else {
+    // ------------------------------ epilogue (both CTAs) ------------------------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = static_cast<int>(rank) * C::kHalf + quad * 32 + lane;
+    const uint32_t tempty0 = peer_addr(smem_u32(&tmem_empty[0]), 0);
+    T* out = static_cast<T*>(p.out);
+    const T* bias = static_cast<const T*>(p.bias);
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
+      const int acc = local & 1;
+      const int use = local >> 1;
+      if (!mbar_wait(&tmem_full[acc], use & 1, p.err)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(tile, p, mb, nb);
+      const int64_t row = int64_t(mb) * C::kTile + row_in_tile;
+      const int64_t col0 = int64_t(nb) * C::kTile;
+      T* orow = out + row * p.out_stride;
+#pragma unroll 1
+      for (int chunk = 0; chunk < C::kTile / 32; ++chunk) {
+        uint32_t r[32];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
+        tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + acc * C::kTile + chunk * 32, r);
+        const int64_t c0 = col0 + chunk * 32;
+        if (row < p.M && c0 < p.N) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          if (bias != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c0 + i < p.N) v[i] += Elem<T>::to_f(bias[c0 + i]);
+          }
+          if (c0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(orow + c0) & 15u) == 0)) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              float w[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) w[i] = v[q * 8 + i];
+              store_f<T, 8>(orow + c0 + q * 8, w);
+            }
+          } else {
+            for (int i = 0; i < 32 && c0 + i < p.N; ++i) orow[c0 + i] = Elem<T>::from_f(v[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(tempty0 + 8 * acc);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  pair_cluster_sync();  // the peer's MMAs, copies and arrivals that touch this CTA are done
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(C::kTmemCols)
                  : "memory");
   }
 }
@@ -713,6 +1000,13 @@ int dispatch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const Small
 // second cluster-reduction round.
 int small_tiles_per_cta(int mp, int64_t n_tiles, int sms) { return (mp >= 128 && n_tiles >= sms / 2) ? 2 : 1; }
 
+// M blocks per raster group: all of them when x fits comfortably in L2, else 8.
+int raster_group(int64_t M, int64_t K, int64_t mblocks) {
+  constexpr int64_t kL2Budget = 48ll << 20;
+  if (M * K * 2 <= kL2Budget || mblocks <= 8) return static_cast<int>(mblocks);
+  return 8;
+}
+
 // Tile width for the large-M kernel: the widest of 256/192/128 whose tiles fill the SMs'
 // waves (and cover N with little padding) to within 95% of the best candidate.
 int pick_tile_width(int64_t M, int64_t N, int sms) {
@@ -750,6 +1044,7 @@ int launch_large(void* out, const void* x, const void* weight, const void* bias,
   prm.out_stride = os;
   prm.num_m_blocks = static_cast<int>(mblocks);
   prm.num_n_blocks = static_cast<int>(nblocks);
+  prm.group_m = raster_group(M, K, mblocks);
   prm.err = device_error_word();
   const int64_t tiles = mblocks * nblocks;
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
@@ -764,6 +1059,58 @@ int launch_large(void* out, const void* x, const void* weight, const void* bias,
   if (st != NTB200_OK) return st;
   return launch_kernel("linear", gemm_tcgen05_kernel<__half, BNV>, dim3(grid), dim3(kThreads),
                        C::kDynamicBytes, s, amap, bmap, prm);
+}
+
+int launch_pair(void* out, const void* x, const void* weight, const void* bias, int64_t M, int64_t N,
+                int64_t K, int64_t xs, int64_t ws, int64_t os, bool bf16, cudaStream_t s) {
+  using C = PairCfg;
+  const int64_t mblocks = ceil_div(M, C::kTile), nblocks = ceil_div(N, C::kTile);
+  if (mblocks * nblocks > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
+  CUtensorMap amap, bmap;
+  int st = make_kmajor_map(&amap, x, bf16, M, K, xs, C::kHalf);
+  if (st != NTB200_OK) return st;
+  st = make_kmajor_map(&bmap, weight, bf16, N, K, ws, C::kHalf);
+  if (st != NTB200_OK) return st;
+  GemmParams prm;
+  prm.out = out;
+  prm.bias = bias;
+  prm.M = M;
+  prm.N = N;
+  prm.K = K;
+  prm.out_stride = os;
+  prm.num_m_blocks = static_cast<int>(mblocks);
+  prm.num_n_blocks = static_cast<int>(nblocks);
+  prm.group_m = raster_group(M, K, mblocks);
+  prm.err = device_error_word();
+  const int slot = bf16 ? 40 : 41;
+  const void* fn = bf16 ? reinterpret_cast<const void*>(gemm_pair_kernel<__nv_bfloat16>)
+                        : reinterpret_cast<const void*>(gemm_pair_kernel<__half>);
+  st = ensure_smem_attribute(fn, C::kDynamicBytes, slot);
+  if (st != NTB200_OK) return st;
+  int pairs = resident_clusters(fn, C::kDynamicBytes, 2, slot);
+  if (pairs <= 0) pairs = num_sms() / 2;
+  const int64_t tiles = mblocks * nblocks;
+  if (tiles < pairs) pairs = static_cast<int>(tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kDynamicBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  set_pdl_attribute(attr[1]);
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, gemm_pair_kernel<__nv_bfloat16>, amap, bmap, prm)
+                             : cudaLaunchKernelEx(&cfg, gemm_pair_kernel<__half>, amap, bmap, prm);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(NTB200_ERR_CUDA, "linear (CTA pairs): launch failed: %s", cudaGetErrorString(e));
+  }
+  return NTB200_OK;
 }
 
 }  // namespace
@@ -836,6 +1183,8 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     return bf16 ? dispatch_small<__nv_bfloat16>(wmap, xmap, sp_big, sp_small, mp, nt, s, 4)
                 : dispatch_small<__half>(wmap, xmap, sp_big, sp_small, mp, nt, s, 18);
   }
+  if (M >= kPairMinM)
+    return launch_pair(out, x, weight, bias, M, N, K, x_row_stride, weight_row_stride, out_row_stride, bf16, s);
   const int bn = pick_tile_width(M, N, num_sms());
   switch (bn) {
     case 128: return launch_large<128>(out, x, weight, bias, M, N, K, x_row_stride, weight_row_stride, out_row_stride, bf16, s);
