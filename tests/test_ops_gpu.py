@@ -312,3 +312,46 @@ def test_embedding_reference_case_int32_and_out_of_range():
     torch.cuda.synchronize()
     assert capi.read_device_error(stream()) & capi.DEVERR_INDEX_RANGE
     assert torch.equal(out[0], w[5]) and not out[1:].any()
+
+
+# ------------------------------------------------------------------ any-rank row layouts
+
+
+def test_torch_ops_take_any_rank_rows():
+    """[batch, tokens, hidden] activations go into the ops without Python reshapes; the
+    in-place fused norm (vLLM's CUDA convention) overwrites x and the residual."""
+    from vllm_nt._ntops.torch.rms_norm import fused_add_rms_norm, rms_norm
+    from vllm_nt._ntops.torch.silu import silu_and_mul
+
+    dev = cuda_device()
+    g = seeded(21)
+    x = torch.randn(2, 3, 4096, generator=g).to(torch.bfloat16)
+    r = torch.randn(2, 3, 4096, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(4096, generator=g)).to(torch.bfloat16)
+    ref_y, ref_r = oracle.fused_add_rms_norm(x.view(6, 4096), r.view(6, 4096), w, 1e-6)
+    xd, rd = x.to(dev), r.to(dev)
+    y, res = fused_add_rms_norm(xd, rd, w.to(dev), 1e-6, inplace=True)
+    assert y.data_ptr() == xd.data_ptr() and res.data_ptr() == rd.data_ptr() and y.shape == (2, 3, 4096)
+    _close(y.view(6, 4096), ref_y, torch.bfloat16)
+    assert bits_equal(res.view(6, 4096).cpu(), ref_r)
+    _close(rms_norm(x.to(dev), 4096, w.to(dev), 1e-6).view(6, 4096), oracle.rms_norm(x.view(6, 4096), w, 1e-6),
+           torch.bfloat16)
+    a = torch.randn(2, 5, 2 * 512, generator=g).to(torch.bfloat16)
+    out = silu_and_mul(a.to(dev))
+    assert out.shape == (2, 5, 512)
+    _close(out.view(10, 512), oracle.silu_and_mul(a.view(10, 1024)), torch.bfloat16)
+
+
+def test_linear_realigns_an_unaligned_activation():
+    """x whose base is 8 bytes off a 16-byte boundary and whose row stride is not a
+    multiple of 8 elements is copied once into a TMA-legal tensor by the op."""
+    from vllm_nt._ntops.torch.linear import linear
+
+    dev = cuda_device()
+    g = seeded(22)
+    big = torch.randn(5, 44, generator=g).to(torch.bfloat16)
+    w = (0.05 * torch.randn(24, 32, generator=g)).to(torch.bfloat16)
+    x = big.to(dev)[:, 4:36]
+    assert x.data_ptr() % 16 != 0 and x.stride(0) % 8 != 0
+    out = linear(x, w.to(dev))
+    _close(out, oracle.linear(big[:, 4:36], w), torch.bfloat16)

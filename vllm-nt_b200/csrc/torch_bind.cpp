@@ -43,88 +43,130 @@ void require_rows(const at::Tensor& t, const char* name) {
               " must be 2-D with unit stride in the last dim");
 }
 
+// A tensor seen as rows of its last dimension: the last dimension has unit stride and the
+// leading dimensions collapse into one row index with a single stride (any contiguous
+// tensor, a row-strided 2-D view, ...).  vLLM hands the hooks [tokens, hidden] or
+// [batch, tokens, hidden] activations; viewing them here saves the Python reshapes.
+struct Rows {
+  int64_t rows = 0, stride = 0, cols = 0;
+};
+
+Rows rows_of(const at::Tensor& t, const char* name) {
+  require_cuda(t, name);
+  const int64_t d = t.dim();
+  TORCH_CHECK(d >= 1 && t.stride(d - 1) == 1, "ntb200: ", name, " needs unit stride in the last dim");
+  Rows r;
+  r.cols = t.size(d - 1);
+  if (d == 1) {
+    r.rows = 1;
+    r.stride = r.cols;
+    return r;
+  }
+  r.rows = t.size(d - 2);
+  r.stride = t.stride(d - 2);
+  int64_t expect = r.stride * t.size(d - 2);
+  for (int64_t i = d - 3; i >= 0; --i) {
+    if (t.size(i) == 1) continue;
+    TORCH_CHECK(t.stride(i) == expect, "ntb200: ", name, "'s leading dims do not collapse into rows");
+    r.rows *= t.size(i);
+    expect = t.stride(i) * t.size(i);
+  }
+  if (r.rows <= 1) r.stride = r.cols > r.stride ? r.cols : r.stride;
+  return r;
+}
+
+void same_leading(const at::Tensor& a, const at::Tensor& b, const char* what) {
+  TORCH_CHECK(a.dim() == b.dim(), "ntb200.", what, ": rank mismatch");
+  for (int64_t i = 0; i + 1 < a.dim(); ++i)
+    TORCH_CHECK(a.size(i) == b.size(i), "ntb200.", what, ": leading shape mismatch");
+}
+
+const void* norm_weight(const std::optional<at::Tensor>& weight, const at::Tensor& x, int64_t hidden,
+                        const char* what) {
+  if (!weight.has_value()) return nullptr;
+  TORCH_CHECK(weight->is_contiguous() && weight->numel() == hidden && weight->scalar_type() == x.scalar_type(),
+              "ntb200.", what, ": weight must be contiguous [hidden] of x's dtype");
+  return weight->data_ptr();
+}
+
 void rms_norm(at::Tensor out, const at::Tensor& x, const std::optional<at::Tensor>& weight,
               double eps) {
-  require_rows(x, "x");
-  require_rows(out, "out");
+  const Rows xr = rows_of(x, "x"), orr = rows_of(out, "out");
   TORCH_CHECK(out.sizes() == x.sizes() && out.scalar_type() == x.scalar_type(), "ntb200.rms_norm: out mismatch");
-  const void* w = nullptr;
-  if (weight.has_value()) {
-    TORCH_CHECK(weight->is_contiguous() && weight->numel() == x.size(1) &&
-                    weight->scalar_type() == x.scalar_type(),
-                "ntb200.rms_norm: weight must be contiguous [hidden] of x's dtype");
-    w = weight->data_ptr();
-  }
+  const void* w = norm_weight(weight, x, xr.cols, "rms_norm");
   c10::cuda::CUDAGuard guard(x.device());
-  check(ntb200_rms_norm(out.data_ptr(), x.data_ptr(), w, x.size(0), x.size(1), x.stride(0),
-                        out.stride(0), static_cast<float>(eps), dtype_code(x), stream_of(x)),
+  check(ntb200_rms_norm(out.data_ptr(), x.data_ptr(), w, xr.rows, xr.cols, xr.stride, orr.stride,
+                        static_cast<float>(eps), dtype_code(x), stream_of(x)),
         "rms_norm");
 }
 
 void fused_add_rms_norm(at::Tensor out, at::Tensor residual, const at::Tensor& x,
                         const std::optional<at::Tensor>& weight, double eps) {
-  require_rows(x, "x");
-  require_rows(out, "out");
-  require_rows(residual, "residual");
+  const Rows xr = rows_of(x, "x"), orr = rows_of(out, "out"), rr = rows_of(residual, "residual");
   TORCH_CHECK(out.sizes() == x.sizes() && residual.sizes() == x.sizes() &&
                   out.scalar_type() == x.scalar_type() &&
                   residual.scalar_type() == x.scalar_type(),
               "ntb200.fused_add_rms_norm: shape/dtype mismatch");
-  const void* w = nullptr;
-  if (weight.has_value()) {
-    TORCH_CHECK(weight->is_contiguous() && weight->numel() == x.size(1) &&
-                    weight->scalar_type() == x.scalar_type(),
-                "ntb200.fused_add_rms_norm: weight must be contiguous [hidden] of x's dtype");
-    w = weight->data_ptr();
-  }
+  const void* w = norm_weight(weight, x, xr.cols, "fused_add_rms_norm");
   c10::cuda::CUDAGuard guard(x.device());
-  check(ntb200_fused_add_rms_norm(out.data_ptr(), residual.data_ptr(), x.data_ptr(), w,
-                                  x.size(0), x.size(1), x.stride(0), residual.stride(0),
-                                  out.stride(0), static_cast<float>(eps), dtype_code(x),
-                                  stream_of(x)),
+  check(ntb200_fused_add_rms_norm(out.data_ptr(), residual.data_ptr(), x.data_ptr(), w, xr.rows,
+                                  xr.cols, xr.stride, rr.stride, orr.stride,
+                                  static_cast<float>(eps), dtype_code(x), stream_of(x)),
         "fused_add_rms_norm");
 }
 
 void silu_and_mul(at::Tensor out, const at::Tensor& x) {
-  require_rows(x, "x");
-  require_rows(out, "out");
-  TORCH_CHECK(x.size(1) % 2 == 0 && out.size(1) == x.size(1) / 2 && out.size(0) == x.size(0) &&
-                  out.scalar_type() == x.scalar_type(),
-              "ntb200.silu_and_mul: out must be [rows, d] for x [rows, 2d]");
+  const Rows xr = rows_of(x, "x"), orr = rows_of(out, "out");
+  same_leading(x, out, "silu_and_mul");
+  TORCH_CHECK(xr.cols % 2 == 0 && orr.cols == xr.cols / 2 && out.scalar_type() == x.scalar_type(),
+              "ntb200.silu_and_mul: out must be [..., d] for x [..., 2d]");
   c10::cuda::CUDAGuard guard(x.device());
-  check(ntb200_silu_and_mul(out.data_ptr(), x.data_ptr(), x.size(0), out.size(1), x.stride(0),
-                            out.stride(0), dtype_code(x), stream_of(x)),
+  check(ntb200_silu_and_mul(out.data_ptr(), x.data_ptr(), xr.rows, orr.cols, xr.stride, orr.stride,
+                            dtype_code(x), stream_of(x)),
         "silu_and_mul");
+}
+
+// query/key as vLLM passes them ([tokens, heads * head_size], a column slice of the qkv
+// projection) or as [tokens, heads, head_size]; returns heads, token and head strides.
+void head_geometry(const at::Tensor& t, int64_t tokens, int64_t head_size, const char* name,
+                   int64_t& heads, int64_t& ts, int64_t& hs) {
+  require_cuda(t, name);
+  if (t.dim() == 2) {
+    TORCH_CHECK(t.stride(1) == 1 && t.size(0) == tokens && t.size(1) % head_size == 0,
+                "ntb200.rope: ", name, " [tokens, heads * head_size] with unit inner stride");
+    heads = t.size(1) / head_size;
+    ts = t.stride(0);
+    hs = head_size;
+    return;
+  }
+  TORCH_CHECK(t.dim() == 3 && t.size(2) == head_size && t.stride(2) == 1 && t.size(0) == tokens,
+              "ntb200.rope: ", name, " must be [tokens, heads, head_size] with unit inner stride");
+  heads = t.size(1);
+  ts = t.stride(0);
+  hs = t.stride(1);
 }
 
 void rotary_embedding_neox(const at::Tensor& positions, at::Tensor query,
                            const std::optional<at::Tensor>& key, const at::Tensor& cache,
                            int64_t head_size, int64_t rotary_dim) {
-  require_cuda(query, "query");
   require_cuda(positions, "positions");
   require_rows(cache, "cos_sin_cache");
-  TORCH_CHECK(positions.dim() == 1 && positions.is_contiguous(), "ntb200.rope: positions must be 1-D contiguous");
-  TORCH_CHECK(query.dim() == 3 && query.size(2) == head_size && query.stride(2) == 1 &&
-                  query.size(0) == positions.size(0),
-              "ntb200.rope: query must be [tokens, heads, head_size] with unit inner stride");
+  TORCH_CHECK(positions.is_contiguous(), "ntb200.rope: positions must be contiguous");
   TORCH_CHECK(cache.scalar_type() == query.scalar_type(), "ntb200.rope: cos_sin_cache dtype must match query");
+  const int64_t tokens = positions.numel();
+  int64_t hq = 0, qts = 0, qhs = 0, hk = 0, kts = 0, khs = 0;
+  head_geometry(query, tokens, head_size, "query", hq, qts, qhs);
   void* kptr = nullptr;
-  int64_t hk = 0, kts = 0, khs = 0;
   if (key.has_value()) {
-    TORCH_CHECK(key->dim() == 3 && key->size(2) == head_size && key->stride(2) == 1 &&
-                    key->size(0) == positions.size(0) && key->scalar_type() == query.scalar_type(),
-                "ntb200.rope: key must be [tokens, heads, head_size] like query");
+    TORCH_CHECK(key->scalar_type() == query.scalar_type(), "ntb200.rope: key dtype must match query");
+    head_geometry(*key, tokens, head_size, "key", hk, kts, khs);
     kptr = key->data_ptr();
-    hk = key->size(1);
-    kts = key->stride(0);
-    khs = key->stride(1);
   }
   c10::cuda::CUDAGuard guard(query.device());
   check(ntb200_rotary_embedding_neox(positions.data_ptr(), dtype_code(positions), query.data_ptr(),
-                                     kptr, cache.data_ptr(), positions.size(0), query.size(1), hk,
-                                     head_size, rotary_dim, query.stride(0), query.stride(1), kts,
-                                     khs, cache.stride(0), cache.size(0), dtype_code(query),
-                                     stream_of(query)),
+                                     kptr, cache.data_ptr(), tokens, hq, hk, head_size, rotary_dim,
+                                     qts, qhs, kts, khs, cache.stride(0), cache.size(0),
+                                     dtype_code(query), stream_of(query)),
         "rotary_embedding_neox");
 }
 
@@ -219,15 +261,23 @@ int64_t decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num
       num_seqs, num_q_heads, num_kv_heads, head_size, block_size, max_seq_len));
 }
 
-void linear(at::Tensor out, const at::Tensor& x, const at::Tensor& weight,
+// x [..., K] (rows must collapse; a TMA operand needs a 16-byte aligned base and a row
+// stride that is a multiple of 8 elements, otherwise x is copied once into a fresh tensor)
+void linear(at::Tensor out, const at::Tensor& x_in, const at::Tensor& weight,
             const std::optional<at::Tensor>& bias, const std::optional<at::Tensor>& workspace) {
-  require_rows(x, "x");
   require_rows(weight, "weight");
-  require_rows(out, "out");
-  TORCH_CHECK(weight.size(1) == x.size(1) && out.size(0) == x.size(0) &&
-                  out.size(1) == weight.size(0) && weight.scalar_type() == x.scalar_type() &&
-                  out.scalar_type() == x.scalar_type(),
-              "ntb200.linear: x [M, K], weight [N, K], out [M, N] of one dtype");
+  at::Tensor x = x_in;
+  Rows xr = rows_of(x, "x");
+  if ((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15u) != 0 || xr.stride % 8 != 0) {
+    x = at::empty(x_in.sizes(), x_in.options());
+    x.copy_(x_in);
+    xr = rows_of(x, "x");
+  }
+  const Rows orr = rows_of(out, "out");
+  same_leading(x, out, "linear");
+  TORCH_CHECK(weight.size(1) == xr.cols && orr.cols == weight.size(0) &&
+                  weight.scalar_type() == x.scalar_type() && out.scalar_type() == x.scalar_type(),
+              "ntb200.linear: x [..., K], weight [N, K], out [..., N] of one dtype");
   const void* b = nullptr;
   if (bias.has_value()) {
     TORCH_CHECK(bias->is_contiguous() && bias->numel() == weight.size(0) &&
@@ -243,9 +293,9 @@ void linear(at::Tensor out, const at::Tensor& x, const at::Tensor& weight,
     ws_bytes = static_cast<size_t>(workspace->numel() * workspace->element_size());
   }
   c10::cuda::CUDAGuard guard(x.device());
-  check(ntb200_linear(out.data_ptr(), x.data_ptr(), weight.data_ptr(), b, x.size(0),
-                      weight.size(0), x.size(1), x.stride(0), weight.stride(0), out.stride(0), ws,
-                      ws_bytes, dtype_code(x), stream_of(x)),
+  check(ntb200_linear(out.data_ptr(), x.data_ptr(), weight.data_ptr(), b, xr.rows, weight.size(0),
+                      xr.cols, xr.stride, weight.stride(0), orr.stride, ws, ws_bytes, dtype_code(x),
+                      stream_of(x)),
         "linear");
 }
 

@@ -56,8 +56,7 @@ def act_and_mul(x: torch.Tensor, act: Callable[[torch.Tensor], torch.Tensor] | N
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
-    out = nt_linear(x.reshape(-1, x.shape[-1]), weight, bias)
-    return out.view(*x.shape[:-1], weight.shape[0])
+    return nt_linear(x, weight, bias)
 
 
 def embedding(layer: torch.nn.Module, input_: torch.Tensor) -> torch.Tensor:

@@ -14,14 +14,19 @@ def _k_contiguous(t: torch.Tensor) -> torch.Tensor:
 
 
 def linear(input: torch.Tensor, other: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
-    """out = input @ other^T (+ bias) for input [M, K] and other [N, K] (vLLM layout)."""
-    x = _k_contiguous(input)
+    """out = input @ other^T (+ bias) for input [..., K] and other [N, K] (vLLM layout)."""
+    if input.is_contiguous() and other.is_contiguous() and (bias is None or bias.is_contiguous()):
+        # the op views [..., K] as rows and realigns an unaligned x itself
+        out = input.new_empty((*input.shape[:-1], other.shape[0]))
+        ops().linear(out, input, other, bias, None)
+        return out
+    x = _k_contiguous(input.reshape(-1, input.shape[-1]))
     w = _k_contiguous(other)
     out = torch.empty((x.shape[0], w.shape[0]), dtype=x.dtype, device=x.device)
     if bias is not None and not bias.is_contiguous():
         bias = bias.contiguous()
     ops().linear(out, x, w, bias, None)
-    return out
+    return out.view(*input.shape[:-1], w.shape[0])
 
 
 def matmul(lhs: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:

@@ -21,6 +21,10 @@ def _weight(weight: torch.Tensor | None, hidden: int, dtype: torch.dtype) -> tor
     return w.contiguous()
 
 
+def _weight_ok(weight: torch.Tensor | None, x: torch.Tensor) -> bool:
+    return weight is None or (weight.dtype == x.dtype and weight.dim() == 1 and weight.is_contiguous())
+
+
 def rms_norm(input, normalized_shape, weight=None, eps=None):
     """y = input * rsqrt(mean(input^2, -1) + eps) * weight over the last dimension.
 
@@ -33,6 +37,11 @@ def rms_norm(input, normalized_shape, weight=None, eps=None):
         raise NotImplementedError("ntb200.rms_norm normalises over the last dimension only")
     if eps is None:
         eps = torch.finfo(input.dtype).eps
+    if input.is_contiguous() and _weight_ok(weight, input):
+        # the op takes any-rank row layouts itself
+        out = torch.empty_like(input)
+        ops().rms_norm(out, input, weight, float(eps))
+        return out
     hidden = input.shape[-1]
     x = _rows(input, hidden)
     out = torch.empty_like(x)
@@ -44,14 +53,18 @@ def fused_add_rms_norm(x, residual, weight, eps, inplace=False):
     """Returns (rms_norm(x + residual), x + residual) with the sum and statistics in
     fp32, as vLLM's fused_add_rms_norm (vllm/ir/ops/layernorm.py:40-62).
 
-    With ``inplace=True`` the sum is written into ``residual`` (vLLM's CUDA convention:
-    the caller no longer needs the old residual), which saves a copy; otherwise neither
-    input is modified."""
+    With ``inplace=True`` both inputs are overwritten, vLLM's CUDA convention
+    (vllm/_custom_ops.py fused_add_rms_norm): the normalised rows go into ``x`` and the
+    sum into ``residual``, and those two tensors are returned; no memory is allocated.
+    Otherwise neither input is modified."""
+    if inplace and x.is_contiguous() and residual.is_contiguous() and _weight_ok(weight, x):
+        ops().fused_add_rms_norm(x, residual, x, weight, float(eps))
+        return x, residual
     hidden = x.shape[-1]
     x2 = _rows(x, hidden)
     res = residual.reshape(-1, hidden)
     if not inplace or res.stride(-1) != 1:
         res = res.clone(memory_format=torch.contiguous_format)
-    out = torch.empty_like(x2)
+    out = x2 if inplace and x2.data_ptr() == x.data_ptr() else torch.empty_like(x2)
     ops().fused_add_rms_norm(out, res, x2, _weight(weight, hidden, x.dtype), float(eps))
     return out.view(x.shape), res.view(residual.shape)

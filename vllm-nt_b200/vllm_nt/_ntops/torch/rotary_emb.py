@@ -27,15 +27,20 @@ def rotary_embedding(
     """Rotates the first ``rotary_dim`` dims of every head of query (and key) in place,
     NeoX style, with cos/sin = cos_sin_cache[positions] split in halves.  The cache must
     already have query's dtype (vLLM's _match_cos_sin_cache_dtype)."""
+    rot = cos_sin_cache.shape[-1] if rotary_dim is None else rotary_dim
+    if (positions.is_contiguous() and cos_sin_cache.is_contiguous() and query.dim() == 2
+            and query.stride(-1) == 1 and (key is None or (key.dim() == 2 and key.stride(-1) == 1))):
+        # vLLM's [tokens, heads * head_size] slices of the qkv projection go straight in
+        ops().rotary_embedding_neox(positions, query, key, cos_sin_cache, head_size, rot)
+        return query, key
     positions = positions.reshape(-1)
     if not positions.is_contiguous():
         positions = positions.contiguous()
     n = positions.shape[0]
-    rot = cos_sin_cache.shape[-1] if rotary_dim is None else int(rotary_dim)
     cache = cos_sin_cache if cos_sin_cache.stride(-1) == 1 else cos_sin_cache.contiguous()
     q = _heads(query, n, head_size)
     k = _heads(key, n, head_size) if key is not None else None
-    ops().rotary_embedding_neox(positions, q, k, cache, int(head_size), rot)
+    ops().rotary_embedding_neox(positions, q, k, cache, int(head_size), int(rot))
     return query, key
 
 
