@@ -212,15 +212,15 @@ def test_attention_hooks_decode_only_and_kv_store(monkeypatch):
     monkeypatch.setattr(patching, "_attn_impl_supported", lambda *a: True)
     monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
 
-    def fake_decode(out, q, kc, vc, seq, table, scale, msl):
-        calls["decode"] = (tuple(out.shape), tuple(q.shape), tuple(kc.shape), tuple(seq.shape), scale, msl)
-        out.fill_(1.0)
+    def fake_decode(out, q, kv, seq, table, n, scale, msl):
+        calls["decode"] = (tuple(out.shape), tuple(q.shape), tuple(kv.shape), tuple(seq.shape), n, scale, msl)
+        out[:n].fill_(1.0)
 
-    def fake_store(key, value, kc, vc, slots):
-        calls["store"] = (tuple(key.shape), tuple(kc.shape), tuple(slots.shape))
+    def fake_store(key, value, kv, slots):
+        calls["store"] = (tuple(key.shape), tuple(kv.shape), tuple(slots.shape))
 
-    monkeypatch.setattr(patching, "nt_paged_decode", fake_decode)
-    monkeypatch.setattr(patching, "store_kv_cache", fake_store)
+    monkeypatch.setattr(patching, "paged_attention_decode_flash", fake_decode)
+    monkeypatch.setattr(patching, "store_kv_cache_flash", fake_store)
     orig = lambda *a, **k: "flash-attn"  # noqa: E731
     fwd = patching._build_flash_attn_forward(orig)
     upd = patching._build_flash_attn_kv_update(orig)
@@ -232,12 +232,12 @@ def test_attention_hooks_decode_only_and_kv_store(monkeypatch):
                            query_start_loc=torch.tensor([0, 1, 2, 3]), seq_lens=torch.tensor([4, 9, 40]),
                            block_table=torch.zeros(3, 3, dtype=torch.int32))
     assert fwd(impl, None, q, q, q, kv, meta, out) is out
-    assert calls["decode"] == ((3, 4, 128), (3, 4, 128), (6, 16, 2, 128), (3,), 0.1, 40)
+    assert calls["decode"] == ((5, 4 * 128), (5, 4, 128), (2, 6, 16, 2, 128), (3,), 3, 0.1, 40)
     assert out[:3].eq(1).all() and out[3:].eq(0).all()
     prefill = SimpleNamespace(**{**vars(meta), "max_query_len": 7})
     assert fwd(impl, None, q, q, q, kv, prefill, out) == "flash-attn"
     upd(impl, None, torch.zeros(5, 2, 128), torch.zeros(5, 2, 128), kv, torch.tensor([1, 2, 3]))
-    assert calls["store"] == ((5, 2, 128), (6, 16, 2, 128), (3,))
+    assert calls["store"] == ((5, 2, 128), (2, 6, 16, 2, 128), (3,))
     ops = patching.get_usage_summary()["operators"]
     assert ops["PagedAttentionDecode"]["hits"] == 1 and ops["StoreKVCache"]["hits"] == 1
 

@@ -261,6 +261,45 @@ int64_t decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num
       num_seqs, num_q_heads, num_kv_heads, head_size, block_size, max_seq_len));
 }
 
+// vLLM FlashAttention layout entry points: the KV cache is one [2, blocks, block_size,
+// kv_heads, head_size] tensor and activations are padded to the batch's token capacity;
+// only the first num_tokens rows are real.  Views, slicing and the split-K workspace (from
+// the caching allocator, on the current stream) are made here, so that a hook makes one
+// call per layer.
+void decode_flash_layout(at::Tensor output, const at::Tensor& query, const at::Tensor& kv_cache,
+                         const at::Tensor& seq_lens, const at::Tensor& block_table, int64_t num_tokens,
+                         double scale, int64_t max_seq_len) {
+  require_cuda(kv_cache, "kv_cache");
+  TORCH_CHECK(kv_cache.dim() == 5 && kv_cache.size(0) == 2,
+              "ntb200.decode_flash_layout: kv_cache must be [2, blocks, block_size, kv_heads, head_size]");
+  const at::Tensor kc = kv_cache.select(0, 0), vc = kv_cache.select(0, 1);
+  const int64_t head = kc.size(3);
+  at::Tensor q = query.dim() == 2 ? query.view({query.size(0), -1, head}) : query;
+  at::Tensor o = output.dim() == 2 ? output.view({output.size(0), -1, head}) : output;
+  TORCH_CHECK(num_tokens >= 0 && num_tokens <= q.size(0) && num_tokens <= o.size(0),
+              "ntb200.decode_flash_layout: num_tokens exceeds the activations");
+  q = q.narrow(0, 0, num_tokens);
+  o = o.narrow(0, 0, num_tokens);
+  const int64_t cap = block_table.size(1) * kc.size(1);
+  const int64_t msl = max_seq_len <= 0 || max_seq_len > cap ? cap : max_seq_len;
+  const size_t need = ntb200_paged_attention_decode_workspace_size(num_tokens, q.size(1), kc.size(2), head,
+                                                                   kc.size(1), msl);
+  at::Tensor ws = at::empty({static_cast<int64_t>(need > 256 ? need : 256)}, query.options().dtype(at::kByte));
+  paged_attention_decode(o, q, kc, vc, seq_lens, block_table, scale, msl, ws);
+}
+
+void store_flash_layout(const at::Tensor& key, const at::Tensor& value, at::Tensor kv_cache,
+                        const at::Tensor& slot_mapping) {
+  require_cuda(kv_cache, "kv_cache");
+  TORCH_CHECK(kv_cache.dim() == 5 && kv_cache.size(0) == 2,
+              "ntb200.store_flash_layout: kv_cache must be [2, blocks, block_size, kv_heads, head_size]");
+  at::Tensor kc = kv_cache.select(0, 0), vc = kv_cache.select(0, 1);
+  const int64_t heads = kc.size(2), head = kc.size(3);
+  const at::Tensor k = key.dim() == 2 ? key.view({key.size(0), heads, head}) : key;
+  const at::Tensor v = value.dim() == 2 ? value.view({value.size(0), heads, head}) : value;
+  reshape_and_cache(k, v, kc, vc, slot_mapping.dim() == 1 ? slot_mapping : slot_mapping.reshape({-1}));
+}
+
 // x [..., K] (rows must collapse; a TMA operand needs a 16-byte aligned base and a row
 // stride that is a multiple of 8 elements, otherwise x is copied once into a fresh tensor)
 void linear(at::Tensor out, const at::Tensor& x_in, const at::Tensor& weight,
@@ -326,6 +365,10 @@ TORCH_LIBRARY(ntb200, m) {
       "decode_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads, int head_size, "
       "int block_size, int max_seq_len) -> int",
       &decode_workspace_size);
+  m.def(
+      "decode_flash_layout(Tensor(a!) output, Tensor query, Tensor kv_cache, Tensor seq_lens, "
+      "Tensor block_table, int num_tokens, float scale, int max_seq_len) -> ()");
+  m.def("store_flash_layout(Tensor key, Tensor value, Tensor(a!) kv_cache, Tensor slot_mapping) -> ()");
   m.def("linear(Tensor(a!) out, Tensor x, Tensor weight, Tensor? bias, Tensor(b!)? workspace) -> ()");
   m.def("linear_workspace_size(int m, int n, int k) -> int", &linear_workspace_size);
 }
@@ -338,5 +381,7 @@ TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("reshape_and_cache", &reshape_and_cache);
   m.impl("embedding", &embedding);
   m.impl("paged_attention_decode", &paged_attention_decode);
+  m.impl("decode_flash_layout", &decode_flash_layout);
+  m.impl("store_flash_layout", &store_flash_layout);
   m.impl("linear", &linear);
 }

@@ -105,7 +105,13 @@ def backend_enabled(op_name: str) -> bool:
 
 
 def _entry(op_name: str, backend: str) -> BackendStats:
-    return _STATS.setdefault(op_name, {}).setdefault(backend, BackendStats())
+    per_op = _STATS.get(op_name)
+    if per_op is None:
+        per_op = _STATS[op_name] = {}
+    entry = per_op.get(backend)
+    if entry is None:
+        entry = per_op[backend] = BackendStats()
+    return entry
 
 
 def record_attempt(op_name: str, backend: str) -> None:
@@ -139,11 +145,10 @@ def reset_backend_state() -> None:
     _disabled_version += 1
 
 
-def _dispatch(op_name: str, backend: str, thunks: dict[str, Thunk | None], original: Thunk) -> Any:
+def _dispatch(op_name: str, backend: str, fn: Thunk | None, original: Thunk) -> Any:
     if backend == "original":
         record_fallback(op_name, backend)
         return original()
-    fn = thunks.get(backend)
     if fn is None:
         raise RuntimeError(f"{op_name} has no adapter for backend {backend}")
     record_attempt(op_name, backend)
@@ -151,6 +156,19 @@ def _dispatch(op_name: str, backend: str, thunks: dict[str, Thunk | None], origi
     if backend.startswith("infinicore"):
         record_hit(op_name, backend)
     return result
+
+
+def _adapter(backend: str, original: Thunk, infinicore: Thunk | None, ninetoothed: Thunk | None,
+             infinicore_flash_attn: Thunk | None, kernels: Thunk | None) -> Thunk | None:
+    if backend == "b200":
+        return kernels
+    if backend == "ninetoothed":
+        return ninetoothed if ninetoothed is not None else kernels
+    if backend == "infinicore":
+        return infinicore
+    if backend == "infinicore-flash-attn":
+        return infinicore_flash_attn
+    return original if backend == "original" else None
 
 
 def route(
@@ -167,16 +185,11 @@ def route(
     ``call_b200`` defaults to ``call_ninetoothed``: in this build both names select the
     sm_100a kernels."""
     kernels = call_b200 if call_b200 is not None else call_ninetoothed
-    thunks = {
-        "infinicore": call_infinicore,
-        "infinicore-flash-attn": call_infinicore_flash_attn,
-        "ninetoothed": call_ninetoothed if call_ninetoothed is not None else kernels,
-        "b200": kernels,
-    }
     cfg = config_for(op_name)
     backend = cfg.fallback_backend if op_name in disabled_ops() else cfg.backend
     try:
-        return _dispatch(op_name, backend, thunks, call_original)
+        fn = _adapter(backend, call_original, call_infinicore, call_ninetoothed, call_infinicore_flash_attn, kernels)
+        return _dispatch(op_name, backend, fn, call_original)
     except Exception as exc:
         record_failure(op_name, backend)
         if cfg.disable_backend_on_first_failure and backend != "original":
@@ -190,4 +203,6 @@ def route(
             )
         if cfg.fallback_backend == backend:
             raise
-        return _dispatch(op_name, cfg.fallback_backend, thunks, call_original)
+        fb = cfg.fallback_backend
+        fn = _adapter(fb, call_original, call_infinicore, call_ninetoothed, call_infinicore_flash_attn, kernels)
+        return _dispatch(op_name, fb, fn, call_original)

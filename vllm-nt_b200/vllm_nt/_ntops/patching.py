@@ -50,8 +50,10 @@ from vllm_nt._ntops.oot_support import (
     linear,
     norm,
     nt_paged_decode,
+    paged_attention_decode_flash,
     rope,
     store_kv_cache,
+    store_kv_cache_flash,
 )
 
 logger = logging.getLogger("vllm_nt")
@@ -379,6 +381,22 @@ def _build_rotary_forward(original: object) -> object:
 
 
 def _attn_impl_supported(impl: Any, dtype: torch.dtype, kv_cache: torch.Tensor) -> bool:
+    """Whether the B200 attention kernels serve this FlashAttentionImpl and cache.  The
+    answer is kept on the impl (its configuration is fixed after construction), keyed by
+    the dtypes and the cache shape, so the per-layer check is one attribute read."""
+    key = (dtype, kv_cache.dtype, kv_cache.shape)
+    cached = getattr(impl, "_ntb200_supported", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    ok = _attn_impl_check(impl, dtype, kv_cache)
+    try:
+        impl._ntb200_supported = (key, ok)
+    except AttributeError:
+        pass
+    return ok
+
+
+def _attn_impl_check(impl: Any, dtype: torch.dtype, kv_cache: torch.Tensor) -> bool:
     attn_type = getattr(impl, "attn_type", "decoder")
     sliding = getattr(impl, "sliding_window", None)
     return (
@@ -412,8 +430,7 @@ def _build_flash_attn_kv_update(original: object) -> object:
 
         def kernels():
             _record_hit("StoreKVCache", key)
-            key_cache, value_cache = kv_cache.unbind(0)
-            store_kv_cache(key, value, key_cache, value_cache, slot_mapping)
+            store_kv_cache_flash(key, value, kv_cache, slot_mapping)
 
         return _route("StoreKVCache", call, kernels)
 
@@ -451,17 +468,8 @@ def _build_flash_attn_forward(original: object) -> object:
 
         def kernels():
             _record_hit("PagedAttentionDecode", query)
-            key_cache, value_cache = kv_cache.unbind(0)
-            out = output[:n].view(n, self.num_heads, self.head_size)
-            nt_paged_decode(
-                out,
-                query[:n],
-                key_cache,
-                value_cache,
-                meta.seq_lens[:n],
-                meta.block_table[:n],
-                self.scale,
-                int(meta.max_seq_len),
+            paged_attention_decode_flash(
+                output, query, kv_cache, meta.seq_lens, meta.block_table, n, self.scale, int(meta.max_seq_len)
             )
             return output
 

@@ -35,6 +35,8 @@ def _register_fakes() -> None:
         "reshape_and_cache",
         "embedding",
         "paged_attention_decode",
+        "decode_flash_layout",
+        "store_flash_layout",
         "linear",
     ):
         torch.library.register_fake(f"ntb200::{name}")(nothing)
