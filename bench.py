@@ -412,17 +412,23 @@ def per_op_table(dev, peaks) -> dict:
 
 def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
     """Row-parallel projections (o_proj K=4096, down K=14336; N=4096) on n ranks: each rank
-    multiplies its K-shard, the partial outputs are summed across ranks with an NCCL
-    all-reduce.  Times (max over ranks, CUDA events, median of 5): the local GEMM, the
-    all-reduce, the two back to back, and an M-chunked pipeline in which the all-reduce of
-    chunk i (on a second stream) overlaps the GEMM of chunk i+1."""
+    multiplies its K-shard and the partial outputs are summed across ranks.  Times (max
+    over ranks, CUDA events, median of 5 runs of 10 back-to-back calls each, per call):
+    - NCCL: the local GEMM, the all-reduce, the two back to back, and an M-chunked
+      pipeline in which the all-reduce of chunk i (on a second stream) overlaps the GEMM of
+      chunk i+1;
+    - peer: the GEMM writing into this rank's peer-mapped slot followed by this library's
+      one-shot all-reduce over NVLink (vllm_nt._ntops.tp.PeerAllReduce), no NCCL."""
     from vllm_nt._ntops import sharding
     from vllm_nt._ntops.torch._ext import ops
+    from vllm_nt._ntops.tp import PeerAllReduce
 
     o = ops()
     g = torch.Generator(device=dev).manual_seed(50 + rank)
     comm = torch.cuda.Stream(device=dev)
+    par = PeerAllReduce(None, capacity=8192 * 4096, device=dev)
     res = {}
+    inner = 10
 
     def timed(fn, reps=5) -> float:
         ts = []
@@ -431,10 +437,11 @@ def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            fn()
+            for _ in range(inner):
+                fn()
             e1.record()
             torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1))
+            ts.append(e0.elapsed_time(e1) / inner)
         t = torch.tensor([statistics.median(ts)], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
@@ -471,20 +478,36 @@ def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
                         dist.all_reduce(out[sl])
                 main.wait_stream(comm)
 
-            for f in (gemm, allreduce, serial, pipelined):
+            out_peer = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
+
+            def peer():
+                part = par.partial_view((m, 4096), torch.bfloat16)
+                o.linear(part, x, w, None, None)
+                par.reduce(part, out_peer)
+
+            for f in (gemm, allreduce, serial, pipelined, peer):
                 f()
             torch.cuda.synchronize()
             t_gemm, t_ar, t_serial, t_pipe = timed(gemm), timed(allreduce), timed(serial), timed(pipelined)
+            t_peer = timed(peer)
+            # the two paths agree (both sum this rank's bf16 partial with its peers')
+            serial()
+            peer()
+            torch.cuda.synchronize()
+            agree = float((out.float() - out_peer.float()).abs().max().item())
             res[f"{name} M={m}"] = {
                 "gemm_us": round(t_gemm * 1e3, 1),
                 "allreduce_us": round(t_ar * 1e3, 1),
                 "serial_us": round(t_serial * 1e3, 1),
                 "chunked_overlap_us": round(t_pipe * 1e3, 1),
+                "peer_gemm_allreduce_us": round(t_peer * 1e3, 1),
+                "peer_vs_nccl_max_abs_diff": round(agree, 4),
                 "allreduce_bytes": m * 4096 * 2,
                 "chunks": chunks,
             }
-            del x, out
+            del x, out, out_peer
         del w
+    del par
     return res
 
 

@@ -188,6 +188,28 @@ int ntb200_linear(void* out, const void* x, const void* weight, const void* bias
                   int64_t out_row_stride, void* workspace, size_t workspace_bytes, int dtype,
                   void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * One-shot all-reduce over peer memory for the row-parallel projections of tensor
+ * parallelism (o_proj and down under TP): replaces the NCCL all-reduce that vLLM's
+ * RowParallelLinear issues after the GEMM (vllm:model_executor/layers/linear.py
+ * RowParallelLinear.forward -> tensor_model_parallel_all_reduce); the reference plugin has
+ * no counterpart of its own (it leaves the collective to vLLM).
+ * Every rank owns a buffer of ntb200_allreduce_buffer_size(capacity, 2) bytes that all
+ * ranks can address (e.g. torch symmetric memory), zero-filled once; capacity is the
+ * largest element count it will reduce.  For call number `epoch` (1, 2, 3, ... the same
+ * sequence on every rank) the rank's partial, numel <= capacity bf16/f16 elements, must be
+ * in its own buffer at ntb200_allreduce_slot_offset(capacity, 2, epoch) before the call
+ * (the GEMM writes it there).  peer_buffers is a DEVICE array of
+ * world_size buffer addresses (index = rank, this rank's own included).  out receives the
+ * elementwise sum (fp32 accumulation).  At most 8 ranks.  Waits for peers are bounded
+ * (NTB200_DEVERR_WAIT_TIMEOUT after ~2 s).  Not for CUDA-graph capture: the epoch is an
+ * argument. */
+size_t ntb200_allreduce_buffer_size(int64_t capacity, int elem_bytes);
+int64_t ntb200_allreduce_slot_offset(int64_t capacity, int elem_bytes, uint32_t epoch);
+int ntb200_allreduce_oneshot(void* out, const uint64_t* peer_buffers, int64_t numel,
+                             int64_t capacity, int rank, int world_size, uint32_t epoch, int dtype,
+                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

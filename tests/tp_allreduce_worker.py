@@ -1,0 +1,65 @@
+"""One rank of the peer-memory all-reduce test (run by tests/test_tp_allreduce_gpu.py
+under torch.distributed.run, one process per GPU).
+
+Each rank computes a row-parallel projection through PeerAllReduce.linear (our GEMM into
+the peer-mapped slot, then ntb200_allreduce_oneshot) and compares it with the same
+partials summed by NCCL: bf16 partial per rank, bias on rank 0, as vLLM's
+RowParallelLinear does.  Exits non-zero on a mismatch or a device-side timeout."""
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path[:0] = [str(ROOT), str(ROOT / "vllm-nt_b200")]
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def main() -> int:
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    from vllm_nt._ntops import capi
+    from vllm_nt._ntops.tp import PeerAllReduce
+
+    stream = torch.cuda.current_stream().cuda_stream
+    capi.read_device_error(stream)
+    par = PeerAllReduce(None, capacity=256 * 4096)
+    # decode and odd shapes; the same (M, N) twice in a row and alternating slots
+    cases = [(1, 4096, 4096), (256, 14336, 4096), (37, 520, 264), (256, 4096, 4096), (3, 64, 8), (256, 4096, 4096),
+             (128, 14336, 4096)]
+    bad = []
+    for step, (m, k_total, n) in enumerate(cases):
+        k = max(8, k_total // world)
+        g = torch.Generator().manual_seed(1000 * step + rank)
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+        w = (0.05 * torch.randn(n, k, generator=g)).to(torch.bfloat16).to(dev)
+        b = torch.randn(n, generator=torch.Generator().manual_seed(step)).to(torch.bfloat16).to(dev)
+        out = par.linear(x, w, b)
+        ref = x.float() @ w.float().t()
+        if rank == 0:
+            ref = ref + b.float()
+        ref = ref.to(torch.bfloat16).float()
+        dist.all_reduce(ref)
+        torch.cuda.synchronize()
+        try:
+            torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+        except AssertionError as exc:
+            bad.append(f"case {step} {(m, k, n)}: {str(exc).splitlines()[0]}")
+    word = capi.read_device_error(stream)
+    if word:
+        bad.append(f"device error word {word}")
+    flags = torch.tensor([len(bad)], device=dev)
+    dist.all_reduce(flags)
+    print(f"rank {rank}/{world}: {'OK' if not bad else bad}", flush=True)
+    del par
+    dist.destroy_process_group()
+    return 0 if int(flags.item()) == 0 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

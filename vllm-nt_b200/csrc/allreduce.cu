@@ -1,0 +1,144 @@
+// One-shot all-reduce over peer memory, for the row-parallel projections of tensor
+// parallelism (o_proj, down): every rank's GEMM writes its partial [M, N] into its own
+// peer-mapped buffer, then each rank reads all W partials over NVLink, sums them in fp32
+// and writes the result into local memory.  No NCCL on this path.
+//
+// Buffer layout (identical on every rank; the caller maps the peers' buffers), for a
+// buffer made for at most `capacity` elements, slot = capacity elements rounded to 256 B:
+//   [0, kFlagBytes)            flags: kMaxBlocks x kMaxRanks uint32, written by peers
+//   [kFlagBytes, +slot)        partial slot 0  (used when epoch is even)
+//   [kFlagBytes + slot, +slot) partial slot 1  (epoch odd)
+// The two slots let a rank's next GEMM write while a slower peer may still read this
+// call's partial: a rank cannot reach the call after next before every peer has entered
+// the next call's barrier, i.e. finished reading this one.
+//
+// Synchronisation: CTA b of every rank stores `epoch` into flag [b][rank] of every peer
+// (release, system scope) and waits, bounded, until its own flags [b][r] reach `epoch`
+// for all r.  Epochs increase by one per call and are the same on all ranks, so flags
+// never need clearing.  A wait that runs out sets NTB200_DEVERR_WAIT_TIMEOUT and the CTA
+// goes on (its output is then not the sum), so no kernel can hang on a missing peer.
+#include "common.cuh"
+
+namespace ntb200 {
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxBlocks = 256;
+constexpr int64_t kFlagBytes = int64_t(kMaxRanks) * kMaxBlocks * 4;  // 8 KiB
+constexpr int kThreads = 512;
+
+int64_t slot_bytes(int64_t numel, int elem_bytes) { return ceil_div(numel * elem_bytes, 256) * 256; }
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// epoch a - epoch b as a signed distance, so that the comparison survives wrap-around
+__device__ __forceinline__ bool reached(uint32_t seen, uint32_t epoch) {
+  return static_cast<int32_t>(seen - epoch) >= 0;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(T* __restrict__ out,
+                                                                     const uint64_t* __restrict__ peers,
+                                                                     int64_t numel, int64_t slot_off,
+                                                                     int rank, int world, uint32_t epoch,
+                                                                     unsigned int* err) {
+  const int b = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();  // the partial of this rank (written by the kernel before) is complete
+  if (threadIdx.x < world) {
+    __threadfence_system();
+    char* peer = reinterpret_cast<char*>(peers[threadIdx.x]);
+    st_release_sys(reinterpret_cast<uint32_t*>(peer) + b * kMaxRanks + rank, epoch);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(peers[rank]) + b * kMaxRanks + threadIdx.x;
+    if (!reached(ld_acquire_sys(mine), epoch)) {
+      const uint64_t t0 = global_timer_ns();
+      for (uint32_t it = 1;; ++it) {
+        if (reached(ld_acquire_sys(mine), epoch)) break;
+        if ((it & 255u) == 0 && global_timer_ns() - t0 > kWaitTimeoutNs) {
+          raise_device_error(err, NTB200_DEVERR_WAIT_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // sum: 16-byte units (8 bf16/f16), all W loads of a unit in flight before the adds
+  constexpr int kVec = 16 / sizeof(T);
+  const int64_t units = numel / kVec;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t u = int64_t(b) * blockDim.x + threadIdx.x; u < units; u += stride) {
+    uint4 raw[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world)
+        raw[r] = __ldcv(reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(peers[r]) + slot_off) + u);
+    float acc[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r < world) {
+        const T* v = reinterpret_cast<const T*>(&raw[r]);
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) acc[j] += Elem<T>::to_f(v[j]);
+      }
+    }
+    store_f<T, kVec>(out + u * kVec, acc);
+  }
+  // ragged tail
+  for (int64_t e = units * kVec + int64_t(b) * blockDim.x + threadIdx.x; e < numel; e += stride) {
+    float acc = 0.f;
+    for (int r = 0; r < world; ++r)
+      acc += Elem<T>::to_f(reinterpret_cast<const T*>(reinterpret_cast<const char*>(peers[r]) + slot_off)[e]);
+    out[e] = Elem<T>::from_f(acc);
+  }
+}
+
+}  // namespace
+}  // namespace ntb200
+
+extern "C" size_t ntb200_allreduce_buffer_size(int64_t capacity, int elem_bytes) {
+  if (capacity < 0 || elem_bytes <= 0) return 0;
+  return static_cast<size_t>(ntb200::kFlagBytes + 2 * ntb200::slot_bytes(capacity, elem_bytes));
+}
+
+extern "C" int64_t ntb200_allreduce_slot_offset(int64_t capacity, int elem_bytes, uint32_t epoch) {
+  if (capacity < 0 || elem_bytes <= 0) return -1;
+  return ntb200::kFlagBytes + int64_t(epoch & 1u) * ntb200::slot_bytes(capacity, elem_bytes);
+}
+
+extern "C" int ntb200_allreduce_oneshot(void* out, const uint64_t* peer_buffers, int64_t numel,
+                                        int64_t capacity, int rank, int world_size, uint32_t epoch,
+                                        int dtype, void* stream) {
+  using namespace ntb200;
+  if (numel < 0 || numel > capacity) return fail(NTB200_ERR_INVALID_ARGUMENT, "allreduce: numel outside [0, capacity]");
+  if (world_size < 1 || world_size > kMaxRanks || rank < 0 || rank >= world_size)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "allreduce: rank %d of %d (at most %d ranks)", rank, world_size,
+                kMaxRanks);
+  if (numel == 0) return NTB200_OK;
+  if (out == nullptr || peer_buffers == nullptr) return fail(NTB200_ERR_INVALID_ARGUMENT, "allreduce: null pointer");
+  if (!aligned16(out)) return fail(NTB200_ERR_MISALIGNED, "allreduce: out must be 16-byte aligned");
+  if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
+    return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "allreduce: dtype %d (bf16/f16 only)", dtype);
+  const int64_t slot_off = ntb200_allreduce_slot_offset(capacity, 2, epoch);
+  const int64_t units = ceil_div(numel, 8);
+  int64_t grid = ceil_div(units, kThreads);
+  const int64_t cap = num_sms() < kMaxBlocks ? num_sms() : kMaxBlocks;
+  if (grid > cap) grid = cap;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == NTB200_DTYPE_BF16)
+    return launch_kernel("allreduce_oneshot", allreduce_oneshot_kernel<__nv_bfloat16>, dim3(unsigned(grid)),
+                         dim3(kThreads), 0, s, static_cast<__nv_bfloat16*>(out), peer_buffers, numel, slot_off,
+                         rank, world_size, epoch, device_error_word());
+  return launch_kernel("allreduce_oneshot", allreduce_oneshot_kernel<__half>, dim3(unsigned(grid)), dim3(kThreads),
+                       0, s, static_cast<__half*>(out), peer_buffers, numel, slot_off, rank, world_size, epoch,
+                       device_error_word());
+}

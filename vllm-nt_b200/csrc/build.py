@@ -39,6 +39,7 @@ KERNEL_SOURCES = (
     "paged_decode.cu",
     "paged_decode_noalloc.cu",
     "gemm.cu",
+    "allreduce.cu",
 )
 SHARED_HEADERS = (CSRC / "common.cuh", INCLUDE / "ntb200.h", Path(__file__).resolve())
 

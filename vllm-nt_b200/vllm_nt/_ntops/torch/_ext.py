@@ -38,6 +38,7 @@ def _register_fakes() -> None:
         "decode_flash_layout",
         "store_flash_layout",
         "linear",
+        "allreduce_oneshot",
     ):
         torch.library.register_fake(f"ntb200::{name}")(nothing)
 

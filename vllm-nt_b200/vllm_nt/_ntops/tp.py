@@ -1,0 +1,69 @@
+"""Row-parallel projection with its all-reduce over peer memory (tensor parallelism).
+
+Under TP, vLLM's RowParallelLinear (o_proj, down) computes a partial product on every
+rank and sums the partials with an NCCL all-reduce
+(vllm:model_executor/layers/linear.py, RowParallelLinear.forward ->
+tensor_model_parallel_all_reduce).  Here the GEMM writes its partial straight into this
+rank's peer-mapped buffer (torch symmetric memory), and ``ntb200_allreduce_oneshot``
+reads every rank's partial over NVLink and sums it: two kernels of this library back to
+back (the second launched as a programmatic dependent of the first), no NCCL call.
+
+Every rank must make the same sequence of calls (the epoch counts them); a call is not
+capturable in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from vllm_nt._ntops.torch._ext import ops
+
+
+class PeerAllReduce:
+    """A peer-mapped buffer for ``capacity`` bf16/f16 elements per rank and the epoch of
+    the calls made through it."""
+
+    def __init__(self, group: dist.ProcessGroup | None, capacity: int, device: torch.device | None = None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.capacity = int(capacity)
+        nbytes = int(ops().allreduce_buffer_size(self.capacity, 2))
+        self.buffer = symm_mem.empty(nbytes, dtype=torch.uint8, device=self.device)
+        self.buffer.zero_()
+        torch.cuda.synchronize(self.device)
+        self.handle = symm_mem.rendezvous(self.buffer, self.group)
+        self.rank = int(self.handle.rank)
+        self.world_size = int(self.handle.world_size)
+        self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=self.device)
+        self.epoch = 0
+        # no rank may write a peer's flags before every rank has cleared its own buffer
+        dist.barrier(group=self.group)
+
+    def partial_view(self, shape: tuple[int, ...], dtype: torch.dtype) -> torch.Tensor:
+        """This rank's slot for the next call, viewed as ``shape``: the GEMM writes its
+        partial product here."""
+        numel = 1
+        for d in shape:
+            numel *= int(d)
+        if numel > self.capacity:
+            raise ValueError(f"{numel} elements exceed the buffer's capacity of {self.capacity}")
+        off = int(ops().allreduce_slot_offset(self.capacity, 2, self.epoch + 1))
+        return self.buffer[off : off + 2 * numel].view(dtype).view(shape)
+
+    def reduce(self, partial: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Sums ``partial`` (a view from :meth:`partial_view`, filled) over all ranks."""
+        self.epoch += 1
+        if out is None:
+            out = torch.empty(partial.shape, dtype=partial.dtype, device=partial.device)
+        ops().allreduce_oneshot(out, self.peers, self.capacity, self.rank, self.world_size, self.epoch)
+        return out
+
+    def linear(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+        """sum over ranks of x_r @ weight_r^T, plus bias once (on rank 0, as vLLM's
+        RowParallelLinear adds it before the reduction)."""
+        partial = self.partial_view((*x.shape[:-1], weight.shape[0]), x.dtype)
+        ops().linear(partial, x, weight, bias if self.rank == 0 else None, None)
+        return self.reduce(partial)
