@@ -189,6 +189,19 @@ int ntb200_linear(void* out, const void* x, const void* weight, const void* bias
                   void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Fused gate_up projection + SiluAndMul:
+ *   out[M, I] = silu(x . W[0:I]^T) * (x . W[I:2I]^T)
+ * for vLLM's merged gate_up weight W [2I, K] (MergedColumnParallelLinear, gate rows then
+ * up rows), with the rounding points of the unfused pair (each half rounded to the dtype,
+ * silu(gate) rounded before the multiply), so the result equals ntb200_linear followed by
+ * ntb200_silu_and_mul.  Replaces the MatMul hook on gate_up_proj followed by the
+ * SiluAndMul hook (vllm_nt/_ntops/patching.py:2630-2658 and 291-316); the reference has
+ * no fused form.  dtype BF16 or F16; K a multiple of 8, rows 16-byte aligned; no bias. */
+int ntb200_linear_silu_and_mul(void* out, const void* x, const void* weight, int64_t M, int64_t I,
+                               int64_t K, int64_t x_row_stride, int64_t weight_row_stride,
+                               int64_t out_row_stride, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * One-shot all-reduce over peer memory for the row-parallel projections of tensor
  * parallelism (o_proj and down under TP): replaces the NCCL all-reduce that vLLM's
  * RowParallelLinear issues after the GEMM (vllm:model_executor/layers/linear.py

@@ -143,3 +143,29 @@ def test_flash_attention_impl_hooks_store_and_decode(_b200_config):
     torch.testing.assert_close(out[:3].view(3, 32, 128).float().cpu(), ref, **TOL)
     assert not out[3].any()
     assert _hits(patching, "StoreKVCache") == 1 and _hits(patching, "PagedAttentionDecode") == 1
+
+
+def test_fused_mlp_hook_on_a_llama_shaped_mlp(_b200_config, vllm_ctx):
+    """The LlamaMLP.forward replacement: fused gate_up + SiluAndMul kernel, then the
+    down projection through its own hook."""
+    from vllm.model_executor.layers.activation import SiluAndMul
+    from vllm.model_executor.layers.linear import UnquantizedLinearMethod
+
+    patching = _b200_config
+    g = seeded(9)
+    wgu = (0.02 * torch.randn(2 * 512, 1024, generator=g)).to(torch.bfloat16)
+    wd = (0.02 * torch.randn(1024, 512, generator=g)).to(torch.bfloat16)
+    x = torch.randn(24, 1024, generator=g).to(torch.bfloat16)
+    down = SimpleNamespace(weight=torch.nn.Parameter(wd.cuda(), requires_grad=False))
+    mlp = SimpleNamespace(
+        gate_up_proj=SimpleNamespace(weight=wgu.cuda(), quant_method=UnquantizedLinearMethod(), bias=None,
+                                     gather_output=False),
+        act_fn=SiluAndMul(),
+        down_proj=lambda h: (UnquantizedLinearMethod().apply(down, h), None),
+    )
+    fwd = patching._build_mlp_forward(lambda *a: pytest.fail("fused MLP fell back to vLLM"))
+    out = fwd(mlp, x.cuda())
+    h = oracle.silu_and_mul(oracle.linear(x, wgu).to(torch.bfloat16))
+    ref = oracle.linear(h.to(torch.bfloat16), wd)
+    torch.testing.assert_close(out.float().cpu(), ref.float(), **TOL)
+    assert _hits(patching, "GateUpSiluAndMul") == 1 and _hits(patching, "MatMul") == 1

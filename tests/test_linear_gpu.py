@@ -122,3 +122,33 @@ def test_linear_rejects_unaligned_and_fp32():
     with pytest.raises(capi.NtB200Error) as e:
         capi.call("ntb200_linear", ptr(out), ptr(x), ptr(w), None, 4, 8, 12, 12, 12, 8, None, 0, 0, stream())
     assert e.value.status == -2
+
+
+@pytest.mark.parametrize("m,k,i", [(1, 4096, 14336), (16, 4096, 14336), (256, 4096, 14336), (200, 72, 300),
+                                   (1000, 4096, 1792), (2048, 4096, 14336), (2300, 136, 520)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_linear_silu_and_mul_fused_capi(m, k, i, dtype):
+    """Fused gate_up + SiluAndMul over every path (swap-AB M <= 256, single CTA, CTA pairs)
+    against the oracle's unfused pair; I not a multiple of the tile covers the tail."""
+    x, w, _ = _inputs(m, k, 2 * i, seed=m + k + i)
+    xd, wd = x.to(dtype).cuda(), w.to(dtype).cuda()
+    out = torch.full((m, i), 5.0, dtype=dtype, device="cuda")
+    capi.call("ntb200_linear_silu_and_mul", ptr(out), ptr(xd), ptr(wd), m, i, k, k, k, i, dtype_code(dtype), stream())
+    torch.cuda.synchronize()
+    ref = oracle.silu_and_mul(oracle.linear(x.to(dtype), w.to(dtype)).to(dtype))
+    torch.testing.assert_close(out.float().cpu(), ref.float(), rtol=TOL, atol=TOL)
+
+
+def test_linear_silu_and_mul_matches_unfused_pair_exactly():
+    """The fused epilogue rounds where the unfused pair does: with the same GEMM
+    decomposition (CTA pairs at M = 2048) the two agree bit for bit."""
+    from vllm_nt._ntops.torch.linear import linear, linear_silu_and_mul
+    from vllm_nt._ntops.torch.silu import silu_and_mul
+
+    dev = cuda_device()
+    gd = torch.Generator(device=dev).manual_seed(77)
+    x = torch.randn(2048, 4096, generator=gd, device=dev, dtype=torch.bfloat16)
+    w = 0.02 * torch.randn(2 * 1024, 4096, generator=gd, device=dev, dtype=torch.bfloat16)
+    fused = linear_silu_and_mul(x, w)
+    unfused = silu_and_mul(linear(x, w))
+    assert torch.equal(fused, unfused)

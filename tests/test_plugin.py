@@ -249,3 +249,44 @@ def test_no_vendor_imports_in_package():
     bad = re.compile(r"^\s*(import|from)\s+(torch_mlu|torch_musa|vllm_mlu|vllm_musa|vllm_metax|ninetoothed|triton|infinicore)\b", re.M)
     offenders = [str(p) for p in pkg.rglob("*.py") if bad.search(p.read_text())]
     assert offenders == []
+
+
+def test_fused_mlp_hook_routes_gate_up_silu_and_down(monkeypatch):
+    """LlamaMLP.forward replacement: one fused gate_up+SiluAndMul call, then down_proj; an
+    ineligible MLP (quantised gate_up) runs vLLM's forward."""
+    from vllm.model_executor.layers.activation import SiluAndMul
+    from vllm.model_executor.layers.linear import UnquantizedLinearMethod
+
+    monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
+    calls = {}
+
+    def fake_fused(x, w):
+        calls["fused"] = (tuple(x.shape), tuple(w.shape))
+        return torch.ones(x.shape[0], w.shape[0] // 2, dtype=x.dtype)
+
+    monkeypatch.setattr(patching, "gate_up_silu_and_mul", fake_fused)
+    fwd = patching._build_mlp_forward(lambda self, x: "vllm")
+    w = torch.zeros(2 * 24, 16, dtype=torch.bfloat16)
+    down = lambda h: (h.sum(-1, keepdim=True), None)  # noqa: E731
+    mlp = SimpleNamespace(gate_up_proj=SimpleNamespace(weight=w, quant_method=UnquantizedLinearMethod(), bias=None,
+                                                       gather_output=False),
+                          act_fn=object.__new__(SiluAndMul), down_proj=down)
+    x = torch.zeros(3, 16, dtype=torch.bfloat16)
+    out = fwd(mlp, x)
+    assert calls["fused"] == ((3, 16), (48, 16)) and out.shape == (3, 1) and float(out[0, 0]) == 24.0
+    assert patching.get_usage_summary()["operators"]["GateUpSiluAndMul"]["hits"] == 1
+    mlp.gate_up_proj.quant_method = object()
+    assert fwd(mlp, x) == "vllm"
+
+
+def test_fused_mlp_patch_is_opt_in(monkeypatch):
+    """Configs written for the reference (no GateUpSiluAndMul key) leave LlamaMLP alone."""
+    spec = next(s for s in patching._FUNCTION_PATCH_SPECS if s.patch_id == "GateUpSiluAndMul")
+    config.reset_backend_config_cache()
+    assert patching._function_patch_enabled(spec)  # all-b200.yaml names it
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/hybrid-default.yaml"))
+    config.reset_backend_config_cache()
+    try:
+        assert not patching._function_patch_enabled(spec)
+    finally:
+        config.reset_backend_config_cache()

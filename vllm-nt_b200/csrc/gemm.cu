@@ -126,8 +126,43 @@ struct GemmParams {
   int64_t out_stride;
   int num_m_blocks, num_n_blocks;
   int group_m;  // M blocks per raster group (num_m_blocks: plain M-fastest order)
+  int64_t n_half;  // SwiGLU variants: output columns I; W rows [0, I) gate, [I, 2I) up
   unsigned int* err;
 };
+
+// silu(gate) * up for the fused gate_up epilogue, with the rounding points of vLLM's
+// unfused pair (the GEMM rounds both halves to T, SiluAndMul rounds silu(gate) to T
+// before the multiply, the store rounds the product) and the same silu expression as
+// silu_and_mul.cu, so the fused and unfused results are identical.
+template <typename T>
+__device__ __forceinline__ float swiglu(float gate_acc, float up_acc) {
+  const float g = Elem<T>::round(gate_acc), u = Elem<T>::round(up_acc);
+  return Elem<T>::round(g / (1.0f + expf(-g))) * u;
+}
+
+// Writes 32 consecutive output columns c0.. of one row (bias added when given; columns at
+// or past ncols are dropped), with 16-byte stores when the segment is whole and aligned.
+template <typename T>
+__device__ __forceinline__ void store_row32(T* orow, int64_t c0, int64_t ncols, float (&v)[32], const T* bias) {
+  if (bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (c0 + i < ncols) v[i] += Elem<T>::to_f(bias[c0 + i]);
+  }
+  if (c0 + 32 <= ncols && ((reinterpret_cast<uintptr_t>(orow + c0) & 15u) == 0)) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = v[q * 8 + i];
+      store_f<T, 8>(orow + c0 + q * 8, w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (c0 + i < ncols) orow[c0 + i] = Elem<T>::from_f(v[i]);
+  }
+}
 
 // Tile order: groups of `group_m` M blocks, M fastest inside a group, then N, then the next
 // group.  With group_m = num_m_blocks this is plain M-fastest order (x stays L2-resident
@@ -143,7 +178,9 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmParams& p, int& 
   nb = r / rows;
 }
 
-template <typename T, int BN_>
+// SWIGLU: out[:, j] = silu(x.W[j]) * x.W[I + j] (W = vLLM's merged gate_up weight); a
+// tile's B operand is BN/2 gate rows followed by the BN/2 matching up rows.
+template <typename T, int BN_, bool SWIGLU = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
     const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
     const GemmParams p) {
@@ -217,7 +254,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
           const uint32_t a_dst = ring + s * kStageBytes;
           const uint32_t b_dst = a_dst + kATileBytes;
           tma_load_2d(a_dst, &a_map, kb * BK, mb * BM, smem_u32(&full[s]));
-          tma_load_2d(b_dst, &b_map, kb * BK, nb * BN, smem_u32(&full[s]));
+          if constexpr (SWIGLU) {
+            tma_load_2d(b_dst, &b_map, kb * BK, nb * (BN / 2), smem_u32(&full[s]));
+            tma_load_2d(b_dst + (BN / 2) * BK * 2, &b_map, kb * BK, static_cast<int>(p.n_half) + nb * (BN / 2),
+                        smem_u32(&full[s]));
+          } else {
+            tma_load_2d(b_dst, &b_map, kb * BK, nb * BN, smem_u32(&full[s]));
+          }
         }
       }
       // drain the copies still in flight
@@ -277,34 +320,38 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tcgen05_kernel(
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       const int64_t row = int64_t(mb) * BM + row_in_tile;
-      const int64_t col0 = int64_t(nb) * BN;
       T* orow = out + row * p.out_stride;
+      const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + acc * kAccStride;
+      if constexpr (SWIGLU) {
+        const int64_t col0 = int64_t(nb) * (BN / 2);
 #pragma unroll 1
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
-        tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + acc * kAccStride + chunk * 32, r);
-        const int64_t c0 = col0 + chunk * 32;
-        if (row < p.M && c0 < p.N) {
-        float v[32];
+        for (int chunk = 0; chunk < BN / 64; ++chunk) {
+          uint32_t g[32], u[32];
+          __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
+          tmem_ld_32(taddr + chunk * 32, g);
+          tmem_ld_32(taddr + BN / 2 + chunk * 32, u);
+          const int64_t c0 = col0 + chunk * 32;
+          if (row < p.M && c0 < p.n_half) {
+            float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-        if (bias != nullptr) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c0 + i < p.N) v[i] += Elem<T>::to_f(bias[c0 + i]);
-        }
-        if (c0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(orow + c0) & 15u) == 0)) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float w[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) w[i] = v[q * 8 + i];
-            store_f<T, 8>(orow + c0 + q * 8, w);
+            for (int i = 0; i < 32; ++i) v[i] = swiglu<T>(__uint_as_float(g[i]), __uint_as_float(u[i]));
+            store_row32<T>(orow, c0, p.n_half, v, nullptr);
           }
-        } else {
-          for (int i = 0; i < 32 && c0 + i < p.N; ++i) orow[c0 + i] = Elem<T>::from_f(v[i]);
         }
+      } else {
+        const int64_t col0 = int64_t(nb) * BN;
+#pragma unroll 1
+        for (int chunk = 0; chunk < BN / 32; ++chunk) {
+          uint32_t r[32];
+          __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
+          tmem_ld_32(taddr + chunk * 32, r);
+          const int64_t c0 = col0 + chunk * 32;
+          if (row < p.M && c0 < p.N) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            store_row32<T>(orow, c0, p.N, v, bias);
+          }
         }
       }
       tc_fence_before();
@@ -411,7 +458,10 @@ __device__ __forceinline__ void pair_cluster_sync() {
       "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-template <typename T>
+// SWIGLU: the even CTA stages gate rows [128*nb, +128) and the odd CTA the matching up
+// rows [I + 128*nb, +128), so accumulator columns [0, 128) hold x.gate and [128, 256)
+// x.up for the same 128 output columns.
+template <typename T, bool SWIGLU = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
     const __grid_constant__ CUtensorMap a_map, const __grid_constant__ CUtensorMap b_map,
     const GemmParams p) {
@@ -476,7 +526,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
         int mb, nb;
         tile_coords(tile, p, mb, nb);
         const int arow = mb * C::kTile + static_cast<int>(rank) * C::kHalf;
-        const int brow = nb * C::kTile + static_cast<int>(rank) * C::kHalf;
+        const int brow = SWIGLU ? (rank == 0 ? nb * C::kHalf : static_cast<int>(p.n_half) + nb * C::kHalf)
+                                : nb * C::kTile + static_cast<int>(rank) * C::kHalf;
         for (int kb = 0; kb < k_steps; ++kb, ++it) {
           const uint32_t s = it % kStages;
           if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, p.err)) {
@@ -547,33 +598,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
       int mb, nb;
       tile_coords(tile, p, mb, nb);
       const int64_t row = int64_t(mb) * C::kTile + row_in_tile;
-      const int64_t col0 = int64_t(nb) * C::kTile;
       T* orow = out + row * p.out_stride;
+      const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + acc * C::kTile;
+      if constexpr (SWIGLU) {
+        const int64_t col0 = int64_t(nb) * C::kHalf;
 #pragma unroll 1
-      for (int chunk = 0; chunk < C::kTile / 32; ++chunk) {
-        uint32_t r[32];
-        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
-        tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + acc * C::kTile + chunk * 32, r);
-        const int64_t c0 = col0 + chunk * 32;
-        if (row < p.M && c0 < p.N) {
-          float v[32];
+        for (int chunk = 0; chunk < C::kHalf / 32; ++chunk) {
+          uint32_t g[32], u[32];
+          __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
+          tmem_ld_32(taddr + chunk * 32, g);
+          tmem_ld_32(taddr + C::kHalf + chunk * 32, u);
+          const int64_t c0 = col0 + chunk * 32;
+          if (row < p.M && c0 < p.n_half) {
+            float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          if (bias != nullptr) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c0 + i < p.N) v[i] += Elem<T>::to_f(bias[c0 + i]);
+            for (int i = 0; i < 32; ++i) v[i] = swiglu<T>(__uint_as_float(g[i]), __uint_as_float(u[i]));
+            store_row32<T>(orow, c0, p.n_half, v, nullptr);
           }
-          if (c0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(orow + c0) & 15u) == 0)) {
+        }
+      } else {
+        const int64_t col0 = int64_t(nb) * C::kTile;
+#pragma unroll 1
+        for (int chunk = 0; chunk < C::kTile / 32; ++chunk) {
+          uint32_t r[32];
+          __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp issues it together
+          tmem_ld_32(taddr + chunk * 32, r);
+          const int64_t c0 = col0 + chunk * 32;
+          if (row < p.M && c0 < p.N) {
+            float v[32];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float w[8];
-#pragma unroll
-              for (int i = 0; i < 8; ++i) w[i] = v[q * 8 + i];
-              store_f<T, 8>(orow + c0 + q * 8, w);
-            }
-          } else {
-            for (int i = 0; i < 32 && c0 + i < p.N; ++i) orow[c0 + i] = Elem<T>::from_f(v[i]);
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            store_row32<T>(orow, c0, p.N, v, bias);
           }
         }
       }
@@ -674,6 +729,7 @@ struct SmallParams {
   int splits;
   int k_steps_per_split;
   int k_steps_total;
+  int64_t n_half;  // SwiGLU variant: output columns I (up rows start at row I of W)
   unsigned int* err;
 };
 
@@ -708,7 +764,10 @@ __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t local_addr, uint32_t r
   return v;
 }
 
-template <typename T, int MP, int NT, bool BIG>
+// SWIGLU (NT = 2, no split): the CTA's two weight tiles are gate rows [128*g, +128) and
+// the matching up rows [I + 128*g, +128), so each epilogue thread holds x.gate and x.up
+// of the same output column.
+template <typename T, int MP, int NT, bool BIG, bool SWIGLU = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
     const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
     const SmallParams p) {
@@ -768,8 +827,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
         const int kx = (kb0 + it) * BK;
         // weight tiles past N (the last group of an odd tile count) are TMA zero-fill
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
-          tma_load_2d(stage + t * kATileBytes, &w_map, kx, (tile0 + t) * BM, smem_u32(&full[s]));
+        for (int t = 0; t < NT; ++t) {
+          const int wrow = SWIGLU ? (t == 0 ? 0 : static_cast<int>(p.n_half)) + (tile0 / NT) * BM : (tile0 + t) * BM;
+          tma_load_2d(stage + t * kATileBytes, &w_map, kx, wrow, smem_u32(&full[s]));
+        }
         tma_load_2d(stage + NT * kATileBytes, &x_map, kx, 0, smem_u32(&full[s]));
         issued = it + 1;
       }
@@ -809,7 +870,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
     tc_fence_after();
   }
 
-  if (p.splits == 1) {
+  if (SWIGLU) {
+    // no split (the host plans none): silu(gate) * up straight from TMEM
+    if (epilogue) {
+      const int64_t n = int64_t(tile0 / NT) * BM + n_local;
+#pragma unroll 1
+      for (int c = 0; c < MP / 16; ++c) {
+        uint32_t g[16], u[16];
+        __syncwarp();
+        tmem_ld_16(tmem_base + (uint32_t(quad * 32) << 16) + c * 16, g);
+        tmem_ld_16(tmem_base + (uint32_t(quad * 32) << 16) + MP + c * 16, u);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int64_t m = c * 16 + i;
+          if (m < p.M && n < p.n_half)
+            out[m * p.out_stride + n] =
+                Elem<T>::from_f(acc_ok ? swiglu<T>(__uint_as_float(g[i]), __uint_as_float(u[i])) : 0.f);
+        }
+      }
+      tc_fence_before();
+    }
+  } else if (p.splits == 1) {
     // no split: TMEM -> registers -> global (lane = output column, column = token row)
     if (epilogue) {
 #pragma unroll 1
@@ -895,11 +976,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
   }
 }
 
-template <typename T, int MP, int NT, bool BIG>
+template <typename T, int MP, int NT, bool BIG, bool SWIGLU = false>
 int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, cudaStream_t s,
                  int attr_slot) {
   using L = SmallSmem<MP, NT, BIG>;
-  const void* fn = reinterpret_cast<const void*>(gemm_small_m_kernel<T, MP, NT, BIG>);
+  const void* fn = reinterpret_cast<const void*>(gemm_small_m_kernel<T, MP, NT, BIG, SWIGLU>);
   int st = ensure_smem_attribute(fn, L::kDynamicBytes, attr_slot);
   if (st != NTB200_OK) return st;
   const int groups = (prm.n_tiles + NT - 1) / NT;
@@ -916,7 +997,7 @@ int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallPa
   set_pdl_attribute(attr[1]);
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_m_kernel<T, MP, NT, BIG>, wmap, xmap, prm);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_m_kernel<T, MP, NT, BIG, SWIGLU>, wmap, xmap, prm);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(NTB200_ERR_CUDA, "linear (small M): launch failed: %s", cudaGetErrorString(e));
@@ -1024,16 +1105,18 @@ int pick_tile_width(int64_t M, int64_t N, int sms) {
   return 256;
 }
 
-template <int BNV>
+// SWIGLU: `N` is the weight's row count 2I and out has I columns (see the kernel).
+template <int BNV, bool SWIGLU = false>
 int launch_large(void* out, const void* x, const void* weight, const void* bias, int64_t M, int64_t N,
                  int64_t K, int64_t xs, int64_t ws, int64_t os, bool bf16, cudaStream_t s) {
   using C = GemmCfg<BNV>;
-  const int64_t mblocks = ceil_div(M, BM), nblocks = ceil_div(N, BNV);
+  const int64_t n_out = SWIGLU ? N / 2 : N;
+  const int64_t mblocks = ceil_div(M, BM), nblocks = ceil_div(n_out, SWIGLU ? BNV / 2 : BNV);
   if (mblocks * nblocks > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
   CUtensorMap amap, bmap;
   int st = make_kmajor_map(&amap, x, bf16, M, K, xs, BM);
   if (st != NTB200_OK) return st;
-  st = make_kmajor_map(&bmap, weight, bf16, N, K, ws, BNV);
+  st = make_kmajor_map(&bmap, weight, bf16, N, K, ws, SWIGLU ? BNV / 2 : BNV);
   if (st != NTB200_OK) return st;
   GemmParams prm;
   prm.out = out;
@@ -1045,26 +1128,31 @@ int launch_large(void* out, const void* x, const void* weight, const void* bias,
   prm.num_m_blocks = static_cast<int>(mblocks);
   prm.num_n_blocks = static_cast<int>(nblocks);
   prm.group_m = raster_group(M, K, mblocks);
+  prm.n_half = n_out;
   prm.err = device_error_word();
   const int64_t tiles = mblocks * nblocks;
   const int grid = static_cast<int>(tiles < num_sms() ? tiles : num_sms());
-  const int slot = 32 + (BNV == 256 ? 0 : (BNV == 192 ? 2 : 4)) + (bf16 ? 0 : 1);
+  const int slot = (SWIGLU ? 42 : 32) + (BNV == 256 ? 0 : (BNV == 192 ? 2 : 4)) + (bf16 ? 0 : 1);
   if (bf16) {
-    st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__nv_bfloat16, BNV>), C::kDynamicBytes, slot);
+    st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__nv_bfloat16, BNV, SWIGLU>),
+                               C::kDynamicBytes, slot);
     if (st != NTB200_OK) return st;
-    return launch_kernel("linear", gemm_tcgen05_kernel<__nv_bfloat16, BNV>, dim3(grid), dim3(kThreads),
+    return launch_kernel("linear", gemm_tcgen05_kernel<__nv_bfloat16, BNV, SWIGLU>, dim3(grid), dim3(kThreads),
                          C::kDynamicBytes, s, amap, bmap, prm);
   }
-  st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__half, BNV>), C::kDynamicBytes, slot);
+  st = ensure_smem_attribute(reinterpret_cast<const void*>(gemm_tcgen05_kernel<__half, BNV, SWIGLU>),
+                             C::kDynamicBytes, slot);
   if (st != NTB200_OK) return st;
-  return launch_kernel("linear", gemm_tcgen05_kernel<__half, BNV>, dim3(grid), dim3(kThreads),
+  return launch_kernel("linear", gemm_tcgen05_kernel<__half, BNV, SWIGLU>, dim3(grid), dim3(kThreads),
                        C::kDynamicBytes, s, amap, bmap, prm);
 }
 
+template <bool SWIGLU = false>
 int launch_pair(void* out, const void* x, const void* weight, const void* bias, int64_t M, int64_t N,
                 int64_t K, int64_t xs, int64_t ws, int64_t os, bool bf16, cudaStream_t s) {
   using C = PairCfg;
-  const int64_t mblocks = ceil_div(M, C::kTile), nblocks = ceil_div(N, C::kTile);
+  const int64_t n_out = SWIGLU ? N / 2 : N;
+  const int64_t mblocks = ceil_div(M, C::kTile), nblocks = ceil_div(n_out, SWIGLU ? C::kHalf : C::kTile);
   if (mblocks * nblocks > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
   CUtensorMap amap, bmap;
   int st = make_kmajor_map(&amap, x, bf16, M, K, xs, C::kHalf);
@@ -1081,10 +1169,11 @@ int launch_pair(void* out, const void* x, const void* weight, const void* bias, 
   prm.num_m_blocks = static_cast<int>(mblocks);
   prm.num_n_blocks = static_cast<int>(nblocks);
   prm.group_m = raster_group(M, K, mblocks);
+  prm.n_half = n_out;
   prm.err = device_error_word();
-  const int slot = bf16 ? 40 : 41;
-  const void* fn = bf16 ? reinterpret_cast<const void*>(gemm_pair_kernel<__nv_bfloat16>)
-                        : reinterpret_cast<const void*>(gemm_pair_kernel<__half>);
+  const int slot = (SWIGLU ? 48 : 40) + (bf16 ? 0 : 1);
+  const void* fn = bf16 ? reinterpret_cast<const void*>(gemm_pair_kernel<__nv_bfloat16, SWIGLU>)
+                        : reinterpret_cast<const void*>(gemm_pair_kernel<__half, SWIGLU>);
   st = ensure_smem_attribute(fn, C::kDynamicBytes, slot);
   if (st != NTB200_OK) return st;
   int pairs = resident_clusters(fn, C::kDynamicBytes, 2, slot);
@@ -1104,8 +1193,8 @@ int launch_pair(void* out, const void* x, const void* weight, const void* bias, 
   set_pdl_attribute(attr[1]);
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, gemm_pair_kernel<__nv_bfloat16>, amap, bmap, prm)
-                             : cudaLaunchKernelEx(&cfg, gemm_pair_kernel<__half>, amap, bmap, prm);
+  const cudaError_t e = bf16 ? cudaLaunchKernelEx(&cfg, gemm_pair_kernel<__nv_bfloat16, SWIGLU>, amap, bmap, prm)
+                             : cudaLaunchKernelEx(&cfg, gemm_pair_kernel<__half, SWIGLU>, amap, bmap, prm);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(NTB200_ERR_CUDA, "linear (CTA pairs): launch failed: %s", cudaGetErrorString(e));
@@ -1113,8 +1202,86 @@ int launch_pair(void* out, const void* x, const void* weight, const void* bias, 
   return NTB200_OK;
 }
 
+// Fused gate_up + SiluAndMul for decode batches: one CTA per 128 output columns, both
+// weight tiles (gate and up) in it, no K split.
+template <typename T, int MP>
+int launch_small_swiglu(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, cudaStream_t s,
+                        int slot) {
+  const int64_t groups = (prm.n_tiles + 1) / 2;
+  if (groups <= num_sms()) return launch_small<T, MP, 2, true, true>(wmap, xmap, prm, s, slot + 1);
+  return launch_small<T, MP, 2, false, true>(wmap, xmap, prm, s, slot);
+}
+
+template <typename T>
+int dispatch_small_swiglu(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, int mp,
+                          cudaStream_t s, int slot_base) {
+  switch (mp) {
+    case 16: return launch_small_swiglu<T, 16>(wmap, xmap, prm, s, slot_base + 0);
+    case 32: return launch_small_swiglu<T, 32>(wmap, xmap, prm, s, slot_base + 2);
+    case 64: return launch_small_swiglu<T, 64>(wmap, xmap, prm, s, slot_base + 4);
+    case 128: return launch_small_swiglu<T, 128>(wmap, xmap, prm, s, slot_base + 6);
+    default: return launch_small_swiglu<T, 256>(wmap, xmap, prm, s, slot_base + 8);
+  }
+}
+
 }  // namespace
 }  // namespace ntb200
+
+extern "C" int ntb200_linear_silu_and_mul(void* out, const void* x, const void* weight, int64_t M,
+                                          int64_t I, int64_t K, int64_t x_row_stride,
+                                          int64_t weight_row_stride, int64_t out_row_stride, int dtype,
+                                          void* stream) {
+  using namespace ntb200;
+  if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
+    return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "linear_silu_and_mul: dtype %d (bf16/f16 only)", dtype);
+  if (M < 0 || I < 0 || K <= 0) return fail(NTB200_ERR_INVALID_ARGUMENT, "linear_silu_and_mul: bad shape");
+  if (M == 0 || I == 0) return NTB200_OK;
+  if (!out || !x || !weight) return fail(NTB200_ERR_INVALID_ARGUMENT, "linear_silu_and_mul: null pointer");
+  if (x_row_stride < K || weight_row_stride < K || out_row_stride < I)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "linear_silu_and_mul: row stride too small");
+  if (!aligned16(x) || !aligned16(weight) || x_row_stride % 8 != 0 || weight_row_stride % 8 != 0)
+    return fail(NTB200_ERR_MISALIGNED,
+                "linear_silu_and_mul: x/weight must be 16-byte aligned with row strides %% 8 == 0");
+  if (2 * I > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear_silu_and_mul: I too large");
+  const bool bf16 = dtype == NTB200_DTYPE_BF16;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M <= 256) {
+    const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    CUtensorMap wmap, xmap;
+    int st = make_kmajor_map(&wmap, weight, bf16, 2 * I, K, weight_row_stride, BM);
+    if (st != NTB200_OK) return st;
+    st = make_kmajor_map(&xmap, x, bf16, M, K, x_row_stride, mp);
+    if (st != NTB200_OK) return st;
+    SmallParams sp;
+    sp.out = out;
+    sp.bias = nullptr;
+    sp.M = M;
+    sp.N = 2 * I;
+    sp.out_stride = out_row_stride;
+    sp.n_tiles = static_cast<int>(2 * ceil_div(I, BM));
+    sp.splits = 1;
+    sp.k_steps_total = static_cast<int>(ceil_div(K, BK));
+    sp.k_steps_per_split = sp.k_steps_total;
+    sp.n_half = I;
+    sp.err = device_error_word();
+    return bf16 ? dispatch_small_swiglu<__nv_bfloat16>(wmap, xmap, sp, mp, s, 50)
+                : dispatch_small_swiglu<__half>(wmap, xmap, sp, mp, s, 60);
+  }
+  if (M >= kPairMinM)
+    return launch_pair<true>(out, x, weight, nullptr, M, 2 * I, K, x_row_stride, weight_row_stride, out_row_stride,
+                             bf16, s);
+  switch (pick_tile_width(M, 2 * I, num_sms())) {
+    case 128:
+      return launch_large<128, true>(out, x, weight, nullptr, M, 2 * I, K, x_row_stride, weight_row_stride,
+                                     out_row_stride, bf16, s);
+    case 192:
+      return launch_large<192, true>(out, x, weight, nullptr, M, 2 * I, K, x_row_stride, weight_row_stride,
+                                     out_row_stride, bf16, s);
+    default:
+      return launch_large<256, true>(out, x, weight, nullptr, M, 2 * I, K, x_row_stride, weight_row_stride,
+                                     out_row_stride, bf16, s);
+  }
+}
 
 extern "C" size_t ntb200_linear_workspace_size(int64_t M, int64_t N, int64_t K) {
   (void)M;
@@ -1174,6 +1341,7 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     sp.out_stride = out_row_stride;
     sp.n_tiles = static_cast<int>(n_tiles);
     sp.k_steps_total = ksteps;
+    sp.n_half = 0;
     sp.err = device_error_word();
     SmallParams sp_big = sp, sp_small = sp;
     sp_big.splits = splits_big;

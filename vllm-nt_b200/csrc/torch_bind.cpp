@@ -338,6 +338,27 @@ void linear(at::Tensor out, const at::Tensor& x_in, const at::Tensor& weight,
         "linear");
 }
 
+// out [..., I] = silu(x W[:I]^T) * (x W[I:]^T) for the merged gate_up weight [2I, K]
+void linear_silu_and_mul(at::Tensor out, const at::Tensor& x_in, const at::Tensor& weight) {
+  require_rows(weight, "weight");
+  at::Tensor x = x_in;
+  Rows xr = rows_of(x, "x");
+  if ((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15u) != 0 || xr.stride % 8 != 0) {
+    x = at::empty(x_in.sizes(), x_in.options());
+    x.copy_(x_in);
+    xr = rows_of(x, "x");
+  }
+  const Rows orr = rows_of(out, "out");
+  same_leading(x, out, "linear_silu_and_mul");
+  TORCH_CHECK(weight.size(1) == xr.cols && weight.size(0) % 2 == 0 && orr.cols == weight.size(0) / 2 &&
+                  weight.scalar_type() == x.scalar_type() && out.scalar_type() == x.scalar_type(),
+              "ntb200.linear_silu_and_mul: x [..., K], weight [2I, K], out [..., I] of one dtype");
+  c10::cuda::CUDAGuard guard(x.device());
+  check(ntb200_linear_silu_and_mul(out.data_ptr(), x.data_ptr(), weight.data_ptr(), xr.rows, orr.cols, xr.cols,
+                                   xr.stride, weight.stride(0), orr.stride, dtype_code(x), stream_of(x)),
+        "linear_silu_and_mul");
+}
+
 // out = sum over ranks of each rank's partial (see ntb200_allreduce_oneshot); peer_buffers
 // is an int64 CUDA tensor of the world's buffer addresses.
 void allreduce_oneshot(at::Tensor out, const at::Tensor& peer_buffers, int64_t capacity, int64_t rank,
@@ -396,6 +417,7 @@ TORCH_LIBRARY(ntb200, m) {
   m.def("store_flash_layout(Tensor key, Tensor value, Tensor(a!) kv_cache, Tensor slot_mapping) -> ()");
   m.def("linear(Tensor(a!) out, Tensor x, Tensor weight, Tensor? bias, Tensor(b!)? workspace) -> ()");
   m.def("linear_workspace_size(int m, int n, int k) -> int", &linear_workspace_size);
+  m.def("linear_silu_and_mul(Tensor(a!) out, Tensor x, Tensor weight) -> ()");
   m.def(
       "allreduce_oneshot(Tensor(a!) out, Tensor peer_buffers, int capacity, int rank, int world_size, "
       "int epoch) -> ()");
@@ -415,4 +437,5 @@ TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("store_flash_layout", &store_flash_layout);
   m.impl("linear", &linear);
   m.impl("allreduce_oneshot", &allreduce_oneshot);
+  m.impl("linear_silu_and_mul", &linear_silu_and_mul);
 }

@@ -19,6 +19,7 @@ from vllm_nt._ntops.torch.embedding import embedding as nt_embedding
 from vllm_nt._ntops.torch.kv_cache import get_kv_from_cache as nt_get_kv_from_cache
 from vllm_nt._ntops.torch.kv_cache import store_kvcache as nt_store_kvcache
 from vllm_nt._ntops.torch.linear import linear as nt_linear
+from vllm_nt._ntops.torch.linear import linear_silu_and_mul as nt_linear_silu_and_mul
 from vllm_nt._ntops.torch.rms_norm import fused_add_rms_norm as nt_fused_add_rms_norm
 from vllm_nt._ntops.torch.rms_norm import rms_norm as nt_rms_norm
 from vllm_nt._ntops.torch.rotary_emb import apply_rotary_emb as nt_apply_rotary_emb
@@ -58,6 +59,11 @@ def act_and_mul(x: torch.Tensor, act: Callable[[torch.Tensor], torch.Tensor] | N
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
     return nt_linear(x, weight, bias)
+
+
+def gate_up_silu_and_mul(x: torch.Tensor, gate_up_weight: torch.Tensor) -> torch.Tensor:
+    """silu(x W_gate^T) * (x W_up^T) for a merged [2I, K] gate_up weight in one kernel."""
+    return nt_linear_silu_and_mul(x, gate_up_weight)
 
 
 def embedding(layer: torch.nn.Module, input_: torch.Tensor) -> torch.Tensor:

@@ -47,6 +47,7 @@ from vllm_nt._ntops.oot_support import (
     OperatorStats,
     act_and_mul,
     embedding,
+    gate_up_silu_and_mul,
     linear,
     norm,
     nt_paged_decode,
@@ -133,10 +134,17 @@ def _operator_enabled(name: str) -> bool:
     return name not in _disabled_ops() and _nt_feature_enabled(_OPERATOR_FEATURES.get(name))
 
 
+# Patches this build adds beyond the reference's op set: applied only when the config
+# names the op with a kernel backend, so configs written for the reference run unchanged.
+_OPT_IN_PATCHES = frozenset({"GateUpSiluAndMul"})
+
+
 def _function_patch_enabled(spec: FunctionPatchSpec) -> bool:
     if spec.patch_id in _disabled_ops():
         return False
     key = canonical_op_name(spec.patch_id)
+    if key in _OPT_IN_PATCHES and not (key in load_backend_config().ops and backends.backend_enabled(key)):
+        return False
     if key == "UnifiedAttentionWithOutput":
         key = "PagedAttentionDecode"
     if spec.module_path.startswith("vllm") and key in load_backend_config().ops and not backends.backend_enabled(key):
@@ -478,6 +486,52 @@ def _build_flash_attn_forward(original: object) -> object:
     return _mark_function_patch(forward, "PagedAttentionDecode")
 
 
+def _fused_mlp_eligible(mlp: Any, x: torch.Tensor) -> bool:
+    """gate_up_proj -> SiluAndMul -> down_proj with an unquantised, bias-free merged
+    gate_up weight whose output stays on this rank (no gather)."""
+    gu = getattr(mlp, "gate_up_proj", None)
+    act = getattr(mlp, "act_fn", None)
+    w = getattr(gu, "weight", None)
+    return (
+        isinstance(act, activation.SiluAndMul)
+        and hasattr(mlp, "down_proj")
+        and isinstance(getattr(gu, "quant_method", None), UnquantizedLinearMethod)
+        and getattr(gu, "bias", None) is None
+        and not getattr(gu, "gather_output", False)
+        and isinstance(w, torch.Tensor)
+        and w.dim() == 2
+        and w.shape[0] % 2 == 0
+        and w.shape[1] % 8 == 0
+        and w.stride(-1) == 1
+        and x.is_cuda
+        and x.dtype in _HALF_TYPES
+        and w.dtype == x.dtype
+        and x.shape[-1] == w.shape[1]
+    )
+
+
+def _build_mlp_forward(original: object) -> object:
+    """Replacement for LlamaMLP.forward (and MLPs of the same shape): gate_up_proj and
+    SiluAndMul become one GEMM whose epilogue applies silu(gate) * up, so the [T, 2I]
+    gate_up activation is never written; down_proj runs through its own hook."""
+    if _is_function_patch(original, "GateUpSiluAndMul"):
+        return original
+    original_fn = cast(Callable[..., Any], original)
+
+    def forward(self, x):
+        if not _fused_mlp_eligible(self, x):
+            return original_fn(self, x)
+
+        def kernels():
+            _record_hit("GateUpSiluAndMul", x)
+            out, _ = self.down_proj(gate_up_silu_and_mul(x, self.gate_up_proj.weight))
+            return out
+
+        return _route("GateUpSiluAndMul", lambda: original_fn(self, x), kernels)
+
+    return _mark_function_patch(forward, "GateUpSiluAndMul")
+
+
 _OPERATOR_SPECS: dict[str, tuple[type, Callable[..., Any]]] = {
     "RMSNorm": (layernorm.RMSNorm, _nt_rms_norm_forward),
     "SiluAndMul": (activation.SiluAndMul, _nt_silu_and_mul_forward),
@@ -500,6 +554,7 @@ _OPERATOR_STATS: dict[str, OperatorStats] = {name: OperatorStats() for name in _
         "PagedAttentionPrefill",
         "PagedAttentionDecode",
         "StoreKVCache",
+        "GateUpSiluAndMul",
         "RoPE",
         "SDPA",
         "TopKTopP",
@@ -533,6 +588,13 @@ _FUNCTION_PATCH_SPECS: tuple[FunctionPatchSpec, ...] = (
     ),
     FunctionPatchSpec("StoreKVCache", _FA_MODULE, "do_kv_cache_update", "FlashAttentionImpl", False, _build_flash_attn_kv_update),
     FunctionPatchSpec("PagedAttentionDecode", _FA_MODULE, "forward", "FlashAttentionImpl", False, _build_flash_attn_forward),
+    *(
+        FunctionPatchSpec("GateUpSiluAndMul", mod, "forward", cls, False, _build_mlp_forward)
+        for mod, cls in (
+            ("vllm.model_executor.models.llama", "LlamaMLP"),
+            ("vllm.model_executor.models.qwen2", "Qwen2MLP"),
+        )
+    ),
 )
 
 _summary_printed = False

@@ -39,6 +39,7 @@ def _register_fakes() -> None:
         "store_flash_layout",
         "linear",
         "allreduce_oneshot",
+        "linear_silu_and_mul",
     ):
         torch.library.register_fake(f"ntb200::{name}")(nothing)
 

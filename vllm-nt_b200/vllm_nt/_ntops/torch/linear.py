@@ -29,6 +29,17 @@ def linear(input: torch.Tensor, other: torch.Tensor, bias: torch.Tensor | None =
     return out.view(*input.shape[:-1], w.shape[0])
 
 
+def linear_silu_and_mul(input: torch.Tensor, gate_up: torch.Tensor) -> torch.Tensor:
+    """silu(input @ gate_up[:I]^T) * (input @ gate_up[I:]^T) for vLLM's merged gate_up
+    weight [2I, K], as one GEMM whose epilogue applies SiluAndMul (no [.., 2I] tensor is
+    written)."""
+    w = _k_contiguous(gate_up)
+    out = input.new_empty((*input.shape[:-1], w.shape[0] // 2))
+    x = input if input.is_contiguous() else input.contiguous()
+    ops().linear_silu_and_mul(out, x, w)
+    return out
+
+
 def matmul(lhs: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
     """lhs [M, K] @ rhs [K, N]; rhs is transposed once into the [N, K] operand layout."""
     return linear(lhs, rhs.t().contiguous())
