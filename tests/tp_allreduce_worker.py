@@ -34,7 +34,7 @@ def main() -> int:
              (128, 14336, 4096)]
     bad = []
     for step, (m, k_total, n) in enumerate(cases):
-        k = max(8, k_total // world)
+        k = max(8, (k_total // world) // 8 * 8)
         g = torch.Generator().manual_seed(1000 * step + rank)
         x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
         w = (0.05 * torch.randn(n, k, generator=g)).to(torch.bfloat16).to(dev)
