@@ -44,12 +44,18 @@ def main() -> int:
         if rank == 0:
             ref = ref + b.float()
         ref = ref.to(torch.bfloat16).float()
+        # the partials are rounded to bf16 on each rank (ours by the GEMM, the reference by
+        # torch) and may differ by a rounding step where the fp32 sums differ in order; the
+        # error bound therefore scales with the partials' magnitudes, not the sum's
+        mag = ref.abs()
         dist.all_reduce(ref)
+        dist.all_reduce(mag)
         torch.cuda.synchronize()
-        try:
-            torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
-        except AssertionError as exc:
-            bad.append(f"case {step} {(m, k, n)}: {str(exc).splitlines()[0]}")
+        d = (out.float() - ref).abs()
+        off = int((d > 2e-2 + 2e-2 * mag).sum())
+        if off:
+            bad.append(f"case {step} {(m, k, n)} epoch {par.epoch}: max |diff| {d.max().item():.3g}, "
+                       f"{off} of {d.numel()} outside 0.02 + 0.02 * sum|partial|")
     word = capi.read_device_error(stream)
     if word:
         bad.append(f"device error word {word}")

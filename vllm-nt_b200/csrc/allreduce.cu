@@ -38,6 +38,23 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// Peer partials are read with strong (relaxed, system-scope) loads: a weak or
+// cache-volatile load may be served from a line this GPU cached in an earlier call, while
+// a strong load observes the value the peer's GEMM wrote before its release of the flag.
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint16_t ld_relaxed_sys_u16(const void* p) {
+  uint16_t v;
+  asm volatile("ld.relaxed.sys.global.u16 %0, [%1];" : "=h"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // epoch a - epoch b as a signed distance, so that the comparison survives wrap-around
 __device__ __forceinline__ bool reached(uint32_t seen, uint32_t epoch) {
   return static_cast<int32_t>(seen - epoch) >= 0;
@@ -79,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(T* __restri
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r)
       if (r < world)
-        raw[r] = __ldcv(reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(peers[r]) + slot_off) + u);
+        raw[r] = ld_relaxed_sys_v4(reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(peers[r]) + slot_off) + u);
     float acc[kVec];
 #pragma unroll
     for (int j = 0; j < kVec; ++j) acc[j] = 0.f;
@@ -96,8 +113,12 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(T* __restri
   // ragged tail
   for (int64_t e = units * kVec + int64_t(b) * blockDim.x + threadIdx.x; e < numel; e += stride) {
     float acc = 0.f;
-    for (int r = 0; r < world; ++r)
-      acc += Elem<T>::to_f(reinterpret_cast<const T*>(reinterpret_cast<const char*>(peers[r]) + slot_off)[e]);
+    for (int r = 0; r < world; ++r) {
+      const uint16_t bits = ld_relaxed_sys_u16(reinterpret_cast<const T*>(reinterpret_cast<const char*>(peers[r]) + slot_off) + e);
+      T v;
+      memcpy(&v, &bits, sizeof(v));
+      acc += Elem<T>::to_f(v);
+    }
     out[e] = Elem<T>::from_f(acc);
   }
 }
