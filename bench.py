@@ -413,7 +413,8 @@ def per_op_table(dev, peaks) -> dict:
 def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
     """Row-parallel projections (o_proj K=4096, down K=14336; N=4096) on n ranks: each rank
     multiplies its K-shard and the partial outputs are summed across ranks.  Times (max
-    over ranks, CUDA events, median of 5 runs of 10 back-to-back calls each, per call):
+    over ranks, CUDA events, median of 5 replays of a CUDA graph of 10 back-to-back calls,
+    per call; the two-stream chunked pipeline is timed eagerly):
     - NCCL: the local GEMM, the all-reduce, the two back to back, and an M-chunked
       pipeline in which the all-reduce of chunk i (on a second stream) overlaps the GEMM of
       chunk i+1;
@@ -430,18 +431,31 @@ def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
     res = {}
     inner = 10
 
-    def timed(fn, reps=5) -> float:
+    def timed(fn, reps=5, graph=True) -> float:
+        """Device time per call: `inner` calls captured in one CUDA graph (so that host
+        launch cost does not count), replayed after a barrier, median of `reps`."""
+        g_ = None
+        if graph:
+            torch.cuda.synchronize()
+            g_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_):
+                for _ in range(inner):
+                    fn()
         ts = []
         for _ in range(reps):
             dist.barrier()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            for _ in range(inner):
-                fn()
+            if g_ is not None:
+                g_.replay()
+            else:
+                for _ in range(inner):
+                    fn()
             e1.record()
             torch.cuda.synchronize()
             ts.append(e0.elapsed_time(e1) / inner)
+        del g_
         t = torch.tensor([statistics.median(ts)], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
@@ -488,7 +502,8 @@ def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
             for f in (gemm, allreduce, serial, pipelined, peer):
                 f()
             torch.cuda.synchronize()
-            t_gemm, t_ar, t_serial, t_pipe = timed(gemm), timed(allreduce), timed(serial), timed(pipelined)
+            t_gemm, t_ar, t_serial = timed(gemm), timed(allreduce), timed(serial)
+            t_pipe = timed(pipelined, graph=False)
             t_peer = timed(peer)
             # the two paths agree (both sum this rank's bf16 partial with its peers')
             serial()

@@ -209,19 +209,17 @@ int ntb200_linear_silu_and_mul(void* out, const void* x, const void* weight, int
  * no counterpart of its own (it leaves the collective to vLLM).
  * Every rank owns a buffer of ntb200_allreduce_buffer_size(capacity, 2) bytes that all
  * ranks can address (e.g. torch symmetric memory), zero-filled once; capacity is the
- * largest element count it will reduce.  For call number `epoch` (1, 2, 3, ... the same
- * sequence on every rank) the rank's partial, numel <= capacity bf16/f16 elements, must be
- * in its own buffer at ntb200_allreduce_slot_offset(capacity, 2, epoch) before the call
- * (the GEMM writes it there).  peer_buffers is a DEVICE array of
- * world_size buffer addresses (index = rank, this rank's own included).  out receives the
- * elementwise sum (fp32 accumulation).  At most 8 ranks.  Waits for peers are bounded
- * (NTB200_DEVERR_WAIT_TIMEOUT after ~2 s).  Not for CUDA-graph capture: the epoch is an
- * argument. */
+ * largest element count it will reduce.  Before a call, the rank's partial (numel bf16/f16
+ * elements) must be in its own buffer at byte ntb200_allreduce_data_offset() (the GEMM
+ * writes it there).  peer_buffers is a DEVICE array of world_size buffer addresses
+ * (index = rank, this rank's own included).  out receives the elementwise sum (fp32
+ * accumulation).  Every rank must make the same sequence of calls on its buffer; the call
+ * count lives in the buffer, so calls may be captured in a CUDA graph and replayed.  At
+ * most 8 ranks.  Waits for peers are bounded (NTB200_DEVERR_WAIT_TIMEOUT after ~2 s). */
 size_t ntb200_allreduce_buffer_size(int64_t capacity, int elem_bytes);
-int64_t ntb200_allreduce_slot_offset(int64_t capacity, int elem_bytes, uint32_t epoch);
-int ntb200_allreduce_oneshot(void* out, const uint64_t* peer_buffers, int64_t numel,
-                             int64_t capacity, int rank, int world_size, uint32_t epoch, int dtype,
-                             void* stream);
+int64_t ntb200_allreduce_data_offset(void);
+int ntb200_allreduce_oneshot(void* out, const uint64_t* peer_buffers, int64_t numel, int rank,
+                             int world_size, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

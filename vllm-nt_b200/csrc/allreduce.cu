@@ -3,20 +3,22 @@
 // peer-mapped buffer, then each rank reads all W partials over NVLink, sums them in fp32
 // and writes the result into local memory.  No NCCL on this path.
 //
-// Buffer layout (identical on every rank; the caller maps the peers' buffers), for a
-// buffer made for at most `capacity` elements, slot = capacity elements rounded to 256 B:
-//   [0, kFlagBytes)            flags: kMaxBlocks x kMaxRanks uint32, written by peers
-//   [kFlagBytes, +slot)        partial slot 0  (used when epoch is even)
-//   [kFlagBytes + slot, +slot) partial slot 1  (epoch odd)
-// The two slots let a rank's next GEMM write while a slower peer may still read this
-// call's partial: a rank cannot reach the call after next before every peer has entered
-// the next call's barrier, i.e. finished reading this one.
+// Buffer layout (identical on every rank; the caller maps the peers' buffers):
+//   [0, kFlagBytes)              flags: kMaxBlocks x kMaxRanks uint32, written by peers
+//   [kFlagBytes, kDataOffset)    header: the number of calls completed on this buffer and
+//                                a count of this call's finished CTAs
+//   [kDataOffset, + capacity)    this rank's partial (the GEMM writes it there)
 //
-// Synchronisation: CTA b of every rank stores `epoch` into flag [b][rank] of every peer
-// (release, system scope) and waits, bounded, until its own flags [b][r] reach `epoch`
-// for all r.  Epochs increase by one per call and are the same on all ranks, so flags
-// never need clearing.  A wait that runs out sets NTB200_DEVERR_WAIT_TIMEOUT and the CTA
-// goes on (its output is then not the sum), so no kernel can hang on a missing peer.
+// Synchronisation, per CTA b (the grid never exceeds the SM count, so all CTAs of a rank
+// are resident together): entry barrier -- CTA b of every rank stores 2e-1 into flag
+// [b][rank] of every peer (release, system scope) and waits, bounded, until its own flags
+// [b][r] reach 2e-1: every peer's partial is complete.  It then sums its share.  Exit
+// barrier -- the same with 2e: no peer reads this rank's partial any more, so the next
+// call's GEMM may overwrite it.  e is the call's number, read from the header; the last
+// CTA to finish advances it.  Flags only grow and are compared by signed distance, so
+// nothing is ever cleared, and everything lives on the device: a call can be captured in
+// a CUDA graph and replayed.  A wait that runs out sets NTB200_DEVERR_WAIT_TIMEOUT and the
+// CTA goes on (its output is then not the sum), so no kernel can hang on a missing peer.
 #include "common.cuh"
 
 namespace ntb200 {
@@ -25,9 +27,15 @@ namespace {
 constexpr int kMaxRanks = 8;
 constexpr int kMaxBlocks = 256;
 constexpr int64_t kFlagBytes = int64_t(kMaxRanks) * kMaxBlocks * 4;  // 8 KiB
+constexpr int64_t kDataOffset = kFlagBytes + 256;
 constexpr int kThreads = 512;
 
 int64_t slot_bytes(int64_t numel, int elem_bytes) { return ceil_div(numel * elem_bytes, 256) * 256; }
+
+struct Header {
+  uint32_t calls;     // calls completed on this buffer
+  uint32_t finished;  // CTAs of the running call that are done
+};
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -60,24 +68,18 @@ __device__ __forceinline__ bool reached(uint32_t seen, uint32_t epoch) {
   return static_cast<int32_t>(seen - epoch) >= 0;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(T* __restrict__ out,
-                                                                     const uint64_t* __restrict__ peers,
-                                                                     int64_t numel, int64_t slot_off,
-                                                                     int rank, int world, uint32_t epoch,
-                                                                     unsigned int* err) {
-  const int b = blockIdx.x;
-  pdl_trigger();
-  pdl_wait();  // the partial of this rank (written by the kernel before) is complete
+// CTA b's barrier with its counterparts on every rank: announce `value`, wait for theirs.
+__device__ __forceinline__ void peer_barrier(const uint64_t* peers, int b, int rank, int world, uint32_t value,
+                                             unsigned int* err) {
   if (threadIdx.x < world) {
     __threadfence_system();
     char* peer = reinterpret_cast<char*>(peers[threadIdx.x]);
-    st_release_sys(reinterpret_cast<uint32_t*>(peer) + b * kMaxRanks + rank, epoch);
+    st_release_sys(reinterpret_cast<uint32_t*>(peer) + b * kMaxRanks + rank, value);
     const uint32_t* mine = reinterpret_cast<const uint32_t*>(peers[rank]) + b * kMaxRanks + threadIdx.x;
-    if (!reached(ld_acquire_sys(mine), epoch)) {
+    if (!reached(ld_acquire_sys(mine), value)) {
       const uint64_t t0 = global_timer_ns();
       for (uint32_t it = 1;; ++it) {
-        if (reached(ld_acquire_sys(mine), epoch)) break;
+        if (reached(ld_acquire_sys(mine), value)) break;
         if ((it & 255u) == 0 && global_timer_ns() - t0 > kWaitTimeoutNs) {
           raise_device_error(err, NTB200_DEVERR_WAIT_TIMEOUT);
           break;
@@ -86,6 +88,22 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(T* __restri
     }
   }
   __syncthreads();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(T* __restrict__ out,
+                                                                     const uint64_t* __restrict__ peers,
+                                                                     int64_t numel, int rank, int world,
+                                                                     unsigned int* err) {
+  const int b = blockIdx.x;
+  __shared__ uint32_t s_call;
+  pdl_trigger();
+  pdl_wait();  // the partial of this rank (written by the kernel before) is complete
+  Header* hdr = reinterpret_cast<Header*>(reinterpret_cast<char*>(peers[rank]) + kFlagBytes);
+  if (threadIdx.x == 0) s_call = *reinterpret_cast<volatile uint32_t*>(&hdr->calls) + 1u;
+  __syncthreads();
+  const uint32_t call = s_call;
+  peer_barrier(peers, b, rank, world, 2u * call - 1u, err);
 
   // sum: 16-byte units (8 bf16/f16), all W loads of a unit in flight before the adds
   constexpr int kVec = 16 / sizeof(T);
@@ -96,7 +114,7 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(T* __restri
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r)
       if (r < world)
-        raw[r] = ld_relaxed_sys_v4(reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(peers[r]) + slot_off) + u);
+        raw[r] = ld_relaxed_sys_v4(reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(peers[r]) + kDataOffset) + u);
     float acc[kVec];
 #pragma unroll
     for (int j = 0; j < kVec; ++j) acc[j] = 0.f;
@@ -114,12 +132,23 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(T* __restri
   for (int64_t e = units * kVec + int64_t(b) * blockDim.x + threadIdx.x; e < numel; e += stride) {
     float acc = 0.f;
     for (int r = 0; r < world; ++r) {
-      const uint16_t bits = ld_relaxed_sys_u16(reinterpret_cast<const T*>(reinterpret_cast<const char*>(peers[r]) + slot_off) + e);
+      const uint16_t bits =
+          ld_relaxed_sys_u16(reinterpret_cast<const T*>(reinterpret_cast<const char*>(peers[r]) + kDataOffset) + e);
       T v;
       memcpy(&v, &bits, sizeof(v));
       acc += Elem<T>::to_f(v);
     }
     out[e] = Elem<T>::from_f(acc);
+  }
+  __syncthreads();  // this CTA's reads of the peers' partials are done
+  peer_barrier(peers, b, rank, world, 2u * call, err);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&hdr->finished, 1u) == gridDim.x - 1u) {  // the call's last CTA
+      hdr->finished = 0u;
+      __threadfence();
+      atomicExch(&hdr->calls, call);
+    }
   }
 }
 
@@ -128,19 +157,15 @@ __global__ void __launch_bounds__(kThreads) allreduce_oneshot_kernel(T* __restri
 
 extern "C" size_t ntb200_allreduce_buffer_size(int64_t capacity, int elem_bytes) {
   if (capacity < 0 || elem_bytes <= 0) return 0;
-  return static_cast<size_t>(ntb200::kFlagBytes + 2 * ntb200::slot_bytes(capacity, elem_bytes));
+  return static_cast<size_t>(ntb200::kDataOffset + ntb200::slot_bytes(capacity, elem_bytes));
 }
 
-extern "C" int64_t ntb200_allreduce_slot_offset(int64_t capacity, int elem_bytes, uint32_t epoch) {
-  if (capacity < 0 || elem_bytes <= 0) return -1;
-  return ntb200::kFlagBytes + int64_t(epoch & 1u) * ntb200::slot_bytes(capacity, elem_bytes);
-}
+extern "C" int64_t ntb200_allreduce_data_offset(void) { return ntb200::kDataOffset; }
 
-extern "C" int ntb200_allreduce_oneshot(void* out, const uint64_t* peer_buffers, int64_t numel,
-                                        int64_t capacity, int rank, int world_size, uint32_t epoch,
-                                        int dtype, void* stream) {
+extern "C" int ntb200_allreduce_oneshot(void* out, const uint64_t* peer_buffers, int64_t numel, int rank,
+                                        int world_size, int dtype, void* stream) {
   using namespace ntb200;
-  if (numel < 0 || numel > capacity) return fail(NTB200_ERR_INVALID_ARGUMENT, "allreduce: numel outside [0, capacity]");
+  if (numel < 0) return fail(NTB200_ERR_INVALID_ARGUMENT, "allreduce: numel < 0");
   if (world_size < 1 || world_size > kMaxRanks || rank < 0 || rank >= world_size)
     return fail(NTB200_ERR_INVALID_ARGUMENT, "allreduce: rank %d of %d (at most %d ranks)", rank, world_size,
                 kMaxRanks);
@@ -149,7 +174,6 @@ extern "C" int ntb200_allreduce_oneshot(void* out, const uint64_t* peer_buffers,
   if (!aligned16(out)) return fail(NTB200_ERR_MISALIGNED, "allreduce: out must be 16-byte aligned");
   if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
     return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "allreduce: dtype %d (bf16/f16 only)", dtype);
-  const int64_t slot_off = ntb200_allreduce_slot_offset(capacity, 2, epoch);
   const int64_t units = ceil_div(numel, 8);
   int64_t grid = ceil_div(units, kThreads);
   const int64_t cap = num_sms() < kMaxBlocks ? num_sms() : kMaxBlocks;
@@ -157,9 +181,8 @@ extern "C" int ntb200_allreduce_oneshot(void* out, const uint64_t* peer_buffers,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == NTB200_DTYPE_BF16)
     return launch_kernel("allreduce_oneshot", allreduce_oneshot_kernel<__nv_bfloat16>, dim3(unsigned(grid)),
-                         dim3(kThreads), 0, s, static_cast<__nv_bfloat16*>(out), peer_buffers, numel, slot_off,
-                         rank, world_size, epoch, device_error_word());
+                         dim3(kThreads), 0, s, static_cast<__nv_bfloat16*>(out), peer_buffers, numel, rank,
+                         world_size, device_error_word());
   return launch_kernel("allreduce_oneshot", allreduce_oneshot_kernel<__half>, dim3(unsigned(grid)), dim3(kThreads),
-                       0, s, static_cast<__half*>(out), peer_buffers, numel, slot_off, rank, world_size, epoch,
-                       device_error_word());
+                       0, s, static_cast<__half*>(out), peer_buffers, numel, rank, world_size, device_error_word());
 }

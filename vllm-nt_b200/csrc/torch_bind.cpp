@@ -361,8 +361,7 @@ void linear_silu_and_mul(at::Tensor out, const at::Tensor& x_in, const at::Tenso
 
 // out = sum over ranks of each rank's partial (see ntb200_allreduce_oneshot); peer_buffers
 // is an int64 CUDA tensor of the world's buffer addresses.
-void allreduce_oneshot(at::Tensor out, const at::Tensor& peer_buffers, int64_t capacity, int64_t rank,
-                       int64_t world_size, int64_t epoch) {
+void allreduce_oneshot(at::Tensor out, const at::Tensor& peer_buffers, int64_t rank, int64_t world_size) {
   require_cuda(out, "out");
   require_cuda(peer_buffers, "peer_buffers");
   TORCH_CHECK(out.is_contiguous(), "ntb200.allreduce_oneshot: out must be contiguous");
@@ -371,8 +370,8 @@ void allreduce_oneshot(at::Tensor out, const at::Tensor& peer_buffers, int64_t c
               "ntb200.allreduce_oneshot: peer_buffers must be int64 [world_size]");
   c10::cuda::CUDAGuard guard(out.device());
   check(ntb200_allreduce_oneshot(out.data_ptr(), reinterpret_cast<const uint64_t*>(peer_buffers.data_ptr()),
-                                 out.numel(), capacity, static_cast<int>(rank), static_cast<int>(world_size),
-                                 static_cast<uint32_t>(epoch), dtype_code(out), stream_of(out)),
+                                 out.numel(), static_cast<int>(rank), static_cast<int>(world_size),
+                                 dtype_code(out), stream_of(out)),
         "allreduce_oneshot");
 }
 
@@ -380,9 +379,7 @@ int64_t allreduce_buffer_size(int64_t capacity, int64_t elem_bytes) {
   return static_cast<int64_t>(ntb200_allreduce_buffer_size(capacity, static_cast<int>(elem_bytes)));
 }
 
-int64_t allreduce_slot_offset(int64_t capacity, int64_t elem_bytes, int64_t epoch) {
-  return ntb200_allreduce_slot_offset(capacity, static_cast<int>(elem_bytes), static_cast<uint32_t>(epoch));
-}
+int64_t allreduce_data_offset() { return ntb200_allreduce_data_offset(); }
 
 int64_t linear_workspace_size(int64_t m, int64_t n, int64_t k) {
   return static_cast<int64_t>(ntb200_linear_workspace_size(m, n, k));
@@ -418,11 +415,9 @@ TORCH_LIBRARY(ntb200, m) {
   m.def("linear(Tensor(a!) out, Tensor x, Tensor weight, Tensor? bias, Tensor(b!)? workspace) -> ()");
   m.def("linear_workspace_size(int m, int n, int k) -> int", &linear_workspace_size);
   m.def("linear_silu_and_mul(Tensor(a!) out, Tensor x, Tensor weight) -> ()");
-  m.def(
-      "allreduce_oneshot(Tensor(a!) out, Tensor peer_buffers, int capacity, int rank, int world_size, "
-      "int epoch) -> ()");
+  m.def("allreduce_oneshot(Tensor(a!) out, Tensor peer_buffers, int rank, int world_size) -> ()");
   m.def("allreduce_buffer_size(int capacity, int elem_bytes) -> int", &allreduce_buffer_size);
-  m.def("allreduce_slot_offset(int capacity, int elem_bytes, int epoch) -> int", &allreduce_slot_offset);
+  m.def("allreduce_data_offset() -> int", &allreduce_data_offset);
 }
 
 TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {

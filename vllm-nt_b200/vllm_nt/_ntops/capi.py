@@ -8,7 +8,7 @@ for a non-zero status."""
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_char_p, c_float, c_int, c_int64, c_size_t, c_uint32, c_void_p
+from ctypes import c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
 from pathlib import Path
 
 LIBRARY = Path(__file__).resolve().parents[1] / "_lib" / "libntb200.so"
@@ -75,10 +75,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p]
     ),
     "ntb200_allreduce_buffer_size": (c_size_t, [c_int64, c_int]),
-    "ntb200_allreduce_slot_offset": (c_int64, [c_int64, c_int, c_uint32]),
-    "ntb200_allreduce_oneshot": (
-        c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_uint32, c_int, c_void_p]
-    ),
+    "ntb200_allreduce_data_offset": (c_int64, []),
+    "ntb200_allreduce_oneshot": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p]),
 }
 
 

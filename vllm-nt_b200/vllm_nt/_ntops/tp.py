@@ -8,8 +8,8 @@ rank's peer-mapped buffer (torch symmetric memory), and ``ntb200_allreduce_onesh
 reads every rank's partial over NVLink and sums it: two kernels of this library back to
 back (the second launched as a programmatic dependent of the first), no NCCL call.
 
-Every rank must make the same sequence of calls (the epoch counts them); a call is not
-capturable in a CUDA graph.
+Every rank must make the same sequence of calls on its buffer.  The call count lives in
+the buffer on the device, so the GEMM + all-reduce pair can be captured in a CUDA graph.
 """
 
 from __future__ import annotations
@@ -21,8 +21,7 @@ from vllm_nt._ntops.torch._ext import ops
 
 
 class PeerAllReduce:
-    """A peer-mapped buffer for ``capacity`` bf16/f16 elements per rank and the epoch of
-    the calls made through it."""
+    """A peer-mapped buffer for ``capacity`` bf16/f16 elements per rank."""
 
     def __init__(self, group: dist.ProcessGroup | None, capacity: int, device: torch.device | None = None):
         import torch.distributed._symmetric_memory as symm_mem
@@ -38,27 +37,30 @@ class PeerAllReduce:
         self.rank = int(self.handle.rank)
         self.world_size = int(self.handle.world_size)
         self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=self.device)
-        self.epoch = 0
+        self._data = int(ops().allreduce_data_offset())
+        self._views: dict[tuple[tuple[int, ...], torch.dtype], torch.Tensor] = {}
         # no rank may write a peer's flags before every rank has cleared its own buffer
         dist.barrier(group=self.group)
 
     def partial_view(self, shape: tuple[int, ...], dtype: torch.dtype) -> torch.Tensor:
-        """This rank's slot for the next call, viewed as ``shape``: the GEMM writes its
-        partial product here."""
-        numel = 1
-        for d in shape:
-            numel *= int(d)
-        if numel > self.capacity:
-            raise ValueError(f"{numel} elements exceed the buffer's capacity of {self.capacity}")
-        off = int(ops().allreduce_slot_offset(self.capacity, 2, self.epoch + 1))
-        return self.buffer[off : off + 2 * numel].view(dtype).view(shape)
+        """This rank's partial, viewed as ``shape``: the GEMM writes its product here."""
+        key = (tuple(int(d) for d in shape), dtype)
+        view = self._views.get(key)
+        if view is None:
+            numel = 1
+            for d in key[0]:
+                numel *= d
+            if numel > self.capacity:
+                raise ValueError(f"{numel} elements exceed the buffer's capacity of {self.capacity}")
+            view = self.buffer[self._data : self._data + 2 * numel].view(dtype).view(key[0])
+            self._views[key] = view
+        return view
 
     def reduce(self, partial: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """Sums ``partial`` (a view from :meth:`partial_view`, filled) over all ranks."""
-        self.epoch += 1
         if out is None:
             out = torch.empty(partial.shape, dtype=partial.dtype, device=partial.device)
-        ops().allreduce_oneshot(out, self.peers, self.capacity, self.rank, self.world_size, self.epoch)
+        ops().allreduce_oneshot(out, self.peers, self.rank, self.world_size)
         return out
 
     def linear(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
