@@ -494,8 +494,9 @@ def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
 
             out_peer = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
 
+            part = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
+
             def peer():
-                part = par.partial_view((m, 4096), torch.bfloat16)
                 o.linear(part, x, w, None, None)
                 par.reduce(part, out_peer)
 
@@ -520,7 +521,7 @@ def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
                 "allreduce_bytes": m * 4096 * 2,
                 "chunks": chunks,
             }
-            del x, out, out_peer
+            del x, out, out_peer, part
         del w
     del par
     return res

@@ -207,19 +207,19 @@ int ntb200_linear_silu_and_mul(void* out, const void* x, const void* weight, int
  * RowParallelLinear issues after the GEMM (vllm:model_executor/layers/linear.py
  * RowParallelLinear.forward -> tensor_model_parallel_all_reduce); the reference plugin has
  * no counterpart of its own (it leaves the collective to vLLM).
- * Every rank owns a buffer of ntb200_allreduce_buffer_size(capacity, 2) bytes that all
- * ranks can address (e.g. torch symmetric memory), zero-filled once; capacity is the
- * largest element count it will reduce.  Before a call, the rank's partial (numel bf16/f16
- * elements) must be in its own buffer at byte ntb200_allreduce_data_offset() (the GEMM
- * writes it there).  peer_buffers is a DEVICE array of world_size buffer addresses
- * (index = rank, this rank's own included).  out receives the elementwise sum (fp32
- * accumulation).  Every rank must make the same sequence of calls on its buffer; the call
+ * Every rank owns a buffer of ntb200_allreduce_buffer_size(capacity, 2, world_size) bytes
+ * that all ranks can address (e.g. torch symmetric memory), zero-filled once; capacity is
+ * the largest element count it will reduce.  partial (numel <= capacity bf16/f16 elements,
+ * this rank's GEMM output, ordinary device memory) is pushed into every rank's buffer and
+ * out receives the elementwise sum of all ranks' partials (fp32 accumulation).
+ * peer_buffers is a DEVICE array of world_size buffer addresses (index = rank, this rank's
+ * own included).  Every rank must make the same sequence of calls on its buffer; the call
  * count lives in the buffer, so calls may be captured in a CUDA graph and replayed.  At
  * most 8 ranks.  Waits for peers are bounded (NTB200_DEVERR_WAIT_TIMEOUT after ~2 s). */
-size_t ntb200_allreduce_buffer_size(int64_t capacity, int elem_bytes);
-int64_t ntb200_allreduce_data_offset(void);
-int ntb200_allreduce_oneshot(void* out, const uint64_t* peer_buffers, int64_t numel, int rank,
-                             int world_size, int dtype, void* stream);
+size_t ntb200_allreduce_buffer_size(int64_t capacity, int elem_bytes, int world_size);
+int ntb200_allreduce_oneshot(void* out, const void* partial, const uint64_t* peer_buffers,
+                             int64_t numel, int64_t capacity, int rank, int world_size, int dtype,
+                             void* stream);
 
 #ifdef __cplusplus
 }

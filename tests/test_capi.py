@@ -80,9 +80,10 @@ def test_workspace_queries():
     assert ws == 256 * 32 * 8 * 128 * 4 + 256 * 32 * 8 * 4
     assert lib.ntb200_paged_attention_decode_workspace_size(256, 32, 8, 64, 16, 8192) == 0
     assert lib.ntb200_linear_workspace_size(1, 4096, 4096) == 0
-    # peer all-reduce buffer: 8 KiB of flags + a 256-byte header + the capacity rounded to 256 B
-    assert lib.ntb200_allreduce_data_offset() == 8192 + 256
-    assert lib.ntb200_allreduce_buffer_size(1000, 2) == 8192 + 256 + 2048
+    # peer all-reduce buffer: 8 KiB of flags + a 256-byte header + two parities x W ranks
+    # of the capacity rounded to 256 B
+    assert lib.ntb200_allreduce_buffer_size(1000, 2, 4) == 8192 + 256 + 2 * 4 * 2048
+    assert lib.ntb200_allreduce_buffer_size(1000, 2, 9) == 0
 
 
 def test_read_device_error_rejects_null():

@@ -61,11 +61,13 @@ def main() -> int:
     xs = torch.empty(m, k, dtype=torch.bfloat16, device=dev)
     ws = (0.05 * torch.randn(n, k, generator=torch.Generator().manual_seed(99 + rank))).to(torch.bfloat16).to(dev)
     xs.normal_()
-    par.linear(xs, ws)  # warm-up outside the capture
+    gout = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    gpart = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    par.linear(xs, ws, out=gout, partial=gpart)  # warm-up outside the capture
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        gout = par.linear(xs, ws)
+        par.linear(xs, ws, out=gout, partial=gpart)
     for rep in range(3):
         xs.copy_(torch.randn(m, k, generator=torch.Generator().manual_seed(500 + 10 * rep + rank)).to(torch.bfloat16))
         dist.barrier()

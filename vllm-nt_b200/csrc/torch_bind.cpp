@@ -359,27 +359,31 @@ void linear_silu_and_mul(at::Tensor out, const at::Tensor& x_in, const at::Tenso
         "linear_silu_and_mul");
 }
 
-// out = sum over ranks of each rank's partial (see ntb200_allreduce_oneshot); peer_buffers
-// is an int64 CUDA tensor of the world's buffer addresses.
-void allreduce_oneshot(at::Tensor out, const at::Tensor& peer_buffers, int64_t rank, int64_t world_size) {
+// out = sum over ranks of their partials (see ntb200_allreduce_oneshot); peer_buffers is an
+// int64 CUDA tensor of the world's buffer addresses.
+void allreduce_oneshot(at::Tensor out, const at::Tensor& partial, const at::Tensor& peer_buffers, int64_t capacity,
+                       int64_t rank, int64_t world_size) {
   require_cuda(out, "out");
+  require_cuda(partial, "partial");
   require_cuda(peer_buffers, "peer_buffers");
-  TORCH_CHECK(out.is_contiguous(), "ntb200.allreduce_oneshot: out must be contiguous");
+  TORCH_CHECK(out.is_contiguous() && partial.is_contiguous() && out.numel() == partial.numel() &&
+                  out.scalar_type() == partial.scalar_type(),
+              "ntb200.allreduce_oneshot: out and partial must be contiguous, of one size and dtype");
   TORCH_CHECK(peer_buffers.scalar_type() == at::kLong && peer_buffers.is_contiguous() &&
                   peer_buffers.numel() == world_size,
               "ntb200.allreduce_oneshot: peer_buffers must be int64 [world_size]");
   c10::cuda::CUDAGuard guard(out.device());
-  check(ntb200_allreduce_oneshot(out.data_ptr(), reinterpret_cast<const uint64_t*>(peer_buffers.data_ptr()),
-                                 out.numel(), static_cast<int>(rank), static_cast<int>(world_size),
-                                 dtype_code(out), stream_of(out)),
+  check(ntb200_allreduce_oneshot(out.data_ptr(), partial.data_ptr(),
+                                 reinterpret_cast<const uint64_t*>(peer_buffers.data_ptr()), out.numel(), capacity,
+                                 static_cast<int>(rank), static_cast<int>(world_size), dtype_code(out),
+                                 stream_of(out)),
         "allreduce_oneshot");
 }
 
-int64_t allreduce_buffer_size(int64_t capacity, int64_t elem_bytes) {
-  return static_cast<int64_t>(ntb200_allreduce_buffer_size(capacity, static_cast<int>(elem_bytes)));
+int64_t allreduce_buffer_size(int64_t capacity, int64_t elem_bytes, int64_t world_size) {
+  return static_cast<int64_t>(
+      ntb200_allreduce_buffer_size(capacity, static_cast<int>(elem_bytes), static_cast<int>(world_size)));
 }
-
-int64_t allreduce_data_offset() { return ntb200_allreduce_data_offset(); }
 
 int64_t linear_workspace_size(int64_t m, int64_t n, int64_t k) {
   return static_cast<int64_t>(ntb200_linear_workspace_size(m, n, k));
@@ -415,9 +419,10 @@ TORCH_LIBRARY(ntb200, m) {
   m.def("linear(Tensor(a!) out, Tensor x, Tensor weight, Tensor? bias, Tensor(b!)? workspace) -> ()");
   m.def("linear_workspace_size(int m, int n, int k) -> int", &linear_workspace_size);
   m.def("linear_silu_and_mul(Tensor(a!) out, Tensor x, Tensor weight) -> ()");
-  m.def("allreduce_oneshot(Tensor(a!) out, Tensor peer_buffers, int rank, int world_size) -> ()");
-  m.def("allreduce_buffer_size(int capacity, int elem_bytes) -> int", &allreduce_buffer_size);
-  m.def("allreduce_data_offset() -> int", &allreduce_data_offset);
+  m.def(
+      "allreduce_oneshot(Tensor(a!) out, Tensor partial, Tensor peer_buffers, int capacity, int rank, "
+      "int world_size) -> ()");
+  m.def("allreduce_buffer_size(int capacity, int elem_bytes, int world_size) -> int", &allreduce_buffer_size);
 }
 
 TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {

@@ -74,9 +74,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ntb200_linear_silu_and_mul": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p]
     ),
-    "ntb200_allreduce_buffer_size": (c_size_t, [c_int64, c_int]),
-    "ntb200_allreduce_data_offset": (c_int64, []),
-    "ntb200_allreduce_oneshot": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p]),
+    "ntb200_allreduce_buffer_size": (c_size_t, [c_int64, c_int, c_int]),
+    "ntb200_allreduce_oneshot": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p]
+    ),
 }
 
 

@@ -3,10 +3,11 @@
 Under TP, vLLM's RowParallelLinear (o_proj, down) computes a partial product on every
 rank and sums the partials with an NCCL all-reduce
 (vllm:model_executor/layers/linear.py, RowParallelLinear.forward ->
-tensor_model_parallel_all_reduce).  Here the GEMM writes its partial straight into this
-rank's peer-mapped buffer (torch symmetric memory), and ``ntb200_allreduce_oneshot``
-reads every rank's partial over NVLink and sums it: two kernels of this library back to
-back (the second launched as a programmatic dependent of the first), no NCCL call.
+tensor_model_parallel_all_reduce).  Here the GEMM writes its partial into local memory and
+``ntb200_allreduce_oneshot`` pushes it over NVLink into every rank's peer-mapped buffer
+(torch symmetric memory), meets the other ranks at one barrier and sums the pushed
+partials: two kernels of this library back to back (the second launched as a programmatic
+dependent of the first), no NCCL call.
 
 Every rank must make the same sequence of calls on its buffer.  The call count lives in
 the buffer on the device, so the GEMM + all-reduce pair can be captured in a CUDA graph.
@@ -29,7 +30,8 @@ class PeerAllReduce:
         self.group = group if group is not None else dist.group.WORLD
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.capacity = int(capacity)
-        nbytes = int(ops().allreduce_buffer_size(self.capacity, 2))
+        world = dist.get_world_size(self.group)
+        nbytes = int(ops().allreduce_buffer_size(self.capacity, 2, world))
         self.buffer = symm_mem.empty(nbytes, dtype=torch.uint8, device=self.device)
         self.buffer.zero_()
         torch.cuda.synchronize(self.device)
@@ -37,35 +39,25 @@ class PeerAllReduce:
         self.rank = int(self.handle.rank)
         self.world_size = int(self.handle.world_size)
         self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=self.device)
-        self._data = int(ops().allreduce_data_offset())
-        self._views: dict[tuple[tuple[int, ...], torch.dtype], torch.Tensor] = {}
         # no rank may write a peer's flags before every rank has cleared its own buffer
         dist.barrier(group=self.group)
 
-    def partial_view(self, shape: tuple[int, ...], dtype: torch.dtype) -> torch.Tensor:
-        """This rank's partial, viewed as ``shape``: the GEMM writes its product here."""
-        key = (tuple(int(d) for d in shape), dtype)
-        view = self._views.get(key)
-        if view is None:
-            numel = 1
-            for d in key[0]:
-                numel *= d
-            if numel > self.capacity:
-                raise ValueError(f"{numel} elements exceed the buffer's capacity of {self.capacity}")
-            view = self.buffer[self._data : self._data + 2 * numel].view(dtype).view(key[0])
-            self._views[key] = view
-        return view
-
     def reduce(self, partial: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Sums ``partial`` (a view from :meth:`partial_view`, filled) over all ranks."""
+        """Sums ``partial`` (contiguous, at most ``capacity`` elements) over all ranks."""
+        if partial.numel() > self.capacity:
+            raise ValueError(f"{partial.numel()} elements exceed the buffer's capacity of {self.capacity}")
         if out is None:
-            out = torch.empty(partial.shape, dtype=partial.dtype, device=partial.device)
-        ops().allreduce_oneshot(out, self.peers, self.rank, self.world_size)
+            out = torch.empty_like(partial)
+        ops().allreduce_oneshot(out, partial, self.peers, self.capacity, self.rank, self.world_size)
         return out
 
-    def linear(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    def linear(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+               out: torch.Tensor | None = None, partial: torch.Tensor | None = None) -> torch.Tensor:
         """sum over ranks of x_r @ weight_r^T, plus bias once (on rank 0, as vLLM's
-        RowParallelLinear adds it before the reduction)."""
-        partial = self.partial_view((*x.shape[:-1], weight.shape[0]), x.dtype)
+        RowParallelLinear adds it before the reduction).  ``partial`` and ``out`` may be
+        given to keep the call free of allocations (e.g. for CUDA-graph capture)."""
+        shape = (*x.shape[:-1], weight.shape[0])
+        if partial is None:
+            partial = x.new_empty(shape)
         ops().linear(partial, x, weight, bias if self.rank == 0 else None, None)
-        return self.reduce(partial)
+        return self.reduce(partial, out)
