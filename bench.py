@@ -498,7 +498,7 @@ def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
 
             def peer():
                 o.linear(part, x, w, None, None)
-                par.reduce(part, out_peer)
+                par.reduce(part, out_peer, oneshot=True)
 
             for f in (gemm, allreduce, serial, pipelined, peer):
                 f()

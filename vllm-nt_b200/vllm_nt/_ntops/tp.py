@@ -39,15 +39,25 @@ class PeerAllReduce:
         self.rank = int(self.handle.rank)
         self.world_size = int(self.handle.world_size)
         self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=self.device)
+        # The one-shot push moves (W-1) x bytes per rank over NVLink; measured on B200s it
+        # beats NCCL up to about 16 MB / (W-1) (8 MB at W=2, 1 MB at W=8) and loses beyond,
+        # where NCCL's bandwidth-optimal algorithms take over.
+        self.oneshot_max_bytes = (16 << 20) // max(1, self.world_size - 1)
         # no rank may write a peer's flags before every rank has cleared its own buffer
         dist.barrier(group=self.group)
 
-    def reduce(self, partial: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-        """Sums ``partial`` (contiguous, at most ``capacity`` elements) over all ranks."""
-        if partial.numel() > self.capacity:
-            raise ValueError(f"{partial.numel()} elements exceed the buffer's capacity of {self.capacity}")
+    def reduce(self, partial: torch.Tensor, out: torch.Tensor | None = None, oneshot: bool | None = None) -> torch.Tensor:
+        """Sums ``partial`` (contiguous) over all ranks: the one-shot push up to
+        ``oneshot_max_bytes`` (and ``capacity``), NCCL beyond.  Every rank takes the same
+        branch, since the sizes are the same on every rank."""
         if out is None:
             out = torch.empty_like(partial)
+        if oneshot is None:
+            oneshot = partial.numel() * partial.element_size() <= self.oneshot_max_bytes
+        if not oneshot or partial.numel() > self.capacity:
+            out.copy_(partial)
+            dist.all_reduce(out, group=self.group)
+            return out
         ops().allreduce_oneshot(out, partial, self.peers, self.capacity, self.rank, self.world_size)
         return out
 
