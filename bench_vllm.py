@@ -72,6 +72,15 @@ def write_plugin_dist(base: Path) -> Path:
     return site
 
 
+def _worker_usage(worker=None) -> dict:
+    """Runs inside a vLLM worker process (collective_rpc): that rank's plugin counters."""
+    from vllm_nt.oot import get_usage_summary
+
+    s = get_usage_summary()
+    return {"hit_ops": list(s["hit_ops"]),
+            "operators": {k: {"hits": v["hits"], "failures": v["failures"]} for k, v in s["operators"].items()}}
+
+
 def child(args) -> int:
     import numpy as np
     from vllm import LLM, SamplingParams
@@ -111,13 +120,23 @@ def child(args) -> int:
     }
     if args.mode == "b200":
         try:
-            from vllm_nt.oot import get_usage_summary
+            if args.tp > 1:
+                # tensor-parallel workers are other processes: ask each for its counters
+                per_rank = llm.collective_rpc(_worker_usage)
+                s = {"hit_ops": sorted({op for r in per_rank for op in r["hit_ops"]}), "operators": {}}
+                for r in per_rank:
+                    for k, v in r["operators"].items():
+                        acc = s["operators"].setdefault(k, {"hits": 0, "failures": 0})
+                        acc["hits"] += v["hits"]
+                        acc["failures"] += v["failures"]
+            else:
+                from vllm_nt.oot import get_usage_summary
 
-            s = get_usage_summary()
+                s = get_usage_summary()
             result["hit_ops"] = s["hit_ops"]
             result["hits"] = {k: v["hits"] for k, v in s["operators"].items() if v["hits"]}
             result["failures"] = {k: v["failures"] for k, v in s["operators"].items() if v["failures"]}
-        except Exception as exc:  # workers in other processes keep their own counters
+        except Exception as exc:  # noqa: BLE001 - the counters are reported, not required
             result["usage_summary_error"] = str(exc)
     print("RESULT_JSON=" + json.dumps(result), flush=True)
     return 0
