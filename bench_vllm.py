@@ -4,7 +4,8 @@
 Workload: a Llama-3-8B-shaped decoder (32 layers, hidden 4096, 32/8 heads of 128,
 intermediate 14336, vocab 128256, RMSNorm eps 1e-5, RoPE base 500000) with vLLM's dummy
 weights (no checkpoint is available offline), 256 prompts of 512 uniform random token ids,
-128 greedy tokens each (ignore_eos), FLASH_ATTN backend, eager mode.
+128 greedy tokens each (ignore_eos), FLASH_ATTN backend (``--attention-backend
+FLASHINFER`` for vLLM's FlashInfer backend), eager mode.
 
     python bench_vllm.py --mode b200|native [--replicas N | --tp N]
 
@@ -96,7 +97,7 @@ def child(args) -> int:
         max_model_len=1024,
         max_num_seqs=256,
         gpu_memory_utilization=0.85,
-        attention_backend="FLASH_ATTN",
+        attention_backend=args.attention_backend,
         seed=0,
     )
     rng = np.random.default_rng(args.seed)
@@ -157,7 +158,7 @@ def launch(args, base: Path, model_dir: Path, gpus: str, tp: int, log: Path) -> 
     env["PYTHONPATH"] = os.pathsep.join(paths + [env.get("PYTHONPATH", "")])
     cmd = [sys.executable, str(Path(__file__).resolve()), "--child", "--mode", args.mode, "--tp", str(tp),
            "--model-dir", str(model_dir), "--prompts", str(args.prompts), "--output-len", str(args.output_len),
-           "--seed", str(args.seed)]
+           "--seed", str(args.seed), "--attention-backend", args.attention_backend]
     return subprocess.Popen(cmd, env=env, stdout=open(log, "w"), stderr=subprocess.STDOUT)
 
 
@@ -179,6 +180,7 @@ def main() -> int:
     ap.add_argument("--log-dir", default="gpurun_out")
     ap.add_argument("--child", action="store_true")
     ap.add_argument("--model-dir")
+    ap.add_argument("--attention-backend", default="FLASH_ATTN", choices=["FLASH_ATTN", "FLASHINFER"])
     args = ap.parse_args()
     if args.child:
         return child(args)

@@ -169,3 +169,44 @@ def test_fused_mlp_hook_on_a_llama_shaped_mlp(_b200_config, vllm_ctx):
     ref = oracle.linear(h.to(torch.bfloat16), wd)
     torch.testing.assert_close(out.float().cpu(), ref.float(), **TOL)
     assert _hits(patching, "GateUpSiluAndMul") == 1 and _hits(patching, "MatMul") == 1
+
+
+@pytest.mark.parametrize("layout", ["NHD", "HND"])
+def test_flashinfer_impl_hooks_store_and_decode(_b200_config, layout):
+    """FlashInferImpl hooks on FlashInfer's cache, logically [blocks, 2, 16, H, D] and
+    stored NHD or HND (heads outside tokens): the kernels take the strides as they are."""
+    patching = _b200_config
+    fwd = patching._build_flashinfer_forward(lambda *a, **k: pytest.fail("decode fell back to FlashInfer"))
+    upd = patching._build_flashinfer_kv_update(lambda *a, **k: pytest.fail("store fell back to FlashInfer"))
+    impl = SimpleNamespace(num_heads=32, num_kv_heads=8, head_size=128, scale=1 / math.sqrt(128), attn_type="decoder",
+                           kv_cache_dtype="auto", alibi_slopes=None, logits_soft_cap=None, sinks=None,
+                           sliding_window=None, kv_sharing_target_layer_name=None)
+    g = seeded(14)
+    nb = 48
+    kv = torch.randn(nb, 2, 16, 8, 128, generator=g).to(torch.bfloat16)
+    if layout == "HND":
+        kvd = kv.permute(0, 1, 3, 2, 4).contiguous().cuda().permute(0, 1, 3, 2, 4)
+        assert kvd.stride(2) == 128 and kvd.stride(3) == 16 * 128
+    else:
+        kvd = kv.cuda()
+    ctx = [0, 17, 200]
+    table = torch.randperm(nb, generator=g)[:3 * 16].view(3, 16).to(torch.int32)
+    slots = torch.tensor([int(table[b, c // 16]) * 16 + c % 16 for b, c in enumerate(ctx)])
+    key = torch.randn(4, 8, 128, generator=g).to(torch.bfloat16)
+    value = torch.randn(4, 8, 128, generator=g).to(torch.bfloat16)
+    upd(impl, None, key.cuda(), value.cuda(), kvd, slots.cuda())
+    ref_kv = kv.clone()
+    ref_kv[slots // 16, 0, slots % 16] = key[:3]
+    ref_kv[slots // 16, 1, slots % 16] = value[:3]
+    assert torch.equal(kvd.cpu(), ref_kv)
+    q = torch.randn(4, 32, 128, generator=g).to(torch.bfloat16)
+    out = torch.zeros(4, 32 * 128, dtype=torch.bfloat16, device="cuda")
+    seq = torch.tensor([c + 1 for c in ctx], dtype=torch.int32)
+    dec = SimpleNamespace(block_tables=table.cuda(), seq_lens=seq.cuda(), max_seq_len=int(seq.max()))
+    meta = SimpleNamespace(num_actual_tokens=3, num_decodes=3, num_decode_tokens=3, num_prefills=0, decode=dec,
+                           use_cascade=False)
+    fwd(impl, None, q.cuda(), None, None, kvd, meta, out)
+    ref = oracle.paged_decode(q[:3], ref_kv[:, 0].contiguous(), ref_kv[:, 1].contiguous(), seq, table, impl.scale)
+    torch.testing.assert_close(out[:3].view(3, 32, 128).float().cpu(), ref, **TOL)
+    assert not out[3].any()
+    assert _hits(patching, "StoreKVCache") == 1 and _hits(patching, "PagedAttentionDecode") == 1

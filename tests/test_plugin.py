@@ -212,11 +212,11 @@ def test_attention_hooks_decode_only_and_kv_store(monkeypatch):
     monkeypatch.setattr(patching, "_attn_impl_supported", lambda *a: True)
     monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
 
-    def fake_decode(out, q, kv, seq, table, n, scale, msl):
+    def fake_decode(out, q, kv, seq, table, n, scale, msl, kv_dim=0):
         calls["decode"] = (tuple(out.shape), tuple(q.shape), tuple(kv.shape), tuple(seq.shape), n, scale, msl)
         out[:n].fill_(1.0)
 
-    def fake_store(key, value, kv, slots):
+    def fake_store(key, value, kv, slots, kv_dim=0):
         calls["store"] = (tuple(key.shape), tuple(kv.shape), tuple(slots.shape))
 
     monkeypatch.setattr(patching, "paged_attention_decode_flash", fake_decode)
@@ -290,3 +290,41 @@ def test_fused_mlp_patch_is_opt_in(monkeypatch):
         assert not patching._function_patch_enabled(spec)
     finally:
         config.reset_backend_config_cache()
+
+
+def test_flashinfer_hooks_decode_only_and_kv_store(monkeypatch):
+    """FlashInferImpl hooks: pure-decode batches with a decode block table go to the
+    kernels on the [blocks, 2, 16, H, D] cache (kv_dim 1); prefill stays on FlashInfer."""
+    calls = {}
+    monkeypatch.setattr(patching, "_attn_impl_supported", lambda *a: True)
+    monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
+
+    def fake_decode(out, q, kv, seq, table, n, scale, msl, kv_dim):
+        calls["decode"] = (tuple(kv.shape), tuple(seq.shape), tuple(table.shape), n, msl, kv_dim)
+        out[:n].fill_(1.0)
+
+    def fake_store(key, value, kv, slots, kv_dim):
+        calls["store"] = (tuple(kv.shape), kv_dim)
+
+    monkeypatch.setattr(patching, "paged_attention_decode_flash", fake_decode)
+    monkeypatch.setattr(patching, "store_kv_cache_flash", fake_store)
+    orig = lambda *a, **k: "flashinfer"  # noqa: E731
+    fwd = patching._build_flashinfer_forward(orig)
+    upd = patching._build_flashinfer_kv_update(orig)
+    impl = SimpleNamespace(num_heads=4, head_size=128, scale=0.1)
+    kv = torch.zeros(6, 2, 16, 2, 128)
+    q = torch.zeros(5, 4, 128)
+    out = torch.zeros(5, 4 * 128)
+    dec = SimpleNamespace(block_tables=torch.zeros(3, 3, dtype=torch.int32), seq_lens=torch.tensor([4, 9, 40]),
+                          max_seq_len=40)
+    meta = SimpleNamespace(num_actual_tokens=3, num_decodes=3, num_decode_tokens=3, num_prefills=0, decode=dec,
+                           use_cascade=False)
+    assert fwd(impl, None, q, q, q, kv, meta, out) is out
+    assert calls["decode"] == ((6, 2, 16, 2, 128), (3,), (3, 3), 3, 40, 1)
+    assert out[:3].eq(1).all() and out[3:].eq(0).all()
+    mixed = SimpleNamespace(**{**vars(meta), "num_prefills": 1})
+    assert fwd(impl, None, q, q, q, kv, mixed, out) == "flashinfer"
+    planned = SimpleNamespace(**{**vars(meta), "decode": SimpleNamespace(wrapper=object())})
+    assert fwd(impl, None, q, q, q, kv, planned, out) == "flashinfer"
+    upd(impl, None, torch.zeros(5, 2, 128), torch.zeros(5, 2, 128), kv, torch.tensor([1, 2, 3]))
+    assert calls["store"] == ((6, 2, 16, 2, 128), 1)

@@ -268,11 +268,12 @@ int64_t decode_workspace_size(int64_t num_seqs, int64_t num_q_heads, int64_t num
 // call per layer.
 void decode_flash_layout(at::Tensor output, const at::Tensor& query, const at::Tensor& kv_cache,
                          const at::Tensor& seq_lens, const at::Tensor& block_table, int64_t num_tokens,
-                         double scale, int64_t max_seq_len) {
+                         double scale, int64_t max_seq_len, int64_t kv_dim) {
   require_cuda(kv_cache, "kv_cache");
-  TORCH_CHECK(kv_cache.dim() == 5 && kv_cache.size(0) == 2,
-              "ntb200.decode_flash_layout: kv_cache must be [2, blocks, block_size, kv_heads, head_size]");
-  const at::Tensor kc = kv_cache.select(0, 0), vc = kv_cache.select(0, 1);
+  TORCH_CHECK((kv_dim == 0 || kv_dim == 1) && kv_cache.dim() == 5 && kv_cache.size(kv_dim) == 2,
+              "ntb200.decode_flash_layout: kv_cache must be [2, blocks, block_size, kv_heads, head_size] "
+              "(kv_dim 0) or [blocks, 2, block_size, kv_heads, head_size] (kv_dim 1)");
+  const at::Tensor kc = kv_cache.select(kv_dim, 0), vc = kv_cache.select(kv_dim, 1);
   const int64_t head = kc.size(3);
   at::Tensor q = query.dim() == 2 ? query.view({query.size(0), -1, head}) : query;
   at::Tensor o = output.dim() == 2 ? output.view({output.size(0), -1, head}) : output;
@@ -289,11 +290,12 @@ void decode_flash_layout(at::Tensor output, const at::Tensor& query, const at::T
 }
 
 void store_flash_layout(const at::Tensor& key, const at::Tensor& value, at::Tensor kv_cache,
-                        const at::Tensor& slot_mapping) {
+                        const at::Tensor& slot_mapping, int64_t kv_dim) {
   require_cuda(kv_cache, "kv_cache");
-  TORCH_CHECK(kv_cache.dim() == 5 && kv_cache.size(0) == 2,
-              "ntb200.store_flash_layout: kv_cache must be [2, blocks, block_size, kv_heads, head_size]");
-  at::Tensor kc = kv_cache.select(0, 0), vc = kv_cache.select(0, 1);
+  TORCH_CHECK((kv_dim == 0 || kv_dim == 1) && kv_cache.dim() == 5 && kv_cache.size(kv_dim) == 2,
+              "ntb200.store_flash_layout: kv_cache must be [2, blocks, block_size, kv_heads, head_size] "
+              "(kv_dim 0) or [blocks, 2, block_size, kv_heads, head_size] (kv_dim 1)");
+  at::Tensor kc = kv_cache.select(kv_dim, 0), vc = kv_cache.select(kv_dim, 1);
   const int64_t heads = kc.size(2), head = kc.size(3);
   const at::Tensor k = key.dim() == 2 ? key.view({key.size(0), heads, head}) : key;
   const at::Tensor v = value.dim() == 2 ? value.view({value.size(0), heads, head}) : value;
@@ -414,8 +416,10 @@ TORCH_LIBRARY(ntb200, m) {
       &decode_workspace_size);
   m.def(
       "decode_flash_layout(Tensor(a!) output, Tensor query, Tensor kv_cache, Tensor seq_lens, "
-      "Tensor block_table, int num_tokens, float scale, int max_seq_len) -> ()");
-  m.def("store_flash_layout(Tensor key, Tensor value, Tensor(a!) kv_cache, Tensor slot_mapping) -> ()");
+      "Tensor block_table, int num_tokens, float scale, int max_seq_len, int kv_dim=0) -> ()");
+  m.def(
+      "store_flash_layout(Tensor key, Tensor value, Tensor(a!) kv_cache, Tensor slot_mapping, "
+      "int kv_dim=0) -> ()");
   m.def("linear(Tensor(a!) out, Tensor x, Tensor weight, Tensor? bias, Tensor(b!)? workspace) -> ()");
   m.def("linear_workspace_size(int m, int n, int k) -> int", &linear_workspace_size);
   m.def("linear_silu_and_mul(Tensor(a!) out, Tensor x, Tensor weight) -> ()");

@@ -95,17 +95,20 @@ def store_kv_cache(key, value, k_cache, v_cache, slot_mapping):
     return nt_store_kvcache(key, value, k_cache, v_cache, slot_mapping)
 
 
-def store_kv_cache_flash(key, value, kv_cache, slot_mapping):
-    """The KV store on vLLM's FlashAttention cache ([2, blocks, block_size, kv_heads,
-    head_size]) in one op call: the K/V split and views happen in the op."""
-    ops().store_flash_layout(key, value, kv_cache, slot_mapping)
+def store_kv_cache_flash(key, value, kv_cache, slot_mapping, kv_dim=0):
+    """The KV store on vLLM's combined cache tensor in one op call: kv_dim 0 is
+    FlashAttention's [2, blocks, block_size, kv_heads, head_size], kv_dim 1 FlashInfer's
+    [blocks, 2, ...]; the K/V split and views happen in the op."""
+    ops().store_flash_layout(key, value, kv_cache, slot_mapping, kv_dim)
 
 
-def paged_attention_decode_flash(output, query, kv_cache, seq_lens, block_table, num_tokens, scale, max_seq_len):
+def paged_attention_decode_flash(output, query, kv_cache, seq_lens, block_table, num_tokens, scale, max_seq_len,
+                                 kv_dim=0):
     """Decode attention for the first ``num_tokens`` rows of vLLM's padded activations on
-    its FlashAttention cache, in one op call (views, slicing and the split-K workspace are
-    made inside the op)."""
-    ops().decode_flash_layout(output, query, kv_cache, seq_lens, block_table, num_tokens, scale, max_seq_len)
+    its combined cache tensor (kv_dim as in store_kv_cache_flash), in one op call (views,
+    slicing and the split-K workspace are made inside the op)."""
+    ops().decode_flash_layout(output, query, kv_cache, seq_lens, block_table, num_tokens, scale, max_seq_len,
+                              kv_dim)
 
 
 def paged_attention_decode(q, k_cache, v_cache, cache_seqlens, block_table, softmax_scale=None, causal=True, max_seq_len=None):

@@ -388,15 +388,18 @@ def _build_rotary_forward(original: object) -> object:
     return _mark_function_patch(forward, "RoPE")
 
 
-def _attn_impl_supported(impl: Any, dtype: torch.dtype, kv_cache: torch.Tensor) -> bool:
-    """Whether the B200 attention kernels serve this FlashAttentionImpl and cache.  The
-    answer is kept on the impl (its configuration is fixed after construction), keyed by
-    the dtypes and the cache shape, so the per-layer check is one attribute read."""
-    key = (dtype, kv_cache.dtype, kv_cache.shape)
+def _attn_impl_supported(impl: Any, dtype: torch.dtype, kv_cache: torch.Tensor, kv_dim: int = 0) -> bool:
+    """Whether the B200 attention kernels serve this attention impl and cache.  kv_dim is
+    the cache dimension that separates K from V: 0 for FlashAttention's
+    [2, blocks, 16, H, D], 1 for FlashInfer's [blocks, 2, 16, H, D] (whose memory order may
+    be NHD or HND; the kernels take the strides).  The answer is kept on the impl (its
+    configuration is fixed after construction), keyed by the dtypes and the cache shape, so
+    the per-layer check is one attribute read."""
+    key = (dtype, kv_cache.dtype, kv_cache.shape, kv_dim)
     cached = getattr(impl, "_ntb200_supported", None)
     if cached is not None and cached[0] == key:
         return cached[1]
-    ok = _attn_impl_check(impl, dtype, kv_cache)
+    ok = _attn_impl_check(impl, dtype, kv_cache, kv_dim)
     try:
         impl._ntb200_supported = (key, ok)
     except AttributeError:
@@ -404,7 +407,7 @@ def _attn_impl_supported(impl: Any, dtype: torch.dtype, kv_cache: torch.Tensor) 
     return ok
 
 
-def _attn_impl_check(impl: Any, dtype: torch.dtype, kv_cache: torch.Tensor) -> bool:
+def _attn_impl_check(impl: Any, dtype: torch.dtype, kv_cache: torch.Tensor, kv_dim: int = 0) -> bool:
     attn_type = getattr(impl, "attn_type", "decoder")
     sliding = getattr(impl, "sliding_window", None)
     return (
@@ -417,9 +420,11 @@ def _attn_impl_check(impl: Any, dtype: torch.dtype, kv_cache: torch.Tensor) -> b
         and getattr(impl, "dcp_world_size", 1) == 1
         and getattr(impl, "head_size", 0) == 128
         and dtype in _HALF_TYPES
+        and getattr(impl, "kv_sharing_target_layer_name", None) is None
         and kv_cache.dim() == 5
-        and kv_cache.shape[0] == 2
+        and kv_cache.shape[kv_dim] == 2
         and kv_cache.shape[2] == 16
+        and kv_cache.stride(-1) == 1
         and kv_cache.dtype == dtype
     )
 
@@ -478,6 +483,72 @@ def _build_flash_attn_forward(original: object) -> object:
             _record_hit("PagedAttentionDecode", query)
             paged_attention_decode_flash(
                 output, query, kv_cache, meta.seq_lens, meta.block_table, n, self.scale, int(meta.max_seq_len)
+            )
+            return output
+
+        return _route("PagedAttentionDecode", call, kernels)
+
+    return _mark_function_patch(forward, "PagedAttentionDecode")
+
+
+def _build_flashinfer_kv_update(original: object) -> object:
+    """Replacement for FlashInferImpl.do_kv_cache_update: the same slot-mapped store on
+    FlashInfer's [blocks, 2, 16, H, D] cache."""
+    if _is_function_patch(original, "StoreKVCache"):
+        return original
+    original_fn = cast(Callable[..., Any], original)
+
+    def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping):
+        call = lambda: original_fn(self, layer, key, value, kv_cache, slot_mapping)  # noqa: E731
+        if not (key.is_cuda and _attn_impl_supported(self, key.dtype, kv_cache, 1)):
+            return call()
+
+        def kernels():
+            _record_hit("StoreKVCache", key)
+            store_kv_cache_flash(key, value, kv_cache, slot_mapping, 1)
+
+        return _route("StoreKVCache", call, kernels)
+
+    return _mark_function_patch(do_kv_cache_update, "StoreKVCache")
+
+
+def _build_flashinfer_forward(original: object) -> object:
+    """Replacement for FlashInferImpl.forward: a pure-decode batch (one query token per
+    request) whose metadata carries the decode block table and lengths (vLLM's TRT-LLM
+    decode metadata on Blackwell) runs on the split-K paged-decode kernel; prefill, mixed
+    batches, cascade and FlashInfer's own planned decode stay on FlashInfer."""
+    if _is_function_patch(original, "PagedAttentionDecode"):
+        return original
+    original_fn = cast(Callable[..., Any], original)
+
+    def forward(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale=None, output_block_scale=None, *rest, **kw):
+        call = lambda: original_fn(  # noqa: E731
+            self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale, output_block_scale, *rest, **kw
+        )
+        meta = attn_metadata
+        dec = getattr(meta, "decode", None)
+        if (
+            meta is None
+            or rest
+            or kw
+            or output_scale is not None
+            or output_block_scale is not None
+            or getattr(meta, "use_cascade", False)
+            or getattr(meta, "num_prefills", 1) != 0
+            or getattr(dec, "block_tables", None) is None
+            or getattr(dec, "seq_lens", None) is None
+            or not query.is_cuda
+            or not _attn_impl_supported(self, query.dtype, kv_cache, 1)
+        ):
+            return call()
+        n = int(meta.num_actual_tokens)
+        if int(getattr(meta, "num_decodes", -1)) != n or int(getattr(meta, "num_decode_tokens", -1)) != n:
+            return call()
+
+        def kernels():
+            _record_hit("PagedAttentionDecode", query)
+            paged_attention_decode_flash(
+                output, query, kv_cache, dec.seq_lens, dec.block_tables, n, self.scale, int(dec.max_seq_len), 1
             )
             return output
 
@@ -580,6 +651,7 @@ for _name, _attr_cls in (("MulAndSilu", "MulAndSilu"), ("GeluAndMul", "GeluAndMu
 
 _ROPE_MODULES = ("vllm.model_executor.layers.rotary_embedding.base",)
 _FA_MODULE = "vllm.v1.attention.backends.flash_attn"
+_FI_MODULE = "vllm.v1.attention.backends.flashinfer"
 _FUNCTION_PATCH_SPECS: tuple[FunctionPatchSpec, ...] = (
     *(
         FunctionPatchSpec("RoPE", mod, attr, "RotaryEmbedding", False, _build_rotary_forward)
@@ -588,6 +660,8 @@ _FUNCTION_PATCH_SPECS: tuple[FunctionPatchSpec, ...] = (
     ),
     FunctionPatchSpec("StoreKVCache", _FA_MODULE, "do_kv_cache_update", "FlashAttentionImpl", False, _build_flash_attn_kv_update),
     FunctionPatchSpec("PagedAttentionDecode", _FA_MODULE, "forward", "FlashAttentionImpl", False, _build_flash_attn_forward),
+    FunctionPatchSpec("StoreKVCache", _FI_MODULE, "do_kv_cache_update", "FlashInferImpl", False, _build_flashinfer_kv_update),
+    FunctionPatchSpec("PagedAttentionDecode", _FI_MODULE, "forward", "FlashInferImpl", False, _build_flashinfer_forward),
     *(
         FunctionPatchSpec("GateUpSiluAndMul", mod, "forward", cls, False, _build_mlp_forward)
         for mod, cls in (
