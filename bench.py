@@ -386,6 +386,31 @@ def per_op_table(dev, peaks) -> dict:
         [lambda i=i: torch.nn.functional.embedding(ids[i], wt) for i in range(8)], 80)
     del wt, outs
 
+    # decode at the vLLM end-to-end shape: 256 sequences, ctx U[512, 640] (prompt 512 + up
+    # to 128 generated), 32/8 heads, block 16: contexts that fit one chunk, so the split
+    # kernel writes the output itself; the K/V working set (~0.6 GB) exceeds L2
+    gs = torch.Generator().manual_seed(11)
+    ctx_s = torch.randint(512, 641, (256,), generator=gs)
+    nblk_s = (ctx_s + BLOCK - 1) // BLOCK
+    pool_s = int(nblk_s.sum())
+    ids_s = torch.randperm(pool_s, generator=gs).to(torch.int32)
+    tab_s = torch.zeros(256, 40, dtype=torch.int32)
+    off = 0
+    for i, nb_i in enumerate(nblk_s.tolist()):
+        tab_s[i, :nb_i] = ids_s[off : off + nb_i]
+        off += nb_i
+    kc_s = torch.randn(pool_s, BLOCK, HKV, HEAD, device=dev, generator=g, dtype=torch.bfloat16)
+    vc_s = torch.randn(pool_s, BLOCK, HKV, HEAD, device=dev, generator=g, dtype=torch.bfloat16)
+    q_s = torch.randn(256, HQ, HEAD, device=dev, generator=g, dtype=torch.bfloat16)
+    o_s = torch.empty_like(q_s)
+    seq_s, tab_d = ctx_s.to(torch.int32).to(dev), tab_s.to(dev)
+    ws_s = torch.empty(max(256, int(o.decode_workspace_size(256, HQ, HKV, HEAD, BLOCK, 640))), dtype=torch.uint8,
+                       device=dev)
+    nb = decode_bytes(ctx_s.to(torch.int32), HKV)
+    fns = [lambda: o.paged_attention_decode(o_s, q_s, kc_s, vc_s, seq_s, tab_d, 1.0 / math.sqrt(HEAD), 640, ws_s)]
+    report("paged decode bf16 B=256 ctx U[512,640] (vLLM e2e shape)", nb, time_graph(fns, 20))
+    del kc_s, vc_s
+
     # projection GEMM bf16 (fp32 accumulate)
     for (K, Nn, tag) in ((4096, 6144, "qkv"), (4096, 4096, "o_proj"), (4096, 28672, "gate_up"), (14336, 4096, "down")):
         for M in (1, 16, 128, 256, 1024, 8192):

@@ -87,19 +87,25 @@ def test_decode_capi_empty_sequence_fp16_and_strided_query():
 
 
 def test_decode_rejects_small_workspace_and_bad_shapes():
+    """A context of 600 tokens splits into several chunks (the partials need a workspace);
+    a 40-token one is a single chunk, written directly, and needs none."""
     dev = cuda_device()
-    q, kc, vc, seq, table = make_case([40], 4, 1, 8, seed=6)
+    q, kc, vc, seq, table = make_case([600], 4, 1, 40, seed=6)
     qd, kd, vd, sd, td = (t.to(dev) for t in (q, kc, vc, seq, table))
     out = torch.empty_like(qd)
     ws = torch.empty(256, dtype=torch.uint8, device=dev)
+    width = table.shape[1]  # 38 blocks
+    msl = width * 16
+    assert capi.lib().ntb200_paged_attention_decode_workspace_size(1, 4, 1, 128, 16, msl) > 256
+    assert capi.lib().ntb200_paged_attention_decode_workspace_size(1, 4, 1, 128, 16, 48) == 0
     with pytest.raises(capi.NtB200Error) as e:
         capi.call("ntb200_paged_attention_decode", ptr(out), ptr(qd), ptr(kd), ptr(vd), ptr(sd), ptr(td),
-                  1, 4, 1, 128, 16, 8, 3, 3, 48, 0.1, 512, 128, 512, 128, kd.stride(0), kd.stride(1),
+                  1, 4, 1, 128, 16, 40, width, width, msl, 0.1, 512, 128, 512, 128, kd.stride(0), kd.stride(1),
                   kd.stride(2), ptr(ws), 16, 1, stream())
     assert e.value.status == -4
     with pytest.raises(capi.NtB200Error) as e:
         capi.call("ntb200_paged_attention_decode", ptr(out), ptr(qd), ptr(kd), ptr(vd), ptr(sd), ptr(td),
-                  1, 4, 1, 64, 16, 8, 3, 3, 48, 0.1, 512, 128, 512, 128, kd.stride(0), kd.stride(1),
+                  1, 4, 1, 64, 16, 40, width, width, msl, 0.1, 512, 128, 512, 128, kd.stride(0), kd.stride(1),
                   kd.stride(2), ptr(ws), 256, 1, stream())
     assert e.value.status == -6
 
@@ -168,3 +174,24 @@ def test_decode_kv_head_sharding_matches_unsharded():
                                    vd[:, :, h0:h1].contiguous(), sd, td, scale))
         # the split size depends on the head count, so shards may round differently
         torch.testing.assert_close(torch.cat(parts, dim=1).float(), full.float(), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("ctx", [[0, 40, 200, 16, 255], [1, 256]])
+def test_decode_single_chunk_writes_output_directly(ctx):
+    """Contexts that fit one chunk: the split kernel writes the output rows (no partials,
+    no combine kernel, no workspace); an empty sequence gives a zero row."""
+    dev = cuda_device()
+    q, kc, vc, seq, table = make_case(ctx, 32, 8, 64, seed=17)
+    ref = oracle.paged_decode(q, kc, vc, seq, table, 0.09)
+    qd, kd, vd, sd, td = (t.to(dev) for t in (q, kc, vc, seq, table))
+    out = torch.full_like(qd, 3.0)
+    msl = table.shape[1] * 16
+    assert capi.lib().ntb200_paged_attention_decode_workspace_size(len(ctx), 32, 8, 128, 16, msl) == 0
+    capi.call("ntb200_paged_attention_decode", ptr(out), ptr(qd), ptr(kd), ptr(vd), ptr(sd), ptr(td),
+              len(ctx), 32, 8, 128, 16, 64, table.shape[1], table.shape[1], msl, 0.09,
+              32 * 128, 128, 32 * 128, 128, kd.stride(0), kd.stride(1), kd.stride(2), None, 0, 1, stream())
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.float().cpu(), ref, rtol=TOL, atol=TOL)
+    if ctx[0] == 0:
+        assert not out[0].any()
+    assert capi.read_device_error(stream()) == 0

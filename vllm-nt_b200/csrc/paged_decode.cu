@@ -127,6 +127,11 @@ struct DecodeParams {
   const int32_t* block_tables;
   float* part_o;    // [B][Hkv][max_chunks][G][128]
   float* part_lse;  // [B][Hkv][max_chunks][G]
+  // one chunk covers every sequence: the split kernel writes the output rows itself and
+  // no partials or combine kernel are needed
+  void* out;
+  int64_t o_seq_stride, o_head_stride;
+  int direct;
   int64_t q_seq_stride, q_head_stride;
   int64_t bt_stride;
   int64_t max_blocks_per_seq;
@@ -156,7 +161,16 @@ __global__ void __launch_bounds__(kThreads) paged_decode_split_kernel(
   int64_t total_blocks = (int64_t(ctx) + kBlockTokens - 1) / kBlockTokens;
   if (total_blocks > p.max_blocks_per_seq) total_blocks = p.max_blocks_per_seq;
   const int64_t blk_begin = int64_t(chunk) * p.chunk_blocks;
-  if (blk_begin >= total_blocks) return;  // uniform across the CTA
+  if (blk_begin >= total_blocks) {  // uniform across the CTA
+    if (p.direct) {  // an empty sequence attends to nothing: zero rows, as the combine writes
+      T* ob = static_cast<T*>(p.out) + int64_t(b) * p.o_seq_stride;
+      for (int idx = threadIdx.x; idx < p.group * kHeadDim; idx += kThreads) {
+        const int hh = idx / kHeadDim;
+        ob[int64_t(kvh * p.group + hh) * p.o_head_stride + (idx - hh * kHeadDim)] = Elem<T>::from_f(0.f);
+      }
+    }
+    return;
+  }
   const int nblk = static_cast<int>(
       total_blocks - blk_begin < p.chunk_blocks ? total_blocks - blk_begin : p.chunk_blocks);
   const int64_t tok_begin = blk_begin * kBlockTokens;
@@ -346,6 +360,26 @@ __global__ void __launch_bounds__(kThreads) paged_decode_split_kernel(
     }
   }
   named_barrier_sync(1, kConsumerWarps * 32);
+  if (p.direct) {
+    T* ob = static_cast<T*>(p.out) + int64_t(b) * p.o_seq_stride;
+    for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kConsumerWarps * 32) {
+      const int hh = idx / kHeadDim;
+      const int d = idx - hh * kHeadDim;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, sm_m[w * 8 + hh]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float mw = sm_m[w * 8 + hh];
+        const float sc = mw == -INFINITY ? 0.f : exp2f(mw - M);
+        L += sm_l[w * 8 + hh] * sc;
+        O += sm_o[(w * 8 + hh) * kHeadDim + d] * sc;
+      }
+      ob[int64_t(kvh * G + hh) * p.o_head_stride + d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
+    }
+    return;
+  }
   const int64_t unit = (int64_t(b) * p.num_kv_heads + kvh) * p.max_chunks + chunk;
   float* po = p.part_o + unit * G * kHeadDim;
   float* pl = p.part_lse + unit * G;
@@ -492,6 +526,7 @@ int64_t effective_max_seq_len(int64_t max_seq_len, int64_t max_blocks_per_seq,
 size_t workspace_bytes_for(int64_t num_seqs, int64_t num_q_heads, int64_t max_seq_len,
                            int chunk_tokens) {
   const int64_t max_chunks = ceil_div(max_seq_len, chunk_tokens);
+  if (max_chunks == 1) return 0;  // the split kernel writes the output directly
   const int64_t units = num_seqs * num_q_heads * max_chunks;  // per query head
   const int64_t o_bytes = units * kHeadDim * 4;
   const int64_t l_bytes = units * 4;
@@ -551,8 +586,8 @@ extern "C" int ntb200_paged_attention_decode(
   const int chunk_tokens = choose_chunk_tokens(num_seqs, num_kv_heads, msl);
   const int64_t max_chunks = ceil_div(msl, chunk_tokens);
   const size_t need = workspace_bytes_for(num_seqs, num_q_heads, msl, chunk_tokens);
-  if (workspace == nullptr || workspace_bytes < need ||
-      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need ||
+                   (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0))
     return fail(NTB200_ERR_WORKSPACE, "paged_decode: workspace needs %zu bytes (256-aligned), got %zu",
                 need, workspace_bytes);
   if (max_chunks > 65535) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "paged_decode: context too long");
@@ -584,6 +619,10 @@ extern "C" int ntb200_paged_attention_decode(
   prm.max_chunks = static_cast<int>(max_chunks);
   prm.scale_log2 = scale * kLog2e;
   prm.err = device_error_word();
+  prm.out = out;
+  prm.o_seq_stride = out_seq_stride;
+  prm.o_head_stride = out_head_stride;
+  prm.direct = max_chunks == 1 ? 1 : 0;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int smem = SmemLayout::kDynamicBytes;
@@ -600,7 +639,7 @@ extern "C" int ntb200_paged_attention_decode(
     st = launch_kernel("paged_decode_split", paged_decode_split_kernel<__half>, grid,
                        dim3(kThreads), smem, s, kmap, vmap, prm);
   }
-  if (st != NTB200_OK) return st;
+  if (st != NTB200_OK || prm.direct) return st;
 
   const int64_t warps = num_seqs * num_q_heads;
   const dim3 cgrid(static_cast<unsigned>(ceil_div(warps, 4)));
