@@ -386,6 +386,39 @@ def per_op_table(dev, peaks) -> dict:
         [lambda i=i: torch.nn.functional.embedding(ids[i], wt) for i in range(8)], 80)
     del wt, outs
 
+    # the same kernels at prefill-sized inputs, where launch latency no longer hides the
+    # bandwidth: silu_and_mul on a 2048-token gate_up output, RoPE over 16384 tokens of
+    # a qkv buffer, the KV store of 16384 tokens
+    xs3 = [torch.randn(2048, 28672, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(2)]
+    outs3 = [torch.empty(2048, 14336, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    nb = 2048 * 28672 * 2 + 2048 * 14336 * 2
+    report("silu_and_mul bf16 [2048,28672]", nb, time_graph([lambda i=i: o.silu_and_mul(outs3[i], xs3[i])
+                                                            for i in range(2)], 10))
+    lib("silu_and_mul bf16 [2048,28672]", "vllm _C.silu_and_mul",
+        vops and [lambda i=i: torch.ops._C.silu_and_mul(outs3[i], xs3[i]) for i in range(2)], 10)
+    del xs3, outs3
+    T3 = 16384
+    qkv3 = [torch.randn(T3, 48 * 128, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(2)]
+    pos3 = torch.randint(0, 4096, (T3,), device=dev, generator=g)
+    cache3 = cache.to(torch.bfloat16)
+    nb = 2 * T3 * 40 * 128 * 2 + T3 * 128 * 2 + T3 * 8
+    report("rope_neox bf16 16384 tokens of qkv [T,48*128]", nb,
+           time_graph([lambda i=i: o.rotary_embedding_neox(pos3, qkv3[i][:, :4096], qkv3[i][:, 4096:5120], cache3,
+                                                           128, 128) for i in range(2)], 10))
+    lib("rope_neox bf16 16384 tokens of qkv [T,48*128]", "vllm _C.rotary_embedding (neox)",
+        vops and [lambda i=i: vops.rotary_embedding(pos3, qkv3[i][:, :4096], qkv3[i][:, 4096:5120], 128, cache3, True)
+                  for i in range(2)], 10)
+    del qkv3
+    kc3 = torch.zeros(8192, 16, 8, 128, device=dev, dtype=torch.bfloat16)
+    vc3 = torch.zeros_like(kc3)
+    k3 = [torch.randn(T3, 8, 128, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(2)]
+    v3 = [torch.randn(T3, 8, 128, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(2)]
+    sl3 = torch.randperm(8192 * 16, device=dev, generator=g)[:T3]
+    nb = 2 * T3 * 8 * 128 * 2 * 2 + T3 * 8
+    report("reshape_and_cache bf16 16384x8x128", nb,
+           time_graph([lambda i=i: o.reshape_and_cache(k3[i], v3[i], kc3, vc3, sl3) for i in range(2)], 10))
+    del kc3, vc3, k3, v3
+
     # decode at the vLLM end-to-end shape: 256 sequences, ctx U[512, 640] (prompt 512 + up
     # to 128 generated), 32/8 heads, block 16: contexts that fit one chunk, so the split
     # kernel writes the output itself; the K/V working set (~0.6 GB) exceeds L2
@@ -432,6 +465,26 @@ def per_op_table(dev, peaks) -> dict:
             lib(name, "cuBLAS (torch.mm, the F.linear GEMM)",
                 [lambda w_=w_: torch.mm(x, w_.t(), out=out) for w_ in wts], iters)
             del x, wts, out
+
+    # LM head + greedy sampling, vocabulary 128256 x hidden 4096 (a 1.05 GB weight, beyond
+    # L2): the fused kernel keeps the logits on chip and emits the int64 token per row;
+    # the unfused pair writes [M, V] logits and reads them back for torch.argmax
+    V = 128256
+    w_lm = 0.02 * torch.randn(V, 4096, device=dev, generator=g, dtype=torch.bfloat16)
+    for M in (1, 16, 128, 256):
+        x = torch.randn(M, 4096, device=dev, generator=g, dtype=torch.bfloat16)
+        tok = torch.empty(M, dtype=torch.int64, device=dev)
+        logits = torch.empty(M, V, device=dev, dtype=torch.bfloat16)
+        name = f"lm_head+argmax V={V} M={M}"
+        nbytes = V * 4096 * 2 + M * 4096 * 2 + M * 8
+        ms = time_graph([lambda: o.linear_argmax(tok, x, w_lm)], 6)
+        report(name, nbytes, ms, {"TFLOP/s": round(2.0 * M * V * 4096 / (ms * 1e-3) / 1e12, 2)})
+        t_ours = time_graph([lambda: (o.linear(logits, x, w_lm, None, None), torch.argmax(logits, -1))], 6)
+        res[name]["unfused_ntb200_linear_plus_torch_argmax_us"] = round(t_ours * 1e3, 1)
+        lib(name, "cuBLAS torch.mm + torch.argmax",
+            [lambda: (torch.mm(x, w_lm.t(), out=logits), torch.argmax(logits, -1))], 6)
+        del x, tok, logits
+    del w_lm
     return res
 
 

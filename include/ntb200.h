@@ -202,6 +202,21 @@ int ntb200_linear_silu_and_mul(void* out, const void* x, const void* weight, int
                                int64_t out_row_stride, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * LM head + greedy argmax:  out_index[m] = argmax_v (x[m] . W[v])  over V vocabulary rows,
+ * comparing the logits rounded to the dtype (what vLLM's greedy sampler compares: the LM
+ * head writes dtype logits) with the first index winning ties, as torch.argmax does.  For
+ * M <= 256 the GEMM epilogue reduces each tile and folds it into a per-token key with a
+ * 64-bit atomicMax, so the [M, V] logits are never written; larger M computes the logits
+ * into the workspace and reduces each row.  Replaces the LMHead hook (vllm_nt/_ntops/
+ * patching.py:2682-2710) followed by the sampler's argmax (vllm:v1/sample/sampler.py
+ * greedy_sample) for greedy decoding.  out_index: int64 [M].  workspace:
+ * ntb200_linear_argmax_workspace_size(M, V, K) bytes, 256-byte aligned. */
+size_t ntb200_linear_argmax_workspace_size(int64_t M, int64_t V, int64_t K);
+int ntb200_linear_argmax(int64_t* out_index, const void* x, const void* weight, int64_t M, int64_t V,
+                         int64_t K, int64_t x_row_stride, int64_t weight_row_stride, void* workspace,
+                         size_t workspace_bytes, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * One-shot all-reduce over peer memory for the row-parallel projections of tensor
  * parallelism (o_proj and down under TP): replaces the NCCL all-reduce that vLLM's
  * RowParallelLinear issues after the GEMM (vllm:model_executor/layers/linear.py

@@ -84,6 +84,11 @@ def test_workspace_queries():
     # of the capacity rounded to 256 B
     assert lib.ntb200_allreduce_buffer_size(1000, 2, 4) == 8192 + 256 + 2 * 4 * 2048
     assert lib.ntb200_allreduce_buffer_size(1000, 2, 9) == 0
+    # LM-head argmax: one 8-byte key per row (256-aligned) while the logits stay on chip
+    # (M <= 256); beyond, the [M, V] logits as well
+    assert lib.ntb200_linear_argmax_workspace_size(256, 128256, 4096) == 2048
+    assert lib.ntb200_linear_argmax_workspace_size(300, 1000, 64) == 2560 + 600064
+    assert lib.ntb200_linear_argmax_workspace_size(0, 1000, 64) == 0
 
 
 def test_read_device_error_rejects_null():

@@ -152,3 +152,32 @@ def test_linear_silu_and_mul_matches_unfused_pair_exactly():
     fused = linear_silu_and_mul(x, w)
     unfused = silu_and_mul(linear(x, w))
     assert torch.equal(fused, unfused)
+
+
+@pytest.mark.parametrize("m,k,v", [(1, 4096, 32000), (7, 512, 32037), (256, 4096, 32000), (300, 512, 5000),
+                                   (64, 136, 1000)])
+def test_linear_argmax_matches_argmax_of_our_logits(m, k, v):
+    """Fused LM head + greedy argmax == torch.argmax of the logits the unfused GEMM writes
+    (same per-logit accumulation, logits compared at bf16, first index on ties)."""
+    from vllm_nt._ntops.torch.linear import linear, linear_argmax
+
+    dev = cuda_device()
+    gd = torch.Generator(device=dev).manual_seed(m + k + v)
+    x = torch.randn(m, k, generator=gd, device=dev, dtype=torch.bfloat16)
+    w = 0.05 * torch.randn(v, k, generator=gd, device=dev, dtype=torch.bfloat16)
+    got = linear_argmax(x, w)
+    want = torch.argmax(linear(x, w), dim=-1)
+    assert torch.equal(got, want)
+
+
+def test_linear_argmax_ties_take_the_first_index():
+    from vllm_nt._ntops.torch.linear import linear_argmax
+
+    dev = cuda_device()
+    x = torch.ones(3, 64, device=dev, dtype=torch.bfloat16)
+    w = torch.zeros(40000, 64, device=dev, dtype=torch.bfloat16)
+    w[[5, 17, 39999]] = 1.0       # three equal maxima for every row
+    w[33000] = -2.0
+    assert linear_argmax(x, w).tolist() == [5, 5, 5]
+    w[39999] = 2.0
+    assert linear_argmax(x, w).tolist() == [39999, 39999, 39999]

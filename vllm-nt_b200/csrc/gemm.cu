@@ -730,8 +730,39 @@ struct SmallParams {
   int k_steps_per_split;
   int k_steps_total;
   int64_t n_half;  // SwiGLU variant: output columns I (up rows start at row I of W)
+  unsigned long long* argmax_keys;  // ARGMAX variant: one packed (value, index) per token
   unsigned int* err;
 };
+
+// Greedy-argmax key of one logit: the logit rounded to T (the dtype the unfused LM head
+// writes and the sampler compares), mapped to an unsigned integer that orders like the
+// float (NaN above +inf, as torch.argmax ranks it), in the high half; the complement of
+// the vocabulary index in the low half, so that among equal logits the first index wins.
+// The signed-integer image of the rounded logit: larger logit, larger integer; -0 is
+// taken as +0 (they compare equal); a NaN rounds to the positive canonical NaN, which
+// sorts above +inf.
+template <typename T>
+__device__ __forceinline__ int32_t argmax_ord(float logit) {
+  uint32_t u = __float_as_uint(Elem<T>::round(logit));
+  u = u == 0x80000000u ? 0u : u;
+  return static_cast<int32_t>(u ^ ((static_cast<uint32_t>(static_cast<int32_t>(u) >> 31)) & 0x7FFFFFFFu));
+}
+
+__device__ __forceinline__ unsigned long long argmax_pack(int32_t ord, int64_t index) {
+  return (static_cast<unsigned long long>(static_cast<uint32_t>(ord) ^ 0x80000000u) << 32) |
+         (0xFFFFFFFFu - static_cast<uint32_t>(index));
+}
+
+template <typename T>
+__device__ __forceinline__ unsigned long long argmax_key(float logit, int64_t index) {
+  return argmax_pack(argmax_ord<T>(logit), index);
+}
+
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int off) {
+  const uint32_t lo = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v), off);
+  const uint32_t hi = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), off);
+  return (static_cast<unsigned long long>(hi) << 32) | lo;
+}
 
 __device__ __forceinline__ void tmem_ld_16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -767,7 +798,10 @@ __device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t local_addr, uint32_t r
 // SWIGLU (NT = 2, no split): the CTA's two weight tiles are gate rows [128*g, +128) and
 // the matching up rows [I + 128*g, +128), so each epilogue thread holds x.gate and x.up
 // of the same output column.
-template <typename T, int MP, int NT, bool BIG, bool SWIGLU = false>
+// ARGMAX (no split): instead of writing logits, every warp reduces its 32 weight rows
+// (vocabulary entries) per token to the best key and folds it into that token's key with
+// one 64-bit atomicMax; the [M, N] logits are never written.
+template <typename T, int MP, int NT, bool BIG, bool SWIGLU = false, bool ARGMAX = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
     const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
     const SmallParams p) {
@@ -870,7 +904,48 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
     tc_fence_after();
   }
 
-  if (SWIGLU) {
+  if (ARGMAX) {
+    // no split (the host plans none).  Per token, each thread keeps the best of its NT
+    // weight rows as a signed ordinal (rows ascend with t, so a strict > keeps the first of
+    // equal logits); the warp then takes the max ordinal and, among the lanes holding it,
+    // the smallest (t, lane) -- the smallest vocabulary index -- with two redux.sync.
+    if (epilogue) {
+      const int64_t row0 = int64_t(tile0) * BM + quad * 32;  // vocabulary index of (t=0, lane 0)
+#pragma unroll 1
+      for (int c = 0; c < MP / 16; ++c) {
+        int32_t bo[16];
+        uint32_t bt[16];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          uint32_t r[16];
+          __syncwarp();
+          tmem_ld_16(tmem_base + (uint32_t(quad * 32) << 16) + t * MP + c * 16, r);
+          const bool valid = acc_ok && row0 + t * BM + lane < p.N;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int32_t o = valid ? argmax_ord<T>(__uint_as_float(r[i])) : INT32_MIN;
+            if (t == 0) {
+              bo[i] = o;
+              bt[i] = 0;
+            } else if (o > bo[i]) {
+              bo[i] = o;
+              bt[i] = t;
+            }
+          }
+        }
+        unsigned long long mine = 0ull;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int32_t m = __reduce_max_sync(0xffffffffu, bo[i]);
+          const uint32_t w = __reduce_min_sync(0xffffffffu, bo[i] == m ? bt[i] * 32u + uint32_t(lane) : 0xFFFFFFFFu);
+          if (lane == i && m != INT32_MIN) mine = argmax_pack(m, row0 + int64_t(w >> 5) * BM + (w & 31u));
+        }
+        const int64_t m = c * 16 + lane;
+        if (lane < 16 && m < p.M && mine != 0ull) atomicMax(p.argmax_keys + m, mine);
+      }
+      tc_fence_before();
+    }
+  } else if (SWIGLU) {
     // no split (the host plans none): silu(gate) * up straight from TMEM
     if (epilogue) {
       const int64_t n = int64_t(tile0 / NT) * BM + n_local;
@@ -976,11 +1051,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_small_m_kernel(
   }
 }
 
-template <typename T, int MP, int NT, bool BIG, bool SWIGLU = false>
+template <typename T, int MP, int NT, bool BIG, bool SWIGLU = false, bool ARGMAX = false>
 int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, cudaStream_t s,
                  int attr_slot) {
   using L = SmallSmem<MP, NT, BIG>;
-  const void* fn = reinterpret_cast<const void*>(gemm_small_m_kernel<T, MP, NT, BIG, SWIGLU>);
+  const void* fn = reinterpret_cast<const void*>(gemm_small_m_kernel<T, MP, NT, BIG, SWIGLU, ARGMAX>);
   int st = ensure_smem_attribute(fn, L::kDynamicBytes, attr_slot);
   if (st != NTB200_OK) return st;
   const int groups = (prm.n_tiles + NT - 1) / NT;
@@ -997,7 +1072,8 @@ int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallPa
   set_pdl_attribute(attr[1]);
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_small_m_kernel<T, MP, NT, BIG, SWIGLU>, wmap, xmap, prm);
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, gemm_small_m_kernel<T, MP, NT, BIG, SWIGLU, ARGMAX>, wmap, xmap, prm);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(NTB200_ERR_CUDA, "linear (small M): launch failed: %s", cudaGetErrorString(e));
@@ -1224,8 +1300,140 @@ int dispatch_small_swiglu(const CUtensorMap& wmap, const CUtensorMap& xmap, cons
   }
 }
 
+// ---- LM head + greedy argmax -------------------------------------------------------
+
+template <typename T, int MP>
+int launch_small_argmax(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, cudaStream_t s,
+                        int slot) {
+  const int64_t groups = (prm.n_tiles + 1) / 2;
+  if (groups <= num_sms()) return launch_small<T, MP, 2, true, false, true>(wmap, xmap, prm, s, slot + 1);
+  return launch_small<T, MP, 2, false, false, true>(wmap, xmap, prm, s, slot);
+}
+
+template <typename T>
+int dispatch_small_argmax(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallParams& prm, int mp,
+                          cudaStream_t s, int slot_base) {
+  switch (mp) {
+    case 16: return launch_small_argmax<T, 16>(wmap, xmap, prm, s, slot_base + 0);
+    case 32: return launch_small_argmax<T, 32>(wmap, xmap, prm, s, slot_base + 2);
+    case 64: return launch_small_argmax<T, 64>(wmap, xmap, prm, s, slot_base + 4);
+    case 128: return launch_small_argmax<T, 128>(wmap, xmap, prm, s, slot_base + 6);
+    default: return launch_small_argmax<T, 256>(wmap, xmap, prm, s, slot_base + 8);
+  }
+}
+
+// token keys -> vocabulary indices
+__global__ void __launch_bounds__(256) argmax_finalize_kernel(const unsigned long long* __restrict__ keys,
+                                                              int64_t* __restrict__ out, int64_t M) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t m = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (m < M) out[m] = static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(keys[m]));
+}
+
+// argmax of one row of logits already in memory (the path for M > 256): one CTA per row
+template <typename T>
+__global__ void __launch_bounds__(512) row_argmax_kernel(const T* __restrict__ logits, int64_t ld, int64_t V,
+                                                          int64_t* __restrict__ out) {
+  __shared__ unsigned long long red[16];
+  pdl_trigger();
+  pdl_wait();
+  const T* row = logits + int64_t(blockIdx.x) * ld;
+  unsigned long long best = 0ull;
+  for (int64_t j = threadIdx.x; j < V; j += blockDim.x) {
+    const unsigned long long k = argmax_key<T>(Elem<T>::to_f(row[j]), j);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const unsigned long long o2 = shfl_xor_u64(best, off);
+    best = o2 > best ? o2 : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    best = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const unsigned long long o2 = shfl_xor_u64(best, off);
+      best = o2 > best ? o2 : best;
+    }
+    if (threadIdx.x == 0) out[blockIdx.x] = static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(best));
+  }
+}
+
 }  // namespace
 }  // namespace ntb200
+
+extern "C" size_t ntb200_linear_argmax_workspace_size(int64_t M, int64_t V, int64_t K) {
+  using ntb200::ceil_div;
+  (void)K;
+  if (M <= 0 || V <= 0) return 0;
+  const size_t keys = static_cast<size_t>(ceil_div(M * 8, 256) * 256);
+  if (M <= 256) return keys;
+  return keys + static_cast<size_t>(ceil_div(M * V * 2, 256) * 256);
+}
+
+extern "C" int ntb200_linear_argmax(int64_t* out_index, const void* x, const void* weight, int64_t M, int64_t V,
+                                    int64_t K, int64_t x_row_stride, int64_t weight_row_stride, void* workspace,
+                                    size_t workspace_bytes, int dtype, void* stream) {
+  using namespace ntb200;
+  if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
+    return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "linear_argmax: dtype %d (bf16/f16 only)", dtype);
+  if (M < 0 || V <= 0 || K <= 0) return fail(NTB200_ERR_INVALID_ARGUMENT, "linear_argmax: bad shape");
+  if (M == 0) return NTB200_OK;
+  if (V > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear_argmax: vocabulary too large");
+  if (!out_index || !x || !weight) return fail(NTB200_ERR_INVALID_ARGUMENT, "linear_argmax: null pointer");
+  if (x_row_stride < K || weight_row_stride < K)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "linear_argmax: row stride too small");
+  if (!aligned16(x) || !aligned16(weight) || x_row_stride % 8 != 0 || weight_row_stride % 8 != 0)
+    return fail(NTB200_ERR_MISALIGNED, "linear_argmax: x/weight must be 16-byte aligned with row strides %% 8 == 0");
+  const size_t need = ntb200_linear_argmax_workspace_size(M, V, K);
+  if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(NTB200_ERR_WORKSPACE, "linear_argmax: workspace needs %zu bytes (256-aligned), got %zu", need,
+                workspace_bytes);
+  const bool bf16 = dtype == NTB200_DTYPE_BF16;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned long long* keys = static_cast<unsigned long long*>(workspace);
+  if (M > 256) {
+    // logits through the ordinary GEMM, then one CTA per row
+    void* logits = static_cast<char*>(workspace) + ceil_div(M * 8, 256) * 256;
+    int st = ntb200_linear(logits, x, weight, nullptr, M, V, K, x_row_stride, weight_row_stride, V, nullptr, 0,
+                           dtype, stream);
+    if (st != NTB200_OK) return st;
+    if (bf16)
+      return launch_kernel("linear_argmax", row_argmax_kernel<__nv_bfloat16>, dim3(unsigned(M)), dim3(512), 0, s,
+                           static_cast<const __nv_bfloat16*>(logits), V, V, out_index);
+    return launch_kernel("linear_argmax", row_argmax_kernel<__half>, dim3(unsigned(M)), dim3(512), 0, s,
+                         static_cast<const __half*>(logits), V, V, out_index);
+  }
+  if (cudaMemsetAsync(keys, 0, static_cast<size_t>(M) * 8, s) != cudaSuccess)
+    return fail(NTB200_ERR_CUDA, "linear_argmax: clearing the keys: %s", cudaGetErrorString(cudaGetLastError()));
+  const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  CUtensorMap wmap, xmap;
+  int st = make_kmajor_map(&wmap, weight, bf16, V, K, weight_row_stride, BM);
+  if (st != NTB200_OK) return st;
+  st = make_kmajor_map(&xmap, x, bf16, M, K, x_row_stride, mp);
+  if (st != NTB200_OK) return st;
+  SmallParams sp;
+  sp.out = nullptr;
+  sp.bias = nullptr;
+  sp.M = M;
+  sp.N = V;
+  sp.out_stride = 0;
+  sp.n_tiles = static_cast<int>(ceil_div(V, BM));
+  sp.splits = 1;
+  sp.k_steps_total = static_cast<int>(ceil_div(K, BK));
+  sp.k_steps_per_split = sp.k_steps_total;
+  sp.n_half = 0;
+  sp.argmax_keys = keys;
+  sp.err = device_error_word();
+  st = bf16 ? dispatch_small_argmax<__nv_bfloat16>(wmap, xmap, sp, mp, s, 70)
+            : dispatch_small_argmax<__half>(wmap, xmap, sp, mp, s, 80);
+  if (st != NTB200_OK) return st;
+  return launch_kernel("linear_argmax", argmax_finalize_kernel, dim3(unsigned(ceil_div(M, 256))), dim3(256), 0, s,
+                       static_cast<const unsigned long long*>(keys), out_index, M);
+}
 
 extern "C" int ntb200_linear_silu_and_mul(void* out, const void* x, const void* weight, int64_t M,
                                           int64_t I, int64_t K, int64_t x_row_stride,
@@ -1263,6 +1471,7 @@ extern "C" int ntb200_linear_silu_and_mul(void* out, const void* x, const void* 
     sp.k_steps_total = static_cast<int>(ceil_div(K, BK));
     sp.k_steps_per_split = sp.k_steps_total;
     sp.n_half = I;
+    sp.argmax_keys = nullptr;
     sp.err = device_error_word();
     return bf16 ? dispatch_small_swiglu<__nv_bfloat16>(wmap, xmap, sp, mp, s, 50)
                 : dispatch_small_swiglu<__half>(wmap, xmap, sp, mp, s, 60);
@@ -1342,6 +1551,7 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     sp.n_tiles = static_cast<int>(n_tiles);
     sp.k_steps_total = ksteps;
     sp.n_half = 0;
+    sp.argmax_keys = nullptr;
     sp.err = device_error_word();
     SmallParams sp_big = sp, sp_small = sp;
     sp_big.splits = splits_big;

@@ -361,6 +361,29 @@ void linear_silu_and_mul(at::Tensor out, const at::Tensor& x_in, const at::Tenso
         "linear_silu_and_mul");
 }
 
+// out_index [M] (int64) = greedy argmax over the vocabulary of x [M, K] . weight [V, K]^T
+void linear_argmax(at::Tensor out_index, const at::Tensor& x_in, const at::Tensor& weight) {
+  require_rows(weight, "weight");
+  require_cuda(out_index, "out_index");
+  at::Tensor x = x_in;
+  Rows xr = rows_of(x, "x");
+  if ((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15u) != 0 || xr.stride % 8 != 0) {
+    x = at::empty(x_in.sizes(), x_in.options());
+    x.copy_(x_in);
+    xr = rows_of(x, "x");
+  }
+  TORCH_CHECK(weight.size(1) == xr.cols && weight.scalar_type() == x.scalar_type() &&
+                  out_index.scalar_type() == at::kLong && out_index.is_contiguous() && out_index.numel() == xr.rows,
+              "ntb200.linear_argmax: x [..., K], weight [V, K] of one dtype, out_index int64 [rows]");
+  c10::cuda::CUDAGuard guard(x.device());
+  const size_t need = ntb200_linear_argmax_workspace_size(xr.rows, weight.size(0), xr.cols);
+  at::Tensor ws = at::empty({static_cast<int64_t>(need > 256 ? need : 256)}, x.options().dtype(at::kByte));
+  check(ntb200_linear_argmax(out_index.data_ptr<int64_t>(), x.data_ptr(), weight.data_ptr(), xr.rows,
+                             weight.size(0), xr.cols, xr.stride, weight.stride(0), ws.data_ptr(),
+                             static_cast<size_t>(ws.numel()), dtype_code(x), stream_of(x)),
+        "linear_argmax");
+}
+
 // out = sum over ranks of their partials (see ntb200_allreduce_oneshot); peer_buffers is an
 // int64 CUDA tensor of the world's buffer addresses.
 void allreduce_oneshot(at::Tensor out, const at::Tensor& partial, const at::Tensor& peer_buffers, int64_t capacity,
@@ -423,6 +446,7 @@ TORCH_LIBRARY(ntb200, m) {
   m.def("linear(Tensor(a!) out, Tensor x, Tensor weight, Tensor? bias, Tensor(b!)? workspace) -> ()");
   m.def("linear_workspace_size(int m, int n, int k) -> int", &linear_workspace_size);
   m.def("linear_silu_and_mul(Tensor(a!) out, Tensor x, Tensor weight) -> ()");
+  m.def("linear_argmax(Tensor(a!) out_index, Tensor x, Tensor weight) -> ()");
   m.def(
       "allreduce_oneshot(Tensor(a!) out, Tensor partial, Tensor peer_buffers, int capacity, int rank, "
       "int world_size) -> ()");
@@ -442,4 +466,5 @@ TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("linear", &linear);
   m.impl("allreduce_oneshot", &allreduce_oneshot);
   m.impl("linear_silu_and_mul", &linear_silu_and_mul);
+  m.impl("linear_argmax", &linear_argmax);
 }

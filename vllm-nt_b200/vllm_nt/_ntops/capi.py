@@ -74,6 +74,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ntb200_linear_silu_and_mul": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p]
     ),
+    "ntb200_linear_argmax_workspace_size": (c_size_t, [c_int64, c_int64, c_int64]),
+    "ntb200_linear_argmax": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_size_t,
+                c_int, c_void_p]
+    ),
     "ntb200_allreduce_buffer_size": (c_size_t, [c_int64, c_int, c_int]),
     "ntb200_allreduce_oneshot": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p]

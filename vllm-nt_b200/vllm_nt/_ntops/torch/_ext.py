@@ -40,6 +40,7 @@ def _register_fakes() -> None:
         "linear",
         "allreduce_oneshot",
         "linear_silu_and_mul",
+        "linear_argmax",
     ):
         torch.library.register_fake(f"ntb200::{name}")(nothing)
 

@@ -40,6 +40,17 @@ def linear_silu_and_mul(input: torch.Tensor, gate_up: torch.Tensor) -> torch.Ten
     return out
 
 
+def linear_argmax(input: torch.Tensor, lm_head: torch.Tensor) -> torch.Tensor:
+    """Greedy next tokens: argmax over the vocabulary of input @ lm_head^T (int64, one per
+    row of input), with the logits compared at input's dtype and the first index winning
+    ties; for up to 256 rows the logits are never written to memory."""
+    w = _k_contiguous(lm_head)
+    x = input if input.is_contiguous() else input.contiguous()
+    out = torch.empty(x.shape[:-1], dtype=torch.int64, device=x.device)
+    ops().linear_argmax(out, x, w)
+    return out
+
+
 def matmul(lhs: torch.Tensor, rhs: torch.Tensor) -> torch.Tensor:
     """lhs [M, K] @ rhs [K, N]; rhs is transposed once into the [N, K] operand layout."""
     return linear(lhs, rhs.t().contiguous())
