@@ -177,6 +177,48 @@ int ntb200_paged_attention_decode_noalloc(
     int64_t cache_page_stride, int64_t cache_head_stride, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Varlen paged prefill attention (a flash-attention forward on the tcgen05 tensor cores):
+ *   out[t, h] = softmax(scale * q[t, h] . K_b^T + mask) V_b
+ * for the queries t of sequence b (rows query_start_loc[b] .. query_start_loc[b+1] of
+ * query/out, [num_tokens, num_q_heads, head_size]) over the seq_lens[b] tokens cached for b
+ * (the queries' own K/V included, as the last q_len of them), K/V head
+ * h / (num_q_heads / num_kv_heads).  causal != 0: query i of a sequence with q_len queries
+ * sits at position seq_lens[b] - q_len + i and sees keys up to that position (vLLM's
+ * FlashAttention rule; it covers a cached prefix and chunked prefill).  fp32 softmax and
+ * accumulation, P rounded to the input type for the P.V product.  Rows that see no key are
+ * zero.  Caches and block tables as ntb200_paged_attention_decode; head_size 128,
+ * block_size 16; dtype BF16 or F16; all pointers 16-byte aligned, strides multiples of 8.
+ * max_query_len bounds every q_len.  Out-of-range page ids and context lengths set
+ * NTB200_DEVERR_INDEX_RANGE (the pages read as zeros).  No workspace.
+ * Replaces vllm_nt/_ntops/kernels/attention.py:10-94 (_VarLen) with the K/V gather of
+ * vllm_nt/_ntops/torch/kv_cache.py:24-63, reached from vllm_nt/_ntops/patching.py:639-671. */
+int ntb200_paged_attention_prefill(
+    void* out, const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* block_tables,
+    int64_t num_seqs, int64_t num_tokens, int64_t num_q_heads, int64_t num_kv_heads,
+    int64_t head_size, int64_t block_size, int64_t num_blocks, int64_t max_blocks_per_seq,
+    int64_t block_table_stride, int64_t max_query_len, float scale, int causal,
+    int64_t q_token_stride, int64_t q_head_stride, int64_t out_token_stride,
+    int64_t out_head_stride, int64_t cache_block_stride, int64_t cache_page_stride,
+    int64_t cache_head_stride, int dtype, void* stream);
+
+/* The same attention over contiguous varlen K/V instead of the paged cache: key/value
+ * [num_k_tokens, num_kv_heads, 128], sequence b's keys at rows cu_seqlens_k[b] ..
+ * cu_seqlens_k[b+1] (its context), its queries at rows cu_seqlens_q[b] .. cu_seqlens_q[b+1]
+ * of query/out; causal as above (aligned to the end of each context).
+ * Replaces vllm_nt/_ntops/torch/attention.py:9-46 (flash_attn_varlen_func) and
+ * vllm_nt/_ntops/kernels/attention.py:10-94, reached from
+ * vllm_nt/_ntops/oot_support.py:88-109 (paged_attention_prefill). */
+int ntb200_flash_attn_varlen(
+    void* out, const void* query, const void* key, const void* value,
+    const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int64_t num_seqs,
+    int64_t num_q_tokens, int64_t num_k_tokens, int64_t num_q_heads, int64_t num_kv_heads,
+    int64_t head_size, int64_t max_query_len, float scale, int causal, int64_t q_token_stride,
+    int64_t q_head_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t v_token_stride, int64_t v_head_stride, int64_t out_token_stride,
+    int64_t out_head_stride, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Dense projection  out[M, N] = x[M, K] . weight[N, K]^T (+ bias[N]),  fp32 accumulate,
  * tcgen05/TMEM tensor cores fed by TMA.  dtype BF16 or F16; K a multiple of 8, rows 16-byte
  * aligned.  bias may be NULL.

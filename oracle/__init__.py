@@ -14,23 +14,29 @@ the plugin patches; other paths are inside the vllm_nt reference project):
 * the KV-cache store and the embedding gather are byte copies (numpy on raw 16-bit views),
   exact;
 * paged decode follows the reference's own test oracle (gather the cached tokens through
-  the block table, fp32 softmax attention per sequence, GQA by head grouping).
+  the block table, fp32 softmax attention per sequence, GQA by head grouping);
+* varlen prefill gathers the cached tokens the same way and applies fp32 softmax attention
+  with the causal mask aligned to the end of each context (vLLM's rule; the reference's
+  start-aligned mask is the same when a sequence has as many keys as queries).
 
 Pinning: tests/golden/make_golden.py runs vLLM's real forward_native code (and torch's
-scaled_dot_product_attention for decode) on seeded inputs and commits the outputs;
+scaled_dot_product_attention for decode and prefill) on seeded inputs and commits the outputs;
 tests/test_oracle.py checks these functions against those fixtures and against the
 known-answer cases of the reference's tests (tests/test_kv_cache.py:26-45,
-tests/test_rope.py:26-46, tests/test_attention.py:75-104, tests/test_oot.py:33-177).
+tests/test_rope.py:26-46, tests/test_attention.py:57-104, tests/test_oot.py:33-177).
 """
 
 from oracle.ops import (  # noqa: F401
     build_cos_sin_cache,
     embedding,
     fused_add_rms_norm,
+    gather_paged_kv,
     linear,
     paged_decode,
+    paged_prefill,
     reshape_and_cache,
     rms_norm,
     rope_neox,
     silu_and_mul,
+    varlen_attention,
 )

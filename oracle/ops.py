@@ -184,6 +184,86 @@ def paged_decode(
     return out
 
 
+def varlen_attention(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    cu_seqlens_q: torch.Tensor,
+    cu_seqlens_k: torch.Tensor,
+    scale: float | None = None,
+    causal: bool = True,
+) -> torch.Tensor:
+    """query [Tq, Hq, D], key/value [Tk, Hkv, D]; returns fp32 [Tq, Hq, D].  Sequence b's
+    queries are rows cu_seqlens_q[b] .. [b+1], its keys rows cu_seqlens_k[b] .. [b+1]
+    (q_len and ctx of them).  s = scale * q . k in fp32; with ``causal`` query i sits at
+    position ctx - q_len + i and sees keys 0 .. that position (vLLM's FlashAttention rule);
+    softmax; o = p . v.  A row that sees no key is zero.  Follows the online-softmax
+    recurrence of vllm_nt/_ntops/kernels/attention.py:40-82 in closed form, with the mask
+    aligned to the end of the keys instead of the start (attention.py:61-63); the two agree
+    when ctx == q_len, the case the reference's own test (tests/test_attention.py:57-72)
+    covers."""
+    tq, hq, d = query.shape
+    hkv = key.shape[1]
+    group = hq // hkv
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    out = torch.zeros((tq, hq, d), dtype=torch.float32)
+    for b in range(cu_seqlens_q.numel() - 1):
+        q0, q1 = int(cu_seqlens_q[b]), int(cu_seqlens_q[b + 1])
+        k0, k1 = int(cu_seqlens_k[b]), int(cu_seqlens_k[b + 1])
+        q_len, ctx = q1 - q0, k1 - k0
+        if q_len <= 0 or ctx <= 0:
+            continue
+        q = query[q0:q1].to(torch.float32).reshape(q_len, hkv, group, d)
+        k = key[k0:k1].to(torch.float32)  # [ctx, Hkv, D]
+        v = value[k0:k1].to(torch.float32)
+        s = torch.einsum("qhgd,khd->hgqk", q, k) * scale
+        if causal:
+            pos = torch.arange(q_len) + (ctx - q_len)
+            visible = torch.arange(ctx)[None, :] <= pos[:, None]  # [q_len, ctx]
+            s = s.masked_fill(~visible, float("-inf"))
+            seen = visible.any(dim=1)
+        else:
+            seen = torch.ones(q_len, dtype=torch.bool)
+        p = torch.softmax(s, dim=-1).nan_to_num(0.0)
+        o = torch.einsum("hgqk,khd->qhgd", p, v).reshape(q_len, hq, d)
+        out[q0:q1] = o * seen[:, None, None]
+    return out
+
+
+def gather_paged_kv(key_cache: torch.Tensor, value_cache: torch.Tensor, seq_lens: torch.Tensor,
+                    block_table: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Each sequence's first seq_lens[b] cached tokens, block by block, concatenated:
+    (key [sum, Hkv, D], value, cu_seqlens [B + 1] int32), as
+    vllm_nt/_ntops/torch/kv_cache.py:24-63 gathers them for the reference's prefill."""
+    bs = key_cache.shape[1]
+    ks, vs, cu = [], [], [0]
+    for b in range(seq_lens.numel()):
+        n = max(int(seq_lens[b]), 0)
+        nblk = (n + bs - 1) // bs
+        ids = block_table[b, :nblk].long()
+        ks.append(key_cache[ids].reshape(nblk * bs, *key_cache.shape[2:])[:n])
+        vs.append(value_cache[ids].reshape(nblk * bs, *value_cache.shape[2:])[:n])
+        cu.append(cu[-1] + n)
+    return torch.cat(ks), torch.cat(vs), torch.tensor(cu, dtype=torch.int32)
+
+
+def paged_prefill(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    query_start_loc: torch.Tensor,
+    seq_lens: torch.Tensor,
+    block_table: torch.Tensor,
+    scale: float | None = None,
+    causal: bool = True,
+) -> torch.Tensor:
+    """query [T, Hq, D]; caches [blocks, bs, Hkv, D]: the reference's prefill path over the
+    cache (vllm_nt/_ntops/patching.py:652-667: gather the cached tokens, then varlen
+    attention) with vLLM's end-aligned causal mask.  Returns fp32 [T, Hq, D]."""
+    k, v, cu_k = gather_paged_kv(key_cache, value_cache, seq_lens, block_table)
+    return varlen_attention(query, k, v, query_start_loc, cu_k, scale, causal)
+
+
 # --------------------------------------------------------------------------------------
 # Dense projection  (vllm_nt/_ntops/kernels/linear.py:9-85; vllm:model_executor/layers/utils.py
 #                    -> F.linear)

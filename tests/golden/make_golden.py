@@ -19,6 +19,7 @@ bf16 tensors are stored as their uint16 bit patterns (key suffix ``__bf16``).
 
 from __future__ import annotations
 
+import itertools
 import math
 from pathlib import Path
 
@@ -125,6 +126,32 @@ def main() -> None:
         outs.append(o[0, :, 0, :])
     save("paged_decode_bf16", query=qd, key_cache=kcd, value_cache=vcd, seq_lens=seq, block_table=table,
          out=torch.stack(outs))
+
+    # varlen prefill over a paged cache: Hq=4, Hkv=2, D=16, bs=4; (q_len, ctx) per sequence
+    # (3, 3) a plain prompt, (2, 7) a prompt after a 5-token cached prefix, (1, 6) a decode
+    # row, (0, 4) no queries; causal, aligned to the end of each context (an explicit mask,
+    # since SDPA's is_causal aligns to the start)
+    hq, hkv, d, bs, nb = 4, 2, 16, 4, 12
+    qlens, ctxs = [3, 2, 1, 0], [3, 7, 6, 4]
+    cu_q = torch.tensor([0] + list(itertools.accumulate(qlens)), dtype=torch.int32)
+    qp = torch.randn(int(cu_q[-1]), hq, d, generator=g).to(torch.bfloat16)
+    kcp = torch.randn(nb, bs, hkv, d, generator=g).to(torch.bfloat16)
+    vcp = torch.randn(nb, bs, hkv, d, generator=g).to(torch.bfloat16)
+    seqp = torch.tensor(ctxs, dtype=torch.int32)
+    tablep = torch.randperm(nb, generator=g)[:8].reshape(4, 2).to(torch.int32)
+    outp = torch.zeros(int(cu_q[-1]), hq, d)
+    for b, (ql, n) in enumerate(zip(qlens, ctxs)):
+        if ql == 0:
+            continue
+        ids = tablep[b].long()
+        kk = kcp[ids].reshape(-1, hkv, d)[:n].float().transpose(0, 1).repeat_interleave(hq // hkv, dim=0)
+        vv = vcp[ids].reshape(-1, hkv, d)[:n].float().transpose(0, 1).repeat_interleave(hq // hkv, dim=0)
+        qq = qp[int(cu_q[b]) : int(cu_q[b + 1])].float().transpose(0, 1)  # [Hq, q_len, D]
+        mask = torch.ones(ql, n, dtype=torch.bool).tril(diagonal=n - ql)
+        o = F.scaled_dot_product_attention(qq[None], kk[None], vv[None], attn_mask=mask, scale=1.0 / math.sqrt(d))
+        outp[int(cu_q[b]) : int(cu_q[b + 1])] = o[0].transpose(0, 1)
+    save("paged_prefill_bf16", query=qp, key_cache=kcp, value_cache=vcp, query_start_loc=cu_q, seq_lens=seqp,
+         block_table=tablep, out=outp)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 

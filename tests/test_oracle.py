@@ -148,3 +148,60 @@ def test_cos_sin_cache_matches_vllm_definition():
     assert c.shape == (4096, 128)
     torch.testing.assert_close(c[:, :64], torch.cos(torch.arange(4096).float()[:, None] * inv), rtol=0, atol=0)
     assert math.isclose(float(c[0, 0]), 1.0)
+
+
+def test_paged_prefill_matches_sdpa_golden():
+    g = golden("paged_prefill_bf16")
+    out = oracle.paged_prefill(g["query"], g["key_cache"], g["value_cache"], g["query_start_loc"], g["seq_lens"],
+                               g["block_table"])
+    torch.testing.assert_close(out, g["out"], rtol=1e-5, atol=1e-5)
+
+
+def test_varlen_reference_known_answer():
+    """vllm_nt/tests/test_attention.py:57-72: q/k/v (5, 2, 8), cu_q = cu_k = [0, 2, 5],
+    causal, checked against SDPA(is_causal=True) per sequence (equal q and k lengths, where
+    the start- and end-aligned masks coincide)."""
+    g = seeded(3)
+    q = torch.randn((5, 2, 8), generator=g)
+    k = torch.randn((5, 2, 8), generator=g)
+    v = torch.randn((5, 2, 8), generator=g)
+    cu = torch.tensor([0, 2, 5], dtype=torch.int32)
+    out = oracle.varlen_attention(q, k, v, cu, cu)
+    for b in range(2):
+        sl = slice(int(cu[b]), int(cu[b + 1]))
+        ref = F.scaled_dot_product_attention(q[sl].transpose(0, 1)[None], k[sl].transpose(0, 1)[None],
+                                             v[sl].transpose(0, 1)[None], is_causal=True)[0].transpose(0, 1)
+        torch.testing.assert_close(out[sl], ref, rtol=1e-5, atol=1e-5)
+
+
+def test_varlen_end_aligned_mask_with_prefix():
+    """With a cached prefix (ctx > q_len) the last query sees every key (a decode step) and
+    the first sees ctx - q_len + 1 of them; the result equals attention over that prefix of
+    the keys."""
+    g = seeded(4)
+    q = torch.randn((3, 4, 16), generator=g)
+    k = torch.randn((10, 2, 16), generator=g)
+    v = torch.randn((10, 2, 16), generator=g)
+    out = oracle.varlen_attention(q, k, v, torch.tensor([0, 3], dtype=torch.int32),
+                                  torch.tensor([0, 10], dtype=torch.int32))
+    for i in range(3):
+        n = 10 - 3 + i + 1
+        kk = k[:n].repeat_interleave(2, dim=1).transpose(0, 1)  # [Hq, n, D]
+        vv = v[:n].repeat_interleave(2, dim=1).transpose(0, 1)
+        ref = F.scaled_dot_product_attention(q[i][:, None], kk, vv)[:, 0]
+        torch.testing.assert_close(out[i], ref, rtol=1e-5, atol=1e-5)
+
+
+def test_paged_prefill_equals_varlen_over_gathered_tokens():
+    g = seeded(5)
+    kc = torch.randn(9, 4, 2, 16, generator=g)
+    vc = torch.randn(9, 4, 2, 16, generator=g)
+    seq = torch.tensor([5, 9], dtype=torch.int32)
+    table = torch.tensor([[3, 7, 0], [8, 1, 5]], dtype=torch.int32)
+    cu_q = torch.tensor([0, 5, 8], dtype=torch.int32)
+    q = torch.randn(8, 4, 16, generator=g)
+    k, v, cu_k = oracle.gather_paged_kv(kc, vc, seq, table)
+    assert cu_k.tolist() == [0, 5, 14]
+    assert torch.equal(k[5:9], kc[8].reshape(4, 2, 16)) and torch.equal(k[13], kc[5, 0])
+    torch.testing.assert_close(oracle.paged_prefill(q, kc, vc, cu_q, seq, table),
+                               oracle.varlen_attention(q, k, v, cu_q, cu_k))

@@ -39,9 +39,10 @@ KERNEL_SOURCES = (
     "paged_decode.cu",
     "paged_decode_noalloc.cu",
     "gemm.cu",
+    "paged_prefill.cu",
     "allreduce.cu",
 )
-SHARED_HEADERS = (CSRC / "common.cuh", INCLUDE / "ntb200.h", Path(__file__).resolve())
+SHARED_HEADERS = (CSRC / "common.cuh", CSRC / "tcgen05.cuh", INCLUDE / "ntb200.h", Path(__file__).resolve())
 
 NVCC_FLAGS = [
     "-gencode",

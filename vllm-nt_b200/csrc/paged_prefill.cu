@@ -1,0 +1,684 @@
+// Varlen paged prefill attention on the 5th-generation tensor cores: a flash-attention
+// forward that reads K/V straight from vLLM's paged cache.
+//   out[t, h] = softmax(scale * q[t, h] . K_b^T + mask) . V_b
+// for every query token t of sequence b, K_b / V_b = the seq_lens[b] tokens cached for b
+// (pages of 16 tokens found through block_table), K/V head h / (Hq / Hkv).  With causal
+// masking the queries are aligned to the END of the context: query i of a sequence with
+// q_len queries and ctx cached tokens sits at position ctx - q_len + i and sees keys
+// 0 .. that position (vLLM's rule, which also covers a cached prefix and chunked prefill).
+//
+// One CTA per (128-query tile, q head, sequence), 192 threads, one CTA per SM:
+//   warp 0     TMA: the Q tile (two 64-column halves, 128-byte swizzle), then per 128-key
+//              tile the 8 K pages and the 8 V pages (16 tokens x 64 columns per copy) into
+//              2-stage rings; page ids come from the block table (ids out of range are
+//              reported and read as zeros: the copy lands outside the tensor map).
+//   warp 1     TMEM (two S buffers and O: 384 of 512 columns); lane 0 issues
+//              S_j = Q K_j^T (M = N = 128, eight K = 16 steps; both operands K-major) and
+//              O += P_j V_j (A = P in shared memory, K-major; B = V as cached, MN-major),
+//              with S_{j+1} issued before O += P_j V_j so the tensor core runs ahead of the
+//              softmax.
+//   warps 2-5  softmax, one query row per thread (warp w owns TMEM lanes 32*(w%4)..+31):
+//              the S row from TMEM, scale and mask, the running max and sum in fp32 in the
+//              exp2 domain, P = exp2(s - m) rounded to the input type into the 128-byte
+//              swizzled K-major tile the MMA reads.  The running max is refreshed lazily:
+//              only when a row's max grows by more than 2^8 is O (in TMEM) rescaled, so
+//              P <= 256 and O / l is the same either way.  Epilogue: O / l, rounded, stored.
+//
+// Every mbarrier wait is bounded (2 s); a timeout sets NTB200_DEVERR_WAIT_TIMEOUT, the
+// roles leave their loops, copies and MMAs in flight are drained, and TMEM is freed.
+//
+// Replaces vllm_nt/_ntops/kernels/attention.py:10-94 (_VarLen, reached from
+// vllm_nt/_ntops/patching.py:639-671), which first copies every sequence's K/V out of the
+// cache (vllm_nt/_ntops/torch/kv_cache.py:24-63) and masks from the upper left
+// (attention.py:61-63); here no copy is made and the mask follows vLLM.
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace ntb200 {
+namespace {
+
+constexpr int kD = 128;                       // head size
+constexpr int kBQ = 128;                      // query rows per CTA
+constexpr int kBKV = 128;                     // keys per tile
+constexpr int kPage = 16;                     // tokens per cache block
+constexpr int kPagesPerTile = kBKV / kPage;   // 8
+constexpr int kThreads = 192;
+constexpr int kHalf = 128 * 64 * 2;           // 128 rows x 64 columns: 16 KB
+constexpr int kTile = 2 * kHalf;              // 128 x 128: 32 KB
+constexpr int kPageBytes = kPage * 128;       // one page of one half: 16 rows x 128 B
+constexpr int kStages = 2;
+constexpr float kRescaleLog2 = 8.0f;          // refresh a row's max when it grows by > 2^8
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemO = 256;              // S buffers at columns 0 and 128, O at 256
+
+struct Smem {
+  static constexpr int kQ = 0;
+  static constexpr int kK = kQ + kTile;
+  static constexpr int kV = kK + kStages * kTile;
+  static constexpr int kP = kV + kStages * kTile;
+  static constexpr int kQFull = kP + kTile;
+  static constexpr int kKFull = kQFull + 8;
+  static constexpr int kKEmpty = kKFull + 8 * kStages;
+  static constexpr int kVFull = kKEmpty + 8 * kStages;
+  static constexpr int kVEmpty = kVFull + 8 * kStages;
+  static constexpr int kSFull = kVEmpty + 8 * kStages;
+  static constexpr int kSFree = kSFull + 16;
+  static constexpr int kPFull = kSFree + 16;
+  static constexpr int kPEmpty = kPFull + 8;
+  static constexpr int kMmaDone = kPEmpty + 8;
+  static constexpr int kTmemBase = kMmaDone + 8;
+  static constexpr int kEnd = kTmemBase + 8;
+  static constexpr int kDynamicBytes = kEnd + 1024;
+  static_assert(kDynamicBytes <= 227 * 1024, "shared memory");
+};
+
+struct PrefillParams {
+  void* out;
+  const int32_t* query_start_loc;  // [num_seqs + 1]
+  const int32_t* seq_lens;         // [num_seqs] (paged K/V)
+  const int32_t* block_table;      // [num_seqs, bt_stride] (paged K/V)
+  const int32_t* key_start_loc;    // [num_seqs + 1] (contiguous K/V)
+  int num_keys;                    // rows of the contiguous K/V
+  int64_t bt_stride;
+  int64_t o_tok_stride, o_head_stride;
+  int num_tokens;
+  int max_blocks;
+  int num_blocks;
+  int group;             // q heads per kv head
+  int causal;
+  int heads_outer;       // cache memory order [block, head, token, d] (else [block, token, head, d])
+  float scale_log2;      // softmax scale * log2(e)
+  unsigned int* err;
+};
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// the hardware base-2 exponential (ex2.approx; exp2(-inf) = +0)
+__device__ __forceinline__ float hw_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  const __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// PAGED: K/V pages of the cache through the block table; else contiguous [keys, kv_heads,
+// 128] K/V, sequence b's keys at rows key_start_loc[b] .. key_start_loc[b + 1].
+template <typename T, bool PAGED>
+__global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
+    const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
+    const __grid_constant__ CUtensorMap v_map, const PrefillParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + Smem::kQFull);
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + Smem::kKFull);
+  uint64_t* k_empty = reinterpret_cast<uint64_t*>(smem + Smem::kKEmpty);
+  uint64_t* v_full = reinterpret_cast<uint64_t*>(smem + Smem::kVFull);
+  uint64_t* v_empty = reinterpret_cast<uint64_t*>(smem + Smem::kVEmpty);
+  uint64_t* s_full = reinterpret_cast<uint64_t*>(smem + Smem::kSFull);
+  uint64_t* s_free = reinterpret_cast<uint64_t*>(smem + Smem::kSFree);
+  uint64_t* p_full = reinterpret_cast<uint64_t*>(smem + Smem::kPFull);
+  uint64_t* p_empty = reinterpret_cast<uint64_t*>(smem + Smem::kPEmpty);
+  uint64_t* mma_done = reinterpret_cast<uint64_t*>(smem + Smem::kMmaDone);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Smem::kTmemBase);
+  const uint32_t sm = smem_u32(smem);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.z;
+  const int qh = blockIdx.y;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (causal) tiles start first
+  const int kvh = qh / p.group;
+  pdl_trigger();
+  pdl_wait();  // queries, cache and metadata come from the kernels before
+
+  const int q_begin = p.query_start_loc[b];
+  int q_len = p.query_start_loc[b + 1] - q_begin;
+  if (q_begin < 0 || q_len < 0 || q_begin + q_len > p.num_tokens) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
+    return;
+  }
+  const int q0 = qt * kBQ;
+  if (q0 >= q_len) return;
+  int ctx, k_begin = 0;
+  if constexpr (PAGED) {
+    ctx = p.seq_lens[b];
+    if (ctx < 0) ctx = 0;
+    if (ctx > p.max_blocks * kPage) {
+      if (threadIdx.x == 0 && blockIdx.x == 0) raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
+      ctx = p.max_blocks * kPage;
+    }
+  } else {
+    k_begin = p.key_start_loc[b];
+    ctx = p.key_start_loc[b + 1] - k_begin;
+    if (k_begin < 0 || ctx < 0 || k_begin + ctx > p.num_keys) {
+      if (threadIdx.x == 0 && blockIdx.x == 0) raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
+      return;
+    }
+  }
+  const int rows = q_len - q0 < kBQ ? q_len - q0 : kBQ;
+  const int shift = ctx - q_len;  // position of the sequence's first query
+  int kv_end = p.causal ? shift + q0 + rows : ctx;  // keys [0, kv_end) are visible to some row
+  if (kv_end > ctx) kv_end = ctx;
+  const int n_tiles = kv_end > 0 ? (kv_end + kBKV - 1) / kBKV : 0;
+  T* out = static_cast<T*>(p.out);
+
+  if (n_tiles == 0) {
+    // no visible key (empty context): zero rows, as for an empty softmax
+    for (int i = threadIdx.x; i < rows * (kD / 8); i += kThreads) {
+      const int r = i / (kD / 8), c = i % (kD / 8);
+      T* orow = out + int64_t(q_begin + q0 + r) * p.o_tok_stride + int64_t(qh) * p.o_head_stride;
+      reinterpret_cast<uint4*>(orow)[c] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&s_full[a], 1);
+      mbar_init(&s_free[a], 4);  // one arrive per softmax warp
+    }
+    mbar_init(p_full, 4);
+    mbar_init(p_empty, 1);
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&q_map)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&k_map)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&v_map)) : "memory");
+      mbar_arrive_expect_tx(q_full, kTile);
+      tma_load_3d(sm + Smem::kQ, &q_map, 0, qh, q_begin + q0, smem_u32(q_full));
+      tma_load_3d(sm + Smem::kQ + kHalf, &q_map, 64, qh, q_begin + q0, smem_u32(q_full));
+      const int32_t* bt = p.block_table + int64_t(b) * p.bt_stride;
+      const int n_pages = (ctx + kPage - 1) / kPage;
+      const int hy = p.heads_outer ? 0 : kvh, hz = p.heads_outer ? kvh : 0;
+      // one 128-key tile of K or V: 8 pages (16 copies) or one 128-row box per half
+      auto load_tile = [&](uint32_t dst, const CUtensorMap* map, int j, const int32_t (&ids)[kPagesPerTile],
+                           uint64_t* bar) {
+        if constexpr (PAGED) {
+#pragma unroll
+          for (int pg = 0; pg < kPagesPerTile; ++pg) {
+            tma_load_4d(dst + pg * kPageBytes, map, 0, hy, hz, ids[pg], smem_u32(bar));
+            tma_load_4d(dst + kHalf + pg * kPageBytes, map, 64, hy, hz, ids[pg], smem_u32(bar));
+          }
+        } else {
+          tma_load_3d(dst, map, 0, kvh, k_begin + j * kBKV, smem_u32(bar));
+          tma_load_3d(dst + kHalf, map, 64, kvh, k_begin + j * kBKV, smem_u32(bar));
+        }
+      };
+      int issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j & 1;
+        int32_t ids[kPagesPerTile];
+#pragma unroll
+        for (int pg = 0; pg < kPagesPerTile; ++pg) {
+          int32_t id = -1;  // pages past the context: zero fill (masked anyway)
+          if constexpr (PAGED) {
+            const int lb = j * kPagesPerTile + pg;
+            if (lb < n_pages) {
+              id = bt[lb];
+              if (id < 0 || id >= p.num_blocks) {
+                raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
+                id = -1;
+              }
+            }
+          }
+          ids[pg] = id;
+        }
+        if (j >= kStages && !mbar_wait(&k_empty[s], ((j / kStages) - 1) & 1, p.err)) break;
+        mbar_arrive_expect_tx(&k_full[s], kTile);
+        load_tile(sm + Smem::kK + s * kTile, &k_map, j, ids, &k_full[s]);
+        if (j >= kStages && !mbar_wait(&v_empty[s], ((j / kStages) - 1) & 1, p.err)) {
+          issued = -(j + 1);  // K of tile j is in flight, V is not
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[s], kTile);
+        load_tile(sm + Smem::kV + s * kTile, &v_map, j, ids, &v_full[s]);
+        issued = j + 1;
+      }
+      // drain the copies that may still be in flight (the last tile of each stage)
+      mbar_wait(q_full, 0, p.err);
+      const int k_issued = issued < 0 ? -issued : issued;
+      const int v_issued = issued < 0 ? -issued - 1 : issued;
+      for (int j = k_issued > kStages ? k_issued - kStages : 0; j < k_issued; ++j)
+        mbar_wait(&k_full[j & 1], (j / kStages) & 1, p.err);
+      for (int j = v_issued > kStages ? v_issued - kStages : 0; j < v_issued; ++j)
+        mbar_wait(&v_full[j & 1], (j / kStages) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+      const uint32_t idesc_s = make_idesc(kBf16, kBQ, kBKV);
+      const uint32_t idesc_o = make_idesc(kBf16, kBQ, kD) | (1u << 16);  // B (V) MN-major
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&k_full[s], (j / kStages) & 1, p.err)) return false;
+        if (j >= 2 && !mbar_wait(&s_free[s], ((j >> 1) - 1) & 1, p.err)) return false;
+        tc_fence_after();
+        const uint32_t kb = sm + Smem::kK + s * kTile;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint64_t adesc = sw128_kmajor_desc(sm + Smem::kQ + hf * kHalf);
+          const uint64_t bdesc = sw128_kmajor_desc(kb + hf * kHalf);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tmem + s * kBKV, adesc + 2 * k, bdesc + 2 * k, idesc_s, (hf | k) ? 1u : 0u);
+        }
+        umma_commit(&k_empty[s]);
+        umma_commit(&s_full[s]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, p.err);
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        const int s = j & 1;
+        if (!mbar_wait(p_full, j & 1, p.err)) break;
+        if (!mbar_wait(&v_full[s], (j / kStages) & 1, p.err)) break;
+        tc_fence_after();
+        const uint32_t vb = sm + Smem::kV + s * kTile;
+#pragma unroll
+        for (int kk = 0; kk < kBKV / 16; ++kk) {
+          // A: P rows, keys [16 kk, +16) in the (kk / 4)-th 64-key half; B: V rows
+          // [16 kk, +16) (2 KB each), both 64-column halves of the head dimension
+          const uint64_t adesc = sw128_kmajor_desc(sm + Smem::kP + (kk >> 2) * kHalf) + 2 * (kk & 3);
+          const uint64_t bdesc = sw128_mnmajor_desc(vb + kk * 2048, kHalf);
+          umma_f16(tmem + kTmemO, adesc, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&v_empty[s]);
+        umma_commit(p_empty);
+      }
+      // every issued MMA completes before TMEM may be released
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.err);
+    }
+  } else {
+    // ------------------------------ softmax + epilogue ------------------------------
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row within the tile (= TMEM lane)
+    const int qi = q0 + r;
+    const uint32_t lanes = uint32_t(quad * 32) << 16;
+    int limit = p.causal ? shift + qi + 1 : ctx;  // this row sees keys [0, limit)
+    if (limit > ctx) limit = ctx;
+    float m_run = -INFINITY;  // running max of scale*s*log2(e)
+    float l_run = 0.f;
+    uint8_t* prow = smem + Smem::kP + (r >> 3) * 1024 + (r & 7) * 128;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&s_full[s], (j / kStages) & 1, p.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[kBKV];
+#pragma unroll
+      for (int c = 0; c < kBKV / 32; ++c) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld_32(tmem + lanes + s * kBKV + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(v[i]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[s]);
+
+      const int nvalid = limit - j * kBKV;  // keys j*128 + i are visible iff i < nvalid
+      float mx = -INFINITY;
+      if (nvalid >= kBKV) {
+#pragma unroll
+        for (int i = 0; i < kBKV; ++i) {
+          x[i] *= p.scale_log2;
+          mx = fmaxf(mx, x[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kBKV; ++i) {
+          x[i] = i < nvalid ? x[i] * p.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, x[i]);
+        }
+      }
+      // lazy max refresh: warp-uniform, since O is rescaled with warp-wide TMEM accesses
+      const float m_new = fmaxf(m_run, mx);
+      const bool grow = m_new > m_run + kRescaleLog2;  // also true for the first finite max
+      float alpha = 1.f;
+      const bool any = __any_sync(0xffffffffu, grow);
+      if (any) {
+        alpha = m_run == -INFINITY ? 0.f : hw_exp2(m_run - m_new);
+        if (m_new != -INFINITY) {
+          l_run *= alpha;
+          m_run = m_new;
+        } else {
+          alpha = 1.f;
+        }
+      }
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;
+      uint32_t pk[kBKV / 2];
+      float lsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kBKV / 2; ++i) {
+        const float p0 = hw_exp2(x[2 * i] - m_use);
+        const float p1 = hw_exp2(x[2 * i + 1] - m_use);
+        lsum += p0 + p1;
+        pk[i] = pack2<T>(p0, p1);
+      }
+      l_run += lsum;
+
+      // P_{j-1} . V has been consumed (and O is final for it) before P and O change
+      if (j > 0) {
+        if (!mbar_wait(p_empty, (j - 1) & 1, p.err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (any) {
+#pragma unroll 1
+          for (int c = 0; c < kD / 32; ++c) {
+            uint32_t v[32];
+            __syncwarp();
+            tmem_ld_32(tmem + lanes + kTmemO + c * 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            tmem_st_32(tmem + lanes + kTmemO + c * 32, v);
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+      }
+      if (ctx > j * kBKV && ctx < (j + 1) * kBKV && (!PAGED || (ctx & (kPage - 1)) != 0)) {
+        // V rows past the context that were copied in hold whatever memory held there (the
+        // rest of the last page, or the rows after the sequence): zero them, so that P = 0
+        // never meets a non-finite value.  (Pages wholly past the context read as zeros.)
+        if (!mbar_wait(&v_full[s], (j / kStages) & 1, p.err)) {
+          ok = false;
+          break;
+        }
+        const int t0 = ctx - j * kBKV;
+        const int t1 = PAGED ? ((ctx + kPage - 1) / kPage) * kPage - j * kBKV : kBKV;  // <= kBKV
+        uint8_t* vb = smem + Smem::kV + s * kTile;
+        for (int i = threadIdx.x - 64; i < (t1 - t0) * 16; i += 128) {
+          const int row = t0 + (i >> 4), hf = (i >> 3) & 1, c = i & 7;
+          *reinterpret_cast<uint4*>(vb + hf * kHalf + row * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = make_uint4(pk[hf * 32 + c * 4], pk[hf * 32 + c * 4 + 1], pk[hf * 32 + c * 4 + 2],
+                                     pk[hf * 32 + c * 4 + 3]);
+          *reinterpret_cast<uint4*>(prow + hf * kHalf + ((c ^ (r & 7)) << 4)) = v;
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (ok) ok = mbar_wait(p_empty, (n_tiles - 1) & 1, p.err);
+    tc_fence_after();
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    T* orow = out + int64_t(q_begin + qi) * p.o_tok_stride + int64_t(qh) * p.o_head_stride;
+#pragma unroll 1
+    for (int c = 0; c < kD / 32; ++c) {
+      uint32_t v[32];
+      __syncwarp();
+      tmem_ld_32(tmem + lanes + kTmemO + c * 32, v);
+      if (ok && r < rows) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint4 w;
+          w.x = pack2<T>(__uint_as_float(v[g * 8 + 0]) * inv, __uint_as_float(v[g * 8 + 1]) * inv);
+          w.y = pack2<T>(__uint_as_float(v[g * 8 + 2]) * inv, __uint_as_float(v[g * 8 + 3]) * inv);
+          w.z = pack2<T>(__uint_as_float(v[g * 8 + 4]) * inv, __uint_as_float(v[g * 8 + 5]) * inv);
+          w.w = pack2<T>(__uint_as_float(v[g * 8 + 6]) * inv, __uint_as_float(v[g * 8 + 7]) * inv);
+          reinterpret_cast<uint4*>(orow + c * 32)[g] = w;
+        }
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// [tokens, heads, 128] queries: box = 128 tokens x one head x 64 columns
+int make_query_map(CUtensorMap* map, const void* base, bool bf16, int64_t tokens, int64_t heads,
+                   int64_t tok_stride, int64_t head_stride) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return fail(NTB200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {cuuint64_t(kD), cuuint64_t(heads), cuuint64_t(tokens)};
+  const cuuint64_t strides[2] = {cuuint64_t(head_stride * 2), cuuint64_t(tok_stride * 2)};
+  const cuuint32_t box[3] = {64, 1, cuuint32_t(kBQ)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NTB200_ERR_CUDA, "cuTensorMapEncodeTiled (prefill q) failed (%d)", int(r));
+  return NTB200_OK;
+}
+
+// one of K/V of the paged cache: box = one 16-token page of one head x 64 columns, with the
+// head and token dimensions ordered as they are in memory
+int make_cache_map(CUtensorMap* map, const void* base, bool bf16, int64_t blocks, int64_t heads,
+                   int64_t block_stride, int64_t page_stride, int64_t head_stride) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return fail(NTB200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const bool heads_outer = head_stride > page_stride;
+  cuuint64_t dims[4], strides[3];
+  cuuint32_t box[4];
+  dims[0] = kD;
+  box[0] = 64;
+  if (heads_outer) {
+    dims[1] = kPage, strides[0] = cuuint64_t(page_stride * 2), box[1] = kPage;
+    dims[2] = cuuint64_t(heads), strides[1] = cuuint64_t(head_stride * 2), box[2] = 1;
+  } else {
+    dims[1] = cuuint64_t(heads), strides[0] = cuuint64_t(head_stride * 2), box[1] = 1;
+    dims[2] = kPage, strides[1] = cuuint64_t(page_stride * 2), box[2] = kPage;
+  }
+  dims[3] = cuuint64_t(blocks), strides[2] = cuuint64_t(block_stride * 2), box[3] = 1;
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NTB200_ERR_CUDA, "cuTensorMapEncodeTiled (prefill cache) failed (%d)", int(r));
+  return NTB200_OK;
+}
+
+template <typename T, bool PAGED>
+int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const PrefillParams& prm,
+                   dim3 grid, cudaStream_t s, int slot) {
+  const void* fn = reinterpret_cast<const void*>(paged_prefill_kernel<T, PAGED>);
+  int st = ensure_smem_attribute(fn, Smem::kDynamicBytes, slot);
+  if (st != NTB200_OK) return st;
+  return launch_kernel(PAGED ? "paged_attention_prefill" : "flash_attn_varlen", paged_prefill_kernel<T, PAGED>, grid,
+                       dim3(kThreads), Smem::kDynamicBytes, s, qm, km, vm, prm);
+}
+
+PrefillParams base_params(void* out, const int32_t* query_start_loc, int64_t num_tokens, int64_t num_q_heads,
+                          int64_t num_kv_heads, float scale, int causal, int64_t out_token_stride,
+                          int64_t out_head_stride) {
+  PrefillParams prm = {};
+  prm.out = out;
+  prm.query_start_loc = query_start_loc;
+  prm.o_tok_stride = out_token_stride;
+  prm.o_head_stride = out_head_stride;
+  prm.num_tokens = static_cast<int>(num_tokens);
+  prm.group = static_cast<int>(num_q_heads / num_kv_heads);
+  prm.causal = causal ? 1 : 0;
+  prm.scale_log2 = scale * 1.4426950408889634f;  // softmax in the exp2 domain
+  prm.err = device_error_word();
+  return prm;
+}
+
+}  // namespace
+}  // namespace ntb200
+
+extern "C" int ntb200_paged_attention_prefill(
+    void* out, const void* query, const void* key_cache, const void* value_cache, const int32_t* query_start_loc,
+    const int32_t* seq_lens, const int32_t* block_tables, int64_t num_seqs, int64_t num_tokens,
+    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size, int64_t num_blocks,
+    int64_t max_blocks_per_seq, int64_t block_table_stride, int64_t max_query_len, float scale, int causal,
+    int64_t q_token_stride, int64_t q_head_stride, int64_t out_token_stride, int64_t out_head_stride,
+    int64_t cache_block_stride, int64_t cache_page_stride, int64_t cache_head_stride, int dtype, void* stream) {
+  using namespace ntb200;
+  if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
+    return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "paged_attention_prefill: dtype %d (bf16/f16 only)", dtype);
+  if (head_size != kD || block_size != kPage)
+    return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "paged_attention_prefill: head_size %lld / block_size %lld (128 / 16 only)",
+                (long long)head_size, (long long)block_size);
+  if (num_seqs < 0 || num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 ||
+      num_blocks <= 0 || max_blocks_per_seq < 0 || block_table_stride < max_blocks_per_seq)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "paged_attention_prefill: bad sizes");
+  if (num_seqs == 0 || num_tokens == 0 || max_query_len <= 0) return NTB200_OK;
+  if (num_seqs > 65535 || num_q_heads > 65535 || num_tokens > 0x7fffffff || num_blocks > 0x7fffffff ||
+      max_blocks_per_seq * kPage > 0x7fffffff)
+    return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "paged_attention_prefill: sizes beyond the launch limits");
+  if (!out || !query || !key_cache || !value_cache || !query_start_loc || !seq_lens || !block_tables)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "paged_attention_prefill: null pointer");
+  if (!aligned16(out) || !aligned16(query) || !aligned16(key_cache) || !aligned16(value_cache) ||
+      q_token_stride % 8 || q_head_stride % 8 || out_token_stride % 8 || out_head_stride % 8 ||
+      cache_block_stride % 8 || cache_page_stride % 8 || cache_head_stride % 8)
+    return fail(NTB200_ERR_MISALIGNED, "paged_attention_prefill: pointers 16-byte aligned, strides multiples of 8");
+  const bool bf16 = dtype == NTB200_DTYPE_BF16;
+  CUtensorMap qm, km, vm;
+  int st = make_query_map(&qm, query, bf16, num_tokens, num_q_heads, q_token_stride, q_head_stride);
+  if (st != NTB200_OK) return st;
+  st = make_cache_map(&km, key_cache, bf16, num_blocks, num_kv_heads, cache_block_stride, cache_page_stride,
+                      cache_head_stride);
+  if (st != NTB200_OK) return st;
+  st = make_cache_map(&vm, value_cache, bf16, num_blocks, num_kv_heads, cache_block_stride, cache_page_stride,
+                      cache_head_stride);
+  if (st != NTB200_OK) return st;
+  PrefillParams prm = base_params(out, query_start_loc, num_tokens, num_q_heads, num_kv_heads, scale, causal,
+                                  out_token_stride, out_head_stride);
+  prm.seq_lens = seq_lens;
+  prm.block_table = block_tables;
+  prm.bt_stride = block_table_stride;
+  prm.max_blocks = static_cast<int>(max_blocks_per_seq);
+  prm.num_blocks = static_cast<int>(num_blocks);
+  prm.heads_outer = cache_head_stride > cache_page_stride ? 1 : 0;
+  const dim3 grid(static_cast<unsigned>(ceil_div(max_query_len, kBQ)), static_cast<unsigned>(num_q_heads),
+                  static_cast<unsigned>(num_seqs));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return bf16 ? launch_prefill<__nv_bfloat16, true>(qm, km, vm, prm, grid, s, 90)
+              : launch_prefill<__half, true>(qm, km, vm, prm, grid, s, 91);
+}
+
+extern "C" int ntb200_flash_attn_varlen(void* out, const void* query, const void* key, const void* value,
+                                        const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int64_t num_seqs,
+                                        int64_t num_q_tokens, int64_t num_k_tokens, int64_t num_q_heads,
+                                        int64_t num_kv_heads, int64_t head_size, int64_t max_query_len, float scale,
+                                        int causal, int64_t q_token_stride, int64_t q_head_stride,
+                                        int64_t k_token_stride, int64_t k_head_stride, int64_t v_token_stride,
+                                        int64_t v_head_stride, int64_t out_token_stride, int64_t out_head_stride,
+                                        int dtype, void* stream) {
+  using namespace ntb200;
+  if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
+    return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "flash_attn_varlen: dtype %d (bf16/f16 only)", dtype);
+  if (head_size != kD)
+    return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "flash_attn_varlen: head_size %lld (128 only)", (long long)head_size);
+  if (num_seqs < 0 || num_q_tokens < 0 || num_k_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0 ||
+      num_q_heads % num_kv_heads != 0)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "flash_attn_varlen: bad sizes");
+  if (num_seqs == 0 || num_q_tokens == 0 || max_query_len <= 0) return NTB200_OK;
+  if (num_seqs > 65535 || num_q_heads > 65535 || num_q_tokens > 0x7fffffff || num_k_tokens > 0x7fffffff)
+    return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "flash_attn_varlen: sizes beyond the launch limits");
+  if (!out || !query || !key || !value || !cu_seqlens_q || !cu_seqlens_k)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "flash_attn_varlen: null pointer");
+  if (!aligned16(out) || !aligned16(query) || !aligned16(key) || !aligned16(value) || q_token_stride % 8 ||
+      q_head_stride % 8 || k_token_stride % 8 || k_head_stride % 8 || v_token_stride % 8 || v_head_stride % 8 ||
+      out_token_stride % 8 || out_head_stride % 8)
+    return fail(NTB200_ERR_MISALIGNED, "flash_attn_varlen: pointers 16-byte aligned, strides multiples of 8");
+  const bool bf16 = dtype == NTB200_DTYPE_BF16;
+  CUtensorMap qm, km, vm;
+  int st = make_query_map(&qm, query, bf16, num_q_tokens, num_q_heads, q_token_stride, q_head_stride);
+  if (st != NTB200_OK) return st;
+  if (num_k_tokens > 0) {
+    st = make_query_map(&km, key, bf16, num_k_tokens, num_kv_heads, k_token_stride, k_head_stride);
+    if (st != NTB200_OK) return st;
+    st = make_query_map(&vm, value, bf16, num_k_tokens, num_kv_heads, v_token_stride, v_head_stride);
+    if (st != NTB200_OK) return st;
+  } else {
+    km = qm;  // never read: every sequence has an empty context
+    vm = qm;
+  }
+  PrefillParams prm = base_params(out, cu_seqlens_q, num_q_tokens, num_q_heads, num_kv_heads, scale, causal,
+                                  out_token_stride, out_head_stride);
+  prm.key_start_loc = cu_seqlens_k;
+  prm.num_keys = static_cast<int>(num_k_tokens);
+  const dim3 grid(static_cast<unsigned>(ceil_div(max_query_len, kBQ)), static_cast<unsigned>(num_q_heads),
+                  static_cast<unsigned>(num_seqs));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return bf16 ? launch_prefill<__nv_bfloat16, false>(qm, km, vm, prm, grid, s, 92)
+              : launch_prefill<__half, false>(qm, km, vm, prm, grid, s, 93);
+}

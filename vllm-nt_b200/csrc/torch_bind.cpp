@@ -289,6 +289,95 @@ void decode_flash_layout(at::Tensor output, const at::Tensor& query, const at::T
   paged_attention_decode(o, q, kc, vc, seq_lens, block_table, scale, msl, ws);
 }
 
+// varlen prefill: query/out [tokens, q_heads, head_size] (the queries of sequence b are rows
+// query_start_loc[b] .. query_start_loc[b + 1]); caches as for decode
+void paged_attention_prefill(at::Tensor out, const at::Tensor& query, const at::Tensor& key_cache,
+                             const at::Tensor& value_cache, const at::Tensor& query_start_loc,
+                             const at::Tensor& seq_lens, const at::Tensor& block_table, int64_t max_query_len,
+                             double scale, bool causal) {
+  require_cuda(query, "query");
+  require_cuda(out, "out");
+  require_cuda(key_cache, "key_cache");
+  require_cuda(value_cache, "value_cache");
+  require_cuda(query_start_loc, "query_start_loc");
+  require_cuda(seq_lens, "seq_lens");
+  require_cuda(block_table, "block_table");
+  TORCH_CHECK(query.dim() == 3 && query.stride(2) == 1 && out.sizes() == query.sizes() && out.stride(2) == 1 &&
+                  out.scalar_type() == query.scalar_type(),
+              "ntb200.paged_attention_prefill: query/out must be [tokens, q_heads, head_size]");
+  TORCH_CHECK(key_cache.dim() == 4 && value_cache.sizes() == key_cache.sizes() &&
+                  key_cache.strides() == value_cache.strides() && key_cache.stride(3) == 1 &&
+                  key_cache.scalar_type() == query.scalar_type() && value_cache.scalar_type() == query.scalar_type(),
+              "ntb200.paged_attention_prefill: caches must be [blocks, block_size, kv_heads, head_size] like query");
+  TORCH_CHECK(query_start_loc.scalar_type() == at::kInt && query_start_loc.is_contiguous() &&
+                  query_start_loc.dim() == 1 && query_start_loc.numel() >= 1,
+              "ntb200.paged_attention_prefill: query_start_loc must be int32 contiguous [seqs + 1]");
+  const int64_t seqs = query_start_loc.numel() - 1;
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt && seq_lens.is_contiguous() && seq_lens.numel() >= seqs,
+              "ntb200.paged_attention_prefill: seq_lens must be int32 contiguous [seqs]");
+  TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2 && block_table.stride(1) == 1 &&
+                  block_table.size(0) >= seqs,
+              "ntb200.paged_attention_prefill: block_table must be int32 [seqs, max_blocks]");
+  c10::cuda::CUDAGuard guard(query.device());
+  check(ntb200_paged_attention_prefill(
+            out.data_ptr(), query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+            query_start_loc.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(), block_table.data_ptr<int32_t>(), seqs,
+            query.size(0), query.size(1), key_cache.size(2), query.size(2), key_cache.size(1), key_cache.size(0),
+            block_table.size(1), block_table.stride(0), max_query_len, static_cast<float>(scale), causal ? 1 : 0,
+            query.stride(0), query.stride(1), out.stride(0), out.stride(1), key_cache.stride(0), key_cache.stride(1),
+            key_cache.stride(2), dtype_code(query), stream_of(query)),
+        "paged_attention_prefill");
+}
+
+// contiguous varlen: query/out [q_tokens, q_heads, 128], key/value [k_tokens, kv_heads, 128]
+void flash_attn_varlen(at::Tensor out, const at::Tensor& query, const at::Tensor& key, const at::Tensor& value,
+                       const at::Tensor& cu_seqlens_q, const at::Tensor& cu_seqlens_k, int64_t max_query_len,
+                       double scale, bool causal) {
+  require_cuda(query, "query");
+  require_cuda(out, "out");
+  require_cuda(key, "key");
+  require_cuda(value, "value");
+  require_cuda(cu_seqlens_q, "cu_seqlens_q");
+  require_cuda(cu_seqlens_k, "cu_seqlens_k");
+  TORCH_CHECK(query.dim() == 3 && query.stride(2) == 1 && out.sizes() == query.sizes() && out.stride(2) == 1 &&
+                  out.scalar_type() == query.scalar_type(),
+              "ntb200.flash_attn_varlen: query/out must be [tokens, q_heads, head_size]");
+  TORCH_CHECK(key.dim() == 3 && value.sizes() == key.sizes() && key.stride(2) == 1 && value.stride(2) == 1 &&
+                  key.size(2) == query.size(2) && key.scalar_type() == query.scalar_type() &&
+                  value.scalar_type() == query.scalar_type(),
+              "ntb200.flash_attn_varlen: key/value must be [tokens, kv_heads, head_size] like query");
+  TORCH_CHECK(cu_seqlens_q.scalar_type() == at::kInt && cu_seqlens_k.scalar_type() == at::kInt &&
+                  cu_seqlens_q.is_contiguous() && cu_seqlens_k.is_contiguous() && cu_seqlens_q.dim() == 1 &&
+                  cu_seqlens_q.numel() >= 1 && cu_seqlens_k.numel() == cu_seqlens_q.numel(),
+              "ntb200.flash_attn_varlen: cu_seqlens_q/k must be int32 contiguous [seqs + 1]");
+  c10::cuda::CUDAGuard guard(query.device());
+  check(ntb200_flash_attn_varlen(out.data_ptr(), query.data_ptr(), key.data_ptr(), value.data_ptr(),
+                                 cu_seqlens_q.data_ptr<int32_t>(), cu_seqlens_k.data_ptr<int32_t>(),
+                                 cu_seqlens_q.numel() - 1, query.size(0), key.size(0), query.size(1), key.size(1),
+                                 query.size(2), max_query_len, static_cast<float>(scale), causal ? 1 : 0,
+                                 query.stride(0), query.stride(1), key.stride(0), key.stride(1), value.stride(0),
+                                 value.stride(1), out.stride(0), out.stride(1), dtype_code(query), stream_of(query)),
+        "flash_attn_varlen");
+}
+
+void prefill_flash_layout(at::Tensor output, const at::Tensor& query, const at::Tensor& kv_cache,
+                          const at::Tensor& query_start_loc, const at::Tensor& seq_lens,
+                          const at::Tensor& block_table, int64_t num_tokens, int64_t max_query_len, double scale,
+                          bool causal, int64_t kv_dim) {
+  require_cuda(kv_cache, "kv_cache");
+  TORCH_CHECK((kv_dim == 0 || kv_dim == 1) && kv_cache.dim() == 5 && kv_cache.size(kv_dim) == 2,
+              "ntb200.prefill_flash_layout: kv_cache must be [2, blocks, block_size, kv_heads, head_size] "
+              "(kv_dim 0) or [blocks, 2, block_size, kv_heads, head_size] (kv_dim 1)");
+  const at::Tensor kc = kv_cache.select(kv_dim, 0), vc = kv_cache.select(kv_dim, 1);
+  const int64_t head = kc.size(3);
+  at::Tensor q = query.dim() == 2 ? query.view({query.size(0), -1, head}) : query;
+  at::Tensor o = output.dim() == 2 ? output.view({output.size(0), -1, head}) : output;
+  TORCH_CHECK(num_tokens >= 0 && num_tokens <= q.size(0) && num_tokens <= o.size(0),
+              "ntb200.prefill_flash_layout: num_tokens exceeds the activations");
+  paged_attention_prefill(o.narrow(0, 0, num_tokens), q.narrow(0, 0, num_tokens), kc, vc, query_start_loc, seq_lens,
+                          block_table, max_query_len, scale, causal);
+}
+
 void store_flash_layout(const at::Tensor& key, const at::Tensor& value, at::Tensor kv_cache,
                         const at::Tensor& slot_mapping, int64_t kv_dim) {
   require_cuda(kv_cache, "kv_cache");
@@ -448,6 +537,17 @@ TORCH_LIBRARY(ntb200, m) {
   m.def("linear_silu_and_mul(Tensor(a!) out, Tensor x, Tensor weight) -> ()");
   m.def("linear_argmax(Tensor(a!) out_index, Tensor x, Tensor weight) -> ()");
   m.def(
+      "paged_attention_prefill(Tensor(a!) out, Tensor query, Tensor key_cache, Tensor value_cache, "
+      "Tensor query_start_loc, Tensor seq_lens, Tensor block_table, int max_query_len, float scale, "
+      "bool causal) -> ()");
+  m.def(
+      "flash_attn_varlen(Tensor(a!) out, Tensor query, Tensor key, Tensor value, Tensor cu_seqlens_q, "
+      "Tensor cu_seqlens_k, int max_query_len, float scale, bool causal) -> ()");
+  m.def(
+      "prefill_flash_layout(Tensor(a!) output, Tensor query, Tensor kv_cache, Tensor query_start_loc, "
+      "Tensor seq_lens, Tensor block_table, int num_tokens, int max_query_len, float scale, bool causal, "
+      "int kv_dim=0) -> ()");
+  m.def(
       "allreduce_oneshot(Tensor(a!) out, Tensor partial, Tensor peer_buffers, int capacity, int rank, "
       "int world_size) -> ()");
   m.def("allreduce_buffer_size(int capacity, int elem_bytes, int world_size) -> int", &allreduce_buffer_size);
@@ -467,4 +567,7 @@ TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("allreduce_oneshot", &allreduce_oneshot);
   m.impl("linear_silu_and_mul", &linear_silu_and_mul);
   m.impl("linear_argmax", &linear_argmax);
+  m.impl("paged_attention_prefill", &paged_attention_prefill);
+  m.impl("prefill_flash_layout", &prefill_flash_layout);
+  m.impl("flash_attn_varlen", &flash_attn_varlen);
 }

@@ -13,6 +13,7 @@ from typing import Callable
 import torch
 
 from vllm_nt._ntops.torch._ext import ops
+from vllm_nt._ntops.torch.attention import flash_attn_varlen_func as nt_flash_attn_varlen_func
 from vllm_nt._ntops.torch.attention import flash_attn_with_kvcache as nt_flash_attn_with_kvcache
 from vllm_nt._ntops.torch.attention import paged_decode as nt_paged_decode
 from vllm_nt._ntops.torch.embedding import embedding as nt_embedding
@@ -117,9 +118,21 @@ def paged_attention_decode(q, k_cache, v_cache, cache_seqlens, block_table, soft
     )
 
 
-def paged_attention_prefill(*args, **kwargs):
-    """Prefill is not on this backend's hot path; callers route it to vLLM's original."""
-    raise NotImplementedError("paged prefill is served by vLLM's original attention backend")
+def paged_attention_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale=None, causal=True,
+                            **kwargs):
+    """Reference signature (vllm_nt/_ntops/oot_support.py:88-109): varlen attention over
+    contiguous K/V on the tcgen05 prefill kernel."""
+    return nt_flash_attn_varlen_func(
+        q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale=softmax_scale, causal=causal, **kwargs
+    )
+
+
+def paged_attention_prefill_flash(output, query, kv_cache, query_start_loc, seq_lens, block_table, num_tokens,
+                                  max_query_len, scale, causal=True, kv_dim=0):
+    """Varlen attention for the first ``num_tokens`` rows of vLLM's padded activations,
+    reading K/V from its combined cache tensor in place (kv_dim as in store_kv_cache_flash)."""
+    ops().prefill_flash_layout(output, query, kv_cache, query_start_loc, seq_lens, block_table, num_tokens,
+                               max_query_len, scale, causal, kv_dim)
 
 
 def get_kv_from_cache(k_cache, v_cache, seq_lens, block_table):

@@ -41,6 +41,9 @@ def _register_fakes() -> None:
         "allreduce_oneshot",
         "linear_silu_and_mul",
         "linear_argmax",
+        "paged_attention_prefill",
+        "prefill_flash_layout",
+        "flash_attn_varlen",
     ):
         torch.library.register_fake(f"ntb200::{name}")(nothing)
 

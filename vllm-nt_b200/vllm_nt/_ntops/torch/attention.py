@@ -1,5 +1,5 @@
-"""Paged-attention decode on the sm_100a split-K kernel (replaces
-vllm_nt/_ntops/torch/attention.py:51-77)."""
+"""Paged-attention decode (split-K kernel) and varlen prefill (tcgen05 flash-attention
+kernel) on sm_100a; replaces vllm_nt/_ntops/torch/attention.py:9-77."""
 
 from __future__ import annotations
 
@@ -64,6 +64,38 @@ def flash_attn_with_kvcache(
     return out.view(q.shape)
 
 
-def flash_attn_varlen_func(*args, **kwargs):
-    """Varlen prefill is served by vLLM's own attention in this build."""
-    raise NotImplementedError("prefill attention is served by vLLM's original backend")
+def flash_attn_varlen_func(
+    q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale=None, causal=True, out=None, **kwargs
+):
+    """Reference signature (vllm_nt/_ntops/torch/attention.py:9-46): q [Tq, Hq, D], k/v
+    [Tk, Hkv, D] with cu_seqlens_q/k [B + 1]; returns [Tq, Hq, D].  Causal masking is aligned
+    to the end of each sequence's keys (vLLM's FlashAttention rule; the reference aligns to
+    the start, which is the same whenever a sequence has as many keys as queries)."""
+    del kwargs
+    scale = 1.0 / math.sqrt(q.shape[-1]) if softmax_scale is None else float(softmax_scale)
+    out = torch.empty_like(q) if out is None else out
+    cu_q = cu_seqlens_q if cu_seqlens_q.dtype == torch.int32 else cu_seqlens_q.to(torch.int32)
+    cu_k = cu_seqlens_k if cu_seqlens_k.dtype == torch.int32 else cu_seqlens_k.to(torch.int32)
+    ops().flash_attn_varlen(out, q, k, v, cu_q.contiguous(), cu_k.contiguous(), int(max_seqlen_q), scale,
+                            bool(causal))
+    return out
+
+
+def paged_prefill(
+    out: torch.Tensor,
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    query_start_loc: torch.Tensor,
+    seq_lens: torch.Tensor,
+    block_table: torch.Tensor,
+    max_query_len: int,
+    scale: float,
+    causal: bool = True,
+) -> torch.Tensor:
+    """Varlen attention straight over the paged cache: query/out [T, Hq, 128] (sequence b's
+    queries at rows query_start_loc[b] .. [b + 1]), caches [blocks, 16, Hkv, 128] holding
+    seq_lens[b] tokens of b (its queries' own keys last)."""
+    ops().paged_attention_prefill(out, query, key_cache, value_cache, query_start_loc, seq_lens, block_table,
+                                  int(max_query_len), float(scale), bool(causal))
+    return out
