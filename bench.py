@@ -21,6 +21,7 @@ config and tensor TFLOP/s for the projection GEMM.
 from __future__ import annotations
 
 import argparse
+import itertools
 import json
 import math
 import os
@@ -444,6 +445,47 @@ def per_op_table(dev, peaks) -> dict:
     report("paged decode bf16 B=256 ctx U[512,640] (vLLM e2e shape)", nb, time_graph(fns, 20))
     del kc_s, vc_s
 
+    # varlen prefill over the paged cache (causal, end-aligned), Llama-3-8B heads: a full
+    # scheduler batch of 32 prompts x 512 tokens, and 8 prompts of 512 new tokens after
+    # 1536 cached ones.  FLOPs = 4 * D * Hq * (visible query-key pairs).
+    def prefill_case(name, qlens, ctxs):
+        nblk = [(c + BLOCK - 1) // BLOCK for c in ctxs]
+        pool_p = sum(nblk)
+        gp = torch.Generator().manual_seed(len(qlens))
+        ids_p = torch.randperm(pool_p, generator=gp).to(torch.int32)
+        tab_p = torch.zeros(len(ctxs), max(nblk), dtype=torch.int32)
+        off = 0
+        for i, n in enumerate(nblk):
+            tab_p[i, :n] = ids_p[off : off + n]
+            off += n
+        cu_p = torch.tensor([0] + list(itertools.accumulate(qlens)), dtype=torch.int32)
+        kc_p = torch.randn(pool_p, BLOCK, HKV, HEAD, device=dev, generator=g, dtype=torch.bfloat16)
+        vc_p = torch.randn(pool_p, BLOCK, HKV, HEAD, device=dev, generator=g, dtype=torch.bfloat16)
+        q_p = torch.randn(int(cu_p[-1]), HQ, HEAD, device=dev, generator=g, dtype=torch.bfloat16)
+        o_p = torch.empty_like(q_p)
+        cu_d, seq_d, tab_d = cu_p.to(dev), torch.tensor(ctxs, dtype=torch.int32, device=dev), tab_p.to(dev)
+        pairs = sum(sum(min(c - ql + i + 1, c) for i in range(ql)) for ql, c in zip(qlens, ctxs))
+        flops = 4.0 * HEAD * HQ * pairs
+        nbytes = 2 * int(cu_p[-1]) * HQ * HEAD * 2 + 2 * sum(ctxs) * HKV * HEAD * 2
+        sc = 1.0 / math.sqrt(HEAD)
+        ms = time_graph([lambda: o.paged_attention_prefill(o_p, q_p, kc_p, vc_p, cu_d, seq_d, tab_d, max(qlens),
+                                                            sc, True)], 10)
+        tf = flops / (ms * 1e-3) / 1e12
+        res[name] = {"us": ms * 1e3, "TFLOP/s": round(tf, 1), "frac_of_bf16": round(tf / tens, 3),
+                     "flops": flops, "bytes": nbytes}
+        try:
+            from vllm.vllm_flash_attn import flash_attn_varlen_func as vllm_fa
+        except Exception:  # noqa: BLE001 - the comparison column is optional
+            vllm_fa = None
+        lib(name, "vLLM flash_attn_varlen_func (paged, causal)",
+            vllm_fa and [lambda: vllm_fa(q_p, kc_p, vc_p, out=o_p, cu_seqlens_q=cu_d, max_seqlen_q=max(qlens),
+                                         seqused_k=seq_d, max_seqlen_k=max(ctxs), softmax_scale=sc, causal=True,
+                                         block_table=tab_d)], 10)
+        del kc_p, vc_p, q_p, o_p
+
+    prefill_case("paged prefill bf16 32 x 512 tokens (causal)", [512] * 32, [512] * 32)
+    prefill_case("paged prefill bf16 8 x 512 new after 1536 cached", [512] * 8, [2048] * 8)
+
     # projection GEMM bf16 (fp32 accumulate)
     for (K, Nn, tag) in ((4096, 6144, "qkv"), (4096, 4096, "o_proj"), (4096, 28672, "gate_up"), (14336, 4096, "down")):
         for M in (1, 16, 128, 256, 1024, 8192):
@@ -631,6 +673,44 @@ def run_linear_case(args) -> int:
     return 0
 
 
+def run_prefill_case(args) -> int:
+    """NSEQ sequences of Q new tokens after CTX - Q cached ones (Llama-3-8B heads, paged
+    cache), warmup + steps launches of the prefill kernel, for profiling."""
+    from vllm_nt._ntops.torch._ext import ops
+
+    q_len, ctx, nseq = args.prefill_case
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    nblk = (ctx + BLOCK - 1) // BLOCK
+    table = torch.randperm(nseq * nblk, device=dev, generator=g).to(torch.int32).view(nseq, nblk)
+    kc = torch.randn(nseq * nblk, BLOCK, HKV, HEAD, device=dev, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    q = torch.randn(nseq * q_len, HQ, HEAD, device=dev, generator=g, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    cu = torch.arange(0, nseq + 1, device=dev, dtype=torch.int32) * q_len
+    seq = torch.full((nseq,), ctx, device=dev, dtype=torch.int32)
+    o = ops()
+
+    def call():
+        o.paged_attention_prefill(out, q, kc, vc, cu, seq, table, q_len, 1.0 / math.sqrt(HEAD), True)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    pairs = nseq * sum(ctx - q_len + i + 1 for i in range(q_len))
+    print(json.dumps({"prefill_case": [q_len, ctx, nseq], "us": ms * 1e3,
+                      "TFLOP/s": 4.0 * HEAD * HQ * pairs / (ms * 1e-3) / 1e12}))
+    return 0
+
+
 # --------------------------------------------------------------------------------------
 # main arm
 # --------------------------------------------------------------------------------------
@@ -649,6 +729,8 @@ def main() -> int:
     ap.add_argument("--pool", type=int, default=POOL, help="profiling: smaller block pool")
     ap.add_argument("--linear-case", type=int, nargs=3, metavar=("M", "N", "K"),
                     help="profiling: run only the GEMM out[M,N] = x[M,K] W[N,K]^T, warmup+steps times")
+    ap.add_argument("--prefill-case", type=int, nargs=3, metavar=("Q", "CTX", "NSEQ"),
+                    help="profiling: run only the paged prefill kernel, warmup+steps times")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -656,6 +738,8 @@ def main() -> int:
         return run_reference(args)
     if args.linear_case:
         return run_linear_case(args)
+    if args.prefill_case:
+        return run_prefill_case(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

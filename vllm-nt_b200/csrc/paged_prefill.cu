@@ -7,20 +7,21 @@
 // q_len queries and ctx cached tokens sits at position ctx - q_len + i and sees keys
 // 0 .. that position (vLLM's rule, which also covers a cached prefix and chunked prefill).
 //
-// One CTA per (128-query tile, q head, sequence), 192 threads, one CTA per SM:
+// One CTA per (128-query tile, q head, sequence), 320 threads, one CTA per SM:
 //   warp 0     TMA: the Q tile (two 64-column halves, 128-byte swizzle), then per 128-key
 //              tile the 8 K pages and the 8 V pages (16 tokens x 64 columns per copy) into
 //              2-stage rings; page ids come from the block table (ids out of range are
 //              reported and read as zeros: the copy lands outside the tensor map).
 //   warp 1     TMEM (two S buffers and O: 384 of 512 columns); lane 0 issues
 //              S_j = Q K_j^T (M = N = 128, eight K = 16 steps; both operands K-major) and
-//              O += P_j V_j (A = P in shared memory, K-major; B = V as cached, MN-major),
+//              O += P_j V_j (A = P_j in TMEM, written over S_j; B = V as cached, MN-major),
 //              with S_{j+1} issued before O += P_j V_j so the tensor core runs ahead of the
-//              softmax.
-//   warps 2-5  softmax, one query row per thread (warp w owns TMEM lanes 32*(w%4)..+31):
-//              the S row from TMEM, scale and mask, the running max and sum in fp32 in the
-//              exp2 domain, P = exp2(s - m) rounded to the input type into the 128-byte
-//              swizzled K-major tile the MMA reads.  The running max is refreshed lazily:
+//              softmax; S_{j+2} reuses the buffer once O += P_j V_j has read P_j.
+//   warps 2-9  softmax, two threads per query row (warp w owns TMEM lanes 32*(w%4)..+31
+//              and 64 of the 128 key columns; the two halves of a row meet at an mbarrier
+//              to combine their maxima): the S row from TMEM, scale and mask, the running
+//              max and sum in fp32 in the exp2 domain, P = exp2(s - m) rounded to the input
+//              type and stored back into TMEM over the S columns just read.  The running max is refreshed lazily:
 //              only when a row's max grows by more than 2^8 is O (in TMEM) rescaled, so
 //              P <= 256 and O / l is the same either way.  Epilogue: O / l, rounded, stored.
 //
@@ -42,7 +43,8 @@ constexpr int kBQ = 128;                      // query rows per CTA
 constexpr int kBKV = 128;                     // keys per tile
 constexpr int kPage = 16;                     // tokens per cache block
 constexpr int kPagesPerTile = kBKV / kPage;   // 8
-constexpr int kThreads = 192;
+constexpr int kSoftmaxThreads = 256;           // warps 2-9: two per query row
+constexpr int kThreads = 64 + kSoftmaxThreads;
 constexpr int kHalf = 128 * 64 * 2;           // 128 rows x 64 columns: 16 KB
 constexpr int kTile = 2 * kHalf;              // 128 x 128: 32 KB
 constexpr int kPageBytes = kPage * 128;       // one page of one half: 16 rows x 128 B
@@ -55,18 +57,18 @@ struct Smem {
   static constexpr int kQ = 0;
   static constexpr int kK = kQ + kTile;
   static constexpr int kV = kK + kStages * kTile;
-  static constexpr int kP = kV + kStages * kTile;
-  static constexpr int kQFull = kP + kTile;
+  static constexpr int kQFull = kV + kStages * kTile;
   static constexpr int kKFull = kQFull + 8;
   static constexpr int kKEmpty = kKFull + 8 * kStages;
   static constexpr int kVFull = kKEmpty + 8 * kStages;
   static constexpr int kVEmpty = kVFull + 8 * kStages;
   static constexpr int kSFull = kVEmpty + 8 * kStages;
-  static constexpr int kSFree = kSFull + 16;
-  static constexpr int kPFull = kSFree + 16;
+  static constexpr int kPFull = kSFull + 16;
   static constexpr int kPEmpty = kPFull + 8;
   static constexpr int kMmaDone = kPEmpty + 8;
-  static constexpr int kTmemBase = kMmaDone + 8;
+  static constexpr int kPair = kMmaDone + 8;       // 4 mbarriers: the two warps of each row quadrant
+  static constexpr int kRed = kPair + 32;          // [2][2][128] floats: row-max / row-sum exchange
+  static constexpr int kTmemBase = kRed + 2 * 2 * 128 * 4;
   static constexpr int kEnd = kTmemBase + 8;
   static constexpr int kDynamicBytes = kEnd + 1024;
   static_assert(kDynamicBytes <= 227 * 1024, "shared memory");
@@ -106,6 +108,17 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
       "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      : "memory");
+}
+
+// D (TMEM) (+)= A (TMEM, M rows on the lanes, K packed two per 32-bit column) . B (smem)
+__device__ __forceinline__ void umma_f16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -157,7 +170,6 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
   uint64_t* v_full = reinterpret_cast<uint64_t*>(smem + Smem::kVFull);
   uint64_t* v_empty = reinterpret_cast<uint64_t*>(smem + Smem::kVEmpty);
   uint64_t* s_full = reinterpret_cast<uint64_t*>(smem + Smem::kSFull);
-  uint64_t* s_free = reinterpret_cast<uint64_t*>(smem + Smem::kSFree);
   uint64_t* p_full = reinterpret_cast<uint64_t*>(smem + Smem::kPFull);
   uint64_t* p_empty = reinterpret_cast<uint64_t*>(smem + Smem::kPEmpty);
   uint64_t* mma_done = reinterpret_cast<uint64_t*>(smem + Smem::kMmaDone);
@@ -222,11 +234,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&s_full[a], 1);
-      mbar_init(&s_free[a], 4);  // one arrive per softmax warp
-    }
-    mbar_init(p_full, 4);
+    for (int a = 0; a < 2; ++a) mbar_init(&s_full[a], 1);
+    mbar_init(p_full, 8);
+    for (int q = 0; q < 4; ++q) mbar_init(reinterpret_cast<uint64_t*>(smem + Smem::kPair) + q, 64);
     mbar_init(p_empty, 1);
     mbar_init(mma_done, 1);
     fence_mbar_init();
@@ -316,7 +326,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
         if (!mbar_wait(&k_full[s], (j / kStages) & 1, p.err)) return false;
-        if (j >= 2 && !mbar_wait(&s_free[s], ((j >> 1) - 1) & 1, p.err)) return false;
+        // S[s] holds P_{j-2} until O += P_{j-2} V_{j-2} has read it (the newest product
+        // issued so far, so its phase cannot be overtaken)
+        if (j >= 2 && !mbar_wait(p_empty, (j - 2) & 1, p.err)) return false;
         tc_fence_after();
         const uint32_t kb = sm + Smem::kK + s * kTile;
 #pragma unroll
@@ -342,11 +354,12 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
         const uint32_t vb = sm + Smem::kV + s * kTile;
 #pragma unroll
         for (int kk = 0; kk < kBKV / 16; ++kk) {
-          // A: P rows, keys [16 kk, +16) in the (kk / 4)-th 64-key half; B: V rows
-          // [16 kk, +16) (2 KB each), both 64-column halves of the head dimension
-          const uint64_t adesc = sw128_kmajor_desc(sm + Smem::kP + (kk >> 2) * kHalf) + 2 * (kk & 3);
+          // A: P_j in TMEM over S[s], keys [16 kk, +16) = 8 packed columns (keys 0-63 at
+          // columns 0-31, keys 64-127 at 64-95); B: V rows [16 kk, +16) (2 KB apart), both
+          // 64-column halves of the head dimension
+          const uint32_t a_tmem = tmem + s * kBKV + (kk >> 2) * 64 + (kk & 3) * 8;
           const uint64_t bdesc = sw128_mnmajor_desc(vb + kk * 2048, kHalf);
-          umma_f16(tmem + kTmemO, adesc, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_tmem_a(tmem + kTmemO, a_tmem, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&v_empty[s]);
         umma_commit(p_empty);
@@ -357,15 +370,32 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
     }
   } else {
     // ------------------------------ softmax + epilogue ------------------------------
+    // Two warps per query row: warp w (2..9) reads TMEM lanes 32*(w%4)..+31 and owns key
+    // columns [64*half, +64) of S, the same 64 columns of O, and the matching half of P.
+    // The row max is exchanged through shared memory at a per-quadrant mbarrier.
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int col0 = half * 64;
     const int r = quad * 32 + lane;  // query row within the tile (= TMEM lane)
     const int qi = q0 + r;
     const uint32_t lanes = uint32_t(quad * 32) << 16;
+    float* red = reinterpret_cast<float*>(smem + Smem::kRed);  // [2 buffers][2 halves][128 rows]
+    uint64_t* pair = reinterpret_cast<uint64_t*>(smem + Smem::kPair) + quad;
+    uint32_t pair_uses = 0;
     int limit = p.causal ? shift + qi + 1 : ctx;  // this row sees keys [0, limit)
     if (limit > ctx) limit = ctx;
-    float m_run = -INFINITY;  // running max of scale*s*log2(e)
-    float l_run = 0.f;
-    uint8_t* prow = smem + Smem::kP + (r >> 3) * 1024 + (r & 7) * 128;
+    float m_run = -INFINITY;  // running max of scale*s*log2(e), the same in both warps of the row
+    float l_run = 0.f;        // this warp's half of the running sum
+    // exchange one float per row with the partner warp; false if the partner never came
+    auto exchange = [&](float mine, float& theirs) -> bool {
+      float* buf = red + (pair_uses & 1) * 256;
+      buf[half * 128 + r] = mine;
+      mbar_arrive(pair);
+      const bool got = mbar_wait(pair, pair_uses & 1, p.err);
+      theirs = buf[(half ^ 1) * 128 + r];
+      ++pair_uses;
+      return got;
+    };
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j & 1;
@@ -374,35 +404,39 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
         break;
       }
       tc_fence_after();
-      float x[kBKV];
+      float x[64];
 #pragma unroll
-      for (int c = 0; c < kBKV / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t v[32];
         __syncwarp();
-        tmem_ld_32(tmem + lanes + s * kBKV + c * 32, v);
+        tmem_ld_32(tmem + lanes + s * kBKV + col0 + c * 32, v);
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(v[i]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[s]);
-
-      const int nvalid = limit - j * kBKV;  // keys j*128 + i are visible iff i < nvalid
-      float mx = -INFINITY;
-      if (nvalid >= kBKV) {
+      const int nvalid = limit - j * kBKV - col0;  // columns col0 + i are visible iff i < nvalid
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
+      if (nvalid >= 64) {
 #pragma unroll
-        for (int i = 0; i < kBKV; ++i) {
+        for (int i = 0; i < 64; ++i) {
           x[i] *= p.scale_log2;
-          mx = fmaxf(mx, x[i]);
+          m4[i & 3] = fmaxf(m4[i & 3], x[i]);
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < kBKV; ++i) {
+        for (int i = 0; i < 64; ++i) {
           x[i] = i < nvalid ? x[i] * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, x[i]);
+          m4[i & 3] = fmaxf(m4[i & 3], x[i]);
         }
       }
-      // lazy max refresh: warp-uniform, since O is rescaled with warp-wide TMEM accesses
+      float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+      float other;
+      if (!exchange(mx, other)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, other);
+      // lazy max refresh, identical in both warps of a row (same rows, same combined max);
+      // warp-uniform, since O is rescaled with warp-wide TMEM accesses
       const float m_new = fmaxf(m_run, mx);
       const bool grow = m_new > m_run + kRescaleLog2;  // also true for the first finite max
       float alpha = 1.f;
@@ -417,33 +451,34 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
         }
       }
       const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      uint32_t pk[kBKV / 2];
-      float lsum = 0.f;
+      uint32_t pk[32];
+      float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < kBKV / 2; ++i) {
+      for (int i = 0; i < 32; ++i) {
         const float p0 = hw_exp2(x[2 * i] - m_use);
         const float p1 = hw_exp2(x[2 * i + 1] - m_use);
-        lsum += p0 + p1;
+        l4[i & 3] += p0 + p1;
         pk[i] = pack2<T>(p0, p1);
       }
-      l_run += lsum;
+      l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
 
-      // P_{j-1} . V has been consumed (and O is final for it) before P and O change
-      if (j > 0) {
+      // O is rescaled only once O += P_{j-1} V_{j-1} is complete (and before P_j is
+      // released, so the next product sees the new scale)
+      if (j > 0 && any) {
         if (!mbar_wait(p_empty, (j - 1) & 1, p.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (any) {
+        {
 #pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t v[32];
             __syncwarp();
-            tmem_ld_32(tmem + lanes + kTmemO + c * 32, v);
+            tmem_ld_32(tmem + lanes + kTmemO + col0 + c * 32, v);
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-            tmem_st_32(tmem + lanes + kTmemO + c * 32, v);
+            tmem_st_32(tmem + lanes + kTmemO + col0 + c * 32, v);
           }
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
@@ -459,34 +494,33 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
         const int t0 = ctx - j * kBKV;
         const int t1 = PAGED ? ((ctx + kPage - 1) / kPage) * kPage - j * kBKV : kBKV;  // <= kBKV
         uint8_t* vb = smem + Smem::kV + s * kTile;
-        for (int i = threadIdx.x - 64; i < (t1 - t0) * 16; i += 128) {
+        for (int i = threadIdx.x - 64; i < (t1 - t0) * 16; i += kSoftmaxThreads) {
           const int row = t0 + (i >> 4), hf = (i >> 3) & 1, c = i & 7;
           *reinterpret_cast<uint4*>(vb + hf * kHalf + row * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
       }
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 v = make_uint4(pk[hf * 32 + c * 4], pk[hf * 32 + c * 4 + 1], pk[hf * 32 + c * 4 + 2],
-                                     pk[hf * 32 + c * 4 + 3]);
-          *reinterpret_cast<uint4*>(prow + hf * kHalf + ((c ^ (r & 7)) << 4)) = v;
-        }
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+      // P_j (this warp's 64 keys, packed in pairs) over the first 32 of the S columns this
+      // warp has just read
+      __syncwarp();
+      tmem_st_32(tmem + lanes + s * kBKV + col0, pk);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
     if (ok) ok = mbar_wait(p_empty, (n_tiles - 1) & 1, p.err);
+    float l_other = 0.f;
+    if (ok) ok = exchange(l_run, l_other);
     tc_fence_after();
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    T* orow = out + int64_t(q_begin + qi) * p.o_tok_stride + int64_t(qh) * p.o_head_stride;
+    const float l = l_run + l_other;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    T* orow = out + int64_t(q_begin + qi) * p.o_tok_stride + int64_t(qh) * p.o_head_stride + col0;
 #pragma unroll 1
-    for (int c = 0; c < kD / 32; ++c) {
+    for (int c = 0; c < 2; ++c) {
       uint32_t v[32];
       __syncwarp();
-      tmem_ld_32(tmem + lanes + kTmemO + c * 32, v);
+      tmem_ld_32(tmem + lanes + kTmemO + col0 + c * 32, v);
       if (ok && r < rows) {
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
