@@ -202,6 +202,35 @@ int ntb200_paged_attention_prefill(
     int64_t out_head_stride, int64_t cache_block_stride, int64_t cache_page_stride,
     int64_t cache_head_stride, int dtype, void* stream);
 
+/* Decode for the single-query sequences of a varlen batch: as ntb200_paged_attention_decode,
+ * but sequence b's query and output row is query_start_loc[b] ([num_seqs + 1] int32) and
+ * sequences whose query count is not 1 are left untouched.  Same workspace. */
+int ntb200_paged_attention_decode_varlen(
+    void* out, const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* block_tables,
+    int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+    int64_t block_size, int64_t num_blocks, int64_t max_blocks_per_seq,
+    int64_t block_table_stride, int64_t max_seq_len, float scale, int64_t q_token_stride,
+    int64_t q_head_stride, int64_t out_token_stride, int64_t out_head_stride,
+    int64_t cache_block_stride, int64_t cache_page_stride, int64_t cache_head_stride,
+    void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
+/* A vLLM attention batch of any mix of decodes and (chunked) prefills, causal: the
+ * single-query sequences through ntb200_paged_attention_decode_varlen, the others through
+ * the prefill kernel (which skips the single-query ones).  Arguments as
+ * ntb200_paged_attention_prefill plus max_seq_len (bounds seq_lens) and the decode
+ * workspace (ntb200_paged_attention_decode_workspace_size(num_seqs, ...) bytes).
+ * Replaces the prefill/decode split of vllm_nt/_ntops/patching.py:565-685. */
+int ntb200_paged_attention_varlen(
+    void* out, const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* block_tables,
+    int64_t num_seqs, int64_t num_tokens, int64_t num_q_heads, int64_t num_kv_heads,
+    int64_t head_size, int64_t block_size, int64_t num_blocks, int64_t max_blocks_per_seq,
+    int64_t block_table_stride, int64_t max_query_len, int64_t max_seq_len, float scale,
+    int64_t q_token_stride, int64_t q_head_stride, int64_t out_token_stride,
+    int64_t out_head_stride, int64_t cache_block_stride, int64_t cache_page_stride,
+    int64_t cache_head_stride, void* workspace, size_t workspace_bytes, int dtype, void* stream);
+
 /* The same attention over contiguous varlen K/V instead of the paged cache: key/value
  * [num_k_tokens, num_kv_heads, 128], sequence b's keys at rows cu_seqlens_k[b] ..
  * cu_seqlens_k[b+1] (its context), its queries at rows cu_seqlens_q[b] .. cu_seqlens_q[b+1]

@@ -54,10 +54,11 @@ def test_default_config_is_hybrid_default():
 def test_all_b200_config_routes_every_hot_op_to_b200(monkeypatch):
     monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(CONFIGS / "all-b200.yaml"))
     config.reset_backend_config_cache()
-    for op in ("RMSNorm", "SiluAndMul", "RoPE", "Embedding", "MatMul", "LMHead", "StoreKVCache", "PagedAttentionDecode"):
+    for op in ("RMSNorm", "SiluAndMul", "RoPE", "Embedding", "MatMul", "LMHead", "StoreKVCache", "PagedAttentionDecode",
+               "PagedAttentionPrefill"):
         assert config.config_for(op).backend == "b200", op
         assert config.config_for(op).fallback_backend == "original"
-    assert config.config_for("PagedAttentionPrefill").backend == "original"
+    assert config.config_for("SDPA").backend == "original"
 
 
 def test_defaults_and_string_form(monkeypatch, tmp_path):

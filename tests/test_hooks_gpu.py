@@ -145,6 +145,33 @@ def test_flash_attention_impl_hooks_store_and_decode(_b200_config):
     assert _hits(patching, "StoreKVCache") == 1 and _hits(patching, "PagedAttentionDecode") == 1
 
 
+def test_flash_attention_impl_hook_mixed_prefill_batch(_b200_config):
+    """A chunked-prefill step: one request prefills 150 new tokens after 100 cached ones, two
+    decode; FlashAttentionImpl.forward runs on the B200 kernels (no fallback) and matches
+    the oracle."""
+    patching = _b200_config
+    fwd = patching._build_flash_attn_forward(lambda *a, **k: pytest.fail("prefill fell back to vLLM"))
+    impl = SimpleNamespace(num_heads=32, num_kv_heads=8, head_size=128, scale=1 / math.sqrt(128), attn_type="decoder",
+                           kv_cache_dtype="auto", alibi_slopes=None, logits_soft_cap=None, sinks=None,
+                           sliding_window=None, dcp_world_size=1)
+    g = seeded(5)
+    nb = 80
+    kv = torch.randn(2, nb, 16, 8, 128, generator=g).to(torch.bfloat16)
+    qlens, ctxs = [1, 150, 1], [37, 250, 400]
+    table = torch.randperm(nb, generator=g)[: 3 * 25].view(3, 25).to(torch.int32)
+    cu = torch.tensor([0, 1, 151, 152], dtype=torch.int32)
+    q = torch.randn(160, 32, 128, generator=g).to(torch.bfloat16)  # 152 real rows + padding
+    out = torch.zeros(160, 32 * 128, dtype=torch.bfloat16, device="cuda")
+    seq = torch.tensor(ctxs, dtype=torch.int32)
+    meta = SimpleNamespace(num_actual_tokens=152, max_query_len=150, use_cascade=False, max_seq_len=400, causal=True,
+                           query_start_loc=cu.cuda(), seq_lens=seq.cuda(), block_table=table.cuda())
+    fwd(impl, None, q.cuda(), None, None, kv.cuda(), meta, out)
+    ref = oracle.paged_prefill(q[:152], kv[0], kv[1], cu, seq, table, impl.scale)
+    torch.testing.assert_close(out[:152].view(152, 32, 128).float().cpu(), ref, **TOL)
+    assert not out[152:].any()
+    assert _hits(patching, "PagedAttentionPrefill") == 1
+
+
 def test_fused_mlp_hook_on_a_llama_shaped_mlp(_b200_config, vllm_ctx):
     """The LlamaMLP.forward replacement: fused gate_up + SiluAndMul kernel, then the
     down projection through its own hook."""

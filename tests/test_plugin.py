@@ -207,7 +207,7 @@ def test_rope_hook_uses_matched_cache_and_counts(monkeypatch):
     assert patching.get_usage_summary()["operators"]["RoPE"]["hits"] == 1
 
 
-def test_attention_hooks_decode_only_and_kv_store(monkeypatch):
+def test_attention_hooks_route_decode_prefill_and_kv_store(monkeypatch):
     calls = {}
     monkeypatch.setattr(patching, "_attn_impl_supported", lambda *a: True)
     monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
@@ -219,7 +219,12 @@ def test_attention_hooks_decode_only_and_kv_store(monkeypatch):
     def fake_store(key, value, kv, slots, kv_dim=0):
         calls["store"] = (tuple(key.shape), tuple(kv.shape), tuple(slots.shape))
 
+    def fake_varlen(out, q, kv, qsl, seq, table, n, max_q, msl, scale, kv_dim=0):
+        calls["varlen"] = (tuple(qsl.shape), n, max_q, msl, scale)
+        out[:n].fill_(2.0)
+
     monkeypatch.setattr(patching, "paged_attention_decode_flash", fake_decode)
+    monkeypatch.setattr(patching, "paged_attention_flash", fake_varlen)
     monkeypatch.setattr(patching, "store_kv_cache_flash", fake_store)
     orig = lambda *a, **k: "flash-attn"  # noqa: E731
     fwd = patching._build_flash_attn_forward(orig)
@@ -234,12 +239,19 @@ def test_attention_hooks_decode_only_and_kv_store(monkeypatch):
     assert fwd(impl, None, q, q, q, kv, meta, out) is out
     assert calls["decode"] == ((5, 4 * 128), (5, 4, 128), (2, 6, 16, 2, 128), (3,), 3, 0.1, 40)
     assert out[:3].eq(1).all() and out[3:].eq(0).all()
-    prefill = SimpleNamespace(**{**vars(meta), "max_query_len": 7})
-    assert fwd(impl, None, q, q, q, kv, prefill, out) == "flash-attn"
+    # a mixed batch (two decodes and a 3-token chunk of a prefill) goes to the varlen entry
+    mixed = SimpleNamespace(**{**vars(meta), "max_query_len": 3, "num_actual_tokens": 5,
+                               "query_start_loc": torch.tensor([0, 1, 2, 5])})
+    assert fwd(impl, None, q, q, q, kv, mixed, out) is out
+    assert calls["varlen"] == ((4,), 5, 3, 40, 0.1) and out[:5].eq(2).all()
+    # cascade and non-causal metadata stay on vLLM's FlashAttention
+    for bad in ({"use_cascade": True}, {"causal": False}):
+        assert fwd(impl, None, q, q, q, kv, SimpleNamespace(**{**vars(mixed), **bad}), out) == "flash-attn"
     upd(impl, None, torch.zeros(5, 2, 128), torch.zeros(5, 2, 128), kv, torch.tensor([1, 2, 3]))
     assert calls["store"] == ((5, 2, 128), (2, 6, 16, 2, 128), (3,))
     ops = patching.get_usage_summary()["operators"]
     assert ops["PagedAttentionDecode"]["hits"] == 1 and ops["StoreKVCache"]["hits"] == 1
+    assert ops["PagedAttentionPrefill"]["hits"] == 1
 
 
 def test_no_vendor_imports_in_package():

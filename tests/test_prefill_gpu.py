@@ -190,3 +190,33 @@ def test_reference_varlen_known_answer_on_gpu():
     out = paged_attention_prefill(q.to(dev), k.to(dev), v.to(dev), cu.to(dev), cu.to(dev), 3)
     ref = oracle.varlen_attention(q, k, v, cu, cu)
     torch.testing.assert_close(out.float().cpu(), ref, rtol=TOL, atol=TOL)
+
+
+def _run_vllm_layout(qlens, ctxs, hq, hkv, seed, scale):
+    from vllm_nt._ntops.oot_support import paged_attention_flash
+
+    q, kc, vc, cu, seq, table = make_paged(qlens, ctxs, hq, hkv, seed=seed)
+    ref = oracle.paged_prefill(q, kc, vc, cu, seq, table, scale)
+    dev = cuda_device()
+    kv = torch.stack([kc, vc]).to(dev)
+    n = q.shape[0]
+    qpad = torch.zeros(n + 8, hq * 128, dtype=q.dtype, device=dev)
+    qpad[:n] = q.reshape(n, -1).to(dev)
+    opad = torch.full_like(qpad, 5.0)
+    paged_attention_flash(opad, qpad, kv, cu.to(dev), seq.to(dev), table.to(dev), n, max(qlens), max(ctxs), scale)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(opad[:n].view(n, hq, 128).float().cpu(), ref, rtol=TOL, atol=TOL)
+    assert (opad[n:] == 5.0).all()
+    assert capi.read_device_error(stream()) == 0
+
+
+def test_mixed_batch_through_vllm_layout():
+    """Decodes (one query), a chunk of a prefill after a cached prefix and fresh prompts in
+    one batch on the FlashAttention cache: decode rows on the split-K kernel, the rest on
+    the prefill kernel, every row against the oracle."""
+    _run_vllm_layout([1, 130, 1, 1, 64, 300, 1, 2], [700, 500, 1, 33, 64, 300, 129, 2], 32, 8, 19, 0.088)
+
+
+def test_decode_only_and_uniform_prefill_batches_through_vllm_layout():
+    _run_vllm_layout([1] * 9, [5, 17, 600, 1, 64, 33, 2000, 16, 128], 8, 2, 20, 0.1)
+    _run_vllm_layout([64] * 5, [64, 100, 700, 64, 129], 8, 2, 21, 0.1)

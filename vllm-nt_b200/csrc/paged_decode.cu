@@ -123,6 +123,9 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
 
 struct DecodeParams {
   const void* query;
+  // varlen batches: sequence b's query row is query_start_loc[b], and sequences with more
+  // (or fewer) than one query are skipped (a prefill kernel serves them); null: row b
+  const int32_t* query_start_loc;
   const int32_t* seq_lens;
   const int32_t* block_tables;
   float* part_o;    // [B][Hkv][max_chunks][G][128]
@@ -155,6 +158,11 @@ __global__ void __launch_bounds__(kThreads) paged_decode_split_kernel(
   const int lane = threadIdx.x & 31;
   pdl_trigger();
   pdl_wait();
+  int64_t row = b;  // query / output row of sequence b
+  if (p.query_start_loc != nullptr) {
+    row = p.query_start_loc[b];
+    if (p.query_start_loc[b + 1] - row != 1) return;  // uniform across the CTA
+  }
 
   int ctx = p.seq_lens[b];
   if (ctx < 0) ctx = 0;
@@ -163,7 +171,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_split_kernel(
   const int64_t blk_begin = int64_t(chunk) * p.chunk_blocks;
   if (blk_begin >= total_blocks) {  // uniform across the CTA
     if (p.direct) {  // an empty sequence attends to nothing: zero rows, as the combine writes
-      T* ob = static_cast<T*>(p.out) + int64_t(b) * p.o_seq_stride;
+      T* ob = static_cast<T*>(p.out) + row * p.o_seq_stride;
       for (int idx = threadIdx.x; idx < p.group * kHeadDim; idx += kThreads) {
         const int hh = idx / kHeadDim;
         ob[int64_t(kvh * p.group + hh) * p.o_head_stride + (idx - hh * kHeadDim)] = Elem<T>::from_f(0.f);
@@ -240,7 +248,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_split_kernel(
   // q^T as the B operand of S^T = K q^T: b0 = q[g][16kk+2c..+1], b1 = q[g][16kk+8+2c..+1]
   uint32_t qf[8][2];
   {
-    const T* qrow = static_cast<const T*>(p.query) + int64_t(b) * p.q_seq_stride +
+    const T* qrow = static_cast<const T*>(p.query) + row * p.q_seq_stride +
                     int64_t(kvh * G + (g < G ? g : 0)) * p.q_head_stride;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
@@ -361,7 +369,7 @@ __global__ void __launch_bounds__(kThreads) paged_decode_split_kernel(
   }
   named_barrier_sync(1, kConsumerWarps * 32);
   if (p.direct) {
-    T* ob = static_cast<T*>(p.out) + int64_t(b) * p.o_seq_stride;
+    T* ob = static_cast<T*>(p.out) + row * p.o_seq_stride;
     for (int idx = threadIdx.x; idx < G * kHeadDim; idx += kConsumerWarps * 32) {
       const int hh = idx / kHeadDim;
       const int d = idx - hh * kHeadDim;
@@ -407,9 +415,9 @@ __global__ void __launch_bounds__(kThreads) paged_decode_split_kernel(
 template <typename T>
 __global__ void __launch_bounds__(128) paged_decode_combine_kernel(
     T* __restrict__ out, const float* __restrict__ part_o, const float* __restrict__ part_lse,
-    const int32_t* __restrict__ seq_lens, int num_seqs, int num_q_heads, int group,
-    int chunk_tokens, int max_chunks, int64_t max_blocks_per_seq, int64_t o_seq_stride,
-    int64_t o_head_stride, unsigned int* err) {
+    const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ query_start_loc, int num_seqs,
+    int num_q_heads, int group, int chunk_tokens, int max_chunks, int64_t max_blocks_per_seq,
+    int64_t o_seq_stride, int64_t o_head_stride, unsigned int* err) {
   const int64_t wid = int64_t(blockIdx.x) * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   pdl_trigger();
@@ -419,6 +427,11 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(
   const int qh = static_cast<int>(wid - int64_t(b) * num_q_heads);
   const int kvh = qh / group, hh = qh - kvh * group;
   const int num_kv = num_q_heads / group;
+  int64_t row = b;
+  if (query_start_loc != nullptr) {
+    row = query_start_loc[b];
+    if (query_start_loc[b + 1] - row != 1) return;  // not a decode row (warp-uniform)
+  }
   int64_t ctx = seq_lens[b] < 0 ? 0 : seq_lens[b];
   if (ctx > max_blocks_per_seq * kBlockTokens) ctx = max_blocks_per_seq * kBlockTokens;
   int64_t nch = (ctx + chunk_tokens - 1) / chunk_tokens;
@@ -426,7 +439,7 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(
     if (lane == 0) raise_device_error(err, NTB200_DEVERR_INDEX_RANGE);
     nch = max_chunks;
   }
-  T* orow = out + int64_t(b) * o_seq_stride + int64_t(qh) * o_head_stride;
+  T* orow = out + row * o_seq_stride + int64_t(qh) * o_head_stride;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   if (nch > 0) {
     const int64_t unit0 = (int64_t(b) * num_kv + kvh) * max_chunks;
@@ -547,16 +560,16 @@ extern "C" size_t ntb200_paged_attention_decode_workspace_size(
   return workspace_bytes_for(num_seqs, num_q_heads, max_seq_len, chunk);
 }
 
-extern "C" int ntb200_paged_attention_decode(
-    void* out, const void* query, const void* key_cache, const void* value_cache,
-    const int32_t* seq_lens, const int32_t* block_tables, int64_t num_seqs,
-    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size,
-    int64_t num_blocks, int64_t max_blocks_per_seq, int64_t block_table_stride,
-    int64_t max_seq_len, float scale, int64_t q_seq_stride, int64_t q_head_stride,
-    int64_t out_seq_stride, int64_t out_head_stride, int64_t cache_block_stride,
-    int64_t cache_page_stride, int64_t cache_head_stride, void* workspace,
-    size_t workspace_bytes, int dtype, void* stream) {
-  using namespace ntb200;
+namespace ntb200 {
+namespace {
+
+int decode_impl(void* out, const void* query, const void* key_cache, const void* value_cache,
+                const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* block_tables,
+                int64_t num_seqs, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size,
+                int64_t num_blocks, int64_t max_blocks_per_seq, int64_t block_table_stride, int64_t max_seq_len,
+                float scale, int64_t q_seq_stride, int64_t q_head_stride, int64_t out_seq_stride,
+                int64_t out_head_stride, int64_t cache_block_stride, int64_t cache_page_stride,
+                int64_t cache_head_stride, void* workspace, size_t workspace_bytes, int dtype, void* stream) {
   if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
     return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "paged_decode: dtype %d (bf16/f16 only)", dtype);
   if (head_size != kHeadDim || block_size != kBlockTokens)
@@ -602,6 +615,7 @@ extern "C" int ntb200_paged_attention_decode(
 
   DecodeParams prm;
   prm.query = query;
+  prm.query_start_loc = query_start_loc;
   prm.seq_lens = seq_lens;
   prm.block_tables = block_tables;
   const int64_t units = num_seqs * num_q_heads * max_chunks;
@@ -646,12 +660,48 @@ extern "C" int ntb200_paged_attention_decode(
   if (dtype == NTB200_DTYPE_BF16)
     return launch_kernel("paged_decode_combine", paged_decode_combine_kernel<__nv_bfloat16>, cgrid,
                          dim3(128), 0, s, static_cast<__nv_bfloat16*>(out), prm.part_o,
-                         prm.part_lse, seq_lens, int(num_seqs), int(num_q_heads), int(group),
-                         chunk_tokens, int(max_chunks), max_blocks_per_seq, out_seq_stride,
+                         prm.part_lse, seq_lens, query_start_loc, int(num_seqs), int(num_q_heads),
+                         int(group), chunk_tokens, int(max_chunks), max_blocks_per_seq, out_seq_stride,
                          out_head_stride, prm.err);
   return launch_kernel("paged_decode_combine", paged_decode_combine_kernel<__half>, cgrid,
                        dim3(128), 0, s, static_cast<__half*>(out), prm.part_o, prm.part_lse,
-                       seq_lens, int(num_seqs), int(num_q_heads), int(group), chunk_tokens,
-                       int(max_chunks), max_blocks_per_seq, out_seq_stride, out_head_stride,
-                       prm.err);
+                       seq_lens, query_start_loc, int(num_seqs), int(num_q_heads), int(group),
+                       chunk_tokens, int(max_chunks), max_blocks_per_seq, out_seq_stride,
+                       out_head_stride, prm.err);
+}
+
+}  // namespace
+}  // namespace ntb200
+
+extern "C" int ntb200_paged_attention_decode(
+    void* out, const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* seq_lens, const int32_t* block_tables, int64_t num_seqs,
+    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size,
+    int64_t num_blocks, int64_t max_blocks_per_seq, int64_t block_table_stride,
+    int64_t max_seq_len, float scale, int64_t q_seq_stride, int64_t q_head_stride,
+    int64_t out_seq_stride, int64_t out_head_stride, int64_t cache_block_stride,
+    int64_t cache_page_stride, int64_t cache_head_stride, void* workspace,
+    size_t workspace_bytes, int dtype, void* stream) {
+  return ntb200::decode_impl(out, query, key_cache, value_cache, nullptr, seq_lens, block_tables, num_seqs,
+                             num_q_heads, num_kv_heads, head_size, block_size, num_blocks, max_blocks_per_seq,
+                             block_table_stride, max_seq_len, scale, q_seq_stride, q_head_stride, out_seq_stride,
+                             out_head_stride, cache_block_stride, cache_page_stride, cache_head_stride, workspace,
+                             workspace_bytes, dtype, stream);
+}
+
+extern "C" int ntb200_paged_attention_decode_varlen(
+    void* out, const void* query, const void* key_cache, const void* value_cache,
+    const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* block_tables, int64_t num_seqs,
+    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size, int64_t num_blocks,
+    int64_t max_blocks_per_seq, int64_t block_table_stride, int64_t max_seq_len, float scale,
+    int64_t q_token_stride, int64_t q_head_stride, int64_t out_token_stride, int64_t out_head_stride,
+    int64_t cache_block_stride, int64_t cache_page_stride, int64_t cache_head_stride, void* workspace,
+    size_t workspace_bytes, int dtype, void* stream) {
+  if (query_start_loc == nullptr)
+    return ntb200::fail(NTB200_ERR_INVALID_ARGUMENT, "paged_decode_varlen: query_start_loc is null");
+  return ntb200::decode_impl(out, query, key_cache, value_cache, query_start_loc, seq_lens, block_tables, num_seqs,
+                             num_q_heads, num_kv_heads, head_size, block_size, num_blocks, max_blocks_per_seq,
+                             block_table_stride, max_seq_len, scale, q_token_stride, q_head_stride,
+                             out_token_stride, out_head_stride, cache_block_stride, cache_page_stride,
+                             cache_head_stride, workspace, workspace_bytes, dtype, stream);
 }

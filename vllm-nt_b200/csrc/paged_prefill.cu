@@ -7,8 +7,11 @@
 // q_len queries and ctx cached tokens sits at position ctx - q_len + i and sees keys
 // 0 .. that position (vLLM's rule, which also covers a cached prefix and chunked prefill).
 //
-// One CTA per (128-query tile, q head, sequence), 320 threads, one CTA per SM:
-//   warp 0     TMA: the Q tile (two 64-column halves, 128-byte swizzle), then per 128-key
+// Persistent: one CTA per SM walks the work items -- (128-query tile, q head) pairs of all
+// sequences, a sequence's last tile first -- found from a prefix sum of the query tiles
+// per sequence that every CTA builds in shared memory.  320 threads:
+//   warp 0     TMA: the Q tile (two 64-column halves, 128-byte swizzle; double-buffered
+//              across items), then per 128-key
 //              tile the 8 K pages and the 8 V pages (16 tokens x 64 columns per copy) into
 //              2-stage rings; page ids come from the block table (ids out of range are
 //              reported and read as zeros: the copy lands outside the tensor map).
@@ -54,25 +57,30 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = 256;              // S buffers at columns 0 and 128, O at 256
 
 struct Smem {
-  static constexpr int kQ = 0;
-  static constexpr int kK = kQ + kTile;
+  static constexpr int kQ = 0;                    // two Q tiles: the next item's loads early
+  static constexpr int kK = kQ + 2 * kTile;
   static constexpr int kV = kK + kStages * kTile;
   static constexpr int kQFull = kV + kStages * kTile;
-  static constexpr int kKFull = kQFull + 8;
+  static constexpr int kQEmpty = kQFull + 16;
+  static constexpr int kKFull = kQEmpty + 16;
   static constexpr int kKEmpty = kKFull + 8 * kStages;
   static constexpr int kVFull = kKEmpty + 8 * kStages;
   static constexpr int kVEmpty = kVFull + 8 * kStages;
   static constexpr int kSFull = kVEmpty + 8 * kStages;
   static constexpr int kPFull = kSFull + 16;
-  static constexpr int kPEmpty = kPFull + 8;
-  static constexpr int kMmaDone = kPEmpty + 8;
+  static constexpr int kPEmpty = kPFull + 16;
+  static constexpr int kPvDone = kPEmpty + 8;     // [2]: O += P V done, per S buffer
+  static constexpr int kOFree = kPvDone + 16;
+  static constexpr int kMmaDone = kOFree + 8;
   static constexpr int kPair = kMmaDone + 8;       // 4 mbarriers: the two warps of each row quadrant
   static constexpr int kRed = kPair + 32;          // [2][2][128] floats: row-max / row-sum exchange
   static constexpr int kTmemBase = kRed + 2 * 2 * 128 * 4;
-  static constexpr int kEnd = kTmemBase + 8;
-  static constexpr int kDynamicBytes = kEnd + 1024;
-  static_assert(kDynamicBytes <= 227 * 1024, "shared memory");
+  static constexpr int kPrefix = kTmemBase + 16;   // [num_seqs + 1] ints: the work list
+  static constexpr int kMaxBytes = 227 * 1024;
+  static constexpr int bytes_for(int64_t num_seqs) { return kPrefix + int(num_seqs + 1) * 4 + 1024; }
+  static constexpr int64_t kMaxSeqs = (kMaxBytes - kPrefix - 1024) / 4 - 1;
 };
+static_assert(Smem::bytes_for(1024) <= Smem::kMaxBytes, "shared memory");
 
 struct PrefillParams {
   void* out;
@@ -86,6 +94,9 @@ struct PrefillParams {
   int num_tokens;
   int max_blocks;
   int num_blocks;
+  int num_seqs;
+  int num_q_heads;
+  int skip_single_query;  // sequences with one query token are left to the decode kernel
   int group;             // q heads per kv head
   int causal;
   int heads_outer;       // cache memory order [block, head, token, d] (else [block, token, head, d])
@@ -155,8 +166,80 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// One work item = (128-query tile, q head) of a sequence; the CTA's roles walk the same
+// items in the same order and derive the same parameters from the metadata.
+struct Item {
+  int b, qh, kvh, q0, rows, q_begin, ctx, k_begin, shift, n_tiles;
+};
+
+// the largest b in [0, n) with prefix[b] <= t
+__device__ __forceinline__ int find_sequence(const int* prefix, int n, int t) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <bool PAGED>
+__device__ __forceinline__ Item make_item(const PrefillParams& p, const int* prefix, int w) {
+  Item it;
+  const int tl = w / p.num_q_heads;
+  it.qh = w - tl * p.num_q_heads;
+  it.kvh = it.qh / p.group;
+  it.b = find_sequence(prefix, p.num_seqs, tl);
+  const int t = tl - prefix[it.b];
+  const int ntq = prefix[it.b + 1] - prefix[it.b];
+  const int qt = ntq - 1 - t;  // a sequence's last (longest, when causal) tile first
+  it.q_begin = p.query_start_loc[it.b];
+  const int q_len = p.query_start_loc[it.b + 1] - it.q_begin;
+  it.q0 = qt * kBQ;
+  it.rows = q_len - it.q0 < kBQ ? q_len - it.q0 : kBQ;
+  it.k_begin = 0;
+  if constexpr (PAGED) {
+    it.ctx = p.seq_lens[it.b] < 0 ? 0 : p.seq_lens[it.b];
+    if (it.ctx > p.max_blocks * kPage) {
+      raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
+      it.ctx = p.max_blocks * kPage;
+    }
+  } else {
+    it.k_begin = p.key_start_loc[it.b];
+    it.ctx = p.key_start_loc[it.b + 1] - it.k_begin;  // validated by the scan
+  }
+  it.shift = it.ctx - q_len;  // position of the sequence's first query
+  int kv_end = p.causal ? it.shift + it.q0 + it.rows : it.ctx;  // keys [0, kv_end) are visible to some row
+  if (kv_end > it.ctx) kv_end = it.ctx;
+  it.n_tiles = kv_end > 0 ? (kv_end + kBKV - 1) / kBKV : 0;
+  return it;
+}
+
+// query tiles of sequence b (0 for a sequence skipped or with inconsistent metadata)
+template <bool PAGED>
+__device__ __forceinline__ int query_tiles(const PrefillParams& p, int b) {
+  const int qb = p.query_start_loc[b];
+  const int ql = p.query_start_loc[b + 1] - qb;
+  if (qb < 0 || ql < 0 || qb + ql > p.num_tokens) {
+    raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
+    return 0;
+  }
+  if constexpr (!PAGED) {
+    const int kb = p.key_start_loc[b];
+    const int kl = p.key_start_loc[b + 1] - kb;
+    if (kb < 0 || kl < 0 || kb + kl > p.num_keys) {
+      raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
+      return 0;
+    }
+  }
+  if (p.skip_single_query && ql == 1) return 0;
+  return (ql + kBQ - 1) / kBQ;
+}
+
 // PAGED: K/V pages of the cache through the block table; else contiguous [keys, kv_heads,
 // 128] K/V, sequence b's keys at rows key_start_loc[b] .. key_start_loc[b + 1].
+// Persistent: CTA i takes work items i, i + gridDim.x, ...; the K/V ring, the S buffers,
+// P and O carry on from one item to the next (phases counted over the CTA's whole run).
 template <typename T, bool PAGED>
 __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
     const __grid_constant__ CUtensorMap q_map, const __grid_constant__ CUtensorMap k_map,
@@ -164,7 +247,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  __shared__ int warp_sums[kThreads / 32];
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + Smem::kQFull);
+  uint64_t* q_empty = reinterpret_cast<uint64_t*>(smem + Smem::kQEmpty);
   uint64_t* k_full = reinterpret_cast<uint64_t*>(smem + Smem::kKFull);
   uint64_t* k_empty = reinterpret_cast<uint64_t*>(smem + Smem::kKEmpty);
   uint64_t* v_full = reinterpret_cast<uint64_t*>(smem + Smem::kVFull);
@@ -172,73 +257,65 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
   uint64_t* s_full = reinterpret_cast<uint64_t*>(smem + Smem::kSFull);
   uint64_t* p_full = reinterpret_cast<uint64_t*>(smem + Smem::kPFull);
   uint64_t* p_empty = reinterpret_cast<uint64_t*>(smem + Smem::kPEmpty);
+  uint64_t* pv_done = reinterpret_cast<uint64_t*>(smem + Smem::kPvDone);
+  uint64_t* o_free = reinterpret_cast<uint64_t*>(smem + Smem::kOFree);
   uint64_t* mma_done = reinterpret_cast<uint64_t*>(smem + Smem::kMmaDone);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Smem::kTmemBase);
+  int* prefix = reinterpret_cast<int*>(smem + Smem::kPrefix);  // [num_seqs + 1] query tiles
   const uint32_t sm = smem_u32(smem);
-
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.z;
-  const int qh = blockIdx.y;
-  const int qt = gridDim.x - 1 - blockIdx.x;  // the longest (causal) tiles start first
-  const int kvh = qh / p.group;
   pdl_trigger();
   pdl_wait();  // queries, cache and metadata come from the kernels before
 
-  const int q_begin = p.query_start_loc[b];
-  int q_len = p.query_start_loc[b + 1] - q_begin;
-  if (q_begin < 0 || q_len < 0 || q_begin + q_len > p.num_tokens) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
-    return;
-  }
-  const int q0 = qt * kBQ;
-  if (q0 >= q_len) return;
-  int ctx, k_begin = 0;
-  if constexpr (PAGED) {
-    ctx = p.seq_lens[b];
-    if (ctx < 0) ctx = 0;
-    if (ctx > p.max_blocks * kPage) {
-      if (threadIdx.x == 0 && blockIdx.x == 0) raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
-      ctx = p.max_blocks * kPage;
+  // ---- work list: prefix sums of the query tiles per sequence (block scan) ----
+  int carry = 0;
+  if (threadIdx.x == 0) prefix[0] = 0;
+  for (int base = 0; base < p.num_seqs; base += kThreads) {
+    const int bb = base + threadIdx.x;
+    const int c = bb < p.num_seqs ? query_tiles<PAGED>(p, bb) : 0;
+    int v = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
     }
-  } else {
-    k_begin = p.key_start_loc[b];
-    ctx = p.key_start_loc[b + 1] - k_begin;
-    if (k_begin < 0 || ctx < 0 || k_begin + ctx > p.num_keys) {
-      if (threadIdx.x == 0 && blockIdx.x == 0) raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
-      return;
+    if (lane == 31) warp_sums[warp] = v;
+    __syncthreads();
+    int before = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) {
+      before += w < warp ? warp_sums[w] : 0;
+      total += warp_sums[w];
     }
+    if (bb < p.num_seqs) prefix[bb + 1] = carry + before + v;
+    carry += total;
+    __syncthreads();
   }
-  const int rows = q_len - q0 < kBQ ? q_len - q0 : kBQ;
-  const int shift = ctx - q_len;  // position of the sequence's first query
-  int kv_end = p.causal ? shift + q0 + rows : ctx;  // keys [0, kv_end) are visible to some row
-  if (kv_end > ctx) kv_end = ctx;
-  const int n_tiles = kv_end > 0 ? (kv_end + kBKV - 1) / kBKV : 0;
+  const int num_items = carry * p.num_q_heads;
+  if (static_cast<int>(blockIdx.x) >= num_items) return;
   T* out = static_cast<T*>(p.out);
 
-  if (n_tiles == 0) {
-    // no visible key (empty context): zero rows, as for an empty softmax
-    for (int i = threadIdx.x; i < rows * (kD / 8); i += kThreads) {
-      const int r = i / (kD / 8), c = i % (kD / 8);
-      T* orow = out + int64_t(q_begin + q0 + r) * p.o_tok_stride + int64_t(qh) * p.o_head_stride;
-      reinterpret_cast<uint4*>(orow)[c] = make_uint4(0u, 0u, 0u, 0u);
-    }
-    return;
-  }
-
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&q_full[a], 1);
+      mbar_init(&q_empty[a], 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) mbar_init(&s_full[a], 1);
-    mbar_init(p_full, 8);
-    for (int q = 0; q < 4; ++q) mbar_init(reinterpret_cast<uint64_t*>(smem + Smem::kPair) + q, 64);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&s_full[a], 1);
+      mbar_init(&p_full[a], 8);  // one arrive per softmax warp
+      mbar_init(&pv_done[a], 1);
+    }
     mbar_init(p_empty, 1);
+    mbar_init(o_free, 8);
     mbar_init(mma_done, 1);
+    for (int q = 0; q < 4; ++q) mbar_init(reinterpret_cast<uint64_t*>(smem + Smem::kPair) + q, 64);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -258,63 +335,82 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&q_map)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&k_map)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&v_map)) : "memory");
-      mbar_arrive_expect_tx(q_full, kTile);
-      tma_load_3d(sm + Smem::kQ, &q_map, 0, qh, q_begin + q0, smem_u32(q_full));
-      tma_load_3d(sm + Smem::kQ + kHalf, &q_map, 64, qh, q_begin + q0, smem_u32(q_full));
-      const int32_t* bt = p.block_table + int64_t(b) * p.bt_stride;
-      const int n_pages = (ctx + kPage - 1) / kPage;
-      const int hy = p.heads_outer ? 0 : kvh, hz = p.heads_outer ? kvh : 0;
-      // one 128-key tile of K or V: 8 pages (16 copies) or one 128-row box per half
-      auto load_tile = [&](uint32_t dst, const CUtensorMap* map, int j, const int32_t (&ids)[kPagesPerTile],
-                           uint64_t* bar) {
-        if constexpr (PAGED) {
+      uint32_t g = 0, nq = 0;    // K/V tiles and Q tiles loaded so far
+      uint32_t k_done = 0, v_done = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+        const Item it = make_item<PAGED>(p, prefix, w);
+        if (it.n_tiles == 0) continue;
+        // the S products of the item two back have read this Q buffer
+        const int qb = nq & 1;
+        if (nq >= 2 && !mbar_wait(&q_empty[qb], ((nq / 2) - 1) & 1, p.err)) break;
+        mbar_arrive_expect_tx(&q_full[qb], kTile);
+        tma_load_3d(sm + Smem::kQ + qb * kTile, &q_map, 0, it.qh, it.q_begin + it.q0, smem_u32(&q_full[qb]));
+        tma_load_3d(sm + Smem::kQ + qb * kTile + kHalf, &q_map, 64, it.qh, it.q_begin + it.q0,
+                    smem_u32(&q_full[qb]));
+        ++nq;
+        const int32_t* bt = p.block_table + int64_t(it.b) * p.bt_stride;
+        const int n_pages = (it.ctx + kPage - 1) / kPage;
+        const int hy = p.heads_outer ? 0 : it.kvh, hz = p.heads_outer ? it.kvh : 0;
+        for (int j = 0; j < it.n_tiles; ++j, ++g) {
+          const int s = g & 1;
+          int32_t ids[kPagesPerTile];
 #pragma unroll
           for (int pg = 0; pg < kPagesPerTile; ++pg) {
-            tma_load_4d(dst + pg * kPageBytes, map, 0, hy, hz, ids[pg], smem_u32(bar));
-            tma_load_4d(dst + kHalf + pg * kPageBytes, map, 64, hy, hz, ids[pg], smem_u32(bar));
-          }
-        } else {
-          tma_load_3d(dst, map, 0, kvh, k_begin + j * kBKV, smem_u32(bar));
-          tma_load_3d(dst + kHalf, map, 64, kvh, k_begin + j * kBKV, smem_u32(bar));
-        }
-      };
-      int issued = 0;
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j & 1;
-        int32_t ids[kPagesPerTile];
-#pragma unroll
-        for (int pg = 0; pg < kPagesPerTile; ++pg) {
-          int32_t id = -1;  // pages past the context: zero fill (masked anyway)
-          if constexpr (PAGED) {
-            const int lb = j * kPagesPerTile + pg;
-            if (lb < n_pages) {
-              id = bt[lb];
-              if (id < 0 || id >= p.num_blocks) {
-                raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
-                id = -1;
+            int32_t id = -1;  // pages past the context: zero fill (masked anyway)
+            if constexpr (PAGED) {
+              const int lb = j * kPagesPerTile + pg;
+              if (lb < n_pages) {
+                id = bt[lb];
+                if (id < 0 || id >= p.num_blocks) {
+                  raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
+                  id = -1;
+                }
               }
             }
+            ids[pg] = id;
           }
-          ids[pg] = id;
+          if (g >= kStages && !mbar_wait(&k_empty[s], ((g / kStages) - 1) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[s], kTile);
+          const uint32_t kdst = sm + Smem::kK + s * kTile;
+          if constexpr (PAGED) {
+#pragma unroll
+            for (int pg = 0; pg < kPagesPerTile; ++pg) {
+              tma_load_4d(kdst + pg * kPageBytes, &k_map, 0, hy, hz, ids[pg], smem_u32(&k_full[s]));
+              tma_load_4d(kdst + kHalf + pg * kPageBytes, &k_map, 64, hy, hz, ids[pg], smem_u32(&k_full[s]));
+            }
+          } else {
+            tma_load_3d(kdst, &k_map, 0, it.kvh, it.k_begin + j * kBKV, smem_u32(&k_full[s]));
+            tma_load_3d(kdst + kHalf, &k_map, 64, it.kvh, it.k_begin + j * kBKV, smem_u32(&k_full[s]));
+          }
+          k_done = g + 1;
+          if (g >= kStages && !mbar_wait(&v_empty[s], ((g / kStages) - 1) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[s], kTile);
+          const uint32_t vdst = sm + Smem::kV + s * kTile;
+          if constexpr (PAGED) {
+#pragma unroll
+            for (int pg = 0; pg < kPagesPerTile; ++pg) {
+              tma_load_4d(vdst + pg * kPageBytes, &v_map, 0, hy, hz, ids[pg], smem_u32(&v_full[s]));
+              tma_load_4d(vdst + kHalf + pg * kPageBytes, &v_map, 64, hy, hz, ids[pg], smem_u32(&v_full[s]));
+            }
+          } else {
+            tma_load_3d(vdst, &v_map, 0, it.kvh, it.k_begin + j * kBKV, smem_u32(&v_full[s]));
+            tma_load_3d(vdst + kHalf, &v_map, 64, it.kvh, it.k_begin + j * kBKV, smem_u32(&v_full[s]));
+          }
+          v_done = g + 1;
         }
-        if (j >= kStages && !mbar_wait(&k_empty[s], ((j / kStages) - 1) & 1, p.err)) break;
-        mbar_arrive_expect_tx(&k_full[s], kTile);
-        load_tile(sm + Smem::kK + s * kTile, &k_map, j, ids, &k_full[s]);
-        if (j >= kStages && !mbar_wait(&v_empty[s], ((j / kStages) - 1) & 1, p.err)) {
-          issued = -(j + 1);  // K of tile j is in flight, V is not
-          break;
-        }
-        mbar_arrive_expect_tx(&v_full[s], kTile);
-        load_tile(sm + Smem::kV + s * kTile, &v_map, j, ids, &v_full[s]);
-        issued = j + 1;
       }
-      // drain the copies that may still be in flight (the last tile of each stage)
-      mbar_wait(q_full, 0, p.err);
-      const int k_issued = issued < 0 ? -issued : issued;
-      const int v_issued = issued < 0 ? -issued - 1 : issued;
-      for (int j = k_issued > kStages ? k_issued - kStages : 0; j < k_issued; ++j)
+      // drain the copies that may still be in flight
+      for (uint32_t j = nq > 2 ? nq - 2 : 0; j < nq; ++j) mbar_wait(&q_full[j & 1], (j / 2) & 1, p.err);
+      for (uint32_t j = k_done > kStages ? k_done - kStages : 0; j < k_done; ++j)
         mbar_wait(&k_full[j & 1], (j / kStages) & 1, p.err);
-      for (int j = v_issued > kStages ? v_issued - kStages : 0; j < v_issued; ++j)
+      for (uint32_t j = v_done > kStages ? v_done - kStages : 0; j < v_done; ++j)
         mbar_wait(&v_full[j & 1], (j / kStages) & 1, p.err);
     }
   } else if (warp == 1) {
@@ -323,17 +419,18 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
       constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
       const uint32_t idesc_s = make_idesc(kBf16, kBQ, kBKV);
       const uint32_t idesc_o = make_idesc(kBf16, kBQ, kD) | (1u << 16);  // B (V) MN-major
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j / kStages) & 1, p.err)) return false;
-        // S[s] holds P_{j-2} until O += P_{j-2} V_{j-2} has read it (the newest product
-        // issued so far, so its phase cannot be overtaken)
-        if (j >= 2 && !mbar_wait(p_empty, (j - 2) & 1, p.err)) return false;
+      // S_g = Q K_g^T into S[g & 1], Q from buffer qb
+      auto issue_s = [&](uint32_t g, int qb) -> bool {
+        const int s = g & 1;
+        if (!mbar_wait(&k_full[s], (g / kStages) & 1, p.err)) return false;
+        // S[s] holds P_{g-2} until O += P_{g-2} V_{g-2} has read it (pv_done[s] completes
+        // once per product on this buffer; the next one, g, is not issued yet)
+        if (g >= 2 && !mbar_wait(&pv_done[s], ((g / 2) - 1) & 1, p.err)) return false;
         tc_fence_after();
         const uint32_t kb = sm + Smem::kK + s * kTile;
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          const uint64_t adesc = sw128_kmajor_desc(sm + Smem::kQ + hf * kHalf);
+          const uint64_t adesc = sw128_kmajor_desc(sm + Smem::kQ + qb * kTile + hf * kHalf);
           const uint64_t bdesc = sw128_kmajor_desc(kb + hf * kHalf);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
@@ -343,26 +440,49 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
         umma_commit(&s_full[s]);
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, p.err);
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        const int s = j & 1;
-        if (!mbar_wait(p_full, j & 1, p.err)) break;
-        if (!mbar_wait(&v_full[s], (j / kStages) & 1, p.err)) break;
-        tc_fence_after();
-        const uint32_t vb = sm + Smem::kV + s * kTile;
+      uint32_t g = 0, nq = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+        const Item it = make_item<PAGED>(p, prefix, w);
+        if (it.n_tiles == 0) continue;
+        const int qb = nq & 1;
+        if (!mbar_wait(&q_full[qb], (nq / 2) & 1, p.err) || !issue_s(g, qb)) break;
+        if (it.n_tiles == 1) umma_commit(&q_empty[qb]);
+        for (int j = 0; j < it.n_tiles; ++j, ++g) {
+          if (j + 1 < it.n_tiles) {
+            if (!issue_s(g + 1, qb)) {
+              ok = false;
+              break;
+            }
+            if (j + 2 == it.n_tiles) umma_commit(&q_empty[qb]);  // the item's last S product is issued
+          }
+          const int s = g & 1;
+          if (!mbar_wait(&p_full[s], (g / 2) & 1, p.err) || !mbar_wait(&v_full[s], (g / kStages) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          // O is overwritten by the item's first product only after the previous item's
+          // epilogue has read it
+          if (j == 0 && nq >= 1 && !mbar_wait(o_free, (nq - 1) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t vb = sm + Smem::kV + s * kTile;
 #pragma unroll
-        for (int kk = 0; kk < kBKV / 16; ++kk) {
-          // A: P_j in TMEM over S[s], keys [16 kk, +16) = 8 packed columns (keys 0-63 at
-          // columns 0-31, keys 64-127 at 64-95); B: V rows [16 kk, +16) (2 KB apart), both
-          // 64-column halves of the head dimension
-          const uint32_t a_tmem = tmem + s * kBKV + (kk >> 2) * 64 + (kk & 3) * 8;
-          const uint64_t bdesc = sw128_mnmajor_desc(vb + kk * 2048, kHalf);
-          umma_f16_tmem_a(tmem + kTmemO, a_tmem, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBKV / 16; ++kk) {
+            // A: P_g in TMEM over S[s], keys [16 kk, +16) = 8 packed columns (keys 0-63 at
+            // columns 0-31, keys 64-127 at 64-95); B: V rows [16 kk, +16) (2 KB apart),
+            // both 64-column halves of the head dimension
+            const uint32_t a_tmem = tmem + s * kBKV + (kk >> 2) * 64 + (kk & 3) * 8;
+            const uint64_t bdesc = sw128_mnmajor_desc(vb + kk * 2048, kHalf);
+            umma_f16_tmem_a(tmem + kTmemO, a_tmem, bdesc, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&v_empty[s]);
+          umma_commit(&pv_done[s]);
+          umma_commit(p_empty);
         }
-        umma_commit(&v_empty[s]);
-        umma_commit(p_empty);
+        ++nq;
       }
       // every issued MMA completes before TMEM may be released
       umma_commit(mma_done);
@@ -377,15 +497,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
     const int half = (warp - 2) >> 2;
     const int col0 = half * 64;
     const int r = quad * 32 + lane;  // query row within the tile (= TMEM lane)
-    const int qi = q0 + r;
     const uint32_t lanes = uint32_t(quad * 32) << 16;
     float* red = reinterpret_cast<float*>(smem + Smem::kRed);  // [2 buffers][2 halves][128 rows]
     uint64_t* pair = reinterpret_cast<uint64_t*>(smem + Smem::kPair) + quad;
     uint32_t pair_uses = 0;
-    int limit = p.causal ? shift + qi + 1 : ctx;  // this row sees keys [0, limit)
-    if (limit > ctx) limit = ctx;
-    float m_run = -INFINITY;  // running max of scale*s*log2(e), the same in both warps of the row
-    float l_run = 0.f;        // this warp's half of the running sum
     // exchange one float per row with the partner warp; false if the partner never came
     auto exchange = [&](float mine, float& theirs) -> bool {
       float* buf = red + (pair_uses & 1) * 256;
@@ -396,81 +511,96 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
       ++pair_uses;
       return got;
     };
+    uint32_t g = 0;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int s = j & 1;
-      if (!mbar_wait(&s_full[s], (j / kStages) & 1, p.err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float x[64];
+    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      const Item it = make_item<PAGED>(p, prefix, w);
+      const int qi = it.q0 + r;
+      T* orow = out + int64_t(it.q_begin + qi) * p.o_tok_stride + int64_t(it.qh) * p.o_head_stride + col0;
+      if (it.n_tiles == 0) {
+        // no visible key (empty context): zero rows, as for an empty softmax
+        if (r < it.rows)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t v[32];
-        __syncwarp();
-        tmem_ld_32(tmem + lanes + s * kBKV + col0 + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(v[i]);
+          for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0u, 0u, 0u, 0u);
+        continue;
       }
-      const int nvalid = limit - j * kBKV - col0;  // columns col0 + i are visible iff i < nvalid
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
-      if (nvalid >= 64) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          x[i] *= p.scale_log2;
-          m4[i & 3] = fmaxf(m4[i & 3], x[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          x[i] = i < nvalid ? x[i] * p.scale_log2 : -INFINITY;
-          m4[i & 3] = fmaxf(m4[i & 3], x[i]);
-        }
-      }
-      float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      float other;
-      if (!exchange(mx, other)) {
-        ok = false;
-        break;
-      }
-      mx = fmaxf(mx, other);
-      // lazy max refresh, identical in both warps of a row (same rows, same combined max);
-      // warp-uniform, since O is rescaled with warp-wide TMEM accesses
-      const float m_new = fmaxf(m_run, mx);
-      const bool grow = m_new > m_run + kRescaleLog2;  // also true for the first finite max
-      float alpha = 1.f;
-      const bool any = __any_sync(0xffffffffu, grow);
-      if (any) {
-        alpha = m_run == -INFINITY ? 0.f : hw_exp2(m_run - m_new);
-        if (m_new != -INFINITY) {
-          l_run *= alpha;
-          m_run = m_new;
-        } else {
-          alpha = 1.f;
-        }
-      }
-      const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      uint32_t pk[32];
-      float l4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float p0 = hw_exp2(x[2 * i] - m_use);
-        const float p1 = hw_exp2(x[2 * i + 1] - m_use);
-        l4[i & 3] += p0 + p1;
-        pk[i] = pack2<T>(p0, p1);
-      }
-      l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
-
-      // O is rescaled only once O += P_{j-1} V_{j-1} is complete (and before P_j is
-      // released, so the next product sees the new scale)
-      if (j > 0 && any) {
-        if (!mbar_wait(p_empty, (j - 1) & 1, p.err)) {
+      int limit = p.causal ? it.shift + qi + 1 : it.ctx;  // this row sees keys [0, limit)
+      if (limit > it.ctx) limit = it.ctx;
+      float m_run = -INFINITY;  // running max of scale*s*log2(e), the same in both warps of a row
+      float l_run = 0.f;        // this warp's half of the running sum
+      for (int j = 0; j < it.n_tiles; ++j, ++g) {
+        const int s = g & 1;
+        if (!mbar_wait(&s_full[s], (g / 2) & 1, p.err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        {
+        float x[64];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld_32(tmem + lanes + s * kBKV + col0 + c * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(v[i]);
+        }
+        const int nvalid = limit - j * kBKV - col0;  // columns col0 + i are visible iff i < nvalid
+        float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
+        if (nvalid >= 64) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            x[i] *= p.scale_log2;
+            m4[i & 3] = fmaxf(m4[i & 3], x[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
+            x[i] = i < nvalid ? x[i] * p.scale_log2 : -INFINITY;
+            m4[i & 3] = fmaxf(m4[i & 3], x[i]);
+          }
+        }
+        float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        float other;
+        if (!exchange(mx, other)) {
+          ok = false;
+          break;
+        }
+        mx = fmaxf(mx, other);
+        // lazy max refresh, identical in both warps of a row (same rows, same combined max);
+        // warp-uniform, since O is rescaled with warp-wide TMEM accesses
+        const float m_new = fmaxf(m_run, mx);
+        const bool grow = m_new > m_run + kRescaleLog2;  // also true for the first finite max
+        float alpha = 1.f;
+        const bool any = __any_sync(0xffffffffu, grow);
+        if (any) {
+          alpha = m_run == -INFINITY ? 0.f : hw_exp2(m_run - m_new);
+          if (m_new != -INFINITY) {
+            l_run *= alpha;
+            m_run = m_new;
+          } else {
+            alpha = 1.f;
+          }
+        }
+        const float m_use = m_run == -INFINITY ? 0.f : m_run;
+        uint32_t pk[32];
+        float l4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = hw_exp2(x[2 * i] - m_use);
+          const float p1 = hw_exp2(x[2 * i + 1] - m_use);
+          l4[i & 3] += p0 + p1;
+          pk[i] = pack2<T>(p0, p1);
+        }
+        l_run += (l4[0] + l4[1]) + (l4[2] + l4[3]);
+
+        // O is rescaled only once O += P_{g-1} V_{g-1} is complete (and before P_g is
+        // released, so the next product sees the new scale)
+        if (j > 0 && any) {
+          if (!mbar_wait(p_empty, (g - 1) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 2; ++c) {
             uint32_t v[32];
@@ -482,60 +612,68 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
           }
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
-      }
-      if (ctx > j * kBKV && ctx < (j + 1) * kBKV && (!PAGED || (ctx & (kPage - 1)) != 0)) {
-        // V rows past the context that were copied in hold whatever memory held there (the
-        // rest of the last page, or the rows after the sequence): zero them, so that P = 0
-        // never meets a non-finite value.  (Pages wholly past the context read as zeros.)
-        if (!mbar_wait(&v_full[s], (j / kStages) & 1, p.err)) {
-          ok = false;
-          break;
+        if (it.ctx > j * kBKV && it.ctx < (j + 1) * kBKV && (!PAGED || (it.ctx & (kPage - 1)) != 0)) {
+          // V rows past the context that were copied in hold whatever memory held there
+          // (the rest of the last page, or the rows after the sequence): zero them, so
+          // that P = 0 never meets a non-finite value.  (Pages wholly past the context
+          // read as zeros.)
+          if (!mbar_wait(&v_full[s], (g / kStages) & 1, p.err)) {
+            ok = false;
+            break;
+          }
+          const int t0 = it.ctx - j * kBKV;
+          const int t1 = PAGED ? ((it.ctx + kPage - 1) / kPage) * kPage - j * kBKV : kBKV;  // <= kBKV
+          uint8_t* vb = smem + Smem::kV + s * kTile;
+          for (int i = threadIdx.x - 64; i < (t1 - t0) * 16; i += kSoftmaxThreads) {
+            const int row = t0 + (i >> 4), hf = (i >> 3) & 1, c = i & 7;
+            *reinterpret_cast<uint4*>(vb + hf * kHalf + row * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
         }
-        const int t0 = ctx - j * kBKV;
-        const int t1 = PAGED ? ((ctx + kPage - 1) / kPage) * kPage - j * kBKV : kBKV;  // <= kBKV
-        uint8_t* vb = smem + Smem::kV + s * kTile;
-        for (int i = threadIdx.x - 64; i < (t1 - t0) * 16; i += kSoftmaxThreads) {
-          const int row = t0 + (i >> 4), hf = (i >> 3) & 1, c = i & 7;
-          *reinterpret_cast<uint4*>(vb + hf * kHalf + row * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+        // P_g (this warp's 64 keys, packed in pairs) over the first 32 of the S columns
+        // this warp has just read
+        __syncwarp();
+        tmem_st_32(tmem + lanes + s * kBKV + col0, pk);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[s]);
       }
-      // P_j (this warp's 64 keys, packed in pairs) over the first 32 of the S columns this
-      // warp has just read
-      __syncwarp();
-      tmem_st_32(tmem + lanes + s * kBKV + col0, pk);
-      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      if (!ok) break;
+      // the item's last product is complete: O is final
+      ok = mbar_wait(p_empty, (g - 1) & 1, p.err);
+      float l_other = 0.f;
+      if (ok) ok = exchange(l_run, l_other);
+      tc_fence_after();
+      const float l = l_run + l_other;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint32_t o[64];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld_32(tmem + lanes + kTmemO + col0 + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[c * 32 + i] = v[i];
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-    }
-    if (ok) ok = mbar_wait(p_empty, (n_tiles - 1) & 1, p.err);
-    float l_other = 0.f;
-    if (ok) ok = exchange(l_run, l_other);
-    tc_fence_after();
-    const float l = l_run + l_other;
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    T* orow = out + int64_t(q_begin + qi) * p.o_tok_stride + int64_t(qh) * p.o_head_stride + col0;
-#pragma unroll 1
-    for (int c = 0; c < 2; ++c) {
-      uint32_t v[32];
-      __syncwarp();
-      tmem_ld_32(tmem + lanes + kTmemO + col0 + c * 32, v);
-      if (ok && r < rows) {
+      if (lane == 0) mbar_arrive(o_free);  // the next item may overwrite O
+      if (ok && r < it.rows) {
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          uint4 w;
-          w.x = pack2<T>(__uint_as_float(v[g * 8 + 0]) * inv, __uint_as_float(v[g * 8 + 1]) * inv);
-          w.y = pack2<T>(__uint_as_float(v[g * 8 + 2]) * inv, __uint_as_float(v[g * 8 + 3]) * inv);
-          w.z = pack2<T>(__uint_as_float(v[g * 8 + 4]) * inv, __uint_as_float(v[g * 8 + 5]) * inv);
-          w.w = pack2<T>(__uint_as_float(v[g * 8 + 6]) * inv, __uint_as_float(v[g * 8 + 7]) * inv);
-          reinterpret_cast<uint4*>(orow + c * 32)[g] = w;
+        for (int g8 = 0; g8 < 8; ++g8) {
+          uint4 w4;
+          w4.x = pack2<T>(__uint_as_float(o[g8 * 8 + 0]) * inv, __uint_as_float(o[g8 * 8 + 1]) * inv);
+          w4.y = pack2<T>(__uint_as_float(o[g8 * 8 + 2]) * inv, __uint_as_float(o[g8 * 8 + 3]) * inv);
+          w4.z = pack2<T>(__uint_as_float(o[g8 * 8 + 4]) * inv, __uint_as_float(o[g8 * 8 + 5]) * inv);
+          w4.w = pack2<T>(__uint_as_float(o[g8 * 8 + 6]) * inv, __uint_as_float(o[g8 * 8 + 7]) * inv);
+          reinterpret_cast<uint4*>(orow)[g8] = w4;
         }
       }
     }
-    tc_fence_before();
   }
 
+  tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -588,14 +726,21 @@ int make_cache_map(CUtensorMap* map, const void* base, bool bf16, int64_t blocks
   return NTB200_OK;
 }
 
+// Persistent grid: at most one CTA per SM, and no more CTAs than the work items can be
+// (sum over sequences of ceil(q_len / 128), times the q heads, bounded from the host's view).
 template <typename T, bool PAGED>
 int launch_prefill(const CUtensorMap& qm, const CUtensorMap& km, const CUtensorMap& vm, const PrefillParams& prm,
-                   dim3 grid, cudaStream_t s, int slot) {
+                   int64_t max_query_len, cudaStream_t s, int slot) {
   const void* fn = reinterpret_cast<const void*>(paged_prefill_kernel<T, PAGED>);
-  int st = ensure_smem_attribute(fn, Smem::kDynamicBytes, slot);
+  const int bytes = Smem::bytes_for(prm.num_seqs);
+  int st = ensure_smem_attribute(fn, bytes, slot);
   if (st != NTB200_OK) return st;
-  return launch_kernel(PAGED ? "paged_attention_prefill" : "flash_attn_varlen", paged_prefill_kernel<T, PAGED>, grid,
-                       dim3(kThreads), Smem::kDynamicBytes, s, qm, km, vm, prm);
+  const int64_t by_len = ceil_div(max_query_len, kBQ) * prm.num_seqs;
+  const int64_t by_tokens = ceil_div(int64_t(prm.num_tokens), kBQ) + prm.num_seqs;
+  const int64_t items = (by_len < by_tokens ? by_len : by_tokens) * prm.num_q_heads;
+  const int64_t grid = items < num_sms() ? items : num_sms();
+  return launch_kernel(PAGED ? "paged_attention_prefill" : "flash_attn_varlen", paged_prefill_kernel<T, PAGED>,
+                       dim3(static_cast<unsigned>(grid)), dim3(kThreads), bytes, s, qm, km, vm, prm);
 }
 
 PrefillParams base_params(void* out, const int32_t* query_start_loc, int64_t num_tokens, int64_t num_q_heads,
@@ -607,6 +752,7 @@ PrefillParams base_params(void* out, const int32_t* query_start_loc, int64_t num
   prm.o_tok_stride = out_token_stride;
   prm.o_head_stride = out_head_stride;
   prm.num_tokens = static_cast<int>(num_tokens);
+  prm.num_q_heads = static_cast<int>(num_q_heads);
   prm.group = static_cast<int>(num_q_heads / num_kv_heads);
   prm.causal = causal ? 1 : 0;
   prm.scale_log2 = scale * 1.4426950408889634f;  // softmax in the exp2 domain
@@ -617,14 +763,17 @@ PrefillParams base_params(void* out, const int32_t* query_start_loc, int64_t num
 }  // namespace
 }  // namespace ntb200
 
-extern "C" int ntb200_paged_attention_prefill(
-    void* out, const void* query, const void* key_cache, const void* value_cache, const int32_t* query_start_loc,
-    const int32_t* seq_lens, const int32_t* block_tables, int64_t num_seqs, int64_t num_tokens,
-    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size, int64_t num_blocks,
-    int64_t max_blocks_per_seq, int64_t block_table_stride, int64_t max_query_len, float scale, int causal,
-    int64_t q_token_stride, int64_t q_head_stride, int64_t out_token_stride, int64_t out_head_stride,
-    int64_t cache_block_stride, int64_t cache_page_stride, int64_t cache_head_stride, int dtype, void* stream) {
-  using namespace ntb200;
+namespace ntb200 {
+namespace {
+
+int prefill_paged(void* out, const void* query, const void* key_cache, const void* value_cache,
+                  const int32_t* query_start_loc, const int32_t* seq_lens, const int32_t* block_tables,
+                  int64_t num_seqs, int64_t num_tokens, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                  int64_t block_size, int64_t num_blocks, int64_t max_blocks_per_seq, int64_t block_table_stride,
+                  int64_t max_query_len, float scale, int causal, int64_t q_token_stride, int64_t q_head_stride,
+                  int64_t out_token_stride, int64_t out_head_stride, int64_t cache_block_stride,
+                  int64_t cache_page_stride, int64_t cache_head_stride, int dtype, void* stream,
+                  bool skip_single_query) {
   if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
     return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "paged_attention_prefill: dtype %d (bf16/f16 only)", dtype);
   if (head_size != kD || block_size != kPage)
@@ -634,7 +783,7 @@ extern "C" int ntb200_paged_attention_prefill(
       num_blocks <= 0 || max_blocks_per_seq < 0 || block_table_stride < max_blocks_per_seq)
     return fail(NTB200_ERR_INVALID_ARGUMENT, "paged_attention_prefill: bad sizes");
   if (num_seqs == 0 || num_tokens == 0 || max_query_len <= 0) return NTB200_OK;
-  if (num_seqs > 65535 || num_q_heads > 65535 || num_tokens > 0x7fffffff || num_blocks > 0x7fffffff ||
+  if (num_seqs > Smem::kMaxSeqs || num_q_heads > 65535 || num_tokens > 0x7fffffff || num_blocks > 0x7fffffff ||
       max_blocks_per_seq * kPage > 0x7fffffff)
     return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "paged_attention_prefill: sizes beyond the launch limits");
   if (!out || !query || !key_cache || !value_cache || !query_start_loc || !seq_lens || !block_tables)
@@ -661,11 +810,28 @@ extern "C" int ntb200_paged_attention_prefill(
   prm.max_blocks = static_cast<int>(max_blocks_per_seq);
   prm.num_blocks = static_cast<int>(num_blocks);
   prm.heads_outer = cache_head_stride > cache_page_stride ? 1 : 0;
-  const dim3 grid(static_cast<unsigned>(ceil_div(max_query_len, kBQ)), static_cast<unsigned>(num_q_heads),
-                  static_cast<unsigned>(num_seqs));
+  prm.num_seqs = static_cast<int>(num_seqs);
+  prm.skip_single_query = skip_single_query ? 1 : 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return bf16 ? launch_prefill<__nv_bfloat16, true>(qm, km, vm, prm, grid, s, 90)
-              : launch_prefill<__half, true>(qm, km, vm, prm, grid, s, 91);
+  return bf16 ? launch_prefill<__nv_bfloat16, true>(qm, km, vm, prm, max_query_len, s, 90)
+              : launch_prefill<__half, true>(qm, km, vm, prm, max_query_len, s, 91);
+}
+
+}  // namespace
+}  // namespace ntb200
+
+extern "C" int ntb200_paged_attention_prefill(
+    void* out, const void* query, const void* key_cache, const void* value_cache, const int32_t* query_start_loc,
+    const int32_t* seq_lens, const int32_t* block_tables, int64_t num_seqs, int64_t num_tokens,
+    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size, int64_t num_blocks,
+    int64_t max_blocks_per_seq, int64_t block_table_stride, int64_t max_query_len, float scale, int causal,
+    int64_t q_token_stride, int64_t q_head_stride, int64_t out_token_stride, int64_t out_head_stride,
+    int64_t cache_block_stride, int64_t cache_page_stride, int64_t cache_head_stride, int dtype, void* stream) {
+  return ntb200::prefill_paged(out, query, key_cache, value_cache, query_start_loc, seq_lens, block_tables, num_seqs,
+                               num_tokens, num_q_heads, num_kv_heads, head_size, block_size, num_blocks,
+                               max_blocks_per_seq, block_table_stride, max_query_len, scale, causal, q_token_stride,
+                               q_head_stride, out_token_stride, out_head_stride, cache_block_stride,
+                               cache_page_stride, cache_head_stride, dtype, stream, false);
 }
 
 extern "C" int ntb200_flash_attn_varlen(void* out, const void* query, const void* key, const void* value,
@@ -685,7 +851,7 @@ extern "C" int ntb200_flash_attn_varlen(void* out, const void* query, const void
       num_q_heads % num_kv_heads != 0)
     return fail(NTB200_ERR_INVALID_ARGUMENT, "flash_attn_varlen: bad sizes");
   if (num_seqs == 0 || num_q_tokens == 0 || max_query_len <= 0) return NTB200_OK;
-  if (num_seqs > 65535 || num_q_heads > 65535 || num_q_tokens > 0x7fffffff || num_k_tokens > 0x7fffffff)
+  if (num_seqs > Smem::kMaxSeqs || num_q_heads > 65535 || num_q_tokens > 0x7fffffff || num_k_tokens > 0x7fffffff)
     return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "flash_attn_varlen: sizes beyond the launch limits");
   if (!out || !query || !key || !value || !cu_seqlens_q || !cu_seqlens_k)
     return fail(NTB200_ERR_INVALID_ARGUMENT, "flash_attn_varlen: null pointer");
@@ -710,9 +876,39 @@ extern "C" int ntb200_flash_attn_varlen(void* out, const void* query, const void
                                   out_token_stride, out_head_stride);
   prm.key_start_loc = cu_seqlens_k;
   prm.num_keys = static_cast<int>(num_k_tokens);
-  const dim3 grid(static_cast<unsigned>(ceil_div(max_query_len, kBQ)), static_cast<unsigned>(num_q_heads),
-                  static_cast<unsigned>(num_seqs));
+  prm.num_seqs = static_cast<int>(num_seqs);
+  prm.skip_single_query = 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return bf16 ? launch_prefill<__nv_bfloat16, false>(qm, km, vm, prm, grid, s, 92)
-              : launch_prefill<__half, false>(qm, km, vm, prm, grid, s, 93);
+  return bf16 ? launch_prefill<__nv_bfloat16, false>(qm, km, vm, prm, max_query_len, s, 92)
+              : launch_prefill<__half, false>(qm, km, vm, prm, max_query_len, s, 93);
+}
+
+// A vLLM batch of any mix: sequences with one query token go to the split-K decode kernel
+// (reading and writing their rows through query_start_loc), the others to the persistent
+// prefill kernel, which skips the single-token ones.  One launch of each (the decode one
+// is left out when every sequence has max_query_len > 1 queries).
+extern "C" int ntb200_paged_attention_varlen(
+    void* out, const void* query, const void* key_cache, const void* value_cache, const int32_t* query_start_loc,
+    const int32_t* seq_lens, const int32_t* block_tables, int64_t num_seqs, int64_t num_tokens,
+    int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size, int64_t block_size, int64_t num_blocks,
+    int64_t max_blocks_per_seq, int64_t block_table_stride, int64_t max_query_len, int64_t max_seq_len, float scale,
+    int64_t q_token_stride, int64_t q_head_stride, int64_t out_token_stride, int64_t out_head_stride,
+    int64_t cache_block_stride, int64_t cache_page_stride, int64_t cache_head_stride, void* workspace,
+    size_t workspace_bytes, int dtype, void* stream) {
+  using namespace ntb200;
+  if (num_seqs == 0 || num_tokens == 0 || max_query_len <= 0) return NTB200_OK;
+  const bool uniform_prefill = max_query_len > 1 && num_tokens == max_query_len * num_seqs;
+  if (!uniform_prefill) {
+    const int st = ntb200_paged_attention_decode_varlen(
+        out, query, key_cache, value_cache, query_start_loc, seq_lens, block_tables, num_seqs, num_q_heads,
+        num_kv_heads, head_size, block_size, num_blocks, max_blocks_per_seq, block_table_stride, max_seq_len, scale,
+        q_token_stride, q_head_stride, out_token_stride, out_head_stride, cache_block_stride, cache_page_stride,
+        cache_head_stride, workspace, workspace_bytes, dtype, stream);
+    if (st != NTB200_OK || max_query_len == 1) return st;
+  }
+  return prefill_paged(out, query, key_cache, value_cache, query_start_loc, seq_lens, block_tables, num_seqs,
+                       num_tokens, num_q_heads, num_kv_heads, head_size, block_size, num_blocks, max_blocks_per_seq,
+                       block_table_stride, max_query_len, scale, 1, q_token_stride, q_head_stride, out_token_stride,
+                       out_head_stride, cache_block_stride, cache_page_stride, cache_head_stride, dtype, stream,
+                       /*skip_single_query=*/true);
 }

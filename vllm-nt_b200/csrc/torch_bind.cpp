@@ -378,6 +378,53 @@ void prefill_flash_layout(at::Tensor output, const at::Tensor& query, const at::
                           block_table, max_query_len, scale, causal);
 }
 
+// Any vLLM batch (decodes, prefills, chunked prefills, mixed) on its combined cache: the
+// single-query sequences through the decode kernel, the rest through the prefill kernel.
+void attention_flash_layout(at::Tensor output, const at::Tensor& query, const at::Tensor& kv_cache,
+                            const at::Tensor& query_start_loc, const at::Tensor& seq_lens,
+                            const at::Tensor& block_table, int64_t num_tokens, int64_t max_query_len,
+                            int64_t max_seq_len, double scale, int64_t kv_dim) {
+  require_cuda(kv_cache, "kv_cache");
+  require_cuda(query, "query");
+  require_cuda(output, "output");
+  require_cuda(query_start_loc, "query_start_loc");
+  require_cuda(seq_lens, "seq_lens");
+  require_cuda(block_table, "block_table");
+  TORCH_CHECK((kv_dim == 0 || kv_dim == 1) && kv_cache.dim() == 5 && kv_cache.size(kv_dim) == 2,
+              "ntb200.attention_flash_layout: kv_cache must be [2, blocks, block_size, kv_heads, head_size] "
+              "(kv_dim 0) or [blocks, 2, block_size, kv_heads, head_size] (kv_dim 1)");
+  const at::Tensor kc = kv_cache.select(kv_dim, 0), vc = kv_cache.select(kv_dim, 1);
+  const int64_t head = kc.size(3);
+  at::Tensor q = query.dim() == 2 ? query.view({query.size(0), -1, head}) : query;
+  at::Tensor o = output.dim() == 2 ? output.view({output.size(0), -1, head}) : output;
+  TORCH_CHECK(num_tokens >= 0 && num_tokens <= q.size(0) && num_tokens <= o.size(0) && q.stride(2) == 1 &&
+                  o.stride(2) == 1 && o.size(1) == q.size(1) && o.scalar_type() == q.scalar_type() &&
+                  kc.scalar_type() == q.scalar_type() && kc.stride(3) == 1,
+              "ntb200.attention_flash_layout: query/output [tokens, heads, head_size] like the cache");
+  TORCH_CHECK(query_start_loc.scalar_type() == at::kInt && query_start_loc.is_contiguous() &&
+                  query_start_loc.dim() == 1 && query_start_loc.numel() >= 1 &&
+                  seq_lens.scalar_type() == at::kInt && seq_lens.is_contiguous() &&
+                  seq_lens.numel() >= query_start_loc.numel() - 1 && block_table.scalar_type() == at::kInt &&
+                  block_table.dim() == 2 && block_table.stride(1) == 1 &&
+                  block_table.size(0) >= query_start_loc.numel() - 1,
+              "ntb200.attention_flash_layout: int32 query_start_loc [seqs + 1], seq_lens [seqs], "
+              "block_table [seqs, max_blocks]");
+  const int64_t seqs = query_start_loc.numel() - 1;
+  const int64_t cap = block_table.size(1) * kc.size(1);
+  const int64_t msl = max_seq_len <= 0 || max_seq_len > cap ? cap : max_seq_len;
+  const size_t need = ntb200_paged_attention_decode_workspace_size(seqs, q.size(1), kc.size(2), head, kc.size(1), msl);
+  at::Tensor ws = at::empty({static_cast<int64_t>(need > 256 ? need : 256)}, query.options().dtype(at::kByte));
+  c10::cuda::CUDAGuard guard(query.device());
+  check(ntb200_paged_attention_varlen(
+            o.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), query_start_loc.data_ptr<int32_t>(),
+            seq_lens.data_ptr<int32_t>(), block_table.data_ptr<int32_t>(), seqs, num_tokens, q.size(1), kc.size(2),
+            head, kc.size(1), kc.size(0), block_table.size(1), block_table.stride(0), max_query_len, msl,
+            static_cast<float>(scale), q.stride(0), q.stride(1), o.stride(0), o.stride(1), kc.stride(0),
+            kc.stride(1), kc.stride(2), ws.data_ptr(), static_cast<size_t>(ws.numel()), dtype_code(query),
+            stream_of(query)),
+        "attention_flash_layout");
+}
+
 void store_flash_layout(const at::Tensor& key, const at::Tensor& value, at::Tensor kv_cache,
                         const at::Tensor& slot_mapping, int64_t kv_dim) {
   require_cuda(kv_cache, "kv_cache");
@@ -541,6 +588,10 @@ TORCH_LIBRARY(ntb200, m) {
       "Tensor query_start_loc, Tensor seq_lens, Tensor block_table, int max_query_len, float scale, "
       "bool causal) -> ()");
   m.def(
+      "attention_flash_layout(Tensor(a!) output, Tensor query, Tensor kv_cache, Tensor query_start_loc, "
+      "Tensor seq_lens, Tensor block_table, int num_tokens, int max_query_len, int max_seq_len, float scale, "
+      "int kv_dim=0) -> ()");
+  m.def(
       "flash_attn_varlen(Tensor(a!) out, Tensor query, Tensor key, Tensor value, Tensor cu_seqlens_q, "
       "Tensor cu_seqlens_k, int max_query_len, float scale, bool causal) -> ()");
   m.def(
@@ -570,4 +621,5 @@ TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("paged_attention_prefill", &paged_attention_prefill);
   m.impl("prefill_flash_layout", &prefill_flash_layout);
   m.impl("flash_attn_varlen", &flash_attn_varlen);
+  m.impl("attention_flash_layout", &attention_flash_layout);
 }

@@ -63,6 +63,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_void_p] * 7 + [c_int64] * 10 + [c_float, c_int] + [c_int64] * 7 + [c_int, c_void_p],
     ),
+    "ntb200_paged_attention_decode_varlen": (
+        c_int,
+        [c_void_p] * 7 + [c_int64] * 9 + [c_float] + [c_int64] * 7 + [c_void_p, c_size_t, c_int, c_void_p],
+    ),
+    "ntb200_paged_attention_varlen": (
+        c_int,
+        [c_void_p] * 7 + [c_int64] * 11 + [c_float] + [c_int64] * 7 + [c_void_p, c_size_t, c_int, c_void_p],
+    ),
     "ntb200_flash_attn_varlen": (
         c_int,
         [c_void_p] * 6 + [c_int64] * 7 + [c_float, c_int] + [c_int64] * 8 + [c_int, c_void_p],

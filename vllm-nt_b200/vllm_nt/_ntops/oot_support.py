@@ -127,6 +127,15 @@ def paged_attention_prefill(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, s
     )
 
 
+def paged_attention_flash(output, query, kv_cache, query_start_loc, seq_lens, block_table, num_tokens,
+                          max_query_len, max_seq_len, scale, kv_dim=0):
+    """Causal attention for any vLLM batch (decodes, prefills, chunked prefills, mixed) on
+    its combined cache: single-query sequences on the split-K decode kernel, the others on
+    the tcgen05 prefill kernel; the first ``num_tokens`` rows of the padded activations."""
+    ops().attention_flash_layout(output, query, kv_cache, query_start_loc, seq_lens, block_table, num_tokens,
+                                 max_query_len, max_seq_len, scale, kv_dim)
+
+
 def paged_attention_prefill_flash(output, query, kv_cache, query_start_loc, seq_lens, block_table, num_tokens,
                                   max_query_len, scale, causal=True, kv_dim=0):
     """Varlen attention for the first ``num_tokens`` rows of vLLM's padded activations,

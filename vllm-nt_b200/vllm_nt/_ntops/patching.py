@@ -52,6 +52,7 @@ from vllm_nt._ntops.oot_support import (
     norm,
     nt_paged_decode,
     paged_attention_decode_flash,
+    paged_attention_flash,
     rope,
     store_kv_cache,
     store_kv_cache_flash,
@@ -452,8 +453,10 @@ def _build_flash_attn_kv_update(original: object) -> object:
 
 def _build_flash_attn_forward(original: object) -> object:
     """Replacement for FlashAttentionImpl.forward: pure-decode batches (one query token
-    per request) run on the split-K paged-decode kernel; everything else (prefill,
-    mixed batches, cascade) stays on vLLM's FlashAttention."""
+    per request) run on the split-K paged-decode kernel; prefill, chunked-prefill and mixed
+    batches on the tcgen05 prefill kernel (its single-query requests on the decode kernel),
+    reading K/V from the paged cache in place.  Cascade attention and non-causal metadata
+    stay on vLLM's FlashAttention."""
     if _is_function_patch(original, "PagedAttentionDecode"):
         return original
     original_fn = cast(Callable[..., Any], original)
@@ -470,23 +473,37 @@ def _build_flash_attn_forward(original: object) -> object:
             or output_scale is not None
             or output_block_scale is not None
             or getattr(meta, "use_cascade", False)
-            or getattr(meta, "max_query_len", 0) != 1
+            or not getattr(meta, "causal", True)
+            or getattr(meta, "max_query_len", 0) < 1
             or not query.is_cuda
             or not _attn_impl_supported(self, query.dtype, kv_cache)
         ):
             return call()
         n = int(meta.num_actual_tokens)
-        if getattr(meta, "query_start_loc", None) is not None and meta.query_start_loc.shape[0] - 1 != n:
+        qsl = getattr(meta, "query_start_loc", None)
+        max_q = int(meta.max_query_len)
+        if max_q == 1 and (qsl is None or qsl.shape[0] - 1 == n):
+
+            def kernels():
+                _record_hit("PagedAttentionDecode", query)
+                paged_attention_decode_flash(
+                    output, query, kv_cache, meta.seq_lens, meta.block_table, n, self.scale, int(meta.max_seq_len)
+                )
+                return output
+
+            return _route("PagedAttentionDecode", call, kernels)
+        if qsl is None:
             return call()
 
-        def kernels():
-            _record_hit("PagedAttentionDecode", query)
-            paged_attention_decode_flash(
-                output, query, kv_cache, meta.seq_lens, meta.block_table, n, self.scale, int(meta.max_seq_len)
+        def varlen():
+            _record_hit("PagedAttentionPrefill", query)
+            paged_attention_flash(
+                output, query, kv_cache, qsl, meta.seq_lens, meta.block_table, n, max_q, int(meta.max_seq_len),
+                self.scale,
             )
             return output
 
-        return _route("PagedAttentionDecode", call, kernels)
+        return _route("PagedAttentionPrefill", call, varlen)
 
     return _mark_function_patch(forward, "PagedAttentionDecode")
 

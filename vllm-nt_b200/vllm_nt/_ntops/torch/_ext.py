@@ -44,6 +44,7 @@ def _register_fakes() -> None:
         "paged_attention_prefill",
         "prefill_flash_layout",
         "flash_attn_varlen",
+        "attention_flash_layout",
     ):
         torch.library.register_fake(f"ntb200::{name}")(nothing)
 
