@@ -9,9 +9,11 @@
 //
 // Persistent: one CTA per SM walks the work items -- (128-query tile, q head) pairs of all
 // sequences, a sequence's last tile first -- found from a prefix sum of the query tiles
-// per sequence that every CTA builds in shared memory.  320 threads:
+// per sequence that every CTA builds in shared memory.  416 threads:
 //   warp 0     TMA: the Q tile (two 64-column halves, 128-byte swizzle; double-buffered
-//              across items), then per 128-key
+//              across items) and half of each K tile's pages; three more producer warps
+//              (after the softmax warps) issue the other half of K's and V's pages, so four
+//              threads issue copies at once (the issue rate of small copies limits).  Per
 //              tile the 8 K pages and the 8 V pages (16 tokens x 64 columns per copy) into
 //              2-stage rings; page ids come from the block table (ids out of range are
 //              reported and read as zeros: the copy lands outside the tensor map).
@@ -47,7 +49,11 @@ constexpr int kBKV = 128;                     // keys per tile
 constexpr int kPage = 16;                     // tokens per cache block
 constexpr int kPagesPerTile = kBKV / kPage;   // 8
 constexpr int kSoftmaxThreads = 256;           // warps 2-9: two per query row
-constexpr int kThreads = 64 + kSoftmaxThreads;
+// Copy issue: four threads (warp 0 and the three warps after the softmax warps), each
+// issuing half of a tile's pages of K or of V (and warp 0 also the Q tiles).
+constexpr int kParts = 2;                           // issuing threads per operand
+constexpr int kExtraWarp = 2 + kSoftmaxThreads / 32;  // first producer warp after the softmax warps
+constexpr int kThreads = 64 + kSoftmaxThreads + 32 * (2 * kParts - 1);
 constexpr int kHalf = 128 * 64 * 2;           // 128 rows x 64 columns: 16 KB
 constexpr int kTile = 2 * kHalf;              // 128 x 128: 32 KB
 constexpr int kPageBytes = kPage * 128;       // one page of one half: 16 rows x 128 B
@@ -302,9 +308,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
       mbar_init(&q_empty[a], 1);
     }
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&k_full[s], 1);
+      mbar_init(&k_full[s], kParts);  // one arrive (with its bytes) per issuing thread
       mbar_init(&k_empty[s], 1);
-      mbar_init(&v_full[s], 1);
+      mbar_init(&v_full[s], kParts);
       mbar_init(&v_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -329,81 +335,95 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------ TMA producer ------------------------------
+  if (warp == 0 || warp >= kExtraWarp) {
+    // ------------------------------ TMA producers ------------------------------
+    // role 0 (warp 0): Q and the first half of K's pages; role 1: the rest of K; roles 2
+    // and 3: V.  Contiguous K/V: each role copies one 64-column half of its operand.
+    const int role = warp == 0 ? 0 : warp - kExtraWarp + 1;
+    const bool v_role = role >= kParts;
+    const int part = role % kParts;
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&q_map)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&k_map)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&v_map)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(v_role ? &v_map : &q_map)) : "memory");
+      if (!v_role) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&k_map)) : "memory");
       uint32_t g = 0, nq = 0;    // K/V tiles and Q tiles loaded so far
       uint32_t k_done = 0, v_done = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
         const Item it = make_item<PAGED>(p, prefix, w);
         if (it.n_tiles == 0) continue;
-        // the S products of the item two back have read this Q buffer
-        const int qb = nq & 1;
-        if (nq >= 2 && !mbar_wait(&q_empty[qb], ((nq / 2) - 1) & 1, p.err)) break;
-        mbar_arrive_expect_tx(&q_full[qb], kTile);
-        tma_load_3d(sm + Smem::kQ + qb * kTile, &q_map, 0, it.qh, it.q_begin + it.q0, smem_u32(&q_full[qb]));
-        tma_load_3d(sm + Smem::kQ + qb * kTile + kHalf, &q_map, 64, it.qh, it.q_begin + it.q0,
-                    smem_u32(&q_full[qb]));
-        ++nq;
+        if (role == 0) {
+          // the S products of the item two back have read this Q buffer
+          const int qb = nq & 1;
+          if (nq >= 2 && !mbar_wait(&q_empty[qb], ((nq / 2) - 1) & 1, p.err)) break;
+          mbar_arrive_expect_tx(&q_full[qb], kTile);
+          tma_load_3d(sm + Smem::kQ + qb * kTile, &q_map, 0, it.qh, it.q_begin + it.q0, smem_u32(&q_full[qb]));
+          tma_load_3d(sm + Smem::kQ + qb * kTile + kHalf, &q_map, 64, it.qh, it.q_begin + it.q0,
+                      smem_u32(&q_full[qb]));
+          ++nq;
+        }
         const int32_t* bt = p.block_table + int64_t(it.b) * p.bt_stride;
         const int n_pages = (it.ctx + kPage - 1) / kPage;
         const int hy = p.heads_outer ? 0 : it.kvh, hz = p.heads_outer ? it.kvh : 0;
+        // page ids of tile j (-1: past the context, read as zeros and masked anyway); the
+        // next tile's are fetched while this tile's copies are issued, so the block-table
+        // round trip is off the copy path
+        auto fetch_ids = [&](int j, int32_t (&ids)[kPagesPerTile]) {
+#pragma unroll
+          for (int pg = 0; pg < kPagesPerTile; ++pg) {
+            const int lb = j * kPagesPerTile + pg;
+            ids[pg] = PAGED && lb < n_pages ? __ldg(bt + lb) : -1;
+          }
+        };
+        int32_t next_ids[kPagesPerTile];
+        fetch_ids(0, next_ids);
         for (int j = 0; j < it.n_tiles; ++j, ++g) {
           const int s = g & 1;
           int32_t ids[kPagesPerTile];
 #pragma unroll
           for (int pg = 0; pg < kPagesPerTile; ++pg) {
-            int32_t id = -1;  // pages past the context: zero fill (masked anyway)
-            if constexpr (PAGED) {
-              const int lb = j * kPagesPerTile + pg;
-              if (lb < n_pages) {
-                id = bt[lb];
-                if (id < 0 || id >= p.num_blocks) {
-                  raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
-                  id = -1;
-                }
-              }
+            ids[pg] = next_ids[pg];
+            if (ids[pg] >= p.num_blocks || ids[pg] < -1 ||
+                (ids[pg] == -1 && PAGED && j * kPagesPerTile + pg < n_pages)) {
+              raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
+              ids[pg] = -1;
             }
-            ids[pg] = id;
+          }
+          if (j + 1 < it.n_tiles) fetch_ids(j + 1, next_ids);
+          if (v_role) {
+            if (g >= kStages && !mbar_wait(&v_empty[s], ((g / kStages) - 1) & 1, p.err)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&v_full[s], kTile / kParts);
+            const uint32_t vdst = sm + Smem::kV + s * kTile;
+            if constexpr (PAGED) {
+#pragma unroll
+              for (int pg = part * (kPagesPerTile / kParts); pg < (part + 1) * (kPagesPerTile / kParts); ++pg) {
+                tma_load_4d(vdst + pg * kPageBytes, &v_map, 0, hy, hz, ids[pg], smem_u32(&v_full[s]));
+                tma_load_4d(vdst + kHalf + pg * kPageBytes, &v_map, 64, hy, hz, ids[pg], smem_u32(&v_full[s]));
+              }
+            } else {
+              tma_load_3d(vdst + part * kHalf, &v_map, part * 64, it.kvh, it.k_begin + j * kBKV, smem_u32(&v_full[s]));
+            }
+            v_done = g + 1;
+            continue;
           }
           if (g >= kStages && !mbar_wait(&k_empty[s], ((g / kStages) - 1) & 1, p.err)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&k_full[s], kTile);
+          mbar_arrive_expect_tx(&k_full[s], kTile / kParts);
           const uint32_t kdst = sm + Smem::kK + s * kTile;
           if constexpr (PAGED) {
 #pragma unroll
-            for (int pg = 0; pg < kPagesPerTile; ++pg) {
+            for (int pg = part * (kPagesPerTile / kParts); pg < (part + 1) * (kPagesPerTile / kParts); ++pg) {
               tma_load_4d(kdst + pg * kPageBytes, &k_map, 0, hy, hz, ids[pg], smem_u32(&k_full[s]));
               tma_load_4d(kdst + kHalf + pg * kPageBytes, &k_map, 64, hy, hz, ids[pg], smem_u32(&k_full[s]));
             }
           } else {
-            tma_load_3d(kdst, &k_map, 0, it.kvh, it.k_begin + j * kBKV, smem_u32(&k_full[s]));
-            tma_load_3d(kdst + kHalf, &k_map, 64, it.kvh, it.k_begin + j * kBKV, smem_u32(&k_full[s]));
+            tma_load_3d(kdst + part * kHalf, &k_map, part * 64, it.kvh, it.k_begin + j * kBKV, smem_u32(&k_full[s]));
           }
           k_done = g + 1;
-          if (g >= kStages && !mbar_wait(&v_empty[s], ((g / kStages) - 1) & 1, p.err)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&v_full[s], kTile);
-          const uint32_t vdst = sm + Smem::kV + s * kTile;
-          if constexpr (PAGED) {
-#pragma unroll
-            for (int pg = 0; pg < kPagesPerTile; ++pg) {
-              tma_load_4d(vdst + pg * kPageBytes, &v_map, 0, hy, hz, ids[pg], smem_u32(&v_full[s]));
-              tma_load_4d(vdst + kHalf + pg * kPageBytes, &v_map, 64, hy, hz, ids[pg], smem_u32(&v_full[s]));
-            }
-          } else {
-            tma_load_3d(vdst, &v_map, 0, it.kvh, it.k_begin + j * kBKV, smem_u32(&v_full[s]));
-            tma_load_3d(vdst + kHalf, &v_map, 64, it.kvh, it.k_begin + j * kBKV, smem_u32(&v_full[s]));
-          }
-          v_done = g + 1;
         }
       }
       // drain the copies that may still be in flight
