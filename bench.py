@@ -420,6 +420,43 @@ def per_op_table(dev, peaks) -> dict:
            time_graph([lambda i=i: o.reshape_and_cache(k3[i], v3[i], kc3, vc3, sl3) for i in range(2)], 10))
     del kc3, vc3, k3, v3
 
+    # RoPE fused with the KV store (one kernel) beside the two kernels it replaces (ours,
+    # and vLLM's _C pair), for a Llama-3-8B layer: qkv [T, 48*128] bf16, FlashAttention
+    # cache [2, 8192, 16, 8, 128], a decode step (256 tokens) and a prefill chunk (16384).
+    # Bytes: q and k read and written, v read, rotated k and v written to the cache,
+    # cos/sin rows, positions and slots.
+    kv4 = torch.zeros(2, 8192, 16, 8, 128, device=dev, dtype=torch.bfloat16)
+    for T4, iters4 in ((256, 20), (16384, 2)):
+        nb = 2 * T4 * 40 * 128 * 2 + T4 * 8 * 128 * 2 + 2 * T4 * 8 * 128 * 2 + T4 * 128 * 2 + T4 * 16
+        r4 = copies(nb)
+        qkv4 = [torch.randn(T4, 48 * 128, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(r4)]
+        pos4 = [torch.randint(0, 4096, (T4,), device=dev, generator=g) for _ in range(r4)]
+        sl4 = [torch.randperm(8192 * 16, device=dev, generator=g)[:T4] for _ in range(r4)]
+        parts = [(x[:, :4096], x[:, 4096:5120], x[:, 5120:]) for x in qkv4]
+        name = f"rope_and_cache bf16 {T4} tokens of qkv [T,48*128]"
+        report(name, nb, time_graph([lambda i=i: o.rope_and_cache_flash_layout(
+            pos4[i], *parts[i], cache3, kv4, sl4[i], 128, 128, 0) for i in range(r4)], iters4 * r4))
+
+        def unfused(i):
+            q4, k4, v4 = parts[i]
+            o.rotary_embedding_neox(pos4[i], q4, k4, cache3, 128, 128)
+            o.store_flash_layout(k4, v4, kv4, sl4[i], 0)
+
+        us = time_graph([lambda i=i: unfused(i) for i in range(r4)], iters4 * r4) * 1e3
+        res[name]["unfused_us"] = round(us, 2)
+        res[name]["unfused_vs_fused"] = round(us / res[name]["us"], 3)
+
+        def vllm_pair(i):
+            q4, k4, v4 = parts[i]
+            vops.rotary_embedding(pos4[i], q4, k4, 128, cache3, True)
+            vops.reshape_and_cache_flash(k4.view(T4, 8, 128), v4.view(T4, 8, 128), kv4[0], kv4[1], sl4[i], "auto",
+                                         one, one)
+
+        lib(name, "vllm _C rotary_embedding + reshape_and_cache_flash",
+            vops and [lambda i=i: vllm_pair(i) for i in range(r4)], iters4 * r4)
+        del qkv4, parts
+    del kv4
+
     # decode at the vLLM end-to-end shape: 256 sequences, ctx U[512, 640] (prompt 512 + up
     # to 128 generated), 32/8 heads, block 16: contexts that fit one chunk, so the split
     # kernel writes the output itself; the K/V working set (~0.6 GB) exceeds L2

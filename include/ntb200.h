@@ -120,6 +120,37 @@ int ntb200_reshape_and_cache(const void* key, const void* value, void* key_cache
                              int elem_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * NeoX RoPE fused with the paged KV-cache store, one pass over the step's q/k/v rows:
+ *   q, k <- rotated in place exactly as ntb200_rotary_embedding_neox does;
+ *   for t < num_store_tokens with slot = slot_mapping[t] >= 0:
+ *     key_cache  [slot / block_size, slot % block_size, h, :] = rotated key[t, h, :]
+ *     value_cache[slot / block_size, slot % block_size, h, :] = value[t, h, :]
+ * The result is bit-identical to ntb200_rotary_embedding_neox followed by
+ * ntb200_reshape_and_cache.  Negative slots (vLLM padding) only rotate; slots >= num_slots
+ * only rotate and set NTB200_DEVERR_INDEX_RANGE; a position outside [0, num_cache_rows)
+ * leaves the token untouched (no rotation, no store) and sets NTB200_DEVERR_INDEX_RANGE.
+ * key and value rows have num_kv_heads heads of head_size; both caches share the strides
+ * given and have the dtype of query/key/value (F32, BF16 or F16).  positions: I64 or I32,
+ * num_tokens entries; slot_mapping: I64 or I32, num_store_tokens (<= num_tokens) entries;
+ * rows past it (vLLM's padded rows) are rotated only.
+ * Replaces the RoPE hook followed by the KV-store hook of one attention layer:
+ * vllm_nt/_ntops/oot_support.py:134-204 with vllm_nt/_ntops/kernels/rotary_emb.py:6-37,
+ * then vllm_nt/_ntops/torch/kv_cache.py:7-21 with vllm_nt/_ntops/kernels/kv_cache.py:4-45
+ * (reached from vllm_nt/_ntops/patching.py:1323-1354 and 532-562); the reference has no
+ * fused form. */
+int ntb200_rope_and_cache(const void* positions, int positions_dtype, void* query, void* key,
+                          const void* value, const void* cos_sin_cache, void* key_cache,
+                          void* value_cache, const void* slot_mapping, int slot_dtype,
+                          int64_t num_tokens, int64_t num_store_tokens, int64_t num_q_heads,
+                          int64_t num_kv_heads,
+                          int64_t head_size, int64_t rotary_dim, int64_t q_token_stride,
+                          int64_t q_head_stride, int64_t k_token_stride, int64_t k_head_stride,
+                          int64_t v_token_stride, int64_t v_head_stride, int64_t cache_row_stride,
+                          int64_t num_cache_rows, int64_t block_size, int64_t num_slots,
+                          int64_t cache_block_stride, int64_t cache_page_stride,
+                          int64_t cache_head_stride, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Embedding gather (bit-exact copy): out[t, :] = weight[ids[t], :].
  * Ids outside [0, num_embeddings) produce a zero row and set NTB200_DEVERR_INDEX_RANGE.
  * ids_dtype: I64 or I32.  elem_bytes: 1, 2 or 4.

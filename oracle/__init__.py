@@ -12,7 +12,7 @@ the plugin patches; other paths are inside the vllm_nt reference project):
   parity -- with the same fp32 intermediates and the same rounding points to the storage
   dtype;
 * the KV-cache store and the embedding gather are byte copies (numpy on raw 16-bit views),
-  exact;
+  exact; RoPE fused with the KV store is the two restatements composed in vLLM's order;
 * paged decode follows the reference's own test oracle (gather the cached tokens through
   the block table, fp32 softmax attention per sequence, GQA by head grouping);
 * varlen prefill gathers the cached tokens the same way and applies fp32 softmax attention
@@ -36,6 +36,7 @@ from oracle.ops import (  # noqa: F401
     paged_prefill,
     reshape_and_cache,
     rms_norm,
+    rope_and_cache,
     rope_neox,
     silu_and_mul,
     varlen_attention,

@@ -134,6 +134,43 @@ def reshape_and_cache(
 
 
 # --------------------------------------------------------------------------------------
+# RoPE followed by the KV-cache store: the two hooks of one attention layer in vLLM's
+# order (vllm:model_executor/models/llama.py:228-231 rotates q/k, then
+# vllm:model_executor/layers/attention/attention.py:498-518 stores the rotated k and v);
+# vllm_nt reaches them as vllm_nt/_ntops/patching.py:1323-1354 then 532-562.
+# --------------------------------------------------------------------------------------
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    """numpy view of a contiguous CPU tensor's raw bits (shares memory)."""
+    width = {1: torch.int8, 2: torch.int16, 4: torch.int32, 8: torch.int64}[t.element_size()]
+    return t.view(width).numpy()
+
+
+def rope_and_cache(
+    positions: torch.Tensor,
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    cos_sin_cache: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    head_size: int,
+    rotary_dim: int,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Returns rotated copies of query/key (rope_neox) and stores the rotated key and the
+    value into the contiguous CPU caches [blocks, bs, Hkv, D] in place (reshape_and_cache,
+    a bit copy): rows t < slot_mapping.numel() with slot >= 0."""
+    q, k = rope_neox(positions, query, key, cos_sin_cache, head_size, rotary_dim)
+    n = slot_mapping.numel()
+    k3 = k.reshape(k.shape[0], -1, head_size)[:n].contiguous()
+    v3 = value.reshape(value.shape[0], -1, head_size)[:n].contiguous()
+    reshape_and_cache(_bits(k3), _bits(v3), _bits(key_cache), _bits(value_cache), slot_mapping.numpy())
+    return q, k
+
+
+# --------------------------------------------------------------------------------------
 # Embedding  (vllm_nt/_ntops/kernels/wpe.py:11-67, vllm_nt/_ntops/torch/embedding.py:7-30;
 #             vllm:model_executor/layers/vocab_parallel_embedding.py:77-78 = F.embedding)
 # --------------------------------------------------------------------------------------

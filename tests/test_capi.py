@@ -52,6 +52,11 @@ def test_status_strings_and_version():
         ("ntb200_silu_and_mul", (1, 1, 4, 8, 8, 8, 1, None), -1),
         ("ntb200_rotary_embedding_neox", (1, 4, 1, None, 1, 4, 2, 0, 64, 63, 128, 64, 0, 0, 64, 10, 1, None), -1),
         ("ntb200_reshape_and_cache", (1, 1, 1, 1, 1, 4, 4, 2, 128, 16, 64, 256, 128, 256, 128, 4096, 256, 128, 3, None), -2),
+        # rope_and_cache: odd rotary_dim; more store tokens than tokens; null key; fp8 dtype code
+        ("ntb200_rope_and_cache", (1, 4, 1, 1, 1, 1, 1, 1, 1, 4, 4, 4, 2, 1, 128, 127) + (128,) * 6 + (128, 64, 16, 64, 2048, 128, 128, 1, None), -1),
+        ("ntb200_rope_and_cache", (1, 4, 1, 1, 1, 1, 1, 1, 1, 4, 4, 5, 2, 1, 128, 128) + (128,) * 6 + (128, 64, 16, 64, 2048, 128, 128, 1, None), -1),
+        ("ntb200_rope_and_cache", (1, 4, 1, None, 1, 1, 1, 1, 1, 4, 4, 4, 2, 1, 128, 128) + (128,) * 6 + (128, 64, 16, 64, 2048, 128, 128, 1, None), -1),
+        ("ntb200_rope_and_cache", (1, 4, 1, 1, 1, 1, 1, 1, 1, 4, 4, 4, 2, 1, 128, 128) + (128,) * 6 + (128, 64, 16, 64, 2048, 128, 128, 7, None), -2),
         ("ntb200_embedding", (1, 1, 4, 1, 4, 10, 16, 8, 16, 2, None), -1),
         ("ntb200_linear", (1, 1, 1, None, 4, 8, 16, 16, 16, 8, None, 0, 0, None), -2),
         ("ntb200_paged_attention_decode",
@@ -71,6 +76,8 @@ def test_zero_sized_calls_are_no_ops():
     assert capi.call("ntb200_rms_norm", 1, 1, None, 0, 8, 8, 8, 1e-6, 0, None) == 0
     assert capi.call("ntb200_silu_and_mul", 1, 1, 0, 8, 16, 8, 1, None) == 0
     assert capi.call("ntb200_linear", 1, 1, 1, None, 0, 8, 16, 16, 16, 8, None, 0, 1, None) == 0
+    assert capi.call("ntb200_rope_and_cache", 1, 4, 1, 1, 1, 1, 1, 1, 1, 4, 0, 0, 2, 1, 128, 128, *(128,) * 6,
+                     128, 64, 16, 64, 2048, 128, 128, 1, None) == 0
 
 
 def test_workspace_queries():

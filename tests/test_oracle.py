@@ -41,6 +41,30 @@ def test_rope_matches_vllm_forward_static(tag):
     assert bits_equal(qp, g["query_out_rot32"]) and bits_equal(kp, g["key_out_rot32"])
 
 
+
+@pytest.mark.parametrize("tag", ["f32", "bf16"])
+@pytest.mark.parametrize("rot", [64, 32])
+def test_rope_and_cache_is_rope_then_store(tag, rot):
+    """The fused restatement against the RoPE golden outputs (vLLM forward_static): q/k
+    rotated as the fixture says, the rotated key rows and the value rows at their slots,
+    padding slots and rows past the slot mapping not stored."""
+    g = golden(f"rope_{tag}")
+    suffix = "" if rot == 64 else "_rot32"
+    value = g["key"].flip(0).contiguous()
+    slots = torch.tensor([5, -1, 0, 13, 7])  # 5 of 6 rows: the last is a padded row
+    kc = torch.zeros(4, 4, 2, 64, dtype=value.dtype)
+    vc = torch.zeros_like(kc)
+    qo, ko = oracle.rope_and_cache(g["positions"], g["query"], g["key"], value, g["cos_sin_cache" + suffix], kc, vc,
+                                   slots, 64, rot)
+    assert bits_equal(qo, g["query_out" + suffix]) and bits_equal(ko, g["key_out" + suffix])
+    kflat, vflat = kc.reshape(16, 2, 64), vc.reshape(16, 2, 64)
+    stored = [(t, int(sl)) for t, sl in enumerate(slots) if sl >= 0]
+    for t, sl in stored:
+        assert bits_equal(kflat[sl], g["key_out" + suffix][t].reshape(2, 64))
+        assert bits_equal(vflat[sl], value[t].reshape(2, 64))
+    untouched = sorted(set(range(16)) - {sl for _, sl in stored})
+    assert not kflat[untouched].any() and not vflat[untouched].any()
+
 def test_kv_store_matches_reference_torch_store():
     g = golden("kv_store_bf16")
     kc = np.zeros((8, 4, 2, 16), dtype=np.uint16)

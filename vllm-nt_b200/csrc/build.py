@@ -34,6 +34,7 @@ KERNEL_SOURCES = (
     "rms_norm.cu",
     "silu_and_mul.cu",
     "rope.cu",
+    "rope_cache.cu",
     "kv_cache.cu",
     "embedding.cu",
     "paged_decode.cu",

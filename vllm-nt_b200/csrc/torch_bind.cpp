@@ -202,6 +202,61 @@ void reshape_and_cache(const at::Tensor& key, const at::Tensor& value, at::Tenso
         "reshape_and_cache");
 }
 
+// RoPE of query/key fused with the store of the rotated key and the value into the paged
+// caches.  query/key/value as the rotary op takes them ([tokens, heads * head_size] rows or
+// [tokens, heads, head_size]); caches [blocks, block_size, kv_heads, head_size] with equal
+// strides.
+void rope_and_cache(const at::Tensor& positions, at::Tensor query, at::Tensor key, const at::Tensor& value,
+                    const at::Tensor& cos_sin_cache, at::Tensor key_cache, at::Tensor value_cache,
+                    const at::Tensor& slot_mapping, int64_t head_size, int64_t rotary_dim) {
+  require_cuda(positions, "positions");
+  require_cuda(slot_mapping, "slot_mapping");
+  require_cuda(key_cache, "key_cache");
+  require_cuda(value_cache, "value_cache");
+  require_rows(cos_sin_cache, "cos_sin_cache");
+  TORCH_CHECK(positions.is_contiguous(), "ntb200.rope_and_cache: positions must be contiguous");
+  const int64_t tokens = positions.numel();
+  TORCH_CHECK(slot_mapping.dim() == 1 && slot_mapping.is_contiguous() && slot_mapping.size(0) <= tokens,
+              "ntb200.rope_and_cache: slot_mapping must be 1-D contiguous, <= tokens");
+  const auto dt = query.scalar_type();
+  TORCH_CHECK(key.scalar_type() == dt && value.scalar_type() == dt && cos_sin_cache.scalar_type() == dt &&
+                  key_cache.scalar_type() == dt && value_cache.scalar_type() == dt,
+              "ntb200.rope_and_cache: query, key, value, cos_sin_cache and the caches must share a dtype");
+  int64_t hq = 0, qts = 0, qhs = 0, hk = 0, kts = 0, khs = 0, hv = 0, vts = 0, vhs = 0;
+  head_geometry(query, tokens, head_size, "query", hq, qts, qhs);
+  head_geometry(key, tokens, head_size, "key", hk, kts, khs);
+  head_geometry(value, tokens, head_size, "value", hv, vts, vhs);
+  TORCH_CHECK(key_cache.dim() == 4 && value_cache.sizes() == key_cache.sizes() &&
+                  key_cache.strides() == value_cache.strides() && key_cache.stride(3) == 1,
+              "ntb200.rope_and_cache: caches must be [blocks, block_size, heads, head_size] with equal strides");
+  TORCH_CHECK(hv == hk && key_cache.size(2) == hk && key_cache.size(3) == head_size,
+              "ntb200.rope_and_cache: kv head geometry mismatch");
+  c10::cuda::CUDAGuard guard(query.device());
+  check(ntb200_rope_and_cache(positions.data_ptr(), dtype_code(positions), query.data_ptr(), key.data_ptr(),
+                              value.data_ptr(), cos_sin_cache.data_ptr(), key_cache.data_ptr(),
+                              value_cache.data_ptr(), slot_mapping.data_ptr(), dtype_code(slot_mapping), tokens,
+                              slot_mapping.size(0), hq, hk, head_size, rotary_dim, qts, qhs, kts, khs, vts, vhs,
+                              cos_sin_cache.stride(0), cos_sin_cache.size(0), key_cache.size(1),
+                              key_cache.size(0) * key_cache.size(1), key_cache.stride(0), key_cache.stride(1),
+                              key_cache.stride(2), dtype_code(query), stream_of(query)),
+        "rope_and_cache");
+}
+
+// rope_and_cache on vLLM's combined cache: [2, blocks, block_size, kv_heads, head_size]
+// (kv_dim 0, FlashAttention) or [blocks, 2, block_size, kv_heads, head_size] (kv_dim 1,
+// FlashInfer).
+void rope_and_cache_flash_layout(const at::Tensor& positions, at::Tensor query, at::Tensor key,
+                                 const at::Tensor& value, const at::Tensor& cos_sin_cache, at::Tensor kv_cache,
+                                 const at::Tensor& slot_mapping, int64_t head_size, int64_t rotary_dim,
+                                 int64_t kv_dim) {
+  require_cuda(kv_cache, "kv_cache");
+  TORCH_CHECK((kv_dim == 0 || kv_dim == 1) && kv_cache.dim() == 5 && kv_cache.size(kv_dim) == 2,
+              "ntb200.rope_and_cache_flash_layout: kv_cache must be [2, blocks, block_size, kv_heads, head_size] "
+              "(kv_dim 0) or [blocks, 2, block_size, kv_heads, head_size] (kv_dim 1)");
+  rope_and_cache(positions, query, key, value, cos_sin_cache, kv_cache.select(kv_dim, 0), kv_cache.select(kv_dim, 1),
+                 slot_mapping.dim() == 1 ? slot_mapping : slot_mapping.reshape({-1}), head_size, rotary_dim);
+}
+
 void embedding(at::Tensor out, const at::Tensor& ids, const at::Tensor& weight) {
   require_rows(weight, "weight");
   require_rows(out, "out");
@@ -564,6 +619,14 @@ TORCH_LIBRARY(ntb200, m) {
   m.def(
       "reshape_and_cache(Tensor key, Tensor value, Tensor(a!) key_cache, "
       "Tensor(b!) value_cache, Tensor slot_mapping) -> ()");
+  m.def(
+      "rope_and_cache(Tensor positions, Tensor(a!) query, Tensor(b!) key, Tensor value, "
+      "Tensor cos_sin_cache, Tensor(c!) key_cache, Tensor(d!) value_cache, Tensor slot_mapping, "
+      "int head_size, int rotary_dim) -> ()");
+  m.def(
+      "rope_and_cache_flash_layout(Tensor positions, Tensor(a!) query, Tensor(b!) key, Tensor value, "
+      "Tensor cos_sin_cache, Tensor(c!) kv_cache, Tensor slot_mapping, int head_size, int rotary_dim, "
+      "int kv_dim=0) -> ()");
   m.def("embedding(Tensor(a!) out, Tensor ids, Tensor weight) -> ()");
   m.def(
       "paged_attention_decode(Tensor(a!) out, Tensor query, Tensor key_cache, "
@@ -610,6 +673,8 @@ TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("silu_and_mul", &silu_and_mul);
   m.impl("rotary_embedding_neox", &rotary_embedding_neox);
   m.impl("reshape_and_cache", &reshape_and_cache);
+  m.impl("rope_and_cache", &rope_and_cache);
+  m.impl("rope_and_cache_flash_layout", &rope_and_cache_flash_layout);
   m.impl("embedding", &embedding);
   m.impl("paged_attention_decode", &paged_attention_decode);
   m.impl("decode_flash_layout", &decode_flash_layout);

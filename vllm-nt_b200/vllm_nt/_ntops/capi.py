@@ -45,6 +45,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int,
          c_void_p],
     ),
+    "ntb200_rope_and_cache": (
+        c_int,
+        [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int]
+        + [c_int64] * 19 + [c_int, c_void_p],
+    ),
     "ntb200_embedding": (
         c_int,
         [c_void_p, c_void_p, c_int, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int,

@@ -9,7 +9,7 @@ from vllm_nt._ntops.torch.embedding import embedding
 from vllm_nt._ntops.torch.kv_cache import get_kv_from_cache, store_kvcache
 from vllm_nt._ntops.torch.linear import linear, matmul
 from vllm_nt._ntops.torch.rms_norm import fused_add_rms_norm, rms_norm
-from vllm_nt._ntops.torch.rotary_emb import apply_rotary_emb, rotary_embedding
+from vllm_nt._ntops.torch.rotary_emb import apply_rotary_emb, rotary_embedding, rotary_embedding_and_cache
 from vllm_nt._ntops.torch.silu import silu_and_mul
 
 __all__ = [
@@ -24,6 +24,7 @@ __all__ = [
     "paged_decode",
     "rms_norm",
     "rotary_embedding",
+    "rotary_embedding_and_cache",
     "silu_and_mul",
     "store_kvcache",
 ]

@@ -33,6 +33,8 @@ def _register_fakes() -> None:
         "silu_and_mul",
         "rotary_embedding_neox",
         "reshape_and_cache",
+        "rope_and_cache",
+        "rope_and_cache_flash_layout",
         "embedding",
         "paged_attention_decode",
         "decode_flash_layout",

@@ -44,6 +44,39 @@ def rotary_embedding(
     return query, key
 
 
+def rotary_embedding_and_cache(
+    positions: torch.Tensor,
+    query: torch.Tensor,
+    key: torch.Tensor,
+    value: torch.Tensor,
+    head_size: int,
+    cos_sin_cache: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    rotary_dim: int | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """rotary_embedding(positions, query, key, ...) followed by
+    store_kvcache(key, value, key_cache, value_cache, slot_mapping) in one kernel: q/k are
+    rotated in place and the rotated key rows and the value rows land in the paged caches
+    [blocks, block_size, kv_heads, head_size].  Bit-identical to the two calls in sequence.
+    Tokens past ``slot_mapping.numel()`` (vLLM's padded rows) are rotated only."""
+    rot = cos_sin_cache.shape[-1] if rotary_dim is None else rotary_dim
+    positions = positions.reshape(-1)
+    if not positions.is_contiguous():
+        positions = positions.contiguous()
+    slots = slot_mapping.reshape(-1)
+    if not slots.is_contiguous():
+        slots = slots.contiguous()
+    cache = cos_sin_cache if cos_sin_cache.stride(-1) == 1 else cos_sin_cache.contiguous()
+    n = positions.shape[0]
+    q = query if query.dim() == 2 and query.stride(-1) == 1 else _heads(query, n, head_size)
+    k = key if key.dim() == 2 and key.stride(-1) == 1 else _heads(key, n, head_size)
+    v = value if value.dim() == 2 and value.stride(-1) == 1 else _heads(value, n, head_size)
+    ops().rope_and_cache(positions, q, k, v, cache, key_cache, value_cache, slots, int(head_size), int(rot))
+    return query, key
+
+
 def apply_rotary_emb(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     """Reference signature (vllm_nt/_ntops/torch/rotary_emb.py:7-9): x [T, H, R] rotated in
     place with per-token cos/sin [T, 1, R/2] (or [T, R/2]).  Implemented by handing the
