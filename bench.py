@@ -457,6 +457,42 @@ def per_op_table(dev, peaks) -> dict:
         del qkv4, parts
     del kv4
 
+    # sampler at a decode batch of 256 over the Llama-3 vocabulary (fp32 logits, as vLLM's
+    # sampler holds them): the top-k/top-p mask (k = 50, p = 0.9 on every row) and the
+    # exponential-race sample.  The mask works in place, so each call first restores its
+    # logits from a pristine copy; the copy is timed alone and subtracted.  Algorithmic
+    # bytes: the logits read once and written once (mask); probs and q read once (sample).
+    B5, V5 = 256, 128256
+    src5 = torch.randn(B5, V5, device=dev, generator=g) * 2
+    lg5 = torch.empty_like(src5)
+    k5 = torch.full((B5,), 50, device=dev, dtype=torch.int32)
+    p5 = torch.full((B5,), 0.9, device=dev)
+    copy_us = time_graph([lambda: lg5.copy_(src5)], 10) * 1e3
+    name = "top_k_top_p f32 [256,128256] k=50 p=0.9"
+    us = time_graph([lambda: (lg5.copy_(src5), o.top_k_top_p(lg5, k5, p5))], 10) * 1e3 - copy_us
+    report(name, 2 * B5 * V5 * 4, us * 1e-3, {"note": "radix select, ~8 passes over each row (L2/HBM)"})
+    try:
+        from vllm.v1.sample.ops.topk_topp_sampler import apply_top_k_top_p_pytorch
+        from vllm.v1.sample.ops.topk_topp_triton import apply_top_k_top_p_triton
+
+        t_us = time_graph([lambda: (lg5.copy_(src5), apply_top_k_top_p_triton(lg5, k5, p5))], 10) * 1e3 - copy_us
+        res[name].update(lib="vllm apply_top_k_top_p_triton (vLLM's choice for batch >= 8)", lib_us=round(t_us, 2),
+                         ours_vs_lib=round(t_us / res[name]["us"], 3))
+        s_us = time_graph([lambda: (lg5.copy_(src5), apply_top_k_top_p_pytorch(lg5, k5, p5))], 3) * 1e3 - copy_us
+        res[name].update(sort_us=round(s_us, 2), ours_vs_sort=round(s_us / res[name]["us"], 3),
+                         sort="torch sort + cumsum + scatter (the reference's algorithm, on the GPU)")
+    except Exception as exc:  # noqa: BLE001 - the comparison columns are optional
+        res[name]["lib"] = f"unavailable ({type(exc).__name__}: {exc})"[:200]
+    del lg5
+    probs5 = src5.softmax(dim=-1)
+    q5 = torch.empty_like(probs5).exponential_(generator=g)
+    ids5 = torch.empty(B5, dtype=torch.int64, device=dev)
+    name = "random_sample f32 [256,128256]"
+    report(name, 2 * B5 * V5 * 4 + B5 * 8, time_graph([lambda: o.random_sample(ids5, probs5, q5)], 20))
+    lib(name, "torch div + argmax (the reference's random_sample after its draws)",
+        [lambda: probs5.div(q5).argmax(dim=-1)], 20)
+    del src5, probs5, q5
+
     # decode at the vLLM end-to-end shape: 256 sequences, ctx U[512, 640] (prompt 512 + up
     # to 128 generated), 32/8 heads, block 16: contexts that fit one chunk, so the split
     # kernel writes the output itself; the K/V working set (~0.6 GB) exceeds L2

@@ -319,6 +319,35 @@ int ntb200_linear_argmax(int64_t* out_index, const void* x, const void* weight, 
                          size_t workspace_bytes, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Top-k / top-p mask of fp32 logits [num_rows, vocab] (row stride row_stride), in place:
+ * for each row b, with k = clamp(top_k[b], 1, vocab) and p = top_p[b],
+ *   top-k: logits below the k-th largest logit of the row become -inf (ties with it kept);
+ *   top-p: over the logits top-k kept, with probabilities exp(x - max) / Z, logits whose
+ *          cumulative probability counted from the smallest upwards (themselves included)
+ *          is <= 1 - p become -inf; the largest logit is always kept.
+ * top_k (I32 or I64 per row, top_k_dtype) or top_p (fp32 per row) may be NULL to skip that
+ * filter; both NULL is a no-op.  No sort: per row, radix selection of the two cut values
+ * over order-preserving 32-bit keys, one CTA per row.  Equal to the reference's sort-based
+ * mask except where a run of equal logits straddles the top-p cut (kept whole here; the
+ * reference keeps the part its unstable sort happens to put last) or where the cumulative
+ * probability at a logit is within fp32 summation error of 1 - p.
+ * Replaces vllm_nt/_ntops/torch/sampler.py:4-31 (apply_top_k_top_p), reached from
+ * vllm_nt/_ntops/patching.py:1446-1463 (the TopKTopP patch of vLLM's
+ * topk_topp_sampler.apply_top_k_top_p). */
+int ntb200_top_k_top_p(float* logits, int64_t num_rows, int64_t vocab, int64_t row_stride,
+                       const void* top_k, int top_k_dtype, const float* top_p, void* stream);
+
+/* Exponential-race sampling from fp32 probabilities: out[b] = argmax_i probs[b, i] / q[b, i]
+ * (int64), q being the caller's Exp(1) draws, with the quotient rounded as IEEE division,
+ * NaN ranked above every number and the first index winning ties (torch.argmax).  One pass
+ * over probs and q; the [num_rows, vocab] quotient is never written.
+ * Replaces vllm_nt/_ntops/torch/sampler.py:34-42 (random_sample: torch.div then argmax),
+ * reached from vllm_nt/_ntops/patching.py:1466-1479 (the RandomSample patch). */
+int ntb200_random_sample(int64_t* out, const float* probs, const float* q, int64_t num_rows,
+                         int64_t vocab, int64_t probs_row_stride, int64_t q_row_stride,
+                         void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * One-shot all-reduce over peer memory for the row-parallel projections of tensor
  * parallelism (o_proj and down under TP): replaces the NCCL all-reduce that vLLM's
  * RowParallelLinear issues after the GEMM (vllm:model_executor/layers/linear.py

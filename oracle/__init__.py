@@ -15,6 +15,8 @@ the plugin patches; other paths are inside the vllm_nt reference project):
   exact; RoPE fused with the KV store is the two restatements composed in vLLM's order;
 * paged decode follows the reference's own test oracle (gather the cached tokens through
   the block table, fp32 softmax attention per sequence, GQA by head grouping);
+* top-k / top-p masking and the exponential-race sample restate the reference's torch
+  sampler (sort, mask in sorted order, scatter back; argmax of probs / q);
 * varlen prefill gathers the cached tokens the same way and applies fp32 softmax attention
   with the causal mask aligned to the end of each context (vLLM's rule; the reference's
   start-aligned mask is the same when a sequence has as many keys as queries).
@@ -27,6 +29,7 @@ tests/test_rope.py:26-46, tests/test_attention.py:57-104, tests/test_oot.py:33-1
 """
 
 from oracle.ops import (  # noqa: F401
+    apply_top_k_top_p,
     build_cos_sin_cache,
     embedding,
     fused_add_rms_norm,
@@ -34,10 +37,12 @@ from oracle.ops import (  # noqa: F401
     linear,
     paged_decode,
     paged_prefill,
+    random_sample_from_draws,
     reshape_and_cache,
     rms_norm,
     rope_and_cache,
     rope_neox,
     silu_and_mul,
+    top_p_cumulative,
     varlen_attention,
 )

@@ -313,3 +313,49 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     if bias is not None:
         y = y + bias.to(torch.float32)
     return y
+
+
+# --------------------------------------------------------------------------------------
+# Sampler  (vllm_nt/_ntops/torch/sampler.py:4-42; vllm:v1/sample/ops/topk_topp_sampler.py
+#           apply_top_k_top_p_pytorch and random_sample)
+# --------------------------------------------------------------------------------------
+
+
+def apply_top_k_top_p(logits: torch.Tensor, k: torch.Tensor | None, p: torch.Tensor | None) -> torch.Tensor:
+    """Masked copy of fp32 logits [B, V] by the reference's sort-based rule: sort each row
+    ascending; top-k sets every value below the (V - k)-th sorted value to -inf (k clamped
+    to [1, V]); top-p takes the softmax of the sorted (top-k masked) row, its running sum
+    from the smallest value up, and sets to -inf every position whose running sum is
+    <= 1 - p, except the last (largest) one; the row is scattered back."""
+    out = logits.clone()
+    if k is None and p is None:
+        return out
+    vocab = out.shape[-1]
+    ordered, order = out.sort(dim=-1)
+    if k is not None:
+        kk = k.to(torch.long).clamp(1, vocab)
+        kth = ordered.gather(1, (vocab - kk).unsqueeze(1))
+        ordered = ordered.masked_fill(ordered < kth, float("-inf"))
+    if p is not None:
+        running = ordered.softmax(dim=-1, dtype=torch.float32).cumsum(dim=-1)
+        drop = running <= 1 - p.to(torch.float32).unsqueeze(1)
+        drop[:, -1] = False
+        ordered = ordered.masked_fill(drop, float("-inf"))
+    return out.scatter(-1, order, ordered)
+
+
+def random_sample_from_draws(probs: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
+    """argmax_i probs[b, i] / q[b, i] per row (int64 [B]): the reference's random_sample
+    once its exponential draws q are fixed (torch.argmax: first index on ties)."""
+    return torch.div(probs, q).argmax(dim=-1).view(-1)
+
+
+def top_p_cumulative(logits: torch.Tensor, k: torch.Tensor | None) -> torch.Tensor:
+    """fp64 running probability, per logit, of the rows after the top-k mask, summed from the
+    smallest logit up to and including each one (the quantity the top-p rule compares with
+    1 - p), returned in the logits' own positions: the yardstick for logits whose fate
+    depends on fp32 summation order."""
+    masked = apply_top_k_top_p(logits, k, None) if k is not None else logits
+    ordered, order = masked.double().sort(dim=-1)
+    running = ordered.softmax(dim=-1).cumsum(dim=-1)
+    return torch.empty_like(running).scatter(-1, order, running)

@@ -14,7 +14,11 @@ Sources of truth per op:
   paged decode                   gather + torch scaled_dot_product_attention per sequence
                                  (the reference's oracle, vllm_nt/tests/test_attention.py:41-102)
   linear                         torch.nn.functional.linear in fp32
+  sampler (top-k / top-p, random the reference's own torch sampler, vllm_nt/_ntops/torch/sampler.py,
+  sample)                        loaded by file path from the read-only reference checkout (it
+                                 imports only torch), and vLLM's apply_top_k_top_p_pytorch
 bf16 tensors are stored as their uint16 bit patterns (key suffix ``__bf16``).
+``--only sampler`` regenerates just the sampler fixture.
 """
 
 from __future__ import annotations
@@ -155,5 +159,50 @@ def main() -> None:
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 
+REFERENCE_SAMPLER = Path("/root/reference/vllm_nt/_ntops/torch/sampler.py")
+
+
+def sampler_fixture() -> None:
+    """Six rows over a 1000-token vocabulary: logits of spread 1, 2, 5 and 0.5, one row with
+    a run of -inf entries (logits processors mask tokens that way), one with ties at the
+    top-k cut; per-row k (1 .. V) and p (0.1 .. 1.0).  Outputs of the reference's
+    apply_top_k_top_p for k alone, p alone and both, vLLM's own native function for both,
+    and the reference's random_sample with a seeded generator for every row (so the
+    exponential draws q are fixed and stored)."""
+    import importlib.util
+
+    from vllm.v1.sample.ops.topk_topp_sampler import apply_top_k_top_p_pytorch
+
+    spec = importlib.util.spec_from_file_location("reference_sampler", REFERENCE_SAMPLER)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+
+    g = torch.Generator().manual_seed(20261202)
+    rows, vocab = 6, 1000
+    scale = torch.tensor([1.0, 2.0, 5.0, 0.5, 2.0, 3.0]).unsqueeze(1)
+    logits = torch.randn(rows, vocab, generator=g) * scale
+    logits[4, torch.randperm(vocab, generator=g)[:300]] = float("-inf")
+    logits[5, :7] = logits[5].sort(descending=True).values[9]  # 7 copies of the 10th-largest value
+    k = torch.tensor([1, 5, 50, vocab, 200, 10], dtype=torch.int64)
+    p = torch.tensor([0.9, 0.5, 0.95, 0.8, 1.0, 0.1], dtype=torch.float32)
+    topk = ref.apply_top_k_top_p(logits.clone(), k, None)
+    topp = ref.apply_top_k_top_p(logits.clone(), None, p)
+    both = ref.apply_top_k_top_p(logits.clone(), k, p)
+    both_vllm = apply_top_k_top_p_pytorch(logits.clone(), k, p)
+    probs = both.softmax(dim=-1, dtype=torch.float32)
+    gens = {i: torch.Generator().manual_seed(900 + i) for i in range(rows)}
+    sample = ref.random_sample(probs.clone(), gens)
+    q = torch.stack([torch.empty(vocab).exponential_(generator=torch.Generator().manual_seed(900 + i))
+                     for i in range(rows)])
+    save("sampler_f32", logits=logits, k=k, p=p, top_k_out=topk, top_p_out=topp, top_k_top_p_out=both,
+         top_k_top_p_out_vllm=both_vllm, probs=probs, q=q, sample=sample)
+
+
 if __name__ == "__main__":
-    main()
+    import sys
+
+    if sys.argv[1:] == ["--only", "sampler"]:
+        sampler_fixture()
+    else:
+        main()
+        sampler_fixture()

@@ -229,3 +229,36 @@ def test_paged_prefill_equals_varlen_over_gathered_tokens():
     assert torch.equal(k[5:9], kc[8].reshape(4, 2, 16)) and torch.equal(k[13], kc[5, 0])
     torch.testing.assert_close(oracle.paged_prefill(q, kc, vc, cu_q, seq, table),
                                oracle.varlen_attention(q, k, v, cu_q, cu_k))
+
+
+def test_sampler_matches_the_reference_torch_sampler():
+    """tests/golden/sampler_f32.npz holds the reference's own apply_top_k_top_p and
+    random_sample outputs (and vLLM's native top-k/top-p, identical on it): the oracle
+    reproduces them bit for bit, ties at a top-k cut and -inf entries included."""
+    g = golden("sampler_f32")
+    logits, k, p = g["logits"], g["k"], g["p"]
+    assert bits_equal(oracle.apply_top_k_top_p(logits, k, None), g["top_k_out"])
+    assert bits_equal(oracle.apply_top_k_top_p(logits, None, p), g["top_p_out"])
+    assert bits_equal(oracle.apply_top_k_top_p(logits, k, p), g["top_k_top_p_out"])
+    assert bits_equal(g["top_k_top_p_out_vllm"], g["top_k_top_p_out"])
+    assert bits_equal(oracle.apply_top_k_top_p(logits, None, None), logits)
+    assert torch.equal(oracle.random_sample_from_draws(g["probs"], g["q"]), g["sample"])
+    # ties at the top-k cut of row 5 are all kept: more than k survive
+    assert int((g["top_k_out"][5] != float("-inf")).sum()) > int(k[5])
+
+
+def test_top_p_cumulative_is_the_quantity_top_p_compares():
+    """Every logit the reference drops for top-p has a running probability <= 1 - p (up to
+    fp32 summation error) and every survivor but the row maximum one above it."""
+    g = golden("sampler_f32")
+    run = oracle.top_p_cumulative(g["logits"], g["k"])
+    both = g["top_k_top_p_out"]
+    topk = g["top_k_out"]
+    for b in range(both.shape[0]):
+        limit = 1 - float(g["p"][b])
+        dropped = (both[b] == float("-inf")) & (topk[b] != float("-inf"))
+        kept = both[b] != float("-inf")
+        assert (run[b][dropped] <= limit + 1e-6).all()
+        top = int(topk[b].argmax())
+        kept[top] = False
+        assert (run[b][kept] > limit - 1e-6).all()

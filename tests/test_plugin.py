@@ -340,3 +340,48 @@ def test_flashinfer_hooks_decode_only_and_kv_store(monkeypatch):
     assert fwd(impl, None, q, q, q, kv, planned, out) == "flashinfer"
     upd(impl, None, torch.zeros(5, 2, 128), torch.zeros(5, 2, 128), kv, torch.tensor([1, 2, 3]))
     assert calls["store"] == ((6, 2, 16, 2, 128), 1)
+
+
+def test_sampler_hooks_patch_vllm_and_route(monkeypatch):
+    """TopKTopP / RandomSample replace vLLM's topk_topp_sampler functions (the reference's
+    patch targets); CPU or non-fp32 tensors go to vLLM's code uncounted, eligible calls to
+    the kernels and are counted; RejectionSample only counts and runs vLLM's code."""
+    from vllm.v1.sample.ops import topk_topp_sampler as tks
+
+    vllm_nt.register()
+    assert patching._is_function_patch(tks.apply_top_k_top_p, "TopKTopP")
+    assert patching._is_function_patch(tks.random_sample, "RandomSample")
+
+    calls = []
+    monkeypatch.setattr(patching, "nt_apply_top_k_top_p", lambda lg, k, p: calls.append("mask") or lg)
+    monkeypatch.setattr(patching, "nt_random_sample", lambda pr, gens: calls.append("sample") or "kernel")
+    mask = patching._build_apply_top_k_top_p_patch(lambda lg, k, p: "vllm")
+    sample = patching._build_random_sample_patch(lambda pr, gens: "vllm")
+    logits = torch.randn(2, 8)
+    k = torch.tensor([2, 3])
+    assert mask(logits, k, None) == "vllm" and sample(logits, {}) == "vllm"  # CPU: vLLM's code
+    monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
+    assert mask(logits, None, None) == "vllm"  # nothing to mask
+    assert mask(logits.half(), k, None) == "vllm"  # not fp32
+    assert mask(logits, k, None) is logits and sample(logits, {}) == "kernel"
+    assert calls == ["mask", "sample"]
+    ops = patching.get_usage_summary()["operators"]
+    assert ops["TopKTopP"]["hits"] == 1 and ops["RandomSample"]["hits"] == 1
+
+    reject = patching._build_rejection_sample_patch(lambda *a, **kw: "vllm")
+    assert reject(None, [1], 1, None, None, torch.zeros(1, 8), None, None) == "vllm"
+    assert reject(target_logits=torch.zeros(1, 8)) == "vllm"
+    assert patching.get_usage_summary()["operators"]["RejectionSample"]["hits"] == 2
+
+
+def test_sampler_patches_follow_the_config(monkeypatch):
+    """The reference's default map sends TopKTopP / RandomSample to its kernel backend, so
+    the patches apply; original-only.yaml keeps vLLM's sampler functions."""
+    def enabled():
+        config.reset_backend_config_cache()
+        return {s.patch_id for s in patching._FUNCTION_PATCH_SPECS if patching._function_patch_enabled(s)}
+
+    monkeypatch.delenv("VLLM_NT_BACKEND_CONFIG")
+    assert {"TopKTopP", "RandomSample", "RejectionSample"} <= enabled()
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/original-only.yaml"))
+    assert not {"TopKTopP", "RandomSample"} & enabled()

@@ -42,6 +42,7 @@ KERNEL_SOURCES = (
     "gemm.cu",
     "paged_prefill.cu",
     "allreduce.cu",
+    "sampler.cu",
 )
 SHARED_HEADERS = (CSRC / "common.cuh", CSRC / "tcgen05.cuh", INCLUDE / "ntb200.h", Path(__file__).resolve())
 

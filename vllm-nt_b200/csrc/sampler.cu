@@ -1,0 +1,408 @@
+// Sampler kernels: the top-k / top-p logits mask and the exponential-race random sample.
+//
+// Top-k / top-p (the reference's apply_top_k_top_p, vllm_nt/_ntops/torch/sampler.py:4-31,
+// which sorts every row of the [B, V] logits, masks in sorted order and scatters back).
+// Here nothing is sorted.  One CTA owns one row and finds the two cut values by radix
+// select over the row's fp32 logits, mapped to order-preserving 32-bit keys, one 11-, 11-
+// and 10-bit digit per pass, with the digit histogram in shared memory:
+//
+//   top-k:  t_k = the k-th largest logit (counts from the top; every logit >= t_k kept,
+//           ties included, as the reference's `logits_sort < threshold` mask does);
+//   top-p:  over the logits kept by top-k, with probabilities pi = exp(x - max) / Z,
+//           the cut c = the smallest logit whose inclusive cumulative probability from the
+//           bottom exceeds 1 - p (the reference's `cumsum <= 1 - p` mask); logits >= c are
+//           kept, the largest logit always.
+//
+// Passes over the row (each from L2 or HBM): max + first top-k digit, two more top-k
+// digits, the softmax normaliser Z, three weighted top-p digits (probability sums per bin
+// in shared memory, the bin search in fp64), then the masking write.  A row with neither
+// filter is left untouched.
+//
+// Random sample (the reference's random_sample, sampler.py:34-42): out[b] =
+// argmax_i probs[b, i] / q[b, i] for the caller's exponential draws q, in one pass over
+// probs and q: the quotient is IEEE-rounded as torch's division, NaN ranks above every
+// number, and the first index wins ties, as torch.argmax does.  The [B, V] quotient the
+// reference materialises is never written.
+#include "common.cuh"
+
+namespace ntb200 {
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int kBins = 2048;  // 11-bit digits
+constexpr int kWarps = kThreads / 32;
+
+__device__ __forceinline__ uint32_t ordered_key(float x) {
+  const uint32_t b = __float_as_uint(x);
+  return b ^ ((b & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u ^ 0x80000000u) : ~u);
+}
+
+// digit d of a key: bits [shift, shift + width) with shifts 21, 10, 0 and widths 11, 11, 10
+__device__ __forceinline__ int digit_shift(int d) { return d == 0 ? 21 : (d == 1 ? 10 : 0); }
+__device__ __forceinline__ uint32_t digit_mask(int d) { return d == 2 ? 0x3FFu : 0x7FFu; }
+// the key bits fixed before digit d
+__device__ __forceinline__ uint32_t prefix_mask(int d) {
+  return d == 0 ? 0u : (d == 1 ? 0xFFE00000u : 0xFFFFFC00u);
+}
+
+struct SamplerSmem {
+  uint32_t count[kBins];
+  float weight[kBins];
+  double warp_d[kWarps];
+  uint32_t warp_u[kWarps];
+  float warp_f[kWarps];
+  uint32_t chosen;     // bin picked by the last selection (or kBins if none)
+  uint32_t fallback;   // largest non-empty bin of the last weighted pass
+};
+
+// Block-wide inclusive prefix sum of one value per thread, in thread order.  `total`
+// receives the block sum.  Every thread of the block must call it.
+template <typename T>
+__device__ __forceinline__ T block_inclusive_scan(T v, T* warp_tot, T& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T n = __shfl_up_sync(0xFFFFFFFFu, v, o);
+    if (lane >= o) v += n;
+  }
+  if (lane == 31) warp_tot[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    T w = lane < kWarps ? warp_tot[lane] : T(0);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const T n = __shfl_up_sync(0xFFFFFFFFu, w, o);
+      if (lane >= o) w += n;
+    }
+    warp_tot[lane] = w;  // inclusive scan of warp totals (kWarps == 32)
+  }
+  __syncthreads();
+  const T before = warp == 0 ? T(0) : warp_tot[warp - 1];
+  total = warp_tot[kWarps - 1];
+  __syncthreads();  // warp_tot may be reused right after
+  return v + before;
+}
+
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = scratch[0];
+#pragma unroll 1
+  for (int w = 1; w < kWarps; ++w) r = fmaxf(r, scratch[w]);
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ double block_sum(double v, double* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  __syncthreads();
+  double r = 0.0;
+#pragma unroll 1
+  for (int w = 0; w < kWarps; ++w) r += scratch[w];
+  __syncthreads();
+  return r;
+}
+
+// Calls f(x) for every logit of the row, VEC at a time when the row allows it.
+template <int VEC, typename F>
+__device__ __forceinline__ void for_row(const float* row, int64_t vocab, F&& f) {
+  if constexpr (VEC == 4) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const int64_t n4 = vocab / 4;
+    for (int64_t i = threadIdx.x; i < n4; i += kThreads) {
+      const float4 v = r4[i];
+      f(v.x);
+      f(v.y);
+      f(v.z);
+      f(v.w);
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < vocab; i += kThreads) f(row[i]);
+  }
+}
+
+// Top-k selection over s.count: the bin holding the `remaining`-th largest key among the
+// keys that match the prefix.  Updates remaining (keys ranked above that bin removed).
+__device__ __forceinline__ uint32_t select_from_top(SamplerSmem& s, uint32_t& remaining) {
+  const int b0 = 2 * threadIdx.x, b1 = b0 + 1;
+  const uint32_t c0 = s.count[b0], c1 = s.count[b1];
+  uint32_t total;
+  const uint32_t incl = block_inclusive_scan<uint32_t>(c0 + c1, s.warp_u, total);
+  // keys in bins above b1 / above b0
+  const uint32_t above1 = total - incl, above0 = above1 + c1;
+  if (c1 > 0 && above1 < remaining && remaining <= above1 + c1) {
+    s.chosen = b1;
+    s.fallback = above1;
+  }
+  if (c0 > 0 && above0 < remaining && remaining <= above0 + c0) {
+    s.chosen = b0;
+    s.fallback = above0;
+  }
+  __syncthreads();
+  const uint32_t bin = s.chosen;
+  remaining -= s.fallback;
+  __syncthreads();
+  return bin;
+}
+
+// Top-p selection over s.weight/s.count: the smallest non-empty bin whose inclusive
+// cumulative weight, added to `base`, exceeds target; if rounding leaves none, the
+// largest non-empty bin.  Updates base with the weight of the bins below the choice.
+__device__ __forceinline__ uint32_t select_from_bottom(SamplerSmem& s, double& base, double target) {
+  const int b0 = 2 * threadIdx.x, b1 = b0 + 1;
+  const double w0 = s.weight[b0], w1 = s.weight[b1];
+  const uint32_t c0 = s.count[b0], c1 = s.count[b1];
+  if (threadIdx.x == 0) {
+    s.chosen = kBins;
+    s.fallback = 0;
+  }
+  double total;
+  const double incl1 = block_inclusive_scan<double>(w0 + w1, s.warp_d, total);  // syncs
+  const double excl0 = incl1 - (w0 + w1), incl0 = excl0 + w0;
+  // the inclusive sums grow with the bin index, so the smallest non-empty bin whose
+  // inclusive sum exceeds the target is the crossing bin (no lower-bound test, which could
+  // leave an ulp-sized gap between neighbouring threads' sums)
+  if (c0 > 0 && target < base + incl0) atomicMin(&s.chosen, uint32_t(b0));
+  if (c1 > 0 && target < base + incl1) atomicMin(&s.chosen, uint32_t(b1));
+  if (c1 > 0) atomicMax(&s.fallback, uint32_t(b1));
+  else if (c0 > 0) atomicMax(&s.fallback, uint32_t(b0));
+  __syncthreads();
+  const uint32_t bin = s.chosen < kBins ? s.chosen : s.fallback;
+  // weight below the chosen bin: the owner of the bin publishes it
+  if (bin == uint32_t(b0)) s.warp_d[0] = excl0;
+  if (bin == uint32_t(b1)) s.warp_d[0] = incl0;
+  __syncthreads();
+  base += s.warp_d[0];
+  __syncthreads();
+  return bin;
+}
+
+template <int VEC, typename KT>
+__global__ void __launch_bounds__(kThreads, 1) top_k_top_p_kernel(
+    float* __restrict__ logits, int64_t vocab, int64_t row_stride, const KT* __restrict__ top_k,
+    const float* __restrict__ top_p) {
+  __shared__ SamplerSmem s;
+  float* row = logits + static_cast<int64_t>(blockIdx.x) * row_stride;
+  pdl_trigger();
+  pdl_wait();
+  const bool use_k = top_k != nullptr, use_p = top_p != nullptr;
+  int64_t k = vocab;
+  if (use_k) {
+    k = static_cast<int64_t>(top_k[blockIdx.x]);
+    k = k < 1 ? 1 : (k > vocab ? vocab : k);
+  }
+  const bool filter_k = use_k && k < vocab;
+  for (int b = threadIdx.x; b < kBins; b += kThreads) s.count[b] = 0;
+  __syncthreads();
+
+  // pass 1: row max (always) and the first top-k digit
+  float m = -INFINITY;
+  for_row<VEC>(row, vocab, [&](float x) {
+    m = fmaxf(m, x);
+    if (filter_k) atomicAdd(&s.count[ordered_key(x) >> 21], 1u);
+  });
+  m = block_max(m, s.warp_f);
+
+  // top-k: three digits; every logit >= t_k survives
+  float t_k = -INFINITY;
+  if (filter_k) {
+    uint32_t remaining = static_cast<uint32_t>(k), prefix = 0;
+    for (int d = 0; d < 3; ++d) {
+      if (d > 0) {
+        for (int b = threadIdx.x; b < kBins; b += kThreads) s.count[b] = 0;
+        __syncthreads();
+        const uint32_t pm = prefix_mask(d), dm = digit_mask(d);
+        const int sh = digit_shift(d);
+        for_row<VEC>(row, vocab, [&](float x) {
+          const uint32_t u = ordered_key(x);
+          if ((u & pm) == prefix) atomicAdd(&s.count[(u >> sh) & dm], 1u);
+        });
+        __syncthreads();
+      } else {
+        __syncthreads();
+      }
+      prefix |= select_from_top(s, remaining) << digit_shift(d);
+    }
+    t_k = key_value(prefix);
+  }
+
+  // top-p over the survivors of top-k
+  uint32_t cut = 0;  // keys >= cut survive (0: everything)
+  // A row of -inf logits has no probabilities (the reference's softmax gives NaN there and
+  // masks nothing): it is left as it is.
+  const bool filter_p = use_p && m != -INFINITY;
+  if (filter_p) {
+    double z = 0.0;
+    {
+      float zt = 0.f;
+      for_row<VEC>(row, vocab, [&](float x) {
+        if (x >= t_k) zt += expf(x - m);
+      });
+      z = block_sum(zt, s.warp_d);
+    }
+    const float zf = static_cast<float>(z);
+    const double target = static_cast<double>(__fsub_rn(1.0f, top_p[blockIdx.x]));
+    double base = 0.0;
+    uint32_t prefix = 0;
+    for (int d = 0; d < 3; ++d) {
+      for (int b = threadIdx.x; b < kBins; b += kThreads) {
+        s.count[b] = 0;
+        s.weight[b] = 0.f;
+      }
+      __syncthreads();
+      const uint32_t pm = prefix_mask(d), dm = digit_mask(d);
+      const int sh = digit_shift(d);
+      for_row<VEC>(row, vocab, [&](float x) {
+        const uint32_t u = ordered_key(x);
+        if (x >= t_k && (u & pm) == prefix) {
+          const int bin = (u >> sh) & dm;
+          atomicAdd(&s.count[bin], 1u);
+          atomicAdd(&s.weight[bin], __fdiv_rn(expf(x - m), zf));
+        }
+      });
+      __syncthreads();
+      prefix |= select_from_bottom(s, base, target) << sh;
+    }
+    cut = prefix;
+  }
+
+  if (!filter_k && !filter_p) return;
+  // masking write, in place
+  if constexpr (VEC == 4) {
+    float4* r4 = reinterpret_cast<float4*>(row);
+    const int64_t n4 = vocab / 4;
+    for (int64_t i = threadIdx.x; i < n4; i += kThreads) {
+      float4 v = r4[i];
+      auto keep = [&](float x) { return x >= t_k && ordered_key(x) >= cut ? x : -INFINITY; };
+      v.x = keep(v.x);
+      v.y = keep(v.y);
+      v.z = keep(v.z);
+      v.w = keep(v.w);
+      r4[i] = v;
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < vocab; i += kThreads) {
+      const float x = row[i];
+      row[i] = x >= t_k && ordered_key(x) >= cut ? x : -INFINITY;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// random sample: argmax_i probs[i] / q[i]
+// ---------------------------------------------------------------------------------------
+
+constexpr int kSampleThreads = 512;
+
+// (quotient, index) packed so that the larger key is the larger quotient, NaN above every
+// number, and on equal quotients the smaller index
+__device__ __forceinline__ uint64_t sample_key(float v, int64_t i) {
+  const uint32_t ord = isnan(v) ? 0xFFFFFFFFu : ordered_key(v);
+  return (static_cast<uint64_t>(ord) << 32) | static_cast<uint64_t>(0xFFFFFFFFu - static_cast<uint32_t>(i));
+}
+
+template <int VEC>
+__global__ void __launch_bounds__(kSampleThreads) random_sample_kernel(
+    int64_t* __restrict__ out, const float* __restrict__ probs, const float* __restrict__ q,
+    int64_t vocab, int64_t probs_stride, int64_t q_stride) {
+  __shared__ uint64_t warp_best[kSampleThreads / 32];
+  const float* pr = probs + static_cast<int64_t>(blockIdx.x) * probs_stride;
+  const float* qr = q + static_cast<int64_t>(blockIdx.x) * q_stride;
+  pdl_trigger();
+  pdl_wait();
+  uint64_t best = 0;
+  if constexpr (VEC == 4) {
+    const int64_t n4 = vocab / 4;
+    const float4* p4 = reinterpret_cast<const float4*>(pr);
+    const float4* q4 = reinterpret_cast<const float4*>(qr);
+    for (int64_t i = threadIdx.x; i < n4; i += kSampleThreads) {
+      const float4 a = __ldcs(p4 + i), b = __ldcs(q4 + i);
+      const int64_t e = 4 * i;
+      uint64_t k0 = sample_key(__fdiv_rn(a.x, b.x), e), k1 = sample_key(__fdiv_rn(a.y, b.y), e + 1);
+      uint64_t k2 = sample_key(__fdiv_rn(a.z, b.z), e + 2), k3 = sample_key(__fdiv_rn(a.w, b.w), e + 3);
+      k0 = k0 > k1 ? k0 : k1;
+      k2 = k2 > k3 ? k2 : k3;
+      k0 = k0 > k2 ? k0 : k2;
+      best = best > k0 ? best : k0;
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < vocab; i += kSampleThreads) {
+      const uint64_t k = sample_key(__fdiv_rn(pr[i], qr[i]), i);
+      best = best > k ? best : k;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t n = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    best = best > n ? best : n;
+  }
+  if ((threadIdx.x & 31) == 0) warp_best[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t r = warp_best[0];
+    for (int w = 1; w < kSampleThreads / 32; ++w) r = r > warp_best[w] ? r : warp_best[w];
+    out[blockIdx.x] = static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(r & 0xFFFFFFFFu));
+  }
+}
+
+template <typename KT>
+int launch_top_k_top_p(float* logits, int64_t rows, int64_t vocab, int64_t stride, const KT* k,
+                       const float* p, cudaStream_t stream) {
+  const bool vec = vocab % 4 == 0 && stride % 4 == 0 && aligned16(logits);
+  if (vec)
+    return launch_kernel("top_k_top_p", top_k_top_p_kernel<4, KT>, dim3(static_cast<unsigned>(rows)),
+                         dim3(kThreads), 0, stream, logits, vocab, stride, k, p);
+  return launch_kernel("top_k_top_p", top_k_top_p_kernel<1, KT>, dim3(static_cast<unsigned>(rows)),
+                       dim3(kThreads), 0, stream, logits, vocab, stride, k, p);
+}
+
+}  // namespace
+}  // namespace ntb200
+
+extern "C" int ntb200_top_k_top_p(float* logits, int64_t num_rows, int64_t vocab, int64_t row_stride,
+                                  const void* top_k, int top_k_dtype, const float* top_p, void* stream) {
+  using namespace ntb200;
+  if (num_rows < 0 || vocab < 0 || row_stride < vocab)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "top_k_top_p: bad shape");
+  if (num_rows == 0 || vocab == 0 || (top_k == nullptr && top_p == nullptr)) return NTB200_OK;
+  if (logits == nullptr) return fail(NTB200_ERR_INVALID_ARGUMENT, "top_k_top_p: null logits");
+  if (num_rows > 0x7fffffff || vocab > 0x7fffffff)
+    return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "top_k_top_p: too many rows or a vocabulary >= 2^31");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (top_k == nullptr)
+    return launch_top_k_top_p<int64_t>(logits, num_rows, vocab, row_stride, nullptr, top_p, s);
+  if (top_k_dtype == NTB200_DTYPE_I64)
+    return launch_top_k_top_p(logits, num_rows, vocab, row_stride, static_cast<const int64_t*>(top_k), top_p, s);
+  if (top_k_dtype == NTB200_DTYPE_I32)
+    return launch_top_k_top_p(logits, num_rows, vocab, row_stride, static_cast<const int32_t*>(top_k), top_p, s);
+  return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "top_k_top_p: top_k dtype %d", top_k_dtype);
+}
+
+extern "C" int ntb200_random_sample(int64_t* out, const float* probs, const float* q, int64_t num_rows,
+                                   int64_t vocab, int64_t probs_row_stride, int64_t q_row_stride,
+                                   void* stream) {
+  using namespace ntb200;
+  if (num_rows < 0 || vocab <= 0 || probs_row_stride < vocab || q_row_stride < vocab)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "random_sample: bad shape");
+  if (num_rows == 0) return NTB200_OK;
+  if (out == nullptr || probs == nullptr || q == nullptr)
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "random_sample: null pointer");
+  if (num_rows > 0x7fffffff || vocab > 0x7fffffff)
+    return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "random_sample: too many rows or a vocabulary >= 2^31");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = vocab % 4 == 0 && probs_row_stride % 4 == 0 && q_row_stride % 4 == 0 && aligned16(probs) &&
+                   aligned16(q);
+  const dim3 grid(static_cast<unsigned>(num_rows));
+  if (vec)
+    return launch_kernel("random_sample", random_sample_kernel<4>, grid, dim3(kSampleThreads), 0, s, out, probs,
+                         q, vocab, probs_row_stride, q_row_stride);
+  return launch_kernel("random_sample", random_sample_kernel<1>, grid, dim3(kSampleThreads), 0, s, out, probs, q,
+                       vocab, probs_row_stride, q_row_stride);
+}

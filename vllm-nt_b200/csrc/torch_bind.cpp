@@ -605,6 +605,50 @@ int64_t linear_workspace_size(int64_t m, int64_t n, int64_t k) {
   return static_cast<int64_t>(ntb200_linear_workspace_size(m, n, k));
 }
 
+
+// Top-k / top-p mask of fp32 logits [rows, vocab] in place; k (int32/int64 [rows]) or p
+// (fp32 [rows]) may be absent.
+void top_k_top_p(at::Tensor logits, const std::optional<at::Tensor>& k, const std::optional<at::Tensor>& p) {
+  require_rows(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat, "ntb200.top_k_top_p: logits must be float32");
+  const int64_t rows = logits.size(0);
+  const void* kp = nullptr;
+  int kdt = NTB200_DTYPE_I64;
+  if (k.has_value()) {
+    require_cuda(*k, "k");
+    TORCH_CHECK(k->dim() == 1 && k->is_contiguous() && k->size(0) == rows &&
+                    (k->scalar_type() == at::kInt || k->scalar_type() == at::kLong),
+                "ntb200.top_k_top_p: k must be contiguous int32/int64 [rows]");
+    kp = k->data_ptr();
+    kdt = dtype_code(*k);
+  }
+  const float* pp = nullptr;
+  if (p.has_value()) {
+    require_cuda(*p, "p");
+    TORCH_CHECK(p->dim() == 1 && p->is_contiguous() && p->size(0) == rows && p->scalar_type() == at::kFloat,
+                "ntb200.top_k_top_p: p must be contiguous float32 [rows]");
+    pp = p->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard guard(logits.device());
+  check(ntb200_top_k_top_p(logits.data_ptr<float>(), rows, logits.size(1), logits.stride(0), kp, kdt, pp,
+                           stream_of(logits)),
+        "top_k_top_p");
+}
+
+// out[b] = argmax_i probs[b, i] / q[b, i] (int64 [rows]); probs and q fp32 [rows, vocab]
+void random_sample(at::Tensor out, const at::Tensor& probs, const at::Tensor& q) {
+  require_rows(probs, "probs");
+  require_rows(q, "q");
+  require_cuda(out, "out");
+  TORCH_CHECK(probs.scalar_type() == at::kFloat && q.scalar_type() == at::kFloat && q.sizes() == probs.sizes(),
+              "ntb200.random_sample: probs and q must be float32 of one shape");
+  TORCH_CHECK(out.scalar_type() == at::kLong && out.is_contiguous() && out.numel() == probs.size(0),
+              "ntb200.random_sample: out must be contiguous int64 [rows]");
+  c10::cuda::CUDAGuard guard(probs.device());
+  check(ntb200_random_sample(out.data_ptr<int64_t>(), probs.data_ptr<float>(), q.data_ptr<float>(), probs.size(0),
+                             probs.size(1), probs.stride(0), q.stride(0), stream_of(probs)),
+        "random_sample");
+}
 }  // namespace
 
 TORCH_LIBRARY(ntb200, m) {
@@ -665,6 +709,8 @@ TORCH_LIBRARY(ntb200, m) {
       "allreduce_oneshot(Tensor(a!) out, Tensor partial, Tensor peer_buffers, int capacity, int rank, "
       "int world_size) -> ()");
   m.def("allreduce_buffer_size(int capacity, int elem_bytes, int world_size) -> int", &allreduce_buffer_size);
+  m.def("top_k_top_p(Tensor(a!) logits, Tensor? k, Tensor? p) -> ()");
+  m.def("random_sample(Tensor(a!) out, Tensor probs, Tensor q) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
@@ -687,4 +733,6 @@ TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("prefill_flash_layout", &prefill_flash_layout);
   m.impl("flash_attn_varlen", &flash_attn_varlen);
   m.impl("attention_flash_layout", &attention_flash_layout);
+  m.impl("top_k_top_p", &top_k_top_p);
+  m.impl("random_sample", &random_sample);
 }

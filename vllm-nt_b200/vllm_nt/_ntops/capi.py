@@ -100,6 +100,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_size_t,
                 c_int, c_void_p]
     ),
+    "ntb200_top_k_top_p": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int, c_void_p, c_void_p]),
+    "ntb200_random_sample": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p]
+    ),
     "ntb200_allreduce_buffer_size": (c_size_t, [c_int64, c_int, c_int]),
     "ntb200_allreduce_oneshot": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p]

@@ -26,6 +26,8 @@ from vllm_nt._ntops.torch.rms_norm import rms_norm as nt_rms_norm
 from vllm_nt._ntops.torch.rotary_emb import apply_rotary_emb as nt_apply_rotary_emb
 from vllm_nt._ntops.torch.rotary_emb import rotary_embedding as nt_rotary_embedding
 from vllm_nt._ntops.torch.silu import silu_and_mul as nt_silu_and_mul
+from vllm_nt._ntops.torch.sampler import apply_top_k_top_p as nt_apply_top_k_top_p  # noqa: F401
+from vllm_nt._ntops.torch.sampler import random_sample as nt_random_sample  # noqa: F401
 
 
 @dataclass

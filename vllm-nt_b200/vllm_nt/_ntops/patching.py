@@ -50,7 +50,9 @@ from vllm_nt._ntops.oot_support import (
     gate_up_silu_and_mul,
     linear,
     norm,
+    nt_apply_top_k_top_p,
     nt_paged_decode,
+    nt_random_sample,
     paged_attention_decode_flash,
     paged_attention_flash,
     rope,
@@ -620,6 +622,75 @@ def _build_mlp_forward(original: object) -> object:
     return _mark_function_patch(forward, "GateUpSiluAndMul")
 
 
+
+def _sampler_logits_eligible(x: torch.Tensor) -> bool:
+    """fp32 rows on a CUDA device with unit stride in the vocabulary dimension."""
+    return x.is_cuda and x.dtype == torch.float32 and x.dim() == 2 and x.stride(-1) == 1
+
+
+def _build_apply_top_k_top_p_patch(original: object) -> object:
+    """Replacement for vLLM's topk_topp_sampler.apply_top_k_top_p(logits, k, p) (the
+    reference's TopKTopP patch, vllm_nt/_ntops/patching.py:1446-1463): the mask is the
+    radix-select kernel instead of a sort of every row.  vLLM's TopKTopPSampler reaches it
+    on its native path (per-request generators, or FlashInfer sampling turned off)."""
+    if _is_function_patch(original, "TopKTopP"):
+        return original
+    original_fn = cast(Callable[..., Any], original)
+
+    def wrapped(logits: torch.Tensor, k: torch.Tensor | None, p: torch.Tensor | None):
+        call = lambda: original_fn(logits, k, p)  # noqa: E731
+        if (k is None and p is None) or not _sampler_logits_eligible(logits):
+            return call()
+
+        def kernels():
+            _record_hit("TopKTopP", logits)
+            return nt_apply_top_k_top_p(logits, k, p)
+
+        return _route("TopKTopP", call, kernels)
+
+    return _mark_function_patch(wrapped, "TopKTopP")
+
+
+def _build_random_sample_patch(original: object) -> object:
+    """Replacement for vLLM's topk_topp_sampler.random_sample(probs, generators) (the
+    reference's RandomSample patch, vllm_nt/_ntops/patching.py:1466-1479): the division by
+    the exponential draws and the argmax are one kernel pass."""
+    if _is_function_patch(original, "RandomSample"):
+        return original
+    original_fn = cast(Callable[..., Any], original)
+
+    def wrapped(probs: torch.Tensor, generators: dict[int, torch.Generator]):
+        call = lambda: original_fn(probs, generators)  # noqa: E731
+        if not _sampler_logits_eligible(probs):
+            return call()
+
+        def kernels():
+            _record_hit("RandomSample", probs)
+            return nt_random_sample(probs, generators)
+
+        return _route("RandomSample", call, kernels)
+
+    return _mark_function_patch(wrapped, "RandomSample")
+
+
+def _build_rejection_sample_patch(original: object) -> object:
+    """Counts vLLM's rejection_sample calls under RejectionSample and runs vLLM's own code,
+    as the reference's patch does (vllm_nt/_ntops/patching.py:1482-1497).  The hit is
+    recorded against the target distribution: the ``target_logits`` (older vLLM:
+    ``target_probs``) keyword, else the sixth positional argument."""
+    if _is_function_patch(original, "RejectionSample"):
+        return original
+    original_fn = cast(Callable[..., Any], original)
+
+    def wrapped(*args: Any, **kwargs: Any):
+        candidates = (kwargs.get("target_logits"), kwargs.get("target_probs"), args[5] if len(args) > 5 else None)
+        target = next((c for c in candidates if isinstance(c, torch.Tensor)), None)
+        if target is not None:
+            _record_hit("RejectionSample", target)
+        return original_fn(*args, **kwargs)
+
+    return _mark_function_patch(wrapped, "RejectionSample")
+
 _OPERATOR_SPECS: dict[str, tuple[type, Callable[..., Any]]] = {
     "RMSNorm": (layernorm.RMSNorm, _nt_rms_norm_forward),
     "SiluAndMul": (activation.SiluAndMul, _nt_silu_and_mul_forward),
@@ -669,6 +740,7 @@ for _name, _attr_cls in (("MulAndSilu", "MulAndSilu"), ("GeluAndMul", "GeluAndMu
 _ROPE_MODULES = ("vllm.model_executor.layers.rotary_embedding.base",)
 _FA_MODULE = "vllm.v1.attention.backends.flash_attn"
 _FI_MODULE = "vllm.v1.attention.backends.flashinfer"
+_SAMPLER_MODULE = "vllm.v1.sample.ops.topk_topp_sampler"
 _FUNCTION_PATCH_SPECS: tuple[FunctionPatchSpec, ...] = (
     *(
         FunctionPatchSpec("RoPE", mod, attr, "RotaryEmbedding", False, _build_rotary_forward)
@@ -679,6 +751,12 @@ _FUNCTION_PATCH_SPECS: tuple[FunctionPatchSpec, ...] = (
     FunctionPatchSpec("PagedAttentionDecode", _FA_MODULE, "forward", "FlashAttentionImpl", False, _build_flash_attn_forward),
     FunctionPatchSpec("StoreKVCache", _FI_MODULE, "do_kv_cache_update", "FlashInferImpl", False, _build_flashinfer_kv_update),
     FunctionPatchSpec("PagedAttentionDecode", _FI_MODULE, "forward", "FlashInferImpl", False, _build_flashinfer_forward),
+    FunctionPatchSpec("TopKTopP", _SAMPLER_MODULE, "apply_top_k_top_p", None, False, _build_apply_top_k_top_p_patch),
+    FunctionPatchSpec("RandomSample", _SAMPLER_MODULE, "random_sample", None, False, _build_random_sample_patch),
+    FunctionPatchSpec(
+        "RejectionSample", "vllm.v1.sample.rejection_sampler", "rejection_sample", None, False,
+        _build_rejection_sample_patch,
+    ),
     *(
         FunctionPatchSpec("GateUpSiluAndMul", mod, "forward", cls, False, _build_mlp_forward)
         for mod, cls in (

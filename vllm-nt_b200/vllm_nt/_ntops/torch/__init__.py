@@ -9,11 +9,13 @@ from vllm_nt._ntops.torch.embedding import embedding
 from vllm_nt._ntops.torch.kv_cache import get_kv_from_cache, store_kvcache
 from vllm_nt._ntops.torch.linear import linear, matmul
 from vllm_nt._ntops.torch.rms_norm import fused_add_rms_norm, rms_norm
+from vllm_nt._ntops.torch.sampler import apply_top_k_top_p, random_sample
 from vllm_nt._ntops.torch.rotary_emb import apply_rotary_emb, rotary_embedding, rotary_embedding_and_cache
 from vllm_nt._ntops.torch.silu import silu_and_mul
 
 __all__ = [
     "apply_rotary_emb",
+    "apply_top_k_top_p",
     "embedding",
     "flash_attn_varlen_func",
     "flash_attn_with_kvcache",
@@ -22,6 +24,7 @@ __all__ = [
     "linear",
     "matmul",
     "paged_decode",
+    "random_sample",
     "rms_norm",
     "rotary_embedding",
     "rotary_embedding_and_cache",

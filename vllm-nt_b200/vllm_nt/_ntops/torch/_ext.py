@@ -47,6 +47,8 @@ def _register_fakes() -> None:
         "prefill_flash_layout",
         "flash_attn_varlen",
         "attention_flash_layout",
+        "top_k_top_p",
+        "random_sample",
     ):
         torch.library.register_fake(f"ntb200::{name}")(nothing)
 
