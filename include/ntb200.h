@@ -126,9 +126,11 @@ int ntb200_reshape_and_cache(const void* key, const void* value, void* key_cache
  *     key_cache  [slot / block_size, slot % block_size, h, :] = rotated key[t, h, :]
  *     value_cache[slot / block_size, slot % block_size, h, :] = value[t, h, :]
  * The result is bit-identical to ntb200_rotary_embedding_neox followed by
- * ntb200_reshape_and_cache.  Negative slots (vLLM padding) only rotate; slots >= num_slots
- * only rotate and set NTB200_DEVERR_INDEX_RANGE; a position outside [0, num_cache_rows)
- * leaves the token untouched (no rotation, no store) and sets NTB200_DEVERR_INDEX_RANGE.
+ * ntb200_reshape_and_cache, in every case: negative slots (vLLM padding) only rotate; slots
+ * >= num_slots only rotate and set NTB200_DEVERR_INDEX_RANGE; a position outside
+ * [0, num_cache_rows) leaves the token's q/k unrotated (its unrotated k and its v are still
+ * stored) and sets NTB200_DEVERR_INDEX_RANGE.  One fused kernel below 2048 tokens; from
+ * 2048 tokens on, where the two kernels keep more bytes in flight, the pair is launched.
  * key and value rows have num_kv_heads heads of head_size; both caches share the strides
  * given and have the dtype of query/key/value (F32, BF16 or F16).  positions: I64 or I32,
  * num_tokens entries; slot_mapping: I64 or I32, num_store_tokens (<= num_tokens) entries;

@@ -127,19 +127,24 @@ def test_partial_rotary_scalar_path_int32_padded_rows(dtype):
     assert capi.read_device_error(stream()) == 0
 
 
-def test_flashinfer_hnd_cache_matches_unfused_kernels():
+@pytest.mark.parametrize("t", [1024, 4096])
+def test_flashinfer_hnd_cache_matches_oracle_and_unfused_kernels(t):
     """FlashInfer's cache [blocks, 2, 16, H, D] in HND memory order (kv_dim 1, head stride
-    16 x 128), at a prefill-sized step of 4096 tokens: the fused kernel and this library's
-    RoPE kernel followed by its KV-store kernel leave identical bits everywhere."""
+    16 x 128) at prefill-sized steps: 1024 tokens (the fused kernel) and 4096 tokens (the
+    entry point launches the RoPE and KV-store kernels from 2048 tokens on).  Both leave
+    the oracle's bits, and the same bits as calling the two kernels directly."""
     dev = cuda_device()
-    t, hq, hk, d = 4096, 32, 8, 128
-    buf, _, _, _ = _qkv(t, hq, hk, d, torch.bfloat16, 26)
+    hq, hk, d = 32, 8, 128
+    buf, q, k, v = _qkv(t, hq, hk, d, torch.bfloat16, 26)
     g = seeded(27)
-    pos = torch.randint(0, 16384, (t,), generator=g).to(dev)
-    cache = oracle.build_cos_sin_cache(d, 16384, 500000.0).to(torch.bfloat16).to(dev)
+    pos = torch.randint(0, 16384, (t,), generator=g)
+    cache = oracle.build_cos_sin_cache(d, 16384, 500000.0)
+    cache_d = cache.to(torch.bfloat16).to(dev)
     blocks = 512
-    slots = torch.randperm(blocks * 16, generator=g)[:t].to(dev)
+    slots = torch.randperm(blocks * 16, generator=g)[:t]
     width = (hq + 2 * hk) * d
+    zeros = torch.zeros(blocks, 16, hk, d, dtype=torch.bfloat16)
+    rq, rk, rkc, rvc = _oracle(pos, q, k, v, cache, zeros, zeros, slots, d, d)
 
     def fresh():
         b = buf.to(dev)
@@ -147,21 +152,23 @@ def test_flashinfer_hnd_cache_matches_unfused_kernels():
         return b, b[:, : hq * d], b[:, hq * d : (hq + hk) * d], b[:, (hq + hk) * d : width], kv
 
     b1, q1, k1, v1, kv1 = fresh()
-    ops().rope_and_cache_flash_layout(pos, q1, k1, v1, cache, kv1, slots, d, d, 1)
+    ops().rope_and_cache_flash_layout(pos.to(dev), q1, k1, v1, cache_d, kv1, slots.to(dev), d, d, 1)
     b2, q2, k2, v2, kv2 = fresh()
-    ops().rotary_embedding_neox(pos, q2, k2, cache, d, d)
-    ops().store_flash_layout(k2, v2, kv2, slots, 1)
+    ops().rotary_embedding_neox(pos.to(dev), q2, k2, cache_d, d, d)
+    ops().store_flash_layout(k2, v2, kv2, slots.to(dev), 1)
     torch.cuda.synchronize()
     assert kv1.stride(3) == 16 * d  # HND: heads outermost inside a page
     assert bits_equal(b1.cpu(), b2.cpu())
     assert bits_equal(kv1.contiguous().cpu(), kv2.contiguous().cpu())
-    assert kv1.view(-1).count_nonzero().item() > 0
+    assert bits_equal(q1.cpu().contiguous(), rq) and bits_equal(k1.cpu().contiguous(), rk)
+    assert bits_equal(kv1[:, 0].contiguous().cpu(), rkc) and bits_equal(kv1[:, 1].contiguous().cpu(), rvc)
     assert capi.read_device_error(stream()) == 0
 
 
 def test_out_of_range_position_and_slot_are_flagged_and_skipped():
-    """A position past the cos/sin cache leaves its token untouched and unstored; a slot
-    past the cache is rotated but not stored; both raise the index-range bit."""
+    """As the two kernels in sequence: a position past the cos/sin cache leaves its token's
+    q/k unrotated (its unrotated k and its v are still stored); a slot past the cache is
+    rotated but not stored; both raise the index-range bit."""
     dev = cuda_device()
     t, hq, hk, d = 4, 2, 1, 128
     buf, q, k, v = _qkv(t, hq, hk, d, torch.bfloat16, 28)
@@ -179,9 +186,9 @@ def test_out_of_range_position_and_slot_are_flagged_and_skipped():
     ok = [0, 2, 3]
     rq, rk = oracle.rope_neox(pos[ok], q[ok].contiguous(), k[ok].contiguous(), cache, d, d)
     assert bits_equal(qd[ok].cpu(), rq) and bits_equal(kd[ok].cpu(), rk)
-    assert bits_equal(qd[1].cpu(), q[1]) and bits_equal(kd[1].cpu(), k[1])  # token 1 untouched
+    assert bits_equal(qd[1].cpu(), q[1]) and bits_equal(kd[1].cpu(), k[1])  # token 1 unrotated
     kflat, vflat = kcd.view(32, hk * d).cpu(), vcd.view(32, hk * d).cpu()
     assert bits_equal(kflat[0], rk[0]) and bits_equal(kflat[2], rk[2])
     assert bits_equal(vflat[0], v[0]) and bits_equal(vflat[2], v[3])
-    assert kflat[1].count_nonzero() == 0 and vflat[1].count_nonzero() == 0  # token 1 not stored
-    assert kflat[3:].count_nonzero() == 0  # token 2 (slot 32) not stored
+    assert bits_equal(kflat[1], k[1]) and bits_equal(vflat[1], v[1])  # token 1 stored unrotated
+    assert kflat[3:].count_nonzero() == 0 and vflat[3:].count_nonzero() == 0  # token 2 (slot 32) not stored

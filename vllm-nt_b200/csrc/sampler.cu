@@ -110,21 +110,42 @@ __device__ __forceinline__ double block_sum(double v, double* scratch) {
   return r;
 }
 
-// Calls f(x) for every logit of the row, VEC at a time when the row allows it.
+// Loads each thread keeps in flight per pass: a single CTA streams a whole row, so at small
+// batches a pass is latency-bound and its speed grows with the bytes in flight.
+constexpr int kInFlight = 4;
+
+// Calls f(x) for every logit of the row, VEC at a time when the row allows it; each thread
+// issues kInFlight loads before it consumes any of them.
 template <int VEC, typename F>
 __device__ __forceinline__ void for_row(const float* row, int64_t vocab, F&& f) {
   if constexpr (VEC == 4) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
     const int64_t n4 = vocab / 4;
-    for (int64_t i = threadIdx.x; i < n4; i += kThreads) {
-      const float4 v = r4[i];
-      f(v.x);
-      f(v.y);
-      f(v.z);
-      f(v.w);
+    for (int64_t i = threadIdx.x; i < n4; i += kInFlight * kThreads) {
+      float4 v[kInFlight];
+#pragma unroll
+      for (int j = 0; j < kInFlight; ++j)
+        if (i + j * kThreads < n4) v[j] = r4[i + j * kThreads];
+#pragma unroll
+      for (int j = 0; j < kInFlight; ++j) {
+        if (i + j * kThreads < n4) {
+          f(v[j].x);
+          f(v[j].y);
+          f(v[j].z);
+          f(v[j].w);
+        }
+      }
     }
   } else {
-    for (int64_t i = threadIdx.x; i < vocab; i += kThreads) f(row[i]);
+    for (int64_t i = threadIdx.x; i < vocab; i += kInFlight * kThreads) {
+      float v[kInFlight];
+#pragma unroll
+      for (int j = 0; j < kInFlight; ++j)
+        if (i + j * kThreads < vocab) v[j] = row[i + j * kThreads];
+#pragma unroll
+      for (int j = 0; j < kInFlight; ++j)
+        if (i + j * kThreads < vocab) f(v[j]);
+    }
   }
 }
 
@@ -278,14 +299,22 @@ __global__ void __launch_bounds__(kThreads, 1) top_k_top_p_kernel(
   if constexpr (VEC == 4) {
     float4* r4 = reinterpret_cast<float4*>(row);
     const int64_t n4 = vocab / 4;
-    for (int64_t i = threadIdx.x; i < n4; i += kThreads) {
-      float4 v = r4[i];
-      auto keep = [&](float x) { return x >= t_k && ordered_key(x) >= cut ? x : -INFINITY; };
-      v.x = keep(v.x);
-      v.y = keep(v.y);
-      v.z = keep(v.z);
-      v.w = keep(v.w);
-      r4[i] = v;
+    auto keep = [&](float x) { return x >= t_k && ordered_key(x) >= cut ? x : -INFINITY; };
+    for (int64_t i = threadIdx.x; i < n4; i += kInFlight * kThreads) {
+      float4 v[kInFlight];
+#pragma unroll
+      for (int j = 0; j < kInFlight; ++j)
+        if (i + j * kThreads < n4) v[j] = r4[i + j * kThreads];
+#pragma unroll
+      for (int j = 0; j < kInFlight; ++j) {
+        if (i + j * kThreads < n4) {
+          v[j].x = keep(v[j].x);
+          v[j].y = keep(v[j].y);
+          v[j].z = keep(v[j].z);
+          v[j].w = keep(v[j].w);
+          r4[i + j * kThreads] = v[j];
+        }
+      }
     }
   } else {
     for (int64_t i = threadIdx.x; i < vocab; i += kThreads) {
@@ -322,15 +351,27 @@ __global__ void __launch_bounds__(kSampleThreads) random_sample_kernel(
     const int64_t n4 = vocab / 4;
     const float4* p4 = reinterpret_cast<const float4*>(pr);
     const float4* q4 = reinterpret_cast<const float4*>(qr);
-    for (int64_t i = threadIdx.x; i < n4; i += kSampleThreads) {
-      const float4 a = __ldcs(p4 + i), b = __ldcs(q4 + i);
-      const int64_t e = 4 * i;
-      uint64_t k0 = sample_key(__fdiv_rn(a.x, b.x), e), k1 = sample_key(__fdiv_rn(a.y, b.y), e + 1);
-      uint64_t k2 = sample_key(__fdiv_rn(a.z, b.z), e + 2), k3 = sample_key(__fdiv_rn(a.w, b.w), e + 3);
-      k0 = k0 > k1 ? k0 : k1;
-      k2 = k2 > k3 ? k2 : k3;
-      k0 = k0 > k2 ? k0 : k2;
-      best = best > k0 ? best : k0;
+    // two float4 of probs and two of q in flight per thread before any is consumed
+    for (int64_t i = threadIdx.x; i < n4; i += 2 * kSampleThreads) {
+      const int64_t i1 = i + kSampleThreads;
+      const float4 a0 = __ldcs(p4 + i), b0 = __ldcs(q4 + i);
+      float4 a1 = a0, b1 = b0;
+      if (i1 < n4) {
+        a1 = __ldcs(p4 + i1);
+        b1 = __ldcs(q4 + i1);
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        if (j == 1 && i1 >= n4) break;
+        const float4 a = j == 0 ? a0 : a1, b = j == 0 ? b0 : b1;
+        const int64_t e = 4 * (j == 0 ? i : i1);
+        uint64_t k0 = sample_key(__fdiv_rn(a.x, b.x), e), k1 = sample_key(__fdiv_rn(a.y, b.y), e + 1);
+        uint64_t k2 = sample_key(__fdiv_rn(a.z, b.z), e + 2), k3 = sample_key(__fdiv_rn(a.w, b.w), e + 3);
+        k0 = k0 > k1 ? k0 : k1;
+        k2 = k2 > k3 ? k2 : k3;
+        k0 = k0 > k2 ? k0 : k2;
+        best = best > k0 ? best : k0;
+      }
     }
   } else {
     for (int64_t i = threadIdx.x; i < vocab; i += kSampleThreads) {

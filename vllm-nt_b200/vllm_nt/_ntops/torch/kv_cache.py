@@ -36,6 +36,8 @@ def store_kvcache(key, value, k_cache, v_cache, slot_mapping):
 
 
 def get_kv_from_cache(k_cache, v_cache, seq_lens, block_table):
-    """Prefill helper of the reference (gathers each sequence's cached tokens); prefill is
-    not on this backend's hot path, so vLLM's own attention serves it."""
-    raise NotImplementedError("get_kv_from_cache is served by vLLM's original prefill path")
+    """Prefill helper of the reference (vllm_nt/_ntops/torch/kv_cache.py:24-63: copies each
+    sequence's cached tokens out of the paged cache).  This backend's prefill kernel reads
+    the paged cache in place through the block table (paged_attention_prefill), so nothing
+    is gathered and this helper has no implementation here."""
+    raise NotImplementedError("the B200 prefill reads the paged cache in place; use paged_attention_prefill")
