@@ -420,78 +420,89 @@ def per_op_table(dev, peaks) -> dict:
            time_graph([lambda i=i: o.reshape_and_cache(k3[i], v3[i], kc3, vc3, sl3) for i in range(2)], 10))
     del kc3, vc3, k3, v3
 
-    # RoPE fused with the KV store (one kernel) beside the two kernels it replaces (ours,
-    # and vLLM's _C pair), for a Llama-3-8B layer: qkv [T, 48*128] bf16, FlashAttention
-    # cache [2, 8192, 16, 8, 128], a decode step (256 tokens) and a prefill chunk (16384).
-    # Bytes: q and k read and written, v read, rotated k and v written to the cache,
-    # cos/sin rows, positions and slots.
-    kv4 = torch.zeros(2, 8192, 16, 8, 128, device=dev, dtype=torch.bfloat16)
-    for T4, iters4 in ((256, 20), (16384, 2)):
-        nb = 2 * T4 * 40 * 128 * 2 + T4 * 8 * 128 * 2 + 2 * T4 * 8 * 128 * 2 + T4 * 128 * 2 + T4 * 16
-        r4 = copies(nb)
-        qkv4 = [torch.randn(T4, 48 * 128, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(r4)]
-        pos4 = [torch.randint(0, 4096, (T4,), device=dev, generator=g) for _ in range(r4)]
-        sl4 = [torch.randperm(8192 * 16, device=dev, generator=g)[:T4] for _ in range(r4)]
-        parts = [(x[:, :4096], x[:, 4096:5120], x[:, 5120:]) for x in qkv4]
-        name = f"rope_and_cache bf16 {T4} tokens of qkv [T,48*128]"
-        report(name, nb, time_graph([lambda i=i: o.rope_and_cache_flash_layout(
-            pos4[i], *parts[i], cache3, kv4, sl4[i], 128, 128, 0) for i in range(r4)], iters4 * r4))
+    def rope_cache_rows():
+        # RoPE fused with the KV store (one kernel) beside the two kernels it replaces (ours,
+        # and vLLM's _C pair), for a Llama-3-8B layer: qkv [T, 48*128] bf16, FlashAttention
+        # cache [2, 8192, 16, 8, 128], a decode step (256 tokens) and a prefill chunk (16384).
+        # Bytes: q and k read and written, v read, rotated k and v written to the cache,
+        # cos/sin rows, positions and slots.
+        kv4 = torch.zeros(2, 8192, 16, 8, 128, device=dev, dtype=torch.bfloat16)
+        for T4, iters4 in ((256, 20), (16384, 2)):
+            nb = 2 * T4 * 40 * 128 * 2 + T4 * 8 * 128 * 2 + 2 * T4 * 8 * 128 * 2 + T4 * 128 * 2 + T4 * 16
+            r4 = copies(nb)
+            qkv4 = [torch.randn(T4, 48 * 128, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(r4)]
+            pos4 = [torch.randint(0, 4096, (T4,), device=dev, generator=g) for _ in range(r4)]
+            sl4 = [torch.randperm(8192 * 16, device=dev, generator=g)[:T4] for _ in range(r4)]
+            parts = [(x[:, :4096], x[:, 4096:5120], x[:, 5120:]) for x in qkv4]
+            name = f"rope_and_cache bf16 {T4} tokens of qkv [T,48*128]"
+            report(name, nb, time_graph([lambda i=i: o.rope_and_cache_flash_layout(
+                pos4[i], *parts[i], cache3, kv4, sl4[i], 128, 128, 0) for i in range(r4)], iters4 * r4))
 
-        def unfused(i):
-            q4, k4, v4 = parts[i]
-            o.rotary_embedding_neox(pos4[i], q4, k4, cache3, 128, 128)
-            o.store_flash_layout(k4, v4, kv4, sl4[i], 0)
+            def unfused(i):
+                q4, k4, v4 = parts[i]
+                o.rotary_embedding_neox(pos4[i], q4, k4, cache3, 128, 128)
+                o.store_flash_layout(k4, v4, kv4, sl4[i], 0)
 
-        us = time_graph([lambda i=i: unfused(i) for i in range(r4)], iters4 * r4) * 1e3
-        res[name]["unfused_us"] = round(us, 2)
-        res[name]["unfused_vs_fused"] = round(us / res[name]["us"], 3)
+            us = time_graph([lambda i=i: unfused(i) for i in range(r4)], iters4 * r4) * 1e3
+            res[name]["unfused_us"] = round(us, 2)
+            res[name]["unfused_vs_fused"] = round(us / res[name]["us"], 3)
 
-        def vllm_pair(i):
-            q4, k4, v4 = parts[i]
-            vops.rotary_embedding(pos4[i], q4, k4, 128, cache3, True)
-            vops.reshape_and_cache_flash(k4.view(T4, 8, 128), v4.view(T4, 8, 128), kv4[0], kv4[1], sl4[i], "auto",
-                                         one, one)
+            def vllm_pair(i):
+                q4, k4, v4 = parts[i]
+                vops.rotary_embedding(pos4[i], q4, k4, 128, cache3, True)
+                vops.reshape_and_cache_flash(k4.view(T4, 8, 128), v4.view(T4, 8, 128), kv4[0], kv4[1], sl4[i], "auto",
+                                             one, one)
 
-        lib(name, "vllm _C rotary_embedding + reshape_and_cache_flash",
-            vops and [lambda i=i: vllm_pair(i) for i in range(r4)], iters4 * r4)
-        del qkv4, parts
-    del kv4
+            lib(name, "vllm _C rotary_embedding + reshape_and_cache_flash",
+                vops and [lambda i=i: vllm_pair(i) for i in range(r4)], iters4 * r4)
+            del qkv4, parts
+        del kv4
 
-    # sampler at a decode batch of 256 over the Llama-3 vocabulary (fp32 logits, as vLLM's
-    # sampler holds them): the top-k/top-p mask (k = 50, p = 0.9 on every row) and the
-    # exponential-race sample.  The mask works in place, so each call first restores its
-    # logits from a pristine copy; the copy is timed alone and subtracted.  Algorithmic
-    # bytes: the logits read once and written once (mask); probs and q read once (sample).
-    B5, V5 = 256, 128256
-    src5 = torch.randn(B5, V5, device=dev, generator=g) * 2
-    lg5 = torch.empty_like(src5)
-    k5 = torch.full((B5,), 50, device=dev, dtype=torch.int32)
-    p5 = torch.full((B5,), 0.9, device=dev)
-    copy_us = time_graph([lambda: lg5.copy_(src5)], 10) * 1e3
-    name = "top_k_top_p f32 [256,128256] k=50 p=0.9"
-    us = time_graph([lambda: (lg5.copy_(src5), o.top_k_top_p(lg5, k5, p5))], 10) * 1e3 - copy_us
-    report(name, 2 * B5 * V5 * 4, us * 1e-3, {"note": "radix select, ~8 passes over each row (L2/HBM)"})
-    try:
-        from vllm.v1.sample.ops.topk_topp_sampler import apply_top_k_top_p_pytorch
-        from vllm.v1.sample.ops.topk_topp_triton import apply_top_k_top_p_triton
+    def sampler_rows():
+        # sampler at a decode batch of 256 over the Llama-3 vocabulary (fp32 logits, as vLLM's
+        # sampler holds them): the top-k/top-p mask (k = 50, p = 0.9 on every row) and the
+        # exponential-race sample.  The mask works in place, so each call first restores its
+        # logits from a pristine copy; the copy is timed alone and subtracted.  Algorithmic
+        # bytes: the logits read once and written once (mask); probs and q read once (sample).
+        B5, V5 = 256, 128256
+        src5 = torch.randn(B5, V5, device=dev, generator=g) * 2
+        lg5 = torch.empty_like(src5)
+        k5 = torch.full((B5,), 50, device=dev, dtype=torch.int32)
+        p5 = torch.full((B5,), 0.9, device=dev)
+        copy_us = time_graph([lambda: lg5.copy_(src5)], 10) * 1e3
+        name = "top_k_top_p f32 [256,128256] k=50 p=0.9"
+        us = time_graph([lambda: (lg5.copy_(src5), o.top_k_top_p(lg5, k5, p5))], 10) * 1e3 - copy_us
+        report(name, 2 * B5 * V5 * 4, us * 1e-3, {"note": "radix select, ~8 passes over each row (L2/HBM)"})
+        try:
+            from vllm.v1.sample.ops.topk_topp_sampler import apply_top_k_top_p_pytorch
+            from vllm.v1.sample.ops.topk_topp_triton import apply_top_k_top_p_triton
 
-        t_us = time_graph([lambda: (lg5.copy_(src5), apply_top_k_top_p_triton(lg5, k5, p5))], 10) * 1e3 - copy_us
-        res[name].update(lib="vllm apply_top_k_top_p_triton (vLLM's choice for batch >= 8)", lib_us=round(t_us, 2),
-                         ours_vs_lib=round(t_us / res[name]["us"], 3))
-        s_us = time_graph([lambda: (lg5.copy_(src5), apply_top_k_top_p_pytorch(lg5, k5, p5))], 3) * 1e3 - copy_us
-        res[name].update(sort_us=round(s_us, 2), ours_vs_sort=round(s_us / res[name]["us"], 3),
-                         sort="torch sort + cumsum + scatter (the reference's algorithm, on the GPU)")
-    except Exception as exc:  # noqa: BLE001 - the comparison columns are optional
-        res[name]["lib"] = f"unavailable ({type(exc).__name__}: {exc})"[:200]
-    del lg5
-    probs5 = src5.softmax(dim=-1)
-    q5 = torch.empty_like(probs5).exponential_(generator=g)
-    ids5 = torch.empty(B5, dtype=torch.int64, device=dev)
-    name = "random_sample f32 [256,128256]"
-    report(name, 2 * B5 * V5 * 4 + B5 * 8, time_graph([lambda: o.random_sample(ids5, probs5, q5)], 20))
-    lib(name, "torch div + argmax (the reference's random_sample after its draws)",
-        [lambda: probs5.div(q5).argmax(dim=-1)], 20)
-    del src5, probs5, q5
+            t_us = time_graph([lambda: (lg5.copy_(src5), apply_top_k_top_p_triton(lg5, k5, p5))], 10) * 1e3 - copy_us
+            res[name].update(lib="vllm apply_top_k_top_p_triton (vLLM's choice for batch >= 8)", lib_us=round(t_us, 2),
+                             ours_vs_lib=round(t_us / res[name]["us"], 3))
+            s_us = time_graph([lambda: (lg5.copy_(src5), apply_top_k_top_p_pytorch(lg5, k5, p5))], 3) * 1e3 - copy_us
+            res[name].update(sort_us=round(s_us, 2), ours_vs_sort=round(s_us / res[name]["us"], 3),
+                             sort="torch sort + cumsum + scatter (the reference's algorithm, on the GPU)")
+        except Exception as exc:  # noqa: BLE001 - the comparison columns are optional
+            res[name]["lib"] = f"unavailable ({type(exc).__name__}: {exc})"[:200]
+        del lg5
+        probs5 = src5.softmax(dim=-1)
+        q5 = torch.empty_like(probs5).exponential_(generator=g)
+        ids5 = torch.empty(B5, dtype=torch.int64, device=dev)
+        name = "random_sample f32 [256,128256]"
+        report(name, 2 * B5 * V5 * 4 + B5 * 8, time_graph([lambda: o.random_sample(ids5, probs5, q5)], 20))
+        lib(name, "torch div + argmax (the reference's random_sample after its draws)",
+            [lambda: probs5.div(q5).argmax(dim=-1)], 20)
+        del src5, probs5, q5
+
+    # rows added beside the headline kernels: a failure is recorded in the table, never
+    # fatal to the bench line
+    for label, rows in (("rope_and_cache", rope_cache_rows), ("sampler", sampler_rows)):
+        try:
+            rows()
+        except Exception as exc:  # noqa: BLE001
+            res[f"{label} (error)"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        torch.cuda.synchronize()
 
     # decode at the vLLM end-to-end shape: 256 sequences, ctx U[512, 640] (prompt 512 + up
     # to 128 generated), 32/8 heads, block 16: contexts that fit one chunk, so the split
