@@ -757,6 +757,62 @@ def run_linear_case(args) -> int:
     return 0
 
 
+def _time_calls(call, warmup: int, steps: int) -> float:
+    """Average device ms of `steps` back-to-back calls after `warmup` untimed ones."""
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_sampler_case(args) -> int:
+    """The top-k/top-p mask (k = 50, p = 0.9 on every row) of fp32 logits [B, V], warmup +
+    steps launches on one buffer, for profiling (prints its own timing).  The mask works in
+    place, so calls after the first see already-masked rows: time with the per-op table."""
+    from vllm_nt._ntops.torch._ext import ops
+
+    b, v = args.sampler_case
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    logits = torch.randn(b, v, device=dev, generator=g) * 2
+    k = torch.full((b,), 50, device=dev, dtype=torch.int32)
+    p = torch.full((b,), 0.9, device=dev)
+    o = ops()
+    ms = _time_calls(lambda: o.top_k_top_p(logits, k, p), args.warmup, args.steps)
+    print(json.dumps({"sampler_case": [b, v], "us": ms * 1e3}))
+    return 0
+
+
+def run_rope_cache_case(args) -> int:
+    """RoPE + KV store of T tokens of a Llama-3-8B qkv [T, 48*128] bf16 into a
+    FlashAttention cache [2, 8192, 16, 8, 128], warmup + steps launches, for profiling."""
+    from vllm_nt._ntops.torch._ext import ops
+    import oracle
+
+    t = args.rope_cache_case
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = torch.randn(t, 48 * HEAD, device=dev, generator=g, dtype=torch.bfloat16)
+    pos = torch.randint(0, 4096, (t,), device=dev, generator=g)
+    slots = torch.randperm(8192 * BLOCK, device=dev, generator=g)[:t]
+    kv = torch.zeros(2, 8192, BLOCK, HKV, HEAD, device=dev, dtype=torch.bfloat16)
+    cache = oracle.build_cos_sin_cache(HEAD, 4096, 10000.0).to(torch.bfloat16).to(dev)
+    q, k, v = qkv[:, : HQ * HEAD], qkv[:, HQ * HEAD : (HQ + HKV) * HEAD], qkv[:, (HQ + HKV) * HEAD :]
+    o = ops()
+    ms = _time_calls(lambda: o.rope_and_cache_flash_layout(pos, q, k, v, cache, kv, slots, HEAD, HEAD, 0),
+                     args.warmup, args.steps)
+    print(json.dumps({"rope_cache_case": t, "us": ms * 1e3}))
+    return 0
+
+
 def run_prefill_case(args) -> int:
     """NSEQ sequences of Q new tokens after CTX - Q cached ones (Llama-3-8B heads, paged
     cache), warmup + steps launches of the prefill kernel, for profiling."""
@@ -815,6 +871,10 @@ def main() -> int:
                     help="profiling: run only the GEMM out[M,N] = x[M,K] W[N,K]^T, warmup+steps times")
     ap.add_argument("--prefill-case", type=int, nargs=3, metavar=("Q", "CTX", "NSEQ"),
                     help="profiling: run only the paged prefill kernel, warmup+steps times")
+    ap.add_argument("--sampler-case", type=int, nargs=2, metavar=("B", "V"),
+                    help="profiling: run only the top-k/top-p mask over [B, V] logits, warmup+steps times")
+    ap.add_argument("--rope-cache-case", type=int, metavar="T",
+                    help="profiling: run only the fused RoPE + KV store over T tokens, warmup+steps times")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -824,6 +884,10 @@ def main() -> int:
         return run_linear_case(args)
     if args.prefill_case:
         return run_prefill_case(args)
+    if args.sampler_case:
+        return run_sampler_case(args)
+    if args.rope_cache_case:
+        return run_rope_cache_case(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
