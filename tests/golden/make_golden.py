@@ -18,7 +18,7 @@ Sources of truth per op:
   sample)                        loaded by file path from the read-only reference checkout (it
                                  imports only torch), and vLLM's apply_top_k_top_p_pytorch
 bf16 tensors are stored as their uint16 bit patterns (key suffix ``__bf16``).
-``--only sampler`` regenerates just the sampler fixture.
+``--only sampler`` / ``--only f16`` regenerate just the sampler / the fp16 fixtures.
 """
 
 from __future__ import annotations
@@ -159,6 +159,38 @@ def main() -> None:
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 
+def half_fixtures() -> None:
+    """fp16 counterparts of the RMS-norm, SiluAndMul and RoPE fixtures (vLLM's native code
+    on fp16 inputs), from their own generator so the other fixtures stay as they are."""
+    from vllm import ir
+    from vllm.model_executor.layers.activation import SiluAndMul
+    from vllm.model_executor.layers.rotary_embedding.base import RotaryEmbedding, RotaryEmbeddingBase
+
+    g = torch.Generator().manual_seed(20261203)
+    dtype = torch.float16
+    x = torch.randn(4, 512, generator=g).to(dtype)
+    r = torch.randn(4, 512, generator=g).to(dtype)
+    w = (1.0 + 0.1 * torch.randn(512, generator=g)).to(dtype)
+    y, res = ir.ops.fused_add_rms_norm(x.clone(), r.clone(), w, 1e-6)
+    y0 = ir.ops.rms_norm(x.clone(), w, 1e-6)
+    save("rms_norm_f16", x=x, residual=r, weight=w, out=y, residual_out=res, out_plain=y0)
+    xs = torch.randn(4, 2 * 256, generator=g).to(dtype)
+    save("silu_and_mul_f16", x=xs, out=SiluAndMul.forward_native(xs.clone()))
+    head, rot, max_pos, base = 64, 64, 128, 10000.0
+    cache = RotaryEmbeddingBase._compute_cos_sin_cache(
+        type("C", (), {"rotary_dim": rot, "base": base, "max_position_embeddings": max_pos,
+                       "_compute_inv_freq": lambda self, b: RotaryEmbeddingBase._compute_inv_freq(self, b)})()
+    )
+    pos = torch.randint(0, max_pos, (6,), generator=g)
+    q = torch.randn(6, 4 * head, generator=g).to(dtype)
+    k = torch.randn(6, 2 * head, generator=g).to(dtype)
+    qo, ko = RotaryEmbedding.forward_static(pos, q.clone(), k.clone(), head, rot, cache.to(dtype), True)
+    cache32 = torch.cat((cache[:, :16], cache[:, 32:48]), dim=-1)
+    qp, kp = RotaryEmbedding.forward_static(pos, q.clone(), k.clone(), head, 32, cache32.to(dtype), True)
+    save("rope_f16", positions=pos, query=q, key=k, cos_sin_cache=cache, query_out=qo, key_out=ko,
+         cos_sin_cache_rot32=cache32, query_out_rot32=qp, key_out_rot32=kp)
+
+
 REFERENCE_SAMPLER = Path("/root/reference/vllm_nt/_ntops/torch/sampler.py")
 
 
@@ -203,6 +235,9 @@ if __name__ == "__main__":
 
     if sys.argv[1:] == ["--only", "sampler"]:
         sampler_fixture()
+    elif sys.argv[1:] == ["--only", "f16"]:
+        half_fixtures()
     else:
         main()
+        half_fixtures()
         sampler_fixture()

@@ -13,7 +13,7 @@ import oracle
 from _util import bits_equal, golden, seeded
 
 
-@pytest.mark.parametrize("tag", ["f32", "bf16"])
+@pytest.mark.parametrize("tag", ["f32", "bf16", "f16"])
 def test_rms_norm_matches_vllm_native(tag):
     g = golden(f"rms_norm_{tag}")
     y, res = oracle.fused_add_rms_norm(g["x"], g["residual"], g["weight"], 1e-6)
@@ -22,7 +22,7 @@ def test_rms_norm_matches_vllm_native(tag):
     torch.testing.assert_close(oracle.rms_norm(g["x"], g["weight"], 1e-6), g["out_plain"], rtol=0, atol=0)
 
 
-@pytest.mark.parametrize("tag", ["f32", "bf16"])
+@pytest.mark.parametrize("tag", ["f32", "bf16", "f16"])
 def test_silu_and_mul_matches_vllm_native(tag):
     g = golden(f"silu_and_mul_{tag}")
     out = oracle.silu_and_mul(g["x"])
@@ -30,7 +30,7 @@ def test_silu_and_mul_matches_vllm_native(tag):
     torch.testing.assert_close(out, g["out"], rtol=tol, atol=tol)
 
 
-@pytest.mark.parametrize("tag", ["f32", "bf16"])
+@pytest.mark.parametrize("tag", ["f32", "bf16", "f16"])
 def test_rope_matches_vllm_forward_static(tag):
     g = golden(f"rope_{tag}")
     cache = oracle.build_cos_sin_cache(64, 128, 10000.0)
