@@ -104,8 +104,16 @@ def child(args) -> int:
     prompts = [TokensPrompt(prompt_token_ids=rng.integers(0, 128256, 512).tolist()) for _ in range(args.prompts)]
     warm = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True, detokenize=False)
     llm.generate(prompts[:16], warm, use_tqdm=False)
-    sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, min_tokens=args.output_len, ignore_eos=True,
-                        detokenize=False)
+    if args.sampling == "topkp":
+        # one seed per request: vLLM then samples through TopKTopPSampler.forward_native (its
+        # FlashInfer sampler takes no per-request generators), where the TopKTopP and
+        # RandomSample hooks sit
+        sp = [SamplingParams(temperature=0.8, top_k=50, top_p=0.9, seed=args.seed * 100003 + i,
+                             max_tokens=args.output_len, min_tokens=args.output_len, ignore_eos=True,
+                             detokenize=False) for i in range(len(prompts))]
+    else:
+        sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, min_tokens=args.output_len,
+                            ignore_eos=True, detokenize=False)
     t0 = time.perf_counter()
     outs = llm.generate(prompts, sp, use_tqdm=False)
     dt = time.perf_counter() - t0
@@ -113,6 +121,7 @@ def child(args) -> int:
     result = {
         "mode": args.mode,
         "tp": args.tp,
+        "sampling": args.sampling,
         "prompts": args.prompts,
         "output_tokens": generated,
         "seconds": dt,
@@ -158,7 +167,7 @@ def launch(args, base: Path, model_dir: Path, gpus: str, tp: int, log: Path) -> 
     env["PYTHONPATH"] = os.pathsep.join(paths + [env.get("PYTHONPATH", "")])
     cmd = [sys.executable, str(Path(__file__).resolve()), "--child", "--mode", args.mode, "--tp", str(tp),
            "--model-dir", str(model_dir), "--prompts", str(args.prompts), "--output-len", str(args.output_len),
-           "--seed", str(args.seed), "--attention-backend", args.attention_backend]
+           "--seed", str(args.seed), "--attention-backend", args.attention_backend, "--sampling", args.sampling]
     return subprocess.Popen(cmd, env=env, stdout=open(log, "w"), stderr=subprocess.STDOUT)
 
 
@@ -181,6 +190,8 @@ def main() -> int:
     ap.add_argument("--child", action="store_true")
     ap.add_argument("--model-dir")
     ap.add_argument("--attention-backend", default="FLASH_ATTN", choices=["FLASH_ATTN", "FLASHINFER"])
+    ap.add_argument("--sampling", default="greedy", choices=["greedy", "topkp"],
+                    help="greedy, or temperature 0.8 / top-k 50 / top-p 0.9 with a seed per request")
     args = ap.parse_args()
     if args.child:
         return child(args)
@@ -206,7 +217,8 @@ def main() -> int:
             return 1
         results.append(res)
     agg = {
-        "metric": "vLLM offline output tok/s (Llama-3-8B-shaped, 256x512 in, 128 greedy out)",
+        "metric": "vLLM offline output tok/s (Llama-3-8B-shaped, 256x512 in, 128 out, "
+                  + ("greedy)" if args.sampling == "greedy" else "top-k 50 / top-p 0.9, seeded per request)"),
         "mode": args.mode,
         "replicas": len(results) if args.tp == 1 else 1,
         "tp": args.tp,
