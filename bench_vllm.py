@@ -186,7 +186,7 @@ def main() -> int:
     ap.add_argument("--prompts", type=int, default=256)
     ap.add_argument("--output-len", type=int, default=128)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--log-dir", default="gpurun_out")
+    ap.add_argument("--log-dir", default="vllm_bench_logs", help="where each engine's log is written")
     ap.add_argument("--child", action="store_true")
     ap.add_argument("--model-dir")
     ap.add_argument("--attention-backend", default="FLASH_ATTN", choices=["FLASH_ATTN", "FLASHINFER"])
