@@ -58,6 +58,14 @@ def test_status_strings_and_version():
         ("ntb200_rope_and_cache", (1, 4, 1, None, 1, 1, 1, 1, 1, 4, 4, 4, 2, 1, 128, 128) + (128,) * 6 + (128, 64, 16, 64, 2048, 128, 128, 1, None), -1),
         ("ntb200_rope_and_cache", (1, 4, 1, 1, 1, 1, 1, 1, 1, 4, 4, 4, 2, 1, 128, 128) + (128,) * 6 + (128, 64, 16, 64, 2048, 128, 128, 7, None), -2),
         ("ntb200_embedding", (1, 1, 4, 1, 4, 10, 16, 8, 16, 2, None), -1),
+        # top_k_top_p: row stride below the vocabulary; a k dtype that is not an integer code
+        ("ntb200_top_k_top_p", (1, 4, 100, 99, 1, 4, None, None), -1),
+        ("ntb200_top_k_top_p", (1, 4, 100, 100, 1, 1, None, None), -2),
+        ("ntb200_top_k_top_p", (None, 4, 100, 100, 1, 4, None, None), -1),
+        # random_sample: empty vocabulary; q row stride below it; null output
+        ("ntb200_random_sample", (1, 1, 1, 4, 0, 8, 8, None), -1),
+        ("ntb200_random_sample", (1, 1, 1, 4, 8, 8, 7, None), -1),
+        ("ntb200_random_sample", (None, 1, 1, 4, 8, 8, 8, None), -1),
         ("ntb200_linear", (1, 1, 1, None, 4, 8, 16, 16, 16, 8, None, 0, 0, None), -2),
         ("ntb200_paged_attention_decode",
          (1, 1, 1, 1, 1, 1, 2, 4, 1, 64, 16, 8, 4, 4, 64, 0.1, 512, 128, 512, 128, 2048, 128, 128, None, 0, 1, None), -6),
@@ -78,6 +86,10 @@ def test_zero_sized_calls_are_no_ops():
     assert capi.call("ntb200_linear", 1, 1, 1, None, 0, 8, 16, 16, 16, 8, None, 0, 1, None) == 0
     assert capi.call("ntb200_rope_and_cache", 1, 4, 1, 1, 1, 1, 1, 1, 1, 4, 0, 0, 2, 1, 128, 128, *(128,) * 6,
                      128, 64, 16, 64, 2048, 128, 128, 1, None) == 0
+    # no rows, no filter: nothing to do (no device is touched)
+    assert capi.call("ntb200_top_k_top_p", 1, 0, 100, 100, 1, 4, None, None) == 0
+    assert capi.call("ntb200_top_k_top_p", 1, 4, 100, 100, None, 4, None, None) == 0
+    assert capi.call("ntb200_random_sample", 1, 1, 1, 0, 8, 8, 8, None) == 0
 
 
 def test_workspace_queries():
