@@ -15,8 +15,9 @@
 //
 // Passes over the row (each from L2 or HBM): max + first top-k digit, two more top-k
 // digits, the softmax normaliser Z, three weighted top-p digits (probability sums per bin
-// in shared memory, the bin search in fp64), then the masking write.  A row with neither
-// filter is left untouched.
+// in shared memory, the bin search in fp64), then the masking write.  Histogram updates
+// are run-length accumulated per thread (one shared atomic per run of equal bins).  A row
+// with neither filter is left untouched.
 //
 // Random sample (the reference's random_sample, sampler.py:34-42): out[b] =
 // argmax_i probs[b, i] / q[b, i] for the caller's exponential draws q, in one pass over
@@ -149,6 +150,39 @@ __device__ __forceinline__ void for_row(const float* row, int64_t vocab, F&& f) 
   }
 }
 
+// Per-thread run-length accumulation into the shared histograms: consecutive keys of a
+// thread that fall into the same bin cost one shared atomic per run instead of one per
+// key.  Rows whose logits are mostly one value (a vocabulary masked to -inf by a logits
+// processor, as guided decoding does) would otherwise serialise every thread of the CTA
+// on a single shared-memory address.
+struct BinRun {
+  uint32_t bin = 0xFFFFFFFFu, n = 0;
+  float w = 0.f;
+  __device__ __forceinline__ void add(SamplerSmem& s, uint32_t b) {
+    if (b != bin) {
+      flush(s, false);
+      bin = b;
+    }
+    ++n;
+  }
+  __device__ __forceinline__ void add(SamplerSmem& s, uint32_t b, float weight) {
+    if (b != bin) {
+      flush(s, true);
+      bin = b;
+    }
+    ++n;
+    w += weight;
+  }
+  __device__ __forceinline__ void flush(SamplerSmem& s, bool weighted) {
+    if (n > 0) {
+      atomicAdd(&s.count[bin], n);
+      if (weighted) atomicAdd(&s.weight[bin], w);
+    }
+    n = 0;
+    w = 0.f;
+  }
+};
+
 // Top-k selection over s.count: the bin holding the `remaining`-th largest key among the
 // keys that match the prefix.  Updates remaining (keys ranked above that bin removed).
 __device__ __forceinline__ uint32_t select_from_top(SamplerSmem& s, uint32_t& remaining) {
@@ -225,10 +259,14 @@ __global__ void __launch_bounds__(kThreads, 1) top_k_top_p_kernel(
 
   // pass 1: row max (always) and the first top-k digit
   float m = -INFINITY;
-  for_row<VEC>(row, vocab, [&](float x) {
-    m = fmaxf(m, x);
-    if (filter_k) atomicAdd(&s.count[ordered_key(x) >> 21], 1u);
-  });
+  {
+    BinRun run;
+    for_row<VEC>(row, vocab, [&](float x) {
+      m = fmaxf(m, x);
+      if (filter_k) run.add(s, ordered_key(x) >> 21);
+    });
+    run.flush(s, false);
+  }
   m = block_max(m, s.warp_f);
 
   // top-k: three digits; every logit >= t_k survives
@@ -241,10 +279,12 @@ __global__ void __launch_bounds__(kThreads, 1) top_k_top_p_kernel(
         __syncthreads();
         const uint32_t pm = prefix_mask(d), dm = digit_mask(d);
         const int sh = digit_shift(d);
+        BinRun run;
         for_row<VEC>(row, vocab, [&](float x) {
           const uint32_t u = ordered_key(x);
-          if ((u & pm) == prefix) atomicAdd(&s.count[(u >> sh) & dm], 1u);
+          if ((u & pm) == prefix) run.add(s, (u >> sh) & dm);
         });
+        run.flush(s, false);
         __syncthreads();
       } else {
         __syncthreads();
@@ -280,14 +320,12 @@ __global__ void __launch_bounds__(kThreads, 1) top_k_top_p_kernel(
       __syncthreads();
       const uint32_t pm = prefix_mask(d), dm = digit_mask(d);
       const int sh = digit_shift(d);
+      BinRun run;
       for_row<VEC>(row, vocab, [&](float x) {
         const uint32_t u = ordered_key(x);
-        if (x >= t_k && (u & pm) == prefix) {
-          const int bin = (u >> sh) & dm;
-          atomicAdd(&s.count[bin], 1u);
-          atomicAdd(&s.weight[bin], __fdiv_rn(expf(x - m), zf));
-        }
+        if (x >= t_k && (u & pm) == prefix) run.add(s, (u >> sh) & dm, __fdiv_rn(expf(x - m), zf));
       });
+      run.flush(s, true);
       __syncthreads();
       prefix |= select_from_bottom(s, base, target) << sh;
     }
