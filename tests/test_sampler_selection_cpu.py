@@ -100,3 +100,19 @@ def test_rule_matches_the_sort_based_mask_on_full_vocabulary_rows(seed):
         running = oracle.top_p_cumulative(logits, k)
         assert float((running - (1 - p.double()).unsqueeze(1)).abs()[diff].max()) < 2e-4
     assert torch.equal(radix_mask(logits, k, None), oracle.apply_top_k_top_p(logits, k, None))
+
+
+def test_tie_run_straddling_the_top_p_cut_is_kept_whole():
+    """The one designed difference from the reference: 100 equal logits whose running mass
+    crosses 1 - p.  The reference keeps the part of the run its sort puts last; the radix
+    rule, which compares values, keeps every member of the run (a superset: nothing the
+    reference keeps is dropped)."""
+    logits = torch.full((1, 200), -2.0)
+    logits[0, 100:] = 0.5  # the run: 100 copies, holding nearly all of the mass
+    p = torch.tensor([0.5])
+    got = radix_mask(logits, None, p)
+    ref = oracle.apply_top_k_top_p(logits, None, p)
+    kept_got, kept_ref = got != float("-inf"), ref != float("-inf")
+    assert int(kept_got.sum()) == 100 and bool(kept_got[0, 100:].all())
+    assert 0 < int(kept_ref.sum()) < 100
+    assert not (kept_ref & ~kept_got).any()
