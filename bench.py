@@ -223,13 +223,13 @@ def run_reference(args) -> int:
 
 def workload_config(n: int) -> dict:
     return {
-        "workload": "paged-attn decode: 256 seqs x 1 token, 32 q / 8 kv heads, head 128, block 16, "
-        "ctx U[512,8192], distinct ids from a 150000-block pool, bf16 (fp32 softmax)",
+        "workload": "paged decode 256 seqs x 1 tok, 32q/8kv heads, d128, block 16, ctx U[512,8192], "
+        "150000-block pool, bf16",
         "global_batch": BATCH,
         "seq_len": "U[512,8192]",
         "parallelism": f"kv-head shard x{n}" if n > 1 else "single GPU",
         "kv_heads_per_gpu": HKV // n,
-        "l2": "inputs larger than L2 (K/V working set per step >= 570 MB per GPU)",
+        "l2": "inputs > L2 (>=570 MB K/V per step per GPU)",
     }
 
 
@@ -292,6 +292,11 @@ def per_op_table(dev, peaks) -> dict:
     except Exception:  # noqa: BLE001 - the comparison column is optional
         vops = None
 
+    def floor(name, fn):
+        """The same kernel on a single-row input: what one launch costs with no data to
+        move (CUDA graph of back-to-back launches)."""
+        res[name]["floor_us"] = round(time_graph([fn], 40) * 1e3, 2)
+
     def lib(name, label, fns, iters):
         if fns is None:
             return
@@ -314,6 +319,7 @@ def per_op_table(dev, peaks) -> dict:
     outs = [torch.empty(M, H, device=dev) for _ in range(r)]
     fns = [lambda i=i: o.fused_add_rms_norm(outs[i], rs[i], xs[i], w, 1e-6) for i in range(r)]
     report("fused_add_rms_norm f32 [128,4096]", nb, time_graph(fns, 20 * r))
+    floor("fused_add_rms_norm f32 [128,4096]", lambda: o.fused_add_rms_norm(outs[0][:1], rs[0][:1], xs[0][:1], w, 1e-6))
     lib("fused_add_rms_norm f32 [128,4096]", "vllm _C.fused_add_rms_norm (in place)",
         vops and [lambda i=i: vops.fused_add_rms_norm(xs[i], rs[i], w, 1e-6) for i in range(r)], 20 * r)
     # bf16 M-sweep point at a size where launch latency no longer dominates
@@ -337,6 +343,7 @@ def per_op_table(dev, peaks) -> dict:
     outs = [torch.empty(128, 11008, device=dev) for _ in range(r)]
     fns = [lambda i=i: o.silu_and_mul(outs[i], xs[i]) for i in range(r)]
     report("silu_and_mul f32 [128,22016]", nb, time_graph(fns, 20 * r))
+    floor("silu_and_mul f32 [128,22016]", lambda: o.silu_and_mul(outs[0][:1], xs[0][:1]))
     lib("silu_and_mul f32 [128,22016]", "vllm _C.silu_and_mul",
         vops and [lambda i=i: torch.ops._C.silu_and_mul(outs[i], xs[i]) for i in range(r)], 20 * r)
     del xs, outs
@@ -353,6 +360,8 @@ def per_op_table(dev, peaks) -> dict:
     cache = oracle.build_cos_sin_cache(128, 4096, 10000.0).to(dev)
     fns = [lambda i=i: o.rotary_embedding_neox(pos[i], qs[i], ks[i], cache, 128, 128) for i in range(r)]
     report("rope_neox f32 q[128,32,128] k[128,8,128]", nb, time_graph(fns, 20 * r))
+    floor("rope_neox f32 q[128,32,128] k[128,8,128]",
+          lambda: o.rotary_embedding_neox(pos[0][:1], qs[0][:1], ks[0][:1], cache, 128, 128))
     lib("rope_neox f32 q[128,32,128] k[128,8,128]", "vllm _C.rotary_embedding (neox)",
         vops and [lambda i=i: vops.rotary_embedding(pos[i], qs[i], ks[i], 128, cache, True) for i in range(r)],
         20 * r)
@@ -369,6 +378,7 @@ def per_op_table(dev, peaks) -> dict:
     slots = [torch.randperm(8192 * 16, device=dev, generator=g)[:N] for _ in range(r)]
     fns = [lambda i=i: o.reshape_and_cache(keys[i], vals[i], kc, vc, slots[i]) for i in range(r)]
     report("reshape_and_cache bf16 4096x8x128", nb, time_graph(fns, 20 * r))
+    floor("reshape_and_cache bf16 4096x8x128", lambda: o.reshape_and_cache(keys[0][:1], vals[0][:1], kc, vc, slots[0][:1]))
     one = torch.ones((), device=dev)
     lib("reshape_and_cache bf16 4096x8x128", "vllm _C_cache_ops.reshape_and_cache_flash",
         vops and [lambda i=i: vops.reshape_and_cache_flash(keys[i], vals[i], kc, vc, slots[i], "auto", one, one)
@@ -614,6 +624,81 @@ def per_op_table(dev, peaks) -> dict:
     return res
 
 
+def _sig3(x):
+    """x to three significant figures (ints stay ints)."""
+    if x is None or isinstance(x, str):
+        return x
+    if x == 0:
+        return 0
+    r = float(f"{x:.3g}")
+    return int(r) if r == int(r) and abs(r) >= 100 else r
+
+
+# short row names of the compact per-op table, in print order: GEMMs and attention first,
+# the memory-bound ops last (the end of the line is what a truncated log keeps)
+_SHORT = {
+    **{f"linear {t} M={m}": f"{t} {m}" for t in ("qkv", "o_proj", "gate_up", "down")
+       for m in (1, 16, 128, 256, 1024, 8192)},
+    **{f"lm_head+argmax V=128256 M={m}": f"lmhead+argmax {m}" for m in (1, 16, 128, 256)},
+    "paged prefill bf16 32 x 512 tokens (causal)": "prefill 32x512",
+    "paged prefill bf16 8 x 512 new after 1536 cached": "prefill 8x512@1536",
+    "paged decode bf16 B=256 ctx U[512,640] (vLLM e2e shape)": "decode ctx512-640",
+    "top_k_top_p f32 [256,128256] k=50 p=0.9": "topk_topp 256x128256",
+    "random_sample f32 [256,128256]": "sample 256x128256",
+    "rope_and_cache bf16 256 tokens of qkv [T,48*128]": "rope+kv 256",
+    "rope_and_cache bf16 16384 tokens of qkv [T,48*128]": "rope+kv 16384",
+    "embedding bf16 4096 ids x 4096": "embed 4096",
+    "silu_and_mul bf16 [2048,28672]": "silu bf16 2048x28672",
+    "rope_neox bf16 16384 tokens of qkv [T,48*128]": "rope bf16 16384",
+    "reshape_and_cache bf16 16384x8x128": "kv 16384",
+    "fused_add_rms_norm bf16 [8192,4096]": "rms bf16 8192x4096",
+    "fused_add_rms_norm f32 [128,4096]": "rms f32 cfg(a)",
+    "silu_and_mul f32 [128,22016]": "silu f32 cfg(b)",
+    "rope_neox f32 q[128,32,128] k[128,8,128]": "rope f32 cfg(c)",
+    "reshape_and_cache bf16 4096x8x128": "kv cfg 4096",
+}
+
+
+def compact_ops(res: dict) -> dict:
+    """The per-op table as short rows [rate, frac, x_lib, floor_us]: rate is GB/s
+    (HBM-bound rows) or TFLOP/s (tensor-bound rows), frac its fraction of the measured
+    peak, x_lib vLLM's kernel time / ours (>1: ours faster), floor_us the same kernel's
+    time on a single-row input (its launch floor), where measured.  Microseconds per call
+    are in the full table (stderr)."""
+    out = {"cols": "GB/s|TF/s,frac,x_lib,floor_us"}
+    order = list(_SHORT) + [k for k in res if k not in _SHORT]
+    for name in order:
+        d = res.get(name)
+        if d is None:
+            continue
+        if "error" in d:
+            out[_SHORT.get(name, name)] = d["error"][:80]
+            continue
+        if "frac_of_hbm" in d:
+            row = [d["GB/s"], d["frac_of_hbm"]]
+        else:
+            row = [d.get("TFLOP/s"), d.get("frac_of_bf16")]
+        row.append(d.get("ours_vs_lib"))
+        if "floor_us" in d:
+            row.append(d["floor_us"])
+        while row and row[-1] is None:
+            row.pop()
+        out[_SHORT.get(name, name)] = [_sig3(v) for v in row]
+    return out
+
+
+def compact_tp(res: dict) -> dict:
+    """The row-parallel table as short rows of microseconds per call."""
+    cols = ("gemm_us", "allreduce_us", "serial_us", "peer_gemm_allreduce_us")
+    out = {"cols": "gemm,nccl_ar,gemm+nccl,gemm+peer_ar (us)"}
+    for name, d in res.items():
+        if name.startswith("_"):
+            out[name] = d
+            continue
+        out[name] = [_sig3(d.get(c)) for c in cols]
+    return out
+
+
 def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
     """Row-parallel projections (o_proj K=4096, down K=14336; N=4096) on n ranks: each rank
     multiplies its K-shard and the partial outputs are summed across ranks.  Times (max
@@ -813,6 +898,92 @@ def run_rope_cache_case(args) -> int:
     return 0
 
 
+OP_CASES = ("rms_f32", "rms_bf16", "silu_f32", "silu_bf16", "rope_f32", "rope_bf16", "kv_store", "kv_store_16k",
+            "embedding", "random_sample")
+
+
+def op_case_calls(name: str, dev, g) -> tuple[int, list]:
+    """(algorithmic bytes per call, calls over rotating input sets) for one memory-bound op
+    at its benchmark size: rms_f32 / silu_f32 / rope_f32 are the fp32 decoder configs
+    (x, r [128, 4096]; [128, 22016] -> [128, 11008]; q [128, 32, 128], k [128, 8, 128]),
+    kv_store the bf16 4096 x 8 x 128 store into [8192, 16, 8, 128] caches; rms_bf16 /
+    silu_bf16 / rope_bf16 / kv_store_16k / embedding are the prefill-sized points
+    ([8192, 4096]; [2048, 28672]; 16384 tokens of a [T, 48*128] qkv; 16384 tokens; 4096
+    ids into a [128256, 4096] table); random_sample is [256, 128256] fp32."""
+    from vllm_nt._ntops.torch._ext import ops
+    import oracle
+
+    o = ops()
+    bf = torch.bfloat16
+
+    def sets(nbytes):
+        return max(2, math.ceil(3 * L2_BYTES / nbytes))
+
+    if name in ("rms_f32", "rms_bf16"):
+        m, dt = (128, torch.float32) if name == "rms_f32" else (8192, bf)
+        es = 4 if dt == torch.float32 else 2
+        nb = 4 * m * 4096 * es + 4096 * es
+        r = sets(nb)
+        xs = [torch.randn(m, 4096, device=dev, generator=g).to(dt) for _ in range(r)]
+        rs = [torch.randn(m, 4096, device=dev, generator=g).to(dt) for _ in range(r)]
+        w = (1 + 0.1 * torch.randn(4096, device=dev, generator=g)).to(dt)
+        outs = [torch.empty_like(xs[0]) for _ in range(r)]
+        return nb, [lambda i=i: o.fused_add_rms_norm(outs[i], rs[i], xs[i], w, 1e-6) for i in range(r)]
+    if name in ("silu_f32", "silu_bf16"):
+        m, d, dt = (128, 11008, torch.float32) if name == "silu_f32" else (2048, 14336, bf)
+        es = 4 if dt == torch.float32 else 2
+        nb = 3 * m * d * es
+        r = sets(nb)
+        xs = [torch.randn(m, 2 * d, device=dev, generator=g).to(dt) for _ in range(r)]
+        outs = [torch.empty(m, d, device=dev, dtype=dt) for _ in range(r)]
+        return nb, [lambda i=i: o.silu_and_mul(outs[i], xs[i]) for i in range(r)]
+    if name in ("rope_f32", "rope_bf16"):
+        t, dt, base = (128, torch.float32, 10000.0) if name == "rope_f32" else (16384, bf, 500000.0)
+        es = 4 if dt == torch.float32 else 2
+        nb = 2 * t * 40 * 128 * es + t * 128 * es + t * 8
+        r = sets(nb)
+        qkv = [torch.randn(t, 48 * 128, device=dev, generator=g).to(dt) for _ in range(r)]
+        pos = [torch.randint(0, 4096, (t,), device=dev, generator=g) for _ in range(r)]
+        cache = oracle.build_cos_sin_cache(128, 4096, base).to(dt).to(dev)
+        return nb, [lambda i=i: o.rotary_embedding_neox(pos[i], qkv[i][:, :4096], qkv[i][:, 4096:5120], cache, 128, 128)
+                    for i in range(r)]
+    if name in ("kv_store", "kv_store_16k"):
+        n = 4096 if name == "kv_store" else 16384
+        nb = 2 * n * 8 * 128 * 2 * 2 + n * 8
+        r = sets(nb)
+        kc = torch.zeros(8192, 16, 8, 128, device=dev, dtype=bf)
+        vc = torch.zeros_like(kc)
+        keys = [torch.randn(n, 8, 128, device=dev, generator=g).to(bf) for _ in range(r)]
+        vals = [torch.randn(n, 8, 128, device=dev, generator=g).to(bf) for _ in range(r)]
+        slots = [torch.randperm(8192 * 16, device=dev, generator=g)[:n] for _ in range(r)]
+        return nb, [lambda i=i: o.reshape_and_cache(keys[i], vals[i], kc, vc, slots[i]) for i in range(r)]
+    if name == "embedding":
+        wt = torch.randn(128256, 4096, device=dev, generator=g).to(bf)
+        ids = [torch.randint(0, 128256, (4096,), device=dev, generator=g) for _ in range(8)]
+        outs = [torch.empty(4096, 4096, device=dev, dtype=bf) for _ in range(8)]
+        return 2 * 4096 * 4096 * 2 + 4096 * 8, [lambda i=i: o.embedding(outs[i], ids[i], wt) for i in range(8)]
+    if name == "random_sample":
+        probs = torch.randn(256, 128256, device=dev, generator=g).softmax(dim=-1)
+        q = torch.empty_like(probs).exponential_(generator=g)
+        ids = torch.empty(256, dtype=torch.int64, device=dev)
+        return 2 * 256 * 128256 * 4 + 256 * 8, [lambda: o.random_sample(ids, probs, q)]
+    raise SystemExit(f"--op-case: unknown op {name!r} (one of {', '.join(OP_CASES)})")
+
+
+def run_op_case(args) -> int:
+    """One memory-bound op at its benchmark size, warmup + steps launches rotating over
+    input sets larger than L2, for profiling (prints its own timing)."""
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    nb, calls = op_case_calls(args.op_case, dev, g)
+    i = iter(itertools.cycle(calls))
+    ms = _time_calls(lambda: next(i)(), args.warmup, args.steps)
+    gbs = nb / (ms * 1e-3) / 1e9
+    print(json.dumps({"op_case": args.op_case, "bytes": nb, "us": round(ms * 1e3, 2), "GB/s": round(gbs, 1)}))
+    return 0
+
+
 def run_prefill_case(args) -> int:
     """NSEQ sequences of Q new tokens after CTX - Q cached ones (Llama-3-8B heads, paged
     cache), warmup + steps launches of the prefill kernel, for profiling."""
@@ -875,6 +1046,8 @@ def main() -> int:
                     help="profiling: run only the top-k/top-p mask over [B, V] logits, warmup+steps times")
     ap.add_argument("--rope-cache-case", type=int, metavar="T",
                     help="profiling: run only the fused RoPE + KV store over T tokens, warmup+steps times")
+    ap.add_argument("--op-case", choices=OP_CASES,
+                    help="profiling: run only one memory-bound op at its benchmark size, warmup+steps times")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -888,6 +1061,8 @@ def main() -> int:
         return run_sampler_case(args)
     if args.rope_cache_case:
         return run_rope_cache_case(args)
+    if args.op_case:
+        return run_op_case(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -963,9 +1138,8 @@ def main() -> int:
         "unit": "GB/s",
         "frac": round(achieved / peaks["hbm_gbs"], 3),
         "traffic": traffic * (hkv / HKV) if traffic is not None else None,
-        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+        "peak_source": "measured hbm_gbs" if peak_kind == "measured" else "fallback 6.65 TB/s",
         "algorithmic_bytes_per_launch": algo,
-        "note": "decode call = split kernel + combine kernel, timed together with CUDA events",
     }
 
     # e2e: the plugin's public decode entry point with host buffers
@@ -1001,12 +1175,12 @@ def main() -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e = None if not e2e_steps else {
-        "value": batch * e2e_steps / (e2e_ms * 1e-3),
+        "value": round(batch * e2e_steps / (e2e_ms * 1e-3), 1),
         "unit": "tok/s",
         "h2d_bytes_per_step": q_host.numel() * 2 + s_host.numel() * 4 + t_host.numel() * 4,
         "d2h_bytes_per_step": o_host.numel() * 2,
         "steps": e2e_steps,
-        "path": "vllm_nt.oot.paged_attention_decode (pinned host in/out)",
+        "path": "oot.paged_attention_decode, pinned host in/out",
     }
 
     per_op = None
@@ -1027,7 +1201,7 @@ def main() -> int:
         per_call = max(1, min(BATCH, int(4.0 * t_one)))
         calls = max(1, min(64, int(15.0 / max(per_call / t_one, 1e-3))))
         v, threads, sample = oracle_decode_rate(ctx, q_all, per_call, calls)
-        cpu = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
+        cpu = {"value": round(v, 2), "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
 
     if dist:
         dist.barrier()
@@ -1036,12 +1210,12 @@ def main() -> int:
         return 0
     line = {
         "metric": METRIC,
-        "value": value,
+        "value": round(value, 1),
         "unit": "tok/s",
         "n_gpus": n,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": ms_per_step,
+        "ms_per_step": round(ms_per_step, 5),
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
@@ -1054,10 +1228,16 @@ def main() -> int:
         "e2e": e2e,
         "gpu_launches": 2 * args.steps,  # split + combine per timed step
         "clocks": clocks,
-        "per_op": per_op,
-        "tp_projection": tp_table,
     }
-    print(json.dumps(line), flush=True)
+    # the full tables go to stderr; the line carries their compact form, so that the whole
+    # line stays within a few thousand characters
+    if per_op is not None:
+        print("per_op " + json.dumps(per_op), file=sys.stderr, flush=True)
+        line["ops"] = compact_ops(per_op)
+    if tp_table is not None:
+        print("tp_projection " + json.dumps(tp_table), file=sys.stderr, flush=True)
+        line["tp"] = compact_tp(tp_table)
+    print(json.dumps(line, separators=(",", ":")), flush=True)
     return 0
 
 

@@ -6,8 +6,9 @@
  * cudaStream_t passed as void*), never synchronises the host, never allocates, and
  * returns NTB200_OK (0) or a negative NTB200_ERR_* status.  The caller owns all memory;
  * the only scratch an op needs (split-K partials of the paged decode) is passed in as
- * `workspace` and sized by the matching *_workspace_size() query.  Nothing here holds a
- * lock: the per-thread error message is thread-local.
+ * `workspace` and sized by the matching *_workspace_size() query.  No lock is taken on a
+ * launch path beyond one-time per-device set-ups (error word, SM count, shared-memory limits,
+ * the no-allocation decode's scratch address); the per-thread error message is thread-local.
  *
  * Each function names the reference (vllm_nt) interface it replaces.  Citations are
  * paths inside the vllm_nt project.
@@ -75,6 +76,25 @@ int ntb200_fused_add_rms_norm(void* out, void* residual, const void* x, const vo
                               int64_t num_rows, int64_t hidden, int64_t x_row_stride,
                               int64_t residual_row_stride, int64_t out_row_stride, float eps,
                               int dtype, void* stream);
+
+/* Gemma RMS norm:  out = round(x * rsqrt(mean(x^2) + eps) * (1 + weight))  with (1 + weight)
+ * formed in fp32 and one rounding (of the product), as vLLM's GemmaRMSNorm.forward_native
+ * (vllm/model_executor/layers/layernorm.py:153-170) computes it.  weight is the raw Gemma
+ * parameter w (not 1 + w) and must not be NULL.
+ * Replaces vllm_nt/_ntops/oot_support.py:32-48 (norm with gemma=True), which vllm_nt's
+ * GemmaRMSNorm hook reaches from vllm_nt/_ntops/patching.py:259-288. */
+int ntb200_gemma_rms_norm(void* out, const void* x, const void* weight, int64_t num_rows,
+                          int64_t hidden, int64_t x_row_stride, int64_t out_row_stride, float eps,
+                          int dtype, void* stream);
+
+/* Gemma residual add + RMS norm:  s = x + residual in the input dtype (a bf16 sum is rounded
+ * to bf16 before the statistics);  residual <- s;  out as ntb200_gemma_rms_norm(s).  F32 and
+ * BF16 only: vLLM returns an fp32 residual for fp16 inputs, which the in-place fp16 residual
+ * cannot hold (NTB200_ERR_UNSUPPORTED_DTYPE).  out may alias x. */
+int ntb200_gemma_fused_add_rms_norm(void* out, void* residual, const void* x, const void* weight,
+                                    int64_t num_rows, int64_t hidden, int64_t x_row_stride,
+                                    int64_t residual_row_stride, int64_t out_row_stride, float eps,
+                                    int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * out[r, i] = silu(x[r, i]) * x[r, d + i],  i < d.
@@ -193,12 +213,14 @@ int ntb200_paged_attention_decode(
  * memory at the call: a serving loop that must not call cudaMalloc/cudaFree while decoding
  * (they can synchronise the device and take a process-wide lock), code being recorded
  * into a CUDA graph, or a host that binds only this C ABI and has no device allocator.
- * The split-K partials go to a fixed 64 MiB array compiled into the library, held by every
- * GPU on which this entry point is set up until the process exits.  A call that needs more
- * scratch than that returns NTB200_ERR_WORKSPACE without launching.  The first call on a
- * device resolves the array's address (cudaGetSymbolAddress), so make it before any stream
- * capture.  All calls on a device share the array: calls that overlap on the GPU race;
- * order them on one stream.  Arguments as ntb200_paged_attention_decode minus the
+ * The split-K partials go to a fixed 64 MiB array compiled into the library, which a GPU
+ * holds until the process exits once the library's device code is loaded on it (under the
+ * default lazy module loading: on first use; with CUDA_MODULE_LOADING=EAGER: on every GPU
+ * whose context loads the library).  A call that needs more scratch than that returns
+ * NTB200_ERR_WORKSPACE without launching.  The first successful call on a device resolves
+ * the array's address (cudaGetSymbolAddress), so make it before any stream capture; a
+ * failed lookup is not remembered, and the next call retries it.  All calls on a device
+ * share the array: calls that overlap on the GPU race; order them on one stream.  Arguments as ntb200_paged_attention_decode minus the
  * workspace.  This entry point has no counterpart in the reference. */
 int ntb200_paged_attention_decode_noalloc(
     void* out, const void* query, const void* key_cache, const void* value_cache,

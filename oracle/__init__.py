@@ -10,7 +10,9 @@ the plugin patches; other paths are inside the vllm_nt reference project):
 
 * floating-point ops follow vLLM's torch-native implementations -- the oracle named for
   parity -- with the same fp32 intermediates and the same rounding points to the storage
-  dtype;
+  dtype (GemmaRMSNorm included: (1 + w) in fp32, one rounding of the product);
+* the LM head's greedy token is the first index of the largest bf16-rounded logit of the
+  fp32 projection (F.linear, then torch.argmax, as vLLM's greedy sampler takes it);
 * the KV-cache store and the embedding gather are byte copies (numpy on raw 16-bit views),
   exact; RoPE fused with the KV store is the two restatements composed in vLLM's order;
 * paged decode follows the reference's own test oracle (gather the cached tokens through
@@ -34,7 +36,9 @@ from oracle.ops import (  # noqa: F401
     embedding,
     fused_add_rms_norm,
     gather_paged_kv,
+    gemma_rms_norm,
     linear,
+    linear_argmax,
     paged_decode,
     paged_prefill,
     random_sample_from_draws,

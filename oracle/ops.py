@@ -50,6 +50,26 @@ def fused_add_rms_norm(
     return y.to(dtype), new_residual
 
 
+def gemma_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+                   residual: torch.Tensor | None = None):
+    """GemmaRMSNorm.forward_native (vllm:model_executor/layers/layernorm.py:153-170):
+    w1 = weight.float() + 1 (fp32); with a residual s = x + residual in x's dtype (fp16 sums
+    in fp32 and keeps an fp32 residual); out = x_f32 * rsqrt(mean(x_f32^2) + eps) * w1,
+    rounded once to x's dtype.  Returns out, or (out, s)."""
+    dtype = x.dtype
+    w1 = weight.to(torch.float32) + 1.0
+    if residual is not None:
+        if dtype == torch.float16:
+            x = x.to(torch.float32) + residual.to(torch.float32)
+        else:
+            x = (x.to(torch.float32) + residual.to(torch.float32)).to(dtype)
+        residual = x
+    xf = x.to(torch.float32)
+    var = xf.pow(2).mean(dim=-1, keepdim=True)
+    out = (xf * torch.rsqrt(var + eps) * w1).to(dtype)
+    return out if residual is None else (out, residual)
+
+
 # --------------------------------------------------------------------------------------
 # SiluAndMul  (vllm:model_executor/layers/activation.py:137-141;
 #              vllm_nt/_ntops/oot_support.py:51-56, vllm_nt/_ntops/kernels/silu.py:9-18)
@@ -359,3 +379,12 @@ def top_p_cumulative(logits: torch.Tensor, k: torch.Tensor | None) -> torch.Tens
     ordered, order = masked.double().sort(dim=-1)
     running = ordered.softmax(dim=-1).cumsum(dim=-1)
     return torch.empty_like(running).scatter(-1, order, running)
+
+
+def linear_argmax(x: torch.Tensor, weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Greedy token of an LM head: argmax over the vocabulary of the logits rounded to x's
+    dtype (vLLM's compute_logits writes them in the model dtype; its greedy sampler takes
+    torch.argmax, which returns the first index among equal maxima).  Returns
+    (token ids, the fp32 logits) -- the logits let a caller bound a disagreement."""
+    logits = linear(x, weight)
+    return torch.argmax(logits.to(x.dtype), dim=-1), logits

@@ -1,10 +1,12 @@
 """Generates tests/golden/*.npz: small seeded inputs and the outputs of the REAL reference
 implementations, used to pin the CPU oracle (oracle/ops.py).
 
-Run here (CPU, vLLM 0.22 importable):  python tests/golden/make_golden.py
+Run on a CPU machine with vLLM 0.22 importable and a checkout of the reference:
+    python tests/golden/make_golden.py --reference <vllm-nt checkout> [--only main|f16|gemma|sampler]
 
 Sources of truth per op:
   rms_norm / fused_add_rms_norm  vllm.ir.ops.rms_norm / fused_add_rms_norm (native)
+  gemma_rms_norm                 vllm GemmaRMSNorm.forward_native (with and without a residual)
   silu_and_mul                   vllm SiluAndMul.forward_native
   rope (NeoX)                    vllm RotaryEmbedding.forward_static with the cache of
                                  RotaryEmbeddingBase._compute_cos_sin_cache
@@ -26,6 +28,7 @@ from __future__ import annotations
 import itertools
 import math
 from pathlib import Path
+from types import SimpleNamespace
 
 import numpy as np
 import torch
@@ -191,7 +194,41 @@ def half_fixtures() -> None:
          cos_sin_cache_rot32=cache32, query_out_rot32=qp, key_out_rot32=kp)
 
 
-REFERENCE_SAMPLER = Path("/root/reference/vllm_nt/_ntops/torch/sampler.py")
+def gemma_fixture() -> None:
+    """GemmaRMSNorm.forward_native (vLLM) in fp32, bf16 and fp16, with and without a
+    residual: (1 + w) in fp32, the product rounded once, the bf16 residual sum rounded to
+    bf16 before the statistics, the fp16 residual sum kept in fp32."""
+    from vllm.model_executor.layers.layernorm import GemmaRMSNorm
+
+    g = torch.Generator().manual_seed(20261204)
+    arrays = {}
+    for dtype, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16"), (torch.float16, "f16")):
+        # forward_native reads only weight and variance_epsilon off the layer (constructing
+        # a CustomOp needs a vLLM config)
+        layer = SimpleNamespace(weight=torch.nn.Parameter((0.3 * torch.randn(512, generator=g)).to(dtype)),
+                                variance_epsilon=1e-6)
+        x = torch.randn(5, 512, generator=g).to(dtype)
+        r = torch.randn(5, 512, generator=g).to(dtype)
+        out_plain = GemmaRMSNorm.forward_native(layer, x.clone())
+        out, res = GemmaRMSNorm.forward_native(layer, x.clone(), r.clone())
+        arrays.update({f"{tag}_x": x, f"{tag}_residual": r, f"{tag}_weight": layer.weight.data, f"{tag}_out_plain": out_plain,
+                       f"{tag}_out": out, f"{tag}_residual_out": res})
+    save("gemma_rms_norm", **arrays)
+
+
+def _reference_sampler_path() -> Path:
+    """The reference's torch sampler module: ``--reference DIR`` (a vllm-nt checkout) or
+    the VLLM_NT_REFERENCE environment variable."""
+    import os
+    import sys
+
+    root = None
+    if "--reference" in sys.argv:
+        root = sys.argv[sys.argv.index("--reference") + 1]
+    root = root or os.environ.get("VLLM_NT_REFERENCE")
+    if not root:
+        raise SystemExit("the sampler fixture needs the reference checkout: --reference DIR or VLLM_NT_REFERENCE=DIR")
+    return Path(root) / "vllm_nt" / "_ntops" / "torch" / "sampler.py"
 
 
 def sampler_fixture() -> None:
@@ -205,7 +242,7 @@ def sampler_fixture() -> None:
 
     from vllm.v1.sample.ops.topk_topp_sampler import apply_top_k_top_p_pytorch
 
-    spec = importlib.util.spec_from_file_location("reference_sampler", REFERENCE_SAMPLER)
+    spec = importlib.util.spec_from_file_location("reference_sampler", _reference_sampler_path())
     ref = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(ref)
 
@@ -233,11 +270,8 @@ def sampler_fixture() -> None:
 if __name__ == "__main__":
     import sys
 
-    if sys.argv[1:] == ["--only", "sampler"]:
-        sampler_fixture()
-    elif sys.argv[1:] == ["--only", "f16"]:
-        half_fixtures()
-    else:
-        main()
-        half_fixtures()
-        sampler_fixture()
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    steps = {"main": main, "f16": half_fixtures, "gemma": gemma_fixture, "sampler": sampler_fixture}
+    for name, step in steps.items():
+        if only in (None, name):
+            step()

@@ -195,3 +195,22 @@ def test_decode_single_chunk_writes_output_directly(ctx):
     if ctx[0] == 0:
         assert not out[0].any()
     assert capi.read_device_error(stream()) == 0
+
+
+def test_decode_direct_mode_flags_a_sequence_longer_than_max_seq_len():
+    """max_seq_len = 256 at a batch of 2 makes the call a single-chunk (direct) decode; a
+    sequence of 600 tokens breaks that contract and must raise the index-range flag (its
+    row covers only the first chunk), while the sequence within the bound is exact."""
+    dev = cuda_device()
+    ctx = [600, 100]
+    q, kc, vc, seq, table = make_case(ctx, 32, 8, 64, seed=23)
+    ref = oracle.paged_decode(q, kc, vc, seq, table, 0.09)
+    qd, kd, vd, sd, td = (t.to(dev) for t in (q, kc, vc, seq, table))
+    out = torch.empty_like(qd)
+    assert capi.lib().ntb200_paged_attention_decode_workspace_size(2, 32, 8, 128, 16, 256) == 0
+    capi.call("ntb200_paged_attention_decode", ptr(out), ptr(qd), ptr(kd), ptr(vd), ptr(sd), ptr(td),
+              2, 32, 8, 128, 16, 64, table.shape[1], table.shape[1], 256, 0.09,
+              32 * 128, 128, 32 * 128, 128, kd.stride(0), kd.stride(1), kd.stride(2), None, 0, 1, stream())
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out[1].float().cpu(), ref[1], rtol=TOL, atol=TOL)
+    assert capi.read_device_error(stream()) == capi.DEVERR_INDEX_RANGE

@@ -4,6 +4,8 @@ Small M is checked against the CPU oracle; for M >= 1024 the reference is a torc
 matmul on the GPU with TF32 disabled (a floating-point kernel's fp32 reference).
 Tolerance 2e-2 (rtol = atol) on the 16-bit output."""
 
+import math
+
 import pytest
 import torch
 
@@ -69,13 +71,17 @@ def test_linear_m2048_cta_pairs_vs_fp32(k, n):
     torch.testing.assert_close(_ntb200_linear(x, w).float(), ref, rtol=TOL, atol=TOL)
 
 
-def test_linear_m8192_gate_up_row_subset():
+@pytest.mark.parametrize("k,n", SHAPES)
+def test_linear_m8192_row_subset(k, n):
+    """The M = 8192 benchmark size of every projection (CTA-pair kernel, grouped
+    rasterisation): 128 seeded rows, which land in many different 256-row tiles, against
+    an fp32 reference of those rows."""
     dev = cuda_device()
-    gd = torch.Generator(device=dev).manual_seed(3)
-    x = torch.randn(8192, 4096, generator=gd, device=dev, dtype=torch.bfloat16)
-    w = 0.02 * torch.randn(28672, 4096, generator=gd, device=dev, dtype=torch.bfloat16)
+    gd = torch.Generator(device=dev).manual_seed(3 + k + n)
+    x = torch.randn(8192, k, generator=gd, device=dev, dtype=torch.bfloat16)
+    w = 0.02 * torch.randn(n, k, generator=gd, device=dev, dtype=torch.bfloat16)
     out = _ntb200_linear(x, w)
-    rows = torch.randperm(8192, generator=seeded(4))[:96].to(dev)
+    rows = torch.randperm(8192, generator=seeded(4 + n))[:128].to(dev)
     ref = x[rows].float() @ w.float().t()
     torch.testing.assert_close(out[rows].float(), ref, rtol=TOL, atol=TOL)
 
@@ -181,3 +187,41 @@ def test_linear_argmax_ties_take_the_first_index():
     assert linear_argmax(x, w).tolist() == [5, 5, 5]
     w[39999] = 2.0
     assert linear_argmax(x, w).tolist() == [39999, 39999, 39999]
+
+
+@pytest.fixture(scope="module")
+def lm_head_case():
+    """Llama-3 LM head: V = 128256, K = 4096, bf16, x ~N(0,1), W ~N(0,0.02); 256 token rows.
+    Rows 100 and 128000 of W (different vocabulary tiles) are made equal and larger than
+    every other logit of token row 3, a deliberate tie across two tiles.  The oracle's fp32
+    logits of all 256 rows are computed once on the CPU."""
+    g = seeded(2026)
+    x = torch.randn(256, 4096, generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(128256, 4096, generator=g)).to(torch.bfloat16)
+    tie = (0.05 * torch.sign(x[3].float())).to(torch.bfloat16)
+    w[100] = tie
+    w[128000] = tie
+    ids, logits = oracle.linear_argmax(x, w)
+    return x, w, w.cuda(), ids, logits
+
+
+@pytest.mark.parametrize("m", [1, 16, 128, 256])
+def test_linear_argmax_lm_head_vs_oracle(lm_head_case, m):
+    """ntb200_linear_argmax at the LM-head shape against the oracle's greedy token (first
+    index of the largest bf16-rounded fp32 logit).  A different index is accepted only where
+    the two candidates' oracle logits lie within one bf16 ulp of each other (the GEMM's own
+    fp32 accumulation order can round such a pair apart), and such rows must be rare; the
+    tie across tiles must resolve to the first index."""
+    x, w, wd, ids, logits = lm_head_case
+    from vllm_nt._ntops.torch.linear import linear_argmax
+
+    got = linear_argmax(x[:m].cuda(), wd).cpu()
+    want = ids[:m]
+    diff = (got != want).nonzero().flatten().tolist()
+    for r in diff:
+        top = float(logits[r, want[r]])
+        ulp = 2.0 ** (math.floor(math.log2(abs(top))) - 7)
+        assert abs(float(logits[r, got[r]]) - top) <= ulp, (r, int(got[r]), int(want[r]))
+    assert len(diff) <= max(1, m // 50)
+    if m > 3:
+        assert int(got[3]) == 100 and int(want[3]) == 100

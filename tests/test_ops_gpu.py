@@ -98,6 +98,88 @@ def test_rms_norm_no_weight_and_strided_rows():
     _close(out, oracle.rms_norm(x, None, 1e-5), torch.bfloat16)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(128, 4096), (7, 4095), (3, 40000), (1, 2304)])
+def test_gemma_rms_norm_capi(dtype, shape):
+    """Gemma variant (vLLM's GemmaRMSNorm.forward_native rounding: (1 + w) in fp32, one
+    rounding of the product) against the oracle; register-resident, second-pass and scalar
+    rows.  The weight is the raw Gemma parameter, ~N(0, 0.3)."""
+    dev = cuda_device()
+    g = seeded(17)
+    x = torch.randn(shape, generator=g).to(dtype)
+    w = (0.3 * torch.randn(shape[-1], generator=g)).to(dtype)
+    rows, hidden = shape
+    xd, wd = x.to(dev), w.to(dev)
+    out = torch.empty_like(xd)
+    capi.call("ntb200_gemma_rms_norm", ptr(out), ptr(xd), ptr(wd), rows, hidden, hidden, hidden, 1e-6,
+              dtype_code(dtype), stream())
+    torch.cuda.synchronize()
+    _close(out, oracle.gemma_rms_norm(x, w, 1e-6), dtype)
+    assert capi.read_device_error(stream()) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(128, 4096), (7, 4095), (3, 40000)])
+def test_gemma_fused_add_rms_norm_capi(dtype, shape):
+    """Gemma with a residual: the sum is taken in the input dtype (bf16 rounds it before the
+    statistics), written back bit-exact; fp16 is rejected (vLLM returns an fp32 residual)."""
+    dev = cuda_device()
+    g = seeded(18)
+    x = torch.randn(shape, generator=g).to(dtype)
+    r = torch.randn(shape, generator=g).to(dtype)
+    w = (0.3 * torch.randn(shape[-1], generator=g)).to(dtype)
+    ref_y, ref_r = oracle.gemma_rms_norm(x, w, 1e-6, r)
+    rows, hidden = shape
+    xd, rd, wd = x.to(dev), r.to(dev), w.to(dev)
+    out = torch.empty_like(xd)
+    capi.call("ntb200_gemma_fused_add_rms_norm", ptr(out), ptr(rd), ptr(xd), ptr(wd), rows, hidden, hidden, hidden,
+              hidden, 1e-6, dtype_code(dtype), stream())
+    torch.cuda.synchronize()
+    _close(out, ref_y, dtype)
+    assert bits_equal(rd.cpu(), ref_r)
+    h = x.to(torch.float16).to(dev)
+    with pytest.raises(capi.NtB200Error) as e:
+        capi.call("ntb200_gemma_fused_add_rms_norm", ptr(h), ptr(h.clone()), ptr(h), ptr(h[0]), rows, hidden, hidden,
+                  hidden, hidden, 1e-6, 2, stream())
+    assert e.value.status == -2
+    assert capi.read_device_error(stream()) == 0
+
+
+def test_gemma_rms_norm_matches_vllm_forward_native_through_the_hook(monkeypatch):
+    """The GemmaRMSNorm hook (all-b200 config) on a layer with vLLM's GemmaRMSNorm state
+    (bf16, with and without a residual) against GemmaRMSNorm.forward_native; the inputs are
+    left untouched, as vLLM's native code leaves them, and every call is a kernel hit."""
+    from pathlib import Path
+    from types import SimpleNamespace
+
+    from vllm.model_executor.layers.layernorm import GemmaRMSNorm
+
+    from vllm_nt._ntops import patching
+
+    root = Path(__file__).resolve().parents[1]
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(root / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml"))
+    monkeypatch.setenv("VLLM_NT_ENABLE_STATS", "1")
+    patching._reset_usage_state()
+    dev = cuda_device()
+    g = seeded(19)
+    layer = SimpleNamespace(weight=torch.nn.Parameter((0.3 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)),
+                            variance_epsilon=1e-6)
+    x = torch.randn(33, 2048, generator=g).to(torch.bfloat16).to(dev)
+    r = torch.randn(33, 2048, generator=g).to(torch.bfloat16).to(dev)
+    x0, r0 = x.clone(), r.clone()
+    want = GemmaRMSNorm.forward_native(layer, x.clone())
+    got = patching._nt_gemma_rms_norm_forward(layer, x)
+    _close(got, want.cpu(), torch.bfloat16)
+    want_y, want_r = GemmaRMSNorm.forward_native(layer, x.clone(), r.clone())
+    got_y, got_r = patching._nt_gemma_rms_norm_forward(layer, x, r)
+    _close(got_y, want_y.cpu(), torch.bfloat16)
+    assert torch.equal(got_r, want_r)
+    assert torch.equal(x, x0) and torch.equal(r, r0)
+    op = patching.get_usage_summary()["operators"]["GemmaRMSNorm"]
+    assert op["hits"] == 2 and op["fallbacks"] == 0
+    patching._reset_usage_state()
+
+
 def test_fused_add_rms_norm_in_place_output_aliases_input():
     dev = cuda_device()
     g = seeded(3)

@@ -23,6 +23,17 @@ def test_rms_norm_matches_vllm_native(tag):
 
 
 @pytest.mark.parametrize("tag", ["f32", "bf16", "f16"])
+def test_gemma_rms_norm_matches_vllm_native(tag):
+    """GemmaRMSNorm.forward_native outputs (tests/golden/gemma_rms_norm.npz), bit for bit,
+    including the fp32 residual vLLM hands back for fp16 inputs."""
+    g = golden("gemma_rms_norm")
+    x, r, w = g[f"{tag}_x"], g[f"{tag}_residual"], g[f"{tag}_weight"]
+    assert bits_equal(oracle.gemma_rms_norm(x, w, 1e-6), g[f"{tag}_out_plain"])
+    out, res = oracle.gemma_rms_norm(x, w, 1e-6, r)
+    assert bits_equal(out, g[f"{tag}_out"]) and bits_equal(res, g[f"{tag}_residual_out"])
+
+
+@pytest.mark.parametrize("tag", ["f32", "bf16", "f16"])
 def test_silu_and_mul_matches_vllm_native(tag):
     g = golden(f"silu_and_mul_{tag}")
     out = oracle.silu_and_mul(g["x"])

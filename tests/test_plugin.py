@@ -71,6 +71,7 @@ def test_usage_summary_shape_and_registered_ops():
         assert op in s["registered_ops"]
     assert s["hit_ops"] == [] and set(s["missed_ops"]) == set(s["registered_ops"])
     d = s["operators"]["MatMul"]
+    # the reference's keys; "declined" appears only once a call was not served
     assert set(d) == {"configured_backend", "active_backend", "hits", "failures", "fallbacks", "registered_via", "backends"}
     assert d["configured_backend"] == "b200"
 
@@ -131,7 +132,7 @@ class _Norm:
 
 
 def test_rms_norm_hook_hits_and_falls_back_on_failure(monkeypatch):
-    monkeypatch.setattr(patching, "_norm_eligible", lambda *a: True)
+    monkeypatch.setattr(patching, "_why_not_norm", lambda *a: None)
     monkeypatch.setattr(patching, "norm", lambda self, x, w, r=None, gemma=False: "kernel")
     monkeypatch.setitem(patching._ORIGINAL_OPERATOR_FORWARDS, "RMSNorm", {"native": lambda self, x, r=None: "native"})
     assert patching._nt_rms_norm_forward(_Norm(), torch.ones(2, 8)) == "kernel"
@@ -146,8 +147,9 @@ def test_rms_norm_hook_hits_and_falls_back_on_failure(monkeypatch):
     assert op["failures"] == 1 and op["active_backend"] == "original"
 
 
-def test_ineligible_calls_go_straight_to_vllm():
-    """CPU tensors are not eligible: vLLM's own forward runs and nothing is counted."""
+def test_ineligible_calls_go_to_vllm_and_are_counted_as_declined():
+    """CPU tensors are not eligible: vLLM's own forward runs, no hit is counted, and the
+    call shows in the summary as a fallback to original with its reason."""
     from vllm.model_executor.layers.layernorm import RMSNorm
     from vllm import ir
 
@@ -158,14 +160,17 @@ def test_ineligible_calls_go_straight_to_vllm():
     out, res = patching._nt_rms_norm_forward(layer, x.clone(), r.clone())
     ref, ref_r = ir.ops.fused_add_rms_norm(x.clone(), r.clone(), layer.weight.data, 1e-6)
     torch.testing.assert_close(out, ref)
-    assert patching.get_usage_summary()["operators"]["RMSNorm"]["hits"] == 0
+    op = patching.get_usage_summary()["operators"]["RMSNorm"]
+    assert op["hits"] == 0 and op["fallbacks"] == 1
+    assert op["declined"] == {"not a CUDA tensor": 1} and op["backends"]["original"]["fallbacks"] == 1
+    assert "declined: not a CUDA tensor=1" in patching.format_usage_summary(use_color=False)
     assert RMSNorm is not None
 
 
 def test_linear_hook_routes_and_handles_residual(monkeypatch):
     from vllm.model_executor.layers.linear import UnquantizedLinearMethod
 
-    monkeypatch.setattr(patching, "_gemm_eligible", lambda *a: True)
+    monkeypatch.setattr(patching, "_why_not_gemm", lambda *a: None)
     monkeypatch.setattr(patching, "linear", lambda x, w, b=None: x @ w.t())
     setattr(patching._nt_unquantized_linear_apply, "_original", lambda *a, **k: "vllm")
     layer = SimpleNamespace(weight=torch.ones(3, 4))
@@ -209,7 +214,7 @@ def test_rope_hook_uses_matched_cache_and_counts(monkeypatch):
 
 def test_attention_hooks_route_decode_prefill_and_kv_store(monkeypatch):
     calls = {}
-    monkeypatch.setattr(patching, "_attn_impl_supported", lambda *a: True)
+    monkeypatch.setattr(patching, "_attn_impl_reason", lambda *a: None)
     monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
 
     def fake_decode(out, q, kv, seq, table, n, scale, msl, kv_dim=0):
@@ -308,7 +313,7 @@ def test_flashinfer_hooks_decode_only_and_kv_store(monkeypatch):
     """FlashInferImpl hooks: pure-decode batches with a decode block table go to the
     kernels on the [blocks, 2, 16, H, D] cache (kv_dim 1); prefill stays on FlashInfer."""
     calls = {}
-    monkeypatch.setattr(patching, "_attn_impl_supported", lambda *a: True)
+    monkeypatch.setattr(patching, "_attn_impl_reason", lambda *a: None)
     monkeypatch.setattr(torch.Tensor, "is_cuda", property(lambda self: True))
 
     def fake_decode(out, q, kv, seq, table, n, scale, msl, kv_dim):

@@ -44,7 +44,7 @@ KERNEL_SOURCES = (
     "allreduce.cu",
     "sampler.cu",
 )
-SHARED_HEADERS = (CSRC / "common.cuh", CSRC / "tcgen05.cuh", INCLUDE / "ntb200.h", Path(__file__).resolve())
+SHARED_HEADERS = (CSRC / "common.cuh", CSRC / "tcgen05.cuh", CSRC / "rope_math.cuh", INCLUDE / "ntb200.h", Path(__file__).resolve())
 
 NVCC_FLAGS = [
     "-gencode",

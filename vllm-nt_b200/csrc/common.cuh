@@ -105,6 +105,38 @@ template <> struct Elem<__half> {
   static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
 };
 
+// Two fp32 values to the storage type with one paired conversion (cvt.rn.{bf16x2,f16x2}.f32:
+// round to nearest even, the same bits as two scalar conversions).  round() rounds in place
+// (identity for fp32); store() writes the pair to two adjacent elements (4-byte aligned).
+template <typename T> struct Pair;
+template <> struct Pair<float> {
+  static __device__ __forceinline__ void round(float&, float&) {}
+  static __device__ __forceinline__ void store(float* dst, float a, float b) {
+    dst[0] = a;
+    dst[1] = b;
+  }
+};
+template <> struct Pair<__nv_bfloat16> {
+  static __device__ __forceinline__ void round(float& a, float& b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    a = __low2float(h);
+    b = __high2float(h);
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* dst, float a, float b) {
+    *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(a, b);
+  }
+};
+template <> struct Pair<__half> {
+  static __device__ __forceinline__ void round(float& a, float& b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    a = __low2float(h);
+    b = __high2float(h);
+  }
+  static __device__ __forceinline__ void store(__half* dst, float a, float b) {
+    *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(a, b);
+  }
+};
+
 // A 16-byte (or narrower) vector of N elements of T, loaded/stored as one transaction.
 template <typename T, int N>
 struct __align__(sizeof(T) * N) Vec {
@@ -117,6 +149,21 @@ __device__ __forceinline__ void load_f(const T* p, float (&out)[N]) {
 #pragma unroll
   for (int i = 0; i < N; ++i) out[i] = Elem<T>::to_f(raw.v[i]);
 }
+// Converts N fp32 values to a vector of T, two at a time with the paired conversion where
+// N is even (the same bits as N scalar conversions).
+template <typename T, int N>
+__device__ __forceinline__ Vec<T, N> pack_f(const float (&in)[N]) {
+  Vec<T, N> raw;
+  if constexpr (N % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 2) Pair<T>::store(&raw.v[i], in[i], in[i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) raw.v[i] = Elem<T>::from_f(in[i]);
+  }
+  return raw;
+}
+
 template <typename T, int N>
 __device__ __forceinline__ void store_f(T* p, const float (&in)[N]) {
   Vec<T, N> raw;
@@ -124,6 +171,11 @@ __device__ __forceinline__ void store_f(T* p, const float (&in)[N]) {
   for (int i = 0; i < N; ++i) raw.v[i] = Elem<T>::from_f(in[i]);
   *reinterpret_cast<Vec<T, N>*>(p) = raw;
 }
+
+// silu(g) = g / (1 + e^-g) in fp32 with the fast exponential and division intrinsics (a
+// few ulp, far inside the bf16/fp16 rounding that follows and the 1e-5 fp32 tolerance);
+// shared by silu_and_mul and the fused gate_up GEMM epilogue so that the two agree bit for bit.
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // Waits until the kernel before this one on the stream has completed (no-op when the
 // launch did not allow programmatic serialization).

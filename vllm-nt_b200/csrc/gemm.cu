@@ -72,7 +72,7 @@ struct GemmParams {
 template <typename T>
 __device__ __forceinline__ float swiglu(float gate_acc, float up_acc) {
   const float g = Elem<T>::round(gate_acc), u = Elem<T>::round(up_acc);
-  return Elem<T>::round(g / (1.0f + expf(-g))) * u;
+  return Elem<T>::round(silu_f(g)) * u;
 }
 
 // Writes 32 consecutive output columns c0.. of one row (bias added when given; columns at

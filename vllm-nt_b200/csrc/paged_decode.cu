@@ -168,6 +168,10 @@ __global__ void __launch_bounds__(kThreads) paged_decode_split_kernel(
   if (ctx < 0) ctx = 0;
   int64_t total_blocks = (int64_t(ctx) + kBlockTokens - 1) / kBlockTokens;
   if (total_blocks > p.max_blocks_per_seq) total_blocks = p.max_blocks_per_seq;
+  // a sequence longer than the max_seq_len the call was sized for would be cut to the
+  // chunks that exist: flag it (the merge step flags the same in split mode)
+  if (chunk == 0 && threadIdx.x == 0 && total_blocks > int64_t(p.max_chunks) * p.chunk_blocks)
+    raise_device_error(p.err, NTB200_DEVERR_INDEX_RANGE);
   const int64_t blk_begin = int64_t(chunk) * p.chunk_blocks;
   if (blk_begin >= total_blocks) {  // uniform across the CTA
     if (p.direct) {  // an empty sequence attends to nothing: zero rows, as the combine writes

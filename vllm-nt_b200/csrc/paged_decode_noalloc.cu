@@ -21,7 +21,13 @@
 //     NTB200_ERR_WORKSPACE and a message naming both sizes; nothing is launched.
 //   * The first call on a device resolves the array's device address (one
 //     cudaGetSymbolAddress with that device current).  Make that first call before
-//     capturing a stream into a CUDA graph.
+//     capturing a stream into a CUDA graph.  Only a successful lookup is kept: a lookup
+//     that fails (for example because the module could not be loaded, or because it was
+//     attempted during a capture) returns NTB200_ERR_CUDA, clears the CUDA error it left,
+//     and the next call on that device tries again.
+//   * Under CUDA's default lazy module loading, a GPU holds the array only once this
+//     library's device code is loaded on it; with CUDA_MODULE_LOADING=EAGER every GPU whose
+//     context loads the library holds it, whether or not this entry point is called.
 //   * Every call on a device shares the one array and leaves its partials there.  No
 //     part of it needs to start at zero: each partial the merge step reads was written by
 //     the same call.  Two calls whose kernels overlap on the GPU (different streams, or
@@ -39,14 +45,22 @@ static __device__ __align__(256) unsigned char g_decode_noalloc_scratch[NTB200_D
 
 namespace {
 constexpr int kMaxDevices = 64;
-std::once_flag g_setup_once[kMaxDevices];
-void* g_scratch_addr[kMaxDevices];
-cudaError_t g_setup_status[kMaxDevices];
+std::mutex g_setup_mutex[kMaxDevices];
+void* g_scratch_addr[kMaxDevices];  // written once under the device's mutex, then only read
 
-void setup_device(int dev) {
+// The device address of the scratch array on `dev` (the current device), or nullptr with
+// *err set when the lookup fails; a failed lookup is not remembered.
+void* scratch_address(int dev, cudaError_t* err) {
+  std::lock_guard<std::mutex> lock(g_setup_mutex[dev]);
+  if (g_scratch_addr[dev] != nullptr) return g_scratch_addr[dev];
   void* p = nullptr;
-  g_setup_status[dev] = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
-  g_scratch_addr[dev] = g_setup_status[dev] == cudaSuccess ? p : nullptr;
+  *err = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch);
+  if (*err != cudaSuccess || p == nullptr) {
+    cudaGetLastError();  // leave no sticky-looking error behind for the caller's next check
+    return nullptr;
+  }
+  g_scratch_addr[dev] = p;
+  return p;
 }
 }  // namespace
 
@@ -64,10 +78,11 @@ extern "C" int ntb200_paged_attention_decode_noalloc(
     cudaGetLastError();
     return fail(NTB200_ERR_CUDA, "paged_decode_noalloc: no current CUDA device");
   }
-  std::call_once(g_setup_once[dev], setup_device, dev);
-  if (g_setup_status[dev] != cudaSuccess || g_scratch_addr[dev] == nullptr) {
+  cudaError_t lookup = cudaSuccess;
+  void* scratch = scratch_address(dev, &lookup);
+  if (scratch == nullptr) {
     return fail(NTB200_ERR_CUDA, "paged_decode_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-                cudaGetErrorString(g_setup_status[dev]));
+                cudaGetErrorString(lookup));
   }
   // the split-K partials this call needs, for the same effective context bound the
   // decode entry point uses (max_seq_len clamped to the block table's capacity)
@@ -87,6 +102,6 @@ extern "C" int ntb200_paged_attention_decode_noalloc(
                                        num_q_heads, num_kv_heads, head_size, block_size, num_blocks,
                                        max_blocks_per_seq, block_table_stride, max_seq_len, scale, q_seq_stride,
                                        q_head_stride, out_seq_stride, out_head_stride, cache_block_stride,
-                                       cache_page_stride, cache_head_stride, g_scratch_addr[dev],
+                                       cache_page_stride, cache_head_stride, scratch,
                                        NTB200_DECODE_NOALLOC_SCRATCH_BYTES, dtype, stream);
 }

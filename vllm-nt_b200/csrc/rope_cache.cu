@@ -6,15 +6,15 @@
 // (FlashAttentionImpl.do_kv_cache_update).  The reference reaches them as two kernels
 // (vllm_nt/_ntops/kernels/rotary_emb.py:6-37 through oot_support.py:134-204, and
 // vllm_nt/_ntops/kernels/kv_cache.py:4-45 through torch/kv_cache.py:7-21).  This kernel
-// does both in one pass: one CTA per token, each thread owns one 16-byte vector item of
+// does both in one pass over the token's 16-byte vector items
 //
 //   [ q rotation pairs | k rotation pairs | k dims past rotary_dim | v ]
 //
 // A q item is rotated and written back.  A k item is rotated, written back to k and the
 // same rounded vector written to key_cache[slot / block_size, slot % block_size, head].
 // The k tail (rotary_dim < head_size) and v items are copied bit for bit into the
-// caches.  The rotation is the one of rope.cu (separately rounded products, no FMA
-// contraction, 16-bit results rounded per torch op), so q, k and both caches are
+// caches.  The rotation is the one of rope.cu (rope_math.cuh: separately rounded products,
+// no FMA contraction, 16-bit results rounded per torch op), so q, k and both caches are
 // bit-identical to the RoPE kernel followed by the KV-store kernel.
 //
 // Slots: negative (vLLM padding) or past the slot mapping (padded rows) -> rotation only;
@@ -22,28 +22,16 @@
 // cos/sin cache sets NTB200_DEVERR_INDEX_RANGE and leaves the token's q/k unrotated; its
 // unrotated k and its v are still stored (what the two kernels in sequence do).
 //
-// Dispatch: the fused kernel keeps a token's dependent chain (position -> cos/sin row ->
-// rotation -> stores) inside one CTA of ~450 threads at 64 registers, two CTAs per SM; at
-// a decode step that costs less than a second launch (256 Llama-3-8B tokens: 3.7 us fused
-// against 6.5 us for the pair on a B200), but from a few thousand tokens on the pair keeps
-// more bytes in flight (16384 tokens: 141 us fused, 117 us for the pair).  The entry point
-// therefore launches the pair from kPairFromTokens tokens on; the results are the same bits
-// either way.
+// One launch for any token count: warps take (token, chunk) work units (see the kernel),
+// so a decode step spreads each token over several warps and a prefill chunk keeps 16
+// units in flight per SM.
+#include <algorithm>
+
 #include "common.cuh"
+#include "rope_math.cuh"
 
 namespace ntb200 {
 namespace {
-
-template <typename T>
-__device__ __forceinline__ void rotate_pair(float x1, float x2, float c, float s, float& o1,
-                                            float& o2) {
-  const float a = Elem<T>::round(__fmul_rn(x1, c));
-  const float b = Elem<T>::round(__fmul_rn(x2, s));
-  const float e = Elem<T>::round(__fmul_rn(x2, c));
-  const float f = Elem<T>::round(__fmul_rn(x1, s));
-  o1 = __fsub_rn(a, b);
-  o2 = __fadd_rn(e, f);
-}
 
 struct Geometry {
   int hq, hk;               // query / kv heads
@@ -92,85 +80,98 @@ __device__ __forceinline__ Item decode_item(const Geometry& g, int item) {
   return it;
 }
 
-template <typename T, int VEC, typename P, typename S>
-__global__ void __launch_bounds__(1024) rope_and_cache_kernel(
+// Work units as in rope.cu: a unit is (token, chunk of 32 x ITEMS items); one warp takes
+// one unit at a time from a grid-stride sequence.  Its item loads (q/k halves, k tail, v)
+// are issued together with the position and slot loads; the cos/sin loads follow the
+// position; then each item is rotated and/or stored.  With SHARED_CS (rotation vectors per
+// head half divide 32) a lane's rotation items share one cos/sin pair (ITEMS = 4, else 2);
+// calls too small to give every SM 16 warps of such units take one item per lane.
+constexpr int kThreads = 256;
+
+template <typename T, int VEC, bool SHARED_CS, int ITEMS, typename P, typename S>
+__global__ void __launch_bounds__(kThreads, ITEMS == 1 ? 4 : 2) rope_and_cache_kernel(
     const P* __restrict__ positions, const S* __restrict__ slots, T* __restrict__ q,
     T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ cos_sin,
-    T* __restrict__ kc, T* __restrict__ vc, Geometry g, unsigned int* err) {
+    T* __restrict__ kc, T* __restrict__ vc, Geometry g, int64_t num_tokens, unsigned int* err) {
   using V = Vec<T, VEC>;
-  const int64_t t = blockIdx.x;
+  constexpr int kItems = ITEMS;
+  constexpr int kUnitItems = 32 * kItems;
+  constexpr int kCs = SHARED_CS ? 1 : kItems;
   const int total = (g.hq + g.hk) * g.pairs + g.hk * (g.tail + g.vvec);
+  const int chunks = (total + kUnitItems - 1) / kUnitItems;
+  const int lane = threadIdx.x & 31;
+  const int64_t units = num_tokens * chunks;
+  const int64_t warps = int64_t(gridDim.x) * (kThreads / 32);
   pdl_trigger();
   pdl_wait();
-  // The first item's data does not depend on the position or the slot: its loads are
-  // issued together with the two index loads.
-  const int item0 = threadIdx.x;
-  V a0, b0;
-  Item it0{0, 0, 0};
-  if (item0 < total) {
-    it0 = decode_item<VEC>(g, item0);
-    const T* src = it0.kind == kQRot   ? q + t * g.qt + int64_t(it0.head) * g.qh
-                   : it0.kind == kVCopy ? v + t * g.vt + int64_t(it0.head) * g.vh
-                                        : k + t * g.kt + int64_t(it0.head) * g.kh;
-    a0 = *reinterpret_cast<const V*>(src + it0.off);
-    if (it0.kind <= kKRot) b0 = *reinterpret_cast<const V*>(src + g.half + it0.off);
-  }
-  const int64_t pos = static_cast<int64_t>(positions[t]);
-  const int64_t slot = t < g.store_tokens ? static_cast<int64_t>(slots[t]) : -1;
-  const bool pos_ok = pos >= 0 && pos < g.cs_rows;
-  if (!pos_ok && threadIdx.x == 0) raise_device_error(err, NTB200_DEVERR_INDEX_RANGE);
-  bool store = slot >= 0;
-  if (slot >= g.num_slots) {
-    if (threadIdx.x == 0) raise_device_error(err, NTB200_DEVERR_INDEX_RANGE);
-    store = false;
-  }
-  int64_t dst_row = 0;
-  if (store) {
-    const int64_t blk = slot / g.block_size;
-    dst_row = blk * g.cbs + (slot - blk * g.block_size) * g.cps;
-  }
-  const T* cs = cos_sin + (pos_ok ? pos : 0) * g.cs_row;
-  for (int item = item0; item < total; item += blockDim.x) {
-    const Item it = item == item0 ? it0 : decode_item<VEC>(g, item);
-    if (it.kind >= kKTail && !store) continue;
-    if (!pos_ok && (it.kind == kQRot || !store)) continue;
-    T* base = it.kind == kQRot   ? q + t * g.qt + int64_t(it.head) * g.qh
-              : it.kind == kVCopy ? const_cast<T*>(v) + t * g.vt + int64_t(it.head) * g.vh
-                                  : k + t * g.kt + int64_t(it.head) * g.kh;
-    V a, b;
-    if (item == item0) {
-      a = a0;
-      b = b0;
-    } else {
-      a = *reinterpret_cast<const V*>(base + it.off);
-      if (it.kind <= kKRot) b = *reinterpret_cast<const V*>(base + g.half + it.off);
-    }
-    T* cache_head = (it.kind == kVCopy ? vc : kc) + dst_row + int64_t(it.head) * g.chs;
-    if (it.kind >= kKTail) {  // bit copy into the cache
-      *reinterpret_cast<V*>(cache_head + it.off) = a;
-      continue;
-    }
-    if (!pos_ok) {  // unrotated key into the cache, as the KV store alone would leave it
-      *reinterpret_cast<V*>(cache_head + it.off) = a;
-      *reinterpret_cast<V*>(cache_head + g.half + it.off) = b;
-      continue;
-    }
-    float c[VEC], s[VEC];
-    load_f<T, VEC>(cs + it.off, c);
-    load_f<T, VEC>(cs + g.half + it.off, s);
-    V r1, r2;
+  for (int64_t u = int64_t(blockIdx.x) * (kThreads / 32) + (threadIdx.x >> 5); u < units; u += warps) {
+    const int64_t t = u / chunks;
+    const int first = int(u - t * chunks) * kUnitItems + lane;
+    V a[kItems], b[kItems], c[kCs], s[kCs];
+    Item it[kItems];
+    T* base[kItems];
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) {
-      float o1, o2;
-      rotate_pair<T>(Elem<T>::to_f(a.v[j]), Elem<T>::to_f(b.v[j]), c[j], s[j], o1, o2);
-      r1.v[j] = Elem<T>::from_f(o1);
-      r2.v[j] = Elem<T>::from_f(o2);
+    for (int j = 0; j < kItems; ++j) {
+      const int item = first + 32 * j;
+      if (item < total) {
+        it[j] = decode_item<VEC>(g, item);
+        base[j] = it[j].kind == kQRot   ? q + t * g.qt + int64_t(it[j].head) * g.qh
+                  : it[j].kind == kVCopy ? const_cast<T*>(v) + t * g.vt + int64_t(it[j].head) * g.vh
+                                         : k + t * g.kt + int64_t(it[j].head) * g.kh;
+        a[j] = *reinterpret_cast<const V*>(base[j] + it[j].off);
+        if (it[j].kind <= kKRot) b[j] = *reinterpret_cast<const V*>(base[j] + g.half + it[j].off);
+      }
     }
-    *reinterpret_cast<V*>(base + it.off) = r1;
-    *reinterpret_cast<V*>(base + g.half + it.off) = r2;
-    if (it.kind == kKRot && store) {
-      *reinterpret_cast<V*>(cache_head + it.off) = r1;
-      *reinterpret_cast<V*>(cache_head + g.half + it.off) = r2;
+    const int64_t pos = static_cast<int64_t>(positions[t]);
+    const int64_t slot = t < g.store_tokens ? static_cast<int64_t>(slots[t]) : -1;
+    const bool pos_ok = pos >= 0 && pos < g.cs_rows;
+    if (!pos_ok && first == 0) raise_device_error(err, NTB200_DEVERR_INDEX_RANGE);
+    bool store = slot >= 0;
+    if (slot >= g.num_slots) {
+      if (first == 0) raise_device_error(err, NTB200_DEVERR_INDEX_RANGE);
+      store = false;
+    }
+    int64_t dst_row = 0;
+    if (store) {
+      const int64_t blk = slot / g.block_size;
+      dst_row = blk * g.cbs + (slot - blk * g.block_size) * g.cps;
+    }
+    const T* cs = cos_sin + (pos_ok ? pos : 0) * g.cs_row;
+    if (pos_ok) {
+#pragma unroll
+      for (int j = 0; j < kCs; ++j) {
+        if (first + 32 * j < total && it[j].kind <= kKRot) {
+          c[j] = *reinterpret_cast<const V*>(cs + it[j].off);
+          s[j] = *reinterpret_cast<const V*>(cs + g.half + it[j].off);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kItems; ++j) {
+      if (first + 32 * j >= total) continue;
+      const Item& m = it[j];
+      T* cache_head = (m.kind == kVCopy ? vc : kc) + dst_row + int64_t(m.head) * g.chs;
+      if (m.kind >= kKTail) {  // bit copy into the cache
+        if (store) *reinterpret_cast<V*>(cache_head + m.off) = a[j];
+        continue;
+      }
+      if (!pos_ok) {  // unrotated key into the cache, as the KV store alone would leave it
+        if (m.kind == kKRot && store) {
+          *reinterpret_cast<V*>(cache_head + m.off) = a[j];
+          *reinterpret_cast<V*>(cache_head + g.half + m.off) = b[j];
+        }
+        continue;
+      }
+      const V& cj = c[SHARED_CS ? 0 : j];
+      const V& sj = s[SHARED_CS ? 0 : j];
+      V r1, r2;
+      rotate_vec<T, VEC>(a[j], b[j], cj, sj, r1, r2);
+      *reinterpret_cast<V*>(base[j] + m.off) = r1;
+      *reinterpret_cast<V*>(base[j] + g.half + m.off) = r2;
+      if (m.kind == kKRot && store) {
+        *reinterpret_cast<V*>(cache_head + m.off) = r1;
+        *reinterpret_cast<V*>(cache_head + g.half + m.off) = r2;
+      }
     }
   }
 }
@@ -190,19 +191,30 @@ int launch(const void* positions, const void* slots, void* q, void* k, const voi
   g.vvec = static_cast<int>(head_size / vec);
   const int64_t items = int64_t(g.hq + g.hk) * g.pairs + int64_t(g.hk) * (g.tail + g.vvec);
   if (items > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "rope_and_cache: too many heads");
-  // one item per thread where possible: all of a token's loads are in flight at once
-  const int threads = static_cast<int>(items >= 1024 ? 1024 : (items < 32 ? 32 : ceil_div(items, 32) * 32));
+  const bool shared_cs = vec_ok && 32 % g.pairs == 0;
+  const int big = shared_cs ? 4 : 2;
+  const int sms = num_sms();
+  // several items per lane once every SM has 16 warps of work at that size; else one
+  const bool many = tokens * ceil_div(items, 32 * big) >= int64_t(sms) * 16;
+  const int per_lane = many ? big : 1;
+  const int64_t units = tokens * ceil_div(items, 32 * per_lane);  // as the kernel counts them
+  // persistent CTAs: the resident count per SM the kernel's launch bound allows, or fewer
+  const int64_t ctas = std::min<int64_t>(ceil_div(units, kThreads / 32), int64_t(sms) * (many ? 2 : 4));
   unsigned int* err = device_error_word();
-  const dim3 grid(static_cast<unsigned>(tokens));
-  if (vec_ok)
-    return launch_kernel("rope_and_cache", rope_and_cache_kernel<T, kVec, P, S>, grid, dim3(threads), 0,
-                         stream, static_cast<const P*>(positions), static_cast<const S*>(slots),
-                         static_cast<T*>(q), static_cast<T*>(k), static_cast<const T*>(v),
-                         static_cast<const T*>(cos_sin), static_cast<T*>(kc), static_cast<T*>(vc), g, err);
-  return launch_kernel("rope_and_cache", rope_and_cache_kernel<T, 1, P, S>, grid, dim3(threads), 0, stream,
-                       static_cast<const P*>(positions), static_cast<const S*>(slots), static_cast<T*>(q),
-                       static_cast<T*>(k), static_cast<const T*>(v), static_cast<const T*>(cos_sin),
-                       static_cast<T*>(kc), static_cast<T*>(vc), g, err);
+  const dim3 grid(static_cast<unsigned>(ctas));
+#define NTB200_RC_LAUNCH(V, SHARED, ITEMS)                                                                     \
+  return launch_kernel("rope_and_cache", rope_and_cache_kernel<T, V, SHARED, ITEMS, P, S>, grid, dim3(kThreads), \
+                       0, stream, static_cast<const P*>(positions), static_cast<const S*>(slots),             \
+                       static_cast<T*>(q), static_cast<T*>(k), static_cast<const T*>(v),                      \
+                       static_cast<const T*>(cos_sin), static_cast<T*>(kc), static_cast<T*>(vc), g, tokens, err)
+  if (!vec_ok) NTB200_RC_LAUNCH(1, false, 1);
+  if (shared_cs) {
+    if (many) NTB200_RC_LAUNCH(kVec, true, 4);
+    NTB200_RC_LAUNCH(kVec, true, 1);
+  }
+  if (many) NTB200_RC_LAUNCH(kVec, false, 2);
+  NTB200_RC_LAUNCH(kVec, false, 1);
+#undef NTB200_RC_LAUNCH
 }
 
 template <typename T, typename P>
@@ -228,9 +240,6 @@ int by_pos(const void* positions, int pos_dtype, const void* slots, int slot_dty
                                stream);
   return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "rope_and_cache: positions dtype %d", pos_dtype);
 }
-
-// token count from which the two-kernel form is launched (see the dispatch note above)
-constexpr int64_t kPairFromTokens = 2048;
 
 }  // namespace
 }  // namespace ntb200
@@ -259,20 +268,6 @@ extern "C" int ntb200_rope_and_cache(
     return fail(NTB200_ERR_INVALID_ARGUMENT, "rope_and_cache: null pointer");
   if (cache_row_stride < rotary_dim)
     return fail(NTB200_ERR_INVALID_ARGUMENT, "rope_and_cache: cache row stride < rotary_dim");
-  if (num_tokens >= kPairFromTokens) {
-    const int es = dtype_size(dtype);
-    if (es == 0 || dtype == NTB200_DTYPE_I32 || dtype == NTB200_DTYPE_I64)
-      return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "rope_and_cache: dtype %d", dtype);
-    const int rc = ntb200_rotary_embedding_neox(positions, positions_dtype, query, key, cos_sin_cache, num_tokens,
-                                                num_q_heads, num_kv_heads, head_size, rotary_dim, q_token_stride,
-                                                q_head_stride, k_token_stride, k_head_stride, cache_row_stride,
-                                                num_cache_rows, dtype, stream);
-    if (rc != NTB200_OK || num_store_tokens == 0) return rc;
-    return ntb200_reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, slot_dtype, num_store_tokens,
-                                    num_kv_heads, head_size, block_size, num_slots, k_token_stride, k_head_stride,
-                                    v_token_stride, v_head_stride, cache_block_stride, cache_page_stride,
-                                    cache_head_stride, es, stream);
-  }
   Geometry g{};
   g.hq = static_cast<int>(num_q_heads);
   g.hk = static_cast<int>(num_kv_heads);

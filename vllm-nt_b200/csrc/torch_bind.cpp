@@ -115,6 +115,30 @@ void fused_add_rms_norm(at::Tensor out, at::Tensor residual, const at::Tensor& x
         "fused_add_rms_norm");
 }
 
+void gemma_rms_norm(at::Tensor out, const at::Tensor& x, const at::Tensor& weight, double eps) {
+  const Rows xr = rows_of(x, "x"), orr = rows_of(out, "out");
+  TORCH_CHECK(out.sizes() == x.sizes() && out.scalar_type() == x.scalar_type(), "ntb200.gemma_rms_norm: out mismatch");
+  const void* w = norm_weight(weight, x, xr.cols, "gemma_rms_norm");
+  c10::cuda::CUDAGuard guard(x.device());
+  check(ntb200_gemma_rms_norm(out.data_ptr(), x.data_ptr(), w, xr.rows, xr.cols, xr.stride, orr.stride,
+                              static_cast<float>(eps), dtype_code(x), stream_of(x)),
+        "gemma_rms_norm");
+}
+
+void gemma_fused_add_rms_norm(at::Tensor out, at::Tensor residual, const at::Tensor& x, const at::Tensor& weight,
+                              double eps) {
+  const Rows xr = rows_of(x, "x"), orr = rows_of(out, "out"), rr = rows_of(residual, "residual");
+  TORCH_CHECK(out.sizes() == x.sizes() && residual.sizes() == x.sizes() && out.scalar_type() == x.scalar_type() &&
+                  residual.scalar_type() == x.scalar_type(),
+              "ntb200.gemma_fused_add_rms_norm: shape/dtype mismatch");
+  const void* w = norm_weight(weight, x, xr.cols, "gemma_fused_add_rms_norm");
+  c10::cuda::CUDAGuard guard(x.device());
+  check(ntb200_gemma_fused_add_rms_norm(out.data_ptr(), residual.data_ptr(), x.data_ptr(), w, xr.rows, xr.cols,
+                                        xr.stride, rr.stride, orr.stride, static_cast<float>(eps), dtype_code(x),
+                                        stream_of(x)),
+        "gemma_fused_add_rms_norm");
+}
+
 void silu_and_mul(at::Tensor out, const at::Tensor& x) {
   const Rows xr = rows_of(x, "x"), orr = rows_of(out, "out");
   same_leading(x, out, "silu_and_mul");
@@ -656,6 +680,10 @@ TORCH_LIBRARY(ntb200, m) {
   m.def(
       "fused_add_rms_norm(Tensor(a!) out, Tensor(b!) residual, Tensor x, Tensor? weight, "
       "float eps) -> ()");
+  m.def("gemma_rms_norm(Tensor(a!) out, Tensor x, Tensor weight, float eps) -> ()");
+  m.def(
+      "gemma_fused_add_rms_norm(Tensor(a!) out, Tensor(b!) residual, Tensor x, Tensor weight, "
+      "float eps) -> ()");
   m.def("silu_and_mul(Tensor(a!) out, Tensor x) -> ()");
   m.def(
       "rotary_embedding_neox(Tensor positions, Tensor(a!) query, Tensor(b!)? key, "
@@ -716,6 +744,8 @@ TORCH_LIBRARY(ntb200, m) {
 TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("rms_norm", &rms_norm);
   m.impl("fused_add_rms_norm", &fused_add_rms_norm);
+  m.impl("gemma_rms_norm", &gemma_rms_norm);
+  m.impl("gemma_fused_add_rms_norm", &gemma_fused_add_rms_norm);
   m.impl("silu_and_mul", &silu_and_mul);
   m.impl("rotary_embedding_neox", &rotary_embedding_neox);
   m.impl("reshape_and_cache", &reshape_and_cache);

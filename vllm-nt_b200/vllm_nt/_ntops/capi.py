@@ -31,6 +31,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
          c_float, c_int, c_void_p],
     ),
+    "ntb200_gemma_rms_norm": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_float, c_int, c_void_p],
+    ),
+    "ntb200_gemma_fused_add_rms_norm": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
+         c_float, c_int, c_void_p],
+    ),
     "ntb200_silu_and_mul": (
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p]
     ),

@@ -7,7 +7,7 @@ gathers cos/sin inside the kernel)."""
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Callable
 
 import torch
@@ -22,6 +22,7 @@ from vllm_nt._ntops.torch.kv_cache import store_kvcache as nt_store_kvcache
 from vllm_nt._ntops.torch.linear import linear as nt_linear
 from vllm_nt._ntops.torch.linear import linear_silu_and_mul as nt_linear_silu_and_mul
 from vllm_nt._ntops.torch.rms_norm import fused_add_rms_norm as nt_fused_add_rms_norm
+from vllm_nt._ntops.torch.rms_norm import gemma_rms_norm as nt_gemma_rms_norm
 from vllm_nt._ntops.torch.rms_norm import rms_norm as nt_rms_norm
 from vllm_nt._ntops.torch.rotary_emb import apply_rotary_emb as nt_apply_rotary_emb
 from vllm_nt._ntops.torch.rotary_emb import rotary_embedding as nt_rotary_embedding
@@ -32,17 +33,26 @@ from vllm_nt._ntops.torch.sampler import random_sample as nt_random_sample  # no
 
 @dataclass
 class OperatorStats:
+    """Per-operator accounting: kernel hits, whether the first hit was logged, the
+    strongest registration path that installed the op, and the calls the kernels did not
+    serve, counted by reason."""
+
     hits: int = 0
     logged: bool = False
     registered_via: str | None = None
+    declined: dict[str, int] = field(default_factory=dict)
 
 
 def norm(self, x: torch.Tensor, weight: torch.Tensor | None, residual: torch.Tensor | None = None, gemma: bool = False):
     """RMSNorm.forward contract: returns ``out`` or ``(out, new_residual)``.
 
     With a residual the sum is formed in fp32 inside the kernel and written into the
-    residual buffer (vLLM's CUDA convention), the norm is taken of the fp32 sum."""
+    residual buffer (vLLM's CUDA convention), the norm is taken of the fp32 sum.  With
+    ``gemma=True`` ``weight`` is the raw Gemma parameter w: the kernel forms (1 + w) in fp32
+    and rounds as GemmaRMSNorm.forward_native does, and returns new tensors."""
     eps = self.variance_epsilon
+    if gemma:
+        return nt_gemma_rms_norm(x, weight, eps, residual)
     if residual is not None:
         return nt_fused_add_rms_norm(x, residual, weight, eps, inplace=True)
     hidden = weight.shape[0] if weight is not None else self.hidden_size

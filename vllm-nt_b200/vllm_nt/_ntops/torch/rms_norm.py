@@ -68,3 +68,28 @@ def fused_add_rms_norm(x, residual, weight, eps, inplace=False):
     out = x2 if inplace and x2.data_ptr() == x.data_ptr() else torch.empty_like(x2)
     ops().fused_add_rms_norm(out, res, x2, _weight(weight, hidden, x.dtype), float(eps))
     return out.view(x.shape), res.view(residual.shape)
+
+
+def gemma_rms_norm(x, weight, eps, residual=None):
+    """vLLM's GemmaRMSNorm.forward_native (vllm/model_executor/layers/layernorm.py:153-170)
+    on one kernel: out = x * rsqrt(mean(x^2) + eps) * (1 + w) with (1 + w) in fp32 and one
+    rounding of the product; ``weight`` is the raw Gemma parameter w.  With a residual the
+    sum is taken in the input dtype and ``(out, sum)`` is returned as new tensors, as vLLM's
+    native code returns them (neither input is modified).  fp16 with a residual is not
+    served (vLLM hands back an fp32 residual there)."""
+    if residual is None:
+        if x.is_contiguous() and _weight_ok(weight, x):
+            out = torch.empty_like(x)
+            ops().gemma_rms_norm(out, x, weight, float(eps))
+            return out
+        hidden = x.shape[-1]
+        x2 = _rows(x, hidden)
+        out = torch.empty_like(x2)
+        ops().gemma_rms_norm(out, x2, _weight(weight, hidden, x.dtype), float(eps))
+        return out.view(x.shape)
+    hidden = x.shape[-1]
+    x2 = _rows(x, hidden)
+    res = residual.reshape(-1, hidden).clone(memory_format=torch.contiguous_format)
+    out = torch.empty_like(x2)
+    ops().gemma_fused_add_rms_norm(out, res, x2, _weight(weight, hidden, x.dtype), float(eps))
+    return out.view(x.shape), res.view(residual.shape)
