@@ -689,8 +689,8 @@ def compact_ops(res: dict) -> dict:
 
 def compact_tp(res: dict) -> dict:
     """The row-parallel table as short rows of microseconds per call."""
-    cols = ("gemm_us", "allreduce_us", "serial_us", "peer_gemm_allreduce_us")
-    out = {"cols": "gemm,nccl_ar,gemm+nccl,gemm+peer_ar (us)"}
+    cols = ("gemm_us", "allreduce_us", "serial_us", "peer_gemm_allreduce_us", "peer_twoshot_gemm_allreduce_us")
+    out = {"cols": "gemm,nccl_ar,gemm+nccl,gemm+peer1,gemm+peer2 (us)"}
     for name, d in res.items():
         if name.startswith("_"):
             out[name] = d
@@ -782,30 +782,38 @@ def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
                 main.wait_stream(comm)
 
             out_peer = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
+            out_peer2 = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
 
             part = torch.empty(m, 4096, device=dev, dtype=torch.bfloat16)
 
             def peer():
                 o.linear(part, x, w, None, None)
-                par.reduce(part, out_peer, oneshot=True)
+                par.reduce(part, out_peer, method="oneshot")
 
-            for f in (gemm, allreduce, serial, pipelined, peer):
+            def peer2():
+                o.linear(part, x, w, None, None)
+                par.reduce(part, out_peer2, method="twoshot")
+
+            for f in (gemm, allreduce, serial, pipelined, peer, peer2):
                 f()
             torch.cuda.synchronize()
             t_gemm, t_ar, t_serial = timed(gemm), timed(allreduce), timed(serial)
             t_pipe = timed(pipelined, graph=False)
-            t_peer = timed(peer)
-            # the two paths agree (both sum this rank's bf16 partial with its peers')
+            t_peer, t_peer2 = timed(peer), timed(peer2)
+            # the paths agree (each sums this rank's bf16 partial with its peers')
             serial()
             peer()
+            peer2()
             torch.cuda.synchronize()
-            agree = float((out.float() - out_peer.float()).abs().max().item())
+            agree = float(max((out.float() - out_peer.float()).abs().max().item(),
+                              (out.float() - out_peer2.float()).abs().max().item()))
             res[f"{name} M={m}"] = {
                 "gemm_us": round(t_gemm * 1e3, 1),
                 "allreduce_us": round(t_ar * 1e3, 1),
                 "serial_us": round(t_serial * 1e3, 1),
                 "chunked_overlap_us": round(t_pipe * 1e3, 1),
                 "peer_gemm_allreduce_us": round(t_peer * 1e3, 1),
+                "peer_twoshot_gemm_allreduce_us": round(t_peer2 * 1e3, 1),
                 "peer_vs_nccl_max_abs_diff": round(agree, 4),
                 "allreduce_bytes": m * 4096 * 2,
                 "chunks": chunks,
@@ -817,7 +825,9 @@ def tp_projection_table(dev, n: int, rank: int, dist) -> dict:
 
 
 def run_linear_case(args) -> int:
-    """One GEMM shape, warmup + steps launches, for profiling (prints its own timing)."""
+    """One GEMM shape for profiling: warmup + steps eager launches (so that ncu can capture
+    one), then the device time per call of CUDA-graph replays over weight copies larger
+    than L2, as the per-op table times it (prints its own timings)."""
     from vllm_nt._ntops.torch._ext import ops
 
     m, n, k = args.linear_case
@@ -825,20 +835,15 @@ def run_linear_case(args) -> int:
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(0)
     x = torch.randn(m, k, device=dev, generator=g, dtype=torch.bfloat16)
-    w = 0.02 * torch.randn(n, k, device=dev, generator=g, dtype=torch.bfloat16)
+    copies = max(1, math.ceil(3 * L2_BYTES / (n * k * 2)))
+    ws = [0.02 * torch.randn(n, k, device=dev, generator=g, dtype=torch.bfloat16) for _ in range(copies)]
     out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
     o = ops()
-    for _ in range(args.warmup):
-        o.linear(out, x, w, None, None)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        o.linear(out, x, w, None, None)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    print(json.dumps({"linear_case": [m, n, k], "us": ms * 1e3, "TFLOP/s": 2.0 * m * n * k / (ms * 1e-3) / 1e12}))
+    ms = _time_calls(lambda: o.linear(out, x, ws[0], None, None), args.warmup, args.steps)
+    graph_us = time_graph([lambda w_=w_: o.linear(out, x, w_, None, None) for w_ in ws], max(8, 2 * copies)) * 1e3
+    print(json.dumps({"linear_case": [m, n, k], "us": ms * 1e3, "graph_us": round(graph_us, 2),
+                      "TFLOP/s": round(2.0 * m * n * k / (graph_us * 1e-6) / 1e12, 1),
+                      "GB/s": round((n * k * 2 + m * k * 2 + m * n * 2) / (graph_us * 1e-6) / 1e9, 1)}))
     return 0
 
 
@@ -894,7 +899,16 @@ def run_rope_cache_case(args) -> int:
     o = ops()
     ms = _time_calls(lambda: o.rope_and_cache_flash_layout(pos, q, k, v, cache, kv, slots, HEAD, HEAD, 0),
                      args.warmup, args.steps)
-    print(json.dumps({"rope_cache_case": t, "us": ms * 1e3}))
+
+    def pair():
+        o.rotary_embedding_neox(pos, q, k, cache, HEAD, HEAD)
+        o.store_flash_layout(k, v, kv, slots, 0)
+
+    fused_us = time_graph([lambda: o.rope_and_cache_flash_layout(pos, q, k, v, cache, kv, slots, HEAD, HEAD, 0)],
+                          10) * 1e3
+    pair_us = time_graph([pair], 10) * 1e3
+    print(json.dumps({"rope_cache_case": t, "us": ms * 1e3, "graph_us": round(fused_us, 2),
+                      "pair_graph_us": round(pair_us, 2)}))
     return 0
 
 
@@ -1127,6 +1141,21 @@ def main() -> int:
     ms_per_step = ms_max / args.steps
     value = batch * args.steps / (ms_max * 1e-3)
 
+    # the same call replayed from a CUDA graph (launch gaps removed): against the eager
+    # time above it separates the kernels' device time from the host's launch cost, per rank
+    graph_ms = time_graph([step], 20)
+    per_rank = torch.tensor([ms / args.steps, graph_ms, decode_bytes(ctx, hkv) / (graph_ms * 1e-3) / 1e9], device=dev)
+    if dist:
+        gathered = [torch.zeros_like(per_rank) for _ in range(n)]
+        dist.all_gather(gathered, per_rank)
+    else:
+        gathered = [per_rank]
+    rank_split = {
+        "eager_us_max": round(max(float(t[0]) for t in gathered) * 1e3, 1),
+        "graph_us_max": round(max(float(t[1]) for t in gathered) * 1e3, 1),
+        "graph_GB/s_min": round(min(float(t[2]) for t in gathered), 1),
+    }
+
     # roofline of this rank's decode call (split + combine launches)
     algo = decode_bytes(ctx, hkv)
     achieved = algo / (ms / args.steps * 1e-3) / 1e9
@@ -1228,6 +1257,7 @@ def main() -> int:
         "e2e": e2e,
         "gpu_launches": 2 * args.steps,  # split + combine per timed step
         "clocks": clocks,
+        "per_rank": rank_split,
     }
     # the full tables go to stderr; the line carries their compact form, so that the whole
     # line stays within a few thousand characters

@@ -391,6 +391,16 @@ int ntb200_allreduce_oneshot(void* out, const void* partial, const uint64_t* pee
                              int64_t numel, int64_t capacity, int rank, int world_size, int dtype,
                              void* stream);
 
+/* The same sum as a two-shot all-reduce (reduce-scatter, then all-gather) over the same
+ * buffers: rank r pushes chunk d of its partial to rank d, sums the W pieces of chunk r, and
+ * reads the other ranks' reduced chunks over NVLink.  Each rank moves 2 (W - 1) / W of the
+ * message over NVLink instead of the one-shot's (W - 1), at the cost of a second barrier: the
+ * form for messages of more than a few hundred KB.  numel must be a multiple of 8.  Calls of
+ * the two kinds may alternate on one buffer (every rank in the same order). */
+int ntb200_allreduce_twoshot(void* out, const void* partial, const uint64_t* peer_buffers,
+                             int64_t numel, int64_t capacity, int rank, int world_size, int dtype,
+                             void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -225,3 +225,32 @@ def test_linear_argmax_lm_head_vs_oracle(lm_head_case, m):
     assert len(diff) <= max(1, m // 50)
     if m > 3:
         assert int(got[3]) == 100 and int(want[3]) == 100
+
+
+def test_linear_small_m_is_deterministic_and_graph_replayable():
+    """The split-K partials are summed in a fixed order, so repeated calls give the same
+    bits; a CUDA graph of the torch op replays correctly several times in a row on new
+    inputs."""
+    from vllm_nt._ntops.torch.linear import linear
+
+    x, w, _ = _inputs(256, 4096, 6144, seed=91)
+    xd, wd = x.cuda(), w.cuda()
+    first = linear(xd, wd)
+    for _ in range(3):
+        assert torch.equal(linear(xd, wd), first)
+    torch.testing.assert_close(first.float().cpu(), oracle.linear(x, w), rtol=TOL, atol=TOL)
+    out = torch.empty_like(first)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        out.copy_(linear(xd, wd))
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out.copy_(linear(xd, wd))
+    for i in range(4):
+        out.zero_()
+        xd.copy_((x * (i + 1)).cuda())
+        graph.replay()
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float().cpu(), oracle.linear(x * (i + 1), w), rtol=TOL, atol=TOL * (i + 1))

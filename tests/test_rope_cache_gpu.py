@@ -130,8 +130,9 @@ def test_partial_rotary_scalar_path_int32_padded_rows(dtype):
 @pytest.mark.parametrize("t", [1024, 4096])
 def test_flashinfer_hnd_cache_matches_oracle_and_unfused_kernels(t):
     """FlashInfer's cache [blocks, 2, 16, H, D] in HND memory order (kv_dim 1, head stride
-    16 x 128) at prefill-sized steps (1024 and 4096 tokens: many work units per warp).  The
-    fused kernel leaves the oracle's bits, and the same bits as calling the two kernels."""
+    16 x 128) at prefill-sized steps: 1024 tokens (the fused kernel) and 4096 tokens (the
+    entry point launches the RoPE and KV-store kernels from 4096 tokens on).  Both leave the
+    oracle's bits, and the same bits as calling the two kernels directly."""
     dev = cuda_device()
     hq, hk, d = 32, 8, 128
     buf, q, k, v = _qkv(t, hq, hk, d, torch.bfloat16, 26)

@@ -599,25 +599,38 @@ void linear_argmax(at::Tensor out_index, const at::Tensor& x_in, const at::Tenso
         "linear_argmax");
 }
 
-// out = sum over ranks of their partials (see ntb200_allreduce_oneshot); peer_buffers is an
-// int64 CUDA tensor of the world's buffer addresses.
-void allreduce_oneshot(at::Tensor out, const at::Tensor& partial, const at::Tensor& peer_buffers, int64_t capacity,
-                       int64_t rank, int64_t world_size) {
+// out = sum over ranks of their partials (see ntb200_allreduce_oneshot / _twoshot);
+// peer_buffers is an int64 CUDA tensor of the world's buffer addresses.
+using AllreduceFn = int (*)(void*, const void*, const uint64_t*, int64_t, int64_t, int, int, int, void*);
+
+void allreduce_call(AllreduceFn fn, const char* name, at::Tensor& out, const at::Tensor& partial,
+                    const at::Tensor& peer_buffers, int64_t capacity, int64_t rank, int64_t world_size) {
   require_cuda(out, "out");
   require_cuda(partial, "partial");
   require_cuda(peer_buffers, "peer_buffers");
   TORCH_CHECK(out.is_contiguous() && partial.is_contiguous() && out.numel() == partial.numel() &&
                   out.scalar_type() == partial.scalar_type(),
-              "ntb200.allreduce_oneshot: out and partial must be contiguous, of one size and dtype");
+              "ntb200.", name, ": out and partial must be contiguous, of one size and dtype");
   TORCH_CHECK(peer_buffers.scalar_type() == at::kLong && peer_buffers.is_contiguous() &&
                   peer_buffers.numel() == world_size,
-              "ntb200.allreduce_oneshot: peer_buffers must be int64 [world_size]");
+              "ntb200.", name, ": peer_buffers must be int64 [world_size]");
   c10::cuda::CUDAGuard guard(out.device());
-  check(ntb200_allreduce_oneshot(out.data_ptr(), partial.data_ptr(),
-                                 reinterpret_cast<const uint64_t*>(peer_buffers.data_ptr()), out.numel(), capacity,
-                                 static_cast<int>(rank), static_cast<int>(world_size), dtype_code(out),
-                                 stream_of(out)),
-        "allreduce_oneshot");
+  check(fn(out.data_ptr(), partial.data_ptr(), reinterpret_cast<const uint64_t*>(peer_buffers.data_ptr()),
+           out.numel(), capacity, static_cast<int>(rank), static_cast<int>(world_size), dtype_code(out),
+           stream_of(out)),
+        name);
+}
+
+void allreduce_oneshot(at::Tensor out, const at::Tensor& partial, const at::Tensor& peer_buffers, int64_t capacity,
+                       int64_t rank, int64_t world_size) {
+  allreduce_call(&ntb200_allreduce_oneshot, "allreduce_oneshot", out, partial, peer_buffers, capacity, rank,
+                 world_size);
+}
+
+void allreduce_twoshot(at::Tensor out, const at::Tensor& partial, const at::Tensor& peer_buffers, int64_t capacity,
+                       int64_t rank, int64_t world_size) {
+  allreduce_call(&ntb200_allreduce_twoshot, "allreduce_twoshot", out, partial, peer_buffers, capacity, rank,
+                 world_size);
 }
 
 int64_t allreduce_buffer_size(int64_t capacity, int64_t elem_bytes, int64_t world_size) {
@@ -736,6 +749,9 @@ TORCH_LIBRARY(ntb200, m) {
   m.def(
       "allreduce_oneshot(Tensor(a!) out, Tensor partial, Tensor peer_buffers, int capacity, int rank, "
       "int world_size) -> ()");
+  m.def(
+      "allreduce_twoshot(Tensor(a!) out, Tensor partial, Tensor peer_buffers, int capacity, int rank, "
+      "int world_size) -> ()");
   m.def("allreduce_buffer_size(int capacity, int elem_bytes, int world_size) -> int", &allreduce_buffer_size);
   m.def("top_k_top_p(Tensor(a!) logits, Tensor? k, Tensor? p) -> ()");
   m.def("random_sample(Tensor(a!) out, Tensor probs, Tensor q) -> ()");
@@ -757,6 +773,7 @@ TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("store_flash_layout", &store_flash_layout);
   m.impl("linear", &linear);
   m.impl("allreduce_oneshot", &allreduce_oneshot);
+  m.impl("allreduce_twoshot", &allreduce_twoshot);
   m.impl("linear_silu_and_mul", &linear_silu_and_mul);
   m.impl("linear_argmax", &linear_argmax);
   m.impl("paged_attention_prefill", &paged_attention_prefill);

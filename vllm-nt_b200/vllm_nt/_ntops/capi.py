@@ -117,6 +117,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ntb200_allreduce_oneshot": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p]
     ),
+    "ntb200_allreduce_twoshot": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_void_p]
+    ),
 }
 
 

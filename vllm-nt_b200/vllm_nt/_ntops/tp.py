@@ -6,8 +6,9 @@ rank and sums the partials with an NCCL all-reduce
 tensor_model_parallel_all_reduce).  Here the GEMM writes its partial into local memory and
 ``ntb200_allreduce_oneshot`` pushes it over NVLink into every rank's peer-mapped buffer
 (torch symmetric memory), meets the other ranks at one barrier and sums the pushed
-partials: two kernels of this library back to back (the second launched as a programmatic
-dependent of the first), no NCCL call.
+partials; for larger messages ``ntb200_allreduce_twoshot`` reduce-scatters and
+all-gathers over the same buffers instead.  Two kernels of this library back to back (the
+second launched as a programmatic dependent of the first), no NCCL call.
 
 Every rank must make the same sequence of calls on its buffer.  The call count lives in
 the buffer on the device, so the GEMM + all-reduce pair can be captured in a CUDA graph.
@@ -39,26 +40,52 @@ class PeerAllReduce:
         self.rank = int(self.handle.rank)
         self.world_size = int(self.handle.world_size)
         self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=self.device)
-        # The one-shot push moves (W-1) x bytes per rank over NVLink; measured on B200s it
-        # beats NCCL up to about 16 MB / (W-1) (8 MB at W=2, 1 MB at W=8) and loses beyond,
-        # where NCCL's bandwidth-optimal algorithms take over.
-        self.oneshot_max_bytes = (16 << 20) // max(1, self.world_size - 1)
+        # The one-shot push moves (W-1) x bytes per rank over NVLink and needs one barrier;
+        # the two-shot form moves 2 (W-1)/W x bytes and needs two.  One-shot for small
+        # messages (latency), two-shot up to the buffer's capacity (bandwidth), NCCL beyond.
+        self.oneshot_max_bytes = (2 << 20) // max(1, self.world_size - 1)
         # no rank may write a peer's flags before every rank has cleared its own buffer
         dist.barrier(group=self.group)
 
-    def reduce(self, partial: torch.Tensor, out: torch.Tensor | None = None, oneshot: bool | None = None) -> torch.Tensor:
-        """Sums ``partial`` (contiguous) over all ranks: the one-shot push up to
-        ``oneshot_max_bytes`` (and ``capacity``), NCCL beyond.  Every rank takes the same
-        branch, since the sizes are the same on every rank."""
+    def method_for(self, partial: torch.Tensor) -> str:
+        """The path ``reduce`` takes for ``partial`` by default; the same on every rank,
+        since the sizes are."""
+        if partial.numel() > self.capacity:
+            return "nccl"
+        if partial.numel() * partial.element_size() <= self.oneshot_max_bytes or partial.numel() % 8:
+            return "oneshot"
+        return "twoshot"
+
+    def reduce(self, partial: torch.Tensor, out: torch.Tensor | None = None, oneshot: bool | None = None,
+               method: str | None = None, check: bool = False) -> torch.Tensor:
+        """Sums ``partial`` (contiguous) over all ranks into ``out``.  ``method`` is
+        "oneshot", "twoshot" or "nccl" (default: ``method_for``); ``oneshot=True/False`` is
+        the older spelling of "oneshot"/"nccl".  Every rank must call with the same method.
+
+        A peer that does not reach a call within ~2 s makes the kernel give up the wait: it
+        sets the device error word (NTB200_DEVERR_WAIT_TIMEOUT) and ``out`` is then not the
+        sum.  Read the word at a step boundary (``capi.read_device_error``), or pass
+        ``check=True``, which synchronises the stream after the call and raises on it."""
         if out is None:
             out = torch.empty_like(partial)
-        if oneshot is None:
-            oneshot = partial.numel() * partial.element_size() <= self.oneshot_max_bytes
-        if not oneshot or partial.numel() > self.capacity:
+        if method is None:
+            method = self.method_for(partial) if oneshot is None else ("oneshot" if oneshot else "nccl")
+        if method != "nccl" and partial.numel() > self.capacity:
+            method = "nccl"
+        if method == "twoshot" and partial.numel() % 8:
+            method = "oneshot"
+        if method == "nccl":
             out.copy_(partial)
             dist.all_reduce(out, group=self.group)
             return out
-        ops().allreduce_oneshot(out, partial, self.peers, self.capacity, self.rank, self.world_size)
+        fn = ops().allreduce_twoshot if method == "twoshot" else ops().allreduce_oneshot
+        fn(out, partial, self.peers, self.capacity, self.rank, self.world_size)
+        if check:
+            from vllm_nt._ntops import capi
+
+            word = capi.read_device_error(torch.cuda.current_stream(self.device).cuda_stream)
+            if word & capi.DEVERR_WAIT_TIMEOUT:
+                raise RuntimeError(f"peer all-reduce on rank {self.rank}: a peer did not arrive (device error {word})")
         return out
 
     def linear(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
