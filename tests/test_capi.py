@@ -101,7 +101,10 @@ def test_workspace_queries():
     assert lib.ntb200_linear_workspace_size(1, 4096, 4096) == 0
     # peer all-reduce buffer: 8 KiB of flags + a 256-byte header + two parities x W ranks
     # of the capacity rounded to 256 B
-    assert lib.ntb200_allreduce_buffer_size(1000, 2, 4) == 8192 + 256 + 2 * 4 * 2048
+    # two flag arrays, the header, the one-shot parity slots (2 x 4 x 2048 B: 1000 bf16
+    # rounded to 256 B), then the two-shot scatter slots and reduced chunk (5 x 512 B:
+    # ceil(1000 / 4) = 250 -> 256 elements)
+    assert lib.ntb200_allreduce_buffer_size(1000, 2, 4) == 2 * 8192 + 256 + 2 * 4 * 2048 + 5 * 512
     assert lib.ntb200_allreduce_buffer_size(1000, 2, 9) == 0
     # LM-head argmax: one 8-byte key per row (256-aligned) while the logits stay on chip
     # (M <= 256); beyond, the [M, V] logits as well
