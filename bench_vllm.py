@@ -79,7 +79,8 @@ def _worker_usage(worker=None) -> dict:
 
     s = get_usage_summary()
     return {"hit_ops": list(s["hit_ops"]),
-            "operators": {k: {"hits": v["hits"], "failures": v["failures"]} for k, v in s["operators"].items()}}
+            "operators": {k: {"hits": v["hits"], "failures": v["failures"], "fallbacks": v["fallbacks"],
+                              "declined": v.get("declined", {})} for k, v in s["operators"].items()}}
 
 
 def child(args) -> int:
@@ -130,22 +131,25 @@ def child(args) -> int:
     }
     if args.mode == "b200":
         try:
-            if args.tp > 1:
-                # tensor-parallel workers are other processes: ask each for its counters
-                per_rank = llm.collective_rpc(_worker_usage)
-                s = {"hit_ops": sorted({op for r in per_rank for op in r["hit_ops"]}), "operators": {}}
-                for r in per_rank:
-                    for k, v in r["operators"].items():
-                        acc = s["operators"].setdefault(k, {"hits": 0, "failures": 0})
-                        acc["hits"] += v["hits"]
-                        acc["failures"] += v["failures"]
-            else:
-                from vllm_nt.oot import get_usage_summary
-
-                s = get_usage_summary()
+            # tensor-parallel workers are other processes: ask each for its counters
+            per_rank = llm.collective_rpc(_worker_usage) if args.tp > 1 else [_worker_usage()]
+            s = {"hit_ops": sorted({op for r in per_rank for op in r["hit_ops"]}), "operators": {}}
+            for r in per_rank:
+                for k, v in r["operators"].items():
+                    acc = s["operators"].setdefault(k, {"hits": 0, "failures": 0, "fallbacks": 0, "declined": {}})
+                    for c in ("hits", "failures", "fallbacks"):
+                        acc[c] += v[c]
+                    for why, n in v["declined"].items():
+                        acc["declined"][why] = acc["declined"].get(why, 0) + n
+            ops_ = s["operators"]
             result["hit_ops"] = s["hit_ops"]
-            result["hits"] = {k: v["hits"] for k, v in s["operators"].items() if v["hits"]}
-            result["failures"] = {k: v["failures"] for k, v in s["operators"].items() if v["failures"]}
+            result["hits"] = {k: v["hits"] for k, v in ops_.items() if v["hits"]}
+            result["failures"] = {k: v["failures"] for k, v in ops_.items() if v["failures"]}
+            result["fallbacks"] = {k: v["fallbacks"] for k, v in ops_.items() if v["fallbacks"]}
+            result["declined"] = {k: v["declined"] for k, v in ops_.items() if v["declined"]}
+            # share of the routed calls of the hooked ops that ran on the kernels
+            calls = sum(v["hits"] + v["fallbacks"] for v in ops_.values())
+            result["kernel_hit_fraction"] = round(sum(v["hits"] for v in ops_.values()) / calls, 5) if calls else None
         except Exception as exc:  # noqa: BLE001 - the counters are reported, not required
             result["usage_summary_error"] = str(exc)
     print("RESULT_JSON=" + json.dumps(result), flush=True)

@@ -237,3 +237,57 @@ def test_flashinfer_impl_hooks_store_and_decode(_b200_config, layout):
     torch.testing.assert_close(out[:3].view(3, 32, 128).float().cpu(), ref, **TOL)
     assert not out[3].any()
     assert _hits(patching, "StoreKVCache") == 1 and _hits(patching, "PagedAttentionDecode") == 1
+
+
+def test_fused_rope_kv_store_attention_hook(_b200_config, vllm_ctx, monkeypatch):
+    """The opt-in LlamaAttention.forward patch: RoPE of q/k and the KV store in one kernel
+    (bit-identical to the RoPE hook followed by the KV-store hook), then the layer's own
+    KV-store call finds its rows stored and returns without storing again."""
+    from vllm.model_executor.layers.attention import attention as vattn
+    from vllm.model_executor.layers.rotary_embedding.base import RotaryEmbedding
+
+    patching = _b200_config
+    rope = RotaryEmbedding(128, 128, 4096, 500000.0, True, torch.bfloat16).cuda()
+    g = seeded(41)
+    t, hq, hk, nb = 6, 32, 8, 32
+    qkv = torch.randn(t, (hq + 2 * hk) * 128, generator=g).to(torch.bfloat16)
+    pos = torch.randint(0, 4096, (t,), generator=g)
+    kv0 = torch.randn(2, nb, 16, hk, 128, generator=g).to(torch.bfloat16)
+    slots = torch.randperm(nb * 16, generator=g)[:t - 1]  # the last row is vLLM padding
+    kvd, slots_d = kv0.cuda(), slots.cuda()
+
+    class FlashAttentionImpl:  # the impl class the hooks recognise, with a supported config
+        num_heads, num_kv_heads, head_size, scale = hq, hk, 128, 1.0
+        attn_type, kv_cache_dtype, alibi_slopes, logits_soft_cap, sinks = "decoder", "auto", None, None, None
+        sliding_window, dcp_world_size = None, 1
+
+    store = patching._build_flash_attn_kv_update(lambda *a, **k: pytest.fail("the KV store ran twice"))
+
+    class Attn:
+        layer_name = "model.layers.0.self_attn.attn"
+        impl = FlashAttentionImpl()
+        kv_sharing_target_layer_name = None
+        attn_backend = SimpleNamespace(forward_includes_kv_cache_update=False)
+
+        def __call__(self, q, k, v):
+            store(self.impl, self, k.view(-1, hk, 128), v.view(-1, hk, 128), kvd, slots_d)
+            return q
+
+    attn = Attn()
+    monkeypatch.setattr(vattn, "get_attention_context", lambda name: (None, attn, kvd, slots_d))
+    qkvd = qkv.cuda()
+    module = SimpleNamespace(qkv_proj=lambda h: (qkvd, None), q_size=hq * 128, kv_size=hk * 128, rotary_emb=rope,
+                             attn=attn, o_proj=lambda a: (a, None))
+    fwd = patching._build_attention_rope_kv_forward(lambda *a, **k: pytest.fail("fell back to vLLM"))
+    out = fwd(module, pos.cuda(), None)
+    torch.cuda.synchronize()
+    cache = rope.cos_sin_cache.float().cpu()
+    ref_q, ref_k = oracle.rope_neox(pos, qkv[:, : hq * 128], qkv[:, hq * 128 : (hq + hk) * 128], cache, 128, 128)
+    assert bits_equal(out.cpu().contiguous(), ref_q.contiguous())
+    ref_kv = kv0.clone()
+    v = qkv[:, (hq + hk) * 128 :]
+    ref_kv[0][slots // 16, slots % 16] = ref_k[: t - 1].reshape(t - 1, hk, 128)
+    ref_kv[1][slots // 16, slots % 16] = v[: t - 1].reshape(t - 1, hk, 128)
+    assert bits_equal(kvd.cpu(), ref_kv)
+    assert not getattr(attn, "_ntb200_kv_stored", False)
+    assert _hits(patching, "RoPEKVCache") == 1 and _hits(patching, "StoreKVCache") == 1

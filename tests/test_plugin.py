@@ -390,3 +390,30 @@ def test_sampler_patches_follow_the_config(monkeypatch):
     assert {"TopKTopP", "RandomSample", "RejectionSample"} <= enabled()
     monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/original-only.yaml"))
     assert not {"TopKTopP", "RandomSample"} & enabled()
+
+
+def test_fused_rope_kv_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypatch):
+    """RoPEKVCache (LlamaAttention.forward) applies only when the config names it; a module
+    whose rotary embedding is not vLLM's base RotaryEmbedding runs vLLM's path (rotary_emb,
+    then attn) and the call is counted as declined with its reason."""
+    spec = next(s for s in patching._FUNCTION_PATCH_SPECS if s.patch_id == "RoPEKVCache")
+    config.reset_backend_config_cache()
+    assert patching._function_patch_enabled(spec)  # all-b200.yaml names it
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/hybrid-default.yaml"))
+    config.reset_backend_config_cache()
+    assert not patching._function_patch_enabled(spec)
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml"))
+    config.reset_backend_config_cache()
+
+    calls = []
+    qkv = torch.zeros(3, 6)
+    module = SimpleNamespace(
+        qkv_proj=lambda h: (qkv, None), q_size=4, kv_size=1,
+        rotary_emb=lambda p, q, k: (calls.append("rope"), (q, k))[1],
+        attn=lambda q, k, v: (calls.append("attn"), q)[1],
+        o_proj=lambda a: (a, None))
+    fwd = patching._build_attention_rope_kv_forward(lambda *a: pytest.fail("the patch replaces forward"))
+    out = fwd(module, torch.arange(3), None)
+    assert calls == ["rope", "attn"] and out.shape == (3, 4)
+    op = patching.get_usage_summary()["operators"]["RoPEKVCache"]
+    assert op["hits"] == 0 and op["declined"] == {"not the base RotaryEmbedding": 1}

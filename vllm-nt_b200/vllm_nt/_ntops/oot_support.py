@@ -108,6 +108,16 @@ def store_kv_cache(key, value, k_cache, v_cache, slot_mapping):
     return nt_store_kvcache(key, value, k_cache, v_cache, slot_mapping)
 
 
+def rope_and_store_kv_cache_flash(positions, query, key, value, cos_sin_cache, head_size, rotary_dim, kv_cache,
+                                  slot_mapping, kv_dim=0):
+    """NeoX RoPE of q/k (in place) and the slot-mapped store of the rotated k and the v into
+    vLLM's combined cache tensor (kv_dim as in store_kv_cache_flash), one kernel for a
+    decode step: the RoPE hook and the KV-store hook of one attention layer fused."""
+    cache = cos_sin_cache if cos_sin_cache.dtype == query.dtype else cos_sin_cache.to(query.dtype)
+    ops().rope_and_cache_flash_layout(positions.reshape(-1), query, key, value, cache, kv_cache, slot_mapping,
+                                      int(head_size), int(rotary_dim), int(kv_dim))
+
+
 def store_kv_cache_flash(key, value, kv_cache, slot_mapping, kv_dim=0):
     """The KV store on vLLM's combined cache tensor in one op call: kv_dim 0 is
     FlashAttention's [2, blocks, block_size, kv_heads, head_size], kv_dim 1 FlashInfer's

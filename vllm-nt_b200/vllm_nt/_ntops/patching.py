@@ -64,6 +64,7 @@ from vllm_nt._ntops.oot_support import (
     paged_attention_decode_flash,
     paged_attention_flash,
     rope,
+    rope_and_store_kv_cache_flash,
     store_kv_cache,  # noqa: F401
     store_kv_cache_flash,
 )
@@ -84,7 +85,7 @@ _FUNCTION_PATCH_FEATURES = dict.fromkeys(
 _OPERATOR_FEATURES = {"MatMul": "MM", "LMHead": "MM"}
 # Patches this build adds beyond the reference's op set: applied only when the config
 # names the op with a kernel backend, so configs written for the reference run unchanged.
-_OPT_IN_PATCHES = frozenset({"GateUpSiluAndMul"})
+_OPT_IN_PATCHES = frozenset({"GateUpSiluAndMul", "RoPEKVCache"})
 _HALF_TYPES = (torch.bfloat16, torch.float16)
 _FLOAT_TYPES = (torch.float32, torch.bfloat16, torch.float16)
 
@@ -133,7 +134,7 @@ _REGISTERED_VIA_PRIORITY = {via: rank for rank, via in enumerate(_VIA_ORDER)}
 _OPERATOR_NAMES = (
     "RMSNorm", "SiluAndMul", "GemmaRMSNorm", "MulAndSilu", "GeluAndMul", "GELU", "LayerNorm", "MatMul", "Embedding",
     "WPE", "NTWPEKernel", "LMHead", "PagedAttentionPrefill", "PagedAttentionDecode", "StoreKVCache",
-    "GateUpSiluAndMul", "RoPE", "SDPA", "TopKTopP", "RandomSample", "RejectionSample",
+    "GateUpSiluAndMul", "RoPE", "RoPEKVCache", "SDPA", "TopKTopP", "RandomSample", "RejectionSample",
 )
 _OPERATOR_STATS: dict[str, OperatorStats] = {}
 
@@ -515,6 +516,11 @@ def _kv_update_builder(patch_id: str, kv_dim: int) -> Callable[[object], object]
         original_fn = cast(Callable[..., Any], original)
 
         def do_kv_cache_update(self, layer, key, value, kv_cache, slot_mapping):
+            if getattr(layer, "_ntb200_kv_stored", False):
+                # the fused RoPE + KV-store kernel of this layer's forward stored these rows
+                layer._ntb200_kv_stored = False
+                _record_hit("StoreKVCache", key)
+                return None
             vllm_path = lambda: original_fn(self, layer, key, value, kv_cache, slot_mapping)  # noqa: E731
             reason = "not a CUDA tensor" if not key.is_cuda else _attn_impl_reason(self, key.dtype, kv_cache, kv_dim)
             if reason:
@@ -682,6 +688,87 @@ def _build_mlp_forward(original: object) -> object:
     return _mark_function_patch(forward, "GateUpSiluAndMul")
 
 
+_KV_DIM_BY_IMPL = {"FlashAttentionImpl": 0, "FlashInferImpl": 1}
+
+
+def _why_not_fused_rope_kv(attn_mod: Any, q: torch.Tensor) -> str | None:
+    """The attention module's RoPE is the plain NeoX RotaryEmbedding whose forward the RoPE
+    hook serves, and its attention layer stores K/V through one of the hooked impls."""
+    from vllm.model_executor.layers.rotary_embedding.base import RotaryEmbedding
+
+    rot = getattr(attn_mod, "rotary_emb", None)
+    layer = getattr(attn_mod, "attn", None)
+    impl = getattr(layer, "impl", None)
+    if not isinstance(rot, RotaryEmbedding) or type(rot).forward_cuda is not RotaryEmbedding.forward_cuda:
+        return "not the base RotaryEmbedding"
+    if not rot.is_neox_style or rot.rotary_dim % 2:
+        return "not NeoX style / odd rotary_dim"
+    if type(impl).__name__ not in _KV_DIM_BY_IMPL:
+        return "attention impl without a hooked KV store"
+    if getattr(layer, "kv_sharing_target_layer_name", None) is not None or getattr(
+            getattr(layer, "attn_backend", None), "forward_includes_kv_cache_update", False):
+        return "layer does not store its own K/V"
+    if not q.is_cuda or q.dtype not in _HALF_TYPES:
+        return "not a CUDA 16-bit tensor"
+    if not backends.backend_enabled("StoreKVCache") or "StoreKVCache" in _disabled_ops():
+        return "KV-store hook disabled"
+    return None
+
+
+def _build_attention_rope_kv_forward(original: object) -> object:
+    """Replacement for LlamaAttention.forward (and attention modules of the same shape):
+    the RoPE of q/k and the KV store of the rotated k and the v become one kernel
+    (ntb200_rope_and_cache); the layer's own KV-store call then finds its rows stored and
+    returns.  Prefill-sized calls take the two kernels inside the same entry point."""
+    if _already(original, "RoPEKVCache"):
+        return original
+    original_fn = cast(Callable[..., Any], original)
+
+    def forward(self, positions, hidden_states):
+        qkv, _ = self.qkv_proj(hidden_states)
+        q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
+        reason = _why_not_fused_rope_kv(self, q)
+        slot_mapping = kv_cache = None
+        if reason is None:
+            from vllm.model_executor.layers.attention.attention import get_attention_context
+
+            try:
+                _, _, kv_cache, slot_mapping = get_attention_context(self.attn.layer_name)
+            except Exception:  # noqa: BLE001 - no forward context (e.g. a bare module call)
+                reason = "no forward context"
+            if reason is None and slot_mapping is None:
+                reason = "no slot mapping (profiling run)"
+            if reason is None:
+                reason = _attn_impl_reason(self.attn.impl, q.dtype, kv_cache, _KV_DIM_BY_IMPL[type(self.attn.impl).__name__])
+        if reason:
+            if backends.stats_enabled():
+                entry = _stats("RoPEKVCache")
+                entry.declined[reason] = entry.declined.get(reason, 0) + 1
+                backends.record_fallback("RoPEKVCache", "original")
+            q, k = self.rotary_emb(positions, q, k)
+            attn_output = self.attn(q, k, v)
+        else:
+            rot = self.rotary_emb
+            cache = rot._match_cos_sin_cache_dtype(q)
+            if cache is None:
+                cache = rot.cos_sin_cache
+            kv_dim = _KV_DIM_BY_IMPL[type(self.attn.impl).__name__]
+
+            def kernels():
+                _record_hit("RoPEKVCache", q)
+                rope_and_store_kv_cache_flash(positions, q, k, v, cache, rot.head_size, rot.rotary_dim, kv_cache,
+                                              slot_mapping, kv_dim)
+                self.attn._ntb200_kv_stored = True
+                return q, k
+
+            q, k = _route("RoPEKVCache", lambda: self.rotary_emb(positions, q, k), kernels)
+            attn_output = self.attn(q, k, v)
+        output, _ = self.o_proj(attn_output)
+        return output
+
+    return _mark_function_patch(forward, "RoPEKVCache")
+
+
 def _why_not_sampler_rows(x: torch.Tensor) -> str | None:
     """The sampler kernels take fp32 rows on a CUDA device with unit vocabulary stride."""
     if not x.is_cuda:
@@ -812,6 +899,8 @@ _FUNCTION_PATCH_SPECS: tuple[FunctionPatchSpec, ...] = (
         for mod, cls in (("vllm.model_executor.models.llama", "LlamaMLP"),
                          ("vllm.model_executor.models.qwen2", "Qwen2MLP"))
     ),
+    FunctionPatchSpec("RoPEKVCache", "vllm.model_executor.models.llama", "forward", "LlamaAttention", False,
+                      _build_attention_rope_kv_forward),
 )
 
 _APPLIED_FUNCTION_PATCHES: list[_AppliedFunctionPatch] = []
