@@ -160,6 +160,10 @@ def launch(args, base: Path, model_dir: Path, gpus: str, tp: int, log: Path) -> 
     env = dict(os.environ)
     env["CUDA_VISIBLE_DEVICES"] = gpus
     env["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0" if tp == 1 else "1"
+    if tp > 1:
+        # the per-rank counters are collected with collective_rpc on a plain function, which
+        # vLLM serialises for its worker processes only with pickle allowed
+        env["VLLM_ALLOW_INSECURE_SERIALIZATION"] = "1"
     paths = [str(ROOT)]
     if args.mode == "b200":
         paths += [str(write_plugin_dist(base)), str(PKG)]

@@ -977,6 +977,9 @@ def _apply_function_patches() -> None:
         applied.append(_AppliedFunctionPatch(spec, owner, current))
         if spec.patch_id in _OPERATOR_STATS:
             _note_registration(spec.patch_id, "function_patch")
+        if spec.patch_id == "PagedAttentionDecode" and spec.module_path == _FA_MODULE:
+            # the FlashAttention forward patch serves prefill batches too
+            _note_registration("PagedAttentionPrefill", "function_patch")
     _APPLIED_FUNCTION_PATCHES = applied
 
 
