@@ -1060,6 +1060,8 @@ def main() -> int:
                     help="profiling: run only the top-k/top-p mask over [B, V] logits, warmup+steps times")
     ap.add_argument("--rope-cache-case", type=int, metavar="T",
                     help="profiling: run only the fused RoPE + KV store over T tokens, warmup+steps times")
+    ap.add_argument("--shard-of", type=int, default=0, metavar="S",
+                    help="profiling: one process runs rank 0's share of an S-way KV-head split of the decode")
     ap.add_argument("--op-case", choices=OP_CASES,
                     help="profiling: run only one memory-bound op at its benchmark size, warmup+steps times")
     args = ap.parse_args()
@@ -1100,8 +1102,10 @@ def main() -> int:
     ctx, table, q_all = workload(0, batch, pool)
     from vllm_nt._ntops import sharding
 
-    h0, h1 = sharding.kv_head_range(rank, n, HKV)
-    q0, q1 = sharding.q_head_range(rank, n, HQ, HKV)
+    # --shard-of S (profiling, one process): run rank 0's share of an S-way KV-head split
+    split = args.shard_of if args.shard_of else n
+    h0, h1 = sharding.kv_head_range(rank, split, HKV)
+    q0, q1 = sharding.q_head_range(rank, split, HQ, HKV)
     hkv, hq = h1 - h0, q1 - q0
     q = q_all[:, q0:q1].contiguous()
     gk = torch.Generator(device=dev).manual_seed(1000 + rank)
@@ -1250,8 +1254,8 @@ def main() -> int:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": workload_config(n) if batch == BATCH and pool == POOL else
-        {**workload_config(n), "profiling_case": f"batch {batch}, pool {pool}"},
+        "config": workload_config(n) if batch == BATCH and pool == POOL and not args.shard_of else
+        {**workload_config(n), "profiling_case": f"batch {batch}, pool {pool}, shard 1 of {args.shard_of or 1}"},
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
