@@ -87,7 +87,10 @@ def test_linear_m8192_row_subset(k, n):
 
 
 @pytest.mark.parametrize("m,k,n", [(200, 72, 300), (5, 32, 12), (129, 4096, 257), (1, 8, 8), (300, 136, 257), (1000, 4096, 640),
-                                   (2100, 136, 520), (2048, 64, 256), (2304, 4096, 200), (4352, 6144, 520)])
+                                   (2100, 136, 520), (2048, 64, 256), (2304, 4096, 200), (4352, 6144, 520),
+                                   # 256-row weight tiles (decode batches): K split over a cluster with
+                                   # ragged N and K; one and two token tiles without a split
+                                   (100, 4104, 6200), (3, 264, 6400), (200, 136, 37000), (129, 72, 36000)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_linear_tails_and_bias_capi(m, k, n, dtype):
     x, w, b = _inputs(m, k, n, seed=m * 7 + n, dtype=dtype, bias=True)
@@ -131,11 +134,12 @@ def test_linear_rejects_unaligned_and_fp32():
 
 
 @pytest.mark.parametrize("m,k,i", [(1, 4096, 14336), (16, 4096, 14336), (256, 4096, 14336), (200, 72, 300),
-                                   (1000, 4096, 1792), (2048, 4096, 14336), (2300, 136, 520)])
+                                   (1000, 4096, 1792), (2048, 4096, 14336), (2300, 136, 520), (100, 136, 14400)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_linear_silu_and_mul_fused_capi(m, k, i, dtype):
-    """Fused gate_up + SiluAndMul over every path (swap-AB M <= 256, single CTA, CTA pairs)
-    against the oracle's unfused pair; I not a multiple of the tile covers the tail."""
+    """Fused gate_up + SiluAndMul over every path (256-row gate/up tiles and swap-AB at
+    M <= 256, single CTA, CTA pairs) against the oracle's unfused pair; I not a multiple of
+    the tile covers the tail."""
     x, w, _ = _inputs(m, k, 2 * i, seed=m + k + i)
     xd, wd = x.to(dtype).cuda(), w.to(dtype).cuda()
     out = torch.full((m, i), 5.0, dtype=dtype, device="cuda")
@@ -143,6 +147,20 @@ def test_linear_silu_and_mul_fused_capi(m, k, i, dtype):
     torch.cuda.synchronize()
     ref = oracle.silu_and_mul(oracle.linear(x.to(dtype), w.to(dtype)).to(dtype))
     torch.testing.assert_close(out.float().cpu(), ref.float(), rtol=TOL, atol=TOL)
+
+
+def test_linear_silu_and_mul_decode_batch_matches_unfused_pair_exactly():
+    """At a decode batch (M = 200, I = 14336) both the fused op and the unfused GEMM use
+    256-row weight tiles without a K split, so each gate and up value is the same dot
+    product in the same order: the two agree bit for bit."""
+    from vllm_nt._ntops.torch.linear import linear, linear_silu_and_mul
+    from vllm_nt._ntops.torch.silu import silu_and_mul
+
+    dev = cuda_device()
+    gd = torch.Generator(device=dev).manual_seed(78)
+    x = torch.randn(200, 4096, generator=gd, device=dev, dtype=torch.bfloat16)
+    w = 0.02 * torch.randn(2 * 14336, 4096, generator=gd, device=dev, dtype=torch.bfloat16)
+    assert torch.equal(linear_silu_and_mul(x, w), silu_and_mul(linear(x, w)))
 
 
 def test_linear_silu_and_mul_matches_unfused_pair_exactly():

@@ -83,7 +83,7 @@ bool pdl_enabled() {
 }
 
 namespace {
-constexpr int kAttrSlots = 96;
+constexpr int kAttrSlots = 128;
 std::atomic<int> g_attr_done[kMaxDevices][kAttrSlots];
 }  // namespace
 

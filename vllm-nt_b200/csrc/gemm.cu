@@ -601,6 +601,23 @@ int make_kmajor_map(CUtensorMap* map, const void* base, bool bf16, int64_t rows,
   return NTB200_OK;
 }
 
+// [2, I, K] view of a merged gate_up weight [2I, K] (K contiguous); box = 64 x 128 rows x
+// both halves, 128-byte swizzle: one load brings 128 gate rows and the matching up rows.
+int make_gate_up_map(CUtensorMap* map, const void* base, bool bf16, int64_t I, int64_t k, int64_t row_stride) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return fail(NTB200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {cuuint64_t(k), cuuint64_t(I), 2};
+  const cuuint64_t strides[2] = {cuuint64_t(row_stride * 2), cuuint64_t(I * row_stride * 2)};
+  const cuuint32_t box[3] = {cuuint32_t(BK), 128, 2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NTB200_ERR_CUDA, "cuTensorMapEncodeTiled (gate_up) failed (%d)", int(r));
+  return NTB200_OK;
+}
+
 // ------------------------------------------------------------------------------------
 // Small-M path (M <= 256: decode batches).  out^T = W . x^T ("swap AB"): weight rows fill
 // the UMMA M=128 side, the few token rows are the UMMA N side (padded to MP = 16 .. 256;
@@ -988,7 +1005,7 @@ int launch_small(const CUtensorMap& wmap, const CUtensorMap& xmap, const SmallPa
 // How many clusters of `cluster` CTAs of `fn` (with `smem` bytes each) can be resident at
 // once on the current device; cached per (device, variant slot, cluster size).
 int resident_clusters(const void* fn, int smem, int cluster, int slot) {
-  constexpr int kDevs = 16, kSlots = 64, kMaxCluster = 9;
+  constexpr int kDevs = 16, kSlots = 128, kMaxCluster = 9;
   static std::atomic<int> cache[kDevs][kSlots][kMaxCluster];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1204,6 +1221,355 @@ int dispatch_small_swiglu(const CUtensorMap& wmap, const CUtensorMap& xmap, cons
   }
 }
 
+// ------------------------------------------------------------------------------------
+// Skinny-activation path of `ntb200_linear` (M <= 256: decode batches).  out = x . W^T with
+// the weight rows on the UMMA N side (a 256-row weight tile per CTA) and the token rows on
+// the M side (one token tile of MP <= 128 rows, or two of 128).  A kind::f16 tcgen05.mma
+// (K = 16) occupies the tensor pipe for the same time whatever its N (16..256) or M (64,
+// 128), so what one instruction consumes of the weights sets the weight streaming rate:
+// 256 rows x 16 here, twice what a weight-rows-on-M tile consumes, which is the difference
+// between falling short of and exceeding HBM bandwidth with a decode batch.
+//   warp 0      TMA producer: per 64-wide k-step the token tile(s) (MP x 64; rows past M
+//               are zero-fill and cost no memory traffic) and the 256 x 64 weight tile;
+//   warp 1      allocates TMEM (TT x 256 fp32 columns) and issues the MMAs;
+//   warps 2-5   epilogue: TMEM lane = token row, 256 output columns per row.
+// With MP < 128 the MMA's A operand rows past MP read the rest of the stage (their
+// accumulator rows are never stored).  When the weight tiles alone leave SMs idle, K is
+// split across the CTAs of a cluster (<= 8 CTAs, sized so the clusters are resident at
+// once): each CTA stages its fp32 partial rows in shared memory and, after a cluster
+// barrier, sums a share of the (row, 4-column) units over the cluster through
+// distributed shared memory, in split order, adds the bias and stores.  One launch, no
+// global workspace, no TMA multicast.
+// ------------------------------------------------------------------------------------
+constexpr int kSkinnyBN = 256;
+constexpr int kSkinnyWTile = kSkinnyBN * BK * 2;  // 32 KB
+
+template <int MP, int TT>
+struct SkinnySmem {
+  static constexpr int kXTile = MP * BK * 2;  // one token tile
+  static constexpr int kX = TT * kXTile;
+  static constexpr int kStage = kX + kSkinnyWTile;
+  static constexpr int kStages = (225 * 1024) / kStage > 6 ? 6 : (225 * 1024) / kStage;
+  static constexpr int kRing = kStages * kStage;
+  static constexpr int kFull = kRing;
+  static constexpr int kEmpty = kFull + 8 * kStages;
+  static constexpr int kTmemFull = kEmpty + 8 * kStages;
+  static constexpr int kTmemBase = kTmemFull + 8;
+  static constexpr int kEnd = kTmemBase + 8;
+  static constexpr int kDynamicBytes = kEnd + 1024;
+  static constexpr int kTmemCols = TT * kSkinnyBN;
+  static constexpr int kPartStride = kSkinnyBN + 4;  // floats per staged partial row (padded)
+  static_assert(TT == 1 || MP == 128, "two token tiles are 128 rows each");
+  static_assert(kStage >= BM * BK * 2, "an M = 128 A operand must lie inside its stage");
+  static_assert(kStages >= 3, "ring too shallow");
+  static_assert(128 * kPartStride * 4 <= kRing, "partial rows must fit in the ring");
+  static_assert(kDynamicBytes <= 227 * 1024, "ring exceeds shared memory");
+};
+
+struct SkinnyParams {
+  void* out;
+  const void* bias;
+  int64_t M, N;
+  int64_t out_stride;
+  int splits;
+  int k_steps_per_split;
+  int k_steps_total;
+  int64_t n_half;  // SwiGLU variant: output columns I (up rows start at row I of W)
+  unsigned int* err;
+};
+
+// SWIGLU (no K split): the weight tile is gate rows [128 nb, +128) then the matching up rows
+// [I + 128 nb, +128) of vLLM's merged [2I, K] weight, fetched as one box of its [2, I, K]
+// view (w_map), so accumulator columns [0, 128) hold x.gate and [128, 256) x.up of the same
+// 128 output columns; the epilogue writes silu(gate) * up with the rounding points of the
+// unfused pair.
+template <typename T, int MP, int TT, bool SWIGLU = false>
+__global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
+    const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
+    const SkinnyParams p) {
+  using L = SkinnySmem<MP, TT>;
+  constexpr int kStages = L::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kFull);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L::kEmpty);
+  uint64_t* tmem_full = reinterpret_cast<uint64_t*>(smem + L::kTmemFull);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemBase);
+  const uint32_t ring = smem_u32(smem);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int split = blockIdx.x % p.splits;  // == rank in the cluster
+  const int nb = blockIdx.x / p.splits;     // weight rows [256 nb, +256)
+  const int kb0 = split * p.k_steps_per_split;
+  const int kb1 = min(kb0 + p.k_steps_per_split, p.k_steps_total);
+  const int nk = kb1 > kb0 ? kb1 - kb0 : 0;
+  pdl_trigger();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tmem_full, 1);
+    fence_mbar_init();
+  }
+  // tensor memory is allocated only after the preceding kernel has finished
+  pdl_wait();
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_base_slot)),
+                 "r"(L::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&w_map)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&x_map)) : "memory");
+      int issued = 0;
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % kStages;
+        if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, p.err)) break;
+        mbar_arrive_expect_tx(&full[s], L::kStage);
+        const uint32_t stage = ring + s * L::kStage;
+        const int kx = (kb0 + it) * BK;
+#pragma unroll
+        for (int t = 0; t < TT; ++t) tma_load_2d(stage + t * L::kXTile, &x_map, kx, t * BM, smem_u32(&full[s]));
+        if (SWIGLU) {
+          // one box of the [2, I, K] view: gate rows then the matching up rows
+          tma_load_3d(stage + L::kX, &w_map, kx, nb * (kSkinnyBN / 2), 0, smem_u32(&full[s]));
+        } else {
+          tma_load_2d(stage + L::kX, &w_map, kx, nb * kSkinnyBN, smem_u32(&full[s]));
+        }
+        issued = it + 1;
+      }
+      // no copy may still be landing when the CTA exits
+      const int first = issued > kStages ? issued - kStages : 0;
+      for (int j = first; j < issued; ++j) mbar_wait(&full[j % kStages], (j / kStages) & 1, p.err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(std::is_same<T, __nv_bfloat16>::value, BM, kSkinnyBN);
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % kStages;
+        if (!mbar_wait(&full[s], (it / kStages) & 1, p.err)) break;
+        tc_fence_after();
+        const uint32_t stage = ring + s * L::kStage;
+        const uint64_t bdesc = sw128_kmajor_desc(stage + L::kX);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+#pragma unroll
+          for (int t = 0; t < TT; ++t)
+            umma_f16(tmem_base + t * kSkinnyBN, sw128_kmajor_desc(stage + t * L::kXTile) + 2 * k, bdesc + 2 * k,
+                     idesc, (it > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(tmem_full);  // also the "all MMAs done" point before TMEM is released
+    }
+  }
+
+  T* out = static_cast<T*>(p.out);
+  const T* bias = static_cast<const T*>(p.bias);
+  const bool epilogue = warp >= 2;
+  const int quad = warp & 3;             // TMEM lane quadrant this warp may access
+  const int row_in_tile = quad * 32 + lane;
+  const int64_t n0 = int64_t(nb) * kSkinnyBN;
+  bool acc_ok = false;
+  if (epilogue) {
+    acc_ok = mbar_wait(tmem_full, 0, p.err) && nk > 0;
+    tc_fence_after();
+  }
+
+  if (SWIGLU) {
+    // no split (the host plans none): silu(gate) * up straight from TMEM
+    if (epilogue) {
+#pragma unroll 1
+      for (int t = 0; t < TT; ++t) {
+        if (int64_t(t) * BM + quad * 32 >= p.M) continue;
+        const int64_t m = int64_t(t) * BM + row_in_tile;
+#pragma unroll 1
+        for (int c = 0; c < kSkinnyBN / 64; ++c) {
+          uint32_t g[32], u[32];
+          __syncwarp();
+          tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + t * kSkinnyBN + c * 32, g);
+          tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + t * kSkinnyBN + kSkinnyBN / 2 + c * 32, u);
+          if (m < p.M) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = acc_ok ? swiglu<T>(__uint_as_float(g[i]), __uint_as_float(u[i])) : 0.f;
+            store_row32<T>(out + m * p.out_stride, int64_t(nb) * (kSkinnyBN / 2) + c * 32, p.n_half, v, nullptr);
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  } else if (p.splits == 1) {
+    // TMEM -> registers -> global: a thread writes 32 consecutive columns of its row at a time
+    if (epilogue) {
+#pragma unroll 1
+      for (int t = 0; t < TT; ++t) {
+        if (int64_t(t) * BM + quad * 32 >= p.M) continue;  // the warp's rows are all past M
+        const int64_t m = int64_t(t) * BM + row_in_tile;
+#pragma unroll 1
+        for (int c = 0; c < kSkinnyBN / 32; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + t * kSkinnyBN + c * 32, r);
+          if (m < p.M) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = acc_ok ? __uint_as_float(r[i]) : 0.f;
+            store_row32<T>(out + m * p.out_stride, n0 + c * 32, p.N, v, bias);
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  } else {
+    float* part = reinterpret_cast<float*>(smem);
+    const uint32_t part_addr = smem_u32(smem);
+#pragma unroll 1
+    for (int t = 0; t < TT; ++t) {
+      const int rows = static_cast<int>(p.M - int64_t(t) * BM < BM ? p.M - int64_t(t) * BM : BM);
+      if (epilogue && quad * 32 < rows) {
+#pragma unroll 1
+        for (int c = 0; c < kSkinnyBN / 32; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld_32(tmem_base + (uint32_t(quad * 32) << 16) + t * kSkinnyBN + c * 32, r);
+          if (row_in_tile < rows) {
+            float4* dst = reinterpret_cast<float4*>(part + row_in_tile * L::kPartStride + c * 32);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              dst[q] = acc_ok ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                            __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+      }
+      // every CTA of the cluster has its partial rows of token tile t in shared memory
+      cluster_sync_all();
+      const int units = rows * (kSkinnyBN / 4);
+      const int u0 = static_cast<int>(int64_t(units) * split / p.splits);
+      const int u1 = static_cast<int>(int64_t(units) * (split + 1) / p.splits);
+      for (int u = u0 + static_cast<int>(threadIdx.x); u < u1; u += kThreads) {
+        const int row = u / (kSkinnyBN / 4);
+        const int c4 = u - row * (kSkinnyBN / 4);
+        const int64_t col = n0 + 4 * c4;
+        if (col >= p.N) continue;
+        const uint32_t off = part_addr + uint32_t((row * L::kPartStride + 4 * c4) * 4);
+        float4 v[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v[r] = r < p.splits ? ld_dsmem_f32x4(off, uint32_t(r)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float acc[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] = (bias != nullptr && col + i < p.N) ? Elem<T>::to_f(bias[col + i]) : 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          acc[0] += v[r].x;
+          acc[1] += v[r].y;
+          acc[2] += v[r].z;
+          acc[3] += v[r].w;
+        }
+        T* orow = out + (int64_t(t) * BM + row) * p.out_stride;
+        if (col + 4 <= p.N && ((reinterpret_cast<uintptr_t>(orow + col) & 7u) == 0)) {
+          store_f<T, 4>(orow + col, acc);
+        } else {
+          for (int i = 0; i < 4; ++i)
+            if (col + i < p.N) orow[col + i] = Elem<T>::from_f(acc[i]);
+        }
+      }
+      // nobody overwrites (or frees) its partial rows while a partner still reads them
+      cluster_sync_all();
+    }
+    if (epilogue) tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(L::kTmemCols)
+                 : "memory");
+  }
+}
+
+// Splits of K for `n_tiles` weight tiles: the most SMs busy (n_tiles x splits <= the SM
+// count) whose clusters of `splits` CTAs are all resident at once.
+template <typename T, int MP, int TT, bool SWIGLU = false>
+int launch_skinny(const CUtensorMap& wmap, const CUtensorMap& xmap, SkinnyParams prm, int n_tiles, cudaStream_t s,
+                  int slot) {
+  using L = SkinnySmem<MP, TT>;
+  const void* fn = reinterpret_cast<const void*>(gemm_skinny_kernel<T, MP, TT, SWIGLU>);
+  int st = ensure_smem_attribute(fn, L::kDynamicBytes, slot);
+  if (st != NTB200_OK) return st;
+  const int sms = num_sms();
+  int splits = 1;
+  for (int cand = SWIGLU ? 1 : 8; cand >= 2; --cand) {
+    if (cand > prm.k_steps_total || int64_t(n_tiles) * cand > sms) continue;
+    const int per = static_cast<int>(ceil_div(prm.k_steps_total, cand));
+    const int used = static_cast<int>(ceil_div(prm.k_steps_total, per));
+    if (used != cand) continue;  // an uneven split that leaves a CTA without k-steps
+    if (resident_clusters(fn, L::kDynamicBytes, cand, slot) < n_tiles) continue;
+    splits = cand;
+    break;
+  }
+  prm.splits = splits;
+  prm.k_steps_per_split = static_cast<int>(ceil_div(prm.k_steps_total, splits));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * splits));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = L::kDynamicBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  set_pdl_attribute(attr[1]);
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_skinny_kernel<T, MP, TT, SWIGLU>, wmap, xmap, prm);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(NTB200_ERR_CUDA, "linear (M <= 256): launch failed: %s", cudaGetErrorString(e));
+  }
+  return NTB200_OK;
+}
+
+template <typename T, bool SWIGLU = false>
+int dispatch_skinny(const CUtensorMap& wmap, const CUtensorMap& xmap, const SkinnyParams& prm, int mp, int n_tiles,
+                    cudaStream_t s, int slot_base) {
+  switch (mp) {
+    case 16: return launch_skinny<T, 16, 1, SWIGLU>(wmap, xmap, prm, n_tiles, s, slot_base + 0);
+    case 32: return launch_skinny<T, 32, 1, SWIGLU>(wmap, xmap, prm, n_tiles, s, slot_base + 1);
+    case 64: return launch_skinny<T, 64, 1, SWIGLU>(wmap, xmap, prm, n_tiles, s, slot_base + 2);
+    case 128: return launch_skinny<T, 128, 1, SWIGLU>(wmap, xmap, prm, n_tiles, s, slot_base + 3);
+    default: return launch_skinny<T, 128, 2, SWIGLU>(wmap, xmap, prm, n_tiles, s, slot_base + 4);
+  }
+}
+
+// Which decode-batch kernel `ntb200_linear` uses (M <= 256), from CUDA-graph timings with
+// the weights beyond L2: the 256-row-tile kernel (gemm_skinny_kernel) wins where its tiles
+// fill >= 70 % of the SMs without a K split (28672 x 4096: 46 vs 51 us at M = 128, 58 vs
+// 68 us at M = 256), and with a split up to M = 128 once there are >= 24 tiles (6144 x 4096:
+// 12.1 vs 13.5 us at M = 1, 16.7 vs 17.6 us at M = 128).  With fewer tiles, or 256 token
+// rows, the fp32 partial rows its K split must sum (M x 256 per CTA) cost more than the
+// halved MMA count saves, and the 128-row weight tiles of gemm_small_m_kernel are faster.
+bool skinny_preferred(int64_t M, int64_t N, int sms) {
+  const int64_t tiles = ceil_div(N, kSkinnyBN);
+  if (tiles * 10 >= int64_t(sms) * 7) return true;
+  return M <= 128 && tiles >= 24;
+}
+
 // ---- LM head + greedy argmax -------------------------------------------------------
 
 template <typename T, int MP>
@@ -1357,6 +1723,31 @@ extern "C" int ntb200_linear_silu_and_mul(void* out, const void* x, const void* 
   if (2 * I > 0x7fffffff) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear_silu_and_mul: I too large");
   const bool bf16 = dtype == NTB200_DTYPE_BF16;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M > 64 && M <= 256 && ceil_div(I, kSkinnyBN / 2) * 10 >= int64_t(num_sms()) * 7) {
+    // 256-row weight tiles (128 gate + 128 up rows) filling the SMs without a K split; at
+    // M <= 64 the 128-row tiles below measured faster (I = 14336, K = 4096: 38.5 against
+    // 47.8 us at M = 1; 52.7 against 56.1 us at M = 128, 70.2 against 76.8 at M = 256)
+    const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    CUtensorMap wmap, xmap;
+    int st = make_gate_up_map(&wmap, weight, bf16, I, K, weight_row_stride);
+    if (st != NTB200_OK) return st;
+    st = make_kmajor_map(&xmap, x, bf16, M, K, x_row_stride, mp > BM ? BM : mp);
+    if (st != NTB200_OK) return st;
+    SkinnyParams sp;
+    sp.out = out;
+    sp.bias = nullptr;
+    sp.M = M;
+    sp.N = 2 * I;
+    sp.out_stride = out_row_stride;
+    sp.splits = 1;
+    sp.k_steps_total = static_cast<int>(ceil_div(K, BK));
+    sp.k_steps_per_split = sp.k_steps_total;
+    sp.n_half = I;
+    sp.err = device_error_word();
+    const int tiles = static_cast<int>(ceil_div(I, kSkinnyBN / 2));
+    return bf16 ? dispatch_skinny<__nv_bfloat16, true>(wmap, xmap, sp, mp, tiles, s, 106)
+                : dispatch_skinny<__half, true>(wmap, xmap, sp, mp, tiles, s, 111);
+  }
   if (M <= 256) {
     const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
     CUtensorMap wmap, xmap;
@@ -1422,6 +1813,30 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
   const bool bf16 = dtype == NTB200_DTYPE_BF16;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (M <= 256) {
+    if (skinny_preferred(M, N, num_sms())) {
+      // decode-sized batches: weight rows on the MMA's N side, K split over a cluster
+      const int64_t n_tiles = ceil_div(N, kSkinnyBN);
+      if (n_tiles > 0x7fffffff / 8) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
+      const int mp = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+      CUtensorMap wmap, xmap;
+      int st = make_kmajor_map(&wmap, weight, bf16, N, K, weight_row_stride, kSkinnyBN);
+      if (st != NTB200_OK) return st;
+      st = make_kmajor_map(&xmap, x, bf16, M, K, x_row_stride, mp > BM ? BM : mp);
+      if (st != NTB200_OK) return st;
+      SkinnyParams sp;
+      sp.out = out;
+      sp.bias = bias;
+      sp.M = M;
+      sp.N = N;
+      sp.out_stride = out_row_stride;
+      sp.splits = 1;
+      sp.k_steps_total = static_cast<int>(ceil_div(K, BK));
+      sp.k_steps_per_split = sp.k_steps_total;
+      sp.n_half = 0;
+      sp.err = device_error_word();
+      return bf16 ? dispatch_skinny<__nv_bfloat16>(wmap, xmap, sp, mp, static_cast<int>(n_tiles), s, 96)
+                  : dispatch_skinny<__half>(wmap, xmap, sp, mp, static_cast<int>(n_tiles), s, 101);
+    }
     // swap-AB + cluster split-K path for decode-sized batches
     const int64_t n_tiles = ceil_div(N, BM);
     if (n_tiles > 0x7fffffff / 8) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "linear: too many tiles");
@@ -1465,6 +1880,7 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     return bf16 ? dispatch_small<__nv_bfloat16>(wmap, xmap, sp_big, sp_small, mp, nt, s, 4)
                 : dispatch_small<__half>(wmap, xmap, sp_big, sp_small, mp, nt, s, 18);
   }
+  if (M >= kPairMinM)
   if (M >= kPairMinM)
     return launch_pair(out, x, weight, bias, M, N, K, x_row_stride, weight_row_stride, out_row_stride, bf16, s);
   const int bn = pick_tile_width(M, N, num_sms());
