@@ -9,7 +9,7 @@
 //
 // Persistent: one CTA per SM walks the work items -- (128-query tile, q head) pairs of all
 // sequences, a sequence's last tile first -- found from a prefix sum of the query tiles
-// per sequence that every CTA builds in shared memory.  416 threads:
+// per sequence that every CTA builds in shared memory.  448 threads:
 //   warp 0     TMA: the Q tile (two 64-column halves, 128-byte swizzle; double-buffered
 //              across items) and half of each K tile's pages; three more producer warps
 //              (after the softmax warps) issue the other half of K's and V's pages, so four
@@ -18,10 +18,12 @@
 //              2-stage rings; page ids come from the block table (ids out of range are
 //              reported and read as zeros: the copy lands outside the tensor map).
 //   warp 1     TMEM (two S buffers and O: 384 of 512 columns); lane 0 issues
-//              S_j = Q K_j^T (M = N = 128, eight K = 16 steps; both operands K-major) and
-//              O += P_j V_j (A = P_j in TMEM, written over S_j; B = V as cached, MN-major),
-//              with S_{j+1} issued before O += P_j V_j so the tensor core runs ahead of the
-//              softmax; S_{j+2} reuses the buffer once O += P_j V_j has read P_j.
+//              S_j = Q K_j^T (M = N = 128, eight K = 16 steps; both operands K-major) as
+//              far ahead as the two S buffers allow: S_{j+2} reuses a buffer once
+//              O += P_j V_j has read P_j.
+//   warp 13    lane 0 issues O += P_j V_j (A = P_j in TMEM, written over S_j; B = V as
+//              cached, MN-major) once the softmax has released P_j.  Two issuing threads
+//              keep the tensor pipe about twice as busy as one.
 //   warps 2-9  softmax, two threads per query row (warp w owns TMEM lanes 32*(w%4)..+31
 //              and 64 of the 128 key columns; the two halves of a row meet at an mbarrier
 //              to combine their maxima): the S row from TMEM, scale and mask, the running
@@ -53,7 +55,11 @@ constexpr int kSoftmaxThreads = 256;           // warps 2-9: two per query row
 // issuing half of a tile's pages of K or of V (and warp 0 also the Q tiles).
 constexpr int kParts = 2;                           // issuing threads per operand
 constexpr int kExtraWarp = 2 + kSoftmaxThreads / 32;  // first producer warp after the softmax warps
-constexpr int kThreads = 64 + kSoftmaxThreads + 32 * (2 * kParts - 1);
+// The MMAs are issued by two threads: warp 1 issues S = Q K^T, this warp O += P V.  A thread
+// issues one tcgen05.mma at a time, and one issuer for both products kept the tensor pipe
+// about a third busy.
+constexpr int kPvWarp = kExtraWarp + 2 * kParts - 1;
+constexpr int kThreads = 64 + kSoftmaxThreads + 32 * (2 * kParts - 1) + 32;
 constexpr int kHalf = 128 * 64 * 2;           // 128 rows x 64 columns: 16 KB
 constexpr int kTile = 2 * kHalf;              // 128 x 128: 32 KB
 constexpr int kPageBytes = kPage * 128;       // one page of one half: 16 rows x 128 B
@@ -311,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
     }
     mbar_init(p_empty, 1);
     mbar_init(o_free, 8);
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, 2);  // a commit from each issuer
     for (int q = 0; q < 4; ++q) mbar_init(reinterpret_cast<uint64_t*>(smem + Smem::kPair) + q, 64);
     fence_mbar_init();
   }
@@ -326,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 || warp >= kExtraWarp) {
+  if (warp == 0 || (warp >= kExtraWarp && warp < kPvWarp)) {
     // ------------------------------ TMA producers ------------------------------
     // role 0 (warp 0): Q and the first half of K's pages; role 1: the rest of K; roles 2
     // and 3: V.  Contiguous K/V: each role copies one 64-column half of its operand.
@@ -425,48 +431,57 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
         mbar_wait(&v_full[j & 1], (j / kStages) & 1, p.err);
     }
   } else if (warp == 1) {
-    // ------------------------------ MMA issuer ------------------------------
+    // -------------------------- MMA issuer: S = Q K^T --------------------------
     if (lane == 0) {
       constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
       const uint32_t idesc_s = make_idesc(kBf16, kBQ, kBKV);
-      const uint32_t idesc_o = make_idesc(kBf16, kBQ, kD) | (1u << 16);  // B (V) MN-major
-      // S_g = Q K_g^T into S[g & 1], Q from buffer qb
-      auto issue_s = [&](uint32_t g, int qb) -> bool {
-        const int s = g & 1;
-        if (!mbar_wait(&k_full[s], (g / kStages) & 1, p.err)) return false;
-        // S[s] holds P_{g-2} until O += P_{g-2} V_{g-2} has read it (pv_done[s] completes
-        // once per product on this buffer; the next one, g, is not issued yet)
-        if (g >= 2 && !mbar_wait(&pv_done[s], ((g / 2) - 1) & 1, p.err)) return false;
-        tc_fence_after();
-        const uint32_t kb = sm + Smem::kK + s * kTile;
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          const uint64_t adesc = sw128_kmajor_desc(sm + Smem::kQ + qb * kTile + hf * kHalf);
-          const uint64_t bdesc = sw128_kmajor_desc(kb + hf * kHalf);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_f16(tmem + s * kBKV, adesc + 2 * k, bdesc + 2 * k, idesc_s, (hf | k) ? 1u : 0u);
-        }
-        umma_commit(&k_empty[s]);
-        umma_commit(&s_full[s]);
-        return true;
-      };
       uint32_t g = 0, nq = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
         const Item it = make_item<PAGED>(p, prefix, w);
         if (it.n_tiles == 0) continue;
         const int qb = nq & 1;
-        if (!mbar_wait(&q_full[qb], (nq / 2) & 1, p.err) || !issue_s(g, qb)) break;
-        if (it.n_tiles == 1) umma_commit(&q_empty[qb]);
+        if (!mbar_wait(&q_full[qb], (nq / 2) & 1, p.err)) break;
         for (int j = 0; j < it.n_tiles; ++j, ++g) {
-          if (j + 1 < it.n_tiles) {
-            if (!issue_s(g + 1, qb)) {
-              ok = false;
-              break;
-            }
-            if (j + 2 == it.n_tiles) umma_commit(&q_empty[qb]);  // the item's last S product is issued
+          // S_g = Q K_g^T into S[g & 1]; the buffer holds P_{g-2} until O += P_{g-2} V_{g-2}
+          // has read it (pv_done[s] completes once per product on this buffer)
+          const int s = g & 1;
+          if (!mbar_wait(&k_full[s], (g / kStages) & 1, p.err) ||
+              (g >= 2 && !mbar_wait(&pv_done[s], ((g / 2) - 1) & 1, p.err))) {
+            ok = false;
+            break;
           }
+          tc_fence_after();
+          const uint32_t kb = sm + Smem::kK + s * kTile;
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const uint64_t adesc = sw128_kmajor_desc(sm + Smem::kQ + qb * kTile + hf * kHalf);
+            const uint64_t bdesc = sw128_kmajor_desc(kb + hf * kHalf);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              umma_f16(tmem + s * kBKV, adesc + 2 * k, bdesc + 2 * k, idesc_s, (hf | k) ? 1u : 0u);
+          }
+          umma_commit(&k_empty[s]);
+          umma_commit(&s_full[s]);
+          if (j + 1 == it.n_tiles) umma_commit(&q_empty[qb]);  // the item's last S product is issued
+        }
+        ++nq;
+      }
+      // every issued MMA completes before TMEM may be released
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.err);
+    }
+  } else if (warp == kPvWarp) {
+    // -------------------------- MMA issuer: O += P V --------------------------
+    if (lane == 0) {
+      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+      const uint32_t idesc_o = make_idesc(kBf16, kBQ, kD) | (1u << 16);  // B (V) MN-major
+      uint32_t g = 0, nq = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+        const Item it = make_item<PAGED>(p, prefix, w);
+        if (it.n_tiles == 0) continue;
+        for (int j = 0; j < it.n_tiles; ++j, ++g) {
           const int s = g & 1;
           if (!mbar_wait(&p_full[s], (g / 2) & 1, p.err) || !mbar_wait(&v_full[s], (g / kStages) & 1, p.err)) {
             ok = false;
@@ -495,7 +510,6 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
         }
         ++nq;
       }
-      // every issued MMA completes before TMEM may be released
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, p.err);
     }
