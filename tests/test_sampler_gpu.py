@@ -61,12 +61,12 @@ def test_golden_fixture_capi():
 
 
 @pytest.mark.parametrize("k_dtype", [torch.int32, torch.int64])
-def test_llama_vocabulary_batch(k_dtype):
-    """64 rows of a 128256-token vocabulary, logit spreads 0.5 .. 8, k from 1 to V (V and
-    V - 1 included), p from 0.3 to 1.0."""
+@pytest.mark.parametrize("b", [8, 64])
+def test_llama_vocabulary_batch(k_dtype, b):
+    """Rows of a 128256-token vocabulary (8: one cluster of CTAs per row; 64: one CTA per
+    row), logit spreads 0.5 .. 8, k from 1 to V (V and V - 1 included), p from 0.3 to 1.0."""
     dev = cuda_device()
     g = seeded(31)
-    b = 64
     spread = torch.tensor([0.5, 1.0, 2.0, 3.0, 5.0, 8.0, 1.5, 4.0]).repeat(b // 8).unsqueeze(1)
     logits = torch.randn(b, VOCAB, generator=g) * spread
     k = torch.randint(1, 2000, (b,), generator=g)
