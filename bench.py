@@ -495,7 +495,22 @@ def per_op_table(dev, peaks) -> dict:
                              sort="torch sort + cumsum + scatter (the reference's algorithm, on the GPU)")
         except Exception as exc:  # noqa: BLE001 - the comparison columns are optional
             res[name]["lib"] = f"unavailable ({type(exc).__name__}: {exc})"[:200]
-        del lg5
+        # a small decode batch (4 rows): one cluster of CTAs per row
+        lg4, src4 = torch.empty_like(src5[:4]), src5[:4].clone()
+        k4, p4 = k5[:4].clone(), p5[:4].clone()
+        copy4 = time_graph([lambda: lg4.copy_(src4)], 10) * 1e3
+        name = "top_k_top_p f32 [4,128256] k=50 p=0.9"
+        us = time_graph([lambda: (lg4.copy_(src4), o.top_k_top_p(lg4, k4, p4))], 10) * 1e3 - copy4
+        report(name, 2 * 4 * V5 * 4, us * 1e-3, {"note": "one cluster of 8 CTAs per row, row slices in shared memory"})
+        try:
+            from vllm.v1.sample.ops.topk_topp_sampler import apply_top_k_top_p_pytorch
+
+            s_us = time_graph([lambda: (lg4.copy_(src4), apply_top_k_top_p_pytorch(lg4, k4, p4))], 3) * 1e3 - copy4
+            res[name].update(lib="vllm apply_top_k_top_p_pytorch (torch sort + cumsum + scatter)", lib_us=round(s_us, 2),
+                             ours_vs_lib=round(s_us / res[name]["us"], 3))
+        except Exception as exc:  # noqa: BLE001 - the comparison column is optional
+            res[name]["lib"] = f"unavailable ({type(exc).__name__}: {exc})"[:200]
+        del lg5, lg4, src4
         probs5 = src5.softmax(dim=-1)
         q5 = torch.empty_like(probs5).exponential_(generator=g)
         ids5 = torch.empty(B5, dtype=torch.int64, device=dev)
@@ -644,6 +659,7 @@ _SHORT = {
     "paged prefill bf16 8 x 512 new after 1536 cached": "prefill 8x512@1536",
     "paged decode bf16 B=256 ctx U[512,640] (vLLM e2e shape)": "decode ctx512-640",
     "top_k_top_p f32 [256,128256] k=50 p=0.9": "topk_topp 256x128256",
+    "top_k_top_p f32 [4,128256] k=50 p=0.9": "topk_topp 4x128256",
     "random_sample f32 [256,128256]": "sample 256x128256",
     "rope_and_cache bf16 256 tokens of qkv [T,48*128]": "rope+kv 256",
     "rope_and_cache bf16 16384 tokens of qkv [T,48*128]": "rope+kv 16384",
