@@ -9,26 +9,27 @@
 //
 // Persistent: one CTA per SM walks the work items -- (128-query tile, q head) pairs of all
 // sequences, a sequence's last tile first -- found from a prefix sum of the query tiles
-// per sequence that every CTA builds in shared memory.  448 threads:
+// per sequence that every CTA builds in shared memory.  704 threads:
 //   warp 0     TMA: the Q tile (two 64-column halves, 128-byte swizzle; double-buffered
 //              across items) and half of each K tile's pages; three more producer warps
-//              (after the softmax warps) issue the other half of K's and V's pages, so four
-//              threads issue copies at once (the issue rate of small copies limits).  Per
-//              tile the 8 K pages and the 8 V pages (16 tokens x 64 columns per copy) into
-//              2-stage rings; page ids come from the block table (ids out of range are
-//              reported and read as zeros: the copy lands outside the tensor map).
+//              (warps 18-20, after the softmax warps) issue the other half of K's and V's
+//              pages, so four threads issue copies at once (the issue rate of small copies
+//              limits).  Per tile the 8 K pages and the 8 V pages (16 tokens x 64 columns
+//              per copy) into 2-stage rings; page ids come from the block table (ids out of
+//              range are reported and read as zeros: the copy lands outside the tensor map).
 //   warp 1     TMEM (two S buffers and O: 384 of 512 columns); lane 0 issues
 //              S_j = Q K_j^T (M = N = 128, eight K = 16 steps; both operands K-major) as
 //              far ahead as the two S buffers allow: S_{j+2} reuses a buffer once
 //              O += P_j V_j has read P_j.
-//   warp 13    lane 0 issues O += P_j V_j (A = P_j in TMEM, written over S_j; B = V as
+//   warp 21    lane 0 issues O += P_j V_j (A = P_j in TMEM, written over S_j; B = V as
 //              cached, MN-major) once the softmax has released P_j.  Two issuing threads
 //              keep the tensor pipe about twice as busy as one.
-//   warps 2-9  softmax, two threads per query row (warp w owns TMEM lanes 32*(w%4)..+31
-//              and 64 of the 128 key columns; the two halves of a row meet at an mbarrier
-//              to combine their maxima): the S row from TMEM, scale and mask, the running
-//              max and sum in fp32 in the exp2 domain, P = exp2(s - m) rounded to the input
-//              type and stored back into TMEM over the S columns just read.  The running max is refreshed lazily:
+//   warps 2-17 softmax, four threads per query row (warp w owns TMEM lanes 32*(w%4)..+31
+//              and 32 of the 128 key columns; the four parts of a row meet at an mbarrier
+//              to combine their maxima and sums): the S row from TMEM, scale and mask, the
+//              running max and sum in fp32 in the exp2 domain, P = exp2(s - m) rounded to
+//              the input type and stored back into TMEM over the S columns (packed in
+//              pairs).  The running max is refreshed lazily:
 //              only when a row's max grows by more than 2^8 is O (in TMEM) rescaled, so
 //              P <= 256 and O / l is the same either way.  Epilogue: O / l, rounded, stored.
 //
@@ -50,7 +51,7 @@ constexpr int kBQ = 128;                      // query rows per CTA
 constexpr int kBKV = 128;                     // keys per tile
 constexpr int kPage = 16;                     // tokens per cache block
 constexpr int kPagesPerTile = kBKV / kPage;   // 8
-constexpr int kSoftmaxThreads = 256;           // warps 2-9: two per query row
+constexpr int kSoftmaxThreads = 512;           // warps 2-17: four per query row
 // Copy issue: four threads (warp 0 and the three warps after the softmax warps), each
 // issuing half of a tile's pages of K or of V (and warp 0 also the Q tiles).
 constexpr int kParts = 2;                           // issuing threads per operand
@@ -60,6 +61,9 @@ constexpr int kExtraWarp = 2 + kSoftmaxThreads / 32;  // first producer warp aft
 // about a third busy.
 constexpr int kPvWarp = kExtraWarp + 2 * kParts - 1;
 constexpr int kThreads = 64 + kSoftmaxThreads + 32 * (2 * kParts - 1) + 32;
+constexpr int kRowParts = kSoftmaxThreads / kBQ;  // threads (warps per lane quadrant) per query row
+constexpr int kPartCols = kBKV / kRowParts;        // S / O columns a softmax thread owns
+static_assert(kPartCols == 32, "a softmax thread moves its columns with one 32-column TMEM access");
 constexpr int kHalf = 128 * 64 * 2;           // 128 rows x 64 columns: 16 KB
 constexpr int kTile = 2 * kHalf;              // 128 x 128: 32 KB
 constexpr int kPageBytes = kPage * 128;       // one page of one half: 16 rows x 128 B
@@ -85,8 +89,8 @@ struct Smem {
   static constexpr int kOFree = kPvDone + 16;
   static constexpr int kMmaDone = kOFree + 8;
   static constexpr int kPair = kMmaDone + 8;       // 4 mbarriers: the two warps of each row quadrant
-  static constexpr int kRed = kPair + 32;          // [2][2][128] floats: row-max / row-sum exchange
-  static constexpr int kTmemBase = kRed + 2 * 2 * 128 * 4;
+  static constexpr int kRed = kPair + 32;          // [2][kRowParts][128] floats: row-max / row-sum exchange
+  static constexpr int kTmemBase = kRed + 2 * kRowParts * 128 * 4;
   static constexpr int kPrefix = kTmemBase + 16;   // [num_seqs + 1] ints: the work list
   static constexpr int kMaxBytes = 227 * 1024;
   static constexpr int bytes_for(int64_t num_seqs) { return kPrefix + int(num_seqs + 1) * 4 + 1024; }
@@ -133,6 +137,15 @@ __device__ __forceinline__ void umma_f16_tmem_a(uint32_t tmem_d, uint32_t tmem_a
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 
@@ -312,13 +325,13 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&s_full[a], 1);
-      mbar_init(&p_full[a], 8);  // one arrive per softmax warp
+      mbar_init(&p_full[a], kSoftmaxThreads / 32);  // one arrive per softmax warp
       mbar_init(&pv_done[a], 1);
     }
     mbar_init(p_empty, 1);
-    mbar_init(o_free, 8);
+    mbar_init(o_free, kSoftmaxThreads / 32);
     mbar_init(mma_done, 2);  // a commit from each issuer
-    for (int q = 0; q < 4; ++q) mbar_init(reinterpret_cast<uint64_t*>(smem + Smem::kPair) + q, 64);
+    for (int q = 0; q < 4; ++q) mbar_init(reinterpret_cast<uint64_t*>(smem + Smem::kPair) + q, 32 * kRowParts);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -515,24 +528,34 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
     }
   } else {
     // ------------------------------ softmax + epilogue ------------------------------
-    // Two warps per query row: warp w (2..9) reads TMEM lanes 32*(w%4)..+31 and owns key
-    // columns [64*half, +64) of S, the same 64 columns of O, and the matching half of P.
-    // The row max is exchanged through shared memory at a per-quadrant mbarrier.
+    // kRowParts warps per query row: warp w (2..17) reads TMEM lanes 32*(w%4)..+31 and owns
+    // key columns [kPartCols*part, +kPartCols) of S, the same columns of O, and the
+    // matching part of P.  The row max and sum are exchanged through shared memory at a
+    // per-quadrant mbarrier.
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int col0 = half * 64;
+    const int part = (warp - 2) >> 2;
+    const int col0 = part * kPartCols;
     const int r = quad * 32 + lane;  // query row within the tile (= TMEM lane)
     const uint32_t lanes = uint32_t(quad * 32) << 16;
-    float* red = reinterpret_cast<float*>(smem + Smem::kRed);  // [2 buffers][2 halves][128 rows]
+    // P of keys [col0, +kPartCols), two per 32-bit column: keys 0-63 are packed into
+    // columns 0-31 and keys 64-127 into columns 64-95 of the S buffer
+    const int pcol = (col0 >> 6) * 64 + (col0 & 63) / 2;
+    float* red = reinterpret_cast<float*>(smem + Smem::kRed);  // [2 buffers][kRowParts][128 rows]
     uint64_t* pair = reinterpret_cast<uint64_t*>(smem + Smem::kPair) + quad;
     uint32_t pair_uses = 0;
-    // exchange one float per row with the partner warp; false if the partner never came
-    auto exchange = [&](float mine, float& theirs) -> bool {
-      float* buf = red + (pair_uses & 1) * 256;
-      buf[half * 128 + r] = mine;
+    // publish one float per row and read the row's kRowParts values (in part order);
+    // false if a partner never came
+    // (the tensor-memory fences order this part's S reads before another part's P writes
+    // over the same columns)
+    auto exchange = [&](float mine, float (&all)[kRowParts]) -> bool {
+      float* buf = red + (pair_uses & 1) * (kRowParts * 128);
+      buf[part * 128 + r] = mine;
+      tc_fence_before();
       mbar_arrive(pair);
       const bool got = mbar_wait(pair, pair_uses & 1, p.err);
-      theirs = buf[(half ^ 1) * 128 + r];
+      tc_fence_after();
+#pragma unroll
+      for (int q = 0; q < kRowParts; ++q) all[q] = buf[q * 128 + r];
       ++pair_uses;
       return got;
     };
@@ -546,13 +569,13 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
         // no visible key (empty context): zero rows, as for an empty softmax
         if (r < it.rows)
 #pragma unroll
-          for (int c = 0; c < 8; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0u, 0u, 0u, 0u);
+          for (int c = 0; c < kPartCols / 8; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0u, 0u, 0u, 0u);
         continue;
       }
       int limit = p.causal ? it.shift + qi + 1 : it.ctx;  // this row sees keys [0, limit)
       if (limit > it.ctx) limit = it.ctx;
-      float m_run = -INFINITY;  // running max of scale*s*log2(e), the same in both warps of a row
-      float l_run = 0.f;        // this warp's half of the running sum
+      float m_run = -INFINITY;  // running max of scale*s*log2(e), the same in every part of a row
+      float l_run = 0.f;        // this part's share of the running sum
       for (int j = 0; j < it.n_tiles; ++j, ++g) {
         const int s = g & 1;
         if (!mbar_wait(&s_full[s], (g / 2) & 1, p.err)) {
@@ -560,38 +583,40 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
           break;
         }
         tc_fence_after();
-        float x[64];
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        float x[kPartCols];
+        {
           uint32_t v[32];
           __syncwarp();
-          tmem_ld_32(tmem + lanes + s * kBKV + col0 + c * 32, v);
+          tmem_ld_32(tmem + lanes + s * kBKV + col0, v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(v[i]);
+          for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(v[i]);
         }
         const int nvalid = limit - j * kBKV - col0;  // columns col0 + i are visible iff i < nvalid
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent chains
-        if (nvalid >= 64) {
+        if (nvalid >= kPartCols) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
+          for (int i = 0; i < kPartCols; ++i) {
             x[i] *= p.scale_log2;
             m4[i & 3] = fmaxf(m4[i & 3], x[i]);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
+          for (int i = 0; i < kPartCols; ++i) {
             x[i] = i < nvalid ? x[i] * p.scale_log2 : -INFINITY;
             m4[i & 3] = fmaxf(m4[i & 3], x[i]);
           }
         }
         float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-        float other;
-        if (!exchange(mx, other)) {
-          ok = false;
-          break;
+        {
+          float all[kRowParts];
+          if (!exchange(mx, all)) {
+            ok = false;
+            break;
+          }
+#pragma unroll
+          for (int q = 0; q < kRowParts; ++q) mx = fmaxf(mx, all[q]);
         }
-        mx = fmaxf(mx, other);
-        // lazy max refresh, identical in both warps of a row (same rows, same combined max);
+        // lazy max refresh, identical in every part of a row (same rows, same combined max);
         // warp-uniform, since O is rescaled with warp-wide TMEM accesses
         const float m_new = fmaxf(m_run, mx);
         const bool grow = m_new > m_run + kRescaleLog2;  // also true for the first finite max
@@ -607,10 +632,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
           }
         }
         const float m_use = m_run == -INFINITY ? 0.f : m_run;
-        uint32_t pk[32];
+        uint32_t pk[kPartCols / 2];
         float l4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < kPartCols / 2; ++i) {
           const float p0 = hw_exp2(x[2 * i] - m_use);
           const float p1 = hw_exp2(x[2 * i + 1] - m_use);
           l4[i & 3] += p0 + p1;
@@ -626,15 +651,12 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
             break;
           }
           tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            uint32_t v[32];
-            __syncwarp();
-            tmem_ld_32(tmem + lanes + kTmemO + col0 + c * 32, v);
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld_32(tmem + lanes + kTmemO + col0, v);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
-            tmem_st_32(tmem + lanes + kTmemO + col0 + c * 32, v);
-          }
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          tmem_st_32(tmem + lanes + kTmemO + col0, v);
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
         if (it.ctx > j * kBKV && it.ctx < (j + 1) * kBKV && (!PAGED || (it.ctx & (kPage - 1)) != 0)) {
@@ -655,10 +677,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
         }
-        // P_g (this warp's 64 keys, packed in pairs) over the first 32 of the S columns
-        // this warp has just read
+        // P_g (this part's keys, packed in pairs); every part of the row has read its S
+        // columns before the exchange above, so the packed columns may overwrite them
         __syncwarp();
-        tmem_st_32(tmem + lanes + s * kBKV + col0, pk);
+        tmem_st_16(tmem + lanes + s * kBKV + pcol, pk);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         __syncwarp();
@@ -667,26 +689,24 @@ __global__ void __launch_bounds__(kThreads, 1) paged_prefill_kernel(
       if (!ok) break;
       // the item's last product is complete: O is final
       ok = mbar_wait(p_empty, (g - 1) & 1, p.err);
-      float l_other = 0.f;
-      if (ok) ok = exchange(l_run, l_other);
-      tc_fence_after();
-      const float l = l_run + l_other;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      uint32_t o[64];
+      float l = 0.f;
+      if (ok) {
+        float all[kRowParts];
+        ok = exchange(l_run, all);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t v[32];
-        __syncwarp();
-        tmem_ld_32(tmem + lanes + kTmemO + col0 + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = v[i];
+        for (int q = 0; q < kRowParts; ++q) l += all[q];
       }
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint32_t o[32];
+      __syncwarp();
+      tmem_ld_32(tmem + lanes + kTmemO + col0, o);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_free);  // the next item may overwrite O
       if (ok && r < it.rows) {
 #pragma unroll
-        for (int g8 = 0; g8 < 8; ++g8) {
+        for (int g8 = 0; g8 < 4; ++g8) {
           uint4 w4;
           w4.x = pack2<T>(__uint_as_float(o[g8 * 8 + 0]) * inv, __uint_as_float(o[g8 * 8 + 1]) * inv);
           w4.y = pack2<T>(__uint_as_float(o[g8 * 8 + 2]) * inv, __uint_as_float(o[g8 * 8 + 3]) * inv);
