@@ -617,6 +617,46 @@ def per_op_table(dev, peaks) -> dict:
                 [lambda w_=w_: torch.mm(x, w_.t(), out=out) for w_ in wts], iters)
             del x, wts, out
 
+    # residual add + RMS norm fused into the qkv projection's input (decode batches <= 16
+    # tokens): one kernel against the norm kernel followed by the GEMM (ours, and vLLM's _C
+    # norm with cuBLAS).  Algorithmic bytes: W, x and residual read, out and the new
+    # residual written.
+    from vllm_nt._ntops.torch.linear import rms_norm_linear
+
+    for M in (1, 16):
+        K, Nn = 4096, 6144
+        x = torch.randn(M, K, device=dev, generator=g, dtype=torch.bfloat16)
+        r = torch.randn(M, K, device=dev, generator=g, dtype=torch.bfloat16)
+        gam = torch.ones(K, device=dev, dtype=torch.bfloat16)
+        wts = [0.02 * torch.randn(Nn, K, device=dev, generator=g, dtype=torch.bfloat16)
+               for _ in range(max(1, math.ceil(3 * L2_BYTES / (Nn * K * 2))))]
+        out = torch.empty(M, Nn, device=dev, dtype=torch.bfloat16)
+        new_r = torch.empty_like(x)
+        h = torch.empty_like(x)
+        iters = max(4, 2 * len(wts))
+        ms = time_graph([lambda w_=w_: o.rms_norm_linear(out, new_r, x, r, gam, 1e-5, w_) for w_ in wts], iters)
+        name = f"rms_norm+linear qkv M={M}"
+        report(name, Nn * K * 2 + 3 * M * K * 2 + M * Nn * 2, ms)
+
+        # the unfused pairs work in place, as vLLM runs them (the residual keeps growing
+        # across replays; the timing does not depend on the values)
+        def unfused(w_):
+            o.fused_add_rms_norm(h, new_r, x, gam, 1e-5)
+            o.linear(out, h, w_, None, None)
+
+        new_r.copy_(r)
+        res[name]["unfused_ntb200_us"] = round(time_graph([lambda w_=w_: unfused(w_) for w_ in wts], iters) * 1e3, 2)
+        if vops is not None:
+
+            def vllm_pair(w_):
+                vops.fused_add_rms_norm(h, new_r, gam, 1e-5)
+                torch.mm(h, w_.t(), out=out)
+
+            h.copy_(x)
+            new_r.copy_(r)
+            lib(name, "vllm _C.fused_add_rms_norm + cuBLAS", [lambda w_=w_: vllm_pair(w_) for w_ in wts], iters)
+        del x, r, wts, out, new_r, h
+
     # LM head + greedy sampling, vocabulary 128256 x hidden 4096 (a 1.05 GB weight, beyond
     # L2): the fused kernel keeps the logits on chip and emits the int64 token per row;
     # the unfused pair writes [M, V] logits and reads them back for torch.argmax
@@ -660,6 +700,8 @@ _SHORT = {
     "paged decode bf16 B=256 ctx U[512,640] (vLLM e2e shape)": "decode ctx512-640",
     "top_k_top_p f32 [256,128256] k=50 p=0.9": "topk_topp 256x128256",
     "top_k_top_p f32 [4,128256] k=50 p=0.9": "topk_topp 4x128256",
+    "rms_norm+linear qkv M=1": "norm+qkv 1",
+    "rms_norm+linear qkv M=16": "norm+qkv 16",
     "random_sample f32 [256,128256]": "sample 256x128256",
     "rope_and_cache bf16 256 tokens of qkv [T,48*128]": "rope+kv 256",
     "rope_and_cache bf16 16384 tokens of qkv [T,48*128]": "rope+kv 16384",

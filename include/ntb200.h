@@ -328,6 +328,27 @@ int ntb200_linear_silu_and_mul(void* out, const void* x, const void* weight, int
                                int64_t out_row_stride, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Fused (residual-add) RMS norm + projection for decode batches of at most 16 tokens:
+ *   s = x (+ residual);  residual_out = s (rounded);  h = rms_norm(s) * norm_weight;
+ *   out[M, N] = h . W^T
+ * Replaces the RMSNorm hook followed by the MatMul hook of the next projection
+ * (vllm_nt/_ntops/oot_support.py:32-48, then vllm_nt/_ntops/torch/linear.py:7-21), which
+ * the reference runs as two kernels with h written to and read back from memory; here h
+ * is formed in shared memory as the GEMM's input and never written.  h is rounded as
+ * ntb200_fused_add_rms_norm rounds it (the normalised fp32 value rounded to the dtype,
+ * times the weight, rounded again); the row statistics are summed in another order, so h
+ * can differ from that entry point's output in the last bit.  residual and residual_out
+ * are both given or both null, and residual_out must not alias x or residual (other CTAs
+ * still read them while it is written).  M <= 16 (NTB200_ERR_UNSUPPORTED_SHAPE above),
+ * dtype BF16 or F16, K a multiple of 8, rows 16-byte aligned; at most 4096 columns of K per
+ * CTA after the K split (NTB200_ERR_UNSUPPORTED_SHAPE otherwise). */
+int ntb200_rms_norm_linear(void* out, void* residual_out, const void* x, const void* residual,
+                           const void* norm_weight, float eps, const void* weight, int64_t M,
+                           int64_t N, int64_t K, int64_t x_row_stride, int64_t residual_row_stride,
+                           int64_t residual_out_row_stride, int64_t weight_row_stride,
+                           int64_t out_row_stride, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * LM head + greedy argmax:  out_index[m] = argmax_v (x[m] . W[v])  over V vocabulary rows,
  * comparing the logits rounded to the dtype (what vLLM's greedy sampler compares: the LM
  * head writes dtype logits) with the first index winning ties, as torch.argmax does.  For

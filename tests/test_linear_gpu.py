@@ -272,3 +272,50 @@ def test_linear_small_m_is_deterministic_and_graph_replayable():
         graph.replay()
         torch.cuda.synchronize()
         torch.testing.assert_close(out.float().cpu(), oracle.linear(x * (i + 1), w), rtol=TOL, atol=TOL * (i + 1))
+
+
+@pytest.mark.parametrize("m", [1, 5, 16])
+@pytest.mark.parametrize("k,n", [(4096, 6144), (4096, 28672), (14336, 4096), (1032, 700)])
+@pytest.mark.parametrize("with_residual", [False, True])
+def test_rms_norm_linear_vs_oracle(m, k, n, with_residual):
+    """RMSNorm (after the residual add) formed as the decode GEMM's input: out against the
+    oracle's norm followed by its linear (split and unsplit K, ragged N and K), the new
+    residual bit for bit against the oracle's, and out against our two separate kernels."""
+    from vllm_nt._ntops.torch.linear import linear, rms_norm_linear
+    from vllm_nt._ntops.torch.rms_norm import fused_add_rms_norm, rms_norm
+
+    g = seeded(m * 31 + k + n + with_residual)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    res = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    gamma = (1.0 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16)
+    w = (0.02 * torch.randn(n, k, generator=g)).to(torch.bfloat16)
+    eps = 1e-5
+    xd, rd, gd, wd = x.cuda(), res.cuda(), gamma.cuda(), w.cuda()
+    if with_residual:
+        out, new_res = rms_norm_linear(xd, gd, eps, wd, rd)
+        h_ref, res_ref = oracle.fused_add_rms_norm(x, res, gamma, eps)
+        assert torch.equal(new_res.cpu(), res_ref)
+        assert torch.equal(rd.cpu(), res)  # the input residual is left as it was
+        h2, _ = fused_add_rms_norm(xd, rd, gd, eps)
+    else:
+        out = rms_norm_linear(xd, gd, eps, wd)
+        h_ref = oracle.rms_norm(x, gamma, eps)
+        h2 = rms_norm(xd, k, gd, eps)
+    torch.testing.assert_close(out.float().cpu(), oracle.linear(h_ref, w), rtol=TOL, atol=TOL)
+    torch.testing.assert_close(out.float(), linear(h2, wd).float(), rtol=TOL, atol=TOL)
+
+
+def test_rms_norm_linear_rejects_large_batches_and_aliasing():
+    x = torch.randn(17, 256, device="cuda", dtype=torch.bfloat16)
+    g = torch.ones(256, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(512, 256, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(17, 512, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(capi.NtB200Error) as e:  # more than 16 rows
+        capi.call("ntb200_rms_norm_linear", ptr(out), None, ptr(x), None, ptr(g), 1e-5, ptr(w), 17, 512, 256,
+                  256, 0, 0, 256, 512, 1, stream())
+    assert e.value.status == -6
+    r = torch.randn(4, 256, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(capi.NtB200Error) as e:  # residual_out aliasing the residual
+        capi.call("ntb200_rms_norm_linear", ptr(out), ptr(r), ptr(x), ptr(r), ptr(g), 1e-5, ptr(w), 4, 512, 256,
+                  256, 256, 256, 256, 512, 1, stream())
+    assert e.value.status == -1

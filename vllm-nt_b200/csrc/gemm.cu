@@ -1248,6 +1248,7 @@ template <int MP, int TT>
 struct SkinnySmem {
   static constexpr int kXTile = MP * BK * 2;  // one token tile
   static constexpr int kX = TT * kXTile;
+  static constexpr int kRingOff = 0;
   static constexpr int kStage = kX + kSkinnyWTile;
   static constexpr int kStages = (225 * 1024) / kStage > 6 ? 6 : (225 * 1024) / kStage;
   static constexpr int kRing = kStages * kStage;
@@ -1276,18 +1277,143 @@ struct SkinnyParams {
   int k_steps_total;
   int64_t n_half;  // SwiGLU variant: output columns I (up rows start at row I of W)
   unsigned int* err;
+  // NORM variant: the GEMM input is RMSNorm(x [+ residual]) * norm_weight, formed here
+  const void* nx;
+  const void* nres;    // null: no residual add
+  void* nres_out;      // the new residual (x + residual), written by the CTAs of weight tile 0
+  const void* ngamma;
+  float eps;
+  int64_t K, x_stride, r_stride, ro_stride;
 };
+
+// Fused RMS norm (decode batches of at most kNormRows tokens): the normalised token rows of
+// the CTA's whole K range stay in shared memory (16 rows x 64 columns = 2 KB per k-step,
+// 128-byte swizzle, at most kNormMaxSteps of them) ahead of a ring of weight tiles; the MMA
+// reads its A operand from there, so only the weights stream through the ring.
+constexpr int kNormRows = 16;
+constexpr int kNormMaxSteps = 64;
+struct SkinnyNormSmem {
+  static constexpr int kXTile = kNormRows * BK * 2;  // 2 KB: one k-step of normalised rows
+  static constexpr int kX = 0;                       // a ring stage holds the weight tile only
+  static constexpr int kA = kNormMaxSteps * kXTile;  // 128 KB
+  static constexpr int kRingOff = kA;
+  static constexpr int kStage = kSkinnyWTile;
+  static constexpr int kStages = 3;
+  static constexpr int kRing = kStages * kStage;
+  static constexpr int kFull = kRingOff + kRing;
+  static constexpr int kEmpty = kFull + 8 * kStages;
+  static constexpr int kTmemFull = kEmpty + 8 * kStages;
+  static constexpr int kTmemBase = kTmemFull + 8;
+  static constexpr int kRowPart = kTmemBase + 8;  // float[16]: this CTA's row sums of squares
+  static constexpr int kRstd = kRowPart + 64;     // float[16]: 1 / rms per row
+  static constexpr int kEnd = kRstd + 64;
+  static constexpr int kDynamicBytes = kEnd + 1024;
+  static constexpr int kTmemCols = kSkinnyBN;
+  static constexpr int kPartStride = kSkinnyBN + 4;
+  // the last k-step's M = 128 operand span (rows past 16 are never stored) stays inside
+  static_assert(kA - kXTile + BM * BK * 2 <= kRingOff + kRing, "A span leaves shared memory");
+  static_assert(128 * kPartStride * 4 <= kRingOff + kRing, "partial rows must fit");
+  static_assert(kDynamicBytes <= 227 * 1024, "exceeds shared memory");
+};
+
+// Remote shared-memory load of one float (see ld_dsmem_f32x4).
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
+  return v;
+}
+
+// NORM prologue (every thread of the CTA): the CTA's K range [64 kb0, +64 nk) of
+// RMSNorm(x [+ residual]) * norm_weight for the M <= 16 token rows, rounded as
+// rms_norm_kernel rounds it for rows that fit its registers (the normalised fp32 value
+// rounded to T, times the weight, rounded again), into the resident A operand (16 rows x 64
+// columns per k-step, 128-byte swizzle).  The row statistics need whole rows: each CTA sums
+// the squares over its K range and the CTAs splitting K for this weight tile add those sums
+// over DSMEM in rank order.  The CTAs of weight tile 0 also write the new residual.
+template <typename T>
+__device__ __forceinline__ void norm_prologue(const SkinnyParams& p, uint8_t* a, uint8_t* rowpart_b, uint8_t* rstd_b,
+                                              int kb0, int nk, bool write_residual) {
+  float* rowpart = reinterpret_cast<float*>(rowpart_b);
+  float* rstd = reinterpret_cast<float*>(rstd_b);
+  const T* x = static_cast<const T*>(p.nx);
+  const T* res = static_cast<const T*>(p.nres);
+  T* res_out = static_cast<T*>(p.nres_out);
+  const T* gamma = static_cast<const T*>(p.ngamma);
+  const int M = static_cast<int>(p.M);
+  const int64_t k0 = int64_t(kb0) * BK;
+  const int64_t k1 = p.K < k0 + int64_t(nk) * BK ? p.K : k0 + int64_t(nk) * BK;
+  const int nvec = k1 > k0 ? static_cast<int>((k1 - k0) / 8) : 0;  // 8-element vectors (K % 8 == 0)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kStepBytes = kNormRows * BK * 2;
+  // the used A region starts at zero: past K the last k-step meets zero-filled weights, and
+  // rows past M must hold finite values
+  for (int i = threadIdx.x; i < nk * (kStepBytes / 16); i += kThreads)
+    reinterpret_cast<uint4*>(a)[i] = make_uint4(0u, 0u, 0u, 0u);
+  for (int m = warp; m < M; m += kThreads / 32) {
+    float acc = 0.f;
+    for (int v = lane; v < nvec; v += 32) {
+      float s8[8];
+      load_f<T, 8>(x + m * p.x_stride + k0 + v * 8, s8);
+      if (res != nullptr) {
+        float r8[8];
+        load_f<T, 8>(res + m * p.r_stride + k0 + v * 8, r8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s8[j] += r8[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc += s8[j] * s8[j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) rowpart[m] = acc;
+  }
+  __syncthreads();
+  if (p.splits > 1) cluster_sync_all();  // every CTA of the cluster has its row sums
+  if (static_cast<int>(threadIdx.x) < M) {
+    float total = 0.f;
+    if (p.splits > 1) {
+      for (int q = 0; q < p.splits; ++q) total += ld_dsmem_f32(smem_u32(rowpart + threadIdx.x), uint32_t(q));
+    } else {
+      total = rowpart[threadIdx.x];
+    }
+    rstd[threadIdx.x] = rsqrtf(total / static_cast<float>(p.K) + p.eps);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < M * nvec; i += kThreads) {
+    const int m = i / nvec, v = i - m * nvec;
+    const int64_t k = k0 + int64_t(v) * 8;
+    float s8[8], g8[8], y[8];
+    load_f<T, 8>(x + m * p.x_stride + k, s8);
+    if (res != nullptr) {
+      float r8[8];
+      load_f<T, 8>(res + m * p.r_stride + k, r8);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s8[j] += r8[j];
+      if (write_residual) store_f<T, 8>(res_out + m * p.ro_stride + k, s8);
+    }
+    load_f<T, 8>(gamma + k, g8);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = Elem<T>::round(s8[j] * rstd[m]) * g8[j];
+    const int step = v >> 3, chunk = v & 7;  // 8 vectors of 16 bytes per 128-byte row
+    *reinterpret_cast<Vec<T, 8>*>(a + step * kStepBytes + m * 128 + ((chunk ^ (m & 7)) << 4)) = pack_f<T, 8>(y);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+  __syncthreads();
+}
 
 // SWIGLU (no K split): the weight tile is gate rows [128 nb, +128) then the matching up rows
 // [I + 128 nb, +128) of vLLM's merged [2I, K] weight, fetched as one box of its [2, I, K]
 // view (w_map), so accumulator columns [0, 128) hold x.gate and [128, 256) x.up of the same
 // 128 output columns; the epilogue writes silu(gate) * up with the rounding points of the
 // unfused pair.
-template <typename T, int MP, int TT, bool SWIGLU = false>
+template <typename T, int MP, int TT, bool SWIGLU = false, bool NORM = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
     const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
     const SkinnyParams p) {
-  using L = SkinnySmem<MP, TT>;
+  static_assert(!NORM || (MP == kNormRows && TT == 1 && !SWIGLU), "fused norm: one 16-row token tile");
+  using L = std::conditional_t<NORM, SkinnyNormSmem, SkinnySmem<MP, TT>>;
   constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1296,7 +1422,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L::kEmpty);
   uint64_t* tmem_full = reinterpret_cast<uint64_t*>(smem + L::kTmemFull);
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemBase);
-  const uint32_t ring = smem_u32(smem);
+  const uint32_t ring = smem_u32(smem + L::kRingOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1329,19 +1455,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
+  // NORM: the first ring of weight tiles is requested before the norm prologue, so that
+  // the normalisation overlaps the weights' first round trip
+  const int prefilled = NORM ? (nk < kStages ? nk : kStages) : 0;
+  if constexpr (NORM) {
+    if (threadIdx.x == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&w_map)) : "memory");
+      for (int it = 0; it < prefilled; ++it) {
+        mbar_arrive_expect_tx(&full[it], L::kStage);
+        tma_load_2d(ring + it * L::kStage, &w_map, (kb0 + it) * BK, nb * kSkinnyBN, smem_u32(&full[it]));
+      }
+    }
+    norm_prologue<T>(p, smem, smem + L::kRowPart, smem + L::kRstd, kb0, nk, nb == 0);
+  }
+
   if (warp == 0) {
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&w_map)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&x_map)) : "memory");
-      int issued = 0;
-      for (int it = 0; it < nk; ++it) {
+      if (!NORM) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&w_map)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&x_map)) : "memory");
+      }
+      int issued = prefilled;
+      for (int it = prefilled; it < nk; ++it) {
         const int s = it % kStages;
         if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, p.err)) break;
         mbar_arrive_expect_tx(&full[s], L::kStage);
         const uint32_t stage = ring + s * L::kStage;
         const int kx = (kb0 + it) * BK;
+        if (!NORM) {
 #pragma unroll
-        for (int t = 0; t < TT; ++t) tma_load_2d(stage + t * L::kXTile, &x_map, kx, t * BM, smem_u32(&full[s]));
+          for (int t = 0; t < TT; ++t) tma_load_2d(stage + t * L::kXTile, &x_map, kx, t * BM, smem_u32(&full[s]));
+        }
         if (SWIGLU) {
           // one box of the [2, I, K] view: gate rows then the matching up rows
           tma_load_3d(stage + L::kX, &w_map, kx, nb * (kSkinnyBN / 2), 0, smem_u32(&full[s]));
@@ -1366,9 +1510,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
 #pragma unroll
-          for (int t = 0; t < TT; ++t)
-            umma_f16(tmem_base + t * kSkinnyBN, sw128_kmajor_desc(stage + t * L::kXTile) + 2 * k, bdesc + 2 * k,
-                     idesc, (it > 0 || k > 0) ? 1u : 0u);
+          for (int t = 0; t < TT; ++t) {
+            // NORM: the normalised rows of k-step `it`, resident ahead of the ring
+            const uint32_t a = NORM ? smem_u32(smem) + it * L::kXTile : stage + t * L::kXTile;
+            umma_f16(tmem_base + t * kSkinnyBN, sw128_kmajor_desc(a) + 2 * k, bdesc + 2 * k, idesc,
+                     (it > 0 || k > 0) ? 1u : 0u);
+          }
         }
         umma_commit(&empty[s]);
       }
@@ -1504,11 +1651,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
 
 // Splits of K for `n_tiles` weight tiles: the most SMs busy (n_tiles x splits <= the SM
 // count) whose clusters of `splits` CTAs are all resident at once.
-template <typename T, int MP, int TT, bool SWIGLU = false>
+// NORM: a CTA's K range must fit the resident A operand (at most kNormMaxSteps k-steps).
+template <typename T, int MP, int TT, bool SWIGLU = false, bool NORM = false>
 int launch_skinny(const CUtensorMap& wmap, const CUtensorMap& xmap, SkinnyParams prm, int n_tiles, cudaStream_t s,
                   int slot) {
-  using L = SkinnySmem<MP, TT>;
-  const void* fn = reinterpret_cast<const void*>(gemm_skinny_kernel<T, MP, TT, SWIGLU>);
+  using L = std::conditional_t<NORM, SkinnyNormSmem, SkinnySmem<MP, TT>>;
+  const void* fn = reinterpret_cast<const void*>(gemm_skinny_kernel<T, MP, TT, SWIGLU, NORM>);
   int st = ensure_smem_attribute(fn, L::kDynamicBytes, slot);
   if (st != NTB200_OK) return st;
   const int sms = num_sms();
@@ -1524,6 +1672,10 @@ int launch_skinny(const CUtensorMap& wmap, const CUtensorMap& xmap, SkinnyParams
   }
   prm.splits = splits;
   prm.k_steps_per_split = static_cast<int>(ceil_div(prm.k_steps_total, splits));
+  if (NORM && prm.k_steps_per_split > kNormMaxSteps)
+    return fail(NTB200_ERR_UNSUPPORTED_SHAPE,
+                "rms_norm_linear: K = %d k-steps per CTA exceeds %d (too few weight tiles to split K)",
+                prm.k_steps_per_split, kNormMaxSteps);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * splits));
   cfg.blockDim = dim3(kThreads);
@@ -1537,7 +1689,7 @@ int launch_skinny(const CUtensorMap& wmap, const CUtensorMap& xmap, SkinnyParams
   set_pdl_attribute(attr[1]);
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_skinny_kernel<T, MP, TT, SWIGLU>, wmap, xmap, prm);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_skinny_kernel<T, MP, TT, SWIGLU, NORM>, wmap, xmap, prm);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(NTB200_ERR_CUDA, "linear (M <= 256): launch failed: %s", cudaGetErrorString(e));
@@ -1889,4 +2041,63 @@ extern "C" int ntb200_linear(void* out, const void* x, const void* weight, const
     case 192: return launch_large<192>(out, x, weight, bias, M, N, K, x_row_stride, weight_row_stride, out_row_stride, bf16, s);
     default: return launch_large<256>(out, x, weight, bias, M, N, K, x_row_stride, weight_row_stride, out_row_stride, bf16, s);
   }
+}
+
+extern "C" int ntb200_rms_norm_linear(void* out, void* residual_out, const void* x, const void* residual,
+                                      const void* norm_weight, float eps, const void* weight, int64_t M, int64_t N,
+                                      int64_t K, int64_t x_row_stride, int64_t residual_row_stride,
+                                      int64_t residual_out_row_stride, int64_t weight_row_stride,
+                                      int64_t out_row_stride, int dtype, void* stream) {
+  using namespace ntb200;
+  if (dtype != NTB200_DTYPE_BF16 && dtype != NTB200_DTYPE_F16)
+    return fail(NTB200_ERR_UNSUPPORTED_DTYPE, "rms_norm_linear: dtype %d (bf16/f16 only)", dtype);
+  if (M < 0 || N < 0 || K <= 0) return fail(NTB200_ERR_INVALID_ARGUMENT, "rms_norm_linear: bad shape");
+  if (M == 0 || N == 0) return NTB200_OK;
+  if (M > kNormRows)
+    return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "rms_norm_linear: decode batches of at most %d tokens (M = %lld)",
+                kNormRows, static_cast<long long>(M));
+  if (!out || !x || !norm_weight || !weight) return fail(NTB200_ERR_INVALID_ARGUMENT, "rms_norm_linear: null pointer");
+  if ((residual == nullptr) != (residual_out == nullptr))
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "rms_norm_linear: residual and residual_out go together");
+  if (residual_out != nullptr && (residual_out == residual || residual_out == x))
+    return fail(NTB200_ERR_INVALID_ARGUMENT,
+                "rms_norm_linear: residual_out must not alias residual or x (other CTAs still read them)");
+  if (x_row_stride < K || weight_row_stride < K || out_row_stride < N ||
+      (residual != nullptr && (residual_row_stride < K || residual_out_row_stride < K)))
+    return fail(NTB200_ERR_INVALID_ARGUMENT, "rms_norm_linear: row stride too small");
+  const bool rows16 = x_row_stride % 8 == 0 && weight_row_stride % 8 == 0 &&
+                      (residual == nullptr || (residual_row_stride % 8 == 0 && residual_out_row_stride % 8 == 0));
+  if (K % 8 != 0 || !rows16 || !aligned16(x) || !aligned16(weight) || !aligned16(norm_weight) ||
+      (residual != nullptr && (!aligned16(residual) || !aligned16(residual_out))))
+    return fail(NTB200_ERR_MISALIGNED, "rms_norm_linear: 16-byte aligned rows and K %% 8 == 0 required");
+  const bool bf16 = dtype == NTB200_DTYPE_BF16;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t n_tiles = ceil_div(N, kSkinnyBN);
+  if (n_tiles > 0x7fffffff / 8) return fail(NTB200_ERR_UNSUPPORTED_SHAPE, "rms_norm_linear: too many tiles");
+  CUtensorMap wmap;
+  int st = make_kmajor_map(&wmap, weight, bf16, N, K, weight_row_stride, kSkinnyBN);
+  if (st != NTB200_OK) return st;
+  SkinnyParams sp = {};
+  sp.out = out;
+  sp.bias = nullptr;
+  sp.M = M;
+  sp.N = N;
+  sp.out_stride = out_row_stride;
+  sp.splits = 1;
+  sp.k_steps_total = static_cast<int>(ceil_div(K, BK));
+  sp.k_steps_per_split = sp.k_steps_total;
+  sp.n_half = 0;
+  sp.err = device_error_word();
+  sp.nx = x;
+  sp.nres = residual;
+  sp.nres_out = residual_out;
+  sp.ngamma = norm_weight;
+  sp.eps = eps;
+  sp.K = K;
+  sp.x_stride = x_row_stride;
+  sp.r_stride = residual_row_stride;
+  sp.ro_stride = residual_out_row_stride;
+  // the token operand comes from shared memory: the second map argument is unused
+  return bf16 ? launch_skinny<__nv_bfloat16, kNormRows, 1, false, true>(wmap, wmap, sp, static_cast<int>(n_tiles), s, 116)
+              : launch_skinny<__half, kNormRows, 1, false, true>(wmap, wmap, sp, static_cast<int>(n_tiles), s, 117);
 }

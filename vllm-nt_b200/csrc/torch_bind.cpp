@@ -576,6 +576,42 @@ void linear_silu_and_mul(at::Tensor out, const at::Tensor& x_in, const at::Tenso
         "linear_silu_and_mul");
 }
 
+// out [M, N] = rms_norm(x (+ residual)) * norm_weight . weight^T for M <= 16 rows; with a
+// residual, residual_out [M, K] receives x + residual
+void rms_norm_linear(at::Tensor out, const std::optional<at::Tensor>& residual_out, const at::Tensor& x,
+                     const std::optional<at::Tensor>& residual, const at::Tensor& norm_weight, double eps,
+                     const at::Tensor& weight) {
+  require_rows(weight, "weight");
+  const Rows xr = rows_of(x, "x");
+  const Rows orr = rows_of(out, "out");
+  same_leading(x, out, "rms_norm_linear");
+  TORCH_CHECK(weight.size(1) == xr.cols && orr.cols == weight.size(0) && weight.scalar_type() == x.scalar_type() &&
+                  out.scalar_type() == x.scalar_type() && norm_weight.is_contiguous() &&
+                  norm_weight.numel() == xr.cols && norm_weight.scalar_type() == x.scalar_type(),
+              "ntb200.rms_norm_linear: x [M, K], norm_weight [K], weight [N, K], out [M, N] of one dtype");
+  TORCH_CHECK(residual.has_value() == residual_out.has_value(),
+              "ntb200.rms_norm_linear: residual and residual_out go together");
+  const void* r = nullptr;
+  void* ro = nullptr;
+  int64_t rs = 0, ros = 0;
+  if (residual.has_value()) {
+    const Rows rr = rows_of(*residual, "residual");
+    const Rows ror = rows_of(*residual_out, "residual_out");
+    TORCH_CHECK(rr.rows == xr.rows && rr.cols == xr.cols && ror.rows == xr.rows && ror.cols == xr.cols &&
+                    residual->scalar_type() == x.scalar_type() && residual_out->scalar_type() == x.scalar_type(),
+                "ntb200.rms_norm_linear: residual / residual_out must match x");
+    r = residual->data_ptr();
+    ro = residual_out->data_ptr();
+    rs = rr.stride;
+    ros = ror.stride;
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  check(ntb200_rms_norm_linear(out.data_ptr(), ro, x.data_ptr(), r, norm_weight.data_ptr(), static_cast<float>(eps),
+                               weight.data_ptr(), xr.rows, weight.size(0), xr.cols, xr.stride, rs, ros,
+                               weight.stride(0), orr.stride, dtype_code(x), stream_of(x)),
+        "rms_norm_linear");
+}
+
 // out_index [M] (int64) = greedy argmax over the vocabulary of x [M, K] . weight [V, K]^T
 void linear_argmax(at::Tensor out_index, const at::Tensor& x_in, const at::Tensor& weight) {
   require_rows(weight, "weight");
@@ -730,6 +766,7 @@ TORCH_LIBRARY(ntb200, m) {
   m.def("linear(Tensor(a!) out, Tensor x, Tensor weight, Tensor? bias, Tensor(b!)? workspace) -> ()");
   m.def("linear_workspace_size(int m, int n, int k) -> int", &linear_workspace_size);
   m.def("linear_silu_and_mul(Tensor(a!) out, Tensor x, Tensor weight) -> ()");
+  m.def("rms_norm_linear(Tensor(a!) out, Tensor(b!)? residual_out, Tensor x, Tensor? residual, Tensor norm_weight, float eps, Tensor weight) -> ()");
   m.def("linear_argmax(Tensor(a!) out_index, Tensor x, Tensor weight) -> ()");
   m.def(
       "paged_attention_prefill(Tensor(a!) out, Tensor query, Tensor key_cache, Tensor value_cache, "
@@ -775,6 +812,7 @@ TORCH_LIBRARY_IMPL(ntb200, CUDA, m) {
   m.impl("allreduce_oneshot", &allreduce_oneshot);
   m.impl("allreduce_twoshot", &allreduce_twoshot);
   m.impl("linear_silu_and_mul", &linear_silu_and_mul);
+  m.impl("rms_norm_linear", &rms_norm_linear);
   m.impl("linear_argmax", &linear_argmax);
   m.impl("paged_attention_prefill", &paged_attention_prefill);
   m.impl("prefill_flash_layout", &prefill_flash_layout);

@@ -104,6 +104,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ntb200_linear_silu_and_mul": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p]
     ),
+    "ntb200_rms_norm_linear": (
+        c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_int64, c_int64, c_int64,
+                c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_void_p]
+    ),
     "ntb200_linear_argmax_workspace_size": (c_size_t, [c_int64, c_int64, c_int64]),
     "ntb200_linear_argmax": (
         c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_size_t,

@@ -40,6 +40,26 @@ def linear_silu_and_mul(input: torch.Tensor, gate_up: torch.Tensor) -> torch.Ten
     return out
 
 
+def rms_norm_linear(input: torch.Tensor, norm_weight: torch.Tensor, eps: float, weight: torch.Tensor,
+                    residual: torch.Tensor | None = None):
+    """RMSNorm (after adding residual, when given) of a decode batch of at most 16 rows,
+    then the projection by weight [N, K], as one kernel: the normalised rows are formed in
+    shared memory as the GEMM's input and never written.  Returns out [M, N], or
+    (out, new_residual) with a residual (new_residual = input + residual, a new tensor)."""
+    x = input if input.is_contiguous() else input.contiguous()
+    x2 = x.reshape(-1, x.shape[-1])
+    w = _k_contiguous(weight)
+    out = torch.empty((x2.shape[0], w.shape[0]), dtype=x.dtype, device=x.device)
+    if residual is None:
+        ops().rms_norm_linear(out, None, x2, None, norm_weight.contiguous(), float(eps), w)
+        return out.view(*input.shape[:-1], w.shape[0])
+    r2 = residual.reshape(-1, residual.shape[-1])
+    r2 = r2 if r2.is_contiguous() else r2.contiguous()
+    new_res = torch.empty_like(x2)
+    ops().rms_norm_linear(out, new_res, x2, r2, norm_weight.contiguous(), float(eps), w)
+    return out.view(*input.shape[:-1], w.shape[0]), new_res.view(input.shape)
+
+
 def linear_argmax(input: torch.Tensor, lm_head: torch.Tensor) -> torch.Tensor:
     """Greedy next tokens: argmax over the vocabulary of input @ lm_head^T (int64, one per
     row of input), with the logits compared at input's dtype and the first index winning
