@@ -291,3 +291,35 @@ def test_fused_rope_kv_store_attention_hook(_b200_config, vllm_ctx, monkeypatch)
     assert bits_equal(kvd.cpu(), ref_kv)
     assert not getattr(attn, "_ntb200_kv_stored", False)
     assert _hits(patching, "RoPEKVCache") == 1 and _hits(patching, "StoreKVCache") == 1
+
+
+def test_norm_qkv_decoder_hook(_b200_config, vllm_ctx):
+    """The opt-in LlamaDecoderLayer.forward patch on a decode batch: vLLM's (hooked) input
+    RMSNorm with its residual add and the qkv projection as one kernel; the new residual
+    bit for bit and the projection against the oracle's norm followed by its linear; the
+    attention and the MLP run as the layer's own modules."""
+    from vllm.model_executor.layers.layernorm import RMSNorm
+
+    patching = _b200_config
+    g = seeded(43)
+    t, hidden, hq, hk = 5, 4096, 32, 8
+    x = torch.randn(t, hidden, generator=g).to(torch.bfloat16)
+    r = torch.randn(t, hidden, generator=g).to(torch.bfloat16)
+    gam = (1 + 0.1 * torch.randn(hidden, generator=g)).to(torch.bfloat16)
+    w = (0.02 * torch.randn((hq + 2 * hk) * 128, hidden, generator=g)).to(torch.bfloat16)
+    ln = RMSNorm(hidden, eps=1e-5).to(device="cuda", dtype=torch.bfloat16)
+    ln.weight.data.copy_(gam)
+    qkv_proj = SimpleNamespace(quant_method=patching.UnquantizedLinearMethod(), bias=None, gather_output=False,
+                               weight=w.cuda())
+    self_attn = SimpleNamespace(qkv_proj=qkv_proj, q_size=hq * 128, kv_size=hk * 128,
+                                rotary_emb=lambda p, q, k: (q, k), attn=lambda q, k, v: q,
+                                o_proj=lambda a: (a, None))
+    layer = SimpleNamespace(input_layernorm=ln, self_attn=self_attn,
+                            post_attention_layernorm=lambda h, res: (h, res), mlp=lambda h: h)
+    fwd = patching._build_decoder_norm_qkv_forward(lambda *a: pytest.fail("fell back to vLLM"))
+    h, res = fwd(layer, torch.arange(t).cuda(), x.cuda(), r.cuda())
+    torch.cuda.synchronize()
+    h_ref, res_ref = oracle.fused_add_rms_norm(x, r, gam, 1e-5)
+    assert bits_equal(res.cpu(), res_ref)
+    torch.testing.assert_close(h.float().cpu(), oracle.linear(h_ref, w)[:, : hq * 128], rtol=2e-2, atol=2e-2)
+    assert _hits(patching, "RMSNormQKV") == 1

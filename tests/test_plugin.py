@@ -417,3 +417,34 @@ def test_fused_rope_kv_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypat
     assert calls == ["rope", "attn"] and out.shape == (3, 4)
     op = patching.get_usage_summary()["operators"]["RoPEKVCache"]
     assert op["hits"] == 0 and op["declined"] == {"not the base RotaryEmbedding": 1}
+
+
+def test_norm_qkv_decoder_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypatch):
+    """RMSNormQKV (LlamaDecoderLayer.forward) applies only when the config names it; a call
+    it cannot serve (here: CPU activations, then a batch above 16 tokens) runs vLLM's layer
+    forward and is counted as declined with its reason."""
+    spec = next(s for s in patching._FUNCTION_PATCH_SPECS if s.patch_id == "RMSNormQKV")
+    config.reset_backend_config_cache()
+    assert patching._function_patch_enabled(spec)  # all-b200.yaml names it
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/hybrid-default.yaml"))
+    config.reset_backend_config_cache()
+    assert not patching._function_patch_enabled(spec)
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml"))
+    config.reset_backend_config_cache()
+
+    from vllm.model_executor.layers.layernorm import RMSNorm
+
+    ln = RMSNorm.__new__(RMSNorm)  # vLLM's class without its config-dependent constructor
+    for name, value in (("weight", torch.ones(8)), ("variance_epsilon", 1e-6), ("has_weight", True),
+                        ("variance_size_override", None)):
+        object.__setattr__(ln, name, value)
+    qkv_proj = SimpleNamespace(quant_method=patching.UnquantizedLinearMethod(), bias=None, gather_output=False,
+                               weight=torch.zeros(12, 8))
+    layer = SimpleNamespace(input_layernorm=ln, self_attn=SimpleNamespace(qkv_proj=qkv_proj))
+    seen = []
+    fwd = patching._build_decoder_norm_qkv_forward(lambda self, p, h, r: (seen.append(h.shape[0]), (h, r))[1])
+    h = torch.zeros(3, 8)
+    assert fwd(layer, torch.arange(3), h, None)[0] is h
+    assert patching._why_not_norm_qkv(layer, torch.zeros(17, 8), None) == "activation / weight dtype or device"
+    op = patching.get_usage_summary()["operators"]["RMSNormQKV"]
+    assert seen == [3] and op["hits"] == 0 and op["declined"] == {"activation / weight dtype or device": 1}

@@ -21,6 +21,7 @@ from vllm_nt._ntops.torch.kv_cache import get_kv_from_cache as nt_get_kv_from_ca
 from vllm_nt._ntops.torch.kv_cache import store_kvcache as nt_store_kvcache
 from vllm_nt._ntops.torch.linear import linear as nt_linear
 from vllm_nt._ntops.torch.linear import linear_silu_and_mul as nt_linear_silu_and_mul
+from vllm_nt._ntops.torch.linear import rms_norm_linear as nt_rms_norm_linear
 from vllm_nt._ntops.torch.rms_norm import fused_add_rms_norm as nt_fused_add_rms_norm
 from vllm_nt._ntops.torch.rms_norm import gemma_rms_norm as nt_gemma_rms_norm
 from vllm_nt._ntops.torch.rms_norm import rms_norm as nt_rms_norm
@@ -77,6 +78,13 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 def gate_up_silu_and_mul(x: torch.Tensor, gate_up_weight: torch.Tensor) -> torch.Tensor:
     """silu(x W_gate^T) * (x W_up^T) for a merged [2I, K] gate_up weight in one kernel."""
     return nt_linear_silu_and_mul(x, gate_up_weight)
+
+
+def norm_linear(norm_layer: torch.nn.Module, x: torch.Tensor, residual: torch.Tensor | None,
+                weight: torch.Tensor):
+    """RMSNorm(x [+ residual]) followed by the projection by ``weight`` in one kernel (at
+    most 16 rows); returns the projection, or (projection, new residual)."""
+    return nt_rms_norm_linear(x, norm_layer.weight, norm_layer.variance_epsilon, weight, residual)
 
 
 def embedding(layer: torch.nn.Module, input_: torch.Tensor) -> torch.Tensor:

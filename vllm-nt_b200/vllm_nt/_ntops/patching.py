@@ -58,6 +58,7 @@ from vllm_nt._ntops.oot_support import (
     gate_up_silu_and_mul,
     linear,
     norm,
+    norm_linear,
     nt_apply_top_k_top_p,
     nt_paged_decode,  # noqa: F401  (re-exported for callers of the reference's module)
     nt_random_sample,
@@ -85,7 +86,7 @@ _FUNCTION_PATCH_FEATURES = dict.fromkeys(
 _OPERATOR_FEATURES = {"MatMul": "MM", "LMHead": "MM"}
 # Patches this build adds beyond the reference's op set: applied only when the config
 # names the op with a kernel backend, so configs written for the reference run unchanged.
-_OPT_IN_PATCHES = frozenset({"GateUpSiluAndMul", "RoPEKVCache"})
+_OPT_IN_PATCHES = frozenset({"GateUpSiluAndMul", "RoPEKVCache", "RMSNormQKV"})
 _HALF_TYPES = (torch.bfloat16, torch.float16)
 _FLOAT_TYPES = (torch.float32, torch.bfloat16, torch.float16)
 
@@ -134,7 +135,7 @@ _REGISTERED_VIA_PRIORITY = {via: rank for rank, via in enumerate(_VIA_ORDER)}
 _OPERATOR_NAMES = (
     "RMSNorm", "SiluAndMul", "GemmaRMSNorm", "MulAndSilu", "GeluAndMul", "GELU", "LayerNorm", "MatMul", "Embedding",
     "WPE", "NTWPEKernel", "LMHead", "PagedAttentionPrefill", "PagedAttentionDecode", "StoreKVCache",
-    "GateUpSiluAndMul", "RoPE", "RoPEKVCache", "SDPA", "TopKTopP", "RandomSample", "RejectionSample",
+    "GateUpSiluAndMul", "RoPE", "RoPEKVCache", "RMSNormQKV", "SDPA", "TopKTopP", "RandomSample", "RejectionSample",
 )
 _OPERATOR_STATS: dict[str, OperatorStats] = {}
 
@@ -715,6 +716,58 @@ def _why_not_fused_rope_kv(attn_mod: Any, q: torch.Tensor) -> str | None:
     return None
 
 
+def _opt_in_active(op: str) -> bool:
+    """Whether the opt-in patch ``op`` is configured with a kernel backend (and not disabled)."""
+    return op not in _disabled_ops() and op in load_backend_config().ops and backends.backend_enabled(op)
+
+
+def _attention_after_qkv(self: Any, positions: torch.Tensor, qkv: torch.Tensor) -> torch.Tensor:
+    """LlamaAttention.forward after its qkv projection: with the RoPEKVCache patch, the RoPE
+    of q/k and the KV store as one kernel (the layer's own KV-store call then finds its rows
+    stored); otherwise the module's RoPE and attention calls, as vLLM makes them."""
+    q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
+    reason = None if _opt_in_active("RoPEKVCache") else "RoPEKVCache not configured"
+    if reason is None:
+        reason = _why_not_fused_rope_kv(self, q)
+    slot_mapping = kv_cache = None
+    if reason is None:
+        from vllm.model_executor.layers.attention.attention import get_attention_context
+
+        try:
+            _, _, kv_cache, slot_mapping = get_attention_context(self.attn.layer_name)
+        except Exception:  # noqa: BLE001 - no forward context (e.g. a bare module call)
+            reason = "no forward context"
+        if reason is None and slot_mapping is None:
+            reason = "no slot mapping (profiling run)"
+        if reason is None:
+            reason = _attn_impl_reason(self.attn.impl, q.dtype, kv_cache, _KV_DIM_BY_IMPL[type(self.attn.impl).__name__])
+    if reason:
+        if backends.stats_enabled():
+            entry = _stats("RoPEKVCache")
+            entry.declined[reason] = entry.declined.get(reason, 0) + 1
+            backends.record_fallback("RoPEKVCache", "original")
+        q, k = self.rotary_emb(positions, q, k)
+        attn_output = self.attn(q, k, v)
+    else:
+        rot = self.rotary_emb
+        cache = rot._match_cos_sin_cache_dtype(q)
+        if cache is None:
+            cache = rot.cos_sin_cache
+        kv_dim = _KV_DIM_BY_IMPL[type(self.attn.impl).__name__]
+
+        def kernels():
+            _record_hit("RoPEKVCache", q)
+            rope_and_store_kv_cache_flash(positions, q, k, v, cache, rot.head_size, rot.rotary_dim, kv_cache,
+                                          slot_mapping, kv_dim)
+            self.attn._ntb200_kv_stored = True
+            return q, k
+
+        q, k = _route("RoPEKVCache", lambda: self.rotary_emb(positions, q, k), kernels)
+        attn_output = self.attn(q, k, v)
+    output, _ = self.o_proj(attn_output)
+    return output
+
+
 def _build_attention_rope_kv_forward(original: object) -> object:
     """Replacement for LlamaAttention.forward (and attention modules of the same shape):
     the RoPE of q/k and the KV store of the rotated k and the v become one kernel
@@ -726,47 +779,72 @@ def _build_attention_rope_kv_forward(original: object) -> object:
 
     def forward(self, positions, hidden_states):
         qkv, _ = self.qkv_proj(hidden_states)
-        q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
-        reason = _why_not_fused_rope_kv(self, q)
-        slot_mapping = kv_cache = None
-        if reason is None:
-            from vllm.model_executor.layers.attention.attention import get_attention_context
-
-            try:
-                _, _, kv_cache, slot_mapping = get_attention_context(self.attn.layer_name)
-            except Exception:  # noqa: BLE001 - no forward context (e.g. a bare module call)
-                reason = "no forward context"
-            if reason is None and slot_mapping is None:
-                reason = "no slot mapping (profiling run)"
-            if reason is None:
-                reason = _attn_impl_reason(self.attn.impl, q.dtype, kv_cache, _KV_DIM_BY_IMPL[type(self.attn.impl).__name__])
-        if reason:
-            if backends.stats_enabled():
-                entry = _stats("RoPEKVCache")
-                entry.declined[reason] = entry.declined.get(reason, 0) + 1
-                backends.record_fallback("RoPEKVCache", "original")
-            q, k = self.rotary_emb(positions, q, k)
-            attn_output = self.attn(q, k, v)
-        else:
-            rot = self.rotary_emb
-            cache = rot._match_cos_sin_cache_dtype(q)
-            if cache is None:
-                cache = rot.cos_sin_cache
-            kv_dim = _KV_DIM_BY_IMPL[type(self.attn.impl).__name__]
-
-            def kernels():
-                _record_hit("RoPEKVCache", q)
-                rope_and_store_kv_cache_flash(positions, q, k, v, cache, rot.head_size, rot.rotary_dim, kv_cache,
-                                              slot_mapping, kv_dim)
-                self.attn._ntb200_kv_stored = True
-                return q, k
-
-            q, k = _route("RoPEKVCache", lambda: self.rotary_emb(positions, q, k), kernels)
-            attn_output = self.attn(q, k, v)
-        output, _ = self.o_proj(attn_output)
-        return output
+        return _attention_after_qkv(self, positions, qkv)
 
     return _mark_function_patch(forward, "RoPEKVCache")
+
+
+_NORM_LINEAR_MAX_ROWS = 16  # ntb200_rms_norm_linear serves decode batches of at most 16 tokens
+
+
+def _why_not_norm_qkv(layer: Any, hidden: torch.Tensor, residual: torch.Tensor | None) -> str | None:
+    """input_layernorm is a plain RMSNorm and self_attn.qkv_proj an unquantised, bias-free
+    projection whose output stays on this rank, for a decode batch of at most 16 tokens."""
+    ln = getattr(layer, "input_layernorm", None)
+    qkv = getattr(getattr(layer, "self_attn", None), "qkv_proj", None)
+    if not isinstance(ln, layernorm.RMSNorm) or not getattr(ln, "has_weight", True) or \
+            getattr(ln, "variance_size_override", None) is not None:
+        return "input_layernorm is not a plain RMSNorm"
+    if not isinstance(getattr(qkv, "quant_method", None), UnquantizedLinearMethod):
+        return "quantised qkv_proj"
+    if getattr(qkv, "bias", None) is not None or getattr(qkv, "gather_output", False):
+        return "qkv_proj bias or gathered output"
+    w, g = getattr(qkv, "weight", None), getattr(ln, "weight", None)
+    if not (isinstance(w, torch.Tensor) and w.dim() == 2 and w.shape[1] % 8 == 0 and w.stride(-1) == 1):
+        return "qkv_proj weight layout"
+    if not (hidden.is_cuda and hidden.dtype in _HALF_TYPES and w.dtype == hidden.dtype and
+            isinstance(g, torch.Tensor) and g.dtype == hidden.dtype):
+        return "activation / weight dtype or device"
+    if hidden.dim() != 2 or hidden.shape[-1] != w.shape[1]:
+        return "hidden states are not [tokens, hidden]"
+    if hidden.shape[0] > _NORM_LINEAR_MAX_ROWS:
+        return f"more than {_NORM_LINEAR_MAX_ROWS} tokens"
+    if residual is not None and (residual.shape != hidden.shape or residual.dtype != hidden.dtype):
+        return "residual shape or dtype"
+    return None
+
+
+def _build_decoder_norm_qkv_forward(original: object) -> object:
+    """Replacement for LlamaDecoderLayer.forward: for decode batches of at most 16 tokens the
+    input RMSNorm (with its residual add) and the qkv projection become one kernel
+    (ntb200_rms_norm_linear), whose normalised rows never leave shared memory; the rest of
+    the layer runs as vLLM's code does (attention through the hooks, with the RoPEKVCache
+    fusion when that patch is configured)."""
+    if _already(original, "RMSNormQKV"):
+        return original
+    original_fn = cast(Callable[..., Any], original)
+
+    def forward(self, positions, hidden_states, residual):
+        vllm_path = lambda: original_fn(self, positions, hidden_states, residual)  # noqa: E731
+        reason = _why_not_norm_qkv(self, hidden_states, residual)
+        if reason:
+            return _decline("RMSNormQKV", reason, vllm_path)
+
+        def kernels():
+            _record_hit("RMSNormQKV", hidden_states)
+            attn = self.self_attn
+            if residual is None:
+                qkv = norm_linear(self.input_layernorm, hidden_states, None, attn.qkv_proj.weight)
+                res = hidden_states
+            else:
+                qkv, res = norm_linear(self.input_layernorm, hidden_states, residual, attn.qkv_proj.weight)
+            h = _attention_after_qkv(attn, positions, qkv)
+            h, res = self.post_attention_layernorm(h, res)
+            return self.mlp(h), res
+
+        return _route("RMSNormQKV", vllm_path, kernels)
+
+    return _mark_function_patch(forward, "RMSNormQKV")
 
 
 def _why_not_sampler_rows(x: torch.Tensor) -> str | None:
@@ -901,6 +979,8 @@ _FUNCTION_PATCH_SPECS: tuple[FunctionPatchSpec, ...] = (
     ),
     FunctionPatchSpec("RoPEKVCache", "vllm.model_executor.models.llama", "forward", "LlamaAttention", False,
                       _build_attention_rope_kv_forward),
+    FunctionPatchSpec("RMSNormQKV", "vllm.model_executor.models.llama", "forward", "LlamaDecoderLayer", False,
+                      _build_decoder_norm_qkv_forward),
 )
 
 _APPLIED_FUNCTION_PATCHES: list[_AppliedFunctionPatch] = []
