@@ -293,14 +293,20 @@ def test_fused_rope_kv_store_attention_hook(_b200_config, vllm_ctx, monkeypatch)
     assert _hits(patching, "RoPEKVCache") == 1 and _hits(patching, "StoreKVCache") == 1
 
 
-def test_norm_qkv_decoder_hook(_b200_config, vllm_ctx):
+def test_norm_qkv_decoder_hook(_b200_config, vllm_ctx, monkeypatch, tmp_path):
     """The opt-in LlamaDecoderLayer.forward patch on a decode batch: vLLM's (hooked) input
     RMSNorm with its residual add and the qkv projection as one kernel; the new residual
     bit for bit and the projection against the oracle's norm followed by its linear; the
     attention and the MLP run as the layer's own modules."""
     from vllm.model_executor.layers.layernorm import RMSNorm
 
+    from vllm_nt._ntops import config
+
     patching = _b200_config
+    cfg = tmp_path / "norm-qkv.yaml"  # all-b200.yaml with the opt-in RMSNormQKV named
+    cfg.write_text((ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml").read_text() + "  RMSNormQKV: b200\n")
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(cfg))
+    config.reset_backend_config_cache()
     g = seeded(43)
     t, hidden, hq, hk = 5, 4096, 32, 8
     x = torch.randn(t, hidden, generator=g).to(torch.bfloat16)

@@ -419,18 +419,19 @@ def test_fused_rope_kv_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypat
     assert op["hits"] == 0 and op["declined"] == {"not the base RotaryEmbedding": 1}
 
 
-def test_norm_qkv_decoder_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypatch):
-    """RMSNormQKV (LlamaDecoderLayer.forward) applies only when the config names it; a call
+def test_norm_qkv_decoder_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypatch, tmp_path):
+    """RMSNormQKV (LlamaDecoderLayer.forward) applies only when a config names it (the
+    shipped all-b200.yaml does not); a call
     it cannot serve (here: CPU activations, then a batch above 16 tokens) runs vLLM's layer
     forward and is counted as declined with its reason."""
     spec = next(s for s in patching._FUNCTION_PATCH_SPECS if s.patch_id == "RMSNormQKV")
     config.reset_backend_config_cache()
-    assert patching._function_patch_enabled(spec)  # all-b200.yaml names it
-    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/hybrid-default.yaml"))
+    assert not patching._function_patch_enabled(spec)  # all-b200.yaml leaves it out (measured slower)
+    cfg = tmp_path / "norm-qkv.yaml"
+    cfg.write_text((ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml").read_text() + "  RMSNormQKV: b200\n")
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(cfg))
     config.reset_backend_config_cache()
-    assert not patching._function_patch_enabled(spec)
-    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml"))
-    config.reset_backend_config_cache()
+    assert patching._function_patch_enabled(spec)
 
     from vllm.model_executor.layers.layernorm import RMSNorm
 

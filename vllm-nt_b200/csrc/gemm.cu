@@ -1288,25 +1288,28 @@ struct SkinnyParams {
 
 // Fused RMS norm (decode batches of at most kNormRows tokens): the normalised token rows of
 // the CTA's whole K range stay in shared memory (16 rows x 64 columns = 2 KB per k-step,
-// 128-byte swizzle, at most kNormMaxSteps of them) ahead of a ring of weight tiles; the MMA
-// reads its A operand from there, so only the weights stream through the ring.
+// 128-byte swizzle, at most STEPS of them) ahead of a ring of weight tiles; the MMA reads
+// its A operand from there, so only the weights stream through the ring.  The smaller A
+// region (32 k-steps) leaves room for 5 ring stages, the larger (64) for 3.
 constexpr int kNormRows = 16;
 constexpr int kNormMaxSteps = 64;
+template <int STEPS>
 struct SkinnyNormSmem {
   static constexpr int kXTile = kNormRows * BK * 2;  // 2 KB: one k-step of normalised rows
   static constexpr int kX = 0;                       // a ring stage holds the weight tile only
-  static constexpr int kA = kNormMaxSteps * kXTile;  // 128 KB
+  static constexpr int kA = STEPS * kXTile;
   static constexpr int kRingOff = kA;
   static constexpr int kStage = kSkinnyWTile;
-  static constexpr int kStages = 3;
+  static constexpr int kStages = (225 * 1024 - kA) / kStage > 6 ? 6 : (225 * 1024 - kA) / kStage;
   static constexpr int kRing = kStages * kStage;
   static constexpr int kFull = kRingOff + kRing;
   static constexpr int kEmpty = kFull + 8 * kStages;
   static constexpr int kTmemFull = kEmpty + 8 * kStages;
   static constexpr int kTmemBase = kTmemFull + 8;
   static constexpr int kRowPart = kTmemBase + 8;  // float[16]: this CTA's row sums of squares
-  static constexpr int kRstd = kRowPart + 64;     // float[16]: 1 / rms per row
-  static constexpr int kEnd = kRstd + 64;
+  static constexpr int kRstd = kRowPart + 64;     // float[16]: 1 / rms per row, then the
+                                                  // [warps][16] partial sums of the block
+  static constexpr int kEnd = kRstd + 64 + (kThreads / 32) * kNormRows * 4;
   static constexpr int kDynamicBytes = kEnd + 1024;
   static constexpr int kTmemCols = kSkinnyBN;
   static constexpr int kPartStride = kSkinnyBN + 4;
@@ -1337,6 +1340,7 @@ __device__ __forceinline__ void norm_prologue(const SkinnyParams& p, uint8_t* a,
                                               int kb0, int nk, bool write_residual) {
   float* rowpart = reinterpret_cast<float*>(rowpart_b);
   float* rstd = reinterpret_cast<float*>(rstd_b);
+  float* red = rstd + kNormRows;  // [kThreads / 32][kNormRows] warp partial sums (in the ring, free here)
   const T* x = static_cast<const T*>(p.nx);
   const T* res = static_cast<const T*>(p.nres);
   T* res_out = static_cast<T*>(p.nres_out);
@@ -1347,27 +1351,64 @@ __device__ __forceinline__ void norm_prologue(const SkinnyParams& p, uint8_t* a,
   const int nvec = k1 > k0 ? static_cast<int>((k1 - k0) / 8) : 0;  // 8-element vectors (K % 8 == 0)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kStepBytes = kNormRows * BK * 2;
+  using V = Vec<T, 8>;
   // the used A region starts at zero: past K the last k-step meets zero-filled weights, and
   // rows past M must hold finite values
   for (int i = threadIdx.x; i < nk * (kStepBytes / 16); i += kThreads)
     reinterpret_cast<uint4*>(a)[i] = make_uint4(0u, 0u, 0u, 0u);
-  for (int m = warp; m < M; m += kThreads / 32) {
-    float acc = 0.f;
-    for (int v = lane; v < nvec; v += 32) {
-      float s8[8];
-      load_f<T, 8>(x + m * p.x_stride + k0 + v * 8, s8);
-      if (res != nullptr) {
-        float r8[8];
-        load_f<T, 8>(res + m * p.r_stride + k0 + v * 8, r8);
+  // s = x (+ residual) of one 8-column vector for rows [m0, m0 + 8): every load issued at once
+  constexpr int kChunk = 8;
+  auto load_column = [&](int v, int m0, float (&s)[kChunk][8]) {
+    V xr[kChunk], rr[kChunk];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) s8[j] += r8[j];
+    for (int i = 0; i < kChunk; ++i) {
+      const int m = m0 + i;
+      if (m < M) {
+        xr[i] = *reinterpret_cast<const V*>(x + m * p.x_stride + k0 + v * 8);
+        if (res != nullptr) rr[i] = *reinterpret_cast<const V*>(res + m * p.r_stride + k0 + v * 8);
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc += s8[j] * s8[j];
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) rowpart[m] = acc;
+    for (int i = 0; i < kChunk; ++i) {
+      if (m0 + i < M) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          s[i][j] = Elem<T>::to_f(xr[i].v[j]);
+          if (res != nullptr) s[i][j] += Elem<T>::to_f(rr[i].v[j]);
+        }
+      }
+    }
+  };
+  // pass 1: the sum of squares of each row over this CTA's K range; thread t owns column
+  // vectors t, t + kThreads, ... of every row (fixed order, so the sums are reproducible)
+  float part[kNormRows];
+#pragma unroll
+  for (int m = 0; m < kNormRows; ++m) part[m] = 0.f;
+  for (int v = threadIdx.x; v < nvec; v += kThreads) {
+#pragma unroll
+    for (int m0 = 0; m0 < kNormRows; m0 += kChunk) {
+      if (m0 >= M) break;
+      float s[kChunk][8];
+      load_column(v, m0, s);
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i)
+        if (m0 + i < M)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) part[m0 + i] += s[i][j] * s[i][j];
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kNormRows; ++m) {
+    float t = part[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) red[warp * kNormRows + m] = t;
+  }
+  __syncthreads();
+  if (static_cast<int>(threadIdx.x) < M) {
+    float t = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) t += red[w * kNormRows + threadIdx.x];
+    rowpart[threadIdx.x] = t;
   }
   __syncthreads();
   if (p.splits > 1) cluster_sync_all();  // every CTA of the cluster has its row sums
@@ -1381,23 +1422,29 @@ __device__ __forceinline__ void norm_prologue(const SkinnyParams& p, uint8_t* a,
     rstd[threadIdx.x] = rsqrtf(total / static_cast<float>(p.K) + p.eps);
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < M * nvec; i += kThreads) {
-    const int m = i / nvec, v = i - m * nvec;
-    const int64_t k = k0 + int64_t(v) * 8;
-    float s8[8], g8[8], y[8];
-    load_f<T, 8>(x + m * p.x_stride + k, s8);
-    if (res != nullptr) {
-      float r8[8];
-      load_f<T, 8>(res + m * p.r_stride + k, r8);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) s8[j] += r8[j];
-      if (write_residual) store_f<T, 8>(res_out + m * p.ro_stride + k, s8);
-    }
-    load_f<T, 8>(gamma + k, g8);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) y[j] = Elem<T>::round(s8[j] * rstd[m]) * g8[j];
+  // pass 2: the normalised rows into the resident A operand (the inputs again, from L2)
+  for (int v = threadIdx.x; v < nvec; v += kThreads) {
+    float g8[8];
+    load_f<T, 8>(gamma + k0 + v * 8, g8);
     const int step = v >> 3, chunk = v & 7;  // 8 vectors of 16 bytes per 128-byte row
-    *reinterpret_cast<Vec<T, 8>*>(a + step * kStepBytes + m * 128 + ((chunk ^ (m & 7)) << 4)) = pack_f<T, 8>(y);
+#pragma unroll
+    for (int m0 = 0; m0 < kNormRows; m0 += kChunk) {
+      if (m0 >= M) break;
+      float s[kChunk][8];
+      load_column(v, m0, s);
+#pragma unroll
+      for (int i = 0; i < kChunk; ++i) {
+        const int m = m0 + i;
+        if (m < M) {
+          if (res != nullptr && write_residual) store_f<T, 8>(res_out + m * p.ro_stride + k0 + v * 8, s[i]);
+          const float r = rstd[m];
+          float y[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[j] = Elem<T>::round(s[i][j] * r) * g8[j];
+          *reinterpret_cast<V*>(a + step * kStepBytes + m * 128 + ((chunk ^ (m & 7)) << 4)) = pack_f<T, 8>(y);
+        }
+      }
+    }
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
   __syncthreads();
@@ -1408,12 +1455,12 @@ __device__ __forceinline__ void norm_prologue(const SkinnyParams& p, uint8_t* a,
 // view (w_map), so accumulator columns [0, 128) hold x.gate and [128, 256) x.up of the same
 // 128 output columns; the epilogue writes silu(gate) * up with the rounding points of the
 // unfused pair.
-template <typename T, int MP, int TT, bool SWIGLU = false, bool NORM = false>
+template <typename T, int MP, int TT, bool SWIGLU = false, bool NORM = false, int NSTEPS = kNormMaxSteps>
 __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
     const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
     const SkinnyParams p) {
   static_assert(!NORM || (MP == kNormRows && TT == 1 && !SWIGLU), "fused norm: one 16-row token tile");
-  using L = std::conditional_t<NORM, SkinnyNormSmem, SkinnySmem<MP, TT>>;
+  using L = std::conditional_t<NORM, SkinnyNormSmem<NSTEPS>, SkinnySmem<MP, TT>>;
   constexpr int kStages = L::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -1652,16 +1699,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
 // Splits of K for `n_tiles` weight tiles: the most SMs busy (n_tiles x splits <= the SM
 // count) whose clusters of `splits` CTAs are all resident at once.
 // NORM: a CTA's K range must fit the resident A operand (at most kNormMaxSteps k-steps).
-template <typename T, int MP, int TT, bool SWIGLU = false, bool NORM = false>
+template <typename T, int MP, int TT, bool SWIGLU = false, bool NORM = false, int NSTEPS = kNormMaxSteps>
 int launch_skinny(const CUtensorMap& wmap, const CUtensorMap& xmap, SkinnyParams prm, int n_tiles, cudaStream_t s,
-                  int slot) {
-  using L = std::conditional_t<NORM, SkinnyNormSmem, SkinnySmem<MP, TT>>;
-  const void* fn = reinterpret_cast<const void*>(gemm_skinny_kernel<T, MP, TT, SWIGLU, NORM>);
+                  int slot, int forced_splits = 0) {
+  using L = std::conditional_t<NORM, SkinnyNormSmem<NSTEPS>, SkinnySmem<MP, TT>>;
+  const void* fn = reinterpret_cast<const void*>(gemm_skinny_kernel<T, MP, TT, SWIGLU, NORM, NSTEPS>);
   int st = ensure_smem_attribute(fn, L::kDynamicBytes, slot);
   if (st != NTB200_OK) return st;
   const int sms = num_sms();
-  int splits = 1;
-  for (int cand = SWIGLU ? 1 : 8; cand >= 2; --cand) {
+  int splits = forced_splits > 0 ? forced_splits : 1;
+  for (int cand = (SWIGLU || forced_splits > 0) ? 1 : 8; cand >= 2; --cand) {
     if (cand > prm.k_steps_total || int64_t(n_tiles) * cand > sms) continue;
     const int per = static_cast<int>(ceil_div(prm.k_steps_total, cand));
     const int used = static_cast<int>(ceil_div(prm.k_steps_total, per));
@@ -1672,10 +1719,14 @@ int launch_skinny(const CUtensorMap& wmap, const CUtensorMap& xmap, SkinnyParams
   }
   prm.splits = splits;
   prm.k_steps_per_split = static_cast<int>(ceil_div(prm.k_steps_total, splits));
-  if (NORM && prm.k_steps_per_split > kNormMaxSteps)
+  if (NORM && prm.k_steps_per_split > NSTEPS)
     return fail(NTB200_ERR_UNSUPPORTED_SHAPE,
                 "rms_norm_linear: K = %d k-steps per CTA exceeds %d (too few weight tiles to split K)",
-                prm.k_steps_per_split, kNormMaxSteps);
+                prm.k_steps_per_split, NSTEPS);
+  // a CTA range of at most 32 k-steps takes the layout with the deeper weight ring
+  if constexpr (NORM && NSTEPS == kNormMaxSteps)
+    if (prm.k_steps_per_split <= 32)
+      return launch_skinny<T, MP, TT, SWIGLU, NORM, 32>(wmap, xmap, prm, n_tiles, s, slot + 2, splits);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * splits));
   cfg.blockDim = dim3(kThreads);
@@ -1689,7 +1740,7 @@ int launch_skinny(const CUtensorMap& wmap, const CUtensorMap& xmap, SkinnyParams
   set_pdl_attribute(attr[1]);
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_skinny_kernel<T, MP, TT, SWIGLU, NORM>, wmap, xmap, prm);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_skinny_kernel<T, MP, TT, SWIGLU, NORM, NSTEPS>, wmap, xmap, prm);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(NTB200_ERR_CUDA, "linear (M <= 256): launch failed: %s", cudaGetErrorString(e));
