@@ -11,6 +11,9 @@ the plugin patches; other paths are inside the vllm_nt reference project):
 * floating-point ops follow vLLM's torch-native implementations -- the oracle named for
   parity -- with the same fp32 intermediates and the same rounding points to the storage
   dtype (GemmaRMSNorm included: (1 + w) in fp32, one rounding of the product);
+* the fused RMSNorm + projection restates its own rounding points (s * w rounded once,
+  1 / rms applied to the fp32 products); its tests also compare it, and the reference's
+  unfused pair, with the unrounded fp64 value;
 * the LM head's greedy token is the first index of the largest bf16-rounded logit of the
   fp32 projection (F.linear, then torch.argmax, as vLLM's greedy sampler takes it);
 * the KV-cache store and the embedding gather are byte copies (numpy on raw 16-bit views),
@@ -44,6 +47,8 @@ from oracle.ops import (  # noqa: F401
     random_sample_from_draws,
     reshape_and_cache,
     rms_norm,
+    rms_norm_linear,
+    rms_norm_linear_exact,
     rope_and_cache,
     rope_neox,
     silu_and_mul,

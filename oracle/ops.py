@@ -335,6 +335,34 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     return y
 
 
+def rms_norm_linear(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, weight: torch.Tensor,
+                    residual: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """The fused decode entry point's arithmetic for RMSNorm followed by a projection (the
+    reference runs the two as separate ops: vllm_nt/_ntops/oot_support.py:32-48, then
+    vllm_nt/_ntops/torch/linear.py:7-21).  s = x (+ residual) in fp32; the GEMM input is
+    s * norm_weight rounded once to x's dtype; the 1 / rms of each row, rsqrt(mean(s^2) + eps),
+    scales the fp32 products.  Returns (fp32 output before its final rounding, s rounded to
+    x's dtype or None)."""
+    s = x.to(torch.float32)
+    if residual is not None:
+        s = s + residual.to(torch.float32)
+    rstd = torch.rsqrt(s.pow(2).mean(dim=-1, keepdim=True) + eps)
+    y = _round(s * norm_weight.to(torch.float32), x.dtype)
+    out = rstd * (y @ weight.to(torch.float32).t())
+    return out, (s.to(x.dtype) if residual is not None else None)
+
+
+def rms_norm_linear_exact(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, weight: torch.Tensor,
+                          residual: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm then the projection in fp64 with no intermediate rounding: the value both the
+    fused entry point and the reference's unfused pair approximate."""
+    s = x.to(torch.float64)
+    if residual is not None:
+        s = s + residual.to(torch.float64)
+    h = s * torch.rsqrt(s.pow(2).mean(dim=-1, keepdim=True) + eps) * norm_weight.to(torch.float64)
+    return h @ weight.to(torch.float64).t()
+
+
 # --------------------------------------------------------------------------------------
 # Sampler  (vllm_nt/_ntops/torch/sampler.py:4-42; vllm:v1/sample/ops/topk_topp_sampler.py
 #           apply_top_k_top_p_pytorch and random_sample)

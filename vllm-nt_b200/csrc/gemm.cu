@@ -1293,6 +1293,9 @@ struct SkinnyParams {
 // region (32 k-steps) leaves room for 5 ring stages, the larger (64) for 3.
 constexpr int kNormRows = 16;
 constexpr int kNormMaxSteps = 64;
+constexpr int kNormThreads = 128;                  // the epilogue warps run the norm prologue
+constexpr int kNormFirstThread = kThreads - kNormThreads;
+constexpr int kNormGroupSteps = kNormThreads / 8;  // one 16-byte column vector per thread
 template <int STEPS>
 struct SkinnyNormSmem {
   static constexpr int kXTile = kNormRows * BK * 2;  // 2 KB: one k-step of normalised rows
@@ -1308,8 +1311,9 @@ struct SkinnyNormSmem {
   static constexpr int kTmemBase = kTmemFull + 8;
   static constexpr int kRowPart = kTmemBase + 8;  // float[16]: this CTA's row sums of squares
   static constexpr int kRstd = kRowPart + 64;     // float[16]: 1 / rms per row, then the
-                                                  // [warps][16] partial sums of the block
-  static constexpr int kEnd = kRstd + 64 + (kThreads / 32) * kNormRows * 4;
+                                                  // [4 warps][16] partial sums of the prologue
+  static constexpr int kAReady = kRstd + 64 + (kNormThreads / 32) * kNormRows * 4;  // per k-step group
+  static constexpr int kEnd = kAReady + 8 * (STEPS / kNormGroupSteps);
   static constexpr int kDynamicBytes = kEnd + 1024;
   static constexpr int kTmemCols = kSkinnyBN;
   static constexpr int kPartStride = kSkinnyBN + 4;
@@ -1328,19 +1332,22 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank
   return v;
 }
 
-// NORM prologue (every thread of the CTA): the CTA's K range [64 kb0, +64 nk) of
-// RMSNorm(x [+ residual]) * norm_weight for the M <= 16 token rows, rounded as
-// rms_norm_kernel rounds it for rows that fit its registers (the normalised fp32 value
-// rounded to T, times the weight, rounded again), into the resident A operand (16 rows x 64
-// columns per k-step, 128-byte swizzle).  The row statistics need whole rows: each CTA sums
-// the squares over its K range and the CTAs splitting K for this weight tile add those sums
-// over DSMEM in rank order.  The CTAs of weight tile 0 also write the new residual.
+// NORM prologue, run by the four epilogue warps while the producer streams the weights:
+// the CTA's K range [64 kb0, +64 nk) of the M <= 16 token rows, s = x (+ residual) in fp32,
+// this CTA's row sums of s^2 (into rowpart, summed in a fixed order), and round(s *
+// norm_weight) into the resident A operand (16 rows x 64 columns per k-step, 128-byte
+// swizzle; rows past M and columns past K hold zeros).  Thread e of the 128 writes column
+// vector e of each group of kNormGroupSteps k-steps and then arrives on that group's
+// a_ready barrier, so the MMAs of a group start as soon as its rows are in place.  The MMAs
+// wait for no row statistics: RMSNorm scales each row by 1 / rms, which is linear in the
+// product, so the epilogue applies it once the CTAs splitting K have their sums
+// (out[m, n] = rstd[m] * sum_k round(s[m, k] w[k]) W[n, k]).  The CTAs of weight tile 0 also
+// write the new residual.
 template <typename T>
-__device__ __forceinline__ void norm_prologue(const SkinnyParams& p, uint8_t* a, uint8_t* rowpart_b, uint8_t* rstd_b,
-                                              int kb0, int nk, bool write_residual) {
+__device__ __forceinline__ void norm_prologue(const SkinnyParams& p, uint8_t* a, uint64_t* a_ready, uint8_t* rowpart_b,
+                                              uint8_t* red_b, int kb0, int nk, bool write_residual) {
   float* rowpart = reinterpret_cast<float*>(rowpart_b);
-  float* rstd = reinterpret_cast<float*>(rstd_b);
-  float* red = rstd + kNormRows;  // [kThreads / 32][kNormRows] warp partial sums (in the ring, free here)
+  float* red = reinterpret_cast<float*>(red_b);  // [4 warps][kNormRows] warp partial sums
   const T* x = static_cast<const T*>(p.nx);
   const T* res = static_cast<const T*>(p.nres);
   T* res_out = static_cast<T*>(p.nres_out);
@@ -1349,70 +1356,84 @@ __device__ __forceinline__ void norm_prologue(const SkinnyParams& p, uint8_t* a,
   const int64_t k0 = int64_t(kb0) * BK;
   const int64_t k1 = p.K < k0 + int64_t(nk) * BK ? p.K : k0 + int64_t(nk) * BK;
   const int nvec = k1 > k0 ? static_cast<int>((k1 - k0) / 8) : 0;  // 8-element vectors (K % 8 == 0)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = static_cast<int>(threadIdx.x) - kNormFirstThread;    // 0 .. kNormThreads - 1
+  const int lane = threadIdx.x & 31;
   constexpr int kStepBytes = kNormRows * BK * 2;
+  constexpr int kChunk = 8;  // rows whose loads are in flight together
   using V = Vec<T, 8>;
-  // the used A region starts at zero: past K the last k-step meets zero-filled weights, and
-  // rows past M must hold finite values
-  for (int i = threadIdx.x; i < nk * (kStepBytes / 16); i += kThreads)
-    reinterpret_cast<uint4*>(a)[i] = make_uint4(0u, 0u, 0u, 0u);
-  // s = x (+ residual) of one 8-column vector for rows [m0, m0 + 8): every load issued at once
-  constexpr int kChunk = 8;
-  auto load_column = [&](int v, int m0, float (&s)[kChunk][8]) {
-    V xr[kChunk], rr[kChunk];
-#pragma unroll
-    for (int i = 0; i < kChunk; ++i) {
-      const int m = m0 + i;
-      if (m < M) {
-        xr[i] = *reinterpret_cast<const V*>(x + m * p.x_stride + k0 + v * 8);
-        if (res != nullptr) rr[i] = *reinterpret_cast<const V*>(res + m * p.r_stride + k0 + v * 8);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < kChunk; ++i) {
-      if (m0 + i < M) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          s[i][j] = Elem<T>::to_f(xr[i].v[j]);
-          if (res != nullptr) s[i][j] += Elem<T>::to_f(rr[i].v[j]);
-        }
-      }
-    }
-  };
-  // pass 1: the sum of squares of each row over this CTA's K range; thread t owns column
-  // vectors t, t + kThreads, ... of every row (fixed order, so the sums are reproducible)
   float part[kNormRows];
 #pragma unroll
   for (int m = 0; m < kNormRows; ++m) part[m] = 0.f;
-  for (int v = threadIdx.x; v < nvec; v += kThreads) {
+  const int groups = (nk + kNormGroupSteps - 1) / kNormGroupSteps;
+  for (int grp = 0; grp < groups; ++grp) {
+    const int v = grp * kNormThreads + e;  // kNormThreads vectors = kNormGroupSteps k-steps
+    if (v < nk * (BK / 8)) {
+      const int step = v >> 3, chunk = v & 7;  // 8 vectors of 16 bytes per 128-byte row
+      uint8_t* st = a + step * kStepBytes;
+      if (v < nvec) {
+        float g8[8];
+        load_f<T, 8>(gamma + k0 + v * 8, g8);
 #pragma unroll
-    for (int m0 = 0; m0 < kNormRows; m0 += kChunk) {
-      if (m0 >= M) break;
-      float s[kChunk][8];
-      load_column(v, m0, s);
+        for (int m0 = 0; m0 < kNormRows; m0 += kChunk) {
+          if (m0 >= M) break;
+          V xr[kChunk], rr[kChunk];
 #pragma unroll
-      for (int i = 0; i < kChunk; ++i)
-        if (m0 + i < M)
+          for (int i = 0; i < kChunk; ++i) {
+            const int m = m0 + i;
+            if (m < M) {
+              xr[i] = *reinterpret_cast<const V*>(x + m * p.x_stride + k0 + v * 8);
+              if (res != nullptr) rr[i] = *reinterpret_cast<const V*>(res + m * p.r_stride + k0 + v * 8);
+            }
+          }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) part[m0 + i] += s[i][j] * s[i][j];
+          for (int i = 0; i < kChunk; ++i) {
+            const int m = m0 + i;
+            if (m < M) {
+              float sv[8], y[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                sv[j] = Elem<T>::to_f(xr[i].v[j]);
+                if (res != nullptr) sv[j] += Elem<T>::to_f(rr[i].v[j]);
+                part[m0 + i] += sv[j] * sv[j];
+                y[j] = sv[j] * g8[j];
+              }
+              if (res != nullptr && write_residual) store_f<T, 8>(res_out + m * p.ro_stride + k0 + v * 8, sv);
+              *reinterpret_cast<V*>(st + m * 128 + ((chunk ^ (m & 7)) << 4)) = pack_f<T, 8>(y);
+            }
+          }
+        }
+      }
+      // rows past M, and the whole column past K, are zeros
+#pragma unroll
+      for (int m = 0; m < kNormRows; ++m)
+        if (m >= M || v >= nvec)
+          *reinterpret_cast<uint4*>(st + m * 128 + ((chunk ^ (m & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
     }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+    mbar_arrive(&a_ready[grp]);
   }
 #pragma unroll
   for (int m = 0; m < kNormRows; ++m) {
     float t = part[m];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (lane == 0) red[warp * kNormRows + m] = t;
+    if (lane == 0) red[(e >> 5) * kNormRows + m] = t;
   }
-  __syncthreads();
-  if (static_cast<int>(threadIdx.x) < M) {
+  asm volatile("bar.sync 1, %0;" ::"r"(kNormThreads) : "memory");
+  if (e < M) {
     float t = 0.f;
-    for (int w = 0; w < kThreads / 32; ++w) t += red[w * kNormRows + threadIdx.x];
-    rowpart[threadIdx.x] = t;
+    for (int w = 0; w < kNormThreads / 32; ++w) t += red[w * kNormRows + e];
+    rowpart[e] = t;
   }
-  __syncthreads();
-  if (p.splits > 1) cluster_sync_all();  // every CTA of the cluster has its row sums
-  if (static_cast<int>(threadIdx.x) < M) {
+}
+
+// 1 / rms of each token row into rstd[0, M), from the row sums of s^2 of the CTAs splitting
+// K (read over DSMEM in rank order; the caller has passed a cluster barrier that follows
+// every CTA's prologue), or from the CTA's own sums when K is not split.  Every thread of
+// the CTA calls it.
+__device__ __forceinline__ void norm_rstd(const SkinnyParams& p, float* rowpart, float* rstd) {
+  __syncthreads();  // this CTA's rowpart is complete
+  if (static_cast<int>(threadIdx.x) < p.M) {
     float total = 0.f;
     if (p.splits > 1) {
       for (int q = 0; q < p.splits; ++q) total += ld_dsmem_f32(smem_u32(rowpart + threadIdx.x), uint32_t(q));
@@ -1421,32 +1442,6 @@ __device__ __forceinline__ void norm_prologue(const SkinnyParams& p, uint8_t* a,
     }
     rstd[threadIdx.x] = rsqrtf(total / static_cast<float>(p.K) + p.eps);
   }
-  __syncthreads();
-  // pass 2: the normalised rows into the resident A operand (the inputs again, from L2)
-  for (int v = threadIdx.x; v < nvec; v += kThreads) {
-    float g8[8];
-    load_f<T, 8>(gamma + k0 + v * 8, g8);
-    const int step = v >> 3, chunk = v & 7;  // 8 vectors of 16 bytes per 128-byte row
-#pragma unroll
-    for (int m0 = 0; m0 < kNormRows; m0 += kChunk) {
-      if (m0 >= M) break;
-      float s[kChunk][8];
-      load_column(v, m0, s);
-#pragma unroll
-      for (int i = 0; i < kChunk; ++i) {
-        const int m = m0 + i;
-        if (m < M) {
-          if (res != nullptr && write_residual) store_f<T, 8>(res_out + m * p.ro_stride + k0 + v * 8, s[i]);
-          const float r = rstd[m];
-          float y[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) y[j] = Elem<T>::round(s[i][j] * r) * g8[j];
-          *reinterpret_cast<V*>(a + step * kStepBytes + m * 128 + ((chunk ^ (m & 7)) << 4)) = pack_f<T, 8>(y);
-        }
-      }
-    }
-  }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
   __syncthreads();
 }
 
@@ -1469,6 +1464,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
   uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L::kEmpty);
   uint64_t* tmem_full = reinterpret_cast<uint64_t*>(smem + L::kTmemFull);
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemBase);
+  // NORM: the normalised rows of k-step group g are in shared memory once a_ready[g] completes
+  uint64_t* a_ready = nullptr;
+  if constexpr (NORM) a_ready = reinterpret_cast<uint64_t*>(smem + L::kAReady);
   const uint32_t ring = smem_u32(smem + L::kRingOff);
 
   const int warp = threadIdx.x >> 5;
@@ -1486,6 +1484,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
       mbar_init(&empty[s], 1);
     }
     mbar_init(tmem_full, 1);
+    if constexpr (NORM)
+      for (int g = 0; g < NSTEPS / kNormGroupSteps; ++g) mbar_init(&a_ready[g], kNormThreads);
     fence_mbar_init();
   }
   // tensor memory is allocated only after the preceding kernel has finished
@@ -1502,28 +1502,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
 
-  // NORM: the first ring of weight tiles is requested before the norm prologue, so that
-  // the normalisation overlaps the weights' first round trip
-  const int prefilled = NORM ? (nk < kStages ? nk : kStages) : 0;
-  if constexpr (NORM) {
-    if (threadIdx.x == 0) {
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&w_map)) : "memory");
-      for (int it = 0; it < prefilled; ++it) {
-        mbar_arrive_expect_tx(&full[it], L::kStage);
-        tma_load_2d(ring + it * L::kStage, &w_map, (kb0 + it) * BK, nb * kSkinnyBN, smem_u32(&full[it]));
-      }
-    }
-    norm_prologue<T>(p, smem, smem + L::kRowPart, smem + L::kRstd, kb0, nk, nb == 0);
-  }
-
   if (warp == 0) {
     if (lane == 0) {
-      if (!NORM) {
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&w_map)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&x_map)) : "memory");
-      }
-      int issued = prefilled;
-      for (int it = prefilled; it < nk; ++it) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&w_map)) : "memory");
+      if (!NORM) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&x_map)) : "memory");
+      int issued = 0;
+      for (int it = 0; it < nk; ++it) {
         const int s = it % kStages;
         if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, p.err)) break;
         mbar_arrive_expect_tx(&full[s], L::kStage);
@@ -1550,6 +1534,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
       const uint32_t idesc = make_idesc(std::is_same<T, __nv_bfloat16>::value, BM, kSkinnyBN);
       for (int it = 0; it < nk; ++it) {
         const int s = it % kStages;
+        if (NORM && it % kNormGroupSteps == 0 && !mbar_wait(&a_ready[it / kNormGroupSteps], 0, p.err)) break;
         if (!mbar_wait(&full[s], (it / kStages) & 1, p.err)) break;
         tc_fence_after();
         const uint32_t stage = ring + s * L::kStage;
@@ -1568,6 +1553,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
       }
       umma_commit(tmem_full);  // also the "all MMAs done" point before TMEM is released
     }
+  } else if constexpr (NORM) {
+    norm_prologue<T>(p, smem, a_ready, smem + L::kRowPart, smem + L::kRstd + 64, kb0, nk, nb == 0);
   }
 
   T* out = static_cast<T*>(p.out);
@@ -1606,12 +1593,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
       tc_fence_before();
     }
   } else if (p.splits == 1) {
+    // NORM: each row scaled by its 1 / rms
+    float* rstd = nullptr;
+    if constexpr (NORM) {
+      rstd = reinterpret_cast<float*>(smem + L::kRstd);
+      norm_rstd(p, reinterpret_cast<float*>(smem + L::kRowPart), rstd);
+    }
     // TMEM -> registers -> global: a thread writes 32 consecutive columns of its row at a time
     if (epilogue) {
 #pragma unroll 1
       for (int t = 0; t < TT; ++t) {
         if (int64_t(t) * BM + quad * 32 >= p.M) continue;  // the warp's rows are all past M
         const int64_t m = int64_t(t) * BM + row_in_tile;
+        float scale = 1.f;
+        if constexpr (NORM) scale = m < p.M ? rstd[m] : 0.f;
 #pragma unroll 1
         for (int c = 0; c < kSkinnyBN / 32; ++c) {
           uint32_t r[32];
@@ -1620,7 +1615,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
           if (m < p.M) {
             float v[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = acc_ok ? __uint_as_float(r[i]) : 0.f;
+            for (int i = 0; i < 32; ++i) v[i] = acc_ok ? __uint_as_float(r[i]) * scale : 0.f;
             store_row32<T>(out + m * p.out_stride, n0 + c * 32, p.N, v, bias);
           }
         }
@@ -1651,6 +1646,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
       }
       // every CTA of the cluster has its partial rows of token tile t in shared memory
       cluster_sync_all();
+      float* rstd = nullptr;
+      if constexpr (NORM) {
+        rstd = reinterpret_cast<float*>(smem + L::kRstd);
+        norm_rstd(p, reinterpret_cast<float*>(smem + L::kRowPart), rstd);
+      }
       const int units = rows * (kSkinnyBN / 4);
       const int u0 = static_cast<int>(int64_t(units) * split / p.splits);
       const int u1 = static_cast<int>(int64_t(units) * (split + 1) / p.splits);
@@ -1672,6 +1672,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(
           acc[1] += v[r].y;
           acc[2] += v[r].z;
           acc[3] += v[r].w;
+        }
+        if constexpr (NORM) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[i] *= rstd[row];
         }
         T* orow = out + (int64_t(t) * BM + row) * p.out_stride;
         if (col + 4 <= p.N && ((reinterpret_cast<uintptr_t>(orow + col) & 7u) == 0)) {
