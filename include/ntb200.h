@@ -329,15 +329,16 @@ int ntb200_linear_silu_and_mul(void* out, const void* x, const void* weight, int
 
 /* ---------------------------------------------------------------------------------------
  * Fused (residual-add) RMS norm + projection for decode batches of at most 16 tokens:
- *   s = x (+ residual);  residual_out = s (rounded);  h = rms_norm(s) * norm_weight;
- *   out[M, N] = h . W^T
+ *   s = x (+ residual) in fp32;  residual_out = s (rounded);
+ *   out[m, n] = rsqrt(mean_k(s[m, k]^2) + eps) * sum_k round(s[m, k] * norm_weight[k]) W[n, k]
  * Replaces the RMSNorm hook followed by the MatMul hook of the next projection
  * (vllm_nt/_ntops/oot_support.py:32-48, then vllm_nt/_ntops/torch/linear.py:7-21), which
- * the reference runs as two kernels with h written to and read back from memory; here h
- * is formed in shared memory as the GEMM's input and never written.  h is rounded as
- * ntb200_fused_add_rms_norm rounds it (the normalised fp32 value rounded to the dtype,
- * times the weight, rounded again); the row statistics are summed in another order, so h
- * can differ from that entry point's output in the last bit.  residual and residual_out
+ * the reference runs as two kernels with the normalised rows written to and read back from
+ * memory; here the GEMM input round(s * norm_weight) is formed in shared memory and never
+ * written, and the per-row 1/rms scales the fp32 products (the projection is linear in
+ * it), so the MMAs do not wait for the row statistics.  The rounding points therefore
+ * differ from the unfused pair's (normalised value rounded, times the weight, rounded
+ * again): one rounding of the input instead of two.  residual and residual_out
  * are both given or both null, and residual_out must not alias x or residual (other CTAs
  * still read them while it is written).  M <= 16 (NTB200_ERR_UNSUPPORTED_SHAPE above),
  * dtype BF16 or F16, K a multiple of 8, rows 16-byte aligned; at most 4096 columns of K per

@@ -293,24 +293,22 @@ def test_fused_rope_kv_store_attention_hook(_b200_config, vllm_ctx, monkeypatch)
     assert _hits(patching, "RoPEKVCache") == 1 and _hits(patching, "StoreKVCache") == 1
 
 
-def test_norm_qkv_decoder_hook(_b200_config, vllm_ctx, monkeypatch, tmp_path):
-    """The opt-in LlamaDecoderLayer.forward patch on a decode batch: vLLM's (hooked) input
-    RMSNorm with its residual add and the qkv projection as one kernel; the new residual
-    bit for bit and the projection against the oracle's norm followed by its linear; the
-    attention and the MLP run as the layer's own modules."""
+def test_norm_qkv_decoder_hook(_b200_config, vllm_ctx):
+    """The LlamaDecoderLayer.forward patch of the shipped config on a single-token decode
+    batch: vLLM's (hooked) input RMSNorm with its residual add and the qkv projection as one
+    kernel; the new residual bit for bit and the projection against the oracle's
+    restatement of the fused kernel; the attention and the MLP run as the layer's own
+    modules.  A five-token batch declines to vLLM's layer forward."""
     from vllm.model_executor.layers.layernorm import RMSNorm
 
     from vllm_nt._ntops import config
 
     patching = _b200_config
-    cfg = tmp_path / "norm-qkv.yaml"  # all-b200.yaml with the opt-in RMSNormQKV named
-    cfg.write_text((ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml").read_text() + "  RMSNormQKV: b200\n")
-    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(cfg))
     config.reset_backend_config_cache()
     g = seeded(43)
-    t, hidden, hq, hk = 5, 4096, 32, 8
-    x = torch.randn(t, hidden, generator=g).to(torch.bfloat16)
-    r = torch.randn(t, hidden, generator=g).to(torch.bfloat16)
+    hidden, hq, hk = 4096, 32, 8
+    x = torch.randn(5, hidden, generator=g).to(torch.bfloat16)
+    r = torch.randn(5, hidden, generator=g).to(torch.bfloat16)
     gam = (1 + 0.1 * torch.randn(hidden, generator=g)).to(torch.bfloat16)
     w = (0.02 * torch.randn((hq + 2 * hk) * 128, hidden, generator=g)).to(torch.bfloat16)
     ln = RMSNorm(hidden, eps=1e-5).to(device="cuda", dtype=torch.bfloat16)
@@ -322,10 +320,13 @@ def test_norm_qkv_decoder_hook(_b200_config, vllm_ctx, monkeypatch, tmp_path):
                                 o_proj=lambda a: (a, None))
     layer = SimpleNamespace(input_layernorm=ln, self_attn=self_attn,
                             post_attention_layernorm=lambda h, res: (h, res), mlp=lambda h: h)
-    fwd = patching._build_decoder_norm_qkv_forward(lambda *a: pytest.fail("fell back to vLLM"))
-    h, res = fwd(layer, torch.arange(t).cuda(), x.cuda(), r.cuda())
+    declined = []
+    fwd = patching._build_decoder_norm_qkv_forward(lambda self, p, h, res: (declined.append(h.shape[0]), (h, res))[1])
+    h, res = fwd(layer, torch.arange(1).cuda(), x[:1].cuda(), r[:1].cuda())
     torch.cuda.synchronize()
-    h_ref, res_ref = oracle.fused_add_rms_norm(x, r, gam, 1e-5)
+    ref, res_ref = oracle.rms_norm_linear(x[:1], gam, 1e-5, w, r[:1])
     assert bits_equal(res.cpu(), res_ref)
-    torch.testing.assert_close(h.float().cpu(), oracle.linear(h_ref, w)[:, : hq * 128], rtol=2e-2, atol=2e-2)
-    assert _hits(patching, "RMSNormQKV") == 1
+    torch.testing.assert_close(h.float().cpu(), ref[:, : hq * 128], rtol=2e-2, atol=2e-2)
+    assert _hits(patching, "RMSNormQKV") == 1 and declined == []
+    fwd(layer, torch.arange(5).cuda(), x.cuda(), r.cuda())
+    assert declined == [5] and _hits(patching, "RMSNormQKV") == 1

@@ -421,17 +421,18 @@ def test_fused_rope_kv_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypat
 
 def test_norm_qkv_decoder_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypatch, tmp_path):
     """RMSNormQKV (LlamaDecoderLayer.forward) applies only when a config names it (the
-    shipped all-b200.yaml does not); a call
-    it cannot serve (here: CPU activations, then a batch above 16 tokens) runs vLLM's layer
-    forward and is counted as declined with its reason."""
+    shipped all-b200.yaml does); a call it cannot serve (here: CPU activations, then a batch
+    above one token) runs vLLM's layer forward and is counted as declined with its reason."""
     spec = next(s for s in patching._FUNCTION_PATCH_SPECS if s.patch_id == "RMSNormQKV")
     config.reset_backend_config_cache()
-    assert not patching._function_patch_enabled(spec)  # all-b200.yaml leaves it out (measured slower)
-    cfg = tmp_path / "norm-qkv.yaml"
-    cfg.write_text((ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml").read_text() + "  RMSNormQKV: b200\n")
+    assert patching._function_patch_enabled(spec)  # all-b200.yaml names it
+    cfg = tmp_path / "no-norm-qkv.yaml"
+    cfg.write_text((ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml").read_text().replace("  RMSNormQKV: b200\n", ""))
     monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(cfg))
     config.reset_backend_config_cache()
-    assert patching._function_patch_enabled(spec)
+    assert not patching._function_patch_enabled(spec)
+    monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml"))
+    config.reset_backend_config_cache()
 
     from vllm.model_executor.layers.layernorm import RMSNorm
 
@@ -444,8 +445,10 @@ def test_norm_qkv_decoder_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkey
     layer = SimpleNamespace(input_layernorm=ln, self_attn=SimpleNamespace(qkv_proj=qkv_proj))
     seen = []
     fwd = patching._build_decoder_norm_qkv_forward(lambda self, p, h, r: (seen.append(h.shape[0]), (h, r))[1])
-    h = torch.zeros(3, 8)
-    assert fwd(layer, torch.arange(3), h, None)[0] is h
-    assert patching._why_not_norm_qkv(layer, torch.zeros(17, 8), None) == "activation / weight dtype or device"
+    h = torch.zeros(1, 8)
+    assert fwd(layer, torch.arange(1), h, None)[0] is h
+    h3 = torch.zeros(3, 8)
+    assert fwd(layer, torch.arange(3), h3, None)[0] is h3
     op = patching.get_usage_summary()["operators"]["RMSNormQKV"]
-    assert seen == [3] and op["hits"] == 0 and op["declined"] == {"activation / weight dtype or device": 1}
+    assert seen == [1, 3] and op["hits"] == 0
+    assert op["declined"] == {"activation / weight dtype or device": 1, "batch above 1 token(s)": 1}

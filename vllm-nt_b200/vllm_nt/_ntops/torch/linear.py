@@ -43,8 +43,9 @@ def linear_silu_and_mul(input: torch.Tensor, gate_up: torch.Tensor) -> torch.Ten
 def rms_norm_linear(input: torch.Tensor, norm_weight: torch.Tensor, eps: float, weight: torch.Tensor,
                     residual: torch.Tensor | None = None):
     """RMSNorm (after adding residual, when given) of a decode batch of at most 16 rows,
-    then the projection by weight [N, K], as one kernel: the normalised rows are formed in
-    shared memory as the GEMM's input and never written.  Returns out [M, N], or
+    then the projection by weight [N, K], as one kernel: the GEMM input round(s *
+    norm_weight) is formed in shared memory and never written, and each row's 1/rms scales
+    the fp32 products before the output's one rounding.  Returns out [M, N], or
     (out, new_residual) with a residual (new_residual = input + residual, a new tensor)."""
     x = input if input.is_contiguous() else input.contiguous()
     x2 = x.reshape(-1, x.shape[-1])
