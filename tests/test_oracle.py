@@ -145,6 +145,33 @@ def test_linear_matches_f_linear(tag):
     torch.testing.assert_close(oracle.linear(g["x"], g["weight"], g["bias"]), g["out"], rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 512), (5, 1032, 700), (16, 2048, 256)])
+@pytest.mark.parametrize("with_residual", [False, True])
+def test_fused_norm_linear_rounding_is_no_less_accurate_than_the_pair(m, k, n, with_residual):
+    """The fused entry point's rounding points (s * w rounded once, 1/rms on the fp32
+    products): the new residual is the pair's bit for bit, the output differs from the
+    pair's (vLLM's RMSNorm rounded, then F.linear) by rounding only, and its RMS error
+    against the unrounded fp64 value is no larger than the pair's."""
+    g = seeded(100 * m + k + n + with_residual)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    res = torch.randn(m, k, generator=g).to(torch.bfloat16) if with_residual else None
+    gamma = (1.0 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16)
+    w = (0.02 * torch.randn(n, k, generator=g)).to(torch.bfloat16)
+    out, new_res = oracle.rms_norm_linear(x, gamma, 1e-5, w, res)
+    if with_residual:
+        h, res_pair = oracle.fused_add_rms_norm(x, res, gamma, 1e-5)
+        assert bits_equal(new_res, res_pair)
+    else:
+        h = oracle.rms_norm(x, gamma, 1e-5)
+        assert new_res is None
+    pair = oracle.linear(h, w)
+    torch.testing.assert_close(out, pair, rtol=2e-2, atol=2e-2)
+    exact = oracle.rms_norm_linear_exact(x, gamma, 1e-5, w, res)
+    err = (out.to(torch.bfloat16).double() - exact).pow(2).mean().sqrt()
+    err_pair = (pair.to(torch.bfloat16).double() - exact).pow(2).mean().sqrt()
+    assert err <= err_pair
+
+
 def test_rope_reference_known_answer():
     """vllm_nt/tests/test_rope.py:26-46: x (5,4,8), per-token cos/sin (5,1,4); reference
     cat(x1*cos - x2*sin, x2*cos + x1*sin)."""
