@@ -422,7 +422,7 @@ def test_fused_rope_kv_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypat
 def test_norm_qkv_decoder_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkeypatch, tmp_path):
     """RMSNormQKV (LlamaDecoderLayer.forward) applies only when a config names it (the
     shipped all-b200.yaml does); a call it cannot serve (here: CPU activations, then a batch
-    above one token) runs vLLM's layer forward and is counted as declined with its reason."""
+    above two tokens) runs vLLM's layer forward and is counted as declined with its reason."""
     spec = next(s for s in patching._FUNCTION_PATCH_SPECS if s.patch_id == "RMSNormQKV")
     config.reset_backend_config_cache()
     assert patching._function_patch_enabled(spec)  # all-b200.yaml names it
@@ -451,4 +451,4 @@ def test_norm_qkv_decoder_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkey
     assert fwd(layer, torch.arange(3), h3, None)[0] is h3
     op = patching.get_usage_summary()["operators"]["RMSNormQKV"]
     assert seen == [1, 3] and op["hits"] == 0
-    assert op["declined"] == {"activation / weight dtype or device": 1, "batch above 1 token(s)": 1}
+    assert op["declined"] == {"activation / weight dtype or device": 1, "batch above 2 token(s)": 1}

@@ -784,15 +784,16 @@ def _build_attention_rope_kv_forward(original: object) -> object:
     return _mark_function_patch(forward, "RoPEKVCache")
 
 
-# ntb200_rms_norm_linear takes up to 16 rows, but only a single-token batch runs faster
-# than the separate norm and projection kernels (Llama-3-8B qkv: 12.6 vs 13.9 us at one
-# token; 14.6 vs 14.0 us at four, 18.3 vs 14.9 us at sixteen), so larger batches decline.
-_NORM_LINEAR_MAX_ROWS = 1
+# ntb200_rms_norm_linear takes up to 16 rows, but only batches of one or two tokens run
+# faster than the separate norm and projection kernels (Llama-3-8B qkv with x and the
+# residual just written, as in a decoder layer: 15.3 against 17.4 us at one token, 17.0
+# against 17.5 at two, 18.4 against 17.8 at four), so larger batches decline.
+_NORM_LINEAR_MAX_ROWS = 2
 
 
 def _why_not_norm_qkv(layer: Any, hidden: torch.Tensor, residual: torch.Tensor | None) -> str | None:
     """input_layernorm is a plain RMSNorm and self_attn.qkv_proj an unquantised, bias-free
-    projection whose output stays on this rank, for a single-token decode batch."""
+    projection whose output stays on this rank, for a decode batch of one or two tokens."""
     ln = getattr(layer, "input_layernorm", None)
     qkv = getattr(getattr(layer, "self_attn", None), "qkv_proj", None)
     if not isinstance(ln, layernorm.RMSNorm) or not getattr(ln, "has_weight", True) or \
@@ -818,7 +819,7 @@ def _why_not_norm_qkv(layer: Any, hidden: torch.Tensor, residual: torch.Tensor |
 
 
 def _build_decoder_norm_qkv_forward(original: object) -> object:
-    """Replacement for LlamaDecoderLayer.forward: for a single-token decode batch the
+    """Replacement for LlamaDecoderLayer.forward: for a decode batch of one or two tokens the
     input RMSNorm (with its residual add) and the qkv projection become one kernel
     (ntb200_rms_norm_linear), whose normalised rows never leave shared memory; the rest of
     the layer runs as vLLM's code does (attention through the hooks, with the RoPEKVCache
