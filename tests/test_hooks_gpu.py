@@ -294,11 +294,11 @@ def test_fused_rope_kv_store_attention_hook(_b200_config, vllm_ctx, monkeypatch)
 
 
 def test_norm_qkv_decoder_hook(_b200_config, vllm_ctx):
-    """The LlamaDecoderLayer.forward patch of the shipped config on a single-token decode
-    batch: vLLM's (hooked) input RMSNorm with its residual add and the qkv projection as one
-    kernel; the new residual bit for bit and the projection against the oracle's
-    restatement of the fused kernel; the attention and the MLP run as the layer's own
-    modules.  A five-token batch declines to vLLM's layer forward."""
+    """The LlamaDecoderLayer.forward patch of the shipped config on decode batches of one
+    and two tokens: vLLM's (hooked) input RMSNorm with its residual add and the qkv
+    projection as one kernel; the new residual bit for bit and the projection against the
+    oracle's restatement of the fused kernel; the attention and the MLP run as the layer's
+    own modules.  A five-token batch declines to vLLM's layer forward."""
     from vllm.model_executor.layers.layernorm import RMSNorm
 
     from vllm_nt._ntops import config
@@ -322,11 +322,12 @@ def test_norm_qkv_decoder_hook(_b200_config, vllm_ctx):
                             post_attention_layernorm=lambda h, res: (h, res), mlp=lambda h: h)
     declined = []
     fwd = patching._build_decoder_norm_qkv_forward(lambda self, p, h, res: (declined.append(h.shape[0]), (h, res))[1])
-    h, res = fwd(layer, torch.arange(1).cuda(), x[:1].cuda(), r[:1].cuda())
-    torch.cuda.synchronize()
-    ref, res_ref = oracle.rms_norm_linear(x[:1], gam, 1e-5, w, r[:1])
-    assert bits_equal(res.cpu(), res_ref)
-    torch.testing.assert_close(h.float().cpu(), ref[:, : hq * 128], rtol=2e-2, atol=2e-2)
-    assert _hits(patching, "RMSNormQKV") == 1 and declined == []
+    for t in (1, 2):
+        h, res = fwd(layer, torch.arange(t).cuda(), x[:t].cuda(), r[:t].cuda())
+        torch.cuda.synchronize()
+        ref, res_ref = oracle.rms_norm_linear(x[:t], gam, 1e-5, w, r[:t])
+        assert bits_equal(res.cpu(), res_ref)
+        torch.testing.assert_close(h.float().cpu(), ref[:, : hq * 128], rtol=2e-2, atol=2e-2)
+    assert _hits(patching, "RMSNormQKV") == 2 and declined == []
     fwd(layer, torch.arange(5).cuda(), x.cuda(), r.cuda())
-    assert declined == [5] and _hits(patching, "RMSNormQKV") == 1
+    assert declined == [5] and _hits(patching, "RMSNormQKV") == 2
