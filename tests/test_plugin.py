@@ -434,15 +434,7 @@ def test_norm_qkv_decoder_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkey
     monkeypatch.setenv("VLLM_NT_BACKEND_CONFIG", str(ROOT / "vllm-nt_b200/vllm_nt/configs/all-b200.yaml"))
     config.reset_backend_config_cache()
 
-    from vllm.model_executor.layers.layernorm import RMSNorm
-
-    ln = RMSNorm.__new__(RMSNorm)  # vLLM's class without its config-dependent constructor
-    for name, value in (("weight", torch.ones(8)), ("variance_epsilon", 1e-6), ("has_weight", True),
-                        ("variance_size_override", None)):
-        object.__setattr__(ln, name, value)
-    qkv_proj = SimpleNamespace(quant_method=patching.UnquantizedLinearMethod(), bias=None, gather_output=False,
-                               weight=torch.zeros(12, 8))
-    layer = SimpleNamespace(input_layernorm=ln, self_attn=SimpleNamespace(qkv_proj=qkv_proj))
+    layer = _norm_qkv_layer()
     seen = []
     fwd = patching._build_decoder_norm_qkv_forward(lambda self, p, h, r: (seen.append(h.shape[0]), (h, r))[1])
     h = torch.zeros(1, 8)
@@ -452,3 +444,45 @@ def test_norm_qkv_decoder_hook_is_opt_in_and_declines_what_it_cannot_fuse(monkey
     op = patching.get_usage_summary()["operators"]["RMSNormQKV"]
     assert seen == [1, 3] and op["hits"] == 0
     assert op["declined"] == {"activation / weight dtype or device": 1, "batch above 2 token(s)": 1}
+
+
+def _norm_qkv_layer(**changes):
+    """A decoder layer stand-in with vLLM's RMSNorm (built without its config-dependent
+    constructor) and an unquantised qkv projection of a [12, 8] weight; ``changes`` sets
+    attributes of the norm (``ln_*``) or of qkv_proj (``qkv_*``)."""
+    from vllm.model_executor.layers.layernorm import RMSNorm
+
+    ln = RMSNorm.__new__(RMSNorm)
+    for name, value in (("weight", torch.ones(8)), ("variance_epsilon", 1e-6), ("has_weight", True),
+                        ("variance_size_override", None)):
+        object.__setattr__(ln, name, value)
+    qkv_proj = SimpleNamespace(quant_method=patching.UnquantizedLinearMethod(), bias=None, gather_output=False,
+                               weight=torch.zeros(12, 8))
+    for key, value in changes.items():
+        owner, attr = key.split("_", 1)
+        if owner == "ln":
+            object.__setattr__(ln, attr, value)
+        else:
+            setattr(qkv_proj, attr, value)
+    return SimpleNamespace(input_layernorm=ln, self_attn=SimpleNamespace(qkv_proj=qkv_proj))
+
+
+@pytest.mark.parametrize("changes,hidden_shape,reason", [
+    ({"ln_has_weight": False}, (1, 8), "input_layernorm is not a plain RMSNorm"),
+    ({"ln_variance_size_override": 4}, (1, 8), "input_layernorm is not a plain RMSNorm"),
+    ({"qkv_quant_method": object()}, (1, 8), "quantised qkv_proj"),
+    ({"qkv_bias": torch.zeros(12)}, (1, 8), "qkv_proj bias or gathered output"),
+    ({"qkv_gather_output": True}, (1, 8), "qkv_proj bias or gathered output"),
+    ({"qkv_weight": torch.zeros(12, 6)}, (1, 6), "qkv_proj weight layout"),
+    ({"qkv_weight": torch.zeros(8, 12).t()}, (1, 8), "qkv_proj weight layout"),
+    ({}, (1, 16), "hidden states are not [tokens, hidden]"),
+    ({}, (1, 1, 8), "hidden states are not [tokens, hidden]"),
+    ({}, (3, 8), "batch above 2 token(s)"),
+    ({}, (2, 8), "activation / weight dtype or device"),  # eligible but for the CPU tensor
+])
+def test_norm_qkv_decline_reasons(changes, hidden_shape, reason):
+    """Each reason the RMSNorm + qkv decoder hook gives for leaving a call to vLLM, checked
+    in the order the hook tests them (the device check last but one, so every layer and
+    shape reason shows on CPU tensors)."""
+    layer = _norm_qkv_layer(**changes)
+    assert patching._why_not_norm_qkv(layer, torch.zeros(hidden_shape), None) == reason
