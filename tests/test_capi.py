@@ -67,6 +67,18 @@ def test_status_strings_and_version():
         ("ntb200_random_sample", (1, 1, 1, 4, 8, 8, 7, None), -1),
         ("ntb200_random_sample", (None, 1, 1, 4, 8, 8, 8, None), -1),
         ("ntb200_linear", (1, 1, 1, None, 4, 8, 16, 16, 16, 8, None, 0, 0, None), -2),
+        # linear_silu_and_mul: fp32; x row stride below K; x not 16-byte aligned
+        ("ntb200_linear_silu_and_mul", (16, 16, 16, 4, 8, 64, 64, 64, 8, 0, None), -2),
+        ("ntb200_linear_silu_and_mul", (16, 16, 16, 4, 8, 64, 32, 64, 8, 1, None), -1),
+        ("ntb200_linear_silu_and_mul", (16, 8, 16, 4, 8, 64, 64, 64, 8, 1, None), -3),
+        # rms_norm_linear (out, residual_out, x, residual, norm_weight, eps, weight, M, N, K,
+        # strides x / residual / residual_out / weight / out, dtype, stream): fp32; 17 rows;
+        # a residual without residual_out; residual_out aliasing x; K not a multiple of 8
+        ("ntb200_rms_norm_linear", (16, None, 16, None, 16, 1e-5, 16, 4, 8, 64, 64, 0, 0, 64, 8, 0, None), -2),
+        ("ntb200_rms_norm_linear", (16, None, 16, None, 16, 1e-5, 16, 17, 8, 64, 64, 0, 0, 64, 8, 1, None), -6),
+        ("ntb200_rms_norm_linear", (16, None, 16, 32, 16, 1e-5, 16, 4, 8, 64, 64, 64, 64, 64, 8, 1, None), -1),
+        ("ntb200_rms_norm_linear", (16, 16, 16, 32, 16, 1e-5, 16, 4, 8, 64, 64, 64, 64, 64, 8, 1, None), -1),
+        ("ntb200_rms_norm_linear", (16, None, 16, None, 16, 1e-5, 16, 4, 8, 60, 64, 0, 0, 64, 8, 1, None), -3),
         ("ntb200_paged_attention_decode",
          (1, 1, 1, 1, 1, 1, 2, 4, 1, 64, 16, 8, 4, 4, 64, 0.1, 512, 128, 512, 128, 2048, 128, 128, None, 0, 1, None), -6),
         ("ntb200_paged_attention_decode",
@@ -90,6 +102,9 @@ def test_zero_sized_calls_are_no_ops():
     assert capi.call("ntb200_top_k_top_p", 1, 0, 100, 100, 1, 4, None, None) == 0
     assert capi.call("ntb200_top_k_top_p", 1, 4, 100, 100, None, 4, None, None) == 0
     assert capi.call("ntb200_random_sample", 1, 1, 1, 0, 8, 8, 8, None) == 0
+    assert capi.call("ntb200_linear_silu_and_mul", 16, 16, 16, 0, 8, 64, 64, 64, 8, 1, None) == 0
+    assert capi.call("ntb200_rms_norm_linear", 16, None, 16, None, 16, 1e-5, 16, 0, 8, 64, 64, 0, 0, 64, 8, 1,
+                     None) == 0
 
 
 def test_workspace_queries():
