@@ -81,6 +81,56 @@ def test_status_strings_and_version():
         ("ntb200_rms_norm_linear", (16, None, 16, None, 16, 1e-5, 16, 4, 8, 60, 64, 0, 0, 64, 8, 1, None), -3),
         ("ntb200_paged_attention_decode",
          (1, 1, 1, 1, 1, 1, 2, 4, 1, 64, 16, 8, 4, 4, 64, 0.1, 512, 128, 512, 128, 2048, 128, 128, None, 0, 1, None), -6),
+        # Gemma norms: the raw weight is required; fp16 with a residual (vLLM keeps it fp32);
+        # a row stride below hidden
+        ("ntb200_gemma_rms_norm", (16, 16, None, 4, 8, 8, 8, 1e-6, 1, None), -1),
+        ("ntb200_gemma_fused_add_rms_norm", (16, 16, 16, 16, 4, 8, 8, 8, 8, 1e-6, 2, None), -2),
+        ("ntb200_gemma_fused_add_rms_norm", (16, 16, 16, 16, 4, 8, 8, 4, 8, 1e-6, 1, None), -1),
+        # paged prefill (out, query, k/v cache, query_start_loc, seq_lens, block_tables,
+        # seqs, tokens, q/kv heads, head_size, block_size, blocks, max blocks, table stride,
+        # max_query_len, scale, causal, q/out token+head strides, cache strides, dtype,
+        # stream): fp32; head_size 64; 30 q heads over 8 kv heads; null query; out 8-aligned
+        ("ntb200_paged_attention_prefill", (16, 16, 16, 16, 16, 16, 16, 2, 8, 32, 8, 128, 16, 64, 4, 4, 4, 0.1, 1,
+                                            4096, 128, 4096, 128, 16384, 1024, 128, 0, None), -2),
+        ("ntb200_paged_attention_prefill", (16, 16, 16, 16, 16, 16, 16, 2, 8, 32, 8, 64, 16, 64, 4, 4, 4, 0.1, 1,
+                                            4096, 128, 4096, 128, 16384, 1024, 128, 1, None), -6),
+        ("ntb200_paged_attention_prefill", (16, 16, 16, 16, 16, 16, 16, 2, 8, 30, 8, 128, 16, 64, 4, 4, 4, 0.1, 1,
+                                            4096, 128, 4096, 128, 16384, 1024, 128, 1, None), -1),
+        ("ntb200_paged_attention_prefill", (16, None, 16, 16, 16, 16, 16, 2, 8, 32, 8, 128, 16, 64, 4, 4, 4, 0.1, 1,
+                                            4096, 128, 4096, 128, 16384, 1024, 128, 1, None), -1),
+        ("ntb200_paged_attention_prefill", (8, 16, 16, 16, 16, 16, 16, 2, 8, 32, 8, 128, 16, 64, 4, 4, 4, 0.1, 1,
+                                            4096, 128, 4096, 128, 16384, 1024, 128, 1, None), -3),
+        # contiguous varlen (out, query, key, value, cu_q, cu_k, seqs, q tokens, k tokens,
+        # q/kv heads, head_size, max_query_len, scale, causal, q/k/v/out token+head strides,
+        # dtype, stream): fp32; head_size 96; negative key count; null cu_seqlens_k; a key
+        # row stride that is not a multiple of 8
+        ("ntb200_flash_attn_varlen", (16, 16, 16, 16, 16, 16, 2, 8, 8, 32, 8, 128, 4, 0.1, 1,
+                                      4096, 128, 1024, 128, 1024, 128, 4096, 128, 0, None), -2),
+        ("ntb200_flash_attn_varlen", (16, 16, 16, 16, 16, 16, 2, 8, 8, 32, 8, 96, 4, 0.1, 1,
+                                      4096, 128, 1024, 128, 1024, 128, 4096, 128, 1, None), -6),
+        ("ntb200_flash_attn_varlen", (16, 16, 16, 16, 16, 16, 2, 8, -1, 32, 8, 128, 4, 0.1, 1,
+                                      4096, 128, 1024, 128, 1024, 128, 4096, 128, 1, None), -1),
+        ("ntb200_flash_attn_varlen", (16, 16, 16, 16, 16, None, 2, 8, 8, 32, 8, 128, 4, 0.1, 1,
+                                      4096, 128, 1024, 128, 1024, 128, 4096, 128, 1, None), -1),
+        ("ntb200_flash_attn_varlen", (16, 16, 16, 16, 16, 16, 2, 8, 8, 32, 8, 128, 4, 0.1, 1,
+                                      4096, 128, 1028, 128, 1024, 128, 4096, 128, 1, None), -3),
+        # decode for the single-query rows of a varlen batch: null query_start_loc; GQA
+        # group 16; a block table stride below its width
+        ("ntb200_paged_attention_decode_varlen", (16, 16, 16, 16, None, 16, 16, 2, 32, 8, 128, 16, 64, 4, 4, 64, 0.1,
+                                                  4096, 128, 4096, 128, 16384, 1024, 128, None, 0, 1, None), -1),
+        ("ntb200_paged_attention_decode_varlen", (16, 16, 16, 16, 16, 16, 16, 2, 128, 8, 128, 16, 64, 4, 4, 64, 0.1,
+                                                  4096, 128, 4096, 128, 16384, 1024, 128, None, 0, 1, None), -6),
+        ("ntb200_paged_attention_decode_varlen", (16, 16, 16, 16, 16, 16, 16, 2, 32, 8, 128, 16, 64, 4, 3, 64, 0.1,
+                                                  4096, 128, 4096, 128, 16384, 1024, 128, None, 0, 1, None), -1),
+        # peer all-reduce (out, partial, peer_buffers, numel, capacity, rank, world_size,
+        # dtype, stream): more elements than the capacity; rank outside the world; nine
+        # ranks; out 8-aligned; fp32; a two-shot count that is not a multiple of 8
+        ("ntb200_allreduce_oneshot", (16, 16, 16, 2000, 1000, 0, 2, 1, None), -1),
+        ("ntb200_allreduce_oneshot", (16, 16, 16, 8, 1000, 2, 2, 1, None), -1),
+        ("ntb200_allreduce_oneshot", (16, 16, 16, 8, 1000, 0, 9, 1, None), -1),
+        ("ntb200_allreduce_oneshot", (8, 16, 16, 8, 1000, 0, 2, 1, None), -3),
+        ("ntb200_allreduce_oneshot", (16, 16, 16, 8, 1000, 0, 2, 0, None), -2),
+        ("ntb200_allreduce_twoshot", (16, 16, 16, 12, 1000, 0, 2, 1, None), -1),
         ("ntb200_paged_attention_decode",
          (1, 1, 1, 1, 1, 1, 2, 36, 4, 128, 16, 8, 4, 4, 64, 0.1, 512, 128, 512, 128, 2048, 128, 128, None, 0, 1, None), -6),
     ],
@@ -105,6 +155,13 @@ def test_zero_sized_calls_are_no_ops():
     assert capi.call("ntb200_linear_silu_and_mul", 16, 16, 16, 0, 8, 64, 64, 64, 8, 1, None) == 0
     assert capi.call("ntb200_rms_norm_linear", 16, None, 16, None, 16, 1e-5, 16, 0, 8, 64, 64, 0, 0, 64, 8, 1,
                      None) == 0
+    assert capi.call("ntb200_gemma_rms_norm", 16, 16, 16, 0, 8, 8, 8, 1e-6, 1, None) == 0
+    assert capi.call("ntb200_paged_attention_prefill", 16, 16, 16, 16, 16, 16, 16, 0, 0, 32, 8, 128, 16, 64, 4, 4,
+                     4, 0.1, 1, 4096, 128, 4096, 128, 16384, 1024, 128, 1, None) == 0
+    assert capi.call("ntb200_flash_attn_varlen", 16, 16, 16, 16, 16, 16, 2, 0, 8, 32, 8, 128, 4, 0.1, 1,
+                     4096, 128, 1024, 128, 1024, 128, 4096, 128, 1, None) == 0
+    assert capi.call("ntb200_allreduce_oneshot", 16, 16, 16, 0, 1000, 0, 2, 1, None) == 0
+    assert capi.call("ntb200_allreduce_twoshot", 16, 16, 16, 0, 1000, 0, 2, 1, None) == 0
 
 
 def test_workspace_queries():
