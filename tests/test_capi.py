@@ -188,3 +188,35 @@ def test_workspace_queries():
 def test_read_device_error_rejects_null():
     with pytest.raises(capi.NtB200Error):
         capi.call("ntb200_read_device_error", ctypes.POINTER(ctypes.c_int)(), None)
+
+
+def test_torch_ops_refuse_host_tensors():
+    """The product path has no CPU fallback: each torch-facing wrapper, given host tensors,
+    raises instead of computing anything (the ntb200 ops are registered for the CUDA
+    dispatch key only, so torch's dispatcher refuses the CPU call)."""
+    import torch
+
+    from vllm_nt._ntops.torch.embedding import embedding
+    from vllm_nt._ntops.torch.linear import linear, linear_argmax, linear_silu_and_mul, rms_norm_linear
+    from vllm_nt._ntops.torch.rms_norm import fused_add_rms_norm, gemma_rms_norm, rms_norm
+    from vllm_nt._ntops.torch.silu import silu_and_mul
+
+    x = torch.randn(4, 64).to(torch.bfloat16)
+    w = torch.randn(32, 64).to(torch.bfloat16)
+    g = torch.ones(64, dtype=torch.bfloat16)
+    ids = torch.tensor([0, 3, 5])
+    calls = {
+        "linear": lambda: linear(x, w),
+        "linear_silu_and_mul": lambda: linear_silu_and_mul(x, w),
+        "linear_argmax": lambda: linear_argmax(x, w),
+        "rms_norm_linear": lambda: rms_norm_linear(x, g, 1e-5, w, x.clone()),
+        "rms_norm": lambda: rms_norm(x, 64, g, 1e-5),
+        "fused_add_rms_norm": lambda: fused_add_rms_norm(x, x.clone(), g, 1e-5),
+        "gemma_rms_norm": lambda: gemma_rms_norm(x, g, 1e-6),
+        "silu_and_mul": lambda: silu_and_mul(x),
+        "embedding": lambda: embedding(ids, w),
+    }
+    for name, call in calls.items():
+        with pytest.raises((RuntimeError, NotImplementedError), match="'CPU' backend|CUDA tensor"):
+            call()
+            pytest.fail(f"{name} ran on host tensors")
